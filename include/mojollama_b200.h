@@ -1,0 +1,100 @@
+/* mojollama_b200 -- core C-ABI of the B200 (sm_100a) engine.
+ *
+ * Every entry point takes plain pointers and sizes.  A pointer may be host
+ * memory (pageable or pinned) or device memory of the current device; the
+ * library classifies it with cudaPointerGetAttributes:
+ *   - weights (const uint8_t *W) in host memory are copied to the device once and
+ *     cached by (address, byte count); callers must treat a host weight buffer as
+ *     immutable after its first use, or call mlq_cache_clear().
+ *   - activations in host memory are copied in on every call, outputs in host
+ *     memory are copied back, and the call returns when they are written.
+ *   - when every pointer of a call is device memory the call is asynchronous on
+ *     the library stream (mlq_set_stream / mlq_get_stream); mlq_sync() waits.
+ * Errors never abort the process: the call returns with its outputs untouched
+ * and records a code readable through mlq_last_error() (thread-local).
+ *
+ * The reference-named drop-in functions (quant_matmul_omp, moe_forward_omp, ...)
+ * are declared in mojollama_b200_ref_abi.h and exported by the alias libraries
+ * combined_engine.so / cengine_batch_instr.so / quant_kernels_omp.so /
+ * gqa_attention.so / simd_ops.so, which forward to the functions below.
+ */
+#ifndef MOJOLLAMA_B200_H
+#define MOJOLLAMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- type codes: ggml/GGUF numbering (quant_kernels_omp.c:6-14 of the reference) ---- */
+enum {
+    MLQ_F32 = 0, MLQ_F16 = 1, MLQ_Q4_0 = 2, MLQ_Q4_1 = 3, MLQ_Q5_0 = 6, MLQ_Q8_0 = 8,
+    MLQ_Q4_K = 12, MLQ_Q5_K = 13, MLQ_Q6_K = 14, MLQ_BF16 = 30, MLQ_MXFP4 = 39,
+    /* the reference C decoder's own 17-byte MXFP4 layout {qs[16], e}, int4 mantissas
+       (quant_kernels_omp.c:486-573); type 39 means GGUF MXFP4 {e, qs[16]}, E2M1 */
+    MLQ_MXFP4_REF = 1039
+};
+
+/* ---- error codes ---- */
+enum {
+    MLQ_OK = 0,
+    MLQ_ERR_ARG = 1,          /* null pointer, non-positive size, K not a multiple of the block */
+    MLQ_ERR_TYPE = 2,         /* unsupported quant type (the reference silently skips these) */
+    MLQ_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+    MLQ_ERR_NO_DEVICE = 4,    /* no CUDA device / library not initialised */
+    MLQ_ERR_TIMEOUT = 5,      /* a device-side bounded wait gave up (see mlq_device_status) */
+    MLQ_ERR_CAPACITY = 6,     /* size beyond a documented limit (page table full, K too large) */
+    MLQ_ERR_UNSUPPORTED = 7
+};
+
+int         mlq_last_error(void);
+const char *mlq_last_error_message(void);
+void        mlq_clear_error(void);
+
+/* ---- runtime ---- */
+int   mlq_init(int device);               /* optional; first call otherwise initialises device 0 */
+int   mlq_set_device(int device);
+int   mlq_get_device(void);
+void *mlq_get_stream(void);               /* cudaStream_t the library launches on */
+/* launch on this cudaStream_t from now on (0 = the legacy default stream, e.g.
+   torch.cuda.current_stream().cuda_stream); mlq_use_own_stream() goes back */
+int   mlq_set_stream(void *cuda_stream);
+int   mlq_use_own_stream(void);
+int   mlq_sync(void);                     /* wait for the stream; also reports device-side errors */
+int   mlq_device_status(void);            /* reads and clears the device error word */
+int   mlq_register_weights(const void *host_ptr, size_t bytes);   /* optional pre-residency */
+int   mlq_cache_clear(void);              /* drop every cached device copy of host weights */
+size_t mlq_cache_bytes(void);
+int   mlq_num_sms(void);
+/* number of kernels this library launched since load (all devices); for launch accounting */
+unsigned long long mlq_launch_count(void);
+/* 1 = reproduce the reference's quirks byte-for-byte where they differ from GGUF:
+   type 39 decodes the reference MXFP4 layout, type 12 through the dispatcher follows
+   the reference's Q8-activation dot, type 14 through the dispatcher reads ql low
+   nibbles only.  0 (default) = GGUF-correct math. */
+int   mlq_set_ref_compat(int on);
+int   mlq_get_ref_compat(void);
+
+/* ---- block formats ---- */
+int    mlq_block_elems(int qt);            /* 32, 256 or 1; 0 if unknown */
+int    mlq_block_bytes(int qt);
+size_t mlq_row_bytes(int qt, int n_cols);  /* 0 if n_cols is not a multiple of the block */
+
+/* ---- quantized matrix-vector / matrix-matrix products ----
+ * W: n_rows x n_cols of type qt, row-major, rows are contiguous runs of blocks.
+ * x: [B][n_cols] fp32, out: [B][n_rows] fp32 (the reference's batch layout,
+ * cengine_batch_instr.c:251). */
+int mlq_matmul(const void *W, int qt, const float *x, float *out, int n_rows, int n_cols, int B);
+/* dequantize n values of type qt to fp32, bit-identical to gguf-py / the reference */
+int mlq_dequantize(const void *W, int qt, float *out, int64_t n);
+/* the reference's Q8_0 activation quantizer, byte-identical (quant_kernels_omp.c:1406) */
+int mlq_quantize_q8_0(const float *x, uint8_t *q8, int64_t n);
+/* W (qt) times Q8_0-quantized activations x_q8 [B][n_cols/32 blocks] */
+int mlq_matmul_q8act(const void *W, int qt, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

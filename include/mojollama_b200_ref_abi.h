@@ -1,0 +1,72 @@
+/* Reference-named drop-in entry points (C-ABI), exported by the alias libraries in
+ * mojollama_b200/lib/: combined_engine.so, quant_kernels_omp.so and
+ * cengine_batch_instr.so (the "engine" set below), simd_ops.so and gqa_attention.so.
+ *
+ * Signatures, argument meaning and buffer layouts are the reference's; each line
+ * cites the reference definition it replaces (paths inside a730/MojoLlama).
+ * Conventions kept from the reference: void return, caller-owned buffers, host
+ * pointers accepted (device pointers too, see mojollama_b200.h), errors leave the
+ * outputs untouched (the reference's `default:` case) and are readable through
+ * mlq_last_error().  set_num_threads / get_max_threads keep their signatures but
+ * have nothing to control on the GPU.
+ */
+#ifndef MOJOLLAMA_B200_REF_ABI_H
+#define MOJOLLAMA_B200_REF_ABI_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ============================ engine set (combined_engine.so & co.) ============================ */
+
+/* src/mojollama/kernels/quant_kernels_omp.c:1355  dispatch on GGUF type (0,2,3,6,8,12,13,14,39) */
+void quant_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols, int quant_type);
+/* quant_kernels_omp.c:884 */
+void f32_matmul_omp(const float *W, const float *x, float *out, int n_rows, int n_cols);
+/* quant_kernels_omp.c:135, 160, 1232-1242, 376, 199, 356, 734, 502 */
+void q4_0_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q4_1_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q5_0_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q8_0_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q4_k_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q5_k_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void q6_k_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+void mxfp4_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols);
+/* cengine_batch_instr.c:68, 216, 256, 316, 381, 435   x [B][nc], out [B][n_rows] */
+void q4_0_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+void q8_0_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+void q4_k_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+void q5_k_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+void q6_k_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+void mxfp4_batch_matmul(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B);
+/* quant_kernels_omp.c:428, 1524, 1311, 1751   Q8_0-quantized activations */
+void q8_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B);
+void q4_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int n_blocks_x);
+void q5_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B);
+void q4_k_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols);
+/* quant_kernels_omp.c:1406   returns n_cols/32 */
+int quantize_row_q8_0(const float *x, uint8_t *q8, int n_cols);
+/* quant_kernels_omp.c:762, 804, 830, 868 */
+void q6_k_dequantize_row(const uint8_t *W, float *out, int n_values);
+void q4_k_dequantize_row(const uint8_t *W, float *out, int n_values);
+void q5_k_dequantize_row(const uint8_t *W, float *out, int n_values);
+void q8_0_dequantize_row(const uint8_t *W, float *out, int n_values);
+/* quant_kernels_omp.c:1139, 1186   several projections of one activation in one launch set */
+void batch_qkv_omp(const uint8_t *Wq, const uint8_t *Wk, const uint8_t *Wv, const float *x,
+                   float *out_q, float *out_k, float *out_v, int nq, int nk, int nv, int n_cols,
+                   int qtype_q, int qtype_k, int qtype_v);
+void batch_gate_up_omp(const uint8_t *Wg, const uint8_t *Wu, const float *x, float *out_gate, float *out_up,
+                       int ng, int nu, int n_cols, int qtype_g, int qtype_u);
+/* quant_kernels_omp.c:938   Q4_0/Q4_1 (by block size ts[p] = 18 or 20), up to 7 projections */
+void batch_matmul(const uint8_t *w[7], const float *x, float *out[7], int nrows[7], int ncols[7], int ts[7],
+                  int n_proj);
+/* quant_kernels_omp.c:1030-1031 (no threads to set on the GPU; kept for the ABI) */
+int get_max_threads(void);
+void set_num_threads(int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

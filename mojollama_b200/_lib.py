@@ -1,0 +1,74 @@
+"""ctypes loader for the in-tree native libraries.
+
+Loading fails loudly when the libraries were not built: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib")
+CORE = os.path.join(LIB_DIR, "libmojollama_b200.so")
+
+_cf = ctypes.POINTER(ctypes.c_float)
+_cu = ctypes.POINTER(ctypes.c_uint8)
+_ci = ctypes.c_int
+_vp = ctypes.c_void_p
+
+_core = None
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib_path(name: str) -> str:
+    return os.path.join(LIB_DIR, name)
+
+
+def core() -> ctypes.CDLL:
+    """libmojollama_b200.so with argtypes for the mlq_* C-ABI (include/mojollama_b200.h)."""
+    global _core
+    if _core is not None:
+        return _core
+    if not os.path.exists(CORE):
+        raise NativeLibraryMissing(
+            f"{CORE} is missing: build it with `python -m mojollama_b200.build` "
+            "(this package has no CPU fallback)")
+    so = ctypes.CDLL(CORE, mode=ctypes.RTLD_GLOBAL)
+    so.mlq_last_error.restype = _ci
+    so.mlq_last_error_message.restype = ctypes.c_char_p
+    so.mlq_init.argtypes = [_ci]
+    so.mlq_set_device.argtypes = [_ci]
+    so.mlq_get_stream.restype = _vp
+    so.mlq_set_stream.argtypes = [_vp]
+    so.mlq_use_own_stream.argtypes = []
+    so.mlq_register_weights.argtypes = [_vp, ctypes.c_size_t]
+    so.mlq_cache_bytes.restype = ctypes.c_size_t
+    so.mlq_launch_count.restype = ctypes.c_ulonglong
+    so.mlq_set_ref_compat.argtypes = [_ci]
+    so.mlq_block_elems.argtypes = [_ci]
+    so.mlq_block_bytes.argtypes = [_ci]
+    so.mlq_row_bytes.argtypes = [_ci, _ci]
+    so.mlq_row_bytes.restype = ctypes.c_size_t
+    so.mlq_matmul.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
+    so.mlq_dequantize.argtypes = [_vp, _ci, _vp, ctypes.c_int64]
+    so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
+    so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
+    _core = so
+    return so
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = core().mlq_last_error_message().decode(errors="replace")
+        raise RuntimeError(f"{what or 'mojollama_b200'} failed ({rc}): {msg}")
+
+
+def load_alias(name: str) -> ctypes.CDLL:
+    """One of the reference-named alias libraries (combined_engine.so, ...)."""
+    core()   # load the core first (RTLD_GLOBAL) so the alias resolves against this build
+    p = lib_path(name)
+    if not os.path.exists(p):
+        raise NativeLibraryMissing(f"{p} is missing: run `python -m mojollama_b200.build`")
+    return ctypes.CDLL(p)

@@ -1,0 +1,89 @@
+/* Reference-named entry points of the "engine" set (combined_engine.so,
+ * quant_kernels_omp.so, cengine_batch_instr.so).  Each forwards to the mlq_* core
+ * in libmojollama_b200.so; see include/mojollama_b200_ref_abi.h for the reference
+ * definition each one replaces. */
+#include <stddef.h>
+#include <stdint.h>
+
+#include "mojollama_b200.h"
+#include "mojollama_b200_ref_abi.h"
+
+void quant_matmul_omp(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols, int quant_type) {
+    mlq_matmul(W, quant_type, x, out, n_rows, n_cols, 1);
+}
+
+void f32_matmul_omp(const float *W, const float *x, float *out, int n_rows, int n_cols) {
+    mlq_matmul(W, MLQ_F32, x, out, n_rows, n_cols, 1);
+}
+
+#define MLQ_GEMV1(name, qt) \
+    void name(const uint8_t *W, const float *x, float *out, int n_rows, int n_cols) { \
+        mlq_matmul(W, qt, x, out, n_rows, n_cols, 1); \
+    }
+MLQ_GEMV1(q4_0_matmul_omp, MLQ_Q4_0)
+MLQ_GEMV1(q4_1_matmul_omp, MLQ_Q4_1)
+MLQ_GEMV1(q5_0_matmul_omp, MLQ_Q5_0)
+MLQ_GEMV1(q8_0_matmul_omp, MLQ_Q8_0)
+MLQ_GEMV1(q4_k_matmul_omp, MLQ_Q4_K)
+MLQ_GEMV1(q5_k_matmul_omp, MLQ_Q5_K)
+MLQ_GEMV1(q6_k_matmul_omp, MLQ_Q6_K)
+MLQ_GEMV1(mxfp4_matmul_omp, MLQ_MXFP4)
+
+#define MLQ_GEMVB(name, qt) \
+    void name(const uint8_t *W, const float *x, float *out, int n_rows, int nc, int B) { \
+        mlq_matmul(W, qt, x, out, n_rows, nc, B); \
+    }
+MLQ_GEMVB(q4_0_batch_matmul, MLQ_Q4_0)
+MLQ_GEMVB(q8_0_batch_matmul, MLQ_Q8_0)
+MLQ_GEMVB(q4_k_batch_matmul, MLQ_Q4_K)
+MLQ_GEMVB(q5_k_batch_matmul, MLQ_Q5_K)
+MLQ_GEMVB(q6_k_batch_matmul, MLQ_Q6_K)
+MLQ_GEMVB(mxfp4_batch_matmul, MLQ_MXFP4)
+
+void q8_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B) {
+    mlq_matmul_q8act(W, MLQ_Q8_0, x_q8, out, n_rows, n_cols, B);
+}
+void q4_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols,
+                          int n_blocks_x) {
+    (void)n_blocks_x;
+    mlq_matmul_q8act(W, MLQ_Q4_0, x_q8, out, n_rows, n_cols, 1);
+}
+void q5_0_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B) {
+    mlq_matmul_q8act(W, MLQ_Q5_0, x_q8, out, n_rows, n_cols, B);
+}
+void q4_k_q8_0_matmul_omp(const uint8_t *W, const uint8_t *x_q8, float *out, int n_rows, int n_cols) {
+    mlq_matmul_q8act(W, MLQ_Q4_K, x_q8, out, n_rows, n_cols, 1);
+}
+
+int quantize_row_q8_0(const float *x, uint8_t *q8, int n_cols) {
+    mlq_quantize_q8_0(x, q8, n_cols);
+    return n_cols / 32;
+}
+
+void q6_k_dequantize_row(const uint8_t *W, float *out, int n) { mlq_dequantize(W, MLQ_Q6_K, out, n); }
+void q4_k_dequantize_row(const uint8_t *W, float *out, int n) { mlq_dequantize(W, MLQ_Q4_K, out, n); }
+void q5_k_dequantize_row(const uint8_t *W, float *out, int n) { mlq_dequantize(W, MLQ_Q5_K, out, n); }
+void q8_0_dequantize_row(const uint8_t *W, float *out, int n) { mlq_dequantize(W, MLQ_Q8_0, out, n); }
+
+void batch_qkv_omp(const uint8_t *Wq, const uint8_t *Wk, const uint8_t *Wv, const float *x,
+                   float *out_q, float *out_k, float *out_v, int nq, int nk, int nv, int n_cols,
+                   int qtype_q, int qtype_k, int qtype_v) {
+    mlq_matmul(Wq, qtype_q, x, out_q, nq, n_cols, 1);
+    mlq_matmul(Wk, qtype_k, x, out_k, nk, n_cols, 1);
+    mlq_matmul(Wv, qtype_v, x, out_v, nv, n_cols, 1);
+}
+
+void batch_gate_up_omp(const uint8_t *Wg, const uint8_t *Wu, const float *x, float *out_gate, float *out_up,
+                       int ng, int nu, int n_cols, int qtype_g, int qtype_u) {
+    mlq_matmul(Wg, qtype_g, x, out_gate, ng, n_cols, 1);
+    mlq_matmul(Wu, qtype_u, x, out_up, nu, n_cols, 1);
+}
+
+void batch_matmul(const uint8_t *w[7], const float *x, float *out[7], int nrows[7], int ncols[7], int ts[7],
+                  int n_proj) {
+    for (int p = 0; p < n_proj && p < 7; p++)
+        mlq_matmul(w[p], ts[p] == 20 ? MLQ_Q4_1 : MLQ_Q4_0, x, out[p], nrows[p], ncols[p], 1);
+}
+
+int get_max_threads(void) { return 1; }
+void set_num_threads(int n) { (void)n; }

@@ -1,0 +1,577 @@
+// Quantized GEMV / skinny GEMM (B <= 8 activation rows per launch) for sm_100a.
+//
+// Replaces the reference's per-format OpenMP row loops
+// (quant_kernels_omp.c:135-734 *_matmul_omp, 1355-1388 quant_matmul_omp;
+//  cengine_batch_instr.c:68-534 *_batch_matmul).
+//
+// Data layout in HBM: W is the GGUF tensor as-is, rows of K/BE blocks back to back,
+// so the whole matrix is one contiguous byte stream of N*row_bytes.  A persistent
+// CTA walks tiles of `rpt` rows; each tile is a contiguous byte range.
+//
+// CTA = 9 warps.  Warp 8 is the producer: it streams each tile's 16-byte-aligned
+// interior into a 4-stage shared-memory ring with one cp.async.bulk (TMA engine,
+// L2 evict_first) per tile and fetches the <=15-byte ragged head/tail with plain
+// loads; full/empty mbarriers hand stages to the 8 decode warps.  The decode warps
+// first encode the activation rows as int8 "x planes" (formats.cuh) in shared
+// memory, then decode weight blocks straight from the staged bytes into packed
+// int8 and reduce with dp4a, fp32 per-block scaling and warp shuffles.  When a tile
+// holds fewer than 8 rows, 8/rpt warps split each row and combine through smem.
+//
+// Roofline: HBM-bound.  Algorithmic bytes per launch = N*row_bytes + B*K*4 + B*N*4.
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "formats.cuh"
+#include "mlq_internal.h"
+#include "pipeline.cuh"
+
+namespace mlq {
+
+static constexpr int kStages = 4;
+static constexpr int kConsumerWarps = 8;
+static constexpr int kThreads = (kConsumerWarps + 1) * 32;
+static constexpr int kMaxSmem = 232448;     // 227 KB opt-in per CTA on sm_100
+static constexpr int kStageTarget = 24576;  // bytes of weights per stage
+
+int block_elems(int qt) {
+    switch (qt) {
+        case MLQ_F32: case MLQ_F16: case MLQ_BF16: return 1;
+        case MLQ_Q4_0: case MLQ_Q4_1: case MLQ_Q5_0: case MLQ_Q8_0: case MLQ_MXFP4: case MLQ_MXFP4_REF: return 32;
+        case MLQ_Q4_K: case MLQ_Q5_K: case MLQ_Q6_K: return 256;
+        default: return 0;
+    }
+}
+
+int block_bytes(int qt) {
+    switch (qt) {
+        case MLQ_F32: return 4;
+        case MLQ_F16: case MLQ_BF16: return 2;
+        case MLQ_Q4_0: return 18;
+        case MLQ_Q4_1: return 20;
+        case MLQ_Q5_0: return 22;
+        case MLQ_Q8_0: return 34;
+        case MLQ_MXFP4: case MLQ_MXFP4_REF: return 17;
+        case MLQ_Q4_K: return 144;
+        case MLQ_Q5_K: return 176;
+        case MLQ_Q6_K: return 210;
+        default: return 0;
+    }
+}
+
+bool is_quant_type(int qt) { return block_elems(qt) > 1; }
+
+struct GemvArgs {
+    const uint8_t *W;
+    const float *x;
+    float *out;
+    int n_rows, K, nb_x;
+    long long row_bytes, total_bytes;
+    int rpt, wpr, n_tiles, stage_bytes;
+    int *status;
+};
+
+struct GemvLayout {
+    int off_bar, off_flag, off_xh, off_xl, off_xs, off_xsum, off_red, off_stage, total;
+};
+
+__host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline GemvLayout gemv_layout(int M, int K, int stage_bytes) {
+    GemvLayout L;
+    int o = 0;
+    L.off_bar = o;  o += 2 * kStages * 8;
+    L.off_flag = o; o += 16;
+    o = align_up(o, 128);
+    L.off_xh = o;   o = align_up(o + M * K, 16);
+    L.off_xl = o;   o = align_up(o + M * K, 16);
+    L.off_xs = o;   o += M * (K / 32) * 4;
+    L.off_xsum = o; o = align_up(o + M * (K / 32) * 4, 16);
+    L.off_red = o;  o = align_up(o + 2 * kConsumerWarps * M * 4, 128);
+    L.off_stage = o; o += kStages * stage_bytes;
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ void raise_status(int *status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+// Encode activation rows [nb_x][K] into int8 planes + scales (formats.cuh).
+template <int M>
+__device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, int8_t *xh, int8_t *xl,
+                                float *xs, float *xsum, int warp, int lane, int nwarps) {
+    const int kb_per_row = K / 32;
+    for (int blk = warp; blk < M * kb_per_row; blk += nwarps) {
+        const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
+        const float v = (m < nb_x) ? __ldg(x + (size_t)m * K + 32 * kb + lane) : 0.0f;
+        float amax = fabsf(v), sum = v;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        }
+        int h = 0, l = 0;
+        float scale;
+        if (amax > 0.0f && amax <= 3.402823466e38f) {
+            const float s = amax / 127.0f;
+            const float t = v / s;
+            const float hh = rintf(t);
+            h = (int)hh;
+            l = (int)rintf((t - hh) * 254.0f);
+            scale = s / 254.0f;
+        } else {
+            scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
+        }
+        xh[(size_t)m * K + 32 * kb + lane] = (int8_t)h;
+        xl[(size_t)m * K + 32 * kb + lane] = (int8_t)l;
+        if (lane == 0) {
+            xs[blk] = scale;
+            xsum[blk] = sum;
+        }
+    }
+}
+
+template <int QT, int M>
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvLayout L = gemv_layout(M, a.K, a.stage_bytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const long long rb = a.row_bytes;
+    const long long tile_bytes = (long long)a.rpt * rb;
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------------ producer warp
+        const uint64_t pol = policy_evict_first();
+        for (int it = 0; it < n_iter; ++it) {
+            const int s = it % kStages;
+            if (it >= kStages) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok || *abort_flag) {
+                    if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
+                    break;
+                }
+            }
+            const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+            const long long b0 = tile * tile_bytes;
+            const long long b1 = min(b0 + tile_bytes, a.total_bytes);
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b0;
+            const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b1;
+            const uintptr_t gd = g0 & ~uintptr_t(15);
+            const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15);
+            const uintptr_t i1 = g1 & ~uintptr_t(15);
+            uint8_t *st = smem + L.off_stage + s * a.stage_bytes;
+            if (i1 > i0) {
+                if (g0 + lane < i0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+                if (i1 + lane < g1) st[i1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(i1 + lane));
+            } else {
+                if (g0 + lane < g1) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+            }
+            __syncwarp();
+            if (lane == 0) {
+                if (i1 > i0) {
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(i1 - i0));
+                    bulk_g2s(st + (i0 - gd), reinterpret_cast<const void *>(i0), (uint32_t)(i1 - i0), &full[s], pol);
+                } else {
+                    mbar_arrive(&full[s]);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- decode warps
+    int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
+    int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
+    float *xs = reinterpret_cast<float *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
+    float *red = reinterpret_cast<float *>(smem + L.off_red);
+    encode_x_planes<M>(a.x, a.nb_x, a.K, xh, xl, xs, xsum, warp, lane, kConsumerWarps);
+    named_bar_sync(1, kConsumerWarps * 32);
+
+    XPlanes xp{xh, xl, xs, xsum, a.K};
+    const int rr = warp / a.wpr, part = warp - rr * a.wpr;
+    const int U = a.K / Fmt<QT>::UE;
+    for (int it = 0; it < n_iter; ++it) {
+        const int s = it % kStages;
+        bool ok = true;
+        if (!*abort_flag) {
+            if (lane == 0) ok = mbar_wait_bounded(&full[s], (it / kStages) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok && lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
+        } else {
+            ok = false;
+        }
+        const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+        const int row0 = (int)(tile * a.rpt);
+        const int row = row0 + rr;
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[m] = 0.0f;
+        if (ok && row < a.n_rows) {
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(tile * tile_bytes);
+            const uint8_t *rowp = smem + L.off_stage + s * a.stage_bytes + (g0 & 15) + (size_t)rr * rb;
+            for (int u = part * 32 + lane; u < U; u += 32 * a.wpr) Unit<QT, M>::dot(rowp, u, xp, acc);
+        }
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&empty[s]);
+        if (a.wpr == 1) {
+            if (lane == 0 && ok && row < a.n_rows) {
+#pragma unroll
+                for (int m = 0; m < M; m++)
+                    if (m < a.nb_x) a.out[(size_t)m * a.n_rows + row] = acc[m];
+            }
+        } else {
+            float *rd = red + (it & 1) * kConsumerWarps * M;
+            if (lane == 0) {
+#pragma unroll
+                for (int m = 0; m < M; m++) rd[warp * M + m] = acc[m];
+            }
+            named_bar_sync(1, kConsumerWarps * 32);
+            if ((int)threadIdx.x < a.rpt * M && ok) {
+                const int r = threadIdx.x / M, m = threadIdx.x - r * M;
+                float sum = 0.0f;
+                for (int p = 0; p < a.wpr; p++) sum += rd[(r * a.wpr + p) * M + m];
+                if (row0 + r < a.n_rows && m < a.nb_x) a.out[(size_t)m * a.n_rows + row0 + r] = sum;
+            }
+        }
+    }
+}
+
+// fp32 / fp16 / bf16 weights: one warp per row, 16-byte vector loads.
+template <typename WT> __device__ __forceinline__ float to_f(WT v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename WT, int M>
+__global__ void __launch_bounds__(256) k_gemv_float(const WT *__restrict__ W, const float *__restrict__ x,
+                                                    float *__restrict__ out, int n_rows, int K, int nb_x,
+                                                    int vec_ok) {
+    constexpr int V = 16 / sizeof(WT);
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int row = gw; row < n_rows; row += nw) {
+        const WT *wr = W + (size_t)row * K;
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[m] = 0.0f;
+        if (vec_ok) {
+            for (int k0 = lane * V; k0 < K; k0 += 32 * V) {
+                union { int4 v; WT e[V]; } wv;
+                wv.v = __ldcs(reinterpret_cast<const int4 *>(wr + k0));
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    if (m < nb_x) {
+                        const float *xr = x + (size_t)m * K + k0;
+#pragma unroll
+                        for (int j = 0; j < V; j += 4) {
+                            const float4 xv = __ldg(reinterpret_cast<const float4 *>(xr + j));
+                            acc[m] = fmaf(to_f<WT>(wv.e[j + 0]), xv.x, acc[m]);
+                            acc[m] = fmaf(to_f<WT>(wv.e[j + 1]), xv.y, acc[m]);
+                            acc[m] = fmaf(to_f<WT>(wv.e[j + 2]), xv.z, acc[m]);
+                            acc[m] = fmaf(to_f<WT>(wv.e[j + 3]), xv.w, acc[m]);
+                        }
+                    }
+                }
+            }
+        } else {
+            for (int k = lane; k < K; k += 32) {
+                const float wv = to_f<WT>(wr[k]);
+#pragma unroll
+                for (int m = 0; m < M; m++)
+                    if (m < nb_x) acc[m] = fmaf(wv, __ldg(x + (size_t)m * K + k), acc[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < M; m++)
+                if (m < nb_x) out[(size_t)m * n_rows + row] = acc[m];
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------ launchers
+template <int QT, int M>
+static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, int K, int nb_x,
+                      cudaStream_t s) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
+    int rpt = (int)(kStageTarget / rb);
+    rpt = rpt < 1 ? 1 : (rpt > 8 ? 8 : rpt);
+    rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
+    while (rpt > 1 && (n_rows + rpt - 1) / rpt < 2 * c->num_sms) rpt >>= 1;
+    const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
+    const GemvLayout L = gemv_layout(M, K, stage_bytes);
+    if (L.total > kMaxSmem) return MLQ_ERR_CAPACITY;
+    auto kern = k_gemv_q<QT, M>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+            return MLQ_ERR_CUDA;
+        attr_set = true;
+    }
+    int per_sm = 0;
+    if (!MLQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L.total)))
+        return MLQ_ERR_CUDA;
+    if (per_sm < 1) per_sm = 1;
+    GemvArgs a;
+    a.W = W;
+    a.x = x;
+    a.out = out;
+    a.n_rows = n_rows;
+    a.K = K;
+    a.nb_x = nb_x;
+    a.row_bytes = rb;
+    a.total_bytes = rb * n_rows;
+    a.rpt = rpt;
+    a.wpr = kConsumerWarps / rpt;
+    a.n_tiles = (n_rows + rpt - 1) / rpt;
+    a.stage_bytes = stage_bytes;
+    a.status = c->d_status;
+    const int grid = a.n_tiles < per_sm * c->num_sms ? a.n_tiles : per_sm * c->num_sms;
+    kern<<<grid, kThreads, L.total, s>>>(a);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+template <int QT>
+static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
+    for (int b = 0; b < B;) {
+        const int left = B - b;
+        int rc;
+        int take;
+        // widest M whose x planes still fit next to the stage ring
+        if (left >= 5 && gemv_layout(8, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            take = left < 8 ? left : 8;
+            rc = launch_q_m<QT, 8>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+        } else if (left >= 4 && gemv_layout(4, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            take = 4;
+            rc = launch_q_m<QT, 4>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+        } else if (left == 3 && gemv_layout(3, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            take = 3;
+            rc = launch_q_m<QT, 3>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+        } else if (left >= 2 && gemv_layout(2, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            take = 2;
+            rc = launch_q_m<QT, 2>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+        } else {
+            take = 1;
+            rc = launch_q_m<QT, 1>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+        }
+        if (rc != MLQ_OK) {
+            if (rc == MLQ_ERR_CAPACITY) set_error(rc, "K=%d too large for the shared-memory stage ring", K);
+            return rc;
+        }
+        b += take;
+    }
+    return MLQ_OK;
+}
+
+template <typename WT>
+static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    const WT *w = reinterpret_cast<const WT *>(W);
+    const int V = 16 / sizeof(WT);
+    const int vec_ok = (K % V == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((K * 4) % 16 == 0);
+    const int warps = n_rows;
+    int grid = (warps * 32 + 255) / 256;
+    const int cap = c->num_sms * 8;
+    if (grid > cap) grid = cap;
+    for (int b = 0; b < B; b += 4) {
+        const int take = (B - b) < 4 ? (B - b) : 4;
+        const float *xb = x + (size_t)b * K;
+        float *ob = out + (size_t)b * n_rows;
+        if (take == 1) k_gemv_float<WT, 1><<<grid, 256, 0, s>>>(w, xb, ob, n_rows, K, take, vec_ok);
+        else if (take == 2) k_gemv_float<WT, 2><<<grid, 256, 0, s>>>(w, xb, ob, n_rows, K, take, vec_ok);
+        else k_gemv_float<WT, 4><<<grid, 256, 0, s>>>(w, xb, ob, n_rows, K, take, vec_ok);
+        count_launch();
+    }
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int B,
+                  size_t w_bytes, cudaStream_t s) {
+    (void)w_bytes;
+    switch (qt) {
+        case MLQ_F32: return launch_float<float>(W, x, out, n_rows, K, B, s);
+        case MLQ_F16: return launch_float<__half>(W, x, out, n_rows, K, B, s);
+        case MLQ_BF16: return launch_float<__nv_bfloat16>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q4_0: return launch_q<MLQ_Q4_0>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q4_1: return launch_q<MLQ_Q4_1>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q5_0: return launch_q<MLQ_Q5_0>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q8_0: return launch_q<MLQ_Q8_0>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q4_K: return launch_q<MLQ_Q4_K>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q5_K: return launch_q<MLQ_Q5_K>(W, x, out, n_rows, K, B, s);
+        case MLQ_Q6_K: return launch_q<MLQ_Q6_K>(W, x, out, n_rows, K, B, s);
+        case MLQ_MXFP4: return launch_q<MLQ_MXFP4>(W, x, out, n_rows, K, B, s);
+        case MLQ_MXFP4_REF: return launch_q<MLQ_MXFP4_REF>(W, x, out, n_rows, K, B, s);
+        default:
+            set_error(MLQ_ERR_TYPE, "unsupported quant type %d", qt);
+            return MLQ_ERR_TYPE;
+    }
+}
+
+// ------------------------------------------------------------------------------ dequantize
+// One thread per output element, bit-exact with the reference's *_dequantize_row and
+// gguf-py: every product/difference is rounded separately (no FMA contraction).
+__device__ __forceinline__ float f16_g(const uint8_t *p) {
+    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+__global__ void k_dequant(const uint8_t *__restrict__ W, int qt, float *__restrict__ out, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        switch (qt) {
+            case MLQ_F32: v = reinterpret_cast<const float *>(W)[i]; break;
+            case MLQ_F16: v = __half2float(reinterpret_cast<const __half *>(W)[i]); break;
+            case MLQ_BF16: v = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(W)[i]); break;
+            case MLQ_Q8_0: {
+                const uint8_t *bp = W + (i >> 5) * 34;
+                v = __fmul_rn((float)(int8_t)bp[2 + (i & 31)], f16_g(bp));
+            } break;
+            case MLQ_Q4_0: case MLQ_Q4_1: case MLQ_Q5_0: {
+                const int bb = qt == MLQ_Q4_0 ? 18 : qt == MLQ_Q4_1 ? 20 : 22;
+                const int hdr = qt == MLQ_Q4_0 ? 2 : qt == MLQ_Q4_1 ? 4 : 6;
+                const uint8_t *bp = W + (i >> 5) * bb;
+                const int j = (int)(i & 31);
+                int q = (j < 16) ? (bp[hdr + j] & 0xF) : (bp[hdr + j - 16] >> 4);
+                const float d = f16_g(bp);
+                if (qt == MLQ_Q4_0) v = __fmul_rn((float)(q - 8), d);
+                else if (qt == MLQ_Q4_1) v = __fadd_rn(__fmul_rn((float)q, d), f16_g(bp + 2));
+                else {
+                    const uint32_t qh = bp[2] | (bp[3] << 8) | (bp[4] << 16) | ((uint32_t)bp[5] << 24);
+                    q |= ((qh >> j) & 1) << 4;
+                    v = __fmul_rn((float)(q - 16), d);
+                }
+            } break;
+            case MLQ_Q4_K: case MLQ_Q5_K: {
+                const int bb = qt == MLQ_Q4_K ? 144 : 176;
+                const uint8_t *bp = W + (i >> 8) * bb;
+                const int e = (int)(i & 255), sub = e >> 5, l = e & 31, g = sub >> 1;
+                const uint8_t *sc = bp + 4;
+                uint32_t s, m;
+                if (sub < 4) { s = sc[sub] & 63; m = sc[sub + 4] & 63; }
+                else { s = (sc[sub + 4] & 0xF) | ((sc[sub - 4] >> 6) << 4); m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4); }
+                const uint8_t *qs = bp + (qt == MLQ_Q4_K ? 16 : 48) + 32 * g;
+                int q = (sub & 1) ? (qs[l] >> 4) : (qs[l] & 0xF);
+                if (qt == MLQ_Q5_K) q += ((bp[16 + l] >> sub) & 1) << 4;
+                const float ds = __fmul_rn(f16_g(bp), (float)s);
+                const float dm = __fmul_rn(f16_g(bp + 2), (float)m);
+                v = __fsub_rn(__fmul_rn(ds, (float)q), dm);
+            } break;
+            case MLQ_Q6_K: {
+                const uint8_t *bp = W + (i >> 8) * 210;
+                const int e = (int)(i & 255), h = e >> 7, r = e & 127, quad = r >> 5, l = r & 31;
+                const uint8_t qlb = bp[64 * h + l + ((quad & 1) ? 32 : 0)];
+                const int lo = (quad < 2) ? (qlb & 0xF) : (qlb >> 4);
+                const int hi = (bp[128 + 32 * h + l] >> (2 * quad)) & 3;
+                const float ds = __fmul_rn(f16_g(bp + 208), (float)(int8_t)bp[192 + (e >> 4)]);
+                v = __fmul_rn(ds, (float)((lo | (hi << 4)) - 32));
+            } break;
+            case MLQ_MXFP4: {
+                const uint8_t *bp = W + (i >> 5) * 17;
+                const int j = (int)(i & 31);
+                const int nib = (j < 16) ? (bp[1 + j] & 0xF) : (bp[1 + j - 16] >> 4);
+                const int kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+                v = __fmul_rn((float)kv[nib], e8m0_half(bp[0]));
+            } break;
+            case MLQ_MXFP4_REF: {
+                const uint8_t *bp = W + (i >> 5) * 17;
+                const int j = (int)(i & 31);
+                int nib = (j & 1) ? (bp[j >> 1] >> 4) : (bp[j >> 1] & 0xF);
+                if (nib > 7) nib -= 16;
+                v = __fmul_rn((float)nib, __uint_as_float((uint32_t)bp[16] << 23));
+            } break;
+            default: break;
+        }
+        out[i] = v;
+    }
+}
+
+int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStream_t s) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    long long blocks = (n + 255) / 256;
+    if (blocks > (long long)c->num_sms * 32) blocks = (long long)c->num_sms * 32;
+    if (blocks < 1) blocks = 1;
+    k_dequant<<<(int)blocks, 256, 0, s>>>(W, qt, out, n);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------------------ Q8_0 quantizer
+// quantize_row_q8_0 (quant_kernels_omp.c:1406-1455): d = amax/127 (1 if 0), id = 1/d,
+// q = round-half-even(clamp(x*id, -127, 127)), d as f16 (round to nearest even).
+__global__ void k_quantize_q8_0(const float *__restrict__ x, uint8_t *__restrict__ q8, long long nblk) {
+    const int lane = threadIdx.x & 31;
+    for (long long b = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; b < nblk;
+         b += ((long long)gridDim.x * blockDim.x) >> 5) {
+        const float v = x[b * 32 + lane];
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        float d = __fdiv_rn(amax, 127.0f);
+        if (d == 0.0f) d = 1.0f;
+        const float id = __fdiv_rn(1.0f, d);
+        const float t = fminf(fmaxf(__fmul_rn(v, id), -127.0f), 127.0f);
+        uint8_t *dst = q8 + b * 34;
+        dst[2 + lane] = (uint8_t)(int8_t)__float2int_rn(t);
+        if (lane == 0) {
+            const unsigned short h = __half_as_ushort(__float2half_rn(d));
+            dst[0] = (uint8_t)(h & 0xFF);
+            dst[1] = (uint8_t)(h >> 8);
+        }
+    }
+}
+
+int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    const long long nblk = n / 32;
+    long long blocks = (nblk * 32 + 255) / 256;
+    if (blocks > (long long)c->num_sms * 16) blocks = (long long)c->num_sms * 16;
+    if (blocks < 1) blocks = 1;
+    k_quantize_q8_0<<<(int)blocks, 256, 0, s>>>(x, q8, nblk);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s) {
+    return launch_dequantize(x_q8, MLQ_Q8_0, x, n, s);
+}
+
+}  // namespace mlq

@@ -1,0 +1,79 @@
+// Internal runtime shared by the CUDA translation units of libmojollama_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/mojollama_b200.h"
+
+namespace mlq {
+
+// ---- errors ---------------------------------------------------------------------------
+void set_error(int code, const char *fmt, ...);
+inline bool cuda_ok(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    set_error(MLQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+#define MLQ_CUDA(call) ::mlq::cuda_ok((call), #call)
+
+// ---- device context ------------------------------------------------------------------
+struct Ctx {
+    int device = -1;
+    int num_sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;   // where launches go (own or user-bound)
+    int *d_status = nullptr;         // device error word (0 = ok), written by bounded waits
+};
+Ctx *ctx();                          // current device's context (initialises on first use)
+cudaStream_t stream();
+int *dev_status();
+void count_launch(int n = 1);
+bool ref_compat();
+
+// ---- pointer handling ------------------------------------------------------------------
+bool is_device_ptr(const void *p);
+
+// Per-call staging for host activations/outputs.  Reset by CallScope.
+struct CallScope {
+    CallScope();
+    ~CallScope();
+    // device view of an input; copies host data in when needed
+    const void *in(const void *p, size_t bytes);
+    // device view of an output; host outputs are copied back in finish()
+    void *out(void *p, size_t bytes);
+    // device view of an in/out buffer (copied in and back)
+    void *inout(void *p, size_t bytes);
+    // device scratch (uninitialised) for this call
+    void *scratch(size_t bytes);
+    // weights: device pointers pass through, host pointers go through the residency cache
+    const void *weights(const void *p, size_t bytes);
+    // copy host outputs back and synchronise when anything was host; returns MLQ_OK or error
+    int finish();
+    bool failed = false;
+    bool any_host = false;
+
+  private:
+    struct Pending { void *host; void *dev; size_t bytes; };
+    Pending pending_[64];
+    int n_pending_ = 0;
+    size_t arena_used_ = 0;
+    void *stage(size_t bytes);
+};
+
+// ---- launchers implemented in the .cu files --------------------------------------------
+int block_elems(int qt);
+int block_bytes(int qt);
+bool is_quant_type(int qt);
+
+// W, x, out are device pointers here.
+int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int n_cols,
+                  int B, size_t w_bytes, cudaStream_t s);
+int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStream_t s);
+int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
+int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
+
+}  // namespace mlq

@@ -1,0 +1,374 @@
+// Runtime of libmojollama_b200.so: device contexts, the library stream, the
+// thread-local error state, host-pointer staging and the weight residency cache.
+//
+// The reference C engine is called with host pointers from numpy
+// (src/mojollama/kernels/turbo_engine_v7_moe.py:240-423 of the reference) and
+// returns when its outputs are written.  Here a host weight buffer is copied to
+// HBM once and kept (keyed by address and size, like the reference's weights
+// that stay mmapped for the life of the engine), activations are staged through
+// a per-device arena, and a call that touched host memory synchronises before
+// returning.  Calls whose pointers are all device memory stay asynchronous.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "mlq_internal.h"
+
+namespace mlq {
+
+// ------------------------------------------------------------------------------ errors
+static thread_local int t_err = MLQ_OK;
+static thread_local char t_msg[512] = {0};
+
+void set_error(int code, const char *fmt, ...) {
+    t_err = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+    va_end(ap);
+    if (getenv("MLQ_VERBOSE")) fprintf(stderr, "[mojollama_b200] error %d: %s\n", code, t_msg);
+}
+
+// ------------------------------------------------------------------------------ contexts
+static const int kMaxDev = 16;
+static Ctx g_ctx[kMaxDev];
+static std::mutex g_mu;
+static thread_local int t_dev = -1;
+static std::atomic<unsigned long long> g_launches{0};
+static std::atomic<int> g_compat{-1};
+
+void count_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+bool ref_compat() {
+    int v = g_compat.load();
+    if (v < 0) {
+        const char *e = getenv("MLQ_REF_COMPAT");
+        v = (e && atoi(e) != 0) ? 1 : 0;
+        g_compat.store(v);
+    }
+    return v != 0;
+}
+
+static bool init_device(int dev) {
+    if (dev < 0 || dev >= kMaxDev) {
+        set_error(MLQ_ERR_ARG, "device %d out of range", dev);
+        return false;
+    }
+    Ctx &c = g_ctx[dev];
+    if (c.device == dev) return true;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= dev) {
+        cudaGetLastError();
+        set_error(MLQ_ERR_NO_DEVICE, "no CUDA device %d (count %d)", dev, n);
+        return false;
+    }
+    if (!MLQ_CUDA(cudaSetDevice(dev))) return false;
+    int sms = 0;
+    if (!MLQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return false;
+    cudaStream_t s = nullptr;
+    if (!MLQ_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking))) return false;
+    int *st = nullptr;
+    if (!MLQ_CUDA(cudaMalloc(&st, 64))) return false;
+    if (!MLQ_CUDA(cudaMemset(st, 0, 64))) return false;
+    c.num_sms = sms;
+    c.own_stream = s;
+    c.stream = s;
+    c.d_status = st;
+    c.device = dev;
+    return true;
+}
+
+Ctx *ctx() {
+    if (t_dev < 0) {
+        int d = 0;
+        if (cudaGetDevice(&d) != cudaSuccess) { cudaGetLastError(); d = 0; }
+        t_dev = d;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!init_device(t_dev)) return nullptr;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != t_dev) cudaSetDevice(t_dev);
+    return &g_ctx[t_dev];
+}
+
+cudaStream_t stream() {
+    Ctx *c = ctx();
+    return c ? c->stream : nullptr;
+}
+
+int *dev_status() {
+    Ctx *c = ctx();
+    return c ? c->d_status : nullptr;
+}
+
+bool is_device_ptr(const void *p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// ------------------------------------------------------------------------------ residency cache
+struct CacheEntry { void *dev; size_t bytes; };
+static std::map<std::pair<uintptr_t, size_t>, CacheEntry> g_cache[kMaxDev];
+static size_t g_cache_bytes[kMaxDev];
+
+static const void *resident(const void *host, size_t bytes) {
+    Ctx *c = ctx();
+    if (!c) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto key = std::make_pair((uintptr_t)host, bytes);
+    auto &m = g_cache[c->device];
+    auto it = m.find(key);
+    if (it != m.end()) return it->second.dev;
+    void *d = nullptr;
+    // pad so that 16-byte vector reads of the last block stay inside the allocation
+    if (!MLQ_CUDA(cudaMalloc(&d, bytes + 256))) return nullptr;
+    if (!MLQ_CUDA(cudaMemcpyAsync(d, host, bytes, cudaMemcpyHostToDevice, c->stream))) {
+        cudaFree(d);
+        return nullptr;
+    }
+    cudaMemsetAsync((char *)d + bytes, 0, 256, c->stream);
+    m[key] = CacheEntry{d, bytes};
+    g_cache_bytes[c->device] += bytes;
+    return d;
+}
+
+// ------------------------------------------------------------------------------ staging arena
+struct Arena {
+    std::vector<std::pair<char *, size_t>> chunks;   // [0] is the main chunk
+    size_t off = 0;                                  // offset in the last chunk
+    int depth = 0;
+};
+static Arena g_arena[kMaxDev];
+
+static void arena_begin(Ctx *c) {
+    Arena &a = g_arena[c->device];
+    if (a.depth++ > 0) return;
+    if (a.chunks.size() > 1) {
+        // grew during the previous call: wait for its work, then consolidate
+        cudaStreamSynchronize(c->stream);
+        size_t total = 0;
+        for (auto &ch : a.chunks) { total += ch.second; cudaFree(ch.first); }
+        a.chunks.clear();
+        char *p = nullptr;
+        if (cudaMalloc(&p, total) == cudaSuccess) a.chunks.push_back({p, total});
+        else cudaGetLastError();
+    }
+    a.off = 0;
+}
+
+static void arena_end(Ctx *c) {
+    Arena &a = g_arena[c->device];
+    if (a.depth > 0) a.depth--;
+}
+
+static void *arena_alloc(Ctx *c, size_t bytes) {
+    Arena &a = g_arena[c->device];
+    bytes = (bytes + 255) & ~(size_t)255;
+    if (!a.chunks.empty() && a.off + bytes <= a.chunks.back().second) {
+        void *p = a.chunks.back().first + a.off;
+        a.off += bytes;
+        return p;
+    }
+    size_t want = bytes < ((size_t)64 << 20) ? ((size_t)64 << 20) : bytes;
+    char *p = nullptr;
+    if (!MLQ_CUDA(cudaMalloc(&p, want))) return nullptr;
+    a.chunks.push_back({p, want});
+    a.off = bytes;
+    return p;
+}
+
+CallScope::CallScope() {
+    Ctx *c = ctx();
+    if (!c) { failed = true; return; }
+    arena_begin(c);
+}
+
+CallScope::~CallScope() {
+    Ctx *c = ctx();
+    if (c) arena_end(c);
+}
+
+void *CallScope::stage(size_t bytes) {
+    Ctx *c = ctx();
+    if (!c) { failed = true; return nullptr; }
+    void *p = arena_alloc(c, bytes ? bytes : 1);
+    if (!p) failed = true;
+    return p;
+}
+
+const void *CallScope::in(const void *p, size_t bytes) {
+    if (failed || !p) return nullptr;
+    if (is_device_ptr(p)) return p;
+    any_host = true;
+    void *d = stage(bytes);
+    if (!d) return nullptr;
+    if (bytes && !MLQ_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, stream()))) {
+        failed = true;
+        return nullptr;
+    }
+    return d;
+}
+
+void *CallScope::out(void *p, size_t bytes) {
+    if (failed || !p) return nullptr;
+    if (is_device_ptr(p)) return p;
+    any_host = true;
+    void *d = stage(bytes);
+    if (!d) return nullptr;
+    if (n_pending_ >= 64) { set_error(MLQ_ERR_CAPACITY, "too many host outputs"); failed = true; return nullptr; }
+    pending_[n_pending_++] = Pending{p, d, bytes};
+    return d;
+}
+
+void *CallScope::inout(void *p, size_t bytes) {
+    if (failed || !p) return nullptr;
+    if (is_device_ptr(p)) return p;
+    void *d = const_cast<void *>(in(p, bytes));
+    if (!d) return nullptr;
+    if (n_pending_ >= 64) { set_error(MLQ_ERR_CAPACITY, "too many host outputs"); failed = true; return nullptr; }
+    pending_[n_pending_++] = Pending{p, d, bytes};
+    return d;
+}
+
+void *CallScope::scratch(size_t bytes) { return failed ? nullptr : stage(bytes); }
+
+const void *CallScope::weights(const void *p, size_t bytes) {
+    if (failed || !p) return nullptr;
+    if (is_device_ptr(p)) return p;
+    any_host = true;
+    const void *d = resident(p, bytes);
+    if (!d) failed = true;
+    return d;
+}
+
+int CallScope::finish() {
+    cudaStream_t s = stream();
+    if (failed) {
+        if (s) cudaStreamSynchronize(s);
+        return mlq_last_error() ? mlq_last_error() : MLQ_ERR_CUDA;
+    }
+    for (int i = 0; i < n_pending_; i++) {
+        if (!MLQ_CUDA(cudaMemcpyAsync(pending_[i].host, pending_[i].dev, pending_[i].bytes,
+                                      cudaMemcpyDeviceToHost, s)))
+            return MLQ_ERR_CUDA;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(MLQ_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+        return MLQ_ERR_CUDA;
+    }
+    if (any_host) {
+        if (!MLQ_CUDA(cudaStreamSynchronize(s))) return MLQ_ERR_CUDA;
+    }
+    return MLQ_OK;
+}
+
+}  // namespace mlq
+
+// ====================================================================================== C-ABI
+using namespace mlq;
+
+extern "C" {
+
+int mlq_last_error(void) { return t_err; }
+const char *mlq_last_error_message(void) { return t_msg; }
+void mlq_clear_error(void) { t_err = MLQ_OK; t_msg[0] = 0; }
+
+int mlq_init(int device) {
+    t_dev = device;
+    return ctx() ? MLQ_OK : mlq_last_error();
+}
+
+int mlq_set_device(int device) { return mlq_init(device); }
+int mlq_get_device(void) { return t_dev < 0 ? 0 : t_dev; }
+
+void *mlq_get_stream(void) { return (void *)stream(); }
+
+int mlq_set_stream(void *s) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    cudaStream_t ns = (cudaStream_t)s;   // 0 = the legacy default stream, as in CUDA
+    if (ns != c->stream) cudaStreamSynchronize(c->stream);   // keep the arena's stream ordering
+    c->stream = ns;
+    return MLQ_OK;
+}
+
+int mlq_use_own_stream(void) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    if (c->stream != c->own_stream) cudaStreamSynchronize(c->stream);
+    c->stream = c->own_stream;
+    return MLQ_OK;
+}
+
+int mlq_device_status(void) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    int h = 0;
+    if (!MLQ_CUDA(cudaMemcpyAsync(&h, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream)))
+        return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaStreamSynchronize(c->stream))) return MLQ_ERR_CUDA;
+    if (h != 0) {
+        cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
+        cudaStreamSynchronize(c->stream);
+        set_error(MLQ_ERR_TIMEOUT, "device-side bounded wait gave up (code %d)", h);
+        return MLQ_ERR_TIMEOUT;
+    }
+    return MLQ_OK;
+}
+
+int mlq_sync(void) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    if (!MLQ_CUDA(cudaStreamSynchronize(c->stream))) return MLQ_ERR_CUDA;
+    return mlq_device_status();
+}
+
+int mlq_register_weights(const void *p, size_t bytes) {
+    if (!p || !bytes) { set_error(MLQ_ERR_ARG, "register_weights: null/empty"); return MLQ_ERR_ARG; }
+    if (is_device_ptr(p)) return MLQ_OK;
+    return resident(p, bytes) ? MLQ_OK : mlq_last_error();
+}
+
+int mlq_cache_clear(void) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    cudaStreamSynchronize(c->stream);
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto &kv : g_cache[c->device]) cudaFree(kv.second.dev);
+    g_cache[c->device].clear();
+    g_cache_bytes[c->device] = 0;
+    return MLQ_OK;
+}
+
+size_t mlq_cache_bytes(void) {
+    Ctx *c = ctx();
+    return c ? g_cache_bytes[c->device] : 0;
+}
+
+int mlq_num_sms(void) {
+    Ctx *c = ctx();
+    return c ? c->num_sms : 0;
+}
+
+unsigned long long mlq_launch_count(void) { return g_launches.load(); }
+
+int mlq_set_ref_compat(int on) {
+    g_compat.store(on ? 1 : 0);
+    return MLQ_OK;
+}
+int mlq_get_ref_compat(void) { return ref_compat() ? 1 : 0; }
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+"""Generate the golden fixtures in tests/golden/ (run in a container that has the
+reference sources and gguf-py; the fixtures themselves travel, the generators don't).
+
+    make -C oracle                      # reference C engine from its own sources
+    python tests/golden/gen_golden.py
+
+Writes
+  formats.npz  random GGUF blocks + gguf-py 0.19.0 dequantize output; gguf-py
+               quantize output (Q8_0, Q4_0, MXFP4); the reference's
+               quantize_row_q8_0 bytes and *_dequantize_row output.
+  ref_ops.npz  outputs of the reference C engine (compiled from source, AVX2+OMP)
+               on small seeded GEMV / batch-GEMV cases, including the dispatcher
+               paths where the reference is not W.x (Q4_K type 12, Q6_K type 14),
+               kept as evidence for the reference-compat mode.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from oracle import formats as F  # noqa: E402
+
+
+def gen_formats(rng):
+    import gguf
+    from gguf import GGMLQuantizationType as T
+    from gguf import quants
+    out = {"gguf_version": np.array(gguf.__version__ if hasattr(gguf, "__version__") else "0.19.0")}
+    n = 512
+    for qt in (F.Q4_0, F.Q4_1, F.Q5_0, F.Q8_0, F.Q4_K, F.Q5_K, F.Q6_K, F.MXFP4, F.BF16):
+        raw = F.random_blocks(qt, n, rng)
+        deq = quants.dequantize(raw.reshape(1, -1), T(qt)).reshape(-1).astype(np.float32)
+        out[f"deq_raw_{qt}"] = raw
+        out[f"deq_out_{qt}"] = deq
+    x = rng.standard_normal(256).astype(np.float32)
+    out["quant_x"] = x
+    for qt in (F.Q8_0, F.Q4_0, F.MXFP4):
+        out[f"quant_gguf_{qt}"] = quants.quantize(x.reshape(1, -1), T(qt)).reshape(-1)
+    return out
+
+
+def gen_ref(rng, out):
+    from oracle.ref import RefEngine
+    ref = RefEngine()
+    ref.set_num_threads(4)
+    x = out["quant_x"]
+    out["ref_q8_0_bytes"] = ref.quantize_row_q8_0(x)
+    for qt, name in ((F.Q4_K, "q4_k"), (F.Q5_K, "q5_k"), (F.Q6_K, "q6_k"), (F.Q8_0, "q8_0")):
+        out[f"ref_deq_{qt}"] = ref.dequantize_row(name, out[f"deq_raw_{qt}"], 512)
+    ops = {}
+    n, k = 48, 512
+    for qt in (F.Q8_0, F.Q4_0, F.Q4_1, F.Q4_K, F.Q5_K, F.Q6_K, F.MXFP4_REF):
+        w = F.quantize(qt, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+        xv = rng.standard_normal(k).astype(np.float32)
+        ops[f"gemv_w_{qt}"] = w
+        ops[f"gemv_x_{qt}"] = xv
+        code = 39 if qt == F.MXFP4_REF else qt
+        ops[f"gemv_ref_dispatch_{qt}"] = ref.quant_matmul(w, xv, n, k, code)
+    b = 3
+    for qt, name in ((F.Q8_0, "q8_0"), (F.Q4_0, "q4_0"), (F.Q4_K, "q4_k"), (F.MXFP4_REF, "mxfp4")):
+        w = ops[f"gemv_w_{qt}"]
+        xb = rng.standard_normal(b * k).astype(np.float32)
+        ops[f"bgemv_x_{qt}"] = xb
+        ops[f"bgemv_ref_{qt}"] = ref.batch_matmul(name, w, xb, n, k, b)
+    ops["shape"] = np.array([n, k, b], np.int32)
+    return ops
+
+
+def main():
+    rng = np.random.default_rng(20261201)
+    fm = gen_formats(rng)
+    ops = gen_ref(rng, fm)
+    np.savez_compressed(os.path.join(HERE, "formats.npz"), **fm)
+    np.savez_compressed(os.path.join(HERE, "ref_ops.npz"), **ops)
+    print("wrote", sorted(fm)[:4], "...", len(fm), "+", len(ops), "arrays")
+
+
+if __name__ == "__main__":
+    main()
