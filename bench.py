@@ -336,8 +336,37 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_profile_case(fmt: str, rows: int, launches: int = 3) -> int:
+    """Small single-kernel case for `ncu --set full`: one format, `rows` x 2048, M=1,
+    two warm-up launches then `launches` more.  Default 65536 rows keeps every matrix
+    above the 126 MB L2 for Q8_0 (142 MB) and the whole run at a few hundred MB."""
+    import torch
+    from mojollama_b200 import core
+    qt = dict(FORMATS)[fmt]
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    from mojollama_b200 import gguf_quant as Q
+    rng = np.random.default_rng(qt)
+    base = Q.quantize(qt, (rng.standard_normal(DISTINCT * K_COLS) * 0.02).astype(np.float32))
+    w = np.tile(base, -(-rows // DISTINCT))[: rows * row_bytes(qt)]
+    wd = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+    x = torch.randn(K_COLS, device="cuda")
+    out = torch.empty(rows, device="cuda")
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    for _ in range(2 + launches):
+        rc = lib.mlq_matmul(ctypes.c_void_p(wd.data_ptr()), qt, ctypes.c_void_p(x.data_ptr()),
+                            ctypes.c_void_p(out.data_ptr()), rows, K_COLS, 1)
+        assert rc == 0, lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": fmt, "rows": rows, "cols": K_COLS, "bytes_per_launch":
+                      rows * row_bytes(qt) + K_COLS * 4 + rows * 4}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile", default=None, help="run the small single-kernel ncu case for FORMAT")
+    ap.add_argument("--profile-rows", type=int, default=65536)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -348,6 +377,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile:
+        return run_profile_case(args.profile, args.profile_rows)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if world > 1:

@@ -94,6 +94,27 @@ int mlq_quantize_q8_0(const float *x, uint8_t *q8, int64_t n);
 /* W (qt) times Q8_0-quantized activations x_q8 [B][n_cols/32 blocks] */
 int mlq_matmul_q8act(const void *W, int qt, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B);
 
+/* ---- row / elementwise ops (out may equal x: in place) ---- */
+/* out = x * w / sqrt(mean(x^2) + eps) per row (w may be NULL = ones).  sanitize = 1
+   first maps NaN to 0 and clamps to +-1000 and, if res != NULL, stores that clamped
+   input there (the batch engine's pre-norm, cengine_batch_instr.c:1258-1279). */
+int mlq_rms_norm(float *out, const float *x, const float *w, int rows, int n, float eps, int sanitize, float *res);
+/* mode 0: x / (1 + exp(-x)); mode 1: the simd_ops.c:56 Pade-tanh form on the first
+   n - n%8 elements and the exact form on the tail, as the reference computes it */
+int mlq_silu(float *out, const float *x, long long n, int mode);
+/* h = silu(clamp(gate, -80, 80)) * up   (quant_kernels_omp.c:2157-2164) */
+int mlq_swiglu(float *h, const float *gate, const float *up, long long n);
+int mlq_add(float *out, const float *a, const float *b, long long n);
+int mlq_softmax(float *x, int rows, int n);                    /* in place, per row */
+/* interleaved-pair RoPE of simd_ops.c:122 on q [n_heads][hd] and k [n_kv_heads][hd] */
+int mlq_rope_interleaved(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos, float base);
+/* cos/sin tables [max_ctx][rope_dim/2] of cengine_batch_instr.c:674 (base 10000 there) */
+int mlq_rope_init(float *cos_t, float *sin_t, int max_ctx, int head_dim, int rope_dim, double base);
+/* NeoX half-split RoPE of cengine_batch_instr.c:686 on `rows` rows of n_heads*head_dim
+   (row_stride floats apart, 0 = packed); position per row from pos[] or pos_scalar */
+int mlq_rope_neox(float *buf, int rows, int row_stride, int n_heads, int head_dim, const int *pos, int pos_scalar,
+                  const float *cos_t, const float *sin_t, int rope_dim, int max_ctx);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,10 @@
 extern "C" {
 #endif
 
+/* The reference ships rms_norm / silu / softmax twice with different signatures
+ * (quant_kernels_omp.c vs simd_ops.c, in different .so files), so a translation
+ * unit sees one set: define MLQ_REF_ABI_SIMD_OPS for the simd_ops.so signatures. */
+#ifndef MLQ_REF_ABI_SIMD_OPS
 /* ============================ engine set (combined_engine.so & co.) ============================ */
 
 /* src/mojollama/kernels/quant_kernels_omp.c:1355  dispatch on GGUF type (0,2,3,6,8,12,13,14,39) */
@@ -65,6 +69,24 @@ void batch_matmul(const uint8_t *w[7], const float *x, float *out[7], int nrows[
 /* quant_kernels_omp.c:1030-1031 (no threads to set on the GPU; kept for the ABI) */
 int get_max_threads(void);
 void set_num_threads(int n);
+/* quant_kernels_omp.c:956 (eps 1e-5), 981, 1000, 1017 */
+void rms_norm(const float *x, const float *weight, float *out, int n);
+void silu(float *x, int n);
+void softmax(float *x, int n);
+void silu_omp(float *x, int n);
+/* cengine_batch_instr.c:674 */
+void rope_init(float *cos_table, float *sin_table, int max_ctx, int hd, int rope_dim);
+
+#else  /* MLQ_REF_ABI_SIMD_OPS */
+/* ================================== simd_ops.so set ================================== */
+/* simd_ops.c:35, 56, 77, 88, 122, 218 */
+void rms_norm(float *out, const float *x, const float *weight, int n, float eps);
+void silu(float *out, const float *x, int n);
+void residual_add(float *out, const float *a, const float *b, int n);
+void softmax(float *x, int n);
+void apply_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos, float rope_base);
+void set_num_threads(int n);
+#endif /* MLQ_REF_ABI_SIMD_OPS */
 
 #ifdef __cplusplus
 }

@@ -87,3 +87,14 @@ void batch_matmul(const uint8_t *w[7], const float *x, float *out[7], int nrows[
 
 int get_max_threads(void) { return 1; }
 void set_num_threads(int n) { (void)n; }
+
+void rms_norm(const float *x, const float *weight, float *out, int n) {
+    mlq_rms_norm(out, x, weight, 1, n, 1e-5f, 0, NULL);
+}
+void silu(float *x, int n) { mlq_silu(x, x, n, 0); }
+void softmax(float *x, int n) { mlq_softmax(x, 1, n); }
+void silu_omp(float *x, int n) { mlq_silu(x, x, n, 0); }
+void rope_init(float *cos_table, float *sin_table, int max_ctx, int hd, int rope_dim) {
+    /* the reference uses 10000^(2j/hd) with hd (not rope_dim) in the exponent */
+    mlq_rope_init(cos_table, sin_table, max_ctx, hd, rope_dim, 10000.0);
+}

@@ -96,14 +96,24 @@ __device__ __forceinline__ uint32_t spread4_to_bit4(uint32_t t) {
     return (((t & 0xFu) * 0x00204081u) & 0x01010101u) << 4;
 }
 
-// doubled-E2M1 code of each byte's low nibble (GGUF MXFP4), as signed int8 bytes
-__device__ __forceinline__ uint32_t e2m1x2_lut(uint32_t v /* low nibbles, bytes 0x0? */) {
-    const uint32_t idx = v & 0x07070707u;
-    const uint32_t t = idx | (idx >> 4);                  // nibble-compact bytes 0/1 and 2/3
-    const uint32_t sel = __byte_perm(t, 0, 0x0020);         // 4 selector nibbles
-    const uint32_t mag = __byte_perm(0x03020100u, 0x0C080604u, sel);   // {0,1,2,3,4,6,8,12}
-    const uint32_t neg = ((v & 0x08080808u) >> 3) * 0xFFu;  // 0xFF where the sign bit is set
-    return __vsub4(mag ^ neg, neg);
+// PTX prmt.b32, default mode: each selector nibble picks one of the 8 bytes of {b:a}
+// with its low 3 bits; when its bit 3 is set the picked byte's sign bit is replicated
+// over the whole result byte instead.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// Doubled-E2M1 codes (GGUF MXFP4) of the four nibbles in the low 16 bits of `sel`,
+// as signed int8 bytes in nibble order.  With P = {0,1,2,3,4,6,8,12} in {b:a}:
+// prmt(P, nib) gives the magnitude for a positive code and 0 for a negative one
+// (sign-replicate of a positive byte); prmt(P, nib ^ 8) the reverse; the code is the
+// bytewise difference.
+__device__ __forceinline__ uint32_t e2m1x2_codes(uint32_t sel) {
+    const uint32_t pos = prmt(0x03020100u, 0x0C080604u, sel);
+    const uint32_t neg = prmt(0x03020100u, 0x0C080604u, sel ^ 0x8888u);
+    return __vsub4(pos, neg);
 }
 
 // ---------------------------------------------------------------------------------- x planes
@@ -115,94 +125,123 @@ struct XPlanes {
     int K;
 };
 
-// 254 * dp4a(q, h) + dp4a(q, l) over NW words; xh/xl 16-byte aligned
+// 254 * dp4a(q, h) + dp4a(q, l) over NW words held in registers
 template <int NW>
-__device__ __forceinline__ int dot_planes(const uint32_t (&q)[NW], const int8_t *xh, const int8_t *xl) {
-    static_assert(NW % 4 == 0, "NW multiple of 4");
+__device__ __forceinline__ int dot_words(const uint32_t *q, const uint32_t *h, const uint32_t *l) {
     int a = 0, b = 0;
 #pragma unroll
-    for (int i = 0; i < NW / 4; i++) {
-        const int4 h = reinterpret_cast<const int4 *>(xh)[i];
-        const int4 l = reinterpret_cast<const int4 *>(xl)[i];
-        a = __dp4a((int)q[4 * i + 0], h.x, a);
-        a = __dp4a((int)q[4 * i + 1], h.y, a);
-        a = __dp4a((int)q[4 * i + 2], h.z, a);
-        a = __dp4a((int)q[4 * i + 3], h.w, a);
-        b = __dp4a((int)q[4 * i + 0], l.x, b);
-        b = __dp4a((int)q[4 * i + 1], l.y, b);
-        b = __dp4a((int)q[4 * i + 2], l.z, b);
-        b = __dp4a((int)q[4 * i + 3], l.w, b);
+    for (int i = 0; i < NW; i++) {
+        a = __dp4a((int)q[i], (int)h[i], a);
+        b = __dp4a((int)q[i], (int)l[i], b);
     }
     return a * 254 + b;
 }
 
-// ---------------------------------------------------------------------------------- units
-// acc[m] += dot(unit u of the row at `row`, x row m)
-template <int QT, int M> struct Unit;
-
-template <int M> struct Unit<MLQ_Q8_0, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
-        const uint8_t *bp = row + 34 * u;
-        const float d = f16_at(bp);
-        uint32_t q[8];
-        load_words<8>(bp + 2, q);
+// copy NW words (NW % 4 == 0) of a plane from 16-byte-aligned shared memory
+template <int NW>
+__device__ __forceinline__ void lds_words(const int8_t *p, uint32_t *w) {
 #pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(d * xp.s[(size_t)m * (xp.K / 32) + u], (float)c, acc[m]);
-        }
+    for (int i = 0; i < NW / 4; i++) {
+        const int4 v = reinterpret_cast<const int4 *>(p)[i];
+        w[4 * i + 0] = (uint32_t)v.x;
+        w[4 * i + 1] = (uint32_t)v.y;
+        w[4 * i + 2] = (uint32_t)v.z;
+        w[4 * i + 3] = (uint32_t)v.w;
+    }
+}
+
+// ---------------------------------------------------------------------------------- units
+// A unit is decoded once into W<QT> (packed int8 codes + per-group fp32 scales) and
+// then dotted with the activation slice XU<QT> of every activation row.  XU comes
+// from shared memory (generic path) or stays in registers for the whole kernel
+// (M = 1 decode path: each lane always sees the same units of every row).
+//   Fmt<QT>::UE      elements per unit
+//   XU<QT>           the unit's activation words: h[], l[] (element order of the
+//                    decoded words), s[] / sum[] per 32-element x block touched
+template <int QT> struct W;
+template <int QT> struct XU;
+
+// ---- 32-element block formats: one block per unit
+struct XU32 {
+    uint32_t h[8], l[8];
+    float s, sum;
+};
+template <> struct XU<MLQ_Q8_0> : XU32 {};
+template <> struct XU<MLQ_Q4_0> : XU32 {};
+template <> struct XU<MLQ_Q4_1> : XU32 {};
+template <> struct XU<MLQ_Q5_0> : XU32 {};
+template <> struct XU<MLQ_MXFP4> : XU32 {};
+template <> struct XU<MLQ_MXFP4_REF> : XU32 {};
+
+template <int QT>
+__device__ __forceinline__ void load_xu32(const XPlanes &xp, int m, int u, XU32 &x) {
+    const size_t xo = (size_t)m * xp.K + 32 * u;
+    lds_words<8>(xp.h + xo, x.h);
+    lds_words<8>(xp.l + xo, x.l);
+    const size_t so = (size_t)m * (xp.K / 32) + u;
+    x.s = xp.s[so];
+    x.sum = xp.sum[so];
+}
+
+template <> struct W<MLQ_Q8_0> {
+    uint32_t q[8];
+    float d;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
+        const uint8_t *bp = row + 34 * u;
+        d = f16_at(bp);
+        load_words<8>(bp + 2, q);
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_Q8_0> &x) const {
+        return d * x.s * (float)dot_words<8>(q, x.h, x.l);
     }
 };
 
-template <int M> struct Unit<MLQ_Q4_0, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+template <> struct W<MLQ_Q4_0> {
+    uint32_t q[8];
+    float d;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 18 * u;
-        const float d = f16_at(bp);
-        uint32_t w[4], q[8];
+        d = f16_at(bp);
+        uint32_t w[4];
         load_words<4>(bp + 2, w);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            q[i] = w[i] & 0x0F0F0F0Fu;
-            q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+            q[i] = w[i] & 0x0F0F0F0Fu;               // elements 4i..4i+3
+            q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;    // elements 16+4i..
         }
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const size_t so = (size_t)m * (xp.K / 32) + u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(d, fmaf(xp.s[so], (float)c, -8.0f * xp.sum[so]), acc[m]);
-        }
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_Q4_0> &x) const {
+        return d * fmaf(x.s, (float)dot_words<8>(q, x.h, x.l), -8.0f * x.sum);
     }
 };
 
-template <int M> struct Unit<MLQ_Q4_1, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+template <> struct W<MLQ_Q4_1> {
+    uint32_t q[8];
+    float d, m;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 20 * u;
-        const float d = f16_at(bp);
-        const float mn = f16_at(bp + 2);
-        uint32_t w[4], q[8];
+        d = f16_at(bp);
+        m = f16_at(bp + 2);
+        uint32_t w[4];
         load_words<4>(bp + 4, w);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             q[i] = w[i] & 0x0F0F0F0Fu;
             q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
         }
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const size_t so = (size_t)m * (xp.K / 32) + u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(d * xp.s[so], (float)c, fmaf(mn, xp.sum[so], acc[m]));
-        }
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_Q4_1> &x) const {
+        return fmaf(d * x.s, (float)dot_words<8>(q, x.h, x.l), m * x.sum);
     }
 };
 
-template <int M> struct Unit<MLQ_Q5_0, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+template <> struct W<MLQ_Q5_0> {
+    uint32_t q[8];
+    float d;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 22 * u;
-        const float d = f16_at(bp);
-        uint32_t qh[1], w[4], q[8];
+        d = f16_at(bp);
+        uint32_t qh[1], w[4];
         load_words<1>(bp + 2, qh);
         load_words<4>(bp + 6, w);
 #pragma unroll
@@ -210,43 +249,44 @@ template <int M> struct Unit<MLQ_Q5_0, M> {
             q[i] = (w[i] & 0x0F0F0F0Fu) | spread4_to_bit4(qh[0] >> (4 * i));
             q[4 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | spread4_to_bit4(qh[0] >> (16 + 4 * i));
         }
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const size_t so = (size_t)m * (xp.K / 32) + u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(d, fmaf(xp.s[so], (float)c, -16.0f * xp.sum[so]), acc[m]);
-        }
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_Q5_0> &x) const {
+        return d * fmaf(x.s, (float)dot_words<8>(q, x.h, x.l), -16.0f * x.sum);
     }
 };
 
-template <int M> struct Unit<MLQ_MXFP4, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+// MXFP4 decodes in nibble order: word 2k holds elements (4k, 4k+16, 4k+1, 4k+17) and
+// word 2k+1 holds (4k+2, 4k+18, 4k+3, 4k+19) -- qs byte j carries element j in its
+// low nibble and j+16 in its high nibble -- so its activation words are permuted to
+// the same order when they are loaded (load_xu).
+template <> struct W<MLQ_MXFP4> {
+    uint32_t q[8];
+    float sc;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 17 * u;
-        uint32_t w[5], q[8];
+        uint32_t w[5];
         load_words<5>(bp, w);   // byte 0 = e, bytes 1..16 = qs
-        const float sc = e8m0_half(w[0] & 0xFFu);
+        sc = e8m0_half(w[0] & 0xFFu);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t qs = __funnelshift_r(w[i], w[i + 1], 8);   // qs bytes 4i..4i+3
-            q[i] = e2m1x2_lut(qs & 0x0F0F0F0Fu);
-            q[4 + i] = e2m1x2_lut((qs >> 4) & 0x0F0F0F0Fu);
+            q[2 * i] = e2m1x2_codes(qs);
+            q[2 * i + 1] = e2m1x2_codes(qs >> 16);
         }
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(sc * xp.s[(size_t)m * (xp.K / 32) + u], (float)c, acc[m]);
-        }
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_MXFP4> &x) const {
+        return sc * x.s * (float)dot_words<8>(q, x.h, x.l);
     }
 };
 
-template <int M> struct Unit<MLQ_MXFP4_REF, M> {
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+template <> struct W<MLQ_MXFP4_REF> {
+    uint32_t q[8];
+    float sc;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 17 * u;
-        uint32_t w[5], q[8];
+        uint32_t w[5];
         load_words<5>(bp, w);   // bytes 0..15 = qs, byte 16 = e
-        const float sc = __uint_as_float((w[4] & 0xFFu) << 23);
+        sc = __uint_as_float((w[4] & 0xFFu) << 23);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
@@ -254,20 +294,37 @@ template <int M> struct Unit<MLQ_MXFP4_REF, M> {
             q[2 * i] = __byte_perm(lo, hi, 0x5140) ^ 0x08080808u;
             q[2 * i + 1] = __byte_perm(lo, hi, 0x7362) ^ 0x08080808u;
         }
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * u;
-            const size_t so = (size_t)m * (xp.K / 32) + u;
-            const int c = dot_planes<8>(q, xp.h + xo, xp.l + xo);
-            acc[m] = fmaf(sc, fmaf(xp.s[so], (float)c, -8.0f * xp.sum[so]), acc[m]);
-        }
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_MXFP4_REF> &x) const {
+        return sc * fmaf(x.s, (float)dot_words<8>(q, x.h, x.l), -8.0f * x.sum);
     }
 };
 
-template <int QT, int M> struct UnitK45 {
-    // Q4_K (QT=12) / Q5_K (QT=13): unit u = sub-block pair g of super-block sb
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
-        constexpr int BB = Fmt<QT>::BB;
+// ---- Q4_K / Q5_K: unit u = sub-block pair g = u%4 of super-block u/4 (64 elements)
+struct XU64 {
+    uint32_t h[16], l[16];
+    float s[2], sum[2];
+};
+template <> struct XU<MLQ_Q4_K> : XU64 {};
+template <> struct XU<MLQ_Q5_K> : XU64 {};
+
+__device__ __forceinline__ void load_xu64(const XPlanes &xp, int m, int u, XU64 &x) {
+    const int xb0 = 2 * u;                       // = 8*(u/4) + 2*(u%4)
+    const size_t xo = (size_t)m * xp.K + 32 * xb0;
+    lds_words<16>(xp.h + xo, x.h);
+    lds_words<16>(xp.l + xo, x.l);
+    const size_t so = (size_t)m * (xp.K / 32) + xb0;
+    x.s[0] = xp.s[so];
+    x.s[1] = xp.s[so + 1];
+    x.sum[0] = xp.sum[so];
+    x.sum[1] = xp.sum[so + 1];
+}
+
+template <int QT> struct WK45 {
+    uint32_t q[16];          // words 0..7 sub-block 2g (lo nibbles), 8..15 sub-block 2g+1
+    float ds0, dm0, ds1, dm1;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
+        constexpr int BB = (QT == MLQ_Q4_K) ? 144 : 176;
         const int sb = u >> 2, g = u & 3;
         const uint8_t *blk = row + BB * sb;
         uint32_t hdr[4];
@@ -278,13 +335,13 @@ template <int QT, int M> struct UnitK45 {
         uint32_t sc0, m0, sc1, m1;
         scale_min_k4(sw, 2 * g, sc0, m0);
         scale_min_k4(sw, 2 * g + 1, sc1, m1);
-        uint32_t w[8], q0[8], q1[8];
+        uint32_t w[8];
         if (QT == MLQ_Q4_K) {
             load_words<8>(blk + 16 + 32 * g, w);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                q0[i] = w[i] & 0x0F0F0F0Fu;
-                q1[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+                q[i] = w[i] & 0x0F0F0F0Fu;
+                q[8 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
             }
         } else {
             uint32_t qh[8];
@@ -292,34 +349,88 @@ template <int QT, int M> struct UnitK45 {
             load_words<8>(blk + 48 + 32 * g, w);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                q0[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g)) & 0x01010101u) << 4);
-                q1[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
+                q[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g)) & 0x01010101u) << 4);
+                q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
             }
         }
-        const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
-        const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
-        const int xb0 = 8 * sb + 2 * g;
+        ds0 = d * (float)sc0;
+        dm0 = dmin * (float)m0;
+        ds1 = d * (float)sc1;
+        dm1 = dmin * (float)m1;
+    }
+    // same, for a row that starts on a 16-byte boundary of shared memory: the block
+    // header and qs/qh are then 16-byte aligned (144 and 176 are multiples of 16),
+    // so they come in with conflict-free 128-bit loads
+    __device__ __forceinline__ void decode_a16(const uint8_t *row, int u) {
+        constexpr int BB = (QT == MLQ_Q4_K) ? 144 : 176;
+        const int sb = u >> 2, g = u & 3;
+        const uint8_t *blk = row + BB * sb;
+        const uint4 hv = *reinterpret_cast<const uint4 *>(blk);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hv.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hv.x >> 16)));
+        const uint32_t sw[3] = {hv.y, hv.z, hv.w};
+        uint32_t sc0, m0, sc1, m1;
+        scale_min_k4(sw, 2 * g, sc0, m0);
+        scale_min_k4(sw, 2 * g + 1, sc1, m1);
+        const uint4 *qp = reinterpret_cast<const uint4 *>(blk + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g);
+        const uint4 v0 = qp[0], v1 = qp[1];
+        const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if (QT == MLQ_Q4_K) {
 #pragma unroll
-        for (int m = 0; m < M; m++) {
-            const size_t xo = (size_t)m * xp.K + 32 * xb0;
-            const size_t so = (size_t)m * (xp.K / 32) + xb0;
-            const int c0 = dot_planes<8>(q0, xp.h + xo, xp.l + xo);
-            const int c1 = dot_planes<8>(q1, xp.h + xo + 32, xp.l + xo + 32);
-            float a = acc[m];
-            a = fmaf(ds0 * xp.s[so], (float)c0, a);
-            a = fmaf(-dm0, xp.sum[so], a);
-            a = fmaf(ds1 * xp.s[so + 1], (float)c1, a);
-            a = fmaf(-dm1, xp.sum[so + 1], a);
-            acc[m] = a;
+            for (int i = 0; i < 8; i++) {
+                q[i] = w[i] & 0x0F0F0F0Fu;
+                q[8 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+            }
+        } else {
+            const uint4 *hp = reinterpret_cast<const uint4 *>(blk + 16);
+            const uint4 h0 = hp[0], h1 = hp[1];
+            const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                q[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g)) & 0x01010101u) << 4);
+                q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
+            }
         }
+        ds0 = d * (float)sc0;
+        dm0 = dmin * (float)m0;
+        ds1 = d * (float)sc1;
+        dm1 = dmin * (float)m1;
+    }
+    __device__ __forceinline__ float dot(const XU64 &x) const {
+        const int c0 = dot_words<8>(q, x.h, x.l);
+        const int c1 = dot_words<8>(q + 8, x.h + 8, x.l + 8);
+        float a = ds0 * x.s[0] * (float)c0;
+        a = fmaf(-dm0, x.sum[0], a);
+        a = fmaf(ds1 * x.s[1], (float)c1, a);
+        return fmaf(-dm1, x.sum[1], a);
     }
 };
-template <int M> struct Unit<MLQ_Q4_K, M> : UnitK45<MLQ_Q4_K, M> {};
-template <int M> struct Unit<MLQ_Q5_K, M> : UnitK45<MLQ_Q5_K, M> {};
+template <> struct W<MLQ_Q4_K> : WK45<MLQ_Q4_K> {};
+template <> struct W<MLQ_Q5_K> : WK45<MLQ_Q5_K> {};
 
-template <int M> struct Unit<MLQ_Q6_K, M> {
-    // unit u: super-block sb = u/4, half h = (u%4)/2, l range [16*(u%2), +16)
-    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+// ---- Q6_K: unit u = super-block u/4, half h = (u%4)/2, l in [16*(u%2), +16):
+// elements 128h + l0 + i + 32k (k = quadrant 0..3, i = 0..15)
+template <> struct XU<MLQ_Q6_K> {
+    uint32_t h[16], l[16];       // words 4k..4k+3 = quadrant k
+    float s[4];
+};
+
+__device__ __forceinline__ void load_xu_q6k(const XPlanes &xp, int m, int u, XU<MLQ_Q6_K> &x) {
+    const int sb = u >> 2, hh = (u >> 1) & 1, l0 = 16 * (u & 1);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int xb = 8 * sb + 4 * hh + k;
+        const size_t xo = (size_t)m * xp.K + 32 * xb + l0;
+        lds_words<4>(xp.h + xo, x.h + 4 * k);
+        lds_words<4>(xp.l + xo, x.l + 4 * k);
+        x.s[k] = xp.s[(size_t)m * (xp.K / 32) + xb];
+    }
+}
+
+template <> struct W<MLQ_Q6_K> {
+    uint32_t q[16];
+    float ds[4];
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const int sb = u >> 2, h = (u >> 1) & 1, lr = u & 1, l0 = 16 * lr;
         const uint8_t *blk = row + 210 * sb;
         uint32_t a[4], b[4], qh[4], scw[4];
@@ -328,28 +439,62 @@ template <int M> struct Unit<MLQ_Q6_K, M> {
         load_words<4>(blk + 128 + 32 * h + l0, qh);
         load_words<4>(blk + 192, scw);
         const float d = f16_at(blk + 208);
-        uint32_t q[4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            q[0][i] = __vsub4((a[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4), 0x20202020u);
-            q[1][i] = __vsub4((b[i] & 0x0F0F0F0Fu) | (((qh[i] >> 2) & 0x03030303u) << 4), 0x20202020u);
-            q[2][i] = __vsub4(((a[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 4) & 0x03030303u) << 4), 0x20202020u);
-            q[3][i] = __vsub4(((b[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 6) & 0x03030303u) << 4), 0x20202020u);
+            q[i] = __vsub4((a[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4), 0x20202020u);
+            q[4 + i] = __vsub4((b[i] & 0x0F0F0F0Fu) | (((qh[i] >> 2) & 0x03030303u) << 4), 0x20202020u);
+            q[8 + i] = __vsub4(((a[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 4) & 0x03030303u) << 4), 0x20202020u);
+            q[12 + i] = __vsub4(((b[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 6) & 0x03030303u) << 4), 0x20202020u);
         }
-        float ds[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) ds[k] = d * (float)sbyte16(scw, 8 * h + lr + 2 * k);
+    }
+    __device__ __forceinline__ float dot(const XU<MLQ_Q6_K> &x) const {
+        float a = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            a = fmaf(ds[k] * x.s[k], (float)dot_words<4>(q + 4 * k, x.h + 4 * k, x.l + 4 * k), a);
+        return a;
+    }
+};
+
+// natural element order -> the MXFP4 nibble order of W<MLQ_MXFP4>
+__device__ __forceinline__ void permute_mxfp4_words(uint32_t (&w)[8]) {
+    uint32_t n[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) n[i] = w[i];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        w[2 * k] = __byte_perm(n[k], n[k + 4], 0x5140);
+        w[2 * k + 1] = __byte_perm(n[k], n[k + 4], 0x7362);
+    }
+}
+
+template <int QT>
+__device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> &x) {
+    if constexpr (QT == MLQ_Q6_K) {
+        load_xu_q6k(xp, m, u, x);
+    } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K) {
+        load_xu64(xp, m, u, x);
+    } else {
+        load_xu32<QT>(xp, m, u, x);
+        if constexpr (QT == MLQ_MXFP4) {
+            permute_mxfp4_words(x.h);
+            permute_mxfp4_words(x.l);
+        }
+    }
+}
+
+// generic path: acc[m] += dot(unit u, x row m), activations from shared memory
+template <int QT, int M> struct Unit {
+    static __device__ __forceinline__ void dot(const uint8_t *row, int u, const XPlanes &xp, float (&acc)[M]) {
+        W<QT> w;
+        w.decode(row, u);
 #pragma unroll
         for (int m = 0; m < M; m++) {
-            float acc_m = acc[m];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int xb = 8 * sb + 4 * h + k;
-                const size_t xo = (size_t)m * xp.K + 32 * xb + l0;
-                const int c = dot_planes<4>(q[k], xp.h + xo, xp.l + xo);
-                acc_m = fmaf(ds[k] * xp.s[(size_t)m * (xp.K / 32) + xb], (float)c, acc_m);
-            }
-            acc[m] = acc_m;
+            XU<QT> x;
+            load_xu<QT>(xp, m, u, x);
+            acc[m] += w.dot(x);
         }
     }
 };

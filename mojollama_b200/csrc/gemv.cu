@@ -8,14 +8,18 @@
 // so the whole matrix is one contiguous byte stream of N*row_bytes.  A persistent
 // CTA walks tiles of `rpt` rows; each tile is a contiguous byte range.
 //
-// CTA = 9 warps.  Warp 8 is the producer: it streams each tile's 16-byte-aligned
-// interior into a 4-stage shared-memory ring with one cp.async.bulk (TMA engine,
-// L2 evict_first) per tile and fetches the <=15-byte ragged head/tail with plain
-// loads; full/empty mbarriers hand stages to the 8 decode warps.  The decode warps
-// first encode the activation rows as int8 "x planes" (formats.cuh) in shared
-// memory, then decode weight blocks straight from the staged bytes into packed
-// int8 and reduce with dp4a, fp32 per-block scaling and warp shuffles.  When a tile
-// holds fewer than 8 rows, 8/rpt warps split each row and combine through smem.
+// CTA = 9 warps, one CTA per SM.  Warp 8 is the producer: it streams each tile's
+// 16-byte-aligned interior into a shared-memory ring of up to 8 stages (as many as
+// fit in ~220 KB) with one cp.async.bulk (TMA engine, L2 evict_first) per tile and
+// fetches the <=15-byte ragged head/tail with plain loads; full/empty mbarriers hand
+// stages to the 8 decode warps.  The decode warps first encode the activation rows
+// as int8 "x planes" (formats.cuh) in shared memory, then decode weight blocks
+// straight from the staged bytes into packed int8 and reduce with dp4a, fp32
+// per-block scaling and warp shuffles.
+//   k_gemv_q1  (M = 1, many rows): 16 decode warps, one row each per tile; each
+//              lane keeps its activation slices in registers for the whole kernel.
+//   k_gemv_q   (any M <= 8): activation slices from shared memory; when a tile holds
+//              fewer than 8 rows, 8/rpt warps split each row and combine through smem.
 //
 // Roofline: HBM-bound.  Algorithmic bytes per launch = N*row_bytes + B*K*4 + B*N*4.
 #include <cuda_fp16.h>
@@ -27,14 +31,18 @@
 #include "formats.cuh"
 #include "mlq_internal.h"
 #include "pipeline.cuh"
+#include <stdlib.h>
 
 namespace mlq {
 
-static constexpr int kStages = 4;
+static constexpr int kMaxStages = 8;
 static constexpr int kConsumerWarps = 8;
 static constexpr int kThreads = (kConsumerWarps + 1) * 32;
-static constexpr int kMaxSmem = 232448;     // 227 KB opt-in per CTA on sm_100
-static constexpr int kStageTarget = 24576;  // bytes of weights per stage
+static constexpr int kMaxSmem = 232448;      // 227 KB opt-in per CTA on sm_100
+static constexpr int kSmemBudget = 220 * 1024;
+static constexpr int kStageTarget = 24576;   // bytes of weights per stage (generic path)
+static constexpr int kFastWarps = 16;        // decode warps of the M=1 kernel (1 row each per tile)
+static constexpr int kFastThreads = (kFastWarps + 1) * 32;
 
 int block_elems(int qt) {
     switch (qt) {
@@ -69,7 +77,7 @@ struct GemvArgs {
     float *out;
     int n_rows, K, nb_x;
     long long row_bytes, total_bytes;
-    int rpt, wpr, n_tiles, stage_bytes;
+    int rpt, wpr, n_tiles, stage_bytes, n_stages;
     int *status;
 };
 
@@ -79,10 +87,10 @@ struct GemvLayout {
 
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline GemvLayout gemv_layout(int M, int K, int stage_bytes) {
+__host__ __device__ inline GemvLayout gemv_layout(int M, int K, int stage_bytes, int n_stages) {
     GemvLayout L;
     int o = 0;
-    L.off_bar = o;  o += 2 * kStages * 8;
+    L.off_bar = o;  o += 2 * kMaxStages * 8;
     L.off_flag = o; o += 16;
     o = align_up(o, 128);
     L.off_xh = o;   o = align_up(o + M * K, 16);
@@ -90,7 +98,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int M, int K, int stage_bytes)
     L.off_xs = o;   o += M * (K / 32) * 4;
     L.off_xsum = o; o = align_up(o + M * (K / 32) * 4, 16);
     L.off_red = o;  o = align_up(o + 2 * kConsumerWarps * M * 4, 128);
-    L.off_stage = o; o += kStages * stage_bytes;
+    L.off_stage = o; o += n_stages * stage_bytes;
     L.total = o;
     return L;
 }
@@ -134,72 +142,91 @@ __device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, in
     }
 }
 
-template <int QT, int M>
-__global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const GemvLayout L = gemv_layout(M, a.K, a.stage_bytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
-    uint64_t *empty = full + kStages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+// Producer warp: stream tile it of this CTA into stage it % n_stages.  The tile's
+// 16-byte-aligned interior goes through one cp.async.bulk (TMA engine, L2
+// evict_first); the <= 15-byte ragged head and tail are plain loads by the lanes.
+__device__ __forceinline__ void produce_tiles(const GemvArgs &a, uint8_t *stages, uint64_t *full, uint64_t *empty,
+                                              volatile int *abort_flag, int n_iter, int lane) {
+    const uint64_t pol = policy_evict_first();
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    for (int it = 0; it < n_iter; ++it) {
+        const int s = it % a.n_stages;
+        if (it >= a.n_stages) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / a.n_stages) - 1) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok || *abort_flag) {
+                if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
+                return;
+            }
+        }
+        const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+        const long long b0 = tile * tile_bytes;
+        const long long b1 = min(b0 + tile_bytes, a.total_bytes);
+        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b0;
+        const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b1;
+        const uintptr_t gd = g0 & ~uintptr_t(15);
+        const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15);
+        const uintptr_t i1 = g1 & ~uintptr_t(15);
+        uint8_t *st = stages + (size_t)s * a.stage_bytes;
+        if (i1 > i0) {
+            if (g0 + lane < i0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+            if (i1 + lane < g1) st[i1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(i1 + lane));
+        } else {
+            if (g0 + lane < g1) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (i1 > i0) {
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(i1 - i0));
+                bulk_g2s(st + (i0 - gd), reinterpret_cast<const void *>(i0), (uint32_t)(i1 - i0), &full[s], pol);
+            } else {
+                mbar_arrive(&full[s]);
+            }
+        }
+    }
+}
 
+// decode warps: bounded wait for stage s of iteration it; false on timeout/abort
+__device__ __forceinline__ bool consume_wait(const GemvArgs &a, uint64_t *full, volatile int *abort_flag, int it,
+                                             int lane) {
+    if (*abort_flag) return false;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait_bounded(&full[it % a.n_stages], (it / a.n_stages) & 1);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok && lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
+    return ok;
+}
+
+__device__ __forceinline__ void init_barriers(uint64_t *full, uint64_t *empty, volatile int *abort_flag, int n_stages,
+                                              int n_consumers) {
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < n_stages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], n_consumers);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
+}
 
-    const long long rb = a.row_bytes;
-    const long long tile_bytes = (long long)a.rpt * rb;
-
+// ---------------------------------------------------------------- generic kernel (any M <= 8)
+// 8/rpt decode warps share each row of a tile when the matrix has few rows.
+template <int QT, int M>
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvLayout L = gemv_layout(M, a.K, a.stage_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMaxStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    init_barriers(full, empty, abort_flag, a.n_stages, kConsumerWarps);
     if (warp == kConsumerWarps) {
-        // ------------------------------------------------------------ producer warp
-        const uint64_t pol = policy_evict_first();
-        for (int it = 0; it < n_iter; ++it) {
-            const int s = it % kStages;
-            if (it >= kStages) {
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok || *abort_flag) {
-                    if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
-                    break;
-                }
-            }
-            const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
-            const long long b0 = tile * tile_bytes;
-            const long long b1 = min(b0 + tile_bytes, a.total_bytes);
-            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b0;
-            const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b1;
-            const uintptr_t gd = g0 & ~uintptr_t(15);
-            const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15);
-            const uintptr_t i1 = g1 & ~uintptr_t(15);
-            uint8_t *st = smem + L.off_stage + s * a.stage_bytes;
-            if (i1 > i0) {
-                if (g0 + lane < i0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
-                if (i1 + lane < g1) st[i1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(i1 + lane));
-            } else {
-                if (g0 + lane < g1) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
-            }
-            __syncwarp();
-            if (lane == 0) {
-                if (i1 > i0) {
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)(i1 - i0));
-                    bulk_g2s(st + (i0 - gd), reinterpret_cast<const void *>(i0), (uint32_t)(i1 - i0), &full[s], pol);
-                } else {
-                    mbar_arrive(&full[s]);
-                }
-            }
-        }
+        produce_tiles(a, smem + L.off_stage, full, empty, abort_flag, n_iter, lane);
         return;
     }
-
-    // ---------------------------------------------------------------- decode warps
     int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
     int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
     float *xs = reinterpret_cast<float *>(smem + L.off_xs);
@@ -209,18 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
     named_bar_sync(1, kConsumerWarps * 32);
 
     XPlanes xp{xh, xl, xs, xsum, a.K};
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
     const int rr = warp / a.wpr, part = warp - rr * a.wpr;
     const int U = a.K / Fmt<QT>::UE;
     for (int it = 0; it < n_iter; ++it) {
-        const int s = it % kStages;
-        bool ok = true;
-        if (!*abort_flag) {
-            if (lane == 0) ok = mbar_wait_bounded(&full[s], (it / kStages) & 1);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok && lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
-        } else {
-            ok = false;
-        }
+        const int s = it % a.n_stages;
+        const bool ok = consume_wait(a, full, abort_flag, it, lane);
         const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
         const int row0 = (int)(tile * a.rpt);
         const int row = row0 + rr;
@@ -229,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
         for (int m = 0; m < M; m++) acc[m] = 0.0f;
         if (ok && row < a.n_rows) {
             const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(tile * tile_bytes);
-            const uint8_t *rowp = smem + L.off_stage + s * a.stage_bytes + (g0 & 15) + (size_t)rr * rb;
+            const uint8_t *rowp = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15) + (size_t)rr * a.row_bytes;
             for (int u = part * 32 + lane; u < U; u += 32 * a.wpr) Unit<QT, M>::dot(rowp, u, xp, acc);
         }
 #pragma unroll
@@ -258,6 +279,71 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
                 for (int p = 0; p < a.wpr; p++) sum += rd[(r * a.wpr + p) * M + m];
                 if (row0 + r < a.n_rows && m < a.nb_x) a.out[(size_t)m * a.n_rows + row0 + r] = sum;
             }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- M = 1 decode kernel
+// kFastWarps decode warps each own one row of every tile, and each lane always
+// handles units lane, lane+32, ... of a row, so the lane's activation slices XU are
+// loaded into registers once and reused for every row the CTA streams.
+// UPL = units per lane (ceil(K/UE/32)); A16 = rows start on 16-byte boundaries in
+// shared memory (Q4_K/Q5_K then use 128-bit loads).
+template <int QT, int UPL, bool A16>
+__global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvLayout L = gemv_layout(1, a.K, a.stage_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMaxStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    init_barriers(full, empty, abort_flag, a.n_stages, kFastWarps);
+    if (warp == kFastWarps) {
+        produce_tiles(a, smem + L.off_stage, full, empty, abort_flag, n_iter, lane);
+        return;
+    }
+    int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
+    int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
+    float *xs = reinterpret_cast<float *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
+    encode_x_planes<1>(a.x, 1, a.K, xh, xl, xs, xsum, warp, lane, kFastWarps);
+    named_bar_sync(1, kFastWarps * 32);
+    const XPlanes xp{xh, xl, xs, xsum, a.K};
+    const int U = a.K / Fmt<QT>::UE;
+    XU<QT> xu[UPL];
+#pragma unroll
+    for (int j = 0; j < UPL; j++) {
+        const int u = lane + 32 * j;
+        if (u < U) load_xu<QT>(xp, 0, u, xu[j]);
+    }
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    for (int it = 0; it < n_iter; ++it) {
+        const int s = it % a.n_stages;
+        const bool ok = consume_wait(a, full, abort_flag, it, lane);
+        const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+        const int row = (int)(tile * a.rpt) + warp;
+        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(tile * tile_bytes);
+        const uint8_t *rowp = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15) + (size_t)warp * a.row_bytes;
+        float acc = 0.0f;
+        if (ok && row < a.n_rows) {
+#pragma unroll
+            for (int j = 0; j < UPL; j++) {
+                const int u = lane + 32 * j;
+                if (u < U) {
+                    W<QT> w;
+                    if constexpr (A16) w.decode_a16(rowp, u);
+                    else w.decode(rowp, u);
+                    acc += w.dot(xu[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        __syncwarp();
+        if (lane == 0 && ok) {
+            mbar_arrive(&empty[s]);
+            if (row < a.n_rows) a.out[row] = acc;
         }
     }
 }
@@ -322,9 +408,33 @@ __global__ void __launch_bounds__(256) k_gemv_float(const WT *__restrict__ W, co
 }
 
 // ------------------------------------------------------------------------------ launchers
+static int stages_for(int fixed, int stage_bytes) {
+    int n = (kSmemBudget - fixed) / stage_bytes;
+    return n > kMaxStages ? kMaxStages : n;
+}
+
+template <typename Kern>
+static int launch_gemv_kernel(Kern kern, GemvArgs &a, int smem, cudaStream_t s, bool &attr_set,
+                              int threads = kThreads) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    if (!attr_set) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+            return MLQ_ERR_CUDA;
+        attr_set = true;
+    }
+    int per_sm = 0;
+    if (!MLQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem))) return MLQ_ERR_CUDA;
+    if (per_sm < 1) per_sm = 1;
+    a.status = c->d_status;
+    const int grid = a.n_tiles < per_sm * c->num_sms ? a.n_tiles : per_sm * c->num_sms;
+    kern<<<grid, threads, smem, s>>>(a);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
 template <int QT, int M>
-static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, int K, int nb_x,
-                      cudaStream_t s) {
+static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, int K, int nb_x, cudaStream_t s) {
     Ctx *c = ctx();
     if (!c) return MLQ_ERR_NO_DEVICE;
     const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
@@ -333,61 +443,95 @@ static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, 
     rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
     while (rpt > 1 && (n_rows + rpt - 1) / rpt < 2 * c->num_sms) rpt >>= 1;
     const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
-    const GemvLayout L = gemv_layout(M, K, stage_bytes);
-    if (L.total > kMaxSmem) return MLQ_ERR_CAPACITY;
-    auto kern = k_gemv_q<QT, M>;
+    const int fixed = gemv_layout(M, K, stage_bytes, 0).total;
+    const int n_stages = stages_for(fixed, stage_bytes);
+    if (n_stages < 2) return MLQ_ERR_CAPACITY;
+    GemvArgs a{};
+    a.W = W; a.x = x; a.out = out; a.n_rows = n_rows; a.K = K; a.nb_x = nb_x;
+    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = kConsumerWarps / rpt;
+    a.n_tiles = (n_rows + rpt - 1) / rpt; a.stage_bytes = stage_bytes; a.n_stages = n_stages;
     static bool attr_set = false;
-    if (!attr_set) {
-        if (!MLQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
-            return MLQ_ERR_CUDA;
-        attr_set = true;
+    return launch_gemv_kernel(k_gemv_q<QT, M>, a, fixed + n_stages * stage_bytes, s, attr_set);
+}
+
+template <int QT, int UPL>
+static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
+    const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
+    const int rpt = kFastWarps;
+    const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
+    const int fixed = gemv_layout(1, K, stage_bytes, 0).total;
+    const int n_stages = stages_for(fixed, stage_bytes);
+    if (n_stages < 3) return MLQ_ERR_CAPACITY;
+    GemvArgs a{};
+    a.W = W; a.x = x; a.out = out; a.n_rows = n_rows; a.K = K; a.nb_x = 1;
+    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = 1;
+    a.n_tiles = (n_rows + rpt - 1) / rpt; a.stage_bytes = stage_bytes; a.n_stages = n_stages;
+    const int smem = fixed + n_stages * stage_bytes;
+    constexpr bool kCanAlign = (QT == MLQ_Q4_K || QT == MLQ_Q5_K);
+    if constexpr (kCanAlign) {
+        if (rb % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
+            static bool attr_a = false;
+            return launch_gemv_kernel(k_gemv_q1<QT, UPL, true>, a, smem, s, attr_a, kFastThreads);
+        }
     }
-    int per_sm = 0;
-    if (!MLQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L.total)))
-        return MLQ_ERR_CUDA;
-    if (per_sm < 1) per_sm = 1;
-    GemvArgs a;
-    a.W = W;
-    a.x = x;
-    a.out = out;
-    a.n_rows = n_rows;
-    a.K = K;
-    a.nb_x = nb_x;
-    a.row_bytes = rb;
-    a.total_bytes = rb * n_rows;
-    a.rpt = rpt;
-    a.wpr = kConsumerWarps / rpt;
-    a.n_tiles = (n_rows + rpt - 1) / rpt;
-    a.stage_bytes = stage_bytes;
-    a.status = c->d_status;
-    const int grid = a.n_tiles < per_sm * c->num_sms ? a.n_tiles : per_sm * c->num_sms;
-    kern<<<grid, kThreads, L.total, s>>>(a);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    static bool attr_set = false;
+    return launch_gemv_kernel(k_gemv_q1<QT, UPL, false>, a, smem, s, attr_set, kFastThreads);
+}
+
+// M = 1 over many rows: the register-resident kernel; returns MLQ_ERR_UNSUPPORTED
+// when the shape does not suit it (few rows, or too many units per lane).
+template <int QT>
+static int launch_q1(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
+    Ctx *c = ctx();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    const int U = K / Fmt<QT>::UE;
+    const int upl = (U + 31) / 32;
+    if (n_rows < 4 * c->num_sms * kFastWarps || getenv("MLQ_GEMV_GENERIC")) return MLQ_ERR_UNSUPPORTED;
+    // only the variants that stay inside the 96 registers a 544-thread CTA allows:
+    // 64-element units at 1 per lane (K <= 2048), 32-element units at <= 3 (K <= 3072)
+    if constexpr (Fmt<QT>::UE == 64) {
+        if (upl == 1) return launch_q1_fast<QT, 1>(W, x, out, n_rows, K, s);
+        return MLQ_ERR_UNSUPPORTED;
+    } else {
+        switch (upl) {
+            case 1: return launch_q1_fast<QT, 1>(W, x, out, n_rows, K, s);
+            case 2: return launch_q1_fast<QT, 2>(W, x, out, n_rows, K, s);
+            case 3: return launch_q1_fast<QT, 3>(W, x, out, n_rows, K, s);
+            default: return MLQ_ERR_UNSUPPORTED;
+        }
+    }
+}
+
+static bool fits(int M, int K) {
+    return gemv_layout(M, K, 0, 0).total + 2 * (kStageTarget + 64) <= kSmemBudget;
 }
 
 template <int QT>
 static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
+    if (B == 1) {
+        const int rc = launch_q1<QT>(W, x, out, n_rows, K, s);
+        if (rc != MLQ_ERR_UNSUPPORTED) return rc;
+    }
     for (int b = 0; b < B;) {
         const int left = B - b;
-        int rc;
-        int take;
-        // widest M whose x planes still fit next to the stage ring
-        if (left >= 5 && gemv_layout(8, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+        const float *xb = x + (size_t)b * K;
+        float *ob = out + (size_t)b * n_rows;
+        int rc, take;
+        if (left >= 5 && fits(8, K)) {
             take = left < 8 ? left : 8;
-            rc = launch_q_m<QT, 8>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
-        } else if (left >= 4 && gemv_layout(4, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            rc = launch_q_m<QT, 8>(W, xb, ob, n_rows, K, take, s);
+        } else if (left >= 4 && fits(4, K)) {
             take = 4;
-            rc = launch_q_m<QT, 4>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
-        } else if (left == 3 && gemv_layout(3, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            rc = launch_q_m<QT, 4>(W, xb, ob, n_rows, K, take, s);
+        } else if (left == 3 && fits(3, K)) {
             take = 3;
-            rc = launch_q_m<QT, 3>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
-        } else if (left >= 2 && gemv_layout(2, K, 1).total + kStages * (kStageTarget + 64) <= kMaxSmem) {
+            rc = launch_q_m<QT, 3>(W, xb, ob, n_rows, K, take, s);
+        } else if (left >= 2 && fits(2, K)) {
             take = 2;
-            rc = launch_q_m<QT, 2>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+            rc = launch_q_m<QT, 2>(W, xb, ob, n_rows, K, take, s);
         } else {
             take = 1;
-            rc = launch_q_m<QT, 1>(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+            rc = launch_q_m<QT, 1>(W, xb, ob, n_rows, K, take, s);
         }
         if (rc != MLQ_OK) {
             if (rc == MLQ_ERR_CAPACITY) set_error(rc, "K=%d too large for the shared-memory stage ring", K);

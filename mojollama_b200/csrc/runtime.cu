@@ -119,9 +119,36 @@ bool is_device_ptr(const void *p) {
 }
 
 // ------------------------------------------------------------------------------ residency cache
-struct CacheEntry { void *dev; size_t bytes; };
+// Each entry keeps a content sample of the host buffer (all of it up to 16 KB; else
+// the first and last 4 KB and 64 evenly spaced 64-byte windows).  A hit whose sample
+// no longer matches -- a freed host buffer re-allocated at the same address with the
+// same size, or weights rewritten in place -- re-uploads the buffer.  Changes that
+// touch none of the sampled bytes are not seen: treat host weights as immutable
+// after first use, or call mlq_cache_clear().
+struct CacheEntry { void *dev; size_t bytes; std::vector<uint8_t> sample; };
 static std::map<std::pair<uintptr_t, size_t>, CacheEntry> g_cache[kMaxDev];
 static size_t g_cache_bytes[kMaxDev];
+
+static void take_sample(const uint8_t *h, size_t bytes, std::vector<uint8_t> &s) {
+    if (bytes <= 16384) {
+        s.assign(h, h + bytes);
+        return;
+    }
+    s.resize(8192 + 64 * 64);
+    memcpy(s.data(), h, 4096);
+    memcpy(s.data() + 4096, h + bytes - 4096, 4096);
+    const size_t stride = (bytes - 64) / 64;
+    for (int i = 0; i < 64; i++) memcpy(s.data() + 8192 + 64 * i, h + stride * i, 64);
+}
+
+static bool sample_matches(const uint8_t *h, size_t bytes, const std::vector<uint8_t> &s) {
+    if (bytes <= 16384) return memcmp(h, s.data(), bytes) == 0;
+    if (memcmp(h, s.data(), 4096) || memcmp(h + bytes - 4096, s.data() + 4096, 4096)) return false;
+    const size_t stride = (bytes - 64) / 64;
+    for (int i = 0; i < 64; i++)
+        if (memcmp(h + stride * i, s.data() + 8192 + 64 * i, 64)) return false;
+    return true;
+}
 
 static const void *resident(const void *host, size_t bytes) {
     Ctx *c = ctx();
@@ -130,7 +157,14 @@ static const void *resident(const void *host, size_t bytes) {
     auto key = std::make_pair((uintptr_t)host, bytes);
     auto &m = g_cache[c->device];
     auto it = m.find(key);
-    if (it != m.end()) return it->second.dev;
+    const uint8_t *h = (const uint8_t *)host;
+    if (it != m.end()) {
+        if (sample_matches(h, bytes, it->second.sample)) return it->second.dev;
+        if (!MLQ_CUDA(cudaMemcpyAsync(it->second.dev, host, bytes, cudaMemcpyHostToDevice, c->stream)))
+            return nullptr;
+        take_sample(h, bytes, it->second.sample);
+        return it->second.dev;
+    }
     void *d = nullptr;
     // pad so that 16-byte vector reads of the last block stay inside the allocation
     if (!MLQ_CUDA(cudaMalloc(&d, bytes + 256))) return nullptr;
@@ -139,7 +173,9 @@ static const void *resident(const void *host, size_t bytes) {
         return nullptr;
     }
     cudaMemsetAsync((char *)d + bytes, 0, 256, c->stream);
-    m[key] = CacheEntry{d, bytes};
+    CacheEntry e{d, bytes, {}};
+    take_sample(h, bytes, e.sample);
+    m[key] = std::move(e);
     g_cache_bytes[c->device] += bytes;
     return d;
 }

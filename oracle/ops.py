@@ -28,3 +28,79 @@ def gemv(w_raw: np.ndarray, qt: int, x: np.ndarray, n_rows: int, n_cols: int) ->
     w = F.dequantize(qt, w_raw, n_rows * n_cols).reshape(n_rows, n_cols).astype(np.float64)
     xb = np.asarray(x, np.float64).reshape(-1, n_cols)
     return (xb @ w.T).astype(np.float32)
+
+
+def rms_norm(x, w, eps, sanitize=False):
+    """simd_ops.c:35 / quant_kernels_omp.c:956 (eps 1e-5); sanitize = the batch engine's
+    RMS_NORM_SIMD (cengine_batch_instr.c:1258-1279): NaN -> 0, clamp +-1000 first.
+    Returns (out, clamped input)."""
+    x = np.asarray(x, np.float32).copy()
+    if sanitize:
+        x = np.where(np.isnan(x), np.float32(0), x)
+        x = np.clip(x, -1000, 1000).astype(np.float32)
+    ss = (x.astype(np.float64) ** 2).sum(axis=-1, keepdims=True)
+    inv = 1.0 / np.sqrt(ss / x.shape[-1] + eps)
+    out = (x * inv) * (np.ones(x.shape[-1]) if w is None else np.asarray(w, np.float64))
+    return out.astype(np.float32), x
+
+
+def silu(x, mode=0):
+    """mode 0: x/(1+exp(-x)) (quant_kernels_omp.c:981); mode 1: simd_ops.c:56 -- Pade
+    tanh on the first n - n%8 elements, exact on the tail."""
+    x = np.asarray(x, np.float64)
+    exact = x / (1.0 + np.exp(-x))
+    if mode == 0:
+        return exact.astype(np.float32)
+    n = x.size
+    body = n - n % 8
+    h = x[:body] * 0.5
+    v2 = h * h
+    t = h * (27 + v2) / (27 + 9 * v2)
+    out = exact.copy()
+    out[:body] = x[:body] * (0.5 + 0.5 * t)
+    return out.astype(np.float32)
+
+
+def swiglu(g, u):
+    """quant_kernels_omp.c:2157-2164: silu(clamp(g, -80, 80)) * u."""
+    g = np.clip(np.asarray(g, np.float64), -80, 80)
+    return (g / (1 + np.exp(-g)) * np.asarray(u, np.float64)).astype(np.float32)
+
+
+def softmax(x):
+    x = np.asarray(x, np.float64)
+    e = np.exp(x - x.max(axis=-1, keepdims=True))
+    return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def rope_interleaved(q, k, n_heads, n_kv, hd, pos, base):
+    """simd_ops.c:122 apply_rope: pairs (d, d+1), freq = 1/base^((d/2)/(hd/2))."""
+    def rot(v, nh):
+        v = np.asarray(v, np.float64).reshape(nh, hd).copy()
+        d = np.arange(0, hd, 2)
+        ang = pos * (1.0 / np.power(base, (d // 2) / (hd // 2)))
+        c, s = np.cos(ang), np.sin(ang)
+        a0, a1 = v[:, 0::2].copy(), v[:, 1::2].copy()
+        v[:, 0::2] = a0 * c - a1 * s
+        v[:, 1::2] = a0 * s + a1 * c
+        return v.reshape(-1).astype(np.float32)
+    return rot(q, n_heads), rot(k, n_kv)
+
+
+def rope_tables(max_ctx, hd, rope_dim, base=10000.0):
+    """cengine_batch_instr.c:674 rope_init: theta = pos / base^(2j/hd), j < rope_dim/2."""
+    j = np.arange(rope_dim // 2)
+    pos = np.arange(max_ctx)[:, None]
+    theta = pos / np.power(base, 2.0 * j / hd)
+    return np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+
+
+def rope_neox(buf, n_heads, hd, pos, cos_t, sin_t, rope_dim):
+    """cengine_batch_instr.c:686 rope_apply: rotate (x[j], x[j + rope_dim/2]) of each head."""
+    b = np.asarray(buf, np.float64).reshape(n_heads, hd).copy()
+    hd2 = rope_dim // 2
+    c, s = cos_t[pos, :hd2].astype(np.float64), sin_t[pos, :hd2].astype(np.float64)
+    a0, a1 = b[:, :hd2].copy(), b[:, hd2:2 * hd2].copy()
+    b[:, :hd2] = a0 * c - a1 * s
+    b[:, hd2:2 * hd2] = a1 * c + a0 * s
+    return b.reshape(-1).astype(np.float32)

@@ -93,7 +93,8 @@ def test_reference_named_batch_matmul(K, name, qt):
 
 
 def test_matches_reference_c_outputs_from_golden(K):
-    ro = np.load(os.path.join(G, "ref_ops.npz"))
+    # materialise every array once: each NpzFile[key] access returns a fresh temporary
+    ro = dict(np.load(os.path.join(G, "ref_ops.npz")))
     n, k, b = (int(v) for v in ro["shape"])
     for qt in (F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_K, F.MXFP4_REF):
         out = np.zeros(n, np.float32)
@@ -222,3 +223,18 @@ def test_full_size_head_rows_sampled(cuda_device, qt):
     assert lib.mlq_matmul(wd.data_ptr(), qt, xs.data_ptr(), os_.data_ptr(), n, k, 1) == 0
     lib.mlq_sync()
     assert O.rel_l2(os_.cpu().numpy()[0], out[0] + out[1]) < TOL
+
+
+def test_host_weight_cache_follows_buffer_contents(cuda_device):
+    """A host weight buffer rewritten in place (or freed and re-allocated at the same
+    address with the same size) must not be served from a stale device copy."""
+    lib = cuda_device
+    n, k = 64, 256
+    w = make_w(F.Q4_0, n, k, 1)
+    x = np.random.default_rng(3).standard_normal(k).astype(np.float32)
+    out = np.zeros(n, np.float32)
+    assert lib.mlq_matmul(w.ctypes.data, F.Q4_0, x.ctypes.data, out.ctypes.data, n, k, 1) == 0
+    assert O.rel_l2(out, O.gemv(w, F.Q4_0, x, n, k)[0]) < TOL
+    w[:] = make_w(F.Q4_0, n, k, 2)                   # same address, same size, new contents
+    assert lib.mlq_matmul(w.ctypes.data, F.Q4_0, x.ctypes.data, out.ctypes.data, n, k, 1) == 0
+    assert O.rel_l2(out, O.gemv(w, F.Q4_0, x, n, k)[0]) < TOL
