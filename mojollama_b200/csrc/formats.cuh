@@ -105,15 +105,14 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
-// Doubled-E2M1 codes (GGUF MXFP4) of the four nibbles in the low 16 bits of `sel`,
-// as signed int8 bytes in nibble order.  With P = {0,1,2,3,4,6,8,12} in {b:a}:
+// Doubled-E2M1 magnitudes (GGUF MXFP4) of the four nibbles in the low 16 bits of
+// `sel`, split by sign, in nibble order.  With P = {0,1,2,3,4,6,8,12} in {b:a}:
 // prmt(P, nib) gives the magnitude for a positive code and 0 for a negative one
-// (sign-replicate of a positive byte); prmt(P, nib ^ 8) the reverse; the code is the
-// bytewise difference.
-__device__ __forceinline__ uint32_t e2m1x2_codes(uint32_t sel) {
-    const uint32_t pos = prmt(0x03020100u, 0x0C080604u, sel);
-    const uint32_t neg = prmt(0x03020100u, 0x0C080604u, sel ^ 0x8888u);
-    return __vsub4(pos, neg);
+// (sign-replicate of a positive byte); prmt(P, nib ^ 8) the reverse.  The dot
+// product takes the two words as separate dp4a streams and subtracts.
+__device__ __forceinline__ void e2m1x2_split(uint32_t sel, uint32_t &pos, uint32_t &neg) {
+    pos = prmt(0x03020100u, 0x0C080604u, sel);
+    neg = prmt(0x03020100u, 0x0C080604u, sel ^ 0x8888u);
 }
 
 // ---------------------------------------------------------------------------------- x planes
@@ -260,7 +259,7 @@ template <> struct W<MLQ_Q5_0> {
 // low nibble and j+16 in its high nibble -- so its activation words are permuted to
 // the same order when they are loaded (load_xu).
 template <> struct W<MLQ_MXFP4> {
-    uint32_t q[8];
+    uint32_t qp[8], qn[8];   // magnitudes of the positive / negative codes
     float sc;
     __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const uint8_t *bp = row + 17 * u;
@@ -270,12 +269,24 @@ template <> struct W<MLQ_MXFP4> {
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t qs = __funnelshift_r(w[i], w[i + 1], 8);   // qs bytes 4i..4i+3
-            q[2 * i] = e2m1x2_codes(qs);
-            q[2 * i + 1] = e2m1x2_codes(qs >> 16);
+            e2m1x2_split(qs, qp[2 * i], qn[2 * i]);
+            e2m1x2_split(qs >> 16, qp[2 * i + 1], qn[2 * i + 1]);
         }
     }
     __device__ __forceinline__ float dot(const XU<MLQ_MXFP4> &x) const {
-        return sc * x.s * (float)dot_words<8>(q, x.h, x.l);
+        int a = 0, b = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            a = __dp4a((int)qp[i], (int)x.h[i], a);
+            b = __dp4a((int)qp[i], (int)x.l[i], b);
+        }
+        int an = 0, bn = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            an = __dp4a((int)qn[i], (int)x.h[i], an);
+            bn = __dp4a((int)qn[i], (int)x.l[i], bn);
+        }
+        return sc * x.s * (float)((a - an) * 254 + (b - bn));
     }
 };
 
@@ -413,6 +424,7 @@ template <> struct W<MLQ_Q5_K> : WK45<MLQ_Q5_K> {};
 template <> struct XU<MLQ_Q6_K> {
     uint32_t h[16], l[16];       // words 4k..4k+3 = quadrant k
     float s[4];
+    int off[4];                  // 32 * (254 * sum(h) + sum(l)) over each quadrant's 16 elements
 };
 
 __device__ __forceinline__ void load_xu_q6k(const XPlanes &xp, int m, int u, XU<MLQ_Q6_K> &x) {
@@ -424,9 +436,17 @@ __device__ __forceinline__ void load_xu_q6k(const XPlanes &xp, int m, int u, XU<
         lds_words<4>(xp.h + xo, x.h + 4 * k);
         lds_words<4>(xp.l + xo, x.l + 4 * k);
         x.s[k] = xp.s[(size_t)m * (xp.K / 32) + xb];
+        int hs = 0, ls = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            hs = __dp4a(0x01010101, (int)x.h[4 * k + i], hs);
+            ls = __dp4a(0x01010101, (int)x.l[4 * k + i], ls);
+        }
+        x.off[k] = 32 * (254 * hs + ls);
     }
 }
 
+// codes stay unsigned (0..63); the -32 offset is applied through XU::off
 template <> struct W<MLQ_Q6_K> {
     uint32_t q[16];
     float ds[4];
@@ -441,10 +461,10 @@ template <> struct W<MLQ_Q6_K> {
         const float d = f16_at(blk + 208);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            q[i] = __vsub4((a[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4), 0x20202020u);
-            q[4 + i] = __vsub4((b[i] & 0x0F0F0F0Fu) | (((qh[i] >> 2) & 0x03030303u) << 4), 0x20202020u);
-            q[8 + i] = __vsub4(((a[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 4) & 0x03030303u) << 4), 0x20202020u);
-            q[12 + i] = __vsub4(((b[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 6) & 0x03030303u) << 4), 0x20202020u);
+            q[i] = (a[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4);
+            q[4 + i] = (b[i] & 0x0F0F0F0Fu) | (((qh[i] >> 2) & 0x03030303u) << 4);
+            q[8 + i] = ((a[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 4) & 0x03030303u) << 4);
+            q[12 + i] = ((b[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 6) & 0x03030303u) << 4);
         }
 #pragma unroll
         for (int k = 0; k < 4; k++) ds[k] = d * (float)sbyte16(scw, 8 * h + lr + 2 * k);
@@ -452,8 +472,10 @@ template <> struct W<MLQ_Q6_K> {
     __device__ __forceinline__ float dot(const XU<MLQ_Q6_K> &x) const {
         float a = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            a = fmaf(ds[k] * x.s[k], (float)dot_words<4>(q + 4 * k, x.h + 4 * k, x.l + 4 * k), a);
+        for (int k = 0; k < 4; k++) {
+            const int c = dot_words<4>(q + 4 * k, x.h + 4 * k, x.l + 4 * k) - x.off[k];
+            a = fmaf(ds[k] * x.s[k], (float)c, a);
+        }
         return a;
     }
 };

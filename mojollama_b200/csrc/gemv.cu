@@ -16,7 +16,7 @@
 // as int8 "x planes" (formats.cuh) in shared memory, then decode weight blocks
 // straight from the staged bytes into packed int8 and reduce with dp4a, fp32
 // per-block scaling and warp shuffles.
-//   k_gemv_q1  (M = 1, many rows): 16 decode warps, one row each per tile; each
+//   k_gemv_q1  (M = 1, many rows): 16 decode warps, 1-2 rows each per tile; each
 //              lane keeps its activation slices in registers for the whole kernel.
 //   k_gemv_q   (any M <= 8): activation slices from shared memory; when a tile holds
 //              fewer than 8 rows, 8/rpt warps split each row and combine through smem.
@@ -284,12 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
 }
 
 // ---------------------------------------------------------------- M = 1 decode kernel
-// kFastWarps decode warps each own one row of every tile, and each lane always
-// handles units lane, lane+32, ... of a row, so the lane's activation slices XU are
-// loaded into registers once and reused for every row the CTA streams.
-// UPL = units per lane (ceil(K/UE/32)); A16 = rows start on 16-byte boundaries in
-// shared memory (Q4_K/Q5_K then use 128-bit loads).
-template <int QT, int UPL, bool A16>
+// kFastWarps decode warps each own RW rows of every tile (rows w, w+16, ...), and
+// each lane always handles units lane, lane+32, ... of a row, so the lane's
+// activation slices XU are loaded into registers once and reused for every row the
+// CTA streams.  UPL = units per lane (ceil(K/UE/32)); A16 = rows start on 16-byte
+// boundaries in shared memory (Q4_K/Q5_K then use 128-bit loads); RW = rows per
+// warp per tile (independent decode chains for latency hiding).
+template <int QT, int UPL, bool A16, int RW>
 __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvLayout L = gemv_layout(1, a.K, a.stage_bytes, a.n_stages);
@@ -322,28 +323,42 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
         const int s = it % a.n_stages;
         const bool ok = consume_wait(a, full, abort_flag, it, lane);
         const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
-        const int row = (int)(tile * a.rpt) + warp;
+        const int row0 = (int)(tile * a.rpt) + warp;
         const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(tile * tile_bytes);
-        const uint8_t *rowp = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15) + (size_t)warp * a.row_bytes;
-        float acc = 0.0f;
-        if (ok && row < a.n_rows) {
+        const uint8_t *st = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15);
+        float acc[RW];
+#pragma unroll
+        for (int r = 0; r < RW; r++) acc[r] = 0.0f;
+        if (ok) {
 #pragma unroll
             for (int j = 0; j < UPL; j++) {
                 const int u = lane + 32 * j;
                 if (u < U) {
-                    W<QT> w;
-                    if constexpr (A16) w.decode_a16(rowp, u);
-                    else w.decode(rowp, u);
-                    acc += w.dot(xu[j]);
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        // rows warp, warp + 16, ...: row r of this warp within the tile
+                        if (row0 + kFastWarps * r < a.n_rows) {
+                            const uint8_t *rowp = st + (size_t)(warp + kFastWarps * r) * a.row_bytes;
+                            W<QT> w;
+                            if constexpr (A16) w.decode_a16(rowp, u);
+                            else w.decode(rowp, u);
+                            acc[r] += w.dot(xu[j]);
+                        }
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        for (int r = 0; r < RW; r++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        }
         __syncwarp();
         if (lane == 0 && ok) {
             mbar_arrive(&empty[s]);
-            if (row < a.n_rows) a.out[row] = acc;
+#pragma unroll
+            for (int r = 0; r < RW; r++)
+                if (row0 + kFastWarps * r < a.n_rows) a.out[row0 + kFastWarps * r] = acc[r];
         }
     }
 }
@@ -454,10 +469,17 @@ static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, 
     return launch_gemv_kernel(k_gemv_q<QT, M>, a, fixed + n_stages * stage_bytes, s, attr_set);
 }
 
-template <int QT, int UPL>
-static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
+// rows per decode warp per tile of the M=1 kernel, per format (MLQ_GEMV_RW overrides)
+template <int QT> static int fast_rw() {
+    const char *e = getenv("MLQ_GEMV_RW");
+    if (e && (atoi(e) == 1 || atoi(e) == 2)) return atoi(e);
+    return 2;
+}
+
+template <int QT, int UPL, int RW>
+static int launch_q1_rw(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
     const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
-    const int rpt = kFastWarps;
+    const int rpt = kFastWarps * RW;
     const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
     const int fixed = gemv_layout(1, K, stage_bytes, 0).total;
     const int n_stages = stages_for(fixed, stage_bytes);
@@ -471,11 +493,17 @@ static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_ro
     if constexpr (kCanAlign) {
         if (rb % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
             static bool attr_a = false;
-            return launch_gemv_kernel(k_gemv_q1<QT, UPL, true>, a, smem, s, attr_a, kFastThreads);
+            return launch_gemv_kernel(k_gemv_q1<QT, UPL, true, RW>, a, smem, s, attr_a, kFastThreads);
         }
     }
     static bool attr_set = false;
-    return launch_gemv_kernel(k_gemv_q1<QT, UPL, false>, a, smem, s, attr_set, kFastThreads);
+    return launch_gemv_kernel(k_gemv_q1<QT, UPL, false, RW>, a, smem, s, attr_set, kFastThreads);
+}
+
+template <int QT, int UPL>
+static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
+    if (fast_rw<QT>() == 2) return launch_q1_rw<QT, UPL, 2>(W, x, out, n_rows, K, s);
+    return launch_q1_rw<QT, UPL, 1>(W, x, out, n_rows, K, s);
 }
 
 // M = 1 over many rows: the register-resident kernel; returns MLQ_ERR_UNSUPPORTED
@@ -486,7 +514,7 @@ static int launch_q1(const uint8_t *W, const float *x, float *out, int n_rows, i
     if (!c) return MLQ_ERR_NO_DEVICE;
     const int U = K / Fmt<QT>::UE;
     const int upl = (U + 31) / 32;
-    if (n_rows < 4 * c->num_sms * kFastWarps || getenv("MLQ_GEMV_GENERIC")) return MLQ_ERR_UNSUPPORTED;
+    if (n_rows < 8 * c->num_sms * kFastWarps || getenv("MLQ_GEMV_GENERIC")) return MLQ_ERR_UNSUPPORTED;
     // only the variants that stay inside the 96 registers a 544-thread CTA allows:
     // 64-element units at 1 per lane (K <= 2048), 32-element units at <= 3 (K <= 3072)
     if constexpr (Fmt<QT>::UE == 64) {
@@ -692,13 +720,15 @@ __global__ void k_quantize_q8_0(const float *__restrict__ x, uint8_t *__restrict
         if (d == 0.0f) d = 1.0f;
         const float id = __fdiv_rn(1.0f, d);
         const float t = fminf(fmaxf(__fmul_rn(v, id), -127.0f), 127.0f);
-        uint8_t *dst = q8 + b * 34;
-        dst[2 + lane] = (uint8_t)(int8_t)__float2int_rn(t);
-        if (lane == 0) {
-            const unsigned short h = __half_as_ushort(__float2half_rn(d));
-            dst[0] = (uint8_t)(h & 0xFF);
-            dst[1] = (uint8_t)(h >> 8);
-        }
+        const uint32_t qb = (uint32_t)__float2int_rn(t) & 0xFFu;
+        unsigned short d16;
+        asm("cvt.rn.f16.f32 %0, %1;" : "=h"(d16) : "f"(d));
+        // the 34-byte block as 17 little-endian 16-bit words: word 0 = d, word i = (q[2i-2], q[2i-1])
+        const uint32_t qlo = __shfl_sync(0xffffffffu, qb, (2 * lane - 2) & 31);
+        const uint32_t qhi = __shfl_sync(0xffffffffu, qb, (2 * lane - 1) & 31);
+        unsigned short *dst = reinterpret_cast<unsigned short *>(q8 + b * 34);
+        if (lane == 0) dst[0] = d16;
+        else if (lane <= 16) dst[lane] = (unsigned short)(qlo | (qhi << 8));
     }
 }
 
