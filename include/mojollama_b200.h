@@ -93,6 +93,18 @@ int mlq_dequantize(const void *W, int qt, float *out, int64_t n);
 int mlq_quantize_q8_0(const float *x, uint8_t *q8, int64_t n);
 /* W (qt) times Q8_0-quantized activations x_q8 [B][n_cols/32 blocks] */
 int mlq_matmul_q8act(const void *W, int qt, const uint8_t *x_q8, float *out, int n_rows, int n_cols, int B);
+/* Same product for callers that cannot let the library allocate device memory (a
+   process whose HBM is all owned by its own allocator, a decode loop that must not
+   hit cudaMalloc/cudaFree).  No counterpart in the reference.  Allocates nothing: the
+   fp32 activations go to a fixed 65536-element (256 KB) scratch array resident on
+   every device that loads the library; B * n_cols beyond that is rejected with
+   MLQ_ERR_CAPACITY.  W, x_q8 and out must be device memory; runs asynchronously on
+   `stream` (a cudaStream_t, 0 = legacy default).  All calls on a device share the
+   scratch, so calls that may overlap on the GPU race.  The first call on a device
+   looks up the scratch address with that device current: make it before any stream
+   capture. */
+int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_q8, float *out, int n_rows, int n_cols,
+                             int B, void *stream);
 
 /* ---- row / elementwise ops (out may equal x: in place) ---- */
 /* out = x * w / sqrt(mean(x^2) + eps) per row (w may be NULL = ones).  sanitize = 1

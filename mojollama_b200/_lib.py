@@ -55,6 +55,7 @@ def core() -> ctypes.CDLL:
     so.mlq_dequantize.argtypes = [_vp, _ci, _vp, ctypes.c_int64]
     so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
     so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
+    so.mlq_matmul_q8act_noalloc.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci, _vp]
     _ll = ctypes.c_longlong
     so.mlq_rms_norm.argtypes = [_vp, _vp, _vp, _ci, _ci, ctypes.c_float, _ci, _vp]
     so.mlq_silu.argtypes = [_vp, _vp, _ll, _ci]

@@ -431,7 +431,7 @@ static int stages_for(int fixed, int stage_bytes) {
 template <typename Kern>
 static int launch_gemv_kernel(Kern kern, GemvArgs &a, int smem, cudaStream_t s, bool &attr_set,
                               int threads = kThreads) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     if (!attr_set) {
         if (!MLQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
@@ -450,7 +450,7 @@ static int launch_gemv_kernel(Kern kern, GemvArgs &a, int smem, cudaStream_t s, 
 
 template <int QT, int M>
 static int launch_q_m(const uint8_t *W, const float *x, float *out, int n_rows, int K, int nb_x, cudaStream_t s) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
     int rpt = (int)(kStageTarget / rb);
@@ -510,7 +510,7 @@ static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_ro
 // when the shape does not suit it (few rows, or too many units per lane).
 template <int QT>
 static int launch_q1(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     const int U = K / Fmt<QT>::UE;
     const int upl = (U + 31) / 32;
@@ -572,7 +572,7 @@ static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, in
 
 template <typename WT>
 static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     const WT *w = reinterpret_cast<const WT *>(W);
     const int V = 16 / sizeof(WT);
@@ -695,7 +695,7 @@ __global__ void k_dequant(const uint8_t *__restrict__ W, int qt, float *__restri
 }
 
 int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStream_t s) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     long long blocks = (n + 255) / 256;
     if (blocks > (long long)c->num_sms * 32) blocks = (long long)c->num_sms * 32;
@@ -733,7 +733,7 @@ __global__ void k_quantize_q8_0(const float *__restrict__ x, uint8_t *__restrict
 }
 
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s) {
-    Ctx *c = ctx();
+    const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
     const long long nblk = n / 32;
     long long blocks = (nblk * 32 + 255) / 256;

@@ -29,6 +29,20 @@ struct Ctx {
     int *d_status = nullptr;         // device error word (0 = ok), written by bounded waits
 };
 Ctx *ctx();                          // current device's context (initialises on first use)
+
+// What the kernel launchers need from the device: SM count and the device status word.
+// Normally taken from ctx(); an entry point that must not allocate installs its own
+// for the duration of its launches with LaunchEnvScope (ctx() allocates on first use).
+struct LaunchEnv {
+    int num_sms;
+    int *d_status;
+};
+const LaunchEnv *launch_env();
+struct LaunchEnvScope {
+    explicit LaunchEnvScope(const LaunchEnv *e);
+    ~LaunchEnvScope();
+    const LaunchEnv *prev;
+};
 cudaStream_t stream();
 int *dev_status();
 void count_launch(int n = 1);

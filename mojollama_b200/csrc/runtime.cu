@@ -103,6 +103,21 @@ cudaStream_t stream() {
     return c ? c->stream : nullptr;
 }
 
+static thread_local const LaunchEnv *t_env_override = nullptr;
+static thread_local LaunchEnv t_env_ctx;
+
+const LaunchEnv *launch_env() {
+    if (t_env_override) return t_env_override;
+    Ctx *c = ctx();
+    if (!c) return nullptr;
+    t_env_ctx.num_sms = c->num_sms;
+    t_env_ctx.d_status = c->d_status;
+    return &t_env_ctx;
+}
+
+LaunchEnvScope::LaunchEnvScope(const LaunchEnv *e) : prev(t_env_override) { t_env_override = e; }
+LaunchEnvScope::~LaunchEnvScope() { t_env_override = prev; }
+
 int *dev_status() {
     Ctx *c = ctx();
     return c ? c->d_status : nullptr;
