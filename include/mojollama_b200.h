@@ -127,6 +127,52 @@ int mlq_rope_init(float *cos_t, float *sin_t, int max_ctx, int head_dim, int rop
 int mlq_rope_neox(float *buf, int rows, int row_stride, int n_heads, int head_dim, const int *pos, int pos_scalar,
                   const float *cos_t, const float *sin_t, int rope_dim, int max_ctx);
 
+/* ---- decode attention (one query per sequence), fp32 KV ---- */
+/* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);
+   head h uses KV head h / (n_head / n_kv_head); window > 0 attends the last `window`
+   positions only; q, out [n_head*head_dim] */
+int mlq_attn_decode_flat(const float *q, const float *k_cache, const float *v_cache, float *out, int seq_len,
+                         int n_head, int n_kv_head, int head_dim, int window);
+/* paged KV: k_pages / v_pages [n_pages][page_size][n_kv_head*head_dim]; table [B][table_stride]
+   logical -> physical page; seq_lens [B]; q, out [B][n_head*head_dim] */
+int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_pages, const int *table,
+                          int table_stride, int page_size, int n_pages, const int *seq_lens, int B, int n_head,
+                          int n_kv_head, int head_dim, int window, float *out);
+
+/* ---- PagedAttention bookkeeping: the reference's structs, byte for byte
+   (cengine_batch_instr.c:160-207).  pages / k / v are device memory in this build. ---- */
+typedef struct {
+    int page_size;     /* KV slots per page */
+    int n_pages;       /* physical pages in the pool */
+    float *pages;      /* [n_layers][n_pages][page_size][nkh*hd] K, then the same for V (device) */
+    int *table;        /* [1024] logical page -> physical page, -1 = unmapped (host) */
+    int *free_pages;   /* LIFO free list (host) */
+    int free_count;
+    int _nkh;
+    int _hd;
+    int _n_layers;
+} MlqPageTable;
+
+typedef struct {
+    float *k, *v;      /* [L][1024][64][nkh*hd] each (device) */
+    int n_blocks, seq_len[64], block_map[64][1024];
+    MlqPageTable pt;
+} MlqKVBlock;
+
+int  mlq_page_table_init(MlqPageTable *pt, int max_pages, int page_size, int nkh, int hd, int n_layers);
+int  mlq_page_table_alloc(MlqPageTable *pt);                 /* -1 when full */
+void mlq_page_table_free(MlqPageTable *pt, int page_id);
+void mlq_map_page(MlqPageTable *pt, int logical_page, int physical_page);
+void mlq_page_table_destroy(MlqPageTable *pt);               /* frees pool, table, free list */
+int  mlq_kv_init(MlqKVBlock *kv, int L, int nkh, int hd);
+int  mlq_kv_alloc(MlqKVBlock *kv);
+void mlq_kv_free(MlqKVBlock *kv);
+size_t mlq_sizeof_page_table(void);
+size_t mlq_sizeof_kv_block(void);
+/* simd_ops.c:209: copy one position's rows to offset n_past*nkh*hd (layer ignored) */
+int  mlq_kv_cache_update(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                         int n_past, int max_seq, int nkh, int hd);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,11 @@
 
 #include <stdint.h>
 
+#include "mojollama_b200.h"
+
+typedef MlqPageTable PageTable;   /* cengine_batch_instr.c:160-171 */
+typedef MlqKVBlock KVBlock;       /* cengine_batch_instr.c:204-207 */
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -76,6 +81,15 @@ void softmax(float *x, int n);
 void silu_omp(float *x, int n);
 /* cengine_batch_instr.c:674 */
 void rope_init(float *cos_table, float *sin_table, int max_ctx, int hd, int rope_dim);
+/* cengine_batch_instr.c:173, 189, 194, 199, 208, 214 (pages / k / v in device memory here) */
+void page_table_init(PageTable *pt, int max_pages, int page_size, int nkh, int hd, int n_layers);
+int page_table_alloc(PageTable *pt);
+void page_table_free(PageTable *pt, int page_id);
+void map_page(PageTable *pt, int logical_page, int physical_page);
+void kv_init(KVBlock *kv, int L, int NKH, int HD);
+int kv_alloc(KVBlock *kv);
+/* cengine_batch_instr.c:141 -- static in the reference, exported here */
+void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd);
 
 #else  /* MLQ_REF_ABI_SIMD_OPS */
 /* ================================== simd_ops.so set ================================== */
@@ -86,7 +100,18 @@ void residual_add(float *out, const float *a, const float *b, int n);
 void softmax(float *x, int n);
 void apply_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos, float rope_base);
 void set_num_threads(int n);
+/* simd_ops.c:159, 209 */
+void attention_forward(const float *q, const float *k_cache, const float *v_cache, float *out, int n_heads,
+                       int n_kv_heads, int head_dim, int n_past, int max_seq);
+void kv_cache_update(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                     int n_past, int max_seq, int n_kv_heads, int head_dim);
 #endif /* MLQ_REF_ABI_SIMD_OPS */
+
+/* ================================ gqa_attention.so set ================================ */
+/* gqa_attention.c:93 */
+void gqa_attention_decode(const float *q, const float *k_cache, const float *v_cache, float *out, int seq_len,
+                          int n_head, int n_kv_head, int head_dim, float *workspace);
+/* end of gqa_attention.so set */
 
 #ifdef __cplusplus
 }

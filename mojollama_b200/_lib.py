@@ -56,6 +56,23 @@ def core() -> ctypes.CDLL:
     so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
     so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
     so.mlq_matmul_q8act_noalloc.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci, _vp]
+    so.mlq_attn_decode_flat.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
+    so.mlq_attn_decode_paged.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _ci, _vp]
+    so.mlq_page_table_init.argtypes = [_vp, _ci, _ci, _ci, _ci, _ci]
+    so.mlq_page_table_alloc.argtypes = [_vp]
+    so.mlq_page_table_free.argtypes = [_vp, _ci]
+    so.mlq_page_table_free.restype = None
+    so.mlq_map_page.argtypes = [_vp, _ci, _ci]
+    so.mlq_map_page.restype = None
+    so.mlq_page_table_destroy.argtypes = [_vp]
+    so.mlq_page_table_destroy.restype = None
+    so.mlq_kv_init.argtypes = [_vp, _ci, _ci, _ci]
+    so.mlq_kv_alloc.argtypes = [_vp]
+    so.mlq_kv_free.argtypes = [_vp]
+    so.mlq_kv_free.restype = None
+    so.mlq_sizeof_page_table.restype = ctypes.c_size_t
+    so.mlq_sizeof_kv_block.restype = ctypes.c_size_t
+    so.mlq_kv_cache_update.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
     _ll = ctypes.c_longlong
     so.mlq_rms_norm.argtypes = [_vp, _vp, _vp, _ci, _ci, ctypes.c_float, _ci, _vp]
     so.mlq_silu.argtypes = [_vp, _vp, _ll, _ci]

@@ -98,3 +98,18 @@ void rope_init(float *cos_table, float *sin_table, int max_ctx, int hd, int rope
     /* the reference uses 10000^(2j/hd) with hd (not rope_dim) in the exponent */
     mlq_rope_init(cos_table, sin_table, max_ctx, hd, rope_dim, 10000.0);
 }
+
+/* PagedAttention (cengine_batch_instr.c:173-214) */
+void page_table_init(PageTable *pt, int max_pages, int page_size, int nkh, int hd, int n_layers) {
+    mlq_page_table_init(pt, max_pages, page_size, nkh, hd, n_layers);
+}
+int page_table_alloc(PageTable *pt) { return mlq_page_table_alloc(pt); }
+void page_table_free(PageTable *pt, int page_id) { mlq_page_table_free(pt, page_id); }
+void map_page(PageTable *pt, int logical_page, int physical_page) { mlq_map_page(pt, logical_page, physical_page); }
+void kv_init(KVBlock *kv, int L, int NKH, int HD) { mlq_kv_init(kv, L, NKH, HD); }
+int kv_alloc(KVBlock *kv) { return mlq_kv_alloc(kv); }
+
+/* cengine_batch_instr.c:141 (static there): flat KV [sl][nkh*hd] */
+void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd) {
+    mlq_attn_decode_flat(q, kc, vc, o, sl, nh, nkh, hd, 0);
+}

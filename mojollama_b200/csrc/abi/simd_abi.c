@@ -14,3 +14,14 @@ void apply_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, i
     mlq_rope_interleaved(q, k, n_heads, n_kv_heads, head_dim, pos, rope_base);
 }
 void set_num_threads(int n) { (void)n; }
+
+/* simd_ops.c:159: k/v caches [max_seq][n_kv_heads][head_dim], n_past+1 positions */
+void attention_forward(const float *q, const float *k_cache, const float *v_cache, float *out, int n_heads,
+                       int n_kv_heads, int head_dim, int n_past, int max_seq) {
+    (void)max_seq;
+    mlq_attn_decode_flat(q, k_cache, v_cache, out, n_past + 1, n_heads, n_kv_heads, head_dim, 0);
+}
+void kv_cache_update(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                     int n_past, int max_seq, int n_kv_heads, int head_dim) {
+    mlq_kv_cache_update(k_cache, v_cache, k_new, v_new, layer, n_past, max_seq, n_kv_heads, head_dim);
+}

@@ -1,0 +1,341 @@
+// Decode attention (one new query per sequence) over a flat or paged fp32 KV cache.
+//
+// Replaces gqa_attention_decode (gqa_attention.c:93: per KV head, Q.K^T / sqrt(hd) by
+// sgemm, softmax, P.V), the static gqa of cengine_batch_instr.c:141 and its paged
+// gather (cengine_batch_instr.c:1354-1401), and attention_forward (simd_ops.c:159).
+//
+// KV addressing (KVView): slot t of a sequence lives in page table[t / page_size]
+// (identity when there is no table) at row t % page_size; a row holds NKH*HD floats,
+// K and V in separate regions:
+//   flat cache  [seq][NKH*HD]                      page_size = huge, table = null
+//   paged pool  [page][page_size][NKH*HD] per layer  (PageTable, cengine_batch_instr.c:160-214)
+// The kernel reads pages in place through the table -- no gather copy.
+//
+// Split-K flash decode: CTA (split, kv head g, sequence b) streams a contiguous chunk
+// of positions in 32-position tiles through shared memory, computes the scores of all
+// NH/NKH query heads that share g, keeps an online softmax (running max / sum) per
+// head and accumulates P.V in registers; it writes (max, sum, acc[HD]) per head and
+// split.  k_attn_merge combines the splits with their log-sum-exp weights.  With one
+// split the first kernel writes the output directly.  Optional sliding window: only
+// the last `window` positions are attended (GPT-OSS alternate layers).
+// Roofline: HBM-bound on the K and V rows read (2 * seq * NKH * HD * 4 bytes per
+// sequence and layer).
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "mlq_internal.h"
+
+namespace mlq {
+
+struct KVView {
+    const float *k, *v;      // base of the K and V regions
+    const int *table;        // [B][max_pages] physical page of each logical page, or null
+    int table_stride;        // ints between sequences' tables
+    long long page_stride;   // floats between pages
+    int page_size;           // slots per page
+    int row_stride;          // floats between slots (NKH * HD)
+};
+
+__device__ __forceinline__ long long kv_offset(const KVView &kv, int b, int t) {
+    if (!kv.table) return (long long)t * kv.row_stride;
+    const int page = kv.table[(size_t)b * kv.table_stride + t / kv.page_size];
+    return (long long)page * kv.page_stride + (long long)(t % kv.page_size) * kv.row_stride;
+}
+
+constexpr int kTile = 32;          // positions per shared-memory tile
+constexpr int kAttnThreads = 128;
+
+// smem: q [rep][HD], K tile [kTile][HD+1], V tile [kTile][HD], p [rep][kTile]
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__restrict__ q, KVView kv,
+                                                              const int *__restrict__ seq_lens, int seq_len_scalar,
+                                                              int nh, int nkh, int window, float scale,
+                                                              int chunk, float *__restrict__ out,
+                                                              float *__restrict__ part_ml, float *__restrict__ part_acc) {
+    extern __shared__ float sm[];
+    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int rep = nh / nkh;
+    const int n_splits = gridDim.x;
+    const int sl = seq_lens ? seq_lens[b] : seq_len_scalar;
+    const int lo_all = (window > 0 && sl > window) ? sl - window : 0;
+    const int t0 = lo_all + split * chunk;
+    const int t1 = min(sl, t0 + chunk);
+    float *qs = sm;                                  // rep * HD
+    float *ks = qs + rep * HD;                       // kTile * (HD + 1)
+    float *vs = ks + kTile * (HD + 1);               // kTile * HD
+    float *ps = vs + kTile * HD;                     // rep * kTile
+    float *ms = ps + rep * kTile;                    // rep running max
+    float *ls = ms + rep;                            // rep running sum
+    float *cs = ls + rep;                            // rep correction factor of this tile
+    const int tid = threadIdx.x;
+    for (int i = tid; i < rep * HD; i += blockDim.x)
+        qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i] * scale;
+    for (int h = tid; h < rep; h += blockDim.x) {
+        ms[h] = -INFINITY;
+        ls[h] = 0.0f;
+    }
+    // accumulators: thread owns (h, d) pairs tid, tid + 128, ...
+    constexpr int kMaxAcc = 16;   // rep * HD <= 16 * 128
+    float acc[kMaxAcc];
+#pragma unroll
+    for (int i = 0; i < kMaxAcc; i++) acc[i] = 0.0f;
+    __syncthreads();
+
+    for (int base = t0; base < t1; base += kTile) {
+        const int nt = min(kTile, t1 - base);
+        // stage K and V rows of this tile (coalesced along HD)
+        for (int i = tid; i < nt * HD; i += blockDim.x) {
+            const int t = i / HD, d = i - t * HD;
+            const long long off = kv_offset(kv, b, base + t) + (long long)g * HD + d;
+            ks[t * (HD + 1) + d] = kv.k[off];
+            vs[t * HD + d] = kv.v[off];
+        }
+        __syncthreads();
+        // scores p[h][t] = q_h . k_t (q already scaled)
+        for (int i = tid; i < rep * kTile; i += blockDim.x) {
+            const int h = i / kTile, t = i - h * kTile;
+            float s = -INFINITY;
+            if (t < nt) {
+                s = 0.0f;
+                const float *qh = qs + h * HD;
+                const float *kt = ks + t * (HD + 1);
+#pragma unroll 8
+                for (int d = 0; d < HD; d++) s = fmaf(qh[d], kt[d], s);
+            }
+            ps[i] = s;
+        }
+        __syncthreads();
+        // online softmax update per head (one warp per head)
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int h = warp; h < rep; h += blockDim.x / 32) {
+            const float s = ps[h * kTile + lane];
+            float mx = s;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float m_old = ms[h];
+            const float m_new = fmaxf(m_old, mx);
+            const float e = (lane < nt) ? expf(s - m_new) : 0.0f;
+            float sum = e;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            ps[h * kTile + lane] = e;
+            if (lane == 0) {
+                const float c = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
+                cs[h] = c;
+                ls[h] = ls[h] * c + sum;
+                ms[h] = m_new;
+            }
+        }
+        __syncthreads();
+        // acc = acc * c + sum_t p[h][t] v[t][d]
+#pragma unroll
+        for (int j = 0; j < kMaxAcc; j++) {
+            const int i = tid + j * kAttnThreads;
+            if (i < rep * HD) {
+                const int h = i / HD, d = i - h * HD;
+                float a = acc[j] * cs[h];
+                const float *ph = ps + h * kTile;
+                for (int t = 0; t < nt; t++) a = fmaf(ph[t], vs[t * HD + d], a);
+                acc[j] = a;
+            }
+        }
+        __syncthreads();
+    }
+    // write the result (one split) or this split's partial state
+#pragma unroll
+    for (int j = 0; j < kMaxAcc; j++) {
+        const int i = tid + j * kAttnThreads;
+        if (i < rep * HD) {
+            const int h = i / HD, d = i - h * HD;
+            const int head = g * rep + h;
+            if (n_splits == 1) {
+                const float l = ls[h];
+                out[((size_t)b * nh + head) * HD + d] = (l > 0.0f) ? acc[j] / l : 0.0f;
+            } else {
+                part_acc[(((size_t)b * nh + head) * n_splits + split) * HD + d] = acc[j];
+            }
+        }
+    }
+    if (n_splits > 1) {
+        for (int h = tid; h < rep; h += blockDim.x) {
+            const size_t o = (((size_t)b * nh + g * rep + h) * n_splits + split) * 2;
+            part_ml[o] = ms[h];
+            part_ml[o + 1] = ls[h];
+        }
+    }
+}
+
+// combine splits: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s
+__global__ void k_attn_merge(const float *__restrict__ part_ml, const float *__restrict__ part_acc, int n_splits,
+                             int hd, float *__restrict__ out) {
+    const int bh = blockIdx.x;   // b * nh + head
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; s++) M = fmaxf(M, part_ml[((size_t)bh * n_splits + s) * 2]);
+    float L = 0.0f;
+    for (int s = 0; s < n_splits; s++) {
+        const float m = part_ml[((size_t)bh * n_splits + s) * 2];
+        if (m != -INFINITY) L += expf(m - M) * part_ml[((size_t)bh * n_splits + s) * 2 + 1];
+    }
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float a = 0.0f;
+        for (int s = 0; s < n_splits; s++) {
+            const float m = part_ml[((size_t)bh * n_splits + s) * 2];
+            if (m != -INFINITY) a += expf(m - M) * part_acc[((size_t)bh * n_splits + s) * hd + d];
+        }
+        out[(size_t)bh * hd + d] = (L > 0.0f) ? a / L : 0.0f;
+    }
+}
+
+// KV append: row (b, pos_b) of K and V gets k_new/v_new [B][NKH*HD]
+__global__ void k_kv_write(KVView kv, float *k_base, float *v_base, const float *__restrict__ k_new,
+                           const float *__restrict__ v_new, const int *__restrict__ pos, int pos_scalar, int row) {
+    const int b = blockIdx.y;
+    const int t = pos ? pos[b] : pos_scalar;
+    const long long off = kv_offset(kv, b, t);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
+        k_base[off + i] = k_new[(size_t)b * row + i];
+        v_base[off + i] = v_new[(size_t)b * row + i];
+    }
+}
+
+static size_t attn_smem(int rep, int hd) {
+    return sizeof(float) * ((size_t)rep * hd + kTile * (hd + 1) + kTile * hd + rep * kTile + 3 * rep);
+}
+
+// q [B][nh][hd] -> out [B][nh][hd]; scratch holds the split partials when needed
+int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
+                       int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
+                       float *scratch, size_t scratch_bytes, cudaStream_t s) {
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    if (nkh <= 0 || nh % nkh) { set_error(MLQ_ERR_ARG, "attention: n_head %d not a multiple of n_kv_head %d", nh, nkh); return MLQ_ERR_ARG; }
+    const int rep = nh / nkh;
+    if ((long long)rep * hd > 16LL * kAttnThreads) {
+        set_error(MLQ_ERR_CAPACITY, "attention: n_head/n_kv_head * head_dim = %d > %d", rep * hd, 16 * kAttnThreads);
+        return MLQ_ERR_CAPACITY;
+    }
+    int span = max_seq_len;
+    if (window > 0 && span > window) span = window;
+    // enough CTAs to cover the SMs; >= 64 positions per split
+    const int ctas = B * nkh;
+    int n_splits = 1;
+    while (n_splits < 64 && ctas * n_splits < 2 * env->num_sms && span / (n_splits * 2) >= 64) n_splits *= 2;
+    const int chunk = (span + n_splits - 1) / n_splits;
+    const size_t need = (size_t)B * nh * n_splits * (hd + 2) * sizeof(float);
+    if (n_splits > 1 && (!scratch || scratch_bytes < need)) n_splits = 1;
+    const int chunk1 = n_splits == 1 ? (span > 0 ? span : 1) : chunk;
+    float *part_ml = scratch;
+    float *part_acc = scratch ? scratch + (size_t)B * nh * n_splits * 2 : nullptr;
+    dim3 grid(n_splits, nkh, B);
+    const size_t smem = attn_smem(rep, hd);
+#define MLQ_ATTN_CASE(HD_)                                                                                    \
+    case HD_: {                                                                                               \
+        static bool attr = false;                                                                             \
+        if (!attr) {                                                                                          \
+            cudaFuncSetAttribute(k_attn_decode<HD_>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024); \
+            attr = true;                                                                                      \
+        }                                                                                                     \
+        k_attn_decode<HD_><<<grid, kAttnThreads, smem, s>>>(q, kv, seq_lens_dev, seq_len_scalar, nh, nkh,     \
+                                                            window, scale, chunk1, out, part_ml, part_acc);   \
+    } break;
+    switch (hd) {
+        MLQ_ATTN_CASE(64)
+        MLQ_ATTN_CASE(80)
+        MLQ_ATTN_CASE(96)
+        MLQ_ATTN_CASE(128)
+        MLQ_ATTN_CASE(256)
+        default:
+            set_error(MLQ_ERR_UNSUPPORTED, "attention: head_dim %d (supported 64, 80, 96, 128, 256)", hd);
+            return MLQ_ERR_UNSUPPORTED;
+    }
+#undef MLQ_ATTN_CASE
+    count_launch();
+    if (n_splits > 1) {
+        k_attn_merge<<<B * nh, 128, 0, s>>>(part_ml, part_acc, n_splits, hd, out);
+        count_launch();
+    }
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
+                    const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s) {
+    dim3 grid((row + 255) / 256, B);
+    k_kv_write<<<grid, 256, 0, s>>>(kv, k_base, v_base, k_new, v_new, pos_dev, pos_scalar, row);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+size_t attn_scratch_bytes(int B, int nh, int hd) { return (size_t)B * nh * 64 * (hd + 2) * sizeof(float); }
+
+}  // namespace mlq
+
+// ====================================================================================== C-ABI
+using namespace mlq;
+
+extern "C" {
+
+// flat KV: k_cache/v_cache [seq_len][n_kv_head * head_dim]
+int mlq_attn_decode_flat(const float *q, const float *k_cache, const float *v_cache, float *out, int seq_len,
+                         int n_head, int n_kv_head, int head_dim, int window) {
+    if (!q || !k_cache || !v_cache || !out || seq_len <= 0 || n_head <= 0 || n_kv_head <= 0 || head_dim <= 0) {
+        set_error(MLQ_ERR_ARG, "mlq_attn_decode_flat: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    CallScope cs;
+    const size_t kvb = sizeof(float) * (size_t)seq_len * n_kv_head * head_dim;
+    const float *dq = (const float *)cs.in(q, sizeof(float) * (size_t)n_head * head_dim);
+    const float *dk = (const float *)cs.in(k_cache, kvb);
+    const float *dv = (const float *)cs.in(v_cache, kvb);
+    float *dout = (float *)cs.out(out, sizeof(float) * (size_t)n_head * head_dim);
+    const size_t sb = attn_scratch_bytes(1, n_head, head_dim);
+    float *scr = (float *)cs.scratch(sb);
+    if (cs.failed) return cs.finish();
+    KVView kv{dk, dv, nullptr, 0, 0, 1 << 30, n_kv_head * head_dim};
+    int rc = launch_attn_decode(dq, kv, nullptr, seq_len, seq_len, 1, n_head, n_kv_head, head_dim, window,
+                                1.0f / sqrtf((float)head_dim), dout, scr, sb, stream());
+    if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
+    return cs.finish();
+}
+
+// paged KV: pages hold [n_pages][page_size][n_kv_head*head_dim] for K (at k_pages) and V
+// (at v_pages); table [B][table_stride] maps logical -> physical pages; seq_lens [B]
+int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_pages, const int *table,
+                          int table_stride, int page_size, int n_pages, const int *seq_lens, int B, int n_head,
+                          int n_kv_head, int head_dim, int window, float *out) {
+    if (!q || !k_pages || !v_pages || !table || !seq_lens || !out || B <= 0 || page_size <= 0 || n_pages <= 0 ||
+        table_stride <= 0 || n_head <= 0 || n_kv_head <= 0 || head_dim <= 0) {
+        set_error(MLQ_ERR_ARG, "mlq_attn_decode_paged: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    int max_len = 0;
+    if (!is_device_ptr(seq_lens)) {
+        for (int b = 0; b < B; b++) {
+            if (seq_lens[b] < 0 || seq_lens[b] > table_stride * page_size) {
+                set_error(MLQ_ERR_CAPACITY, "mlq_attn_decode_paged: seq_len %d beyond the page table", seq_lens[b]);
+                return MLQ_ERR_CAPACITY;
+            }
+            if (seq_lens[b] > max_len) max_len = seq_lens[b];
+        }
+    } else {
+        max_len = table_stride * page_size;
+    }
+    CallScope cs;
+    const size_t pool = sizeof(float) * (size_t)n_pages * page_size * n_kv_head * head_dim;
+    const float *dq = (const float *)cs.in(q, sizeof(float) * (size_t)B * n_head * head_dim);
+    const float *dk = (const float *)cs.in(k_pages, pool);
+    const float *dv = (const float *)cs.in(v_pages, pool);
+    const int *dt = (const int *)cs.in(table, sizeof(int) * (size_t)B * table_stride);
+    const int *dl = (const int *)cs.in(seq_lens, sizeof(int) * (size_t)B);
+    float *dout = (float *)cs.out(out, sizeof(float) * (size_t)B * n_head * head_dim);
+    const size_t sb = attn_scratch_bytes(B, n_head, head_dim);
+    float *scr = (float *)cs.scratch(sb);
+    if (cs.failed) return cs.finish();
+    KVView kv{dk, dv, dt, table_stride, (long long)page_size * n_kv_head * head_dim, page_size,
+              n_kv_head * head_dim};
+    int rc = launch_attn_decode(dq, kv, dl, 0, max_len, B, n_head, n_kv_head, head_dim, window,
+                                1.0f / sqrtf((float)head_dim), dout, scr, sb, stream());
+    if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
+    return cs.finish();
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+// PagedAttention bookkeeping of the reference (cengine_batch_instr.c:160-214) with the
+// same structs, byte for byte, so ctypes mirrors (forward/zaya_bc.py:32-130 of the
+// reference) keep working:
+//   PageTable { page_size, n_pages, pages, table, free_pages, free_count, _nkh, _hd, _n_layers }
+//   KVBlock   { k, v, n_blocks, seq_len[64], block_map[64][1024], pt }
+// Difference: `pages`, `k` and `v` are device memory (HBM) here -- the KV cache lives
+// where attention runs; `table` and `free_pages` stay host memory (pure bookkeeping,
+// uploaded with each step).  The page pool is [n_layers][n_pages][page_size][nkh*hd]
+// for K followed by the same for V (cengine_batch_instr.c:1354-1361).
+#include <cuda_runtime.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "mlq_internal.h"
+
+namespace mlq {
+constexpr int kMaxBlocks = 1024;   // MAX_BLOCKS, cengine_batch_instr.c:23
+constexpr int kBlockSize = 64;     // BLOCK_SIZE, cengine_batch_instr.c:22
+}  // namespace mlq
+
+using namespace mlq;
+
+extern "C" {
+
+int mlq_page_table_init(MlqPageTable *pt, int max_pages, int page_size, int nkh, int hd, int n_layers) {
+    if (!pt || max_pages <= 0 || page_size <= 0 || nkh <= 0 || hd <= 0 || n_layers <= 0) {
+        set_error(MLQ_ERR_ARG, "page_table_init: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    if (!ctx()) return mlq_last_error();
+    memset(pt, 0, sizeof(*pt));
+    pt->page_size = page_size;
+    pt->n_pages = max_pages;
+    pt->_nkh = nkh;
+    pt->_hd = hd;
+    pt->_n_layers = n_layers;
+    const size_t total = (size_t)n_layers * max_pages * page_size * nkh * hd * 2;
+    void *d = nullptr;
+    if (!MLQ_CUDA(cudaMalloc(&d, total * sizeof(float)))) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaMemset(d, 0, total * sizeof(float)))) { cudaFree(d); return MLQ_ERR_CUDA; }
+    pt->pages = (float *)d;
+    pt->table = (int *)malloc(kMaxBlocks * sizeof(int));
+    pt->free_pages = (int *)malloc((size_t)max_pages * sizeof(int));
+    if (!pt->table || !pt->free_pages) {
+        set_error(MLQ_ERR_CAPACITY, "page_table_init: host allocation failed");
+        return MLQ_ERR_CAPACITY;
+    }
+    memset(pt->table, -1, kMaxBlocks * sizeof(int));
+    for (int i = 0; i < max_pages; i++) pt->free_pages[i] = max_pages - 1 - i;   // LIFO: page 0 first
+    pt->free_count = max_pages;
+    return MLQ_OK;
+}
+
+int mlq_page_table_alloc(MlqPageTable *pt) {
+    if (!pt || pt->free_count <= 0) return -1;
+    return pt->free_pages[--pt->free_count];
+}
+
+void mlq_page_table_free(MlqPageTable *pt, int page_id) {
+    if (pt && pt->free_count < pt->n_pages) pt->free_pages[pt->free_count++] = page_id;
+}
+
+void mlq_map_page(MlqPageTable *pt, int logical_page, int physical_page) {
+    if (pt && logical_page >= 0 && logical_page < kMaxBlocks) pt->table[logical_page] = physical_page;
+}
+
+void mlq_page_table_destroy(MlqPageTable *pt) {
+    if (!pt) return;
+    if (pt->pages) cudaFree(pt->pages);
+    free(pt->table);
+    free(pt->free_pages);
+    memset(pt, 0, sizeof(*pt));
+}
+
+// kv_init (cengine_batch_instr.c:208): flat k/v of L * MAX_BLOCKS * BLOCK_SIZE * nkh * hd
+// floats each plus a page table of MAX_BLOCKS pages of BLOCK_SIZE slots
+int mlq_kv_init(MlqKVBlock *kv, int L, int nkh, int hd) {
+    if (!kv || L <= 0 || nkh <= 0 || hd <= 0) {
+        set_error(MLQ_ERR_ARG, "kv_init: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    if (!ctx()) return mlq_last_error();
+    const size_t sz = (size_t)L * kMaxBlocks * kBlockSize * nkh * hd * sizeof(float);
+    void *k = nullptr, *v = nullptr;
+    if (!MLQ_CUDA(cudaMalloc(&k, sz))) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaMalloc(&v, sz))) { cudaFree(k); return MLQ_ERR_CUDA; }
+    cudaMemset(k, 0, sz);
+    cudaMemset(v, 0, sz);
+    kv->k = (float *)k;
+    kv->v = (float *)v;
+    kv->n_blocks = 0;
+    memset(kv->block_map, -1, sizeof(kv->block_map));
+    memset(kv->seq_len, 0, sizeof(kv->seq_len));
+    return mlq_page_table_init(&kv->pt, kMaxBlocks, kBlockSize, nkh, hd, L);
+}
+
+int mlq_kv_alloc(MlqKVBlock *kv) { return kv ? mlq_page_table_alloc(&kv->pt) : -1; }
+
+void mlq_kv_free(MlqKVBlock *kv) {
+    if (!kv) return;
+    if (kv->k) cudaFree(kv->k);
+    if (kv->v) cudaFree(kv->v);
+    kv->k = kv->v = nullptr;
+    mlq_page_table_destroy(&kv->pt);
+}
+
+size_t mlq_sizeof_page_table(void) { return sizeof(MlqPageTable); }
+size_t mlq_sizeof_kv_block(void) { return sizeof(MlqKVBlock); }
+
+// kv_cache_update (simd_ops.c:209): copy one position's K/V rows (nkh*hd floats) to
+// offset n_past*nkh*hd of flat caches; `layer` and `max_seq` are ignored, as there
+int mlq_kv_cache_update(float *k_cache, float *v_cache, const float *k_new, const float *v_new, int layer,
+                        int n_past, int max_seq, int nkh, int hd) {
+    (void)layer;
+    (void)max_seq;
+    if (!k_cache || !v_cache || !k_new || !v_new || n_past < 0 || nkh <= 0 || hd <= 0) {
+        set_error(MLQ_ERR_ARG, "kv_cache_update: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    const size_t row = (size_t)nkh * hd;
+    const size_t off = (size_t)n_past * row;
+    if (!is_device_ptr(k_cache) && !is_device_ptr(k_new) && !is_device_ptr(v_cache) && !is_device_ptr(v_new)) {
+        memcpy(k_cache + off, k_new, row * sizeof(float));    // all host: nothing for the GPU to do
+        memcpy(v_cache + off, v_new, row * sizeof(float));
+        return MLQ_OK;
+    }
+    cudaStream_t s = stream();
+    if (!MLQ_CUDA(cudaMemcpyAsync(k_cache + off, k_new, row * sizeof(float), cudaMemcpyDefault, s))) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaMemcpyAsync(v_cache + off, v_new, row * sizeof(float), cudaMemcpyDefault, s))) return MLQ_ERR_CUDA;
+    return MLQ_CUDA(cudaStreamSynchronize(s)) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -104,3 +104,95 @@ def rope_neox(buf, n_heads, hd, pos, cos_t, sin_t, rope_dim):
     b[:, :hd2] = a0 * c - a1 * s
     b[:, hd2:2 * hd2] = a1 * c + a0 * s
     return b.reshape(-1).astype(np.float32)
+
+
+def gqa_decode(q, k, v, n_head, n_kv, hd, window=0):
+    """Decode attention of one query per head over a flat KV [seq][n_kv*hd]
+    (gqa_attention.c:93-135, cengine_batch_instr.c:141-158): head h uses KV head
+    h // (n_head // n_kv); scores scaled by 1/sqrt(hd); softmax; P.V.  window > 0
+    keeps the last `window` positions."""
+    q = np.asarray(q, np.float64).reshape(n_head, hd)
+    k = np.asarray(k, np.float64).reshape(-1, n_kv, hd)
+    v = np.asarray(v, np.float64).reshape(-1, n_kv, hd)
+    sl = k.shape[0]
+    lo = sl - window if (window and sl > window) else 0
+    rep = n_head // n_kv
+    out = np.zeros((n_head, hd))
+    for h in range(n_head):
+        g = h // rep
+        s = k[lo:, g, :] @ q[h] / np.sqrt(hd)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        out[h] = p @ v[lo:, g, :]
+    return out.reshape(-1).astype(np.float32)
+
+
+class PagedKV:
+    """The reference's page table semantics (cengine_batch_instr.c:173-202): LIFO free
+    list starting at page 0, logical -> physical table, pages [n_pages][page_size][row]."""
+
+    def __init__(self, n_pages, page_size, row):
+        self.page_size, self.row = page_size, row
+        self.k = np.zeros((n_pages, page_size, row), np.float32)
+        self.v = np.zeros_like(self.k)
+        self.free = list(range(n_pages - 1, -1, -1))
+        self.tables = {}
+
+    def alloc(self):
+        return self.free.pop() if self.free else -1
+
+    def write(self, seq, pos, krow, vrow):
+        t = self.tables.setdefault(seq, {})
+        blk, off = divmod(pos, self.page_size)
+        if blk not in t:
+            t[blk] = self.alloc()
+        self.k[t[blk], off] = krow
+        self.v[t[blk], off] = vrow
+
+    def gather(self, seq, length):
+        t = self.tables[seq]
+        ks = np.stack([self.k[t[p // self.page_size], p % self.page_size] for p in range(length)])
+        vs = np.stack([self.v[t[p // self.page_size], p % self.page_size] for p in range(length)])
+        return ks, vs
+
+
+def _exp_ps_simd_ref(x):
+    """The reference's exp_ps_simd (gqa_attention.c:32-48) as it computes: n = rint(x*log2e
+    + 0.5), f = x*log2e - n, then a Horner chain that starts at 1 and adds the Taylor
+    coefficients of 2^f in reverse order (0.693, 0.240, 0.0555, 0.00962, 0.00133), times
+    2^n.  It is not exp(x) (p(0) = 0.00133); this models the reference, not the math."""
+    x = np.asarray(x, np.float32)
+    t = (x * np.float32(1.4426950408889634)).astype(np.float32)
+    n = np.rint((t + np.float32(0.5)).astype(np.float32)).astype(np.int32)
+    f = (t - n.astype(np.float32)).astype(np.float32)
+    p = np.ones_like(f)
+    for c in (0.6931471805599453, 0.2402265069591007, 0.0555041086648216, 0.0096181291076285,
+              0.0013333558146428):
+        p = (p * f + np.float32(c)).astype(np.float32)
+    biased = np.clip(n + 127, 0, 255).astype(np.uint32)
+    return (p * (biased << np.uint32(23)).view(np.float32)).astype(np.float32)
+
+
+def gqa_decode_reference_quirk(q, k, v, n_head, n_kv, hd):
+    """gqa_attention_decode exactly as the reference computes it single-threaded
+    (gqa_attention.c:50-135): fp32 scores, softmax_simd with exp_ps_simd on the first
+    seq_len - seq_len%8 scores (clamped to [-80, 80] after the max shift), expf on the
+    tail, 1/(sum + 1e-10).  Used only to show the deviation is understood."""
+    q = np.asarray(q, np.float32).reshape(n_head, hd)
+    k = np.asarray(k, np.float32).reshape(-1, n_kv, hd)
+    v = np.asarray(v, np.float32).reshape(-1, n_kv, hd)
+    sl = k.shape[0]
+    rep = n_head // n_kv
+    body = sl - sl % 8
+    out = np.zeros((n_head, hd), np.float64)
+    for h in range(n_head):
+        g = h // rep
+        s = ((k[:, g, :].astype(np.float64) @ q[h].astype(np.float64)).astype(np.float32)
+             * np.float32(1.0 / np.sqrt(np.float32(hd)))).astype(np.float32)
+        m = s.max()
+        e = np.empty(sl, np.float32)
+        e[:body] = _exp_ps_simd_ref(np.clip(s[:body] - m, -80, 80))
+        e[body:] = np.minimum(np.exp((s[body:] - m).astype(np.float64)), 1e38).astype(np.float32)
+        p = e / (e.astype(np.float64).sum() + 1e-10)
+        out[h] = p @ v[:, g, :].astype(np.float64)
+    return out.reshape(-1).astype(np.float32)

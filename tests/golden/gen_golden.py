@@ -68,6 +68,22 @@ def gen_ref(rng, out):
         ops[f"bgemv_x_{qt}"] = xb
         ops[f"bgemv_ref_{qt}"] = ref.batch_matmul(name, w, xb, n, k, b)
     ops["shape"] = np.array([n, k, b], np.int32)
+    # gqa_attention_decode (gqa_attention.c:93, built with the oracle's cblas shim).
+    # Single-threaded: every OpenMP thread of the reference writes the same tmp_scores
+    # buffer (gqa_attention.c:104, 113), so its multi-threaded output is a data race.
+    ref.set_num_threads(1)
+    if ref.gqa is not None:
+        from oracle.ref import fptr
+        for nh, nkh, hd, sl in ((32, 4, 64, 37), (16, 2, 256, 200)):
+            qv = rng.standard_normal(nh * hd).astype(np.float32)
+            kc = rng.standard_normal(sl * nkh * hd).astype(np.float32)
+            vc = rng.standard_normal(sl * nkh * hd).astype(np.float32)
+            out = np.zeros(nh * hd, np.float32)
+            ws = np.zeros(2 * nh * sl + 16, np.float32)
+            ref.gqa.gqa_attention_decode(fptr(qv), fptr(kc), fptr(vc), fptr(out), sl, nh, nkh, hd, fptr(ws))
+            tag = f"{nh}_{nkh}_{hd}_{sl}"
+            ops[f"gqa_q_{tag}"], ops[f"gqa_k_{tag}"], ops[f"gqa_v_{tag}"] = qv, kc, vc
+            ops[f"gqa_out_{tag}"] = out
     return ops
 
 

@@ -49,10 +49,10 @@ def test_engine_alias_exports_reference_symbols(lib):
 
 def test_simd_and_gqa_alias_exports():
     text = open(os.path.join(INC, "mojollama_b200_ref_abi.h")).read()
-    for section, lib in (("simd_ops.so set", "simd_ops.so"), ("gqa_attention.so set", "gqa_attention.so")):
-        if section not in text:
-            continue
-        names = _declared("mojollama_b200_ref_abi.h", section, "#endif")
+    for section, lib, end in (("simd_ops.so set", "simd_ops.so", "#endif"),
+                              ("gqa_attention.so set", "gqa_attention.so", "end of gqa_attention.so set")):
+        names = _declared("mojollama_b200_ref_abi.h", section, end)
+        assert names, section
         missing = [n for n in names if n not in _exports(_lib.lib_path(lib))]
         assert not missing, (lib, missing)
 

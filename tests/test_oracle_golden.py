@@ -70,3 +70,15 @@ def test_quantize_roundtrip_is_a_valid_encoding(qt):
     assert raw.size == F.row_bytes(qt, 1024)
     back = F.dequantize(qt, raw, 1024)
     assert O.rel_l2(back, x) < 0.2
+
+
+@pytest.mark.parametrize("tag", ["32_4_64_37", "16_2_256_200"])
+def test_gqa_reference_output_is_modelled_and_deviates(tag):
+    """gqa_attention_decode of the reference (gqa_attention.c:93) evaluates exp with a
+    reversed polynomial (gqa_attention.c:32-48): the oracle's model of that quirk
+    reproduces the reference's output, and the true softmax attention differs from it.
+    The GPU kernels are checked against the true attention (oracle.ops.gqa_decode)."""
+    nh, nkh, hd, sl = (int(t) for t in tag.split("_"))
+    q, k, v = RO[f"gqa_q_{tag}"], RO[f"gqa_k_{tag}"], RO[f"gqa_v_{tag}"]
+    assert O.rel_l2(RO[f"gqa_out_{tag}"], O.gqa_decode_reference_quirk(q, k, v, nh, nkh, hd)) < 1e-4
+    assert O.rel_l2(RO[f"gqa_out_{tag}"], O.gqa_decode(q, k, v, nh, nkh, hd)) > 1e-2
