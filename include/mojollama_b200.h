@@ -64,7 +64,10 @@ int   mlq_set_stream(void *cuda_stream);
 int   mlq_use_own_stream(void);
 int   mlq_sync(void);                     /* wait for the stream; also reports device-side errors */
 int   mlq_device_status(void);            /* reads and clears the device error word */
-int   mlq_register_weights(const void *host_ptr, size_t bytes);   /* optional pre-residency */
+/* optional pre-residency of a whole host tensor (e.g. a 3-D expert tensor): every pointer
+   inside it then maps to its device copy; unregister before freeing the host memory */
+int   mlq_register_weights(const void *host_ptr, size_t bytes);
+int   mlq_unregister_weights(const void *host_ptr);
 int   mlq_cache_clear(void);              /* drop every cached device copy of host weights */
 size_t mlq_cache_bytes(void);
 int   mlq_num_sms(void);
@@ -126,6 +129,20 @@ int mlq_rope_init(float *cos_t, float *sin_t, int max_ctx, int head_dim, int rop
    (row_stride floats apart, 0 = packed); position per row from pos[] or pos_scalar */
 int mlq_rope_neox(float *buf, int rows, int row_stride, int n_heads, int head_dim, const int *pos, int pos_scalar,
                   const float *cos_t, const float *sin_t, int rope_dim, int max_ctx);
+
+/* ---- mixture of experts ---- */
+/* moe_forward_omp (quant_kernels_omp.c:2066) semantics, GGUF-correct for every expert
+   type: combined = sum_i top_w[i] * down[e] . (silu(clamp(gate[e] . x, +-80)) * (up[e] . x)),
+   e = top_idx[i].  gate/up/down are arrays of per-expert pointers (host arrays; the
+   pointers host or device), gate/up n_ff x n_embd, down n_embd x n_ff; top_k <= 16. */
+int mlq_moe_forward(const void *const *gate, const void *const *up, const void *const *down, const float *x,
+                    int n_ff, int n_embd, int qt_gate, int qt_up, int qt_down, const int *top_idx,
+                    const float *top_w, int top_k, float *combined);
+/* router: logits = W_r . x (E x N, type qt_r), softmax (1/(sum + 1e-10)), top-k with the
+   reference's tie rule (lower expert index first), renorm = 1 rescales the k weights to
+   sum 1 (cengine_batch_instr.c:1113-1152); x [B][N] -> idx, w [B][k]; E <= 256 */
+int mlq_moe_router(const float *x, int B, int N, const void *W_r, int qt_r, int E, int k, int renorm, int *idx,
+                   float *w);
 
 /* ---- decode attention (one query per sequence), fp32 KV ---- */
 /* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);

@@ -88,6 +88,11 @@ void page_table_free(PageTable *pt, int page_id);
 void map_page(PageTable *pt, int logical_page, int physical_page);
 void kv_init(KVBlock *kv, int L, int NKH, int HD);
 int kv_alloc(KVBlock *kv);
+/* quant_kernels_omp.c:2066 */
+void moe_forward_omp(const uint8_t **gate_raw, const uint8_t **up_raw, const uint8_t **down_raw, const float *x_norm,
+                     int n_ff_expert, int n_embd, int qt_gate, int qt_up, int qt_down, const int *top_indices,
+                     const float *top_weights, int top_k, float *combined, float *prealloc_buf,
+                     uint8_t *prealloc_q8);
 /* cengine_batch_instr.c:141 -- static in the reference, exported here */
 void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd);
 

@@ -44,6 +44,7 @@ def core() -> ctypes.CDLL:
     so.mlq_set_stream.argtypes = [_vp]
     so.mlq_use_own_stream.argtypes = []
     so.mlq_register_weights.argtypes = [_vp, ctypes.c_size_t]
+    so.mlq_unregister_weights.argtypes = [_vp]
     so.mlq_cache_bytes.restype = ctypes.c_size_t
     so.mlq_launch_count.restype = ctypes.c_ulonglong
     so.mlq_set_ref_compat.argtypes = [_ci]
@@ -56,6 +57,8 @@ def core() -> ctypes.CDLL:
     so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
     so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
     so.mlq_matmul_q8act_noalloc.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci, _vp]
+    so.mlq_moe_forward.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _vp, _vp, _ci, _vp]
+    so.mlq_moe_router.argtypes = [_vp, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _vp, _vp]
     so.mlq_attn_decode_flat.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
     so.mlq_attn_decode_paged.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _ci, _vp]
     so.mlq_page_table_init.argtypes = [_vp, _ci, _ci, _ci, _ci, _ci]

@@ -113,3 +113,15 @@ int kv_alloc(KVBlock *kv) { return mlq_kv_alloc(kv); }
 void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd) {
     mlq_attn_decode_flat(q, kc, vc, o, sl, nh, nkh, hd, 0);
 }
+
+/* quant_kernels_omp.c:2066; prealloc_buf / prealloc_q8 are not needed (the expert
+   intermediates stay in device scratch) */
+void moe_forward_omp(const uint8_t **gate_raw, const uint8_t **up_raw, const uint8_t **down_raw, const float *x_norm,
+                     int n_ff_expert, int n_embd, int qt_gate, int qt_up, int qt_down, const int *top_indices,
+                     const float *top_weights, int top_k, float *combined, float *prealloc_buf,
+                     uint8_t *prealloc_q8) {
+    (void)prealloc_buf;
+    (void)prealloc_q8;
+    mlq_moe_forward((const void *const *)gate_raw, (const void *const *)up_raw, (const void *const *)down_raw, x_norm,
+                    n_ff_expert, n_embd, qt_gate, qt_up, qt_down, top_indices, top_weights, top_k, combined);
+}

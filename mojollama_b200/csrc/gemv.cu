@@ -107,41 +107,6 @@ __device__ __forceinline__ void raise_status(int *status, int code) {
     if (status) atomicCAS(status, 0, code);
 }
 
-// Encode activation rows [nb_x][K] into int8 planes + scales (formats.cuh).
-template <int M>
-__device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, int8_t *xh, int8_t *xl,
-                                float *xs, float *xsum, int warp, int lane, int nwarps) {
-    const int kb_per_row = K / 32;
-    for (int blk = warp; blk < M * kb_per_row; blk += nwarps) {
-        const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
-        const float v = (m < nb_x) ? __ldg(x + (size_t)m * K + 32 * kb + lane) : 0.0f;
-        float amax = fabsf(v), sum = v;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        }
-        int h = 0, l = 0;
-        float scale;
-        if (amax > 0.0f && amax <= 3.402823466e38f) {
-            const float s = amax / 127.0f;
-            const float t = v / s;
-            const float hh = rintf(t);
-            h = (int)hh;
-            l = (int)rintf((t - hh) * 254.0f);
-            scale = s / 254.0f;
-        } else {
-            scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
-        }
-        xh[(size_t)m * K + 32 * kb + lane] = (int8_t)h;
-        xl[(size_t)m * K + 32 * kb + lane] = (int8_t)l;
-        if (lane == 0) {
-            xs[blk] = scale;
-            xsum[blk] = sum;
-        }
-    }
-}
-
 // Producer warp: stream tile it of this CTA into stage it % n_stages.  The tile's
 // 16-byte-aligned interior goes through one cp.async.bulk (TMA engine, L2
 // evict_first); the <= 15-byte ragged head and tail are plain loads by the lanes.

@@ -90,4 +90,20 @@ int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStrea
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
 int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
 
+// ops.cu
+int launch_rms_norm(float *out, const float *x, const float *w, float *res, int rows, int n, float eps, int flags,
+                    cudaStream_t s);
+int launch_silu(float *out, const float *x, long long n, int mode, cudaStream_t s);
+int launch_swiglu(float *h, const float *g, const float *u, long long n, cudaStream_t s);
+int launch_add(float *out, const float *a, const float *b, long long n, cudaStream_t s);
+int launch_softmax(float *x, int rows, int n, cudaStream_t s);
+int launch_rope_init(float *cos_t, float *sin_t, int max_ctx, int hd, int rope_dim, double base, cudaStream_t s);
+int launch_rope_neox(float *buf, int rows, int rows_stride, int nh, int hd, const int *pos_dev, int pos_host,
+                     const float *cos_t, const float *sin_t, int rope_dim, cudaStream_t s);
+
+// moe.cu: mode 0 = SwiGLU pairs, 1 = weighted sum, 2 = store
+int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt, int G, int n_rows, int K,
+                    const float *x, int nx, float *out, const float *residual, cudaStream_t s);
+int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s);
+
 }  // namespace mlq

@@ -1,0 +1,444 @@
+// Mixture-of-experts FFN of the reference engine on the GPU.
+//
+// Replaces moe_forward_omp (quant_kernels_omp.c:2066-2250), the routers of
+// moe_ffn / qwen36_batch_forward / router_topk (cengine_batch_instr.c:615-646,
+// 1113-1152; gptoss_batch_forward.c:53-93) and the per-expert loop of moe_ffn.
+//
+// k_moe_gemv: a grouped GEMV whose tile is the same `rpt` rows of G matrices (the
+// selected experts' gate/up, or their down projections).  The producer warp streams
+// the G row-ranges of a tile into one shared-memory stage (one cp.async.bulk each);
+// the 8 decode warps compute the G*rpt row dots (weights decoded from the staged
+// GGUF blocks, activations from int8 planes, dp4a) and an epilogue combines them:
+//   MOE_SWIGLU  matrices come as (gate_e, up_e) pairs:
+//               h_e[r] = silu(clamp(gate, -80, 80)) * up      (quant_kernels_omp.c:2157-2164)
+//   MOE_WSUM    out[r] = sum_g w_g * dot_g(r) (+ residual[r]), g in order -- the
+//               weighted combine of the down projections, deterministic (the
+//               reference accumulates with `omp atomic`, :2199-2243)
+//   MOE_STORE   out[g][r] = dot_g(r)
+// A token's MoE layer is therefore two launches: gate/up/SwiGLU, then down/combine.
+// Roofline: HBM-bound on the selected experts' weight bytes (k * 3 matrices).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdlib.h>
+
+#include <map>
+#include <vector>
+
+#include "formats.cuh"
+#include "mlq_internal.h"
+#include "pipeline.cuh"
+
+namespace mlq {
+
+constexpr int kMoeMaxG = 32;
+constexpr int kMoeWarps = 8;
+constexpr int kMoeThreads = (kMoeWarps + 1) * 32;
+constexpr int kMoeMaxStages = 6;
+constexpr int kMoeSmemBudget = 200 * 1024;
+enum { MOE_SWIGLU = 0, MOE_WSUM = 1, MOE_STORE = 2 };
+
+struct MoeArgs {
+    const uint8_t *W[kMoeMaxG];
+    float wgt[kMoeMaxG];
+    int G, n_rows, K;
+    long long row_bytes;
+    int rpt, n_tiles, slot_bytes, n_stages;
+    const float *x;      // [nx][K]; matrix g uses activation row (nx == 1 ? 0 : g)
+    int nx;
+    float *out;
+    const float *residual;
+    int *status;
+};
+
+struct MoeLayout {
+    int off_bar, off_flag, off_xh, off_xl, off_xs, off_xsum, off_res, off_stage, total;
+};
+
+__host__ __device__ inline int mo_align(int v, int a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline MoeLayout moe_layout(int nx, int K, int G, int rpt, int slot_bytes, int n_stages) {
+    MoeLayout L;
+    int o = 0;
+    L.off_bar = o;  o += 2 * kMoeMaxStages * 8;
+    L.off_flag = o; o += 16;
+    o = mo_align(o, 128);
+    L.off_xh = o;   o = mo_align(o + nx * K, 16);
+    L.off_xl = o;   o = mo_align(o + nx * K, 16);
+    L.off_xs = o;   o += nx * (K / 32) * 4;
+    L.off_xsum = o; o = mo_align(o + nx * (K / 32) * 4, 16);
+    L.off_res = o;  o = mo_align(o + 2 * G * rpt * 4, 128);
+    L.off_stage = o; o += n_stages * G * slot_bytes;
+    L.total = o;
+    return L;
+}
+
+template <int QT, int MODE>
+__global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const MoeLayout L = moe_layout(a.nx, a.K, a.G, a.rpt, a.slot_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMoeMaxStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    const long long total = (long long)a.n_rows * a.row_bytes;
+    const int stage_bytes = a.G * a.slot_bytes;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.n_stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kMoeWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kMoeWarps) {
+        // ---------------------------------------------------------------- producer
+        const uint64_t pol = policy_evict_first();
+        for (int it = 0; it < n_iter; ++it) {
+            const int s = it % a.n_stages;
+            if (it >= a.n_stages) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / a.n_stages) - 1) & 1);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok || *abort_flag) {
+                    if (lane == 0) { *abort_flag = 1; if (a.status) atomicCAS(a.status, 0, DEV_ST_WAIT_EMPTY); }
+                    return;
+                }
+            }
+            const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+            const long long b0 = tile * tile_bytes, b1 = min(b0 + tile_bytes, total);
+            uint32_t tx = 0;
+            for (int g = 0; g < a.G; g++) {
+                const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b0;
+                const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b1;
+                const uintptr_t gd = g0 & ~uintptr_t(15);
+                const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15), i1 = g1 & ~uintptr_t(15);
+                uint8_t *st = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes;
+                if (i1 > i0) {
+                    if (g0 + lane < i0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+                    if (i1 + lane < g1) st[i1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(i1 + lane));
+                    tx += (uint32_t)(i1 - i0);
+                } else if (g0 + lane < g1) {
+                    st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                if (tx) {
+                    mbar_arrive_expect_tx(&full[s], tx);
+                    for (int g = 0; g < a.G; g++) {
+                        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b0;
+                        const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b1;
+                        const uintptr_t gd = g0 & ~uintptr_t(15);
+                        const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15), i1 = g1 & ~uintptr_t(15);
+                        if (i1 > i0) {
+                            uint8_t *st = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes;
+                            bulk_g2s(st + (i0 - gd), reinterpret_cast<const void *>(i0), (uint32_t)(i1 - i0), &full[s], pol);
+                        }
+                    }
+                } else {
+                    mbar_arrive(&full[s]);
+                }
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------------- decode warps
+    int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
+    int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
+    float *xs = reinterpret_cast<float *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
+    float *res = reinterpret_cast<float *>(smem + L.off_res);
+    for (int m = 0; m < a.nx; m++)
+        encode_x_planes<1>(a.x + (size_t)m * a.K, 1, a.K, xh + (size_t)m * a.K, xl + (size_t)m * a.K,
+                           xs + (size_t)m * (a.K / 32), xsum + (size_t)m * (a.K / 32), warp, lane, kMoeWarps);
+    named_bar_sync(1, kMoeWarps * 32);
+    const int U = a.K / Fmt<QT>::UE;
+    const int items = a.G * a.rpt;
+    for (int it = 0; it < n_iter; ++it) {
+        const int s = it % a.n_stages;
+        bool ok = false;
+        if (!*abort_flag) {
+            if (lane == 0) ok = mbar_wait_bounded(&full[s], (it / a.n_stages) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok && lane == 0) { *abort_flag = 1; if (a.status) atomicCAS(a.status, 0, DEV_ST_WAIT_FULL); }
+        }
+        const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
+        const int row0 = (int)(tile * a.rpt);
+        float *rs = res + (it & 1) * items;
+        for (int i = warp; i < items; i += kMoeWarps) {
+            const int g = i / a.rpt, r = i - g * a.rpt;
+            float acc[1] = {0.0f};
+            if (ok && row0 + r < a.n_rows) {
+                const int xr = (a.nx == 1) ? 0 : g;
+                const XPlanes xp{xh + (size_t)xr * a.K, xl + (size_t)xr * a.K, xs + (size_t)xr * (a.K / 32),
+                                 xsum + (size_t)xr * (a.K / 32), a.K};
+                const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)(tile * tile_bytes);
+                const uint8_t *rowp = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes +
+                                      (g0 & 15) + (size_t)r * a.row_bytes;
+                for (int u = lane; u < U; u += 32) Unit<QT, 1>::dot(rowp, u, xp, acc);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+            if (lane == 0) rs[i] = acc[0];
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&empty[s]);
+        named_bar_sync(1, kMoeWarps * 32);
+        if (!ok) continue;
+        if (MODE == MOE_SWIGLU) {
+            const int pairs = a.G / 2;
+            for (int t = threadIdx.x; t < pairs * a.rpt; t += kMoeWarps * 32) {
+                const int e = t / a.rpt, r = t - e * a.rpt;
+                if (row0 + r < a.n_rows) {
+                    float gv = fminf(fmaxf(rs[(2 * e) * a.rpt + r], -80.0f), 80.0f);
+                    a.out[(size_t)e * a.n_rows + row0 + r] = (gv / (1.0f + expf(-gv))) * rs[(2 * e + 1) * a.rpt + r];
+                }
+            }
+        } else if (MODE == MOE_WSUM) {
+            for (int r = threadIdx.x; r < a.rpt; r += kMoeWarps * 32) {
+                if (row0 + r < a.n_rows) {
+                    float sum = a.residual ? a.residual[row0 + r] : 0.0f;
+                    for (int g = 0; g < a.G; g++) sum = fmaf(a.wgt[g], rs[g * a.rpt + r], sum);
+                    a.out[row0 + r] = sum;
+                }
+            }
+        } else {
+            for (int t = threadIdx.x; t < items; t += kMoeWarps * 32) {
+                const int g = t / a.rpt, r = t - g * a.rpt;
+                if (row0 + r < a.n_rows) a.out[(size_t)g * a.n_rows + row0 + r] = rs[t];
+            }
+        }
+    }
+}
+
+template <int QT, int MODE>
+static int launch_moe_t(MoeArgs &a, cudaStream_t s) {
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    const long long rb = a.row_bytes;
+    int rpt = (int)(32768 / (a.G * rb));
+    rpt = rpt < 1 ? 1 : (rpt > 16 ? 16 : rpt);
+    while (rpt > 1 && (a.n_rows + rpt - 1) / rpt < env->num_sms) rpt >>= 1;
+    a.rpt = rpt;
+    a.slot_bytes = mo_align((int)(rpt * rb), 16) + 48;
+    const int fixed = moe_layout(a.nx, a.K, a.G, rpt, a.slot_bytes, 0).total;
+    int n_stages = (kMoeSmemBudget - fixed) / (a.G * a.slot_bytes);
+    if (n_stages > kMoeMaxStages) n_stages = kMoeMaxStages;
+    if (n_stages < 2) {
+        set_error(MLQ_ERR_CAPACITY, "moe: %d matrices x K=%d do not fit the shared-memory ring", a.G, a.K);
+        return MLQ_ERR_CAPACITY;
+    }
+    a.n_stages = n_stages;
+    a.n_tiles = (a.n_rows + rpt - 1) / rpt;
+    a.status = env->d_status;
+    const int smem = fixed + n_stages * a.G * a.slot_bytes;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_moe_gemv<QT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    const int grid = a.n_tiles < env->num_sms ? a.n_tiles : env->num_sms;
+    k_moe_gemv<QT, MODE><<<grid, kMoeThreads, smem, s>>>(a);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+template <int MODE>
+static int launch_moe_mode(int qt, MoeArgs &a, cudaStream_t s) {
+    switch (qt) {
+        case MLQ_Q4_0: return launch_moe_t<MLQ_Q4_0, MODE>(a, s);
+        case MLQ_Q4_1: return launch_moe_t<MLQ_Q4_1, MODE>(a, s);
+        case MLQ_Q5_0: return launch_moe_t<MLQ_Q5_0, MODE>(a, s);
+        case MLQ_Q8_0: return launch_moe_t<MLQ_Q8_0, MODE>(a, s);
+        case MLQ_Q4_K: return launch_moe_t<MLQ_Q4_K, MODE>(a, s);
+        case MLQ_Q5_K: return launch_moe_t<MLQ_Q5_K, MODE>(a, s);
+        case MLQ_Q6_K: return launch_moe_t<MLQ_Q6_K, MODE>(a, s);
+        case MLQ_MXFP4: return launch_moe_t<MLQ_MXFP4, MODE>(a, s);
+        case MLQ_MXFP4_REF: return launch_moe_t<MLQ_MXFP4_REF, MODE>(a, s);
+        default:
+            set_error(MLQ_ERR_TYPE, "moe: expert type %d not supported on the grouped path", qt);
+            return MLQ_ERR_TYPE;
+    }
+}
+
+// G matrices W[g] (n_rows x K, type qt) against activations x [nx][K]
+int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt, int G, int n_rows, int K,
+                    const float *x, int nx, float *out, const float *residual, cudaStream_t s) {
+    if (G < 1 || G > kMoeMaxG || (mode == MOE_SWIGLU && G % 2)) {
+        set_error(MLQ_ERR_ARG, "moe: %d matrices per launch (1..%d, even for SwiGLU)", G, kMoeMaxG);
+        return MLQ_ERR_ARG;
+    }
+    if (ref_compat() && qt == MLQ_MXFP4) qt = MLQ_MXFP4_REF;
+    MoeArgs a{};
+    for (int g = 0; g < G; g++) {
+        a.W[g] = W[g];
+        a.wgt[g] = wgt ? wgt[g] : 0.0f;
+    }
+    a.G = G;
+    a.n_rows = n_rows;
+    a.K = K;
+    a.row_bytes = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    a.x = x;
+    a.nx = nx;
+    a.out = out;
+    a.residual = residual;
+    if (mode == MOE_SWIGLU) return launch_moe_mode<MOE_SWIGLU>(qt, a, s);
+    if (mode == MOE_WSUM) return launch_moe_mode<MOE_WSUM>(qt, a, s);
+    return launch_moe_mode<MOE_STORE>(qt, a, s);
+}
+
+// ------------------------------------------------------------------------------ router
+// One warp per token: softmax over E logits (1/(sum + 1e-10)), top-k by the reference's
+// insertion rule (strictly greater wins, so ties keep the lower expert index), optional
+// renormalisation of the k weights (1/(sum + 1e-10)).
+__global__ void k_router_topk(const float *__restrict__ logits, int B, int E, int k, int renorm,
+                              int *__restrict__ idx, float *__restrict__ w) {
+    const int lane = threadIdx.x & 31;
+    const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (b >= B) return;
+    const float *lg = logits + (size_t)b * E;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+    for (int e = lane; e < E; e += 32) sum += expf(lg[e] - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.0f / (sum + 1e-10f);
+    unsigned long long taken[4] = {0, 0, 0, 0};   // up to 256 experts
+    float tsum = 0.0f;
+    for (int j = 0; j < k; j++) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            if ((taken[e >> 6] >> (e & 63)) & 1ull) continue;
+            const float p = expf(lg[e] - mx) * inv;
+            if (p > best || (p == best && e < bi)) { best = p; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (bi >= 0 && bi < E) taken[bi >> 6] |= 1ull << (bi & 63);
+        if (lane == 0) {
+            idx[(size_t)b * k + j] = (bi < E) ? bi : -1;
+            w[(size_t)b * k + j] = best;
+        }
+        tsum += best;
+    }
+    if (renorm && lane == 0) {
+        const float ti = 1.0f / (tsum + 1e-10f);
+        for (int j = 0; j < k; j++) w[(size_t)b * k + j] *= ti;
+    }
+}
+
+int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s) {
+    if (E > 256 || k < 1 || k > E) {
+        set_error(MLQ_ERR_CAPACITY, "router: %d experts, top-%d (at most 256 experts)", E, k);
+        return MLQ_ERR_CAPACITY;
+    }
+    k_router_topk<<<(B * 32 + 127) / 128, 128, 0, s>>>(logits, B, E, k, renorm, idx, w);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+}  // namespace mlq
+
+// ====================================================================================== C-ABI
+using namespace mlq;
+
+extern "C" {
+
+// moe_forward_omp semantics with GGUF-correct math for every expert type:
+// combined = sum_i w[i] * W_down[idx[i]] . (silu(clamp(W_gate[idx[i]] x)) * (W_up[idx[i]] x))
+int mlq_moe_forward(const void *const *gate, const void *const *up, const void *const *down, const float *x,
+                    int n_ff, int n_embd, int qt_gate, int qt_up, int qt_down, const int *top_idx,
+                    const float *top_w, int top_k, float *combined) {
+    if (!gate || !up || !down || !x || !top_idx || !top_w || !combined || n_ff <= 0 || n_embd <= 0 ||
+        top_k <= 0 || 2 * top_k > kMoeMaxG) {
+        set_error(MLQ_ERR_ARG, "mlq_moe_forward: bad arguments (top_k 1..%d)", kMoeMaxG / 2);
+        return MLQ_ERR_ARG;
+    }
+    const size_t rb_g = mlq_row_bytes(qt_gate, n_embd), rb_u = mlq_row_bytes(qt_up, n_embd);
+    const size_t rb_d = mlq_row_bytes(qt_down, n_ff);
+    if (!rb_g || !rb_u || !rb_d) {
+        set_error(MLQ_ERR_TYPE, "mlq_moe_forward: types %d/%d/%d with n_embd %d, n_ff %d", qt_gate, qt_up, qt_down,
+                  n_embd, n_ff);
+        return MLQ_ERR_TYPE;
+    }
+    // the selected experts and their weights are read on the host (as the reference does)
+    std::vector<int> idx(top_k);
+    std::vector<float> w(top_k);
+    const bool idx_dev = is_device_ptr(top_idx), w_dev = is_device_ptr(top_w);
+    if (idx_dev) cudaMemcpy(idx.data(), top_idx, sizeof(int) * top_k, cudaMemcpyDeviceToHost);
+    else for (int i = 0; i < top_k; i++) idx[i] = top_idx[i];
+    if (w_dev) cudaMemcpy(w.data(), top_w, sizeof(float) * top_k, cudaMemcpyDeviceToHost);
+    else for (int i = 0; i < top_k; i++) w[i] = top_w[i];
+    CallScope cs;
+    std::vector<const uint8_t *> gu(2 * top_k), dn(top_k);
+    for (int i = 0; i < top_k; i++) {
+        if (idx[i] < 0) {
+            set_error(MLQ_ERR_ARG, "mlq_moe_forward: expert index %d", idx[i]);
+            return MLQ_ERR_ARG;
+        }
+        gu[2 * i] = (const uint8_t *)cs.weights(gate[idx[i]], rb_g * n_ff);
+        gu[2 * i + 1] = (const uint8_t *)cs.weights(up[idx[i]], rb_u * n_ff);
+        dn[i] = (const uint8_t *)cs.weights(down[idx[i]], rb_d * n_embd);
+    }
+    const float *dx = (const float *)cs.in(x, sizeof(float) * (size_t)n_embd);
+    float *h = (float *)cs.scratch(sizeof(float) * (size_t)top_k * n_ff);
+    float *dout = (float *)cs.out(combined, sizeof(float) * (size_t)n_embd);
+    if (cs.failed) return cs.finish();
+    cudaStream_t s = stream();
+    int rc;
+    if (qt_gate == qt_up) {
+        rc = launch_moe_gemv(MOE_SWIGLU, qt_gate, gu.data(), nullptr, 2 * top_k, n_ff, n_embd, dx, 1, h, nullptr, s);
+    } else {
+        float *gbuf = (float *)cs.scratch(sizeof(float) * (size_t)2 * top_k * n_ff);
+        std::vector<const uint8_t *> gs(top_k), us(top_k);
+        for (int i = 0; i < top_k; i++) { gs[i] = gu[2 * i]; us[i] = gu[2 * i + 1]; }
+        rc = launch_moe_gemv(MOE_STORE, qt_gate, gs.data(), nullptr, top_k, n_ff, n_embd, dx, 1, gbuf, nullptr, s);
+        if (rc == MLQ_OK)
+            rc = launch_moe_gemv(MOE_STORE, qt_up, us.data(), nullptr, top_k, n_ff, n_embd, dx, 1,
+                                 gbuf + (size_t)top_k * n_ff, nullptr, s);
+        if (rc == MLQ_OK) rc = launch_swiglu(h, gbuf, gbuf + (size_t)top_k * n_ff, (long long)top_k * n_ff, s);
+    }
+    if (rc == MLQ_OK)
+        rc = launch_moe_gemv(MOE_WSUM, qt_down, dn.data(), w.data(), top_k, n_embd, n_ff, h, top_k, dout, nullptr, s);
+    if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
+    return cs.finish();
+}
+
+// logits = W_r x (W_r: E x N of type qt_r), softmax, top-k, optional renormalisation.
+// x [B][N] -> idx [B][k], w [B][k]
+int mlq_moe_router(const float *x, int B, int N, const void *W_r, int qt_r, int E, int k, int renorm, int *idx,
+                   float *w) {
+    if (!x || !W_r || !idx || !w || B <= 0 || N <= 0 || E <= 0 || k <= 0 || k > E) {
+        set_error(MLQ_ERR_ARG, "mlq_moe_router: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    const size_t rb = mlq_row_bytes(qt_r, N);
+    if (!rb) { set_error(MLQ_ERR_TYPE, "mlq_moe_router: type %d, N %d", qt_r, N); return MLQ_ERR_TYPE; }
+    CallScope cs;
+    const uint8_t *dW = (const uint8_t *)cs.weights(W_r, rb * E);
+    const float *dx = (const float *)cs.in(x, sizeof(float) * (size_t)B * N);
+    float *logits = (float *)cs.scratch(sizeof(float) * (size_t)B * E);
+    int *di = (int *)cs.out(idx, sizeof(int) * (size_t)B * k);
+    float *dw = (float *)cs.out(w, sizeof(float) * (size_t)B * k);
+    if (cs.failed) return cs.finish();
+    int rc = launch_matmul(dW, qt_r, dx, logits, E, N, B, rb * E, stream());
+    if (rc == MLQ_OK) rc = launch_router_topk(logits, B, E, k, renorm, di, dw, stream());
+    if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
+    return cs.finish();
+}
+
+}  // extern "C"

@@ -165,10 +165,51 @@ static bool sample_matches(const uint8_t *h, size_t bytes, const std::vector<uin
     return true;
 }
 
+// Whole host tensors registered with mlq_register_weights: any pointer inside one
+// (e.g. one expert of a 3-D expert tensor) maps to the same offset of its device copy.
+// Each range keeps a small content sample (first/last 64 bytes and 16 spread 16-byte
+// windows, 384 bytes) checked on every lookup, so a range whose host memory was freed
+// and reused for other data is re-uploaded instead of serving a stale copy.
+struct RangeEntry { size_t bytes; void *dev; std::vector<uint8_t> sample; };
+static std::map<uintptr_t, RangeEntry> g_ranges[kMaxDev];
+
+static void range_sample(const uint8_t *h, size_t bytes, std::vector<uint8_t> &s) {
+    if (bytes <= 384) {
+        s.assign(h, h + bytes);
+        return;
+    }
+    s.resize(384);
+    memcpy(s.data(), h, 64);
+    memcpy(s.data() + 64, h + bytes - 64, 64);
+    const size_t stride = (bytes - 16) / 16;
+    for (int i = 0; i < 16; i++) memcpy(s.data() + 128 + 16 * i, h + stride * i, 16);
+}
+
+static const void *in_registered_range(int dev, const void *host, size_t bytes) {
+    auto &m = g_ranges[dev];
+    const uintptr_t p = (uintptr_t)host;
+    auto it = m.upper_bound(p);
+    if (it == m.begin()) return nullptr;
+    --it;
+    if (p + bytes > it->first + it->second.bytes) return nullptr;
+    std::vector<uint8_t> now;
+    range_sample((const uint8_t *)it->first, it->second.bytes, now);
+    if (now != it->second.sample) {
+        if (cudaMemcpy(it->second.dev, (const void *)it->first, it->second.bytes, cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        it->second.sample.swap(now);
+    }
+    return (const char *)it->second.dev + (p - it->first);
+}
+
 static const void *resident(const void *host, size_t bytes) {
     Ctx *c = ctx();
     if (!c) return nullptr;
     std::lock_guard<std::mutex> lk(g_mu);
+    if (const void *r = in_registered_range(c->device, host, bytes)) return r;
     auto key = std::make_pair((uintptr_t)host, bytes);
     auto &m = g_cache[c->device];
     auto it = m.find(key);
@@ -387,10 +428,42 @@ int mlq_sync(void) {
     return mlq_device_status();
 }
 
+// Upload a whole host tensor once; every pointer inside [p, p + bytes) then resolves to
+// its device copy without a content check (the caller promises the bytes stay fixed).
 int mlq_register_weights(const void *p, size_t bytes) {
     if (!p || !bytes) { set_error(MLQ_ERR_ARG, "register_weights: null/empty"); return MLQ_ERR_ARG; }
     if (is_device_ptr(p)) return MLQ_OK;
-    return resident(p, bytes) ? MLQ_OK : mlq_last_error();
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (in_registered_range(c->device, p, bytes)) return MLQ_OK;
+    void *d = nullptr;
+    if (!MLQ_CUDA(cudaMalloc(&d, bytes + 256))) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaMemcpy(d, p, bytes, cudaMemcpyHostToDevice))) { cudaFree(d); return MLQ_ERR_CUDA; }
+    cudaMemset((char *)d + bytes, 0, 256);
+    RangeEntry e{bytes, d, {}};
+    range_sample((const uint8_t *)p, bytes, e.sample);
+    g_ranges[c->device][(uintptr_t)p] = std::move(e);
+    g_cache_bytes[c->device] += bytes;
+    return MLQ_OK;
+}
+
+// Drop the device copy of a tensor registered at exactly `p` (call before freeing it).
+int mlq_unregister_weights(const void *p) {
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    cudaStreamSynchronize(c->stream);
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto &m = g_ranges[c->device];
+    auto it = m.find((uintptr_t)p);
+    if (it == m.end()) {
+        set_error(MLQ_ERR_ARG, "unregister_weights: %p was not registered", p);
+        return MLQ_ERR_ARG;
+    }
+    cudaFree(it->second.dev);
+    g_cache_bytes[c->device] -= it->second.bytes;
+    m.erase(it);
+    return MLQ_OK;
 }
 
 int mlq_cache_clear(void) {
@@ -400,6 +473,8 @@ int mlq_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto &kv : g_cache[c->device]) cudaFree(kv.second.dev);
     g_cache[c->device].clear();
+    for (auto &kv : g_ranges[c->device]) cudaFree(kv.second.dev);
+    g_ranges[c->device].clear();
     g_cache_bytes[c->device] = 0;
     return MLQ_OK;
 }

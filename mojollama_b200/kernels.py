@@ -53,6 +53,10 @@ def _bind_engine(so: ctypes.CDLL) -> None:
     so.quantize_row_q8_0.restype = ci
     so.q8_0_q8_0_matmul_omp.argtypes = [cu, cu, cf, ci, ci, ci]
     so.q8_0_q8_0_matmul_omp.restype = None
+    # turbo_engine_v7_moe.py:338-353
+    so.moe_forward_omp.argtypes = [ctypes.POINTER(cu), ctypes.POINTER(cu), ctypes.POINTER(cu), cf, ci, ci, ci, ci, ci,
+                                   ctypes.POINTER(ctypes.c_int), cf, ci, cf, cf, cu]
+    so.moe_forward_omp.restype = None
 
 
 def load_kernels() -> Kernels:

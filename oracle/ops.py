@@ -196,3 +196,37 @@ def gqa_decode_reference_quirk(q, k, v, n_head, n_kv, hd):
         p = e / (e.astype(np.float64).sum() + 1e-10)
         out[h] = p @ v[:, g, :].astype(np.float64)
     return out.reshape(-1).astype(np.float32)
+
+
+def silu_clamped(g):
+    g = np.clip(np.asarray(g, np.float64), -80, 80)
+    return g / (1 + np.exp(-g))
+
+
+def moe_forward(gate, up, down, qts, x, n_ff, n_embd, idx, w):
+    """moe_forward_omp (quant_kernels_omp.c:2066-2250) where it is W.x: for each selected
+    expert e = idx[i]: h = silu(clamp(gate_e x, +-80)) * (up_e x); combined += w[i] * down_e h.
+    gate/up/down: dict expert -> raw bytes; fp64 accumulation."""
+    qg, qu, qd = qts
+    x = np.asarray(x, np.float64)
+    out = np.zeros(n_embd)
+    for i, e in enumerate(idx):
+        g = gemv(gate[e], qg, x, n_ff, n_embd)[0].astype(np.float64)
+        u = gemv(up[e], qu, x, n_ff, n_embd)[0].astype(np.float64)
+        h = silu_clamped(g) * u
+        out += float(w[i]) * gemv(down[e], qd, h, n_embd, n_ff)[0].astype(np.float64)
+    return out.astype(np.float32)
+
+
+def router_topk(logits, k, renorm):
+    """cengine_batch_instr.c:1116-1152 / gptoss_batch_forward.c:53-93: softmax with
+    1/(sum + 1e-10), insertion top-k (strictly greater wins: ties keep the lower index),
+    optional renormalisation with 1/(sum + 1e-10)."""
+    lg = np.asarray(logits, np.float64)
+    p = np.exp(lg - lg.max())
+    p = p / (p.sum() + 1e-10)
+    order = sorted(range(len(p)), key=lambda e: (-p[e], e))[:k]
+    w = p[order]
+    if renorm:
+        w = w / (w.sum() + 1e-10)
+    return np.array(order, np.int32), w.astype(np.float32)

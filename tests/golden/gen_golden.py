@@ -46,6 +46,8 @@ def gen_formats(rng):
 
 def gen_ref(rng, out):
     from oracle.ref import RefEngine
+    from oracle.ref import fptr as R_fptr
+    from oracle.ref import uptr as R_uptr
     ref = RefEngine()
     ref.set_num_threads(4)
     x = out["quant_x"]
@@ -68,6 +70,28 @@ def gen_ref(rng, out):
         ops[f"bgemv_x_{qt}"] = xb
         ops[f"bgemv_ref_{qt}"] = ref.batch_matmul(name, w, xb, n, k, b)
     ops["shape"] = np.array([n, k, b], np.int32)
+    # moe_forward_omp with Q4_0 experts (its gate/up/down Q4_0 paths are W.x:
+    # quant_kernels_omp.c:2122-2131, 2225-2227)
+    import ctypes
+    ne, n_embd, n_ff, topk = 6, 256, 128, 3
+    gate = [F.quantize(F.Q4_0, (rng.standard_normal(n_ff * n_embd) * 0.05).astype(np.float32)) for _ in range(ne)]
+    up = [F.quantize(F.Q4_0, (rng.standard_normal(n_ff * n_embd) * 0.05).astype(np.float32)) for _ in range(ne)]
+    down = [F.quantize(F.Q4_0, (rng.standard_normal(n_embd * n_ff) * 0.05).astype(np.float32)) for _ in range(ne)]
+    xm = rng.standard_normal(n_embd).astype(np.float32)
+    idx = np.array([4, 1, 3], np.int32)
+    wt = np.array([0.5, 0.3, 0.2], np.float32)
+    arr = ctypes.POINTER(ctypes.c_uint8) * ne
+    gp, upp, dp = (arr(*[R_uptr(a) for a in lst]) for lst in (gate, up, down))
+    comb = np.zeros(n_embd, np.float32)
+    buf = np.zeros(3 * topk * n_ff, np.float32)
+    q8 = np.zeros(n_embd // 32 * 34 * 4, np.uint8)
+    ref.set_num_threads(1)
+    ref.so.moe_forward_omp(gp, upp, dp, R_fptr(xm), n_ff, n_embd, 2, 2, 2,
+                           idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), R_fptr(wt), topk, R_fptr(comb),
+                           R_fptr(buf), R_uptr(q8))
+    ops["moe_gate"], ops["moe_up"], ops["moe_down"] = np.stack(gate), np.stack(up), np.stack(down)
+    ops["moe_x"], ops["moe_idx"], ops["moe_w"], ops["moe_out"] = xm, idx, wt, comb
+    ops["moe_dims"] = np.array([ne, n_embd, n_ff, topk], np.int32)
     # gqa_attention_decode (gqa_attention.c:93, built with the oracle's cblas shim).
     # Single-threaded: every OpenMP thread of the reference writes the same tmp_scores
     # buffer (gqa_attention.c:104, 113), so its multi-threaded output is a data race.

@@ -82,3 +82,18 @@ def test_gqa_reference_output_is_modelled_and_deviates(tag):
     q, k, v = RO[f"gqa_q_{tag}"], RO[f"gqa_k_{tag}"], RO[f"gqa_v_{tag}"]
     assert O.rel_l2(RO[f"gqa_out_{tag}"], O.gqa_decode_reference_quirk(q, k, v, nh, nkh, hd)) < 1e-4
     assert O.rel_l2(RO[f"gqa_out_{tag}"], O.gqa_decode(q, k, v, nh, nkh, hd)) > 1e-2
+
+
+def test_moe_oracle_matches_reference_c():
+    ne, n_embd, n_ff, topk = (int(v) for v in RO["moe_dims"])
+    g = {e: RO["moe_gate"][e] for e in range(ne)}
+    u = {e: RO["moe_up"][e] for e in range(ne)}
+    d = {e: RO["moe_down"][e] for e in range(ne)}
+    got = O.moe_forward(g, u, d, (F.Q4_0, F.Q4_0, F.Q4_0), RO["moe_x"], n_ff, n_embd, RO["moe_idx"], RO["moe_w"])
+    assert O.rel_l2(RO["moe_out"], got) < 1e-5
+
+
+def test_router_tie_rule_and_renorm():
+    lg = np.array([1.0, 3.0, 3.0, 0.5, 3.0], np.float32)
+    idx, w = O.router_topk(lg, 2, renorm=True)
+    assert list(idx) == [1, 2] and abs(float(w.sum()) - 1.0) < 1e-6
