@@ -144,6 +144,20 @@ int mlq_moe_forward(const void *const *gate, const void *const *up, const void *
 int mlq_moe_router(const float *x, int B, int N, const void *W_r, int qt_r, int E, int k, int renorm, int *idx,
                    float *w);
 
+/* ---- SSM decode step, the reference's semantics (cengine_batch_instr.c:736-849) ----
+   x [B][N] -> interm [B][inner]; state [groups][state_size] shared by all B sequences and
+   updated in sequence order.  ssm_norm_w and conv_kernel are accepted and unused, as there. */
+int mlq_ssm_decode_step(const float *x, float *interm, const float *conv1d_w, const float *a_param,
+                        const float *dt_bias, const float *alpha, const float *beta, const float *ssm_norm_w,
+                        float *state, int B, int N, int inner, int groups, int state_size, int conv_kernel,
+                        int dt_rank);
+/* output_b = residual_b + W_out . ((W_gate . x_b) * interm_b);  W_gate inner x N, W_out N x inner */
+int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, const float *conv1d_w,
+                        const float *a_param, const float *dt_bias, const float *alpha, const float *beta,
+                        const float *ssm_norm_w, float *state, const void *gate_raw, int gate_nr, int gate_nc,
+                        int gate_qt, const void *ssm_out_raw, int ssm_out_nr, int ssm_out_nc, int ssm_out_qt, int B,
+                        int N, int inner, int groups, int state_size, int conv_kernel, int dt_rank);
+
 /* ---- decode attention (one query per sequence), fp32 KV ---- */
 /* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);
    head h uses KV head h / (n_head / n_kv_head); window > 0 attends the last `window`

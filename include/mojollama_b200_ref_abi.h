@@ -93,6 +93,16 @@ void moe_forward_omp(const uint8_t **gate_raw, const uint8_t **up_raw, const uin
                      int n_ff_expert, int n_embd, int qt_gate, int qt_up, int qt_down, const int *top_indices,
                      const float *top_weights, int top_k, float *combined, float *prealloc_buf,
                      uint8_t *prealloc_q8);
+/* cengine_batch_instr.c:736, 803 */
+void ssm_decode_step(const float *x, float *ssm_intermediate, const float *conv1d_w, const float *a_param,
+                     const float *dt_bias, const float *alpha, const float *beta, const float *ssm_norm_w,
+                     float *state, int B, int N, int inner, int groups, int state_size, int conv_kernel,
+                     int dt_rank);
+void ssm_layer_fused(const float *x, float *residual, float *output, const float *conv1d_w, const float *a_param,
+                     const float *dt_bias, const float *alpha, const float *beta, const float *ssm_norm_w,
+                     float *state, const uint8_t *gate_raw, int gate_nr, int gate_nc, int gate_qt,
+                     const uint8_t *ssm_out_raw, int ssm_out_nr, int ssm_out_nc, int ssm_out_qt, int B, int N,
+                     int inner, int groups, int state_size, int conv_kernel, int dt_rank);
 /* cengine_batch_instr.c:141 -- static in the reference, exported here */
 void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd);
 

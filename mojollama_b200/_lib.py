@@ -59,6 +59,8 @@ def core() -> ctypes.CDLL:
     so.mlq_matmul_q8act_noalloc.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci, _vp]
     so.mlq_moe_forward.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _vp, _vp, _ci, _vp]
     so.mlq_moe_router.argtypes = [_vp, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _vp, _vp]
+    so.mlq_ssm_decode_step.argtypes = [_vp] * 9 + [_ci] * 7
+    so.mlq_ssm_layer_fused.argtypes = [_vp] * 10 + [_vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci] + [_ci] * 7
     so.mlq_attn_decode_flat.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
     so.mlq_attn_decode_paged.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _ci, _vp]
     so.mlq_page_table_init.argtypes = [_vp, _ci, _ci, _ci, _ci, _ci]

@@ -125,3 +125,21 @@ void moe_forward_omp(const uint8_t **gate_raw, const uint8_t **up_raw, const uin
     mlq_moe_forward((const void *const *)gate_raw, (const void *const *)up_raw, (const void *const *)down_raw, x_norm,
                     n_ff_expert, n_embd, qt_gate, qt_up, qt_down, top_indices, top_weights, top_k, combined);
 }
+
+/* cengine_batch_instr.c:736, 803 */
+void ssm_decode_step(const float *x, float *ssm_intermediate, const float *conv1d_w, const float *a_param,
+                     const float *dt_bias, const float *alpha, const float *beta, const float *ssm_norm_w,
+                     float *state, int B, int N, int inner, int groups, int state_size, int conv_kernel,
+                     int dt_rank) {
+    mlq_ssm_decode_step(x, ssm_intermediate, conv1d_w, a_param, dt_bias, alpha, beta, ssm_norm_w, state, B, N, inner,
+                        groups, state_size, conv_kernel, dt_rank);
+}
+void ssm_layer_fused(const float *x, float *residual, float *output, const float *conv1d_w, const float *a_param,
+                     const float *dt_bias, const float *alpha, const float *beta, const float *ssm_norm_w,
+                     float *state, const uint8_t *gate_raw, int gate_nr, int gate_nc, int gate_qt,
+                     const uint8_t *ssm_out_raw, int ssm_out_nr, int ssm_out_nc, int ssm_out_qt, int B, int N,
+                     int inner, int groups, int state_size, int conv_kernel, int dt_rank) {
+    mlq_ssm_layer_fused(x, residual, output, conv1d_w, a_param, dt_bias, alpha, beta, ssm_norm_w, state, gate_raw,
+                        gate_nr, gate_nc, gate_qt, ssm_out_raw, ssm_out_nr, ssm_out_nc, ssm_out_qt, B, N, inner,
+                        groups, state_size, conv_kernel, dt_rank);
+}

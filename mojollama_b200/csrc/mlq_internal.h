@@ -101,6 +101,12 @@ int launch_rope_init(float *cos_t, float *sin_t, int max_ctx, int hd, int rope_d
 int launch_rope_neox(float *buf, int rows, int rows_stride, int nh, int hd, const int *pos_dev, int pos_host,
                      const float *cos_t, const float *sin_t, int rope_dim, cudaStream_t s);
 
+// ssm.cu
+int launch_ssm_decode_step(const float *x, float *interm, const float *conv_w, const float *a_param,
+                           const float *dt_bias, const float *alpha, const float *beta, float *state, int B, int N,
+                           int inner, int groups, int state_size, int dt_rank, cudaStream_t s);
+int launch_mul(float *a, const float *b, long long n, cudaStream_t s);
+
 // moe.cu: mode 0 = SwiGLU pairs, 1 = weighted sum, 2 = store
 int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt, int G, int n_rows, int K,
                     const float *x, int nx, float *out, const float *residual, cudaStream_t s);

@@ -230,3 +230,23 @@ def router_topk(logits, k, renorm):
     if renorm:
         w = w / (w.sum() + 1e-10)
     return np.array(order, np.int32), w.astype(np.float32)
+
+
+def ssm_decode_step(x, conv_w, a, dt_bias, alpha, beta, state, B, N, inner, groups, state_size, dt_rank):
+    """cengine_batch_instr.c:736-797 as the reference computes it (see its docstring in
+    mojollama_b200/csrc/ssm.cu): returns (interm [B][inner], new state)."""
+    x = np.asarray(x, np.float64).reshape(B, N)
+    st = np.asarray(state, np.float64).reshape(groups, state_size).copy()
+    interm = np.zeros((B, inner))
+    for b in range(B):
+        conv = np.array([x[b, i % N] * conv_w[i] for i in range(2 * inner)])
+        g = conv[:inner]
+        interm[b] = g / (1 + np.exp(-g)) * conv[inner:]
+        xi = np.array([x[b, j % N] for j in range(dt_rank)])
+        for grp in range(groups):
+            dt = dt_bias[grp] + np.dot(alpha[grp * dt_rank:(grp + 1) * dt_rank], xi)
+            dt = dt if dt > 20 else np.log1p(np.exp(dt))
+            bx = np.dot(beta[grp * dt_rank:(grp + 1) * dt_rank], xi) * dt
+            st[grp] *= np.exp(a[grp] * dt)
+            st[grp, 0] += bx
+    return interm.astype(np.float32), st.astype(np.float32)

@@ -92,6 +92,24 @@ def gen_ref(rng, out):
     ops["moe_gate"], ops["moe_up"], ops["moe_down"] = np.stack(gate), np.stack(up), np.stack(down)
     ops["moe_x"], ops["moe_idx"], ops["moe_w"], ops["moe_out"] = xm, idx, wt, comb
     ops["moe_dims"] = np.array([ne, n_embd, n_ff, topk], np.int32)
+    # ssm_decode_step (cengine_batch_instr.c:736), B = 3 sequences sharing one state
+    B_, N_, inner_, groups_, ss_, dtr_ = 3, 64, 96, 4, 8, 5
+    sx = rng.standard_normal(B_ * N_).astype(np.float32)
+    sconv = rng.standard_normal(4 * 2 * inner_).astype(np.float32)
+    sa = -rng.uniform(0.1, 1.0, groups_).astype(np.float32)
+    sdt = rng.standard_normal(groups_).astype(np.float32)
+    sal = (rng.standard_normal(groups_ * dtr_) * 0.3).astype(np.float32)
+    sbe = (rng.standard_normal(groups_ * dtr_) * 0.3).astype(np.float32)
+    sst = rng.standard_normal(groups_ * ss_).astype(np.float32)
+    snorm = np.ones(ss_, np.float32)
+    sint = np.zeros(B_ * inner_, np.float32)
+    st_out = sst.copy()
+    ref.so.ssm_decode_step(R_fptr(sx), R_fptr(sint), R_fptr(sconv), R_fptr(sa), R_fptr(sdt), R_fptr(sal), R_fptr(sbe),
+                           R_fptr(snorm), R_fptr(st_out), B_, N_, inner_, groups_, ss_, 4, dtr_)
+    for key, val in dict(ssm_x=sx, ssm_conv=sconv, ssm_a=sa, ssm_dt=sdt, ssm_alpha=sal, ssm_beta=sbe,
+                         ssm_state_in=sst, ssm_interm=sint, ssm_state_out=st_out,
+                         ssm_dims=np.array([B_, N_, inner_, groups_, ss_, dtr_], np.int32)).items():
+        ops[key] = val
     # gqa_attention_decode (gqa_attention.c:93, built with the oracle's cblas shim).
     # Single-threaded: every OpenMP thread of the reference writes the same tmp_scores
     # buffer (gqa_attention.c:104, 113), so its multi-threaded output is a data race.

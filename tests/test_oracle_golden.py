@@ -97,3 +97,11 @@ def test_router_tie_rule_and_renorm():
     lg = np.array([1.0, 3.0, 3.0, 0.5, 3.0], np.float32)
     idx, w = O.router_topk(lg, 2, renorm=True)
     assert list(idx) == [1, 2] and abs(float(w.sum()) - 1.0) < 1e-6
+
+
+def test_ssm_oracle_matches_reference_c():
+    B, N, inner, groups, ss, dtr = (int(v) for v in RO["ssm_dims"])
+    interm, st = O.ssm_decode_step(RO["ssm_x"], RO["ssm_conv"], RO["ssm_a"], RO["ssm_dt"], RO["ssm_alpha"],
+                                   RO["ssm_beta"], RO["ssm_state_in"], B, N, inner, groups, ss, dtr)
+    assert O.rel_l2(RO["ssm_interm"], interm.reshape(-1)) < 1e-6
+    assert O.rel_l2(RO["ssm_state_out"], st.reshape(-1)) < 1e-6
