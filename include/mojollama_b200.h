@@ -158,6 +158,18 @@ int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, co
                         int gate_qt, const void *ssm_out_raw, int ssm_out_nr, int ssm_out_nc, int ssm_out_qt, int B,
                         int N, int inner, int groups, int state_size, int conv_kernel, int dt_rank);
 
+/* ---- whole-model decode step over the reference's BC model description ----
+   bc points to a BC struct (mojollama_b200_ref_abi.h, cengine_batch_instr.c:536-589);
+   tokens [B] (B <= 64), one new token per sequence; c->logits [B][outNR] is written and
+   every kv_array[b]->seq_len[0] advances by one.  ws is accepted and unused. */
+int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws);
+/* moe_ffn: layer l's routed experts for x [B][N] -> ffn [B][N] (cengine_batch_instr.c:591) */
+int mlq_moe_ffn(const void *bc, int l, const float *x, float *ffn, int B);
+/* forget the cached per-model device plans (also done by mlq_cache_clear) */
+void mlq_forget_model_plans(void);
+/* sizeof(BC) as this library compiles it (layout check for ctypes mirrors) */
+size_t mlq_sizeof_bc(void);
+
 /* ---- decode attention (one query per sequence), fp32 KV ---- */
 /* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);
    head h uses KV head h / (n_head / n_kv_head); window > 0 attends the last `window`

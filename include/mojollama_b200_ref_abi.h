@@ -20,6 +20,68 @@
 typedef MlqPageTable PageTable;   /* cengine_batch_instr.c:160-171 */
 typedef MlqKVBlock KVBlock;       /* cengine_batch_instr.c:204-207 */
 
+/* The batch engine's model description, field for field as cengine_batch_instr.c:536-589
+ * defines it (the reference's Python mirrors it with ctypes, forward/zaya_bc.py:32-130),
+ * so the same struct bytes drive this build.  Per-layer members are arrays of length L. */
+typedef struct {
+    int L, N, NH, NKH, HD, FF, V;
+    float eps;
+    const uint8_t **wQ, **wK, **wV, **wO, **wG, **wU, **wD;
+    const float **wAN, **wFN;
+    const int *nQ, *nK, *nV, *nO, *nG, *nU, *nD;
+    int nc;
+    const float *emb, *onw;
+    const uint8_t *wOut;
+    int outNR, outNC, outQuant;
+    KVBlock **kv_array;
+    float *logits;
+    int n_experts, n_experts_per_tok, moe_intermediate;
+    const float **w_gate_inp;
+    const uint8_t **w_gate_exps;
+    const uint8_t **w_up_exps;
+    const uint8_t **w_down_exps;
+    int gate_exp_quant, up_exp_quant, down_exp_quant;
+    const int *q_quant, *k_quant, *v_quant, *o_quant;
+    const int *g_quant, *u_quant, *d_quant;
+    int emb_quant;
+    const uint8_t **wQK;
+    const int *qk_quant;
+    float *cos_table;
+    float *sin_table;
+    int max_ctx;
+    float *workspace;
+    int ws_size;
+    int rope_dim;
+    int full_attn_interval;
+    const uint8_t **wQKV;
+    const int *qkv_quant;
+    const uint8_t **wAttnG;
+    const int *attnG_quant;
+    const float **ssm_conv1d;
+    const float **ssm_a;
+    const float **ssm_dt_bias;
+    const float **ssm_alpha;
+    const float **ssm_beta;
+    const float **ssm_norm;
+    const uint8_t **wSsmOut;
+    const int *ssm_out_quant;
+    float *ssm_state;
+    const uint8_t **wSHexpG, **wSHexpU, **wSHexpD;
+    const int *shexp_g_quant, *shexp_u_quant, *shexp_d_quant;
+    const float **wShexpRouter;
+    const int *layer_types;
+    int n_layers_actual;
+    const uint8_t **w_zaya_ffn_gate_inp, **w_zaya_ffn_gate, **w_zaya_mlp2, **w_zaya_mlp4;
+    const float **w_zaya_router_bias, **w_zaya_ffn_norm;
+    const float **w_zaya_res_hs_w, **w_zaya_res_hs_b, **w_zaya_res_res_w, **w_zaya_res_res_b;
+    int zaya_ffn_gate_inp_quant, zaya_ffn_gate_quant, zaya_mlp2_quant, zaya_mlp4_quant;
+    int *has_moe_layer;
+    int zaya_expert_n;
+    int zaya_moe_intermediate;
+    const uint8_t **w_cca_v1, **w_cca_v2, **w_ssm_conv1d;
+    int cca_v1_quant, cca_v2_quant;
+} BC;
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -103,6 +165,9 @@ void ssm_layer_fused(const float *x, float *residual, float *output, const float
                      float *state, const uint8_t *gate_raw, int gate_nr, int gate_nc, int gate_qt,
                      const uint8_t *ssm_out_raw, int ssm_out_nr, int ssm_out_nc, int ssm_out_qt, int B, int N,
                      int inner, int groups, int state_size, int conv_kernel, int dt_rank);
+/* cengine_batch_instr.c:1233 (computing the intended forward: see mojollama_b200.h) and :591 */
+void batch_forward(const BC *c, const int *tokens, int B, float *ws);
+void moe_ffn(const BC *c, int l, float *x, float *gate_buf, float *up_buf, float *ffn_buf, int B);
 /* cengine_batch_instr.c:141 -- static in the reference, exported here */
 void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd);
 

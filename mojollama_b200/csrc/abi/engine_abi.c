@@ -143,3 +143,13 @@ void ssm_layer_fused(const float *x, float *residual, float *output, const float
                         gate_nr, gate_nc, gate_qt, ssm_out_raw, ssm_out_nr, ssm_out_nc, ssm_out_qt, B, N, inner,
                         groups, state_size, conv_kernel, dt_rank);
 }
+
+/* cengine_batch_instr.c:1233: one decode step for B sequences (see mlq_batch_forward) */
+void batch_forward(const BC *c, const int *tokens, int B, float *ws) { mlq_batch_forward(c, tokens, B, ws); }
+
+/* cengine_batch_instr.c:591: gate_buf / up_buf are not needed */
+void moe_ffn(const BC *c, int l, float *x, float *gate_buf, float *up_buf, float *ffn_buf, int B) {
+    (void)gate_buf;
+    (void)up_buf;
+    mlq_moe_ffn(c, l, x, ffn_buf, B);
+}

@@ -27,14 +27,12 @@
 
 namespace mlq {
 
-struct KVView {
-    const float *k, *v;      // base of the K and V regions
-    const int *table;        // [B][max_pages] physical page of each logical page, or null
-    int table_stride;        // ints between sequences' tables
-    long long page_stride;   // floats between pages
-    int page_size;           // slots per page
-    int row_stride;          // floats between slots (NKH * HD)
-};
+__device__ __forceinline__ const float *kv_kbase(const KVView &kv, int b) {
+    return kv.pool_seq ? kv.pool_seq[b] + (long long)kv.layer * kv.layer_stride : kv.k;
+}
+__device__ __forceinline__ const float *kv_vbase(const KVView &kv, int b) {
+    return kv.pool_seq ? kv.pool_seq[b] + (long long)(kv.n_layers + kv.layer) * kv.layer_stride : kv.v;
+}
 
 __device__ __forceinline__ long long kv_offset(const KVView &kv, int b, int t) {
     if (!kv.table) return (long long)t * kv.row_stride;
@@ -81,14 +79,16 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
     for (int i = 0; i < kMaxAcc; i++) acc[i] = 0.0f;
     __syncthreads();
 
+    const float *kb = kv_kbase(kv, b);
+    const float *vb = kv_vbase(kv, b);
     for (int base = t0; base < t1; base += kTile) {
         const int nt = min(kTile, t1 - base);
         // stage K and V rows of this tile (coalesced along HD)
         for (int i = tid; i < nt * HD; i += blockDim.x) {
             const int t = i / HD, d = i - t * HD;
             const long long off = kv_offset(kv, b, base + t) + (long long)g * HD + d;
-            ks[t * (HD + 1) + d] = kv.k[off];
-            vs[t * HD + d] = kv.v[off];
+            ks[t * (HD + 1) + d] = kb[off];
+            vs[t * HD + d] = vb[off];
         }
         __syncthreads();
         // scores p[h][t] = q_h . k_t (q already scaled)
@@ -192,9 +192,11 @@ __global__ void k_kv_write(KVView kv, float *k_base, float *v_base, const float 
     const int b = blockIdx.y;
     const int t = pos ? pos[b] : pos_scalar;
     const long long off = kv_offset(kv, b, t);
+    float *kb = kv.pool_seq ? const_cast<float *>(kv_kbase(kv, b)) : k_base;
+    float *vb = kv.pool_seq ? const_cast<float *>(kv_vbase(kv, b)) : v_base;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
-        k_base[off + i] = k_new[(size_t)b * row + i];
-        v_base[off + i] = v_new[(size_t)b * row + i];
+        kb[off + i] = k_new[(size_t)b * row + i];
+        vb[off + i] = v_new[(size_t)b * row + i];
     }
 }
 
@@ -290,7 +292,7 @@ int mlq_attn_decode_flat(const float *q, const float *k_cache, const float *v_ca
     const size_t sb = attn_scratch_bytes(1, n_head, head_dim);
     float *scr = (float *)cs.scratch(sb);
     if (cs.failed) return cs.finish();
-    KVView kv{dk, dv, nullptr, 0, 0, 1 << 30, n_kv_head * head_dim};
+    KVView kv{dk, dv, nullptr, 0, 0, 1 << 30, n_kv_head * head_dim, nullptr, 0, 0, 0};
     int rc = launch_attn_decode(dq, kv, nullptr, seq_len, seq_len, 1, n_head, n_kv_head, head_dim, window,
                                 1.0f / sqrtf((float)head_dim), dout, scr, sb, stream());
     if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
@@ -331,7 +333,7 @@ int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_p
     float *scr = (float *)cs.scratch(sb);
     if (cs.failed) return cs.finish();
     KVView kv{dk, dv, dt, table_stride, (long long)page_size * n_kv_head * head_dim, page_size,
-              n_kv_head * head_dim};
+              n_kv_head * head_dim, nullptr, 0, 0, 0};
     int rc = launch_attn_decode(dq, kv, dl, 0, max_len, B, n_head, n_kv_head, head_dim, window,
                                 1.0f / sqrtf((float)head_dim), dout, scr, sb, stream());
     if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }

@@ -1,0 +1,685 @@
+// Whole-model decode step: batch_forward(const BC*, tokens, B, ws)
+// (cengine_batch_instr.c:1233-1493) -- B sequences, one new token each.
+//
+// Per layer, as the reference structures it, but with the normalised activations
+// actually feeding the projections (the reference writes its pre-norm output back
+// into x and projects an untouched buffer, so every layer adds nothing):
+//   xn, res = RMSNorm(clamp(x)) * w_attn_norm, clamp(x)          (NaN -> 0, +-1000)
+//   SSM layer (layer_types[l] == 1): x = res + W_ssm_out . ((W_attn_gate . xn) * ssm_step(xn))
+//   attention layer: q, k, v from fused QKV / fused QK + V / separate projections;
+//     NeoX RoPE at the sequence position; K, V appended to the sequence's KVBlock page
+//     pool (page allocated on first touch from its LIFO free list); split-K attention
+//     over the pages; x = res + (W_attn_gate or W_o) . att
+//   xn, res = RMSNorm(clamp(x)) * w_ffn_norm, clamp(x)
+//   MoE (n_experts > 0): F32 router, softmax, top-k without renormalisation (moe_ffn,
+//     :615-646), experts through the grouped GEMV with device-side indices, shared expert
+//     scaled by its router score when positive (:1440-1452); dense: SiLU(gate)*up, down
+//   x = res + ffn
+// then seq_len += 1 for every sequence, final RMSNorm and the output projection into
+// c->logits [B][outNR].
+//
+// All weight pointers reachable from the BC (host or device) are resolved once per BC
+// into a device plan (host weights uploaded through the residency cache); later calls
+// with the same BC contents reuse it.  Weights are treated as immutable while a plan
+// exists; mlq_cache_clear() drops the plans with the cache.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "../../include/mojollama_b200_ref_abi.h"
+#include "mlq_internal.h"
+
+namespace mlq {
+
+// ------------------------------------------------------------------------------ kernels
+__global__ void k_embed_f32(const float *__restrict__ emb, const int *__restrict__ tokens, float *__restrict__ x,
+                            int N, int V) {
+    const int b = blockIdx.y;
+    int t = tokens[b];
+    if (t < 0 || t >= V) t = 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x)
+        x[(size_t)b * N + i] = emb[(size_t)t * N + i];
+}
+
+// dst[b][0:n] = src[b*src_stride + off : +n]
+__global__ void k_copy_cols(float *__restrict__ dst, const float *__restrict__ src, int n, int src_stride, int off) {
+    const int b = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        dst[(size_t)b * n + i] = src[(size_t)b * src_stride + off + i];
+}
+
+// h = silu(g) * u, exact, no clamp (cengine_batch_instr.c:1465)
+__global__ void k_silu_mul(float *__restrict__ h, const float *__restrict__ g, const float *__restrict__ u, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        h[i] = (gv / (1.0f + expf(-gv))) * u[i];
+    }
+}
+
+// score[b] = xn[b] . r  (one block per token)
+__global__ void k_dot_rows(const float *__restrict__ xn, const float *__restrict__ r, float *__restrict__ score, int N) {
+    __shared__ float sh[32];
+    const int b = blockIdx.x;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) s = fmaf(xn[(size_t)b * N + i], r[i], s);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (threadIdx.x == 0) score[b] = s;
+    }
+}
+
+// The KVBlock's own k/v arrays ([L][1024][64][row], cengine_batch_instr.c:1349-1350) get the
+// same rows as the page pool; pages index them with the fixed 64-slot block size.
+__global__ void k_kv_mirror(float *const *__restrict__ mk, float *const *__restrict__ mv,
+                            const int *__restrict__ tab, const int *__restrict__ pos, const float *__restrict__ k,
+                            const float *__restrict__ v, int row, int page_size, int layer) {
+    const int b = blockIdx.y;
+    float *kb = mk[b], *vb = mv[b];
+    if (!kb || !vb) return;
+    const int p = pos[b];
+    const int page = tab[(size_t)b * 1024 + p / page_size];
+    if (page < 0 || page >= 1024) return;
+    const size_t off = ((size_t)layer * 1024 * 64 + (size_t)page * 64 + (p % page_size)) * row;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
+        kb[off + i] = k[(size_t)b * row + i];
+        vb[off + i] = v[(size_t)b * row + i];
+    }
+}
+
+// shared expert input (reference :1446-1447): h = silu(up) * gate
+__global__ void k_shexp_act(float *__restrict__ h, const float *__restrict__ gate, const float *__restrict__ up, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float u = up[i];
+        h[i] = (u / (1.0f + expf(-u))) * gate[i];
+    }
+}
+
+// x[b] += score[b] * y[b] when score[b] > 0
+__global__ void k_add_scaled_pos(float *__restrict__ x, const float *__restrict__ y, const float *__restrict__ score, int N) {
+    const int b = blockIdx.y;
+    const float sc = score[b];
+    if (!(sc > 0.0f)) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x)
+        x[(size_t)b * N + i] += sc * y[(size_t)b * N + i];
+}
+
+static int grid1(long long n) {
+    long long g = (n + 255) / 256;
+    return (int)(g > 2048 ? 2048 : (g < 1 ? 1 : g));
+}
+
+// ------------------------------------------------------------------------------ plan
+struct LayerPlan {
+    bool ssm = false;
+    const float *an = nullptr, *fn = nullptr;
+    const uint8_t *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *wqk = nullptr, *wqkv = nullptr,
+                  *wattng = nullptr;
+    int qq = 0, qk = 0, qv = 0, qo = 0, qqk = 0, qqkv = 0, qattng = 0;
+    int nq = 0, nk = 0, nv = 0, no = 0;
+    const uint8_t *wg = nullptr, *wu = nullptr, *wd = nullptr;
+    int qg = 0, qu = 0, qd = 0, ng = 0, nu = 0, nd = 0;
+    const float *router = nullptr;
+    const uint8_t *gexp = nullptr, *uexp = nullptr, *dexp = nullptr;
+    long long gstride = 0, ustride = 0, dstride = 0;
+    const uint8_t *shg = nullptr, *shu = nullptr, *shd = nullptr;
+    int qshg = 0, qshu = 0, qshd = 0;
+    const float *shrouter = nullptr;
+    const float *conv = nullptr, *ssm_a = nullptr, *ssm_dt = nullptr, *ssm_alpha = nullptr, *ssm_beta = nullptr;
+    const uint8_t *wssmout = nullptr;
+    int qssmout = 0;
+};
+
+struct ModelPlan {
+    std::vector<uint8_t> fingerprint;
+    std::vector<LayerPlan> layers;
+    const float *emb = nullptr;
+    const float *onw = nullptr;
+    const uint8_t *wout = nullptr;
+    const float *cos_t = nullptr, *sin_t = nullptr;
+    float *ssm_state = nullptr;   // device view of c->ssm_state (host state is staged per call)
+};
+
+static std::mutex g_plan_mu;
+static std::map<std::pair<int, uintptr_t>, ModelPlan> g_plans;
+
+// SSM dims hard-coded by the reference engine (cengine_batch_instr.c:1253-1254)
+constexpr int kSsmGroups = 32, kSsmState = 128, kSsmDtRank = 32;
+constexpr int kShexpFF = 512;   // shared expert width (cengine_batch_instr.c:1444)
+
+template <typename T>
+static void fp_push(std::vector<uint8_t> &f, const T *arr, int n) {
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(&arr);
+    f.insert(f.end(), p, p + sizeof(arr));
+    if (arr) {
+        const uint8_t *q = reinterpret_cast<const uint8_t *>(arr);
+        f.insert(f.end(), q, q + sizeof(T) * (size_t)n);
+    }
+}
+
+// The per-call members (KV blocks, logits, workspace, SSM state) are left out, so a caller
+// that swaps them between steps keeps its plan.
+static std::vector<uint8_t> fingerprint(const BC *c) {
+    BC k = *c;
+    k.kv_array = nullptr;
+    k.logits = nullptr;
+    k.workspace = nullptr;
+    k.ws_size = 0;
+    k.ssm_state = nullptr;
+    std::vector<uint8_t> f(reinterpret_cast<const uint8_t *>(&k), reinterpret_cast<const uint8_t *>(&k) + sizeof(BC));
+    const int L = c->L;
+    f.push_back(ref_compat() ? 1 : 0);
+    fp_push(f, c->wQ, L); fp_push(f, c->wK, L); fp_push(f, c->wV, L); fp_push(f, c->wO, L);
+    fp_push(f, c->wG, L); fp_push(f, c->wU, L); fp_push(f, c->wD, L); fp_push(f, c->wAN, L); fp_push(f, c->wFN, L);
+    fp_push(f, c->q_quant, L); fp_push(f, c->k_quant, L); fp_push(f, c->v_quant, L); fp_push(f, c->o_quant, L);
+    fp_push(f, c->g_quant, L); fp_push(f, c->u_quant, L); fp_push(f, c->d_quant, L);
+    fp_push(f, c->nQ, L); fp_push(f, c->nK, L); fp_push(f, c->nV, L); fp_push(f, c->nO, L);
+    fp_push(f, c->nG, L); fp_push(f, c->nU, L); fp_push(f, c->nD, L);
+    fp_push(f, c->w_gate_inp, L); fp_push(f, c->w_gate_exps, L); fp_push(f, c->w_up_exps, L);
+    fp_push(f, c->w_down_exps, L); fp_push(f, c->wQK, L); fp_push(f, c->qk_quant, L); fp_push(f, c->wQKV, L);
+    fp_push(f, c->qkv_quant, L); fp_push(f, c->wAttnG, L); fp_push(f, c->attnG_quant, L);
+    fp_push(f, c->ssm_conv1d, L); fp_push(f, c->wSsmOut, L); fp_push(f, c->layer_types, L);
+    fp_push(f, c->wSHexpG, L); fp_push(f, c->wShexpRouter, L);
+    return f;
+}
+
+static const uint8_t *W(CallScope &cs, const void *p, int qt, int rows, int cols) {
+    if (!p) return nullptr;
+    const size_t rb = mlq_row_bytes(qt, cols);
+    if (!rb || rows <= 0) {
+        set_error(MLQ_ERR_TYPE, "batch_forward: weight type %d with %d x %d", qt, rows, cols);
+        cs.failed = true;
+        return nullptr;
+    }
+    return (const uint8_t *)cs.weights(p, rb * (size_t)rows);
+}
+
+static const float *Fv(CallScope &cs, const void *p, size_t n) {
+    return p ? (const float *)cs.weights(p, sizeof(float) * n) : nullptr;
+}
+
+static int at(const int *a, int l, int dflt) { return a ? a[l] : dflt; }
+
+// Bytes between experts of a 3-D expert tensor [E][rows][cols].  Default: the type's row
+// size.  Reference-compatibility mode: moe_ffn's own rule (cengine_batch_instr.c:592-604),
+// which knows Q4_K/Q5_K/Q6_K/MXFP4 only and uses the Q4_K size for any other gate/up type
+// and the Q6_K size for any other down type (integer division by the 256-wide super-block).
+static long long expert_stride(int qt, int rows, int cols, bool down) {
+    if (!ref_compat()) return (long long)rows * mlq_row_bytes(qt, cols);
+    if (qt == MLQ_MXFP4) return (long long)rows * (cols / 32) * 17;
+    int bytes = down ? 210 : 144;
+    if (qt == MLQ_Q4_K && down) bytes = 144;
+    if (qt == MLQ_Q5_K) bytes = 176;
+    if (qt == MLQ_Q6_K) bytes = 210;
+    return (long long)rows * (cols / 256) * bytes;
+}
+
+// Bytes the kernels read from an expert tensor: E experts at `stride` apart, each
+// rows x row_bytes (the two differ only under the reference's stride rule).
+static size_t expert_extent(long long stride, int E, int qt, int rows, int cols) {
+    const size_t mat = (size_t)rows * mlq_row_bytes(qt, cols);
+    const size_t a = (size_t)stride * E, b = (size_t)stride * (E - 1) + mat;
+    return a > b ? a : b;
+}
+
+static bool build_plan(const BC *c, CallScope &cs, ModelPlan &P) {
+    const int L = c->L, N = c->N, NH = c->NH, NKH = c->NKH, HD = c->HD, inner = NH * HD;
+    P.layers.assign(L, LayerPlan{});
+    for (int l = 0; l < L; l++) {
+        LayerPlan &lp = P.layers[l];
+        lp.an = Fv(cs, c->wAN ? c->wAN[l] : nullptr, N);
+        lp.fn = Fv(cs, c->wFN ? c->wFN[l] : nullptr, N);
+        lp.ssm = c->layer_types && c->layer_types[l] == 1 && c->ssm_conv1d && c->ssm_conv1d[l];
+        if (c->wAttnG && c->wAttnG[l]) {
+            lp.qattng = at(c->attnG_quant, l, 8);
+            lp.wattng = lp.ssm ? W(cs, c->wAttnG[l], lp.qattng, inner, N) : W(cs, c->wAttnG[l], lp.qattng, N, inner);
+        }
+        if (lp.ssm) {
+            lp.conv = Fv(cs, c->ssm_conv1d[l], (size_t)2 * inner);
+            lp.ssm_a = Fv(cs, c->ssm_a ? c->ssm_a[l] : nullptr, kSsmGroups);
+            lp.ssm_dt = Fv(cs, c->ssm_dt_bias ? c->ssm_dt_bias[l] : nullptr, kSsmGroups);
+            lp.ssm_alpha = Fv(cs, c->ssm_alpha ? c->ssm_alpha[l] : nullptr, (size_t)kSsmGroups * kSsmDtRank);
+            lp.ssm_beta = Fv(cs, c->ssm_beta ? c->ssm_beta[l] : nullptr, (size_t)kSsmGroups * kSsmDtRank);
+            if (c->wSsmOut && c->wSsmOut[l]) {
+                lp.qssmout = at(c->ssm_out_quant, l, 8);
+                lp.wssmout = W(cs, c->wSsmOut[l], lp.qssmout, N, inner);
+            }
+            if (!lp.ssm_a || !lp.ssm_dt || !lp.ssm_alpha || !lp.ssm_beta) {
+                set_error(MLQ_ERR_ARG, "batch_forward: SSM layer %d without its parameters", l);
+                return false;
+            }
+        } else {
+            lp.nq = at(c->nQ, l, inner);
+            lp.nk = at(c->nK, l, NKH * HD);
+            lp.nv = at(c->nV, l, NKH * HD);
+            lp.no = at(c->nO, l, N);
+            // the reference reads Q, K, V rows at b*NH*HD / b*NKH*HD and o-proj rows at b*N
+            if (lp.nq != inner || lp.nk != NKH * HD || lp.nv != NKH * HD || lp.no != N || NKH * HD > N) {
+                set_error(MLQ_ERR_ARG, "batch_forward: layer %d projection sizes %d/%d/%d/%d do not match NH*HD, "
+                                       "NKH*HD, N", l, lp.nq, lp.nk, lp.nv, lp.no);
+                return false;
+            }
+            if (c->wQKV && c->wQKV[l]) {
+                lp.qqkv = at(c->qkv_quant, l, 8);
+                lp.wqkv = W(cs, c->wQKV[l], lp.qqkv, inner + 2 * N, c->nc);
+            } else if (c->wQK && c->wQK[l]) {
+                lp.qqk = at(c->qk_quant, l, 8);
+                lp.wqk = W(cs, c->wQK[l], lp.qqk, lp.nq + lp.nk, c->nc);
+                lp.qv = at(c->v_quant, l, 8);
+                lp.wv = W(cs, c->wV[l], lp.qv, lp.nv, c->nc);
+            } else {
+                lp.qq = at(c->q_quant, l, 8);
+                lp.qk = at(c->k_quant, l, 8);
+                lp.qv = at(c->v_quant, l, 8);
+                lp.wq = W(cs, c->wQ ? c->wQ[l] : nullptr, lp.qq, lp.nq, c->nc);
+                lp.wk = W(cs, c->wK ? c->wK[l] : nullptr, lp.qk, lp.nk, c->nc);
+                lp.wv = W(cs, c->wV ? c->wV[l] : nullptr, lp.qv, lp.nv, c->nc);
+                if (!lp.wq || !lp.wk || !lp.wv) {
+                    set_error(MLQ_ERR_ARG, "batch_forward: attention layer %d without Q/K/V weights", l);
+                    return false;
+                }
+            }
+            if (!lp.wattng) {
+                lp.qo = at(c->o_quant, l, 8);
+                lp.wo = W(cs, c->wO ? c->wO[l] : nullptr, lp.qo, lp.no, inner);
+                if (!lp.wo) {
+                    set_error(MLQ_ERR_ARG, "batch_forward: attention layer %d without an output projection", l);
+                    return false;
+                }
+            }
+        }
+        if (c->n_experts > 0 && c->n_experts_per_tok > 0) {
+            const int E = c->n_experts, M = c->moe_intermediate;
+            lp.router = Fv(cs, c->w_gate_inp ? c->w_gate_inp[l] : nullptr, (size_t)E * N);
+            lp.gstride = expert_stride(c->gate_exp_quant, M, N, false);
+            lp.ustride = expert_stride(c->up_exp_quant, M, N, false);
+            lp.dstride = expert_stride(c->down_exp_quant, N, M, true);
+            if (!lp.router || !lp.gstride || !lp.ustride || !lp.dstride || !c->w_gate_exps || !c->w_up_exps ||
+                !c->w_down_exps) {
+                set_error(MLQ_ERR_ARG, "batch_forward: MoE layer %d incomplete", l);
+                return false;
+            }
+            lp.gexp = (const uint8_t *)cs.weights(c->w_gate_exps[l], expert_extent(lp.gstride, E, c->gate_exp_quant, M, N));
+            lp.uexp = (const uint8_t *)cs.weights(c->w_up_exps[l], expert_extent(lp.ustride, E, c->up_exp_quant, M, N));
+            lp.dexp = (const uint8_t *)cs.weights(c->w_down_exps[l], expert_extent(lp.dstride, E, c->down_exp_quant, N, M));
+            if (c->wSHexpG && c->wSHexpG[l]) {
+                lp.qshg = at(c->shexp_g_quant, l, 8);
+                lp.qshu = at(c->shexp_u_quant, l, 8);
+                lp.qshd = at(c->shexp_d_quant, l, 8);
+                lp.shg = W(cs, c->wSHexpG[l], lp.qshg, kShexpFF, N);
+                lp.shu = W(cs, c->wSHexpU[l], lp.qshu, kShexpFF, N);
+                lp.shd = W(cs, c->wSHexpD[l], lp.qshd, N, kShexpFF);
+                lp.shrouter = Fv(cs, c->wShexpRouter ? c->wShexpRouter[l] : nullptr, N);
+            }
+        } else if (c->wG && c->wG[l]) {
+            lp.qg = at(c->g_quant, l, 8);
+            lp.qu = at(c->u_quant, l, 8);
+            lp.qd = at(c->d_quant, l, 8);
+            lp.ng = at(c->nG, l, c->FF);
+            lp.nu = at(c->nU, l, c->FF);
+            lp.nd = at(c->nD, l, N);
+            lp.wg = W(cs, c->wG[l], lp.qg, lp.ng, c->nc);
+            lp.wu = W(cs, c->wU[l], lp.qu, lp.nu, c->nc);
+            lp.wd = W(cs, c->wD[l], lp.qd, lp.nd, c->FF);
+        }
+        if (cs.failed) return false;
+    }
+    const int rope_dim = c->rope_dim > 0 ? c->rope_dim : HD;
+    P.emb = c->emb_quant == 0 ? Fv(cs, c->emb, (size_t)c->V * N) : (const float *)W(cs, c->emb, c->emb_quant, c->V, N);
+    P.onw = Fv(cs, c->onw, N);
+    P.wout = W(cs, c->wOut, c->outQuant, c->outNR, c->outNC);
+    P.cos_t = Fv(cs, c->cos_table, (size_t)c->max_ctx * (rope_dim / 2));
+    P.sin_t = Fv(cs, c->sin_table, (size_t)c->max_ctx * (rope_dim / 2));
+    return !cs.failed && P.emb && P.wout && P.cos_t && P.sin_t;
+}
+
+static int fwd_fail(CallScope &cs, int rc) {
+    cs.failed = true;
+    cs.finish();
+    return rc;
+}
+
+}  // namespace mlq
+
+using namespace mlq;
+
+extern "C" {
+
+size_t mlq_sizeof_bc(void) { return sizeof(BC); }
+
+void mlq_forget_model_plans(void) {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    g_plans.clear();
+}
+
+int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
+    const BC *c = static_cast<const BC *>(bc);
+    if (!c || !tokens || B <= 0 || B > 64 || c->L <= 0 || c->N <= 0 || c->NH <= 0 || c->NKH <= 0 ||
+        c->NH % c->NKH || c->HD <= 0 || !c->kv_array || !c->logits || c->max_ctx <= 0 || c->N % 32) {
+        set_error(MLQ_ERR_ARG, "batch_forward: bad model description or batch (B 1..64)");
+        return MLQ_ERR_ARG;
+    }
+    const int L = c->L, N = c->N, NH = c->NH, NKH = c->NKH, HD = c->HD, inner = NH * HD, kvrow = NKH * HD;
+    const int rope_dim = c->rope_dim > 0 ? c->rope_dim : HD;
+    // Reference-compatibility mode reproduces the reference's data flow: every projection
+    // reads the workspace's xn region (ws + B*S, never written by the reference), the
+    // normalised activations overwrite x, and the fused QKV / QK projections hand
+    // sequence b the Q slice at b*NH*HD of the projection buffer.
+    const bool compat = ref_compat();
+    int S = N;
+    if (inner > S) S = inner;
+    if (c->FF > S) S = c->FF;
+    if (kvrow > S) S = kvrow;
+    if (inner + kvrow > S) S = inner + kvrow;
+    if (S < 8192) S = 8192;
+    if (compat && !ws) {
+        set_error(MLQ_ERR_ARG, "batch_forward: reference-compatibility mode reads the workspace; ws is NULL");
+        return MLQ_ERR_ARG;
+    }
+    CallScope cs;
+    Ctx *cx = ctx();
+    if (!cx) return mlq_last_error();
+    // ------------------------------------------------------------------ plan
+    ModelPlan *P;
+    {
+        std::lock_guard<std::mutex> lk(g_plan_mu);
+        auto key = std::make_pair(cx->device, (uintptr_t)c);
+        auto fp = fingerprint(c);
+        auto it = g_plans.find(key);
+        if (it == g_plans.end() || it->second.fingerprint != fp) {
+            ModelPlan np;
+            if (!build_plan(c, cs, np)) return fwd_fail(cs, mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG);
+            np.fingerprint = std::move(fp);
+            g_plans[key] = std::move(np);
+            it = g_plans.find(key);
+        }
+        P = &it->second;
+    }
+    cudaStream_t s = stream();
+    // ------------------------------------------------------------------ KV pages (host bookkeeping)
+    std::vector<int> pos(B), tables((size_t)B * 1024);
+    std::vector<float *> pools(B), mirror_k(B), mirror_v(B);
+    int max_len = 0;
+    MlqKVBlock *kv0 = c->kv_array[0];
+    for (int b = 0; b < B; b++) {
+        MlqKVBlock *kv = c->kv_array[b];
+        if (!kv || !kv->pt.pages || !kv->pt.table || kv->pt._nkh != NKH || kv->pt._hd != HD || kv->pt._n_layers < L ||
+            kv->pt.page_size != kv0->pt.page_size || kv->pt.n_pages != kv0->pt.n_pages ||
+            kv->pt._n_layers != kv0->pt._n_layers || kv->pt.page_size <= 0 || kv->pt.n_pages <= 0) {
+            set_error(MLQ_ERR_ARG, "batch_forward: KVBlock of sequence %d does not match the model", b);
+            return fwd_fail(cs, MLQ_ERR_ARG);
+        }
+        if (!is_device_ptr(kv->pt.pages)) {
+            set_error(MLQ_ERR_ARG, "batch_forward: KVBlock of sequence %d was not made by kv_init / page_table_init "
+                                   "of this library (its pages are not device memory)", b);
+            return fwd_fail(cs, MLQ_ERR_ARG);
+        }
+        const int p = kv->seq_len[0];
+        const int blk = p / kv->pt.page_size;
+        if (p >= c->max_ctx || blk >= 1024) {
+            set_error(MLQ_ERR_CAPACITY, "batch_forward: sequence %d at position %d (max_ctx %d)", b, p, c->max_ctx);
+            return fwd_fail(cs, MLQ_ERR_CAPACITY);
+        }
+        // every page below the new position must be mapped (attention reads them all)
+        for (int i = 0; i < blk; i++) {
+            if (kv->pt.table[i] < 0 || kv->pt.table[i] >= kv->pt.n_pages) {
+                set_error(MLQ_ERR_ARG, "batch_forward: sequence %d has logical page %d unmapped (%d) below position %d",
+                          b, i, kv->pt.table[i], p);
+                return fwd_fail(cs, MLQ_ERR_ARG);
+            }
+        }
+        if (kv->pt.table[blk] >= kv->pt.n_pages) {
+            set_error(MLQ_ERR_ARG, "batch_forward: sequence %d maps page %d beyond the pool", b, kv->pt.table[blk]);
+            return fwd_fail(cs, MLQ_ERR_ARG);
+        }
+        if (kv->pt.table[blk] < 0) {
+            const int page = mlq_page_table_alloc(&kv->pt);
+            if (page < 0) {
+                set_error(MLQ_ERR_CAPACITY, "batch_forward: sequence %d: page pool full", b);
+                return fwd_fail(cs, MLQ_ERR_CAPACITY);
+            }
+            kv->pt.table[blk] = page;
+        }
+        pos[b] = p;
+        memcpy(&tables[(size_t)b * 1024], kv->pt.table, 1024 * sizeof(int));
+        pools[b] = kv->pt.pages;
+        // the KVBlock's own k/v arrays ([L][1024][64][row]) are written only when kv_init of
+        // this library made them and the page geometry is the reference's (64 slots)
+        const size_t need = (size_t)L * 1024 * 64 * kvrow * sizeof(float);
+        const bool mirror = kv->pt.page_size == 64 && kv->k && kv->v && kv_array_bytes(kv->k) >= need &&
+                            kv_array_bytes(kv->v) >= need;
+        mirror_k[b] = mirror ? kv->k : nullptr;
+        mirror_v[b] = mirror ? kv->v : nullptr;
+        if (p + 1 > max_len) max_len = p + 1;
+    }
+    // ------------------------------------------------------------------ buffers
+    const int FFmax = c->FF > kShexpFF ? c->FF : kShexpFF;
+    const int qkv_w = inner + 2 * N > inner + 2 * kvrow ? inner + 2 * N : inner + 2 * kvrow;
+    const int topk = c->n_experts_per_tok, M = c->moe_intermediate;
+    int *d_tok = (int *)cs.in(tokens, sizeof(int) * B);
+    int *d_pos = (int *)cs.scratch(sizeof(int) * B);
+    int *d_len = (int *)cs.scratch(sizeof(int) * B);
+    int *d_tab = (int *)cs.scratch(sizeof(int) * (size_t)B * 1024);
+    float **d_pools = (float **)cs.scratch(sizeof(float *) * B);
+    float **d_mk = (float **)cs.scratch(sizeof(float *) * B);
+    float **d_mv = (float **)cs.scratch(sizeof(float *) * B);
+    const float *xin = compat ? (const float *)cs.in(ws + (size_t)B * S, sizeof(float) * (size_t)B * N) : nullptr;
+    float *ws_out = ws ? (float *)cs.out(ws, sizeof(float) * (size_t)B * N) : nullptr;
+    float *x = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
+    float *xn = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
+    float *res = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
+    float *qkv = (float *)cs.scratch(sizeof(float) * (size_t)B * (qkv_w > N ? qkv_w : N));
+    float *q = (float *)cs.scratch(sizeof(float) * (size_t)B * inner);
+    float *k = (float *)cs.scratch(sizeof(float) * (size_t)B * kvrow);
+    float *v = (float *)cs.scratch(sizeof(float) * (size_t)B * kvrow);
+    float *att = (float *)cs.scratch(sizeof(float) * (size_t)B * inner);
+    float *tmp = (float *)cs.scratch(sizeof(float) * (size_t)B * (inner > N ? inner : N));
+    float *g = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
+    float *u = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
+    float *h = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
+    float *logits_e = (float *)cs.scratch(sizeof(float) * (size_t)B * (c->n_experts > 0 ? c->n_experts : 1));
+    int *e_idx = (int *)cs.scratch(sizeof(int) * (size_t)B * (topk > 0 ? topk : 1));
+    float *e_w = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1));
+    float *hm = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1) * (M > 0 ? M : 1));
+    float *score = (float *)cs.scratch(sizeof(float) * B);
+    const size_t attn_sb = attn_scratch_bytes(B, NH, HD);
+    float *attn_scr = (float *)cs.scratch(attn_sb);
+    float *d_state = nullptr;
+    bool any_ssm = false;
+    for (int l = 0; l < L; l++) any_ssm |= P->layers[l].ssm;
+    if (any_ssm) {
+        if (!c->ssm_state) {
+            set_error(MLQ_ERR_ARG, "batch_forward: SSM layers without ssm_state");
+            return fwd_fail(cs, MLQ_ERR_ARG);
+        }
+        d_state = (float *)cs.inout(c->ssm_state, sizeof(float) * (size_t)L * kSsmGroups * kSsmState);
+    }
+    float *d_logits = (float *)cs.out(c->logits, sizeof(float) * (size_t)B * c->outNR);
+    if (cs.failed) return cs.finish();
+    std::vector<int> lens(B);
+    for (int b = 0; b < B; b++) lens[b] = pos[b] + 1;
+    if (!MLQ_CUDA(cudaMemcpyAsync(d_pos, pos.data(), sizeof(int) * B, cudaMemcpyHostToDevice, s)) ||
+        !MLQ_CUDA(cudaMemcpyAsync(d_len, lens.data(), sizeof(int) * B, cudaMemcpyHostToDevice, s)) ||
+        !MLQ_CUDA(cudaMemcpyAsync(d_tab, tables.data(), sizeof(int) * (size_t)B * 1024, cudaMemcpyHostToDevice, s)) ||
+        !MLQ_CUDA(cudaMemcpyAsync(d_pools, pools.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)) ||
+        !MLQ_CUDA(cudaMemcpyAsync(d_mk, mirror_k.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)) ||
+        !MLQ_CUDA(cudaMemcpyAsync(d_mv, mirror_v.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)))
+        return fwd_fail(cs, MLQ_ERR_CUDA);
+
+    int rc = MLQ_OK;
+#define MLQ_TRY(expr)                               \
+    do {                                            \
+        if (rc == MLQ_OK) rc = (expr);              \
+    } while (0)
+    // ------------------------------------------------------------------ embedding
+    if (c->emb_quant == 0) {
+        k_embed_f32<<<dim3(grid1(N) > 16 ? 16 : grid1(N), B), 256, 0, s>>>(P->emb, d_tok, x, N, c->V);
+        count_launch();
+    } else {
+        const size_t rb = mlq_row_bytes(c->emb_quant, N);
+        for (int b = 0; b < B; b++) {
+            int t = tokens[b];
+            if (t < 0 || t >= c->V) t = 0;
+            MLQ_TRY(launch_dequantize((const uint8_t *)P->emb + rb * (size_t)t, c->emb_quant, x + (size_t)b * N, N, s));
+        }
+    }
+    const int ps = kv0->pt.page_size;
+    const long long layer_stride = (long long)kv0->pt.n_pages * ps * kvrow;
+    const float scale = 1.0f / sqrtf((float)HD);
+    // ------------------------------------------------------------------ layers
+    // norm output and projection input: xn / xn normally; x / the workspace's xn region in
+    // reference-compatibility mode
+    float *nout = compat ? x : xn;
+    const float *pin = compat ? xin : xn;
+    const float inf = HUGE_VALF;
+    for (int l = 0; l < L && rc == MLQ_OK; l++) {
+        const LayerPlan &lp = P->layers[l];
+        MLQ_TRY(launch_rms_norm(nout, x, lp.an, res, B, N, c->eps, 1, s));
+        if (lp.ssm) {
+            float *st = d_state + (size_t)l * kSsmGroups * kSsmState;
+            MLQ_TRY(launch_ssm_decode_step(pin, att, lp.conv, lp.ssm_a, lp.ssm_dt, lp.ssm_alpha, lp.ssm_beta, st, B, N,
+                                           inner, kSsmGroups, kSsmState, kSsmDtRank, s));
+            if (lp.wattng) {
+                MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, pin, g, inner, N, B, 0, s));
+                MLQ_TRY(launch_mul(att, g, (long long)B * inner, s));
+            } else {
+                cudaMemsetAsync(att, 0, sizeof(float) * (size_t)B * inner, s);
+            }
+            if (lp.wssmout) {
+                MLQ_TRY(launch_matmul(lp.wssmout, lp.qssmout, att, tmp, N, inner, B, 0, s));
+                MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            } else {
+                cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
+            }
+        } else {
+            // projections
+            if (lp.wqkv) {
+                const int n_qkv = inner + 2 * N;
+                MLQ_TRY(launch_matmul(lp.wqkv, lp.qqkv, pin, qkv, n_qkv, c->nc, B, 0, s));
+                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
+                                                                                        compat ? inner : n_qkv, 0);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, n_qkv, inner);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(v, qkv, kvrow, n_qkv, inner + N);
+                count_launch(3);
+            } else if (lp.wqk) {
+                const int nqk = lp.nq + lp.nk;
+                MLQ_TRY(launch_matmul(lp.wqk, lp.qqk, pin, qkv, nqk, c->nc, B, 0, s));
+                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
+                                                                                        compat ? inner : nqk, 0);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, nqk, lp.nq);
+                count_launch(2);
+                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
+            } else {
+                MLQ_TRY(launch_matmul(lp.wq, lp.qq, pin, q, lp.nq, c->nc, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.wk, lp.qk, pin, k, lp.nk, c->nc, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
+            }
+            MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, d_pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+            MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, d_pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+            KVView kv{nullptr, nullptr, d_tab, 1024, (long long)ps * kvrow, ps, kvrow, d_pools, layer_stride, l,
+                      kv0->pt._n_layers};
+            MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, d_pos, 0, B, kvrow, s));
+            if (rc == MLQ_OK) {
+                k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(d_mk, d_mv, d_tab, d_pos, k,
+                                                                                        v, kvrow, ps, l);
+                count_launch();
+            }
+            // attention over positions 0..pos (length pos + 1 per sequence)
+            MLQ_TRY(launch_attn_decode(q, kv, d_len, 0, max_len, B, NH, NKH, HD, 0, scale, att, attn_scr, attn_sb, s));
+            if (lp.wattng) MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, att, tmp, N, inner, B, 0, s));
+            else MLQ_TRY(launch_matmul(lp.wo, lp.qo, att, tmp, lp.no, inner, B, 0, s));
+            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+        }
+        // FFN
+        MLQ_TRY(launch_rms_norm(nout, x, lp.fn, res, B, N, c->eps, 1, s));
+        if (lp.router) {
+            const int E = c->n_experts;
+            MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, logits_e, E, N, B, 0, s));
+            MLQ_TRY(launch_router_topk(logits_e, B, E, topk, 0, e_idx, e_w, s));
+            MLQ_TRY(launch_moe_indexed(0, c->gate_exp_quant, lp.gexp, lp.uexp, lp.gstride, e_idx, e_w, topk, B, M, N,
+                                       pin, hm, nullptr, s, inf));
+            MLQ_TRY(launch_moe_indexed(1, c->down_exp_quant, lp.dexp, nullptr, lp.dstride, e_idx, e_w, topk, B, N, M,
+                                       hm, x, res, s));
+            if (lp.shg && lp.shrouter) {
+                k_dot_rows<<<B, 256, 0, s>>>(pin, lp.shrouter, score, N);
+                count_launch();
+                MLQ_TRY(launch_matmul(lp.shg, lp.qshg, pin, g, kShexpFF, N, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.shu, lp.qshu, pin, u, kShexpFF, N, B, 0, s));
+                k_shexp_act<<<grid1((long long)B * kShexpFF), 256, 0, s>>>(h, g, u, (long long)B * kShexpFF);
+                count_launch();
+                MLQ_TRY(launch_matmul(lp.shd, lp.qshd, h, tmp, N, kShexpFF, B, 0, s));
+                k_add_scaled_pos<<<dim3(grid1(N) > 16 ? 16 : grid1(N), B), 256, 0, s>>>(x, tmp, score, N);
+                count_launch();
+            }
+        } else if (lp.wg) {
+            MLQ_TRY(launch_matmul(lp.wg, lp.qg, pin, g, lp.ng, c->nc, B, 0, s));
+            MLQ_TRY(launch_matmul(lp.wu, lp.qu, pin, u, lp.nu, c->nc, B, 0, s));
+            k_silu_mul<<<grid1((long long)B * c->FF), 256, 0, s>>>(h, g, u, (long long)B * c->FF);
+            count_launch();
+            MLQ_TRY(launch_matmul(lp.wd, lp.qd, h, tmp, lp.nd, c->FF, B, 0, s));
+            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+        } else if (!compat) {
+            cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
+        }   // (with no FFN the reference leaves the normalised activations in x)
+    }
+    // ------------------------------------------------------------------ head
+    // the final normalised hidden state also lands in ws[0 : B*N], where the reference
+    // leaves it (its x buffer is the start of the workspace)
+    float *hfin = ws_out ? ws_out : xn;
+    MLQ_TRY(launch_rms_norm(hfin, x, P->onw, res, B, N, c->eps, 1, s));
+    MLQ_TRY(launch_matmul(P->wout, c->outQuant, hfin, d_logits, c->outNR, c->outNC, B, 0, s));
+#undef MLQ_TRY
+    if (rc != MLQ_OK) return fwd_fail(cs, rc);
+    for (int b = 0; b < B; b++) c->kv_array[b]->seq_len[0]++;
+    return cs.finish();
+}
+
+// moe_ffn (cengine_batch_instr.c:591-665): for each of the B tokens of x [B][N], F32 router
+// of layer l, softmax, top-k without renormalisation, experts, weighted sum -> ffn [B][N]
+// (the reference keeps only the last token's result in its single ffn_buf; every token's
+// row is written here).
+int mlq_moe_ffn(const void *bc, int l, const float *x, float *ffn, int B) {
+    const BC *c = static_cast<const BC *>(bc);
+    if (!c || !x || !ffn || B <= 0 || l < 0 || l >= c->L || c->n_experts <= 0 || c->n_experts_per_tok <= 0 ||
+        !c->w_gate_inp || !c->w_gate_exps || !c->w_up_exps || !c->w_down_exps) {
+        set_error(MLQ_ERR_ARG, "moe_ffn: bad arguments or no MoE in the model");
+        return MLQ_ERR_ARG;
+    }
+    const int N = c->N, E = c->n_experts, k = c->n_experts_per_tok, M = c->moe_intermediate;
+    const long long gs = expert_stride(c->gate_exp_quant, M, N, false);
+    const long long us = expert_stride(c->up_exp_quant, M, N, false);
+    const long long ds = expert_stride(c->down_exp_quant, N, M, true);
+    if (!gs || !us || !ds) { set_error(MLQ_ERR_TYPE, "moe_ffn: expert types"); return MLQ_ERR_TYPE; }
+    CallScope cs;
+    const float *router = (const float *)cs.weights(c->w_gate_inp[l], sizeof(float) * (size_t)E * N);
+    const uint8_t *gexp = (const uint8_t *)cs.weights(c->w_gate_exps[l], expert_extent(gs, E, c->gate_exp_quant, M, N));
+    const uint8_t *uexp = (const uint8_t *)cs.weights(c->w_up_exps[l], expert_extent(us, E, c->up_exp_quant, M, N));
+    const uint8_t *dexp = (const uint8_t *)cs.weights(c->w_down_exps[l], expert_extent(ds, E, c->down_exp_quant, N, M));
+    const float *dx = (const float *)cs.in(x, sizeof(float) * (size_t)B * N);
+    float *logits = (float *)cs.scratch(sizeof(float) * (size_t)B * E);
+    int *idx = (int *)cs.scratch(sizeof(int) * (size_t)B * k);
+    float *w = (float *)cs.scratch(sizeof(float) * (size_t)B * k);
+    float *hm = (float *)cs.scratch(sizeof(float) * (size_t)B * k * M);
+    float *dout = (float *)cs.out(ffn, sizeof(float) * (size_t)B * N);
+    if (cs.failed) return cs.finish();
+    cudaStream_t s = stream();
+    int rc = launch_matmul((const uint8_t *)router, MLQ_F32, dx, logits, E, N, B, 0, s);
+    if (rc == MLQ_OK) rc = launch_router_topk(logits, B, E, k, 0, idx, w, s);
+    if (rc == MLQ_OK)
+        rc = launch_moe_indexed(0, c->gate_exp_quant, gexp, uexp, gs, idx, w, k, B, M, N, dx, hm, nullptr, s,
+                                HUGE_VALF);
+    if (rc == MLQ_OK) rc = launch_moe_indexed(1, c->down_exp_quant, dexp, nullptr, ds, idx, w, k, B, N, M, hm, dout, nullptr, s);
+    if (rc != MLQ_OK) return fwd_fail(cs, rc);
+    return cs.finish();
+}
+
+}  // extern "C"

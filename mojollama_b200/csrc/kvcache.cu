@@ -11,11 +11,24 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <map>
+#include <mutex>
+
 #include "mlq_internal.h"
 
 namespace mlq {
 constexpr int kMaxBlocks = 1024;   // MAX_BLOCKS, cengine_batch_instr.c:23
 constexpr int kBlockSize = 64;     // BLOCK_SIZE, cengine_batch_instr.c:22
+
+// sizes of the k/v arrays kv_init allocated, so a kernel writing them can check its extent
+static std::mutex g_kv_mu;
+static std::map<const void *, size_t> g_kv_arrays;
+
+size_t kv_array_bytes(const void *p) {
+    std::lock_guard<std::mutex> lk(g_kv_mu);
+    auto it = g_kv_arrays.find(p);
+    return it == g_kv_arrays.end() ? 0 : it->second;
+}
 }  // namespace mlq
 
 using namespace mlq;
@@ -88,6 +101,11 @@ int mlq_kv_init(MlqKVBlock *kv, int L, int nkh, int hd) {
     cudaMemset(v, 0, sz);
     kv->k = (float *)k;
     kv->v = (float *)v;
+    {
+        std::lock_guard<std::mutex> lk(g_kv_mu);
+        g_kv_arrays[k] = sz;
+        g_kv_arrays[v] = sz;
+    }
     kv->n_blocks = 0;
     memset(kv->block_map, -1, sizeof(kv->block_map));
     memset(kv->seq_len, 0, sizeof(kv->seq_len));
@@ -98,6 +116,11 @@ int mlq_kv_alloc(MlqKVBlock *kv) { return kv ? mlq_page_table_alloc(&kv->pt) : -
 
 void mlq_kv_free(MlqKVBlock *kv) {
     if (!kv) return;
+    {
+        std::lock_guard<std::mutex> lk(g_kv_mu);
+        g_kv_arrays.erase(kv->k);
+        g_kv_arrays.erase(kv->v);
+    }
     if (kv->k) cudaFree(kv->k);
     if (kv->v) cudaFree(kv->v);
     kv->k = kv->v = nullptr;

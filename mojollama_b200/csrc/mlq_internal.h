@@ -101,6 +101,31 @@ int launch_rope_init(float *cos_t, float *sin_t, int max_ctx, int hd, int rope_d
 int launch_rope_neox(float *buf, int rows, int rows_stride, int nh, int hd, const int *pos_dev, int pos_host,
                      const float *cos_t, const float *sin_t, int rope_dim, cudaStream_t s);
 
+// attention.cu: fp32 KV cache addressing
+struct KVView {
+    const float *k, *v;      // base of the K and V regions
+    const int *table;        // [B][max_pages] physical page of each logical page, or null
+    int table_stride;        // ints between sequences' tables
+    long long page_stride;   // floats between pages
+    int page_size;           // slots per page
+    int row_stride;          // floats between slots (NKH * HD)
+    // optional per-sequence page pools (one KVBlock per sequence): pool_seq[b] holds
+    // [n_layers][n_pages][page_size][row] K then the same for V; K of layer `layer`
+    // starts at layer * layer_stride, V at (n_layers + layer) * layer_stride
+    float *const *pool_seq;
+    long long layer_stride;
+    int layer, n_layers;
+};
+
+int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
+                       int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
+                       float *scratch, size_t scratch_bytes, cudaStream_t s);
+int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
+                    const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s);
+size_t attn_scratch_bytes(int B, int nh, int hd);
+// bytes of a KVBlock k or v array allocated by kv_init of this library (0 if unknown)
+size_t kv_array_bytes(const void *p);
+
 // ssm.cu
 int launch_ssm_decode_step(const float *x, float *interm, const float *conv_w, const float *a_param,
                            const float *dt_bias, const float *alpha, const float *beta, float *state, int B, int N,
@@ -110,6 +135,9 @@ int launch_mul(float *a, const float *b, long long n, cudaStream_t s);
 // moe.cu: mode 0 = SwiGLU pairs, 1 = weighted sum, 2 = store
 int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt, int G, int n_rows, int K,
                     const float *x, int nx, float *out, const float *residual, cudaStream_t s);
+int launch_moe_indexed(int mode, int qt, const uint8_t *base_a, const uint8_t *base_b, long long expert_stride,
+                       const int *d_idx, const float *d_w, int top_k, int n_tok, int n_rows, int K, const float *x,
+                       float *out, const float *residual, cudaStream_t s, float swiglu_clamp = 80.0f);
 int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s);
 
 }  // namespace mlq

@@ -48,7 +48,30 @@ struct MoeArgs {
     float *out;
     const float *residual;
     int *status;
+    // indexed mode (routing stays on the device): matrix g is expert e = idx[g / per] of
+    // the expert tensor base[g % per] (stride estride bytes per expert), weight w[g];
+    // per = 2 for SwiGLU (gate, up), 1 otherwise.  Token t = blockIdx.y reads idx/w at
+    // t * G / per, x at t * x_tok, writes out at t * out_tok, residual at t * out_tok.
+    int indexed;
+    const int *idx;
+    const float *w;
+    const uint8_t *base[2];
+    long long estride;
+    long long x_tok, out_tok;
+    float clamp;   // SwiGLU gate clamp (+-80 for moe_forward_omp; infinity for moe_ffn)
 };
+
+__device__ __forceinline__ const uint8_t *moe_mat(const MoeArgs &a, int g) {
+    if (!a.indexed) return a.W[g];
+    const int per = (a.G > 0 && a.base[1]) ? 2 : 1;
+    const int e = a.idx[(size_t)blockIdx.y * (a.G / per) + g / per];
+    if (e < 0) return nullptr;
+    return a.base[g % per] + (size_t)e * a.estride;
+}
+
+__device__ __forceinline__ float moe_wgt(const MoeArgs &a, int g) {
+    return a.indexed ? a.w[(size_t)blockIdx.y * a.G + g] : a.wgt[g];
+}
 
 struct MoeLayout {
     int off_bar, off_flag, off_xh, off_xl, off_xs, off_xsum, off_res, off_stage, total;
@@ -112,8 +135,10 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
             const long long b0 = tile * tile_bytes, b1 = min(b0 + tile_bytes, total);
             uint32_t tx = 0;
             for (int g = 0; g < a.G; g++) {
-                const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b0;
-                const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b1;
+                const uint8_t *Wg = moe_mat(a, g);
+                if (!Wg) continue;
+                const uintptr_t g0 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)b0;
+                const uintptr_t g1 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)b1;
                 const uintptr_t gd = g0 & ~uintptr_t(15);
                 const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15), i1 = g1 & ~uintptr_t(15);
                 uint8_t *st = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes;
@@ -130,8 +155,10 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
                 if (tx) {
                     mbar_arrive_expect_tx(&full[s], tx);
                     for (int g = 0; g < a.G; g++) {
-                        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b0;
-                        const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)b1;
+                        const uint8_t *Wg = moe_mat(a, g);
+                        if (!Wg) continue;
+                        const uintptr_t g0 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)b0;
+                        const uintptr_t g1 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)b1;
                         const uintptr_t gd = g0 & ~uintptr_t(15);
                         const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15), i1 = g1 & ~uintptr_t(15);
                         if (i1 > i0) {
@@ -153,9 +180,12 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
     float *xs = reinterpret_cast<float *>(smem + L.off_xs);
     float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
     float *res = reinterpret_cast<float *>(smem + L.off_res);
+    const float *xt = a.x + (size_t)blockIdx.y * a.x_tok;
     for (int m = 0; m < a.nx; m++)
-        encode_x_planes<1>(a.x + (size_t)m * a.K, 1, a.K, xh + (size_t)m * a.K, xl + (size_t)m * a.K,
+        encode_x_planes<1>(xt + (size_t)m * a.K, 1, a.K, xh + (size_t)m * a.K, xl + (size_t)m * a.K,
                            xs + (size_t)m * (a.K / 32), xsum + (size_t)m * (a.K / 32), warp, lane, kMoeWarps);
+    float *out = a.out + (size_t)blockIdx.y * a.out_tok;
+    const float *residual = a.residual ? a.residual + (size_t)blockIdx.y * a.out_tok : nullptr;
     named_bar_sync(1, kMoeWarps * 32);
     const int U = a.K / Fmt<QT>::UE;
     const int items = a.G * a.rpt;
@@ -173,11 +203,12 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
         for (int i = warp; i < items; i += kMoeWarps) {
             const int g = i / a.rpt, r = i - g * a.rpt;
             float acc[1] = {0.0f};
-            if (ok && row0 + r < a.n_rows) {
+            const uint8_t *Wg = moe_mat(a, g);
+            if (ok && Wg && row0 + r < a.n_rows) {
                 const int xr = (a.nx == 1) ? 0 : g;
                 const XPlanes xp{xh + (size_t)xr * a.K, xl + (size_t)xr * a.K, xs + (size_t)xr * (a.K / 32),
                                  xsum + (size_t)xr * (a.K / 32), a.K};
-                const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W[g]) + (uintptr_t)(tile * tile_bytes);
+                const uintptr_t g0 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)(tile * tile_bytes);
                 const uint8_t *rowp = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes +
                                       (g0 & 15) + (size_t)r * a.row_bytes;
                 for (int u = lane; u < U; u += 32) Unit<QT, 1>::dot(rowp, u, xp, acc);
@@ -195,29 +226,29 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
             for (int t = threadIdx.x; t < pairs * a.rpt; t += kMoeWarps * 32) {
                 const int e = t / a.rpt, r = t - e * a.rpt;
                 if (row0 + r < a.n_rows) {
-                    float gv = fminf(fmaxf(rs[(2 * e) * a.rpt + r], -80.0f), 80.0f);
-                    a.out[(size_t)e * a.n_rows + row0 + r] = (gv / (1.0f + expf(-gv))) * rs[(2 * e + 1) * a.rpt + r];
+                    float gv = fminf(fmaxf(rs[(2 * e) * a.rpt + r], -a.clamp), a.clamp);
+                    out[(size_t)e * a.n_rows + row0 + r] = (gv / (1.0f + expf(-gv))) * rs[(2 * e + 1) * a.rpt + r];
                 }
             }
         } else if (MODE == MOE_WSUM) {
             for (int r = threadIdx.x; r < a.rpt; r += kMoeWarps * 32) {
                 if (row0 + r < a.n_rows) {
-                    float sum = a.residual ? a.residual[row0 + r] : 0.0f;
-                    for (int g = 0; g < a.G; g++) sum = fmaf(a.wgt[g], rs[g * a.rpt + r], sum);
-                    a.out[row0 + r] = sum;
+                    float sum = residual ? residual[row0 + r] : 0.0f;
+                    for (int g = 0; g < a.G; g++) sum = fmaf(moe_wgt(a, g), rs[g * a.rpt + r], sum);
+                    out[row0 + r] = sum;
                 }
             }
         } else {
             for (int t = threadIdx.x; t < items; t += kMoeWarps * 32) {
                 const int g = t / a.rpt, r = t - g * a.rpt;
-                if (row0 + r < a.n_rows) a.out[(size_t)g * a.n_rows + row0 + r] = rs[t];
+                if (row0 + r < a.n_rows) out[(size_t)g * a.n_rows + row0 + r] = rs[t];
             }
         }
     }
 }
 
 template <int QT, int MODE>
-static int launch_moe_t(MoeArgs &a, cudaStream_t s) {
+static int launch_moe_t(MoeArgs &a, int n_tok, cudaStream_t s) {
     const LaunchEnv *env = launch_env();
     if (!env) return MLQ_ERR_NO_DEVICE;
     const long long rb = a.row_bytes;
@@ -243,24 +274,29 @@ static int launch_moe_t(MoeArgs &a, cudaStream_t s) {
             return MLQ_ERR_CUDA;
         attr = true;
     }
-    const int grid = a.n_tiles < env->num_sms ? a.n_tiles : env->num_sms;
-    k_moe_gemv<QT, MODE><<<grid, kMoeThreads, smem, s>>>(a);
+    int gx = a.n_tiles < env->num_sms ? a.n_tiles : env->num_sms;
+    if (n_tok > 1) {
+        gx = (env->num_sms + n_tok - 1) / n_tok;
+        if (gx > a.n_tiles) gx = a.n_tiles;
+        if (gx < 1) gx = 1;
+    }
+    k_moe_gemv<QT, MODE><<<dim3(gx, n_tok), kMoeThreads, smem, s>>>(a);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 template <int MODE>
-static int launch_moe_mode(int qt, MoeArgs &a, cudaStream_t s) {
+static int launch_moe_mode(int qt, MoeArgs &a, int n_tok, cudaStream_t s) {
     switch (qt) {
-        case MLQ_Q4_0: return launch_moe_t<MLQ_Q4_0, MODE>(a, s);
-        case MLQ_Q4_1: return launch_moe_t<MLQ_Q4_1, MODE>(a, s);
-        case MLQ_Q5_0: return launch_moe_t<MLQ_Q5_0, MODE>(a, s);
-        case MLQ_Q8_0: return launch_moe_t<MLQ_Q8_0, MODE>(a, s);
-        case MLQ_Q4_K: return launch_moe_t<MLQ_Q4_K, MODE>(a, s);
-        case MLQ_Q5_K: return launch_moe_t<MLQ_Q5_K, MODE>(a, s);
-        case MLQ_Q6_K: return launch_moe_t<MLQ_Q6_K, MODE>(a, s);
-        case MLQ_MXFP4: return launch_moe_t<MLQ_MXFP4, MODE>(a, s);
-        case MLQ_MXFP4_REF: return launch_moe_t<MLQ_MXFP4_REF, MODE>(a, s);
+        case MLQ_Q4_0: return launch_moe_t<MLQ_Q4_0, MODE>(a, n_tok, s);
+        case MLQ_Q4_1: return launch_moe_t<MLQ_Q4_1, MODE>(a, n_tok, s);
+        case MLQ_Q5_0: return launch_moe_t<MLQ_Q5_0, MODE>(a, n_tok, s);
+        case MLQ_Q8_0: return launch_moe_t<MLQ_Q8_0, MODE>(a, n_tok, s);
+        case MLQ_Q4_K: return launch_moe_t<MLQ_Q4_K, MODE>(a, n_tok, s);
+        case MLQ_Q5_K: return launch_moe_t<MLQ_Q5_K, MODE>(a, n_tok, s);
+        case MLQ_Q6_K: return launch_moe_t<MLQ_Q6_K, MODE>(a, n_tok, s);
+        case MLQ_MXFP4: return launch_moe_t<MLQ_MXFP4, MODE>(a, n_tok, s);
+        case MLQ_MXFP4_REF: return launch_moe_t<MLQ_MXFP4_REF, MODE>(a, n_tok, s);
         default:
             set_error(MLQ_ERR_TYPE, "moe: expert type %d not supported on the grouped path", qt);
             return MLQ_ERR_TYPE;
@@ -276,6 +312,7 @@ int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt,
     }
     if (ref_compat() && qt == MLQ_MXFP4) qt = MLQ_MXFP4_REF;
     MoeArgs a{};
+    a.clamp = 80.0f;
     for (int g = 0; g < G; g++) {
         a.W[g] = W[g];
         a.wgt[g] = wgt ? wgt[g] : 0.0f;
@@ -288,9 +325,49 @@ int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt,
     a.nx = nx;
     a.out = out;
     a.residual = residual;
-    if (mode == MOE_SWIGLU) return launch_moe_mode<MOE_SWIGLU>(qt, a, s);
-    if (mode == MOE_WSUM) return launch_moe_mode<MOE_WSUM>(qt, a, s);
-    return launch_moe_mode<MOE_STORE>(qt, a, s);
+    if (mode == MOE_SWIGLU) return launch_moe_mode<MOE_SWIGLU>(qt, a, 1, s);
+    if (mode == MOE_WSUM) return launch_moe_mode<MOE_WSUM>(qt, a, 1, s);
+    return launch_moe_mode<MOE_STORE>(qt, a, 1, s);
+}
+
+// Routing on the device: n_tok tokens, top_k experts each from d_idx / d_w [n_tok][top_k].
+// SwiGLU: experts' gate (base_a) and up (base_b) n_ff x K, x [n_tok][K] -> h [n_tok][top_k][n_ff].
+// Weighted sum: experts' down (base_a) N x n_ff, h [n_tok][top_k][n_ff] -> out [n_tok][N]
+// (+ residual [n_tok][N]).
+int launch_moe_indexed(int mode, int qt, const uint8_t *base_a, const uint8_t *base_b, long long expert_stride,
+                       const int *d_idx, const float *d_w, int top_k, int n_tok, int n_rows, int K, const float *x,
+                       float *out, const float *residual, cudaStream_t s, float swiglu_clamp) {
+    const int G = (mode == MOE_SWIGLU) ? 2 * top_k : top_k;
+    if (G < 1 || G > kMoeMaxG || n_tok < 1 || n_tok > 65535) {
+        set_error(MLQ_ERR_ARG, "moe: top_k %d / tokens %d out of range", top_k, n_tok);
+        return MLQ_ERR_ARG;
+    }
+    if (ref_compat() && qt == MLQ_MXFP4) qt = MLQ_MXFP4_REF;
+    MoeArgs a{};
+    a.G = G;
+    a.n_rows = n_rows;
+    a.K = K;
+    a.row_bytes = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    a.indexed = 1;
+    a.clamp = swiglu_clamp;
+    a.idx = d_idx;
+    a.w = d_w;
+    a.base[0] = base_a;
+    a.base[1] = (mode == MOE_SWIGLU) ? base_b : nullptr;
+    a.estride = expert_stride;
+    a.x = x;
+    a.residual = residual;
+    a.out = out;
+    if (mode == MOE_SWIGLU) {
+        a.nx = 1;
+        a.x_tok = K;
+        a.out_tok = (long long)top_k * n_rows;
+        return launch_moe_mode<MOE_SWIGLU>(qt, a, n_tok, s);
+    }
+    a.nx = top_k;
+    a.x_tok = (long long)top_k * K;
+    a.out_tok = n_rows;
+    return launch_moe_mode<MOE_WSUM>(qt, a, n_tok, s);
 }
 
 // ------------------------------------------------------------------------------ router

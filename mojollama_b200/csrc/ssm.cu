@@ -8,7 +8,8 @@
 //   dt  = softplus(dt_bias[g] + sum_j alpha[g][j] * x_b[j % N])   (softplus = x above 20)
 //   state[g][s] = exp(a[g] * dt) * state[g][s] + (s == 0 ? dt * sum_j beta[g][j] * x_b[j % N] : 0)
 // The state never feeds the output.  These are the reference's semantics, kept for the
-// drop-in (SURVEY.md F10 describes why they are not a Mamba-2 step); one launch computes
+// drop-in (only the first conv tap is used, the state is shared by the batch and is never
+// read back, so this is not a Mamba-2 step); one launch computes
 // the gated intermediate, one the state update (a thread per (group, state) element
 // walking the B updates in order, so the result is deterministic).
 // ssm_layer_fused: out_b = residual_b + W_out . ((W_gate . x_b) * interm_b).

@@ -57,6 +57,12 @@ def _bind_engine(so: ctypes.CDLL) -> None:
     so.moe_forward_omp.argtypes = [ctypes.POINTER(cu), ctypes.POINTER(cu), ctypes.POINTER(cu), cf, ci, ci, ci, ci, ci,
                                    ctypes.POINTER(ctypes.c_int), cf, ci, cf, cf, cu]
     so.moe_forward_omp.restype = None
+    # turbo_engine_v7_moe.py:396-410 (BC and KVBlock are passed by pointer)
+    vp = ctypes.c_void_p
+    so.batch_forward.argtypes = [vp, vp, ci, vp]
+    so.batch_forward.restype = None
+    so.moe_ffn.argtypes = [vp, ci, vp, vp, vp, vp, ci]
+    so.moe_ffn.restype = None
 
 
 def load_kernels() -> Kernels:

@@ -203,9 +203,10 @@ def silu_clamped(g):
     return g / (1 + np.exp(-g))
 
 
-def moe_forward(gate, up, down, qts, x, n_ff, n_embd, idx, w):
+def moe_forward(gate, up, down, qts, x, n_ff, n_embd, idx, w, clamp=True):
     """moe_forward_omp (quant_kernels_omp.c:2066-2250) where it is W.x: for each selected
     expert e = idx[i]: h = silu(clamp(gate_e x, +-80)) * (up_e x); combined += w[i] * down_e h.
+    clamp=False: the batch engine's moe_ffn (cengine_batch_instr.c:648-663), no clamp.
     gate/up/down: dict expert -> raw bytes; fp64 accumulation."""
     qg, qu, qd = qts
     x = np.asarray(x, np.float64)
@@ -213,7 +214,7 @@ def moe_forward(gate, up, down, qts, x, n_ff, n_embd, idx, w):
     for i, e in enumerate(idx):
         g = gemv(gate[e], qg, x, n_ff, n_embd)[0].astype(np.float64)
         u = gemv(up[e], qu, x, n_ff, n_embd)[0].astype(np.float64)
-        h = silu_clamped(g) * u
+        h = (silu_clamped(g) if clamp else g / (1 + np.exp(-g))) * u
         out += float(w[i]) * gemv(down[e], qd, h, n_embd, n_ff)[0].astype(np.float64)
     return out.astype(np.float32)
 

@@ -70,6 +70,13 @@ class RefEngine:
                                                                   _cf, _cf, _cu]
         so.ssm_decode_step.argtypes = [_cf] * 9 + [_ci] * 7
         so.rope_init.argtypes = [_cf, _cf, _ci, _ci, _ci]
+        # cengine_batch_instr.c:1233, 208, 591 (struct pointers passed as void*)
+        so.batch_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _ci, ctypes.c_void_p]
+        so.batch_forward.restype = None
+        so.kv_init.argtypes = [ctypes.c_void_p, _ci, _ci, _ci]
+        so.kv_init.restype = None
+        so.moe_ffn.argtypes = [ctypes.c_void_p, _ci] + [ctypes.c_void_p] * 4 + [_ci]
+        so.moe_ffn.restype = None
         so.set_num_threads.argtypes = [_ci]
         so.get_max_threads.restype = _ci
         so.silu.argtypes = [_cf, _ci]

@@ -27,3 +27,13 @@ def test_struct_sizes_match_reference_mirror():
     assert lib.mlq_sizeof_page_table() == ctypes.sizeof(PageTable)
     assert lib.mlq_sizeof_kv_block() == ctypes.sizeof(KVBlock)
     assert KVBlock.pt.offset == ctypes.sizeof(KVBlock) - ctypes.sizeof(PageTable)
+
+
+def test_bc_struct_matches_package_mirror():
+    """BC (cengine_batch_instr.c:536-589) as the library compiles it has the size of the
+    package's ctypes mirror, which lists the reference's fields in order."""
+    from mojollama_b200.bc import BC, KVBlock as PkgKV
+    lib = core()
+    assert lib.mlq_sizeof_bc() == ctypes.sizeof(BC)
+    assert ctypes.sizeof(PkgKV) == ctypes.sizeof(KVBlock)
+    assert BC.kv_array.offset < BC.logits.offset < BC.n_experts.offset

@@ -1,0 +1,55 @@
+"""CPU pin of the whole-model oracle (oracle/model.py) against the reference's own
+batch_forward (cengine_batch_instr.c:1233-1493, built from its sources into oracle/_ref).
+
+The reference projects its workspace's never-written xn region; the oracle's
+compatibility mode follows that data flow, so the two must agree on every step's logits,
+final hidden state (left in ws[0:B*N]), SSM state and sequence lengths.  The oracle's
+default mode differs from it only in which buffer feeds the projections."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from mojollama_b200.bc import BCBuilder, KVBlock
+from oracle import model as OM
+from oracle import ops as O
+from oracle import ref as R
+
+from model_fixture import fill_bc, make_model, ws_stride
+
+pytestmark = pytest.mark.skipif(not R.available(), reason="reference build (oracle/_ref) not present")
+
+
+@pytest.mark.parametrize("kind,kw,B,steps", [
+    ("dense", dict(attn_modes=["sep", "qk", "sep"]), 2, 3),
+    ("hybrid", {}, 3, 2),
+    ("qkv8192", {}, 2, 2),
+], ids=["dense", "hybrid_ssm_moe", "fused_qkv"])
+def test_oracle_compat_step_matches_reference_build(kind, kw, B, steps):
+    ref = R.RefEngine()
+    m = make_model(kind, seed=21, **kw)
+    L, V, N = m["L"], m["V"], m["N"]
+    kvrow = m["NKH"] * m["HD"]
+    S = ws_stride(m, B)
+    kvs = [KVBlock() for _ in range(B)]
+    for kv in kvs:
+        ref.so.kv_init(ctypes.byref(kv), L, m["NKH"], m["HD"])
+    logits = np.zeros(B * V, np.float32)
+    ssm = np.zeros(L * OM.SSM_GROUPS * OM.SSM_STATE, np.float32)
+    work = np.zeros(m["max_ctx"] * kvrow * 2 + 4096, np.float32)
+    b = BCBuilder()
+    fill_bc(m, b, kvs, logits, ssm_state=ssm, workspace=work)
+    st = OM.new_state(m, B)
+    rng = np.random.default_rng(22)
+    xn = (rng.standard_normal((B, N)) * 0.7).astype(np.float32)
+    for step in range(steps):
+        toks = rng.integers(0, V, B).astype(np.int32)
+        ws = np.zeros(12 * B * S, np.float32)
+        ws[B * S:B * S + B * N] = xn.reshape(-1)
+        ref.so.batch_forward(ctypes.byref(b.bc), toks.ctypes.data, B, ws.ctypes.data)
+        want, h = OM.forward_step(m, st, list(range(B)), toks, compat_xn=xn)
+        assert O.rel_l2(logits.reshape(B, V), want) < 1e-5
+        assert O.rel_l2(ws[:B * N].reshape(B, N), h) < 1e-5
+        if m["moe"]:
+            assert O.rel_l2(ssm, st["ssm"].reshape(-1)) < 1e-5
+        assert all(kv.seq_len[0] == step + 1 for kv in kvs)
