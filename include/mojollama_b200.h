@@ -170,6 +170,42 @@ void mlq_forget_model_plans(void);
 /* sizeof(BC) as this library compiles it (layout check for ctypes mirrors) */
 size_t mlq_sizeof_bc(void);
 
+/* ---- qwen36_batch_forward (cengine_batch_instr.c:859-899): the reference's 76 arguments,
+   field for field and in order, packed into one struct; the reference-named 76-argument
+   function in mojollama_b200_ref_abi.h fills it.  Semantics in csrc/qwen36.cu. */
+typedef struct {
+    int B, L, N, NH, n_kv_h, HD, FF;
+    int n_experts, top_k, n_ff_expert;
+    float eps;
+    int rope_dim, max_ctx, ssm_inner, ssm_groups, ssm_state_size, ssm_conv_kernel, ssm_dt_rank;
+    const float *emb;
+    int emb_quant;
+    const int *layer_types;
+    const int *tokens;
+    float *logits;
+    const float **attn_norm_w, **ffn_norm_w;
+    const uint8_t **attn_qkv_raw; const int *qkv_nr, *qkv_nc, *qkv_qt;
+    const uint8_t **attn_gate_raw; const int *gate_nr, *gate_nc, *gate_qt;
+    const uint8_t **ssm_out_raw; const int *ssm_out_nr, *ssm_out_nc, *ssm_out_qt;
+    const uint8_t **attn_out_raw; const int *out_nr, *out_nc, *out_qt;
+    uint8_t **gate_exp_raw; const int *gate_exp_qt;
+    uint8_t **up_exp_raw; const int *up_exp_qt;
+    uint8_t **down_exp_raw; const int *down_exp_qt;
+    const float **shexp_gate_raw, **shexp_up_raw, **shexp_down_raw;
+    const float **shexp_router;
+    const int *shexp_int;
+    const uint8_t **moe_router_raw; const int *moe_router_qt;
+    const int *shexp_gate_qt, *shexp_up_qt, *shexp_down_qt;
+    const float *out_norm_w;
+    const uint8_t *out_w; int out_nr_final, out_nc_final, out_qt_final;
+    const float **ssm_conv1d, **ssm_a, **ssm_dt_bias, **ssm_alpha, **ssm_beta, **ssm_norm;
+    float *ssm_state;
+    float *kv_k, *kv_v; int *kv_lens;
+    const float *cos_table, *sin_table;
+    float *ws; uint8_t *q8_ws;
+} MlqQwen36Args;
+int mlq_qwen36_batch_forward(const MlqQwen36Args *args);
+
 /* ---- decode attention (one query per sequence), fp32 KV ---- */
 /* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);
    head h uses KV head h / (n_head / n_kv_head); window > 0 attends the last `window`

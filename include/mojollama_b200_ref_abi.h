@@ -168,6 +168,23 @@ void ssm_layer_fused(const float *x, float *residual, float *output, const float
 /* cengine_batch_instr.c:1233 (computing the intended forward: see mojollama_b200.h) and :591 */
 void batch_forward(const BC *c, const int *tokens, int B, float *ws);
 void moe_ffn(const BC *c, int l, float *x, float *gate_buf, float *up_buf, float *ffn_buf, int B);
+/* cengine_batch_instr.c:859-899 (the argument list of MlqQwen36Args, in order) */
+void qwen36_batch_forward(
+    int B, int L, int N, int NH, int n_kv_h, int HD, int FF, int n_experts, int top_k, int n_ff_expert, float eps,
+    int rope_dim, int max_ctx, int ssm_inner, int ssm_groups, int ssm_state_size, int ssm_conv_kernel,
+    int ssm_dt_rank, const float *emb, int emb_quant, const int *layer_types, const int *tokens, float *logits,
+    const float **attn_norm_w, const float **ffn_norm_w, const uint8_t **attn_qkv_raw, const int *qkv_nr,
+    const int *qkv_nc, const int *qkv_qt, const uint8_t **attn_gate_raw, const int *gate_nr, const int *gate_nc,
+    const int *gate_qt, const uint8_t **ssm_out_raw, const int *ssm_out_nr, const int *ssm_out_nc,
+    const int *ssm_out_qt, const uint8_t **attn_out_raw, const int *out_nr, const int *out_nc, const int *out_qt,
+    uint8_t **gate_exp_raw, const int *gate_exp_qt, uint8_t **up_exp_raw, const int *up_exp_qt,
+    uint8_t **down_exp_raw, const int *down_exp_qt, const float **shexp_gate_raw, const float **shexp_up_raw,
+    const float **shexp_down_raw, const float **shexp_router, const int *shexp_int, const uint8_t **moe_router_raw,
+    const int *moe_router_qt, const int *shexp_gate_qt, const int *shexp_up_qt, const int *shexp_down_qt,
+    const float *out_norm_w, const uint8_t *out_w, int out_nr_final, int out_nc_final, int out_qt_final,
+    const float **ssm_conv1d, const float **ssm_a, const float **ssm_dt_bias, const float **ssm_alpha,
+    const float **ssm_beta, const float **ssm_norm, float *ssm_state, float *kv_k, float *kv_v, int *kv_lens,
+    const float *cos_table, const float *sin_table, float *ws, uint8_t *q8_ws);
 /* cengine_batch_instr.c:141 -- static in the reference, exported here */
 void gqa(float *o, const float *q, const float *kc, const float *vc, int sl, int nh, int nkh, int hd);
 

@@ -153,3 +153,38 @@ void moe_ffn(const BC *c, int l, float *x, float *gate_buf, float *up_buf, float
     (void)up_buf;
     mlq_moe_ffn(c, l, x, ffn_buf, B);
 }
+
+/* cengine_batch_instr.c:859: the 76 arguments, in order, into MlqQwen36Args */
+void qwen36_batch_forward(
+    int B, int L, int N, int NH, int n_kv_h, int HD, int FF, int n_experts, int top_k, int n_ff_expert, float eps,
+    int rope_dim, int max_ctx, int ssm_inner, int ssm_groups, int ssm_state_size, int ssm_conv_kernel,
+    int ssm_dt_rank, const float *emb, int emb_quant, const int *layer_types, const int *tokens, float *logits,
+    const float **attn_norm_w, const float **ffn_norm_w, const uint8_t **attn_qkv_raw, const int *qkv_nr,
+    const int *qkv_nc, const int *qkv_qt, const uint8_t **attn_gate_raw, const int *gate_nr, const int *gate_nc,
+    const int *gate_qt, const uint8_t **ssm_out_raw, const int *ssm_out_nr, const int *ssm_out_nc,
+    const int *ssm_out_qt, const uint8_t **attn_out_raw, const int *out_nr, const int *out_nc, const int *out_qt,
+    uint8_t **gate_exp_raw, const int *gate_exp_qt, uint8_t **up_exp_raw, const int *up_exp_qt,
+    uint8_t **down_exp_raw, const int *down_exp_qt, const float **shexp_gate_raw, const float **shexp_up_raw,
+    const float **shexp_down_raw, const float **shexp_router, const int *shexp_int, const uint8_t **moe_router_raw,
+    const int *moe_router_qt, const int *shexp_gate_qt, const int *shexp_up_qt, const int *shexp_down_qt,
+    const float *out_norm_w, const uint8_t *out_w, int out_nr_final, int out_nc_final, int out_qt_final,
+    const float **ssm_conv1d, const float **ssm_a, const float **ssm_dt_bias, const float **ssm_alpha,
+    const float **ssm_beta, const float **ssm_norm, float *ssm_state, float *kv_k, float *kv_v, int *kv_lens,
+    const float *cos_table, const float *sin_table, float *ws, uint8_t *q8_ws) {
+    MlqQwen36Args a = {
+        B, L, N, NH, n_kv_h, HD, FF, n_experts, top_k, n_ff_expert, eps,
+        rope_dim, max_ctx, ssm_inner, ssm_groups, ssm_state_size, ssm_conv_kernel, ssm_dt_rank,
+        emb, emb_quant, layer_types, tokens, logits,
+        attn_norm_w, ffn_norm_w,
+        attn_qkv_raw, qkv_nr, qkv_nc, qkv_qt,
+        attn_gate_raw, gate_nr, gate_nc, gate_qt,
+        ssm_out_raw, ssm_out_nr, ssm_out_nc, ssm_out_qt,
+        attn_out_raw, out_nr, out_nc, out_qt,
+        gate_exp_raw, gate_exp_qt, up_exp_raw, up_exp_qt, down_exp_raw, down_exp_qt,
+        shexp_gate_raw, shexp_up_raw, shexp_down_raw, shexp_router, shexp_int,
+        moe_router_raw, moe_router_qt, shexp_gate_qt, shexp_up_qt, shexp_down_qt,
+        out_norm_w, out_w, out_nr_final, out_nc_final, out_qt_final,
+        ssm_conv1d, ssm_a, ssm_dt_bias, ssm_alpha, ssm_beta, ssm_norm, ssm_state,
+        kv_k, kv_v, kv_lens, cos_table, sin_table, ws, q8_ws};
+    mlq_qwen36_batch_forward(&a);
+}

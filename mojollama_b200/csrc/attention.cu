@@ -86,6 +86,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
         // stage K and V rows of this tile (coalesced along HD)
         for (int i = tid; i < nt * HD; i += blockDim.x) {
             const int t = i / HD, d = i - t * HD;
+            if (kv.tail_k && base + t == sl - 1) {
+                const size_t o = (size_t)b * kv.tail_stride + (size_t)g * HD + d;
+                ks[t * (HD + 1) + d] = kv.tail_k[o];
+                vs[t * HD + d] = kv.tail_v[o];
+                continue;
+            }
             const long long off = kv_offset(kv, b, base + t) + (long long)g * HD + d;
             ks[t * (HD + 1) + d] = kb[off];
             vs[t * HD + d] = vb[off];

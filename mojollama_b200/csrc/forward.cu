@@ -36,15 +36,6 @@
 namespace mlq {
 
 // ------------------------------------------------------------------------------ kernels
-__global__ void k_embed_f32(const float *__restrict__ emb, const int *__restrict__ tokens, float *__restrict__ x,
-                            int N, int V) {
-    const int b = blockIdx.y;
-    int t = tokens[b];
-    if (t < 0 || t >= V) t = 0;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x)
-        x[(size_t)b * N + i] = emb[(size_t)t * N + i];
-}
-
 // dst[b][0:n] = src[b*src_stride + off : +n]
 __global__ void k_copy_cols(float *__restrict__ dst, const float *__restrict__ src, int n, int src_stride, int off) {
     const int b = blockIdx.y;
@@ -334,7 +325,7 @@ static bool build_plan(const BC *c, CallScope &cs, ModelPlan &P) {
         if (cs.failed) return false;
     }
     const int rope_dim = c->rope_dim > 0 ? c->rope_dim : HD;
-    P.emb = c->emb_quant == 0 ? Fv(cs, c->emb, (size_t)c->V * N) : (const float *)W(cs, c->emb, c->emb_quant, c->V, N);
+    P.emb = (const float *)cs.weights(c->emb, embed_bytes(c->emb_quant, N, c->V));
     P.onw = Fv(cs, c->onw, N);
     P.wout = W(cs, c->wOut, c->outQuant, c->outNR, c->outNC);
     P.cos_t = Fv(cs, c->cos_table, (size_t)c->max_ctx * (rope_dim / 2));
@@ -490,6 +481,7 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
     int *e_idx = (int *)cs.scratch(sizeof(int) * (size_t)B * (topk > 0 ? topk : 1));
     float *e_w = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1));
     float *hm = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1) * (M > 0 ? M : 1));
+    float *hm2 = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1) * (M > 0 ? M : 1));
     float *score = (float *)cs.scratch(sizeof(float) * B);
     const size_t attn_sb = attn_scratch_bytes(B, NH, HD);
     float *attn_scr = (float *)cs.scratch(attn_sb);
@@ -521,16 +513,10 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
         if (rc == MLQ_OK) rc = (expr);              \
     } while (0)
     // ------------------------------------------------------------------ embedding
-    if (c->emb_quant == 0) {
-        k_embed_f32<<<dim3(grid1(N) > 16 ? 16 : grid1(N), B), 256, 0, s>>>(P->emb, d_tok, x, N, c->V);
-        count_launch();
-    } else {
-        const size_t rb = mlq_row_bytes(c->emb_quant, N);
-        for (int b = 0; b < B; b++) {
-            int t = tokens[b];
-            if (t < 0 || t >= c->V) t = 0;
-            MLQ_TRY(launch_dequantize((const uint8_t *)P->emb + rb * (size_t)t, c->emb_quant, x + (size_t)b * N, N, s));
-        }
+    {
+        std::vector<int> th;
+        if (!host_tokens(tokens, B, th)) rc = MLQ_ERR_CUDA;
+        MLQ_TRY(launch_embed(P->emb, c->emb_quant, d_tok, th.data(), x, B, N, c->V, s));
     }
     const int ps = kv0->pt.page_size;
     const long long layer_stride = (long long)kv0->pt.n_pages * ps * kvrow;
@@ -605,10 +591,9 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
             const int E = c->n_experts;
             MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, logits_e, E, N, B, 0, s));
             MLQ_TRY(launch_router_topk(logits_e, B, E, topk, 0, e_idx, e_w, s));
-            MLQ_TRY(launch_moe_indexed(0, c->gate_exp_quant, lp.gexp, lp.uexp, lp.gstride, e_idx, e_w, topk, B, M, N,
-                                       pin, hm, nullptr, s, inf));
-            MLQ_TRY(launch_moe_indexed(1, c->down_exp_quant, lp.dexp, nullptr, lp.dstride, e_idx, e_w, topk, B, N, M,
-                                       hm, x, res, s));
+            MLQ_TRY(launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
+                                       lp.dexp, lp.gstride, lp.ustride, lp.dstride, e_idx, e_w, topk, B, M, N, pin,
+                                       hm, hm2, x, res, inf, s));
             if (lp.shg && lp.shrouter) {
                 k_dot_rows<<<B, 256, 0, s>>>(pin, lp.shrouter, score, N);
                 count_launch();
@@ -669,15 +654,15 @@ int mlq_moe_ffn(const void *bc, int l, const float *x, float *ffn, int B) {
     int *idx = (int *)cs.scratch(sizeof(int) * (size_t)B * k);
     float *w = (float *)cs.scratch(sizeof(float) * (size_t)B * k);
     float *hm = (float *)cs.scratch(sizeof(float) * (size_t)B * k * M);
+    float *hm2 = (float *)cs.scratch(sizeof(float) * (size_t)B * k * M);
     float *dout = (float *)cs.out(ffn, sizeof(float) * (size_t)B * N);
     if (cs.failed) return cs.finish();
     cudaStream_t s = stream();
     int rc = launch_matmul((const uint8_t *)router, MLQ_F32, dx, logits, E, N, B, 0, s);
     if (rc == MLQ_OK) rc = launch_router_topk(logits, B, E, k, 0, idx, w, s);
     if (rc == MLQ_OK)
-        rc = launch_moe_indexed(0, c->gate_exp_quant, gexp, uexp, gs, idx, w, k, B, M, N, dx, hm, nullptr, s,
-                                HUGE_VALF);
-    if (rc == MLQ_OK) rc = launch_moe_indexed(1, c->down_exp_quant, dexp, nullptr, ds, idx, w, k, B, N, M, hm, dout, nullptr, s);
+        rc = launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, gexp, uexp, dexp, gs, us, ds,
+                                idx, w, k, B, M, N, dx, hm, hm2, dout, nullptr, HUGE_VALF, s);
     if (rc != MLQ_OK) return fwd_fail(cs, rc);
     return cs.finish();
 }

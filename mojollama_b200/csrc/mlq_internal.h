@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <vector>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -115,6 +116,10 @@ struct KVView {
     float *const *pool_seq;
     long long layer_stride;
     int layer, n_layers;
+    // optional own rows: position seq_len-1 of sequence b is read from tail_k/tail_v
+    // [B][tail_stride] instead of the cache (sequences that share one cache slot)
+    const float *tail_k = nullptr, *tail_v = nullptr;
+    int tail_stride = 0;
 };
 
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
@@ -138,6 +143,16 @@ int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt,
 int launch_moe_indexed(int mode, int qt, const uint8_t *base_a, const uint8_t *base_b, long long expert_stride,
                        const int *d_idx, const float *d_w, int top_k, int n_tok, int n_rows, int K, const float *x,
                        float *out, const float *residual, cudaStream_t s, float swiglu_clamp = 80.0f);
+int launch_moe_experts(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
+                       long long gs, long long us, long long ds, const int *idx, const float *w, int top_k,
+                       int n_tok, int n_ff, int N, const float *x, float *h, float *h2, float *out,
+                       const float *residual, float clamp, cudaStream_t s);
+// batch-engine embedding rows (qwen36.cu)
+int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_tok, float *x, int B, int N, int V,
+                 cudaStream_t s);
+size_t embed_bytes(int emb_quant, int N, int V);
+bool host_tokens(const int *tokens, int B, std::vector<int> &out);
+void forget_kv_mirrors();
 int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s);
 
 }  // namespace mlq

@@ -332,6 +332,7 @@ int launch_moe_gemv(int mode, int qt, const uint8_t *const *W, const float *wgt,
 
 // Routing on the device: n_tok tokens, top_k experts each from d_idx / d_w [n_tok][top_k].
 // SwiGLU: experts' gate (base_a) and up (base_b) n_ff x K, x [n_tok][K] -> h [n_tok][top_k][n_ff].
+// Store: experts' matrices (base_a) n_rows x K, x [n_tok][K] -> out [n_tok][top_k][n_rows].
 // Weighted sum: experts' down (base_a) N x n_ff, h [n_tok][top_k][n_ff] -> out [n_tok][N]
 // (+ residual [n_tok][N]).
 int launch_moe_indexed(int mode, int qt, const uint8_t *base_a, const uint8_t *base_b, long long expert_stride,
@@ -358,16 +359,56 @@ int launch_moe_indexed(int mode, int qt, const uint8_t *base_a, const uint8_t *b
     a.x = x;
     a.residual = residual;
     a.out = out;
-    if (mode == MOE_SWIGLU) {
+    if (mode == MOE_SWIGLU || mode == MOE_STORE) {
         a.nx = 1;
         a.x_tok = K;
         a.out_tok = (long long)top_k * n_rows;
-        return launch_moe_mode<MOE_SWIGLU>(qt, a, n_tok, s);
+        return mode == MOE_SWIGLU ? launch_moe_mode<MOE_SWIGLU>(qt, a, n_tok, s)
+                                  : launch_moe_mode<MOE_STORE>(qt, a, n_tok, s);
     }
     a.nx = top_k;
     a.x_tok = (long long)top_k * K;
     a.out_tok = n_rows;
     return launch_moe_mode<MOE_WSUM>(qt, a, n_tok, s);
+}
+
+__global__ void k_swiglu_clamp(float *__restrict__ h, const float *__restrict__ g, const float *__restrict__ u,
+                               long long n, float clamp) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float gv = fminf(fmaxf(g[i], -clamp), clamp);
+        h[i] = (gv / (1.0f + expf(-gv))) * u[i];
+    }
+}
+
+// Routed experts of n_tok tokens with the routing on the device:
+//   h_t,i = silu(clamp(gate_e x_t)) * (up_e x_t)  for e = idx[t][i], i < top_k
+//   out_t = residual_t + sum_i w[t][i] * down_e h_t,i       (fixed order i = 0..top_k-1)
+// Gate and up of one type and stride share one launch (fused SwiGLU epilogue); otherwise
+// each is stored ([n_tok][top_k][n_ff] in h and h2) and combined elementwise.  out may
+// alias residual.
+int launch_moe_experts(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
+                       long long gs, long long us, long long ds, const int *idx, const float *w, int top_k,
+                       int n_tok, int n_ff, int N, const float *x, float *h, float *h2, float *out,
+                       const float *residual, float clamp, cudaStream_t s) {
+    int rc;
+    if (gqt == uqt && gs == us) {
+        rc = launch_moe_indexed(MOE_SWIGLU, gqt, gexp, uexp, gs, idx, w, top_k, n_tok, n_ff, N, x, h, nullptr, s,
+                                clamp);
+    } else {
+        rc = launch_moe_indexed(MOE_STORE, gqt, gexp, nullptr, gs, idx, w, top_k, n_tok, n_ff, N, x, h, nullptr, s);
+        if (rc == MLQ_OK)
+            rc = launch_moe_indexed(MOE_STORE, uqt, uexp, nullptr, us, idx, w, top_k, n_tok, n_ff, N, x, h2, nullptr,
+                                    s);
+        if (rc == MLQ_OK) {
+            const long long n = (long long)n_tok * top_k * n_ff;
+            long long g = (n + 255) / 256;
+            k_swiglu_clamp<<<(int)(g > 4096 ? 4096 : g), 256, 0, s>>>(h, h, h2, n, clamp);
+            count_launch();
+            rc = MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+        }
+    }
+    if (rc != MLQ_OK) return rc;
+    return launch_moe_indexed(MOE_WSUM, dqt, dexp, nullptr, ds, idx, w, top_k, n_tok, N, n_ff, h, out, residual, s);
 }
 
 // ------------------------------------------------------------------------------ router

@@ -470,6 +470,7 @@ int mlq_cache_clear(void) {
     Ctx *c = ctx();
     if (!c) return mlq_last_error();
     mlq_forget_model_plans();
+    forget_kv_mirrors();
     cudaStreamSynchronize(c->stream);
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto &kv : g_cache[c->device]) cudaFree(kv.second.dev);

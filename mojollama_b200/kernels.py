@@ -63,6 +63,10 @@ def _bind_engine(so: ctypes.CDLL) -> None:
     so.batch_forward.restype = None
     so.moe_ffn.argtypes = [vp, ci, vp, vp, vp, vp, ci]
     so.moe_ffn.restype = None
+    # turbo_engine_v7_moe.py:273-311 (cengine_batch_instr.c:859-899, 76 arguments)
+    so.qwen36_batch_forward.argtypes = ([ci] * 10 + [ctypes.c_float] + [ci] * 7 + [vp, ci] + [vp] * 39 + [ci] * 3 +
+                                        [vp] * 14)
+    so.qwen36_batch_forward.restype = None
 
 
 def load_kernels() -> Kernels:

@@ -127,3 +127,77 @@ def forward_step(model, state, seqs, tokens, compat_xn=None):
             x = res
     h, _ = O.rms_norm(x, model["onw"], eps, sanitize=True)           # :1469-1489
     return _mv(model["wout"], h, model["V"], N), h
+
+
+# ------------------------------------------------------------------ qwen36_batch_forward
+def qwen36_new_state(model):
+    L, n_kv = model["L"], model["NKH"] * model["HD"]
+    return {"kv_k": np.zeros((L, model["max_ctx"], n_kv), np.float32),
+            "kv_v": np.zeros((L, model["max_ctx"], n_kv), np.float32),
+            "kv_lens": np.zeros(L, np.int32),
+            "ssm": np.zeros((L, model["ssm_groups"], model["ssm_state"]), np.float32)}
+
+
+def qwen36_step(model, state, tokens):
+    """One qwen36_batch_forward call (cengine_batch_instr.c:859-1231) for tokens [B].
+
+    x stays the residual (the norm clamps only its own output, :996-1002); attention layers
+    read Q at 0, K at NH*HD and V half-way through the non-Q part of the projection; every
+    token writes its K/V to slot kv_lens[l] of the shared flat cache (the last token's row
+    stays) and attends over slots 0..pos-1 plus its own row (:1055-1079); MoE: router,
+    softmax, insertion top-k, renormalised weights (:1113-1152), moe_forward_omp with the
+    +-80 SiLU clamp (:1169), shared expert silu(clamp(gate)) * up scaled by its positive
+    router score (:1178-1207); final norm and logits (:1222-1227).  kv_lens is not advanced
+    (the caller does that).  Returns (logits [B][V], x before the final norm [B][N])."""
+    L, N, NH, NKH, HD = model["L"], model["N"], model["NH"], model["NKH"], model["HD"]
+    inner, n_kv = NH * HD, NKH * HD
+    eps = model["eps"]
+    rope_dim = model.get("rope_dim") or HD
+    B = len(tokens)
+    x = np.stack([model["emb"][t] for t in tokens]).astype(np.float32)
+    for l in range(L):
+        ly = model["layers"][l]
+        xn, _ = O.rms_norm(x, ly["an"], eps, sanitize=True)
+        if ly["type"] == "ssm":
+            IN = model["ssm_inner"]
+            interm, st = O.ssm_decode_step(xn, ly["conv"], ly["a"], ly["dt_bias"], ly["alpha"], ly["beta"],
+                                           state["ssm"][l], B, N, IN, model["ssm_groups"], model["ssm_state"],
+                                           model["ssm_dt_rank"])
+            state["ssm"][l] = st
+            att = (interm.astype(np.float64) * _mv(ly["attn_gate"], xn, IN, N)).astype(np.float32)
+            x = (x + _mv(ly["ssm_out"], att, N, IN)).astype(np.float32)
+        else:
+            nq = ly["qkv_rows"]
+            qkv = _mv(ly["qkv"], xn, nq, N)
+            voff = inner + (nq - inner) // 2
+            pos = int(state["kv_lens"][l])
+            att = np.zeros((B, inner), np.float32)
+            for b in range(B):
+                qb = O.rope_neox(qkv[b, :inner], NH, HD, pos, model["cos"], model["sin"], rope_dim)
+                kb = O.rope_neox(qkv[b, inner:inner + n_kv], NKH, HD, pos, model["cos"], model["sin"], rope_dim)
+                vb = qkv[b, voff:voff + n_kv]
+                ks = np.concatenate([state["kv_k"][l, :pos], kb[None]])
+                vs = np.concatenate([state["kv_v"][l, :pos], vb[None]])
+                att[b] = O.gqa_decode(qb, ks, vs, NH, NKH, HD)
+                state["kv_k"][l, pos], state["kv_v"][l, pos] = kb, vb
+            x = (x + _mv(ly["o"], att, N, inner)).astype(np.float32)
+        xn, _ = O.rms_norm(x, ly["fn"], eps, sanitize=True)
+        moe = model.get("moe")
+        if moe and ly.get("router") is not None:
+            ffn = np.zeros((B, N))
+            for b in range(B):
+                lg = ly["router"].astype(np.float64) @ xn[b].astype(np.float64)
+                idx, w = O.router_topk(lg, moe["k"], renorm=True)
+                ffn[b] = O.moe_forward(ly["gate_exps"], ly["up_exps"], ly["down_exps"],
+                                       (moe["gq"], moe["uq"], moe["dq"]), xn[b], moe["M"], N, idx, w, clamp=True)
+                sh = ly.get("shexp")
+                if sh:
+                    score = float(xn[b].astype(np.float64) @ sh["router"].astype(np.float64))
+                    if score > 0:
+                        si = sh["si"]
+                        g = _mv(sh["g"], xn[b], si, N)[0].astype(np.float64)
+                        u = _mv(sh["u"], xn[b], si, N)[0].astype(np.float64)
+                        ffn[b] += score * _mv(sh["d"], O.silu_clamped(g) * u, N, si)[0]
+            x = (x + ffn).astype(np.float32)
+    h, _ = O.rms_norm(x, model["onw"], eps, sanitize=True)
+    return _mv(model["wout"], h, model["V"], N), x

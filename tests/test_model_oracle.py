@@ -53,3 +53,38 @@ def test_oracle_compat_step_matches_reference_build(kind, kw, B, steps):
         if m["moe"]:
             assert O.rel_l2(ssm, st["ssm"].reshape(-1)) < 1e-5
         assert all(kv.seq_len[0] == step + 1 for kv in kvs)
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_oracle_qwen36_step_matches_reference_build(B):
+    """qwen36_batch_forward (cengine_batch_instr.c:859-1231) on a 3 SSM + 1 attention layer
+    MoE model whose fused QKV uses the layout the reference's split reads (N-wide K and V
+    sections), Q4_0 experts (which moe_forward_omp computes exactly), three steps with the
+    caller advancing kv_lens as the reference's Python does (turbo_engine_v7_moe.py:1889)."""
+    from model_fixture import Qwen36Call, make_qwen36_model
+    ref = R.RefEngine()
+    m = make_qwen36_model(seed=31, qkv_layout="ref")
+    L, N, V = m["L"], m["N"], m["V"]
+    n_kv = m["NKH"] * m["HD"]
+    kv_k = np.zeros((L, m["max_ctx"], n_kv), np.float32)
+    kv_v = np.zeros_like(kv_k)
+    kv_lens = np.zeros(L, np.int32)
+    ssm = np.zeros(L * 32 * 128, np.float32)
+    call = Qwen36Call(m, kv_k, kv_v, kv_lens, ssm)
+    st = OM.qwen36_new_state(m)
+    rng = np.random.default_rng(32)
+    for step in range(3):
+        toks = rng.integers(0, V, B).astype(np.int32)
+        logits = np.zeros(B * V, np.float32)
+        wsn, S = call.ws_size(B)
+        ws = np.zeros(wsn, np.float32)
+        q8 = np.zeros(64 * 1024, np.uint8)
+        call(ref.so.qwen36_batch_forward, toks, logits, ws, q8)
+        want, x = OM.qwen36_step(m, st, toks)
+        assert O.rel_l2(logits.reshape(B, V), want) < 1e-5
+        assert O.rel_l2(ws[:B * N].reshape(B, N), x) < 1e-5
+        assert O.rel_l2(ssm, st["ssm"].reshape(-1)) < 1e-5
+        assert O.rel_l2(kv_k[:, :step + 1], st["kv_k"][:, :step + 1]) < 1e-5
+        assert O.rel_l2(kv_v[:, :step + 1], st["kv_v"][:, :step + 1]) < 1e-5
+        kv_lens += 1
+        st["kv_lens"] += 1

@@ -1,0 +1,140 @@
+"""qwen36_batch_forward (cengine_batch_instr.c:859-1231) on the GPU, through the
+reference-named 76-argument entry of combined_engine.so.
+
+Default mode against the numpy oracle (oracle/model.py qwen36_step, itself pinned against
+the reference build on CPU); reference-compatibility mode against the reference build on
+the same arguments.  KV caches as host arrays (device mirror + write-back) and as device
+memory.  Bar: relative L2 <= TOL on logits, the workspace's hidden state, the SSM state
+and the KV rows."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from mojollama_b200.kernels import load_kernels
+from oracle import model as OM
+from oracle import ops as O
+from oracle import ref as R
+
+from model_fixture import Qwen36Call, make_qwen36_model
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _state(m):
+    L, n_kv = m["L"], m["NKH"] * m["HD"]
+    return (np.zeros((L, m["max_ctx"], n_kv), np.float32), np.zeros((L, m["max_ctx"], n_kv), np.float32),
+            np.zeros(L, np.int32), np.zeros(L * 32 * 128, np.float32))
+
+
+def _step(call, fn, m, B, toks):
+    logits = np.zeros(B * m["V"], np.float32)
+    wsn, _ = call.ws_size(B)
+    ws = np.zeros(wsn, np.float32)
+    call(fn, toks, logits, ws, np.zeros(64 * 1024, np.uint8))
+    return logits.reshape(B, m["V"]), ws[:B * m["N"]].reshape(B, m["N"]), ws
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_qwen36_host_kv_matches_oracle(cuda_device, B):
+    k = load_kernels()
+    m = make_qwen36_model(seed=41, qkv_layout="std")
+    kv_k, kv_v, kv_lens, ssm = _state(m)
+    call = Qwen36Call(m, kv_k, kv_v, kv_lens, ssm)
+    st = OM.qwen36_new_state(m)
+    rng = np.random.default_rng(42)
+    for step in range(4):
+        toks = rng.integers(0, m["V"], B).astype(np.int32)
+        got, x, _ = _step(call, k.cengine.qwen36_batch_forward, m, B, toks)
+        want, xw = OM.qwen36_step(m, st, toks)
+        assert O.rel_l2(got, want) < TOL, (step, O.rel_l2(got, want))
+        assert O.rel_l2(x, xw) < TOL
+        assert O.rel_l2(ssm, st["ssm"].reshape(-1)) < TOL
+        # the new rows were written back into the host cache
+        assert O.rel_l2(kv_k[:, :step + 1], st["kv_k"][:, :step + 1]) < TOL
+        assert O.rel_l2(kv_v[:, :step + 1], st["kv_v"][:, :step + 1]) < TOL
+        kv_lens += 1
+        st["kv_lens"] += 1
+
+
+def test_qwen36_host_kv_external_rows_and_rewind(cuda_device):
+    """Rows the caller wrote into the host cache itself are picked up, and a rewound cache
+    holding a different conversation is re-read rather than served from the mirror."""
+    k = load_kernels()
+    m = make_qwen36_model(seed=43, qkv_layout="std")
+    kv_k, kv_v, kv_lens, ssm = _state(m)
+    call = Qwen36Call(m, kv_k, kv_v, kv_lens, ssm)
+    rng = np.random.default_rng(44)
+    fn = k.cengine.qwen36_batch_forward
+    for conv in range(2):
+        # the oracle fills three positions of the host cache (a prefill done elsewhere)
+        st = OM.qwen36_new_state(m)
+        for p in range(3):
+            OM.qwen36_step(m, st, rng.integers(0, m["V"], 1).astype(np.int32))
+            st["kv_lens"] += 1
+        kv_k[:], kv_v[:], kv_lens[:] = st["kv_k"], st["kv_v"], st["kv_lens"]
+        ssm[:] = st["ssm"].reshape(-1)
+        for step in range(2):
+            toks = rng.integers(0, m["V"], 2).astype(np.int32)
+            got, _, _ = _step(call, fn, m, 2, toks)
+            want, _ = OM.qwen36_step(m, st, toks)
+            assert O.rel_l2(got, want) < TOL, (conv, step)
+            kv_lens += 1
+            st["kv_lens"] += 1
+
+
+def test_qwen36_device_kv_matches_oracle(cuda_device):
+    import torch
+    k = load_kernels()
+    m = make_qwen36_model(seed=45, qkv_layout="std")
+    _, _, kv_lens, ssm = _state(m)
+    L, n_kv = m["L"], m["NKH"] * m["HD"]
+    dk = torch.zeros((L, m["max_ctx"], n_kv), dtype=torch.float32, device="cuda")
+    dv = torch.zeros_like(dk)
+    call = Qwen36Call(m, dk.data_ptr(), dv.data_ptr(), kv_lens, ssm)
+    st = OM.qwen36_new_state(m)
+    rng = np.random.default_rng(46)
+    for step in range(3):
+        toks = rng.integers(0, m["V"], 2).astype(np.int32)
+        got, _, _ = _step(call, k.cengine.qwen36_batch_forward, m, 2, toks)
+        want, _ = OM.qwen36_step(m, st, toks)
+        assert O.rel_l2(got, want) < TOL
+        torch.cuda.synchronize()
+        assert O.rel_l2(dk[:, :step + 1].cpu().numpy(), st["kv_k"][:, :step + 1]) < TOL
+        kv_lens += 1
+        st["kv_lens"] += 1
+
+
+needs_ref = pytest.mark.skipif(not R.available(), reason="reference build (oracle/_ref) not present")
+
+
+@needs_ref
+@pytest.mark.parametrize("layout", ["ref", "std"])
+def test_qwen36_ref_compat_matches_reference_build(cuda_device, layout):
+    """'ref': the projection holds N-wide K/V sections (both read V at NH*HD + N).
+    'std': Q|K|V with n_kv-wide sections -- the reference reads V past the projection, from
+    its workspace; compatibility mode reads the same workspace bytes."""
+    lib = cuda_device
+    k = load_kernels()
+    ref = R.RefEngine()
+    m = make_qwen36_model(seed=47, qkv_layout=layout)
+    ours = _state(m)
+    theirs = _state(m)
+    c_ours = Qwen36Call(m, *ours)
+    c_ref = Qwen36Call(m, *theirs)
+    rng = np.random.default_rng(48)
+    assert lib.mlq_set_ref_compat(1) == 0
+    try:
+        for step in range(3):
+            toks = rng.integers(0, m["V"], 2).astype(np.int32)
+            got, x, _ = _step(c_ours, k.cengine.qwen36_batch_forward, m, 2, toks)
+            want, xr, _ = _step(c_ref, ref.so.qwen36_batch_forward, m, 2, toks)
+            assert O.rel_l2(got, want) < TOL, (layout, step, O.rel_l2(got, want))
+            assert O.rel_l2(x, xr) < TOL
+            assert O.rel_l2(ours[3], theirs[3]) < TOL
+            assert O.rel_l2(ours[0][:, :step + 1], theirs[0][:, :step + 1]) < TOL
+            for s in (ours, theirs):
+                s[2][:] += 1
+    finally:
+        lib.mlq_set_ref_compat(0)
