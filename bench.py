@@ -332,8 +332,336 @@ def run_ours(args, rank, world, local_rank):
     line["per_format_gbs"] = per
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
+    if not args.no_decode:
+        line["decode"] = run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
+                                    cpu_seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
     return 0
+
+
+def run_decode_profile(args):
+    """Small case for an ncu launch list of decode steps: the config-1 model, B = 4,
+    `--profile-steps` batch_forward calls at positions 0.. (weights ~1.1 GB in HBM)."""
+    import torch
+    from mojollama_b200 import core
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    b, keep, caches = build_tinyllama(torch, lib, 64)
+    d_logits = torch.empty(TL["B"] * TL["V"], device="cuda")
+    d_tok = torch.zeros(TL["B"], dtype=torch.int32, device="cuda")
+    b.bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+    l0 = lib.mlq_launch_count()
+    for _ in range(args.profile_steps):
+        rc = lib.mlq_batch_forward(ctypes.byref(b.bc), ctypes.c_void_p(d_tok.data_ptr()), TL["B"], None)
+        assert rc == 0, lib.mlq_last_error_message()
+    stream.synchronize()
+    print(json.dumps({"decode_profile_steps": args.profile_steps,
+                      "launches_per_step": (lib.mlq_launch_count() - l0) // args.profile_steps}))
+    for kv in caches:
+        kv.free()
+    return 0
+
+
+SWEEP_SHAPES = [(2048, 2048), (5632, 2048), (2880, 2880), (151936, 2048)]
+SWEEP_M = [1, 4, 16, 64, 256]
+
+
+def run_sweep(args):
+    """BASELINE config 2 in full: every format x shape x M, device-resident, CUDA events,
+    weights rotated over enough distinct copies that each launch reads from HBM (the set
+    of copies is > 2x L2).  Prints one JSON object with GB/s (algorithmic bytes) and
+    TFLOP/s (2*M*N*K) per case."""
+    import torch
+    from mojollama_b200 import core
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    from mojollama_b200 import gguf_quant as Q
+    ms = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else SWEEP_M
+    out = {"metric": "config-2 sweep: GB/s = (N*row_bytes + M*K*4 + M*N*4)/t, TFLOP/s = 2*M*N*K/t", "cases": []}
+    for name, qt in FORMATS:
+        be, bb = BLOCK[qt]
+        for (n, k) in SWEEP_SHAPES:
+            if k % be:
+                continue
+            rb = k // be * bb
+            rng = np.random.default_rng(qt * 7 + n)
+            distinct = min(n, 1024)
+            base = Q.quantize(qt, (rng.standard_normal(distinct * k) * 0.02).astype(np.float32))
+            w1 = np.tile(base, -(-n // distinct))[: n * rb]
+            mat = n * rb
+            copies = max(1, min(64, int(2 * 126e6 // mat) + 1))
+            dev = torch.from_numpy(np.ascontiguousarray(np.tile(w1, copies))).cuda()
+            for m in ms:
+                x = torch.randn(m * k, device="cuda")
+                o = torch.empty(m * n, device="cuda")
+
+                def launch(i):
+                    rc = lib.mlq_matmul(ctypes.c_void_p(dev.data_ptr() + (i % copies) * mat), qt,
+                                        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(o.data_ptr()), n, k, m)
+                    if rc:
+                        raise RuntimeError(lib.mlq_last_error_message())
+
+                for i in range(3):
+                    launch(i)
+                reps = max(5, min(50, int(2e9 // max(mat, 1))))
+                a, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for i in range(reps):
+                    launch(i)
+                b2.record(stream)
+                stream.synchronize()
+                t = a.elapsed_time(b2) / reps / 1e3
+                byts = mat + m * k * 4 + m * n * 4
+                out["cases"].append({"fmt": name, "N": n, "K": k, "M": m, "us": round(t * 1e6, 2),
+                                     "gbs": round(byts / t / 1e9, 1), "tflops": round(2 * m * n * k / t / 1e12, 2)})
+            del dev
+            torch.cuda.empty_cache()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_decode_only(args):
+    import torch
+    from mojollama_b200 import core
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    print(json.dumps({"decode": run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
+                                           cpu_seconds=args.cpu_seconds)}), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ model decode
+# BASELINE config 1: TinyLlama-1.1B architecture, Q8_0 weights N(0, 0.02) from seed 0,
+# norms 1.0, B = 4 sequences, 16 prompt tokens each uniform in [0, 32000) from seed 0, then
+# 32 greedy tokens -- one batch_forward call per position (the batch engine's decode step).
+TL = dict(L=22, N=2048, NH=32, NKH=4, HD=64, FF=5632, V=32000, eps=1e-5, B=4, prompt=16, gen=32)
+
+
+def tinyllama_step_bytes(pos):
+    """Algorithmic HBM bytes of one decode step at position pos (0-based) for B sequences:
+    every weight once (Q8_0, 34 B per 32) + the embedding rows + K/V rows read and written."""
+    c = TL
+    N, FF, kv = c["N"], c["FF"], c["NKH"] * c["HD"]
+    per_layer = (N * N * 2 + kv * N * 2 + FF * N * 3) // 32 * 34 + 2 * N * 4
+    weights = c["L"] * per_layer + c["V"] * N // 32 * 34 + N * 4
+    kv_bytes = c["B"] * c["L"] * 2 * kv * 4 * (pos + 2)
+    act = c["B"] * (N * 4 + c["V"] * 4)
+    return weights + kv_bytes + act
+
+
+def build_tinyllama(torch, lib, max_ctx):
+    """Random-init TinyLlama-shape model in HBM (Q8_0 by this library's quantizer) behind a
+    BC; returns (builder, device tensors, host copies for the reference, kv caches)."""
+    from mojollama_b200 import bc as BCm
+    c = TL
+    L, N, NH, NKH, HD, FF, V = c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["FF"], c["V"]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    keep = []
+
+    def q8(rows, cols):
+        w = torch.randn(rows * cols, generator=g, device="cuda") * 0.02
+        q = torch.empty(rows * cols // 32 * 34, dtype=torch.uint8, device="cuda")
+        rc = lib.mlq_quantize_q8_0(ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(q.data_ptr()), rows * cols)
+        assert rc == 0, lib.mlq_last_error_message()
+        keep.append(q)
+        return q.data_ptr()
+
+    b = BCm.BCBuilder()
+    bc = b.bc
+    bc.L, bc.N, bc.NH, bc.NKH, bc.HD, bc.FF, bc.V, bc.eps, bc.nc = L, N, NH, NKH, HD, FF, V, c["eps"], N
+    names = [("wQ", N, N), ("wK", NKH * HD, N), ("wV", NKH * HD, N), ("wO", N, N), ("wG", FF, N), ("wU", FF, N),
+             ("wD", N, FF)]
+    ptrs = {nm: [] for nm, _, _ in names}
+    for l in range(L):
+        for nm, r, k in names:
+            ptrs[nm].append(q8(r, k))
+    for nm, r, k in names:
+        b.layers(nm, ptrs[nm])
+    for f, v in (("nQ", N), ("nK", NKH * HD), ("nV", NKH * HD), ("nO", N), ("nG", FF), ("nU", FF), ("nD", N)):
+        b.ints(f, [v] * L)
+    for f in ("q_quant", "k_quant", "v_quant", "o_quant", "g_quant", "u_quant", "d_quant"):
+        b.ints(f, [8] * L)
+    ones = torch.ones(N, device="cuda")
+    keep.append(ones)
+    b.layers("wAN", [ones.data_ptr()] * L)
+    b.layers("wFN", [ones.data_ptr()] * L)
+    emb = torch.randn(V * N, generator=g, device="cuda") * 0.02
+    keep.append(emb)
+    bc.emb = emb.data_ptr()
+    bc.onw = ones.data_ptr()
+    bc.wOut = q8(V, N)
+    bc.outNR, bc.outNC, bc.outQuant, bc.emb_quant = V, N, 8, 0
+    hd2 = HD // 2
+    j = np.arange(hd2)
+    theta = np.arange(max_ctx)[:, None] / np.power(10000.0, 2.0 * j / HD)
+    cos_t, sin_t = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    b.ptr("cos_table", cos_t)
+    b.ptr("sin_table", sin_t)
+    bc.max_ctx, bc.rope_dim = max_ctx, HD
+    caches = [BCm.KVCache(L, NKH, HD) for _ in range(c["B"])]
+    b.kv_array([kv.block for kv in caches])
+    torch.cuda.synchronize()
+    return b, keep, caches
+
+
+def run_decode(torch, lib, stream, with_cpu=True, cpu_seconds=10.0):
+    """Config 1 through batch_forward: device-resident (logits and tokens in HBM, greedy
+    argmax on the device) and end to end (host tokens and logits, the reference's usage)."""
+    c = TL
+    B, V, N, P, G = c["B"], c["V"], c["N"], c["prompt"], c["gen"]
+    max_ctx = 64
+    b, keep, caches = build_tinyllama(torch, lib, max_ctx)
+    rng = np.random.default_rng(0)
+    prompts = rng.integers(0, V, (B, P)).astype(np.int32)
+    d_logits = torch.empty(B * V, device="cuda")
+    d_tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    d_prompts = torch.from_numpy(np.ascontiguousarray(prompts.T)).cuda()
+    bc = b.bc
+
+    def reset():
+        for kv in caches:
+            lib.mlq_kv_free(ctypes.byref(kv.block))
+            assert lib.mlq_kv_init(ctypes.byref(kv.block), c["L"], c["NKH"], c["HD"]) == 0
+        b.kv_array([kv.block for kv in caches])
+
+    def fwd():
+        rc = lib.mlq_batch_forward(ctypes.byref(bc), ctypes.c_void_p(d_tok.data_ptr()), B, None)
+        if rc:
+            raise RuntimeError(lib.mlq_last_error_message())
+
+    def generate(ev=None):
+        """prompt positions then greedy positions, all on the device; ev: per-phase events"""
+        bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        with torch.cuda.stream(stream):
+            if ev:
+                ev[0].record(stream)
+            for t in range(P):
+                d_tok.copy_(d_prompts[t])
+                fwd()
+            if ev:
+                ev[1].record(stream)
+            for t in range(G):
+                d_tok.copy_(torch.argmax(d_logits.view(B, V), dim=1).to(torch.int32))
+                fwd()
+            if ev:
+                ev[2].record(stream)
+
+    generate()            # warm-up (plan, residency, graphs of nothing)
+    stream.synchronize()
+    reset()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    l0 = lib.mlq_launch_count()
+    generate(evs)
+    stream.synchronize()
+    launches = (lib.mlq_launch_count() - l0) // (P + G)
+    pre_ms, dec_ms = evs[0].elapsed_time(evs[1]), evs[1].elapsed_time(evs[2])
+    greedy_dev = torch.argmax(d_logits.view(B, V), dim=1).cpu().numpy()
+
+    # end to end: host tokens, host logits, host argmax (the reference Python's loop)
+    reset()
+    h_logits = np.zeros(B * V, np.float32)
+    bc.logits = h_logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    from mojollama_b200.kernels import load_kernels
+    ce = load_kernels().cengine
+    ws = np.zeros(B * N, np.float32)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for t in range(P):
+        tok = np.ascontiguousarray(prompts[:, t])
+        ce.batch_forward(ctypes.byref(bc), tok.ctypes.data, B, ws.ctypes.data)
+    t1 = time.perf_counter()
+    for t in range(G):
+        tok = np.argmax(h_logits.reshape(B, V), axis=1).astype(np.int32)
+        ce.batch_forward(ctypes.byref(bc), tok.ctypes.data, B, ws.ctypes.data)
+    t2 = time.perf_counter()
+    assert lib.mlq_last_error() == 0, lib.mlq_last_error_message()
+    greedy_host = np.argmax(h_logits.reshape(B, V), axis=1)
+    step_bytes = sum(tinyllama_step_bytes(P + t) for t in range(G)) / G
+    out = {
+        "workload": "TinyLlama-1.1B shape, Q8_0, B=4 x (16 prompt + 32 greedy) through batch_forward (config 1)",
+        "tok_s": round(B * G / (dec_ms / 1e3), 1), "ms_per_step": round(dec_ms / G, 3),
+        "prefill_tok_s": round(B * P / (pre_ms / 1e3), 1),
+        "e2e_tok_s": round(B * G / (t2 - t1), 1), "e2e_ms_per_step": round((t2 - t1) * 1e3 / G, 3),
+        "e2e_io": {"h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * V * 4 + B * N * 4},
+        "launches_per_step": int(launches),
+        "greedy_tokens_agree": bool(np.array_equal(greedy_dev, greedy_host)),
+        "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                     "achieved_gbs": round(step_bytes / (dec_ms / G / 1e3) / 1e9, 1)},
+    }
+    if with_cpu:
+        out["cpu_baseline"] = decode_cpu_baseline(keep, b, caches, cpu_seconds)
+    for kv in caches:
+        kv.free()
+    return out
+
+
+def decode_cpu_baseline(keep, b, caches, seconds):
+    """The reference C batch_forward (oracle/_ref) on the host cores with host copies of
+    the same weights, B = 4, one token per sequence per call; a bounded number of steps."""
+    try:
+        from oracle import ref as R
+        from mojollama_b200 import bc as BCm
+        if not R.available():
+            return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+        import torch
+        eng = R.RefEngine()
+        threads = os.cpu_count() or 1
+        eng.set_num_threads(threads)
+        c = TL
+        src = b.bc
+        hb = BCm.BCBuilder()
+        hc = hb.bc
+        for name, _ in BCm.BC._fields_:
+            setattr(hc, name, getattr(src, name))
+        host = {}
+
+        def to_host(ptr, nbytes):
+            if ptr not in host:
+                t = torch.empty(nbytes, dtype=torch.uint8)
+                src_t = next(k for k in keep if k.data_ptr() <= ptr < k.data_ptr() + k.numel() * k.element_size())
+                off = ptr - src_t.data_ptr()
+                t.copy_(src_t.view(torch.uint8)[off:off + nbytes].cpu())
+                host[ptr] = t
+            return host[ptr].data_ptr()
+
+        L, N, FF, V, kv = c["L"], c["N"], c["FF"], c["V"], c["NKH"] * c["HD"]
+        sizes = {"wQ": N * N, "wK": kv * N, "wV": kv * N, "wO": N * N, "wG": FF * N, "wU": FF * N, "wD": N * FF}
+        for nm, n in sizes.items():
+            arr = getattr(src, nm)
+            hb.layers(nm, [to_host(arr[l], n // 32 * 34) for l in range(L)])
+        hb.layers("wAN", [to_host(src.wAN[0], N * 4)] * L)
+        hb.layers("wFN", [to_host(src.wFN[0], N * 4)] * L)
+        hc.emb = to_host(src.emb, V * N * 4)
+        hc.onw = to_host(src.onw, N * 4)
+        hc.wOut = to_host(src.wOut, V * N // 32 * 34)
+        kvs = [BCm.KVBlock() for _ in range(c["B"])]
+        for k in kvs:
+            eng.so.kv_init(ctypes.byref(k), L, c["NKH"], c["HD"])
+        hb.kv_array(kvs)
+        logits = np.zeros(c["B"] * V, np.float32)
+        hb.ptr("logits", logits)
+        work = np.zeros(64 * kv * 2 + 4096, np.float32)
+        hb.ptr("workspace", work)
+        hc.ws_size = work.size
+        S = max(N, c["NH"] * c["HD"], FF, 8192)
+        ws = np.zeros(12 * c["B"] * S, np.float32)
+        tok = np.zeros(c["B"], np.int32)
+        eng.so.batch_forward(ctypes.byref(hc), tok.ctypes.data, c["B"], ws.ctypes.data)   # warm
+        n, t0 = 0, time.perf_counter()
+        while (time.perf_counter() - t0 < seconds or n < 2) and n < 40:
+            eng.so.batch_forward(ctypes.byref(hc), tok.ctypes.data, c["B"], ws.ctypes.data)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return {"value": round(c["B"] / dt, 2), "unit": "tok/s", "cores": threads, "kind": "reference",
+                "sample": f"{n} batch_forward steps (B=4, positions 1..{n}) of the reference C engine"}
+    except Exception as e:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": f"failed: {e}"}
 
 
 def run_profile_case(fmt: str, rows: int, launches: int = 3) -> int:
@@ -373,12 +701,24 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-1 model decode section")
+    ap.add_argument("--decode-only", action="store_true", help="run only the config-1 model decode section")
+    ap.add_argument("--decode-profile", action="store_true", help="small decode case for an ncu launch list")
+    ap.add_argument("--profile-steps", type=int, default=3)
+    ap.add_argument("--sweep", action="store_true", help="config-2 sweep (formats x shapes x M), one JSON object")
+    ap.add_argument("--sweep-m", default=None, help="comma-separated M values for --sweep")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.profile:
         return run_profile_case(args.profile, args.profile_rows)
+    if args.decode_only:
+        return run_decode_only(args)
+    if args.decode_profile:
+        return run_decode_profile(args)
+    if args.sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if world > 1:

@@ -509,36 +509,52 @@ __device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> 
 
 // Encode activation rows [nb_x][K] (rows >= nb_x of the M read as zero) into the int8
 // planes + scales described at the top of this file; one warp per 32-element block.
+// Each warp takes kEncBatch blocks at a time and issues all their loads before the
+// reductions, so the L2 latency is paid once per batch rather than once per block.
+constexpr int kEncBatch = 8;
+
 template <int M>
 __device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, int8_t *xh, int8_t *xl,
                                 float *xs, float *xsum, int warp, int lane, int nwarps) {
     const int kb_per_row = K / 32;
-    for (int blk = warp; blk < M * kb_per_row; blk += nwarps) {
-        const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
-        const float v = (m < nb_x) ? __ldg(x + (size_t)m * K + 32 * kb + lane) : 0.0f;
-        float amax = fabsf(v), sum = v;
+    const int total = M * kb_per_row;
+    for (int blk0 = warp * kEncBatch; blk0 < total; blk0 += nwarps * kEncBatch) {
+        float v[kEncBatch];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        for (int i = 0; i < kEncBatch; i++) {
+            const int blk = blk0 + i;
+            const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
+            v[i] = (blk < total && m < nb_x) ? __ldg(x + (size_t)m * K + 32 * kb + lane) : 0.0f;
         }
-        int h = 0, l = 0;
-        float scale;
-        if (amax > 0.0f && amax <= 3.402823466e38f) {
-            const float s = amax / 127.0f;
-            const float t = v / s;
-            const float hh = rintf(t);
-            h = (int)hh;
-            l = (int)rintf((t - hh) * 254.0f);
-            scale = s / 254.0f;
-        } else {
-            scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
-        }
-        xh[(size_t)m * K + 32 * kb + lane] = (int8_t)h;
-        xl[(size_t)m * K + 32 * kb + lane] = (int8_t)l;
-        if (lane == 0) {
-            xs[blk] = scale;
-            xsum[blk] = sum;
+#pragma unroll
+        for (int i = 0; i < kEncBatch; i++) {
+            const int blk = blk0 + i;
+            if (blk >= total) break;
+            const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
+            float amax = fabsf(v[i]), sum = v[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            }
+            int h = 0, l = 0;
+            float scale;
+            if (amax > 0.0f && amax <= 3.402823466e38f) {
+                const float sc = amax / 127.0f;
+                const float t = v[i] / sc;
+                const float hh = rintf(t);
+                h = (int)hh;
+                l = (int)rintf((t - hh) * 254.0f);
+                scale = sc / 254.0f;
+            } else {
+                scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
+            }
+            xh[(size_t)m * K + 32 * kb + lane] = (int8_t)h;
+            xl[(size_t)m * K + 32 * kb + lane] = (int8_t)l;
+            if (lane == 0) {
+                xs[blk] = scale;
+                xsum[blk] = sum;
+            }
         }
     }
 }

@@ -28,6 +28,7 @@
 
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "../../include/mojollama_b200_ref_abi.h"
@@ -72,13 +73,14 @@ __global__ void k_dot_rows(const float *__restrict__ xn, const float *__restrict
 // The KVBlock's own k/v arrays ([L][1024][64][row], cengine_batch_instr.c:1349-1350) get the
 // same rows as the page pool; pages index them with the fixed 64-slot block size.
 __global__ void k_kv_mirror(float *const *__restrict__ mk, float *const *__restrict__ mv,
-                            const int *__restrict__ tab, const int *__restrict__ pos, const float *__restrict__ k,
-                            const float *__restrict__ v, int row, int page_size, int layer) {
+                            const int *__restrict__ tab, int tab_stride, const int *__restrict__ pos,
+                            const float *__restrict__ k, const float *__restrict__ v, int row, int page_size,
+                            int layer) {
     const int b = blockIdx.y;
     float *kb = mk[b], *vb = mv[b];
     if (!kb || !vb) return;
     const int p = pos[b];
-    const int page = tab[(size_t)b * 1024 + p / page_size];
+    const int page = tab[(size_t)b * tab_stride + p / page_size];
     if (page < 0 || page >= 1024) return;
     const size_t off = ((size_t)layer * 1024 * 64 + (size_t)page * 64 + (p % page_size)) * row;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
@@ -131,6 +133,7 @@ struct LayerPlan {
 };
 
 struct ModelPlan {
+    unsigned long long gen = 0;   // distinguishes rebuilt plans of one BC address
     std::vector<uint8_t> fingerprint;
     std::vector<LayerPlan> layers;
     const float *emb = nullptr;
@@ -339,6 +342,372 @@ static int fwd_fail(CallScope &cs, int rc) {
     return rc;
 }
 
+// ------------------------------------------------------------------------------ step buffers
+struct StepDims {
+    int B, N, inner, kvrow, FF, E, topk, M, outNR, NH, HD, L;
+    bool ssm;
+};
+
+// Device buffers of one decode step.  The head (pos, len, KV pointer arrays, page tables)
+// is one contiguous block so the per-step host inputs go up in one copy.
+struct StepBufs {
+    uint8_t *head = nullptr;
+    size_t head_fixed = 0;   // bytes before the page tables
+    int *pos = nullptr, *len = nullptr, *tab = nullptr;
+    float **pools = nullptr, **mk = nullptr, **mv = nullptr;
+    int *tok = nullptr, *e_idx = nullptr;
+    float *xin = nullptr, *x = nullptr, *xn = nullptr, *res = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr,
+          *v = nullptr, *att = nullptr, *tmp = nullptr, *g = nullptr, *u = nullptr, *h = nullptr, *logits_e = nullptr,
+          *e_w = nullptr, *hm = nullptr, *hm2 = nullptr, *score = nullptr, *attn_scr = nullptr, *hfin = nullptr,
+          *logits = nullptr, *state = nullptr;
+    size_t attn_sb = 0;
+};
+
+static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// lay the buffers out from base (base == nullptr: only count); returns the bytes used
+static size_t carve(StepBufs &b, uint8_t *base, const StepDims &d) {
+    size_t o = 0;
+    auto take = [&](size_t bytes) -> uint8_t * {
+        uint8_t *p = base ? base + o : nullptr;
+        o += al256(bytes);
+        return p;
+    };
+    const size_t B = d.B;
+    // head: pos[B] len[B] | pools[B] mk[B] mv[B] | tab[B][1024]
+    b.head = base ? base : nullptr;
+    const size_t ints = 2 * B * sizeof(int);
+    const size_t ptr_off = (ints + 15) & ~(size_t)15;
+    b.head_fixed = ptr_off + 3 * B * sizeof(float *);
+    uint8_t *h = take(b.head_fixed + B * 1024 * sizeof(int));
+    if (h) {
+        b.pos = (int *)h;
+        b.len = b.pos + B;
+        b.pools = (float **)(h + ptr_off);
+        b.mk = b.pools + B;
+        b.mv = b.mk + B;
+        b.tab = (int *)(h + b.head_fixed);
+    }
+    const int FFmax = d.FF > kShexpFF ? d.FF : kShexpFF;
+    const int wide = FFmax > d.inner ? FFmax : d.inner;
+    const int qkv_w = d.inner + 2 * (d.N > d.kvrow ? d.N : d.kvrow);
+    const int tk = d.topk > 0 ? d.topk : 1, M = d.M > 0 ? d.M : 1;
+    b.tok = (int *)take(B * sizeof(int));
+    b.xin = (float *)take(B * d.N * 4);
+    b.x = (float *)take(B * d.N * 4);
+    b.xn = (float *)take(B * d.N * 4);
+    b.res = (float *)take(B * d.N * 4);
+    b.qkv = (float *)take(B * (size_t)(qkv_w > d.N ? qkv_w : d.N) * 4);
+    b.q = (float *)take(B * d.inner * 4);
+    b.k = (float *)take(B * d.kvrow * 4);
+    b.v = (float *)take(B * d.kvrow * 4);
+    b.att = (float *)take(B * d.inner * 4);
+    b.tmp = (float *)take(B * (size_t)(d.inner > d.N ? d.inner : d.N) * 4);
+    b.g = (float *)take(B * (size_t)wide * 4);
+    b.u = (float *)take(B * (size_t)wide * 4);
+    b.h = (float *)take(B * (size_t)wide * 4);
+    b.logits_e = (float *)take(B * (size_t)(d.E > 0 ? d.E : 1) * 4);
+    b.e_idx = (int *)take(B * tk * sizeof(int));
+    b.e_w = (float *)take(B * tk * 4);
+    b.hm = (float *)take(B * (size_t)tk * M * 4);
+    b.hm2 = (float *)take(B * (size_t)tk * M * 4);
+    b.score = (float *)take(B * 4);
+    b.attn_sb = attn_scratch_bytes(d.B, d.NH, d.HD);
+    b.attn_scr = (float *)take(b.attn_sb);
+    b.hfin = (float *)take(B * d.N * 4);
+    b.logits = (float *)take(B * (size_t)d.outNR * 4);
+    b.state = d.ssm ? (float *)take((size_t)d.L * kSsmGroups * kSsmState * 4) : nullptr;
+    return o;
+}
+
+static size_t step_bytes(const StepDims &d) {
+    StepBufs tmp;
+    return carve(tmp, nullptr, d);
+}
+
+static int max_blocks_used(const std::vector<int> &pos, int ps) {
+    int m = 0;
+    for (int p : pos) m = p / ps + 1 > m ? p / ps + 1 : m;
+    return m;
+}
+
+// positions, lengths, KV pointer arrays and page tables (row stride tab_w) in one copy
+static int upload_step_inputs(const StepBufs &sb, const StepDims &d, const std::vector<int> &pos,
+                              const std::vector<int> &lens, const std::vector<int> &tables,
+                              const std::vector<float *> &pools, const std::vector<float *> &mk,
+                              const std::vector<float *> &mv, int tab_w, cudaStream_t s) {
+    const int B = d.B;
+    std::vector<uint8_t> host(sb.head_fixed + (size_t)B * tab_w * sizeof(int));
+    int *hp = (int *)host.data();
+    memcpy(hp, pos.data(), B * sizeof(int));
+    memcpy(hp + B, lens.data(), B * sizeof(int));
+    uint8_t *ptrs = host.data() + ((uint8_t *)sb.pools - sb.head);
+    memcpy(ptrs, pools.data(), B * sizeof(float *));
+    memcpy(ptrs + B * sizeof(float *), mk.data(), B * sizeof(float *));
+    memcpy(ptrs + 2 * B * sizeof(float *), mv.data(), B * sizeof(float *));
+    int *ht = (int *)(host.data() + sb.head_fixed);
+    for (int b = 0; b < B; b++) memcpy(ht + (size_t)b * tab_w, &tables[(size_t)b * 1024], tab_w * sizeof(int));
+    return MLQ_CUDA(cudaMemcpyAsync(sb.head, host.data(), host.size(), cudaMemcpyHostToDevice, s)) ? MLQ_OK
+                                                                                                : MLQ_ERR_CUDA;
+}
+
+// Every device launch of one step.  tab_w: page-table row stride in sb.tab; attn_len: the
+// length the attention splits are planned for (>= every sequence's length); h_tok: host
+// token ids (only the per-row Q4_K embedding decode reads them).
+static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, const StepDims &d, bool compat,
+                        int attn_len, int tab_w, const int *d_tok, const int *h_tok, const float *xin, float *d_state,
+                        float *hfin, float *d_logits, cudaStream_t s) {
+    const int B = d.B, N = d.N, inner = d.inner, kvrow = d.kvrow, NH = c->NH, NKH = c->NKH, HD = c->HD, L = d.L;
+    const int rope_dim = c->rope_dim > 0 ? c->rope_dim : HD;
+    const int topk = d.topk, M = d.M;
+    const MlqKVBlock *kv0 = c->kv_array[0];
+    float *x = sb.x, *xn = sb.xn, *res = sb.res, *qkv = sb.qkv, *q = sb.q, *k = sb.k, *v = sb.v, *att = sb.att,
+          *tmp = sb.tmp, *g = sb.g, *u = sb.u, *h = sb.h;
+    int rc = MLQ_OK;
+#define MLQ_TRY(expr)                  \
+    do {                               \
+        if (rc == MLQ_OK) rc = (expr); \
+    } while (0)
+    MLQ_TRY(launch_embed(P->emb, c->emb_quant, d_tok, h_tok, x, B, N, c->V, s));
+    const int ps = kv0->pt.page_size;
+    const long long layer_stride = (long long)kv0->pt.n_pages * ps * kvrow;
+    const float scale = 1.0f / sqrtf((float)HD);
+    // norm output and projection input: xn / xn normally; x / the workspace's xn region in
+    // reference-compatibility mode
+    float *nout = compat ? x : xn;
+    const float *pin = compat ? xin : xn;
+    const float inf = HUGE_VALF;
+    for (int l = 0; l < L && rc == MLQ_OK; l++) {
+        const LayerPlan &lp = P->layers[l];
+        MLQ_TRY(launch_rms_norm(nout, x, lp.an, res, B, N, c->eps, 1, s));
+        if (lp.ssm) {
+            float *st = d_state + (size_t)l * kSsmGroups * kSsmState;
+            MLQ_TRY(launch_ssm_decode_step(pin, att, lp.conv, lp.ssm_a, lp.ssm_dt, lp.ssm_alpha, lp.ssm_beta, st, B, N,
+                                           inner, kSsmGroups, kSsmState, kSsmDtRank, s));
+            if (lp.wattng) {
+                MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, pin, g, inner, N, B, 0, s));
+                MLQ_TRY(launch_mul(att, g, (long long)B * inner, s));
+            } else {
+                cudaMemsetAsync(att, 0, sizeof(float) * (size_t)B * inner, s);
+            }
+            if (lp.wssmout) {
+                MLQ_TRY(launch_matmul(lp.wssmout, lp.qssmout, att, tmp, N, inner, B, 0, s));
+                MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            } else {
+                cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
+            }
+        } else {
+            if (lp.wqkv) {
+                const int n_qkv = inner + 2 * N;
+                MLQ_TRY(launch_matmul(lp.wqkv, lp.qqkv, pin, qkv, n_qkv, c->nc, B, 0, s));
+                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
+                                                                                        compat ? inner : n_qkv, 0);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, n_qkv, inner);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(v, qkv, kvrow, n_qkv,
+                                                                                        inner + N);
+                count_launch(3);
+            } else if (lp.wqk) {
+                const int nqk = lp.nq + lp.nk;
+                MLQ_TRY(launch_matmul(lp.wqk, lp.qqk, pin, qkv, nqk, c->nc, B, 0, s));
+                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
+                                                                                        compat ? inner : nqk, 0);
+                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, nqk, lp.nq);
+                count_launch(2);
+                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
+            } else {
+                MLQ_TRY(launch_matmul(lp.wq, lp.qq, pin, q, lp.nq, c->nc, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.wk, lp.qk, pin, k, lp.nk, c->nc, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
+            }
+            MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+            MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+            KVView kv{nullptr, nullptr, sb.tab, tab_w, (long long)ps * kvrow, ps, kvrow, sb.pools, layer_stride, l,
+                      kv0->pt._n_layers};
+            MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, sb.pos, 0, B, kvrow, s));
+            if (rc == MLQ_OK) {
+                k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(sb.mk, sb.mv, sb.tab, tab_w,
+                                                                                        sb.pos, k, v, kvrow, ps, l);
+                count_launch();
+            }
+            MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, 0, scale, att, sb.attn_scr,
+                                       sb.attn_sb, s));
+            if (lp.wattng) MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, att, tmp, N, inner, B, 0, s));
+            else MLQ_TRY(launch_matmul(lp.wo, lp.qo, att, tmp, lp.no, inner, B, 0, s));
+            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+        }
+        MLQ_TRY(launch_rms_norm(nout, x, lp.fn, res, B, N, c->eps, 1, s));
+        if (lp.router) {
+            const int E = c->n_experts;
+            MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, sb.logits_e, E, N, B, 0, s));
+            MLQ_TRY(launch_router_topk(sb.logits_e, B, E, topk, 0, sb.e_idx, sb.e_w, s));
+            MLQ_TRY(launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
+                                       lp.dexp, lp.gstride, lp.ustride, lp.dstride, sb.e_idx, sb.e_w, topk, B, M, N,
+                                       pin, sb.hm, sb.hm2, x, res, inf, s));
+            if (lp.shg && lp.shrouter) {
+                k_dot_rows<<<B, 256, 0, s>>>(pin, lp.shrouter, sb.score, N);
+                count_launch();
+                MLQ_TRY(launch_matmul(lp.shg, lp.qshg, pin, g, kShexpFF, N, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.shu, lp.qshu, pin, u, kShexpFF, N, B, 0, s));
+                k_shexp_act<<<grid1((long long)B * kShexpFF), 256, 0, s>>>(h, g, u, (long long)B * kShexpFF);
+                count_launch();
+                MLQ_TRY(launch_matmul(lp.shd, lp.qshd, h, tmp, N, kShexpFF, B, 0, s));
+                k_add_scaled_pos<<<dim3(grid1(N) > 16 ? 16 : grid1(N), B), 256, 0, s>>>(x, tmp, sb.score, N);
+                count_launch();
+            }
+        } else if (lp.wg) {
+            MLQ_TRY(launch_matmul(lp.wg, lp.qg, pin, g, lp.ng, c->nc, B, 0, s));
+            MLQ_TRY(launch_matmul(lp.wu, lp.qu, pin, u, lp.nu, c->nc, B, 0, s));
+            k_silu_mul<<<grid1((long long)B * c->FF), 256, 0, s>>>(h, g, u, (long long)B * c->FF);
+            count_launch();
+            MLQ_TRY(launch_matmul(lp.wd, lp.qd, h, tmp, lp.nd, c->FF, B, 0, s));
+            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+        } else if (!compat) {
+            cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
+        }   // (with no FFN the reference leaves the normalised activations in x)
+    }
+    // the final normalised hidden state also lands in ws[0 : B*N], where the reference
+    // leaves it (its x buffer is the start of the workspace)
+    MLQ_TRY(launch_rms_norm(hfin, x, P->onw, res, B, N, c->eps, 1, s));
+    MLQ_TRY(launch_matmul(P->wout, c->outQuant, hfin, d_logits, c->outNR, c->outNC, B, 0, s));
+#undef MLQ_TRY
+    return rc;
+}
+
+// ------------------------------------------------------------------------------ CUDA graphs
+// A step is captured once per (plan, batch size, attention-length bucket, mode) and
+// replayed; the per-step inputs (positions, page tables, KV pointers, tokens, the
+// compatibility-mode projection input, a host SSM state) are copied into the graph's own
+// buffers before the replay and its outputs copied out after it.  Attention splits are
+// planned for the bucket (a power of two >= the longest sequence), the kernels read each
+// sequence's own length, so one graph serves every step inside the bucket.
+struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    uint8_t *mem = nullptr;
+    StepBufs sb;
+    unsigned long long launches = 0;
+};
+struct GraphKey {
+    int dev;
+    uintptr_t bc;
+    unsigned long long gen;
+    int B, bucket, tab_w, compat, state_dev, ws_out;
+    uintptr_t state_ptr;
+    bool operator<(const GraphKey &o) const {
+        return std::tie(dev, bc, gen, B, bucket, tab_w, compat, state_dev, ws_out, state_ptr) <
+               std::tie(o.dev, o.bc, o.gen, o.B, o.bucket, o.tab_w, o.compat, o.state_dev, o.ws_out, o.state_ptr);
+    }
+};
+static std::mutex g_graph_mu;
+static std::map<GraphKey, GraphEntry> g_graphs;
+static std::map<GraphKey, bool> g_graph_failed;
+static std::map<GraphKey, bool> g_graph_seen;
+
+static bool graphs_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_NO_GRAPHS");
+        v = (e && atoi(e) != 0) ? 0 : 1;
+    }
+    return v == 1;
+}
+
+// the legacy default stream cannot be captured
+static bool capturable(cudaStream_t s) { return s != nullptr && s != cudaStreamLegacy; }
+
+static void destroy_graphs() {
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    for (auto &kv : g_graphs) {
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        if (kv.second.mem) cudaFree(kv.second.mem);
+    }
+    g_graphs.clear();
+    g_graph_failed.clear();
+    g_graph_seen.clear();
+}
+
+static int run_graph_step(const BC *c, const ModelPlan *P, const StepDims &d, bool compat, const std::vector<int> &pos,
+                          const std::vector<int> &lens, const std::vector<int> &tables,
+                          const std::vector<float *> &pools, const std::vector<float *> &mk,
+                          const std::vector<float *> &mv, int tab_w_used, int max_len, const int *tokens,
+                          const float *ws_xn, float *ws, cudaStream_t s) {
+    Ctx *cx = ctx();
+    if (!cx) return mlq_last_error();
+    const MlqKVBlock *kv0 = c->kv_array[0];
+    int bucket = 64;
+    while (bucket < max_len) bucket *= 2;
+    int tab_w = (bucket + kv0->pt.page_size - 1) / kv0->pt.page_size;
+    if (tab_w > 1024) tab_w = 1024;
+    if (tab_w < tab_w_used) tab_w = tab_w_used;
+    const bool state_dev = d.ssm && is_device_ptr(c->ssm_state);
+    GraphKey key{cx->device, (uintptr_t)c, P->gen, d.B, bucket, tab_w, compat ? 1 : 0, state_dev ? 1 : 0,
+                 ws ? 1 : 0, state_dev ? (uintptr_t)c->ssm_state : 0};
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    if (g_graph_failed.count(key)) return MLQ_ERR_UNSUPPORTED;
+    auto it = g_graphs.find(key);
+    if (it == g_graphs.end() && !g_graph_seen.count(key)) {
+        // the first step of a shape runs eagerly (one-time kernel attributes, lazy state)
+        g_graph_seen[key] = true;
+        return MLQ_ERR_UNSUPPORTED;
+    }
+    if (it == g_graphs.end()) {
+        GraphEntry e;
+        const size_t bytes = step_bytes(d);
+        if (!MLQ_CUDA(cudaMalloc(&e.mem, bytes))) return MLQ_ERR_CUDA;
+        carve(e.sb, e.mem, d);
+        float *dstate = d.ssm ? (state_dev ? c->ssm_state : e.sb.state) : nullptr;
+        // capture (nothing executes); zero host ids: the graph path never decodes Q4_K rows
+        std::vector<int> h_tok(d.B, 0);
+        const unsigned long long l0 = mlq_launch_count();
+        cudaGraph_t graph = nullptr;
+        int rc = MLQ_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)) ? MLQ_OK : MLQ_ERR_CUDA;
+        if (rc == MLQ_OK) {
+            rc = enqueue_step(c, P, e.sb, d, compat, bucket, tab_w, e.sb.tok, h_tok.data(), e.sb.xin, dstate,
+                              e.sb.hfin, e.sb.logits, s);
+            const cudaError_t ce = cudaStreamEndCapture(s, &graph);
+            if (ce != cudaSuccess) {
+                cudaGetLastError();
+                if (rc == MLQ_OK) rc = MLQ_ERR_UNSUPPORTED;
+            }
+        }
+        if (rc == MLQ_OK && graph) {
+            if (cudaGraphInstantiate(&e.exec, graph, 0) != cudaSuccess) {
+                cudaGetLastError();
+                rc = MLQ_ERR_UNSUPPORTED;
+            }
+        }
+        if (graph) cudaGraphDestroy(graph);
+        e.launches = mlq_launch_count() - l0;
+        if (rc != MLQ_OK) {
+            cudaFree(e.mem);
+            g_graph_failed[key] = true;
+            cudaGetLastError();
+            return MLQ_ERR_UNSUPPORTED;
+        }
+        it = g_graphs.emplace(key, e).first;
+    } else {
+        count_launch((int)it->second.launches);
+    }
+    GraphEntry &e = it->second;
+    const StepDims &dd = d;
+    int rc = upload_step_inputs(e.sb, dd, pos, lens, tables, pools, mk, mv, tab_w, s);
+    bool host_io = false;
+    auto cp = [&](void *dst, const void *src, size_t bytes) {
+        if (rc != MLQ_OK) return;
+        if (!is_device_ptr(dst) || !is_device_ptr(src)) host_io = true;
+        if (!MLQ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, s))) rc = MLQ_ERR_CUDA;
+    };
+    cp(e.sb.tok, tokens, sizeof(int) * d.B);
+    if (compat) cp(e.sb.xin, ws_xn, sizeof(float) * (size_t)d.B * d.N);
+    const size_t state_bytes = sizeof(float) * (size_t)d.L * kSsmGroups * kSsmState;
+    if (d.ssm && !state_dev) cp(e.sb.state, c->ssm_state, state_bytes);
+    if (rc == MLQ_OK && !MLQ_CUDA(cudaGraphLaunch(e.exec, s))) rc = MLQ_ERR_CUDA;
+    cp(c->logits, e.sb.logits, sizeof(float) * (size_t)d.B * d.outNR);
+    if (ws) cp(ws, e.sb.hfin, sizeof(float) * (size_t)d.B * d.N);
+    if (d.ssm && !state_dev) cp(c->ssm_state, e.sb.state, state_bytes);
+    if (rc == MLQ_OK && host_io && !MLQ_CUDA(cudaStreamSynchronize(s))) rc = MLQ_ERR_CUDA;
+    return rc;
+}
+
 }  // namespace mlq
 
 using namespace mlq;
@@ -348,6 +717,7 @@ extern "C" {
 size_t mlq_sizeof_bc(void) { return sizeof(BC); }
 
 void mlq_forget_model_plans(void) {
+    destroy_graphs();
     std::lock_guard<std::mutex> lk(g_plan_mu);
     g_plans.clear();
 }
@@ -390,6 +760,8 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
             ModelPlan np;
             if (!build_plan(c, cs, np)) return fwd_fail(cs, mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG);
             np.fingerprint = std::move(fp);
+            static unsigned long long next_gen = 0;
+            np.gen = ++next_gen;
             g_plans[key] = std::move(np);
             it = g_plans.find(key);
         }
@@ -452,177 +824,52 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
         mirror_v[b] = mirror ? kv->v : nullptr;
         if (p + 1 > max_len) max_len = p + 1;
     }
-    // ------------------------------------------------------------------ buffers
-    const int FFmax = c->FF > kShexpFF ? c->FF : kShexpFF;
-    const int qkv_w = inner + 2 * N > inner + 2 * kvrow ? inner + 2 * N : inner + 2 * kvrow;
-    const int topk = c->n_experts_per_tok, M = c->moe_intermediate;
-    int *d_tok = (int *)cs.in(tokens, sizeof(int) * B);
-    int *d_pos = (int *)cs.scratch(sizeof(int) * B);
-    int *d_len = (int *)cs.scratch(sizeof(int) * B);
-    int *d_tab = (int *)cs.scratch(sizeof(int) * (size_t)B * 1024);
-    float **d_pools = (float **)cs.scratch(sizeof(float *) * B);
-    float **d_mk = (float **)cs.scratch(sizeof(float *) * B);
-    float **d_mv = (float **)cs.scratch(sizeof(float *) * B);
-    const float *xin = compat ? (const float *)cs.in(ws + (size_t)B * S, sizeof(float) * (size_t)B * N) : nullptr;
-    float *ws_out = ws ? (float *)cs.out(ws, sizeof(float) * (size_t)B * N) : nullptr;
-    float *x = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
-    float *xn = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
-    float *res = (float *)cs.scratch(sizeof(float) * (size_t)B * N);
-    float *qkv = (float *)cs.scratch(sizeof(float) * (size_t)B * (qkv_w > N ? qkv_w : N));
-    float *q = (float *)cs.scratch(sizeof(float) * (size_t)B * inner);
-    float *k = (float *)cs.scratch(sizeof(float) * (size_t)B * kvrow);
-    float *v = (float *)cs.scratch(sizeof(float) * (size_t)B * kvrow);
-    float *att = (float *)cs.scratch(sizeof(float) * (size_t)B * inner);
-    float *tmp = (float *)cs.scratch(sizeof(float) * (size_t)B * (inner > N ? inner : N));
-    float *g = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
-    float *u = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
-    float *h = (float *)cs.scratch(sizeof(float) * (size_t)B * (FFmax > inner ? FFmax : inner));
-    float *logits_e = (float *)cs.scratch(sizeof(float) * (size_t)B * (c->n_experts > 0 ? c->n_experts : 1));
-    int *e_idx = (int *)cs.scratch(sizeof(int) * (size_t)B * (topk > 0 ? topk : 1));
-    float *e_w = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1));
-    float *hm = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1) * (M > 0 ? M : 1));
-    float *hm2 = (float *)cs.scratch(sizeof(float) * (size_t)B * (topk > 0 ? topk : 1) * (M > 0 ? M : 1));
-    float *score = (float *)cs.scratch(sizeof(float) * B);
-    const size_t attn_sb = attn_scratch_bytes(B, NH, HD);
-    float *attn_scr = (float *)cs.scratch(attn_sb);
-    float *d_state = nullptr;
-    bool any_ssm = false;
-    for (int l = 0; l < L; l++) any_ssm |= P->layers[l].ssm;
-    if (any_ssm) {
-        if (!c->ssm_state) {
-            set_error(MLQ_ERR_ARG, "batch_forward: SSM layers without ssm_state");
-            return fwd_fail(cs, MLQ_ERR_ARG);
-        }
-        d_state = (float *)cs.inout(c->ssm_state, sizeof(float) * (size_t)L * kSsmGroups * kSsmState);
-    }
-    float *d_logits = (float *)cs.out(c->logits, sizeof(float) * (size_t)B * c->outNR);
-    if (cs.failed) return cs.finish();
+    // ------------------------------------------------------------------ step
     std::vector<int> lens(B);
     for (int b = 0; b < B; b++) lens[b] = pos[b] + 1;
-    if (!MLQ_CUDA(cudaMemcpyAsync(d_pos, pos.data(), sizeof(int) * B, cudaMemcpyHostToDevice, s)) ||
-        !MLQ_CUDA(cudaMemcpyAsync(d_len, lens.data(), sizeof(int) * B, cudaMemcpyHostToDevice, s)) ||
-        !MLQ_CUDA(cudaMemcpyAsync(d_tab, tables.data(), sizeof(int) * (size_t)B * 1024, cudaMemcpyHostToDevice, s)) ||
-        !MLQ_CUDA(cudaMemcpyAsync(d_pools, pools.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)) ||
-        !MLQ_CUDA(cudaMemcpyAsync(d_mk, mirror_k.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)) ||
-        !MLQ_CUDA(cudaMemcpyAsync(d_mv, mirror_v.data(), sizeof(float *) * B, cudaMemcpyHostToDevice, s)))
-        return fwd_fail(cs, MLQ_ERR_CUDA);
-
-    int rc = MLQ_OK;
-#define MLQ_TRY(expr)                               \
-    do {                                            \
-        if (rc == MLQ_OK) rc = (expr);              \
-    } while (0)
-    // ------------------------------------------------------------------ embedding
-    {
-        std::vector<int> th;
-        if (!host_tokens(tokens, B, th)) rc = MLQ_ERR_CUDA;
-        MLQ_TRY(launch_embed(P->emb, c->emb_quant, d_tok, th.data(), x, B, N, c->V, s));
+    bool any_ssm = false;
+    for (int l = 0; l < L; l++) any_ssm |= P->layers[l].ssm;
+    if (any_ssm && !c->ssm_state) {
+        set_error(MLQ_ERR_ARG, "batch_forward: SSM layers without ssm_state");
+        return fwd_fail(cs, MLQ_ERR_ARG);
     }
-    const int ps = kv0->pt.page_size;
-    const long long layer_stride = (long long)kv0->pt.n_pages * ps * kvrow;
-    const float scale = 1.0f / sqrtf((float)HD);
-    // ------------------------------------------------------------------ layers
-    // norm output and projection input: xn / xn normally; x / the workspace's xn region in
-    // reference-compatibility mode
-    float *nout = compat ? x : xn;
-    const float *pin = compat ? xin : xn;
-    const float inf = HUGE_VALF;
-    for (int l = 0; l < L && rc == MLQ_OK; l++) {
-        const LayerPlan &lp = P->layers[l];
-        MLQ_TRY(launch_rms_norm(nout, x, lp.an, res, B, N, c->eps, 1, s));
-        if (lp.ssm) {
-            float *st = d_state + (size_t)l * kSsmGroups * kSsmState;
-            MLQ_TRY(launch_ssm_decode_step(pin, att, lp.conv, lp.ssm_a, lp.ssm_dt, lp.ssm_alpha, lp.ssm_beta, st, B, N,
-                                           inner, kSsmGroups, kSsmState, kSsmDtRank, s));
-            if (lp.wattng) {
-                MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, pin, g, inner, N, B, 0, s));
-                MLQ_TRY(launch_mul(att, g, (long long)B * inner, s));
-            } else {
-                cudaMemsetAsync(att, 0, sizeof(float) * (size_t)B * inner, s);
-            }
-            if (lp.wssmout) {
-                MLQ_TRY(launch_matmul(lp.wssmout, lp.qssmout, att, tmp, N, inner, B, 0, s));
-                MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
-            } else {
-                cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
-            }
-        } else {
-            // projections
-            if (lp.wqkv) {
-                const int n_qkv = inner + 2 * N;
-                MLQ_TRY(launch_matmul(lp.wqkv, lp.qqkv, pin, qkv, n_qkv, c->nc, B, 0, s));
-                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
-                                                                                        compat ? inner : n_qkv, 0);
-                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, n_qkv, inner);
-                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(v, qkv, kvrow, n_qkv, inner + N);
-                count_launch(3);
-            } else if (lp.wqk) {
-                const int nqk = lp.nq + lp.nk;
-                MLQ_TRY(launch_matmul(lp.wqk, lp.qqk, pin, qkv, nqk, c->nc, B, 0, s));
-                k_copy_cols<<<dim3(grid1(inner) > 16 ? 16 : grid1(inner), B), 256, 0, s>>>(q, qkv, inner,
-                                                                                        compat ? inner : nqk, 0);
-                k_copy_cols<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(k, qkv, kvrow, nqk, lp.nq);
-                count_launch(2);
-                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
-            } else {
-                MLQ_TRY(launch_matmul(lp.wq, lp.qq, pin, q, lp.nq, c->nc, B, 0, s));
-                MLQ_TRY(launch_matmul(lp.wk, lp.qk, pin, k, lp.nk, c->nc, B, 0, s));
-                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
-            }
-            MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, d_pos, 0, P->cos_t, P->sin_t, rope_dim, s));
-            MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, d_pos, 0, P->cos_t, P->sin_t, rope_dim, s));
-            KVView kv{nullptr, nullptr, d_tab, 1024, (long long)ps * kvrow, ps, kvrow, d_pools, layer_stride, l,
-                      kv0->pt._n_layers};
-            MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, d_pos, 0, B, kvrow, s));
-            if (rc == MLQ_OK) {
-                k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(d_mk, d_mv, d_tab, d_pos, k,
-                                                                                        v, kvrow, ps, l);
-                count_launch();
-            }
-            // attention over positions 0..pos (length pos + 1 per sequence)
-            MLQ_TRY(launch_attn_decode(q, kv, d_len, 0, max_len, B, NH, NKH, HD, 0, scale, att, attn_scr, attn_sb, s));
-            if (lp.wattng) MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, att, tmp, N, inner, B, 0, s));
-            else MLQ_TRY(launch_matmul(lp.wo, lp.qo, att, tmp, lp.no, inner, B, 0, s));
-            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+    StepDims d{B, N, inner, kvrow, c->FF, c->n_experts, c->n_experts_per_tok, c->moe_intermediate, c->outNR, NH, HD,
+               L, any_ssm};
+    const int tab_w = max_blocks_used(pos, kv0->pt.page_size);
+    const float *ws_xn = compat ? ws + (size_t)B * S : nullptr;
+    const bool graphable = graphs_enabled() && !(c->emb_quant == MLQ_Q4_K && !compat) && capturable(s);
+    int rc;
+    if (graphable) {
+        rc = run_graph_step(c, P, d, compat, pos, lens, tables, pools, mirror_k, mirror_v, tab_w, max_len, tokens, ws_xn,
+                            ws, s);
+        if (rc == MLQ_OK) {
+            for (int b = 0; b < B; b++) c->kv_array[b]->seq_len[0]++;
+            cs.finish();
+            return MLQ_OK;
         }
-        // FFN
-        MLQ_TRY(launch_rms_norm(nout, x, lp.fn, res, B, N, c->eps, 1, s));
-        if (lp.router) {
-            const int E = c->n_experts;
-            MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, logits_e, E, N, B, 0, s));
-            MLQ_TRY(launch_router_topk(logits_e, B, E, topk, 0, e_idx, e_w, s));
-            MLQ_TRY(launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
-                                       lp.dexp, lp.gstride, lp.ustride, lp.dstride, e_idx, e_w, topk, B, M, N, pin,
-                                       hm, hm2, x, res, inf, s));
-            if (lp.shg && lp.shrouter) {
-                k_dot_rows<<<B, 256, 0, s>>>(pin, lp.shrouter, score, N);
-                count_launch();
-                MLQ_TRY(launch_matmul(lp.shg, lp.qshg, pin, g, kShexpFF, N, B, 0, s));
-                MLQ_TRY(launch_matmul(lp.shu, lp.qshu, pin, u, kShexpFF, N, B, 0, s));
-                k_shexp_act<<<grid1((long long)B * kShexpFF), 256, 0, s>>>(h, g, u, (long long)B * kShexpFF);
-                count_launch();
-                MLQ_TRY(launch_matmul(lp.shd, lp.qshd, h, tmp, N, kShexpFF, B, 0, s));
-                k_add_scaled_pos<<<dim3(grid1(N) > 16 ? 16 : grid1(N), B), 256, 0, s>>>(x, tmp, score, N);
-                count_launch();
-            }
-        } else if (lp.wg) {
-            MLQ_TRY(launch_matmul(lp.wg, lp.qg, pin, g, lp.ng, c->nc, B, 0, s));
-            MLQ_TRY(launch_matmul(lp.wu, lp.qu, pin, u, lp.nu, c->nc, B, 0, s));
-            k_silu_mul<<<grid1((long long)B * c->FF), 256, 0, s>>>(h, g, u, (long long)B * c->FF);
-            count_launch();
-            MLQ_TRY(launch_matmul(lp.wd, lp.qd, h, tmp, lp.nd, c->FF, B, 0, s));
-            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
-        } else if (!compat) {
-            cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
-        }   // (with no FFN the reference leaves the normalised activations in x)
+        if (rc != MLQ_ERR_UNSUPPORTED) return fwd_fail(cs, rc);
     }
-    // ------------------------------------------------------------------ head
-    // the final normalised hidden state also lands in ws[0 : B*N], where the reference
-    // leaves it (its x buffer is the start of the workspace)
-    float *hfin = ws_out ? ws_out : xn;
-    MLQ_TRY(launch_rms_norm(hfin, x, P->onw, res, B, N, c->eps, 1, s));
-    MLQ_TRY(launch_matmul(P->wout, c->outQuant, hfin, d_logits, c->outNR, c->outNC, B, 0, s));
-#undef MLQ_TRY
+    // direct launches with this call's scratch
+    StepBufs sb;
+    const size_t bytes = step_bytes(d);
+    uint8_t *mem = (uint8_t *)cs.scratch(bytes);
+    if (!mem) return fwd_fail(cs, mlq_last_error() ? mlq_last_error() : MLQ_ERR_CUDA);
+    carve(sb, mem, d);
+    const int *d_tok = (const int *)cs.in(tokens, sizeof(int) * B);
+    const float *xin = compat ? (const float *)cs.in(ws_xn, sizeof(float) * (size_t)B * N) : nullptr;
+    float *ws_out = ws ? (float *)cs.out(ws, sizeof(float) * (size_t)B * N) : nullptr;
+    float *d_state = any_ssm ? (float *)cs.inout(c->ssm_state, sizeof(float) * (size_t)L * kSsmGroups * kSsmState)
+                             : nullptr;
+    float *d_logits = (float *)cs.out(c->logits, sizeof(float) * (size_t)B * c->outNR);
+    if (cs.failed) return cs.finish();
+    rc = upload_step_inputs(sb, d, pos, lens, tables, pools, mirror_k, mirror_v, tab_w, s);
+    if (rc == MLQ_OK) {
+        std::vector<int> th(B, 0);   // host ids are needed only by the per-row Q4_K decode
+        if (c->emb_quant == MLQ_Q4_K && !compat && !host_tokens(tokens, B, th)) rc = MLQ_ERR_CUDA;
+        if (rc == MLQ_OK)
+            rc = enqueue_step(c, P, sb, d, compat, max_len, tab_w, d_tok, th.data(), xin, d_state,
+                              ws_out ? ws_out : sb.xn, d_logits, s);
+    }
     if (rc != MLQ_OK) return fwd_fail(cs, rc);
     for (int b = 0; b < B; b++) c->kv_array[b]->seq_len[0]++;
     return cs.finish();

@@ -1,0 +1,470 @@
+// Tensor-core quantized GEMM for many tokens: out[t][r] = sum_k W[r][k] * x[t][k]
+// (the math of the reference's *_batch_matmul, cengine_batch_instr.c:68-534, at B >= 16).
+//
+// tcgen05 (5th-generation tensor cores) with the weights on the MMA's M side:
+//   * a CTA owns 128 weight rows x NT tokens; the fp32 accumulator tile [128][NT] lives in
+//     TMEM (NT columns), allocated once per CTA;
+//   * K advances in chunks of 256 elements.  The raw GGUF bytes of the 128 rows' chunk are
+//     copied into shared memory with cp.async (16-byte pieces, two stages), every thread
+//     then decodes 8-element groups to fp16 and stores them in the canonical K-major
+//     128-byte-swizzled operand layout (8-row x 128-byte atoms, 16-byte chunk c of row r at
+//     c ^ (r & 7));
+//   * the activations were converted once per call to fp16 with a power-of-two scale per
+//     token (|x/s| <= 1, so fp16 keeps 11 significant bits and never overflows); their
+//     chunk is copied straight into the same swizzled layout (two stages);
+//   * one thread issues 16 tcgen05.mma.kind::f16 (K = 16 each) per chunk and commits them
+//     to an mbarrier; the next chunk's decode waits on that barrier before it overwrites
+//     the A operand;
+//   * the epilogue reads the accumulators with tcgen05.ld (warp w reads TMEM lanes
+//     32*(w%4).. = weight rows), multiplies by the token scale and writes fp32.
+// Error model: weights rounded once to fp16 (relative 2^-11), activations once (2^-11),
+// products and sums exact / fp32 -- relative L2 of the outputs ~3e-4.
+// Formats: Q8_0, Q4_0, Q4_1, Q5_0, Q4_K, Q5_K with K % 256 == 0 and 16-byte aligned rows
+// and chunks; others (Q6_K, MXFP4, odd K) stay on the dp4a kernels.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+
+#include "formats.cuh"
+#include "mlq_internal.h"
+#include "pipeline.cuh"
+
+namespace mlq {
+
+constexpr int kTcRows = 128;      // MMA M
+constexpr int kTcThreads = 256;   // 8 warps
+constexpr int kTcKC = 256;        // K elements per chunk
+constexpr int kTcAtomBytes = 16384;   // one 64-wide K atom of the A tile: 128 rows x 128 B
+
+// ---------------------------------------------------------------- activations
+// x [M][K] fp32 -> xh [Mp][K] fp16 of x / s_t, s_t = 2^ceil(log2(max|x_t|)) (1 for a zero
+// row); rows M..Mp-1 are zero with scale 0.
+__global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh, float *__restrict__ scale, int M,
+                           int K) {
+    __shared__ float sh[32];
+    const int t = blockIdx.x;
+    __half *dst = xh + (size_t)t * K;
+    if (t >= M) {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = __float2half_rn(0.0f);
+        if (threadIdx.x == 0) scale[t] = 0.0f;
+        return;
+    }
+    const float *src = x + (size_t)t * K;
+    float amax = 0.0f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(src[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) sh[0] = v;
+    }
+    __syncthreads();
+    amax = sh[0];
+    float s;
+    if (!(amax <= 3.402823466e38f)) s = __int_as_float(0x7fc00000);   // inf / NaN row -> NaN outputs
+    else if (amax == 0.0f) s = 1.0f;
+    else {
+        int e;
+        frexpf(amax, &e);            // amax = f * 2^e, f in [0.5, 1)
+        s = ldexpf(1.0f, e);         // amax / s in [0.5, 1)
+    }
+    const float inv = 1.0f / s;      // exact: s is a power of two
+#pragma unroll 4
+    for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = __float2half_rn(src[i] * inv);
+    if (threadIdx.x == 0) scale[t] = s;
+}
+
+// ---------------------------------------------------------------- tcgen05 primitives
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    // K-major, 128-byte swizzle: start >> 4, LBO 16 B (unused for swizzled K-major),
+    // SBO 1024 B (8-row atoms), version 1 (sm_100), layout type 2 (SWIZZLE_128B)
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = nt, M = 128
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int nt) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 8 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- decode of 8 weights
+template <int QT> struct TcFmt;
+template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34; };
+template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18; };
+template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20; };
+template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22; };
+template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144; };
+template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176; };
+
+// elements 8j .. 8j+7 of a 256-element row chunk (raw bytes `c`), the GGUF dequantization
+// of each format in fp32, rounded to fp16
+template <int QT>
+__device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
+    float v[8];
+    if constexpr (QT == MLQ_Q8_0) {
+        const uint8_t *bp = c + (j >> 2) * 34;
+        const int o = (j & 3) * 8;
+        const float d = f16_at(bp);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = d * (float)(int8_t)bp[2 + o + i];
+    } else if constexpr (QT == MLQ_Q4_0 || QT == MLQ_Q4_1 || QT == MLQ_Q5_0) {
+        constexpr int bb = QT == MLQ_Q4_0 ? 18 : QT == MLQ_Q4_1 ? 20 : 22;
+        constexpr int hdr = QT == MLQ_Q4_0 ? 2 : QT == MLQ_Q4_1 ? 4 : 6;
+        const uint8_t *bp = c + (j >> 2) * bb;
+        const int o = (j & 3) * 8;
+        const float d = f16_at(bp);
+        uint32_t qh = 0;
+        if constexpr (QT == MLQ_Q5_0) qh = bp[2] | (bp[3] << 8) | (bp[4] << 16) | ((uint32_t)bp[5] << 24);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = o + i;
+            int q = e < 16 ? (bp[hdr + e] & 0xF) : (bp[hdr + e - 16] >> 4);
+            if constexpr (QT == MLQ_Q4_0) v[i] = d * (float)(q - 8);
+            else if constexpr (QT == MLQ_Q4_1) v[i] = d * (float)q + f16_at(bp + 2);
+            else v[i] = d * (float)((q | (int)(((qh >> e) & 1u) << 4)) - 16);
+        }
+    } else {   // Q4_K, Q5_K: one 256-element super-block per chunk
+        const int sub = j >> 2, g = sub >> 1, l0 = (j & 3) * 8;
+        const uint8_t *sc = c + 4;
+        int s, m;
+        if (sub < 4) {
+            s = sc[sub] & 63;
+            m = sc[sub + 4] & 63;
+        } else {
+            s = (sc[sub + 4] & 0xF) | ((sc[sub - 4] >> 6) << 4);
+            m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
+        }
+        const float ds = f16_at(c) * (float)s, dm = f16_at(c + 2) * (float)m;
+        const uint8_t *qs = c + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int l = l0 + i;
+            int q = (sub & 1) ? (qs[l] >> 4) : (qs[l] & 0xF);
+            if constexpr (QT == MLQ_Q5_K) q += ((c[16 + l] >> sub) & 1) << 4;
+            v[i] = ds * (float)q - dm;
+        }
+    }
+    __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+    __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
+    uint4 r;
+    r.x = *reinterpret_cast<uint32_t *>(&h0);
+    r.y = *reinterpret_cast<uint32_t *>(&h1);
+    r.z = *reinterpret_cast<uint32_t *>(&h2);
+    r.w = *reinterpret_cast<uint32_t *>(&h3);
+    return r;
+}
+
+// byte offset of the 16-byte chunk (row r, K group j of 8) in a [rows][256] fp16 operand
+// stored as four 64-wide K atoms of `atom_bytes` each
+__device__ __forceinline__ uint32_t sw128_off(int r, int j, int atom_bytes) {
+    const int kb = j >> 3, c = j & 7;
+    return (uint32_t)(kb * atom_bytes + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+struct TcArgs {
+    const uint8_t *W;
+    const __half *xh;
+    const float *xs;
+    float *out;
+    int n_rows, K, M;
+    long long row_bytes;
+    int n_row_tiles;
+    int *status;
+};
+
+template <int QT, int NT>
+struct TcSmem {
+    static constexpr int a_bytes = 4 * kTcAtomBytes;                          // 64 KB
+    static constexpr int b_atom = NT * 128;
+    static constexpr int b_bytes = 4 * b_atom;                                // NT * 512
+    static constexpr int raw_bytes = kTcRows * TcFmt<QT>::chunk_bytes;
+    static constexpr int off_a = 0;
+    static constexpr int off_b = a_bytes;                                     // 2 stages
+    static constexpr int off_raw = off_b + 2 * b_bytes;                       // 2 stages
+    static constexpr int off_bar = (off_raw + 2 * raw_bytes + 15) / 16 * 16;
+    static constexpr int total = off_bar + 64 + 1024;                         // + alignment slack
+};
+
+template <int QT, int NT>
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
+    using S = TcSmem<QT, NT>;
+    extern __shared__ uint8_t smem_raw[];
+    // operand atoms must start on 1024-byte boundaries
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sa = smem + S::off_a;
+    uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + S::off_bar);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::off_bar + 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::off_bar + 16);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    constexpr int ncols = NT < 32 ? 32 : NT;
+    constexpr int chunk_bytes = TcFmt<QT>::chunk_bytes;
+    constexpr int pieces = chunk_bytes / 16;
+    const int tok0 = blockIdx.y * NT;
+    const int n_chunks = a.K / kTcKC;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(mma_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    uint32_t issued = 0, waited = 0;   // MMA groups committed (all threads) / seen complete (thread 0)
+    constexpr uint32_t idesc = umma_idesc_f16(NT);
+
+    // every committed MMA group has completed; thread 0 waits (bounded) and the verdict
+    // reaches all threads through the barrier, so control flow stays uniform
+    auto wait_mma = [&]() -> bool {
+        if (tid == 0 && !*abort_flag) {
+            while (waited < issued) {
+                if (!mbar_wait_bounded(mma_bar, waited & 1)) {
+                    *abort_flag = 1;
+                    atomicCAS(a.status, 0, DEV_ST_WAIT_FULL);
+                    break;
+                }
+                waited++;
+            }
+        }
+        __syncthreads();
+        return !*abort_flag;
+    };
+    // chunk ci of row tile rt: raw weights and activation atoms into stage st
+    auto issue_copies = [&](int rt, int ci, int st) {
+        const int r0 = rt * kTcRows;
+        uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
+        for (int p = tid; p < kTcRows * pieces; p += kTcThreads) {
+            const int r = p / pieces, i = p - r * pieces;
+            if (r0 + r < a.n_rows)
+                cp_async16(raw + r * chunk_bytes + 16 * i,
+                           a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
+        }
+        uint8_t *sb = smem + S::off_b + st * S::b_bytes;
+        for (int p = tid; p < NT * 32; p += kTcThreads) {
+            const int n = p >> 5, j = p & 31;
+            cp_async16(sb + sw128_off(n, j, S::b_atom), a.xh + (size_t)(tok0 + n) * a.K + (size_t)ci * kTcKC + 8 * j);
+        }
+        cp_async_commit();
+    };
+
+    for (int rt = blockIdx.x; rt < a.n_row_tiles && !*abort_flag; rt += gridDim.x) {
+        const int r0 = rt * kTcRows;
+        issue_copies(rt, 0, 0);
+        for (int ci = 0; ci < n_chunks; ci++) {
+            const int st = ci & 1;
+            // the previous chunk's MMAs read A and the other B stage: wait before reuse
+            if (!wait_mma()) break;
+            if (ci + 1 < n_chunks) issue_copies(rt, ci + 1, st ^ 1);
+            else cp_async_commit();
+            cp_async_wait<1>();
+            __syncthreads();
+            // decode this chunk's raw weights into the swizzled fp16 A operand
+            const uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
+            for (int p = tid; p < kTcRows * 32; p += kTcThreads) {
+                const int r = p >> 5, j = p & 31;
+                const uint4 h = (r0 + r < a.n_rows) ? deq8<QT>(raw + r * chunk_bytes, j) : make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4 *>(sa + sw128_off(r, j, kTcAtomBytes)) = h;
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sa), b0 = smem_u32(smem + S::off_b + st * S::b_bytes);
+#pragma unroll
+                for (int k = 0; k < kTcKC / 16; k++) {
+                    const int kb = k >> 2, k16 = k & 3;
+                    umma_f16(tmem, umma_desc_sw128(a0 + kb * kTcAtomBytes + k16 * 32),
+                             umma_desc_sw128(b0 + kb * S::b_atom + k16 * 32), idesc, (ci > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit(mma_bar);
+            }
+            issued++;
+        }
+        // epilogue: accumulators -> scaled fp32 outputs
+        if (!wait_mma()) break;
+        tc_fence_after();
+        {
+            const int q = warp & 3, half = warp >> 2;
+            const int row = r0 + 32 * q + (tid & 31);
+            constexpr int per = NT / 2;   // columns per warp
+#pragma unroll
+            for (int c0 = 0; c0 < per; c0 += 8) {
+                float v[8];
+                tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int t = tok0 + half * per + c0 + i;
+                    if (t < a.M && row < a.n_rows) a.out[(size_t)t * a.n_rows + row] = v[i] * a.xs[t];
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+    }
+    // drain: no copy or MMA may still target this CTA's memory when it exits
+    cp_async_wait<0>();
+    if (tid == 0) {   // one more bounded wait for MMAs still in flight after an abort
+        while (waited < issued && mbar_wait_bounded(mma_bar, waited & 1)) waited++;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- host side
+// per-(device, stream) fp16 activation buffer, grown on demand outside graph capture
+struct TcScratch { void *p = nullptr; size_t bytes = 0; };
+static std::mutex g_tc_mu;
+static std::map<std::pair<int, cudaStream_t>, TcScratch> g_tc_scratch;
+
+static void *tc_scratch(cudaStream_t s, size_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_tc_mu);
+    TcScratch &t = g_tc_scratch[std::make_pair(dev, s)];
+    if (t.bytes >= bytes) return t.p;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;   // no allocation inside a capture: the caller falls back
+    }
+    if (t.p) {
+        cudaStreamSynchronize(s);
+        cudaFree(t.p);
+    }
+    t.p = nullptr;
+    t.bytes = 0;
+    if (cudaMalloc(&t.p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        t.p = nullptr;
+        return nullptr;
+    }
+    t.bytes = bytes;
+    return t.p;
+}
+
+bool tc_supported(int qt, const uint8_t *W, int K, long long row_bytes) {
+    int cb = 0;
+    switch (qt) {
+        case MLQ_Q8_0: cb = TcFmt<MLQ_Q8_0>::chunk_bytes; break;
+        case MLQ_Q4_0: cb = TcFmt<MLQ_Q4_0>::chunk_bytes; break;
+        case MLQ_Q4_1: cb = TcFmt<MLQ_Q4_1>::chunk_bytes; break;
+        case MLQ_Q5_0: cb = TcFmt<MLQ_Q5_0>::chunk_bytes; break;
+        case MLQ_Q4_K: cb = TcFmt<MLQ_Q4_K>::chunk_bytes; break;
+        case MLQ_Q5_K: cb = TcFmt<MLQ_Q5_K>::chunk_bytes; break;
+        default: return false;
+    }
+    return K % kTcKC == 0 && cb % 16 == 0 && row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
+}
+
+template <int QT, int NT>
+static int launch_tc_t(const TcArgs &a, int n_tok_tiles, cudaStream_t s) {
+    using S = TcSmem<QT, NT>;
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemm_tc<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::total)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    int gx = env->num_sms / n_tok_tiles;
+    if (gx < 1) gx = 1;
+    if (gx > a.n_row_tiles) gx = a.n_row_tiles;
+    k_gemm_tc<QT, NT><<<dim3(gx, n_tok_tiles), kTcThreads, S::total, s>>>(a);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+template <int QT>
+static int launch_tc_q(const TcArgs &a, int NT, int n_tok_tiles, cudaStream_t s) {
+    if (NT == 16) return launch_tc_t<QT, 16>(a, n_tok_tiles, s);
+    if (NT == 32) return launch_tc_t<QT, 32>(a, n_tok_tiles, s);
+    return launch_tc_t<QT, 64>(a, n_tok_tiles, s);
+}
+
+// out [M][n_rows] = x [M][K] . W^T on the tensor cores; MLQ_ERR_UNSUPPORTED when the
+// format / shape / alignment is not covered (the caller then uses the dp4a kernels)
+int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s) {
+    const long long rb = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    if (!tc_supported(qt, W, K, rb) || M < 1) return MLQ_ERR_UNSUPPORTED;
+    const int NT = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    const int n_tok_tiles = (M + NT - 1) / NT;
+    const int Mp = n_tok_tiles * NT;
+    const size_t xh_bytes = ((size_t)Mp * K * sizeof(__half) + 255) & ~(size_t)255;
+    uint8_t *scr = (uint8_t *)tc_scratch(s, xh_bytes + (size_t)Mp * sizeof(float));
+    if (!scr) return MLQ_ERR_UNSUPPORTED;
+    __half *xh = (__half *)scr;
+    float *xs = (float *)(scr + xh_bytes);
+    k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K);
+    count_launch();
+    if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    TcArgs a{W, xh, xs, out, n_rows, K, M, rb, (n_rows + kTcRows - 1) / kTcRows, env->d_status};
+    switch (qt) {
+        case MLQ_Q8_0: return launch_tc_q<MLQ_Q8_0>(a, NT, n_tok_tiles, s);
+        case MLQ_Q4_0: return launch_tc_q<MLQ_Q4_0>(a, NT, n_tok_tiles, s);
+        case MLQ_Q4_1: return launch_tc_q<MLQ_Q4_1>(a, NT, n_tok_tiles, s);
+        case MLQ_Q5_0: return launch_tc_q<MLQ_Q5_0>(a, NT, n_tok_tiles, s);
+        case MLQ_Q4_K: return launch_tc_q<MLQ_Q4_K>(a, NT, n_tok_tiles, s);
+        case MLQ_Q5_K: return launch_tc_q<MLQ_Q5_K>(a, NT, n_tok_tiles, s);
+        default: return MLQ_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace mlq

@@ -499,8 +499,23 @@ static bool fits(int M, int K) {
     return gemv_layout(M, K, 0, 0).total + 2 * (kStageTarget + 64) <= kSmemBudget;
 }
 
+// batch size from which the tensor-core GEMM takes over (MLQ_TC_MIN_M overrides; 0 = never)
+static int tc_min_m() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_TC_MIN_M");
+        v = e ? atoi(e) : 16;
+        if (v < 0) v = 0;
+    }
+    return v;
+}
+
 template <int QT>
 static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
+    if (tc_min_m() > 0 && B >= tc_min_m()) {
+        const int rc = launch_gemm_tc(W, QT, x, out, n_rows, K, B, s);
+        if (rc != MLQ_ERR_UNSUPPORTED) return rc;
+    }
     if (B == 1) {
         const int rc = launch_q1<QT>(W, x, out, n_rows, K, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;

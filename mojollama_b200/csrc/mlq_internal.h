@@ -88,6 +88,8 @@ bool is_quant_type(int qt);
 int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int n_cols,
                   int B, size_t w_bytes, cudaStream_t s);
 int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStream_t s);
+// tensor-core GEMM (gemm_tc.cu); MLQ_ERR_UNSUPPORTED for formats/shapes it does not cover
+int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s);
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
 int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
 

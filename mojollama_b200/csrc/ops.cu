@@ -59,6 +59,7 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
     const float *xr = x + (size_t)blockIdx.x * n;
     float *orow = out + (size_t)blockIdx.x * n;
     float ss = 0.0f;
+#pragma unroll 8
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = xr[i];
         if (flags & 1) {
@@ -70,6 +71,7 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
     }
     ss = block_sum(ss, sh);
     const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll 8
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = xr[i];
         if (flags & 1) {

@@ -392,9 +392,10 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
     {
         // the vocabulary is the output projection's row count (the reference reads emb[token])
         const int V = a->out_nr_final;
-        std::vector<int> th;
+        std::vector<int> th(B, 0);   // host ids are needed only by the per-row Q4_K decode
         const void *emb = cs.weights(a->emb, embed_bytes(a->emb_quant, N, V));
-        if (!emb || !host_tokens(a->tokens, B, th)) rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG;
+        if (!emb || (a->emb_quant == MLQ_Q4_K && !compat && !host_tokens(a->tokens, B, th)))
+            rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG;
         MLQ_TRY(launch_embed(emb, a->emb_quant, d_tok, th.data(), x, B, N, V, s));
     }
     const float scale = 1.0f / sqrtf((float)HD);

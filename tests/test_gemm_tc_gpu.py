@@ -1,0 +1,78 @@
+"""GPU parity of the tensor-core (tcgen05) quantized GEMM that serves batches of >= 16
+tokens (the reference's *_batch_matmul math, cengine_batch_instr.c:68-534), against the
+fp64 oracle: weights dequantized exactly, x [M][K] fp32, out [M][N] fp32.
+
+Tolerance: relative L2 <= 1e-3 (the kernel rounds weights and activations once to fp16
+with a power-of-two scale per token; products and sums are fp32).  Covered: every format
+the tensor-core path takes, ragged row tiles (N not a multiple of 128), token counts that
+are not multiples of the token tile, several tiles of tokens, activations with a large
+dynamic range, and the reference-named batch entry points."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import formats as F
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+TC_FORMATS = [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.Q4_K, F.Q5_K]
+
+
+def _mm(lib, torch, w, qt, x, n, k):
+    m = x.shape[0]
+    dw = torch.from_numpy(w).cuda()
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    do = torch.empty(m * n, device="cuda")
+    rc = lib.mlq_matmul(ctypes.c_void_p(dw.data_ptr()), qt, ctypes.c_void_p(dx.data_ptr()),
+                        ctypes.c_void_p(do.data_ptr()), n, k, m)
+    assert rc == 0, lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    return do.cpu().numpy().reshape(m, n)
+
+
+@pytest.mark.parametrize("qt", TC_FORMATS, ids=lambda q: F.NAMES[q])
+@pytest.mark.parametrize("n,k,m", [(384, 512, 16), (200, 256, 17), (1000, 2048, 64), (130, 768, 100),
+                                   (256, 512, 256)])
+def test_tc_gemm_matches_oracle(cuda_device, qt, n, k, m):
+    import torch
+    rng = np.random.default_rng(qt * 1000 + n + m)
+    w = F.quantize(qt, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    got = _mm(cuda_device, torch, w, qt, x, n, k)
+    want = O.gemv(w, qt, x, n, k)
+    assert O.rel_l2(got, want) < TOL, O.rel_l2(got, want)
+
+
+def test_tc_gemm_per_token_scale(cuda_device):
+    """Tokens whose magnitudes differ by 1e8 (and a zero token) keep their own precision."""
+    import torch
+    n, k, m = 256, 512, 24
+    rng = np.random.default_rng(5)
+    w = F.quantize(F.Q8_0, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= np.logspace(-4, 4, m, dtype=np.float32)[:, None]
+    x[3] = 0.0
+    got = _mm(cuda_device, torch, w, F.Q8_0, x, n, k)
+    want = O.gemv(w, F.Q8_0, x, n, k)
+    for t in range(m):
+        assert O.rel_l2(got[t], want[t]) < TOL, t
+    assert np.all(got[3] == 0.0)
+
+
+@pytest.mark.parametrize("name,qt", [("q8_0", F.Q8_0), ("q4_0", F.Q4_0), ("q4_k", F.Q4_K)])
+def test_tc_through_batch_matmul_abi(cuda_device, name, qt):
+    """The reference-named x [B][nc] -> out [B][n_rows] entry with host buffers, B = 32."""
+    from mojollama_b200.kernels import load_kernels
+    kern = load_kernels().kern
+    n, k, b = 512, 1024, 32
+    rng = np.random.default_rng(qt)
+    w = F.quantize(qt, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = rng.standard_normal((b, k)).astype(np.float32)
+    out = np.zeros(b * n, np.float32)
+    getattr(kern, f"{name}_batch_matmul")(w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                                          x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n, k, b)
+    want = O.gemv(w, qt, x, n, k)
+    assert O.rel_l2(out.reshape(b, n), want) < TOL
