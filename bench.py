@@ -154,6 +154,21 @@ def run_reference(args, rank, world):
     return 0
 
 
+def gemv_traffic(fmt):
+    """DRAM bytes (read + write) per full 151936 x 2048 launch of the M=1 GEMV of `fmt`,
+    from the committed ncu summary profiles/gemv_traffic.md (rows `| FMT | ... | bytes |`),
+    or None when that format has not been captured."""
+    path = os.path.join(ROOT, "profiles", "gemv_traffic.md")
+    try:
+        for line in open(path):
+            cells = [c.strip() for c in line.strip().strip("|").split("|")]
+            if len(cells) >= 2 and cells[0] == fmt and cells[-1].replace(".", "").isdigit():
+                return int(float(cells[-1]))
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline_sample(seconds=12.0):
     """Reference C quant_matmul_omp on the host cores, bounded sample of the workload."""
     try:
@@ -209,14 +224,17 @@ def run_ours(args, rank, world, local_rank):
     outs = {qt: torch.empty(N_ROWS, device="cuda") for _, qt in FORMATS}
     torch.cuda.synchronize()
 
-    def step_dev(ev_pairs=None):
+    def step_dev(ev=None):
+        """one step; ev: {qt: [(start, end), ...]} gets a pair of events around each launch"""
         for name, qt in FORMATS:
-            if ev_pairs is not None and qt == 8:
-                ev_pairs[-1][0].record(stream)
+            if ev is not None:
+                pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev.setdefault(qt, []).append(pair)
+                pair[0].record(stream)
             rc = lib.mlq_matmul(ctypes.c_void_p(dev_w[qt].data_ptr()), qt, ctypes.c_void_p(x.data_ptr()),
                                 ctypes.c_void_p(outs[qt].data_ptr()), N_ROWS, K_COLS, 1)
-            if ev_pairs is not None and qt == 8:
-                ev_pairs[-1][1].record(stream)
+            if ev is not None:
+                pair[1].record(stream)
             if rc:
                 raise RuntimeError(lib.mlq_last_error_message())
 
@@ -234,18 +252,17 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     launches0 = lib.mlq_launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    q8_events = []
+    fmt_events = {}
     start.record(stream)
     for _ in range(args.steps):
-        q8_events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
-        step_dev(q8_events)
+        step_dev(fmt_events)
     end.record(stream)
     stream.synchronize()
     barrier()
     torch.cuda.synchronize()
     launches = lib.mlq_launch_count() - launches0
     ms = start.elapsed_time(end)
-    q8_ms = [a.elapsed_time(b) for a, b in q8_events]
+    fmt_ms = {qt: statistics.mean(a.elapsed_time(b) for a, b in pairs) for qt, pairs in fmt_events.items()}
     clk = clocks.stop()
 
     # e2e through the reference-named C-ABI with pinned host buffers
@@ -274,10 +291,12 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = e_start.elapsed_time(e_end)
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms, statistics.mean(q8_ms)], device="cuda")
+    t = torch.tensor([ms, e2e_ms] + [fmt_ms[qt] for _, qt in FORMATS], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, q8_avg = (float(v) for v in t.tolist())
+    vals = [float(v) for v in t.tolist()]
+    ms, e2e_ms = vals[0], vals[1]
+    fmt_ms = {qt: vals[2 + i] for i, (_, qt) in enumerate(FORMATS)}
 
     step_bytes = sum(alg_bytes(qt) for _, qt in FORMATS)
     value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
@@ -290,15 +309,10 @@ def run_ours(args, rank, world, local_rank):
     except Exception:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    q8_bytes = alg_bytes(8)
-    achieved = q8_bytes / (q8_avg / 1e3) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemv_q8_0_traffic.json")
-    if os.path.exists(tp):
-        try:
-            traffic = json.load(open(tp)).get("bytes_per_launch")
-        except Exception:
-            traffic = None
+    # the dominant kernel: the format whose launches take the largest share of the step
+    dom_name, dom_qt = max(FORMATS, key=lambda f: fmt_ms[f[1]])
+    achieved = alg_bytes(dom_qt) / (fmt_ms[dom_qt] / 1e3) / 1e9
+    traffic = gemv_traffic(dom_name)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -311,25 +325,15 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": K_COLS * 4 * len(FORMATS), "d2h_bytes_per_step": N_ROWS * 4 * len(FORMATS),
                 "api": "combined_engine.so quant_matmul_omp, pinned host x/out, resident weights"},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "hbm", "kernel": "k_gemv_q<Q8_0,1>", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": f"k_gemv_q1<{dom_name}> (M=1 GEMV)", "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                     "traffic": traffic, "peak_source": "measured" if peaks else "fallback"},
+                     "traffic": traffic, "algorithmic_bytes": alg_bytes(dom_qt),
+                     "share_of_step": round(fmt_ms[dom_qt] / sum(fmt_ms.values()), 3),
+                     "peak_source": "measured" if peaks else "fallback"},
         "clocks": clk,
     }
-    # per-format device GB/s (one extra timed pass, events around each launch)
-    per = {}
-    for name, qt in FORMATS:
-        evs = []
-        for _ in range(5):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            lib.mlq_matmul(ctypes.c_void_p(dev_w[qt].data_ptr()), qt, ctypes.c_void_p(x.data_ptr()),
-                           ctypes.c_void_p(outs[qt].data_ptr()), N_ROWS, K_COLS, 1)
-            b.record(stream)
-            evs.append((a, b))
-        stream.synchronize()
-        per[name] = round(alg_bytes(qt) / (statistics.median(a.elapsed_time(b) for a, b in evs) / 1e3) / 1e9, 1)
-    line["per_format_gbs"] = per
+    # per-format device GB/s from the same timed launches
+    line["per_format_gbs"] = {name: round(alg_bytes(qt) / (fmt_ms[qt] / 1e3) / 1e9, 1) for name, qt in FORMATS}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
     if not args.no_decode:
@@ -664,6 +668,33 @@ def decode_cpu_baseline(keep, b, caches, seconds):
         return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": f"failed: {e}"}
 
 
+def run_profile_tc(fmt: str, rows: int, m: int, launches: int = 3) -> int:
+    """Small case for ncu on the tensor-core GEMM: one format, rows x 2048 weights, M tokens,
+    two warm-up launches then `launches` more (weights ~143 MB for Q8_0 at 65536 rows)."""
+    import torch
+    from mojollama_b200 import core
+    from mojollama_b200 import gguf_quant as Q
+    qt = dict(FORMATS)[fmt]
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    rng = np.random.default_rng(qt)
+    base = Q.quantize(qt, (rng.standard_normal(DISTINCT * K_COLS) * 0.02).astype(np.float32))
+    w = np.tile(base, -(-rows // DISTINCT))[: rows * row_bytes(qt)]
+    wd = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+    x = torch.randn(m * K_COLS, device="cuda")
+    out = torch.empty(m * rows, device="cuda")
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    for _ in range(2 + launches):
+        rc = lib.mlq_matmul(ctypes.c_void_p(wd.data_ptr()), qt, ctypes.c_void_p(x.data_ptr()),
+                            ctypes.c_void_p(out.data_ptr()), rows, K_COLS, m)
+        assert rc == 0, lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_tc": fmt, "rows": rows, "cols": K_COLS, "m": m,
+                      "flops_per_launch": 2 * m * rows * K_COLS,
+                      "bytes_per_launch": rows * row_bytes(qt) + m * K_COLS * 4 + m * rows * 4}))
+    return 0
+
+
 def run_profile_case(fmt: str, rows: int, launches: int = 3) -> int:
     """Small single-kernel case for `ncu --set full`: one format, `rows` x 2048, M=1,
     two warm-up launches then `launches` more.  Default 65536 rows keeps every matrix
@@ -695,6 +726,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile", default=None, help="run the small single-kernel ncu case for FORMAT")
     ap.add_argument("--profile-rows", type=int, default=65536)
+    ap.add_argument("--profile-tc", default=None, help="small tensor-core GEMM case for ncu: FORMAT")
+    ap.add_argument("--profile-m", type=int, default=64)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -713,6 +746,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.profile:
         return run_profile_case(args.profile, args.profile_rows)
+    if args.profile_tc:
+        return run_profile_tc(args.profile_tc, args.profile_rows, args.profile_m)
     if args.decode_only:
         return run_decode_only(args)
     if args.decode_profile:

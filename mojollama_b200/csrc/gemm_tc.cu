@@ -26,6 +26,7 @@
 
 #include <map>
 #include <mutex>
+#include <vector>
 
 #include "formats.cuh"
 #include "mlq_internal.h"
@@ -197,6 +198,49 @@ __device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
     return r;
 }
 
+// Packed decode of one whole 32-element block (Q8_0 / Q4_0) into four 16-byte fp16 chunks.
+// An integer code c in 0..255 becomes the fp16 value 1024 + c by placing it under the
+// exponent byte 0x64 (PRMT); subtracting 1024 + bias (HSUB2) is exact, and the one HMUL2
+// by the block scale rounds the exact product once -- the same fp16 as rounding d*q.
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+__device__ __forceinline__ void bytes_to_h2(uint32_t u, __half2 bias, __half2 d, uint32_t &lo, uint32_t &hi) {
+    lo = h22u(__hmul2(__hsub2(u2h2(__byte_perm(u, 0x64646464u, 0x5140)), bias), d));
+    hi = h22u(__hmul2(__hsub2(u2h2(__byte_perm(u, 0x64646464u, 0x7362)), bias), d));
+}
+
+template <int QT>
+__device__ __forceinline__ void deq_block32(const uint8_t *bp, uint4 (&o)[4]) {
+    const __half2 d = __half2half2(*reinterpret_cast<const __half *>(bp));   // 2-byte aligned
+    if constexpr (QT == MLQ_Q8_0) {
+        uint32_t w[8];
+        load_words<8>(bp + 2, w);
+        const __half2 bias = u2h2(0x64806480u);   // 1152 = 1024 + 128
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            uint32_t a0, a1, b0, b1;
+            bytes_to_h2(w[i] ^ 0x80808080u, bias, d, a0, a1);
+            bytes_to_h2(w[i + 1] ^ 0x80808080u, bias, d, b0, b1);
+            o[i >> 1] = make_uint4(a0, a1, b0, b1);
+        }
+    } else {   // Q4_0: element j < 16 is the low nibble of qs[j], j >= 16 the high nibble of qs[j-16]
+        uint32_t w[4];
+        load_words<4>(bp + 2, w);
+        const __half2 bias = u2h2(0x64086408u);   // 1032 = 1024 + 8
+        uint32_t l[8], h[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            bytes_to_h2(w[i] & 0x0F0F0F0Fu, bias, d, l[2 * i], l[2 * i + 1]);
+            bytes_to_h2((w[i] >> 4) & 0x0F0F0F0Fu, bias, d, h[2 * i], h[2 * i + 1]);
+        }
+        o[0] = make_uint4(l[0], l[1], l[2], l[3]);
+        o[1] = make_uint4(l[4], l[5], l[6], l[7]);
+        o[2] = make_uint4(h[0], h[1], h[2], h[3]);
+        o[3] = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+}
+
 // byte offset of the 16-byte chunk (row r, K group j of 8) in a [rows][256] fp16 operand
 // stored as four 64-wide K atoms of `atom_bytes` each
 __device__ __forceinline__ uint32_t sw128_off(int r, int j, int atom_bytes) {
@@ -213,6 +257,12 @@ struct TcArgs {
     long long row_bytes;
     int n_row_tiles;
     int *status;
+    // split-K: work item w = (row tile w / n_splits, K slice w % n_splits of chunks_per_split
+    // chunks); with n_splits > 1 each item leaves its partial tile in part and the last item
+    // of a tile to finish (counters) adds the slices in order and writes the outputs
+    int n_splits, chunks_per_split;
+    float *part;
+    int *counters;
 };
 
 template <int QT, int NT>
@@ -238,12 +288,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
     uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + S::off_bar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::off_bar + 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::off_bar + 16);
+    volatile int *flag_last = reinterpret_cast<volatile int *>(smem + S::off_bar + 20);
     const int tid = threadIdx.x, warp = tid >> 5;
     constexpr int ncols = NT < 32 ? 32 : NT;
     constexpr int chunk_bytes = TcFmt<QT>::chunk_bytes;
     constexpr int pieces = chunk_bytes / 16;
     const int tok0 = blockIdx.y * NT;
     const int n_chunks = a.K / kTcKC;
+    (void)n_chunks;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -297,23 +349,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         cp_async_commit();
     };
 
-    for (int rt = blockIdx.x; rt < a.n_row_tiles && !*abort_flag; rt += gridDim.x) {
+    const int n_items = a.n_row_tiles * a.n_splits;
+    for (int wi = blockIdx.x; wi < n_items && !*abort_flag; wi += gridDim.x) {
+        const int rt = wi / a.n_splits, sp = wi - rt * a.n_splits;
         const int r0 = rt * kTcRows;
-        issue_copies(rt, 0, 0);
-        for (int ci = 0; ci < n_chunks; ci++) {
-            const int st = ci & 1;
+        const int c_begin = sp * a.chunks_per_split;
+        const int c_end = min(n_chunks, c_begin + a.chunks_per_split);
+        issue_copies(rt, c_begin, 0);
+        for (int ci = c_begin; ci < c_end; ci++) {
+            const int st = (ci - c_begin) & 1;
             // the previous chunk's MMAs read A and the other B stage: wait before reuse
             if (!wait_mma()) break;
-            if (ci + 1 < n_chunks) issue_copies(rt, ci + 1, st ^ 1);
+            if (ci + 1 < c_end) issue_copies(rt, ci + 1, st ^ 1);
             else cp_async_commit();
             cp_async_wait<1>();
             __syncthreads();
             // decode this chunk's raw weights into the swizzled fp16 A operand
             const uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
-            for (int p = tid; p < kTcRows * 32; p += kTcThreads) {
-                const int r = p >> 5, j = p & 31;
-                const uint4 h = (r0 + r < a.n_rows) ? deq8<QT>(raw + r * chunk_bytes, j) : make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4 *>(sa + sw128_off(r, j, kTcAtomBytes)) = h;
+            if constexpr (QT == MLQ_Q8_0 || QT == MLQ_Q4_0) {
+                constexpr int bb = QT == MLQ_Q8_0 ? 34 : 18;
+                for (int p = tid; p < kTcRows * 8; p += kTcThreads) {
+                    const int r = p >> 3, b = p & 7;
+                    uint4 o[4];
+                    if (r0 + r < a.n_rows) {
+                        deq_block32<QT>(raw + r * chunk_bytes + b * bb, o);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 4; c++) o[c] = make_uint4(0, 0, 0, 0);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; c++) *reinterpret_cast<uint4 *>(sa + sw128_off(r, 4 * b + c, kTcAtomBytes)) = o[c];
+                }
+            } else {
+                for (int p = tid; p < kTcRows * 32; p += kTcThreads) {
+                    const int r = p >> 5, j = p & 31;
+                    const uint4 h = (r0 + r < a.n_rows) ? deq8<QT>(raw + r * chunk_bytes, j) : make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(sa + sw128_off(r, j, kTcAtomBytes)) = h;
+                }
             }
             fence_async_smem();
             tc_fence_before();
@@ -325,7 +397,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                 for (int k = 0; k < kTcKC / 16; k++) {
                     const int kb = k >> 2, k16 = k & 3;
                     umma_f16(tmem, umma_desc_sw128(a0 + kb * kTcAtomBytes + k16 * 32),
-                             umma_desc_sw128(b0 + kb * S::b_atom + k16 * 32), idesc, (ci > 0 || k > 0) ? 1u : 0u);
+                             umma_desc_sw128(b0 + kb * S::b_atom + k16 * 32), idesc,
+                             (ci > c_begin || k > 0) ? 1u : 0u);
                 }
                 umma_commit(mma_bar);
             }
@@ -334,10 +407,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         // epilogue: accumulators -> scaled fp32 outputs
         if (!wait_mma()) break;
         tc_fence_after();
-        {
-            const int q = warp & 3, half = warp >> 2;
-            const int row = r0 + 32 * q + (tid & 31);
-            constexpr int per = NT / 2;   // columns per warp
+        const int q = warp & 3, half = warp >> 2;
+        const int rl = 32 * q + (tid & 31), row = r0 + rl;
+        constexpr int per = NT / 2;   // columns per warp
+        if (a.n_splits == 1) {
 #pragma unroll
             for (int c0 = 0; c0 < per; c0 += 8) {
                 float v[8];
@@ -348,9 +421,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                     if (t < a.M && row < a.n_rows) a.out[(size_t)t * a.n_rows + row] = v[i] * a.xs[t];
                 }
             }
+            tc_fence_before();
+            __syncthreads();
+        } else {
+            // partial tile [NT][128] of this K slice; the last slice to land reduces in order
+            const size_t tile = (size_t)rt * gridDim.y + blockIdx.y;
+            float *pt = a.part + (tile * a.n_splits + sp) * (size_t)(NT * kTcRows);
+#pragma unroll
+            for (int c0 = 0; c0 < per; c0 += 8) {
+                float v[8];
+                tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+#pragma unroll
+                for (int i = 0; i < 8; i++) pt[(size_t)(half * per + c0 + i) * kTcRows + rl] = v[i];
+            }
+            tc_fence_before();
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) *flag_last = (atomicAdd(a.counters + tile, 1) == a.n_splits - 1) ? 1 : 0;
+            __syncthreads();
+            if (*flag_last) {
+                __threadfence();
+                const float *p0 = a.part + tile * a.n_splits * (size_t)(NT * kTcRows);
+                for (int c = half * per; c < half * per + per; c++) {
+                    float acc = 0.0f;
+                    for (int k = 0; k < a.n_splits; k++) acc += __ldcg(p0 + ((size_t)k * NT + c) * kTcRows + rl);
+                    const int t = tok0 + c;
+                    if (t < a.M && row < a.n_rows) a.out[(size_t)t * a.n_rows + row] = acc * a.xs[t];
+                }
+                if (tid == 0) a.counters[tile] = 0;
+            }
+            __syncthreads();
         }
-        tc_fence_before();
-        __syncthreads();
     }
     // drain: no copy or MMA may still target this CTA's memory when it exits
     cp_async_wait<0>();
@@ -366,10 +467,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
 }
 
 // ---------------------------------------------------------------- host side
-// per-(device, stream) fp16 activation buffer, grown on demand outside graph capture
+// per-(device, stream) fp16 activation / split-K buffer, grown on demand outside graph
+// capture.  A grown-out buffer is retired, not freed: a captured graph may still hold its
+// address.  Retired buffers are freed with the graphs (forget_tc_scratch, after the
+// plans and their graphs are destroyed).
 struct TcScratch { void *p = nullptr; size_t bytes = 0; };
 static std::mutex g_tc_mu;
 static std::map<std::pair<int, cudaStream_t>, TcScratch> g_tc_scratch;
+static std::vector<void *> g_tc_retired;
+
+void forget_tc_scratch() {
+    std::lock_guard<std::mutex> lk(g_tc_mu);
+    cudaDeviceSynchronize();
+    for (auto &kv : g_tc_scratch)
+        if (kv.second.p) cudaFree(kv.second.p);
+    for (void *p : g_tc_retired) cudaFree(p);
+    g_tc_scratch.clear();
+    g_tc_retired.clear();
+}
 
 static void *tc_scratch(cudaStream_t s, size_t bytes) {
     int dev = 0;
@@ -382,10 +497,7 @@ static void *tc_scratch(cudaStream_t s, size_t bytes) {
         cudaGetLastError();
         return nullptr;   // no allocation inside a capture: the caller falls back
     }
-    if (t.p) {
-        cudaStreamSynchronize(s);
-        cudaFree(t.p);
-    }
+    if (t.p) g_tc_retired.push_back(t.p);
     t.p = nullptr;
     t.bytes = 0;
     if (cudaMalloc(&t.p, bytes) != cudaSuccess) {
@@ -424,7 +536,7 @@ static int launch_tc_t(const TcArgs &a, int n_tok_tiles, cudaStream_t s) {
     }
     int gx = env->num_sms / n_tok_tiles;
     if (gx < 1) gx = 1;
-    if (gx > a.n_row_tiles) gx = a.n_row_tiles;
+    if (gx > a.n_row_tiles * a.n_splits) gx = a.n_row_tiles * a.n_splits;
     k_gemm_tc<QT, NT><<<dim3(gx, n_tok_tiles), kTcThreads, S::total, s>>>(a);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
@@ -445,17 +557,35 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     const int NT = M <= 16 ? 16 : M <= 32 ? 32 : 64;
     const int n_tok_tiles = (M + NT - 1) / NT;
     const int Mp = n_tok_tiles * NT;
-    const size_t xh_bytes = ((size_t)Mp * K * sizeof(__half) + 255) & ~(size_t)255;
-    uint8_t *scr = (uint8_t *)tc_scratch(s, xh_bytes + (size_t)Mp * sizeof(float));
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    // split K over CTAs when the row tiles alone cannot fill the SMs
+    const int n_row_tiles = (n_rows + kTcRows - 1) / kTcRows, n_chunks = K / kTcKC;
+    int n_splits = 1;
+    if (n_row_tiles * n_tok_tiles < env->num_sms) {
+        n_splits = env->num_sms / (n_row_tiles * n_tok_tiles);
+        if (n_splits > n_chunks) n_splits = n_chunks;
+        if (n_splits < 1) n_splits = 1;
+    }
+    const int cps = (n_chunks + n_splits - 1) / n_splits;
+    n_splits = (n_chunks + cps - 1) / cps;
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t xh_bytes = al((size_t)Mp * K * sizeof(__half));
+    const size_t xs_bytes = al((size_t)Mp * sizeof(float));
+    const size_t n_tiles = (size_t)n_row_tiles * n_tok_tiles;
+    const size_t cnt_bytes = n_splits > 1 ? al(n_tiles * sizeof(int)) : 0;
+    const size_t part_bytes = n_splits > 1 ? n_tiles * n_splits * NT * kTcRows * sizeof(float) : 0;
+    uint8_t *scr = (uint8_t *)tc_scratch(s, xh_bytes + xs_bytes + cnt_bytes + part_bytes);
     if (!scr) return MLQ_ERR_UNSUPPORTED;
     __half *xh = (__half *)scr;
     float *xs = (float *)(scr + xh_bytes);
+    int *counters = n_splits > 1 ? (int *)(scr + xh_bytes + xs_bytes) : nullptr;
+    float *part = n_splits > 1 ? (float *)(scr + xh_bytes + xs_bytes + cnt_bytes) : nullptr;
+    if (counters && !MLQ_CUDA(cudaMemsetAsync(counters, 0, n_tiles * sizeof(int), s))) return MLQ_ERR_CUDA;
     k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K);
     count_launch();
     if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
-    const LaunchEnv *env = launch_env();
-    if (!env) return MLQ_ERR_NO_DEVICE;
-    TcArgs a{W, xh, xs, out, n_rows, K, M, rb, (n_rows + kTcRows - 1) / kTcRows, env->d_status};
+    TcArgs a{W, xh, xs, out, n_rows, K, M, rb, n_row_tiles, env->d_status, n_splits, cps, part, counters};
     switch (qt) {
         case MLQ_Q8_0: return launch_tc_q<MLQ_Q8_0>(a, NT, n_tok_tiles, s);
         case MLQ_Q4_0: return launch_tc_q<MLQ_Q4_0>(a, NT, n_tok_tiles, s);

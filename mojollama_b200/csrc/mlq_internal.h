@@ -155,6 +155,7 @@ int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_
 size_t embed_bytes(int emb_quant, int N, int V);
 bool host_tokens(const int *tokens, int B, std::vector<int> &out);
 void forget_kv_mirrors();
+void forget_tc_scratch();
 int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s);
 
 }  // namespace mlq

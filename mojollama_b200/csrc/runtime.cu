@@ -471,6 +471,7 @@ int mlq_cache_clear(void) {
     if (!c) return mlq_last_error();
     mlq_forget_model_plans();
     forget_kv_mirrors();
+    forget_tc_scratch();
     cudaStreamSynchronize(c->stream);
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto &kv : g_cache[c->device]) cudaFree(kv.second.dev);
