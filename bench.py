@@ -11,7 +11,13 @@ value     device-resident (weights and x in HBM), CUDA events on the library str
 e2e       through the reference-named C-ABI (quant_matmul_omp of combined_engine.so)
           with pinned HOST x/out: H2D of x and D2H of out inside the timed region
           (weights resident after their first use, as the reference's are loaded once).
-roofline  the dominant kernel (Q8_0 GEMV) timed per launch with CUDA events.
+roofline  the dominant kernel (the format whose GEMV takes the largest share of the step),
+          each launch timed with CUDA events inside the timed region.
+decode    config 1 (TinyLlama-1.1B shape, Q8_0, B=4) through batch_forward: tok/s device
+          resident and end to end, with the reference C engine's batch_forward on the host
+          cores as its CPU baseline (N = 1 only).
+moe_ep    config 3's MoE FFN stack (48 layers, 128 experts top-8) with the experts split over
+          the N GPUs and NCCL all-to-all dispatch/combine: tok/s (weak scaling).
 cpu_baseline  the reference C engine (compiled from its own sources into oracle/_ref)
           on the host cores, on the same weights (MXFP4 re-encoded in the reference's
           own layout), with all host threads.
@@ -302,6 +308,8 @@ def run_ours(args, rank, world, local_rank):
     value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
     e2e_value = world * step_bytes * args.steps / (e2e_ms / 1e3) / 1e9
     if rank != 0:
+        if not args.no_moe_ep:
+            run_moe_ep(torch, lib, rank, world)   # every rank takes part in the collectives
         return 0
     peaks = {}
     try:
@@ -336,9 +344,11 @@ def run_ours(args, rank, world, local_rank):
     line["per_format_gbs"] = {name: round(alg_bytes(qt) / (fmt_ms[qt] / 1e3) / 1e9, 1) for name, qt in FORMATS}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
-    if not args.no_decode:
+    if not args.no_decode and world == 1:
         line["decode"] = run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                     cpu_seconds=args.cpu_seconds)
+    if not args.no_moe_ep:
+        line["moe_ep"] = run_moe_ep(torch, lib, rank, world)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -366,6 +376,78 @@ def run_decode_profile(args):
     for kv in caches:
         kv.free()
     return 0
+
+
+# ------------------------------------------------------------------------------ MoE expert parallelism
+# BASELINE config 3's MoE FFN: 48 layers, d_model 2048, 128 experts, softmax top-8 with
+# renormalised weights, expert FFN 768, gate/up Q4_K and down Q6_K; the experts are split
+# over the ranks (expert parallelism), the router replicated.  Tokens per rank fixed (weak
+# scaling); each layer runs on the same N(0,1) token rows so the routing stays the one of
+# the N(0,1)-scaled router (values are synthetic; the expert blocks are random bytes with
+# small fp16 scales).
+MOE = dict(L=48, E=128, k=8, N=2048, FF=768, gq=12, uq=12, dq=14)
+
+
+def _random_kquant(torch, qt, n_blocks, gen):
+    """random K-quant blocks on the device with a small fp16 super-block scale (1/1024) and
+    dmin 0: finite, bounded weights for timing"""
+    bb = {12: 144, 14: 210}[qt]
+    w = torch.randint(0, 256, (n_blocks, bb), dtype=torch.uint8, device="cuda", generator=gen)
+    if qt == 12:
+        w[:, 0], w[:, 1], w[:, 2], w[:, 3] = 0x00, 0x14, 0x00, 0x00
+    else:
+        w[:, 208], w[:, 209] = 0x00, 0x14
+    return w.reshape(-1)
+
+
+def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None):
+    import torch.distributed as dist
+    from mojollama_b200.ep import EPMoELayer, row_bytes as rbytes
+    c = dict(MOE)
+    L = layers or c["L"]
+    E, k, N, FF = c["E"], c["k"], c["N"], c["FF"]
+    el = E // world
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    rgen = torch.Generator(device="cuda").manual_seed(99)   # same router on every rank
+    layer_objs = []
+    exp_bytes = FF * rbytes(c["gq"], N) * 2 + N * rbytes(c["dq"], FF)
+    for _ in range(L):
+        g = _random_kquant(torch, c["gq"], el * FF * N // 256, gen)
+        u = _random_kquant(torch, c["uq"], el * FF * N // 256, gen)
+        d = _random_kquant(torch, c["dq"], el * N * FF // 256, gen)
+        router = torch.randn(E, N, device="cuda", generator=rgen) * 0.02
+        layer_objs.append(EPMoELayer(rank, world, E, k, N, FF, c["gq"], c["uq"], c["dq"], g, u, d, router,
+                                     renorm=True))
+    x = torch.randn(tokens, N, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7 + rank))
+
+    def step():
+        y = x
+        for lay in layer_objs:
+            y = lay.forward(x, residual=x)
+        return y
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        out = step()
+    b.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = torch.tensor([a.elapsed_time(b)], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    t = float(ms.item()) / steps
+    finite = bool(torch.isfinite(out).all().item())
+    return {"workload": f"config-3 MoE FFN stack: {L} layers, {E} experts top-{k} (renormalised), FF {FF}, "
+                        f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), NCCL all-to-all",
+            "tokens_per_rank": tokens, "tok_s": round(world * tokens / (t / 1e3), 1), "ms_per_step": round(t, 3),
+            "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite}
 
 
 SWEEP_SHAPES = [(2048, 2048), (5632, 2048), (2880, 2880), (151936, 2048)]
@@ -425,6 +507,30 @@ def run_sweep(args):
             del dev
             torch.cuda.empty_cache()
     print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_moe_ep_only(args, rank, world, local_rank):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from mojollama_b200 import core
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        lib = core()
+        assert lib.mlq_init(local_rank) == 0
+        lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        res = run_moe_ep(torch, lib, rank, world, tokens=args.moe_tokens, steps=args.moe_steps,
+                         warmup=args.moe_warmup, layers=args.moe_layers)
+        if rank == 0:
+            print(json.dumps({"moe_ep": res, "n_gpus": world}), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
     return 0
 
 
@@ -737,6 +843,12 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-1 model decode section")
     ap.add_argument("--decode-only", action="store_true", help="run only the config-1 model decode section")
     ap.add_argument("--decode-profile", action="store_true", help="small decode case for an ncu launch list")
+    ap.add_argument("--no-moe-ep", action="store_true", help="skip the config-3 expert-parallel MoE section")
+    ap.add_argument("--moe-ep-only", action="store_true", help="run only the expert-parallel MoE section")
+    ap.add_argument("--moe-layers", type=int, default=None)
+    ap.add_argument("--moe-tokens", type=int, default=16)
+    ap.add_argument("--moe-steps", type=int, default=5)
+    ap.add_argument("--moe-warmup", type=int, default=3)
     ap.add_argument("--profile-steps", type=int, default=3)
     ap.add_argument("--sweep", action="store_true", help="config-2 sweep (formats x shapes x M), one JSON object")
     ap.add_argument("--sweep-m", default=None, help="comma-separated M values for --sweep")
@@ -752,6 +864,8 @@ def main():
         return run_decode_only(args)
     if args.decode_profile:
         return run_decode_profile(args)
+    if args.moe_ep_only:
+        return run_moe_ep_only(args, rank, world, local_rank)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":

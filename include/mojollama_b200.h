@@ -206,6 +206,23 @@ typedef struct {
 } MlqQwen36Args;
 int mlq_qwen36_batch_forward(const MlqQwen36Args *args);
 
+/* ---- expert parallelism (device pointers; the exchanges are the caller's collectives) ----
+   A rank owns experts [rank*experts_per_rank, (rank+1)*experts_per_rank).
+   mlq_ep_dispatch: idx [T][k] global expert ids -> counts[world] rows per destination rank,
+     pos[T*k] row of slot t*k+i in the send buffer (grouped by destination, slot order kept),
+     send_x [T*k][N] token rows, send_eid [T*k] local expert id at the destination (world <= 8).
+   mlq_moe_rows: y[r] = down_e(silu(clamp(gate_e x_r, +-80)) * up_e x_r), e = eid[r] < n_experts,
+     expert tensors [n_experts][rows][cols] at the given byte strides; rows are grouped by
+     expert on the device and each active expert is streamed once (grouped GEMV).
+   mlq_ep_combine: out[t] = residual[t] + sum_i w[t][i] * recv_y[pos[t*k+i]] (residual may be NULL). */
+int mlq_ep_dispatch(const int *idx, int T, int k, int experts_per_rank, int world, const float *x, int N, int *counts,
+                    int *pos, float *send_x, int *send_eid);
+int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp, long long gstride,
+                 long long ustride, long long dstride, int n_experts, const int *eid, int R, int n_ff, int N,
+                 const float *x, float *y);
+int mlq_ep_combine(const float *recv_y, const int *pos, const float *w, int T, int k, int N, const float *residual,
+                   float *out);
+
 /* ---- decode attention (one query per sequence), fp32 KV ---- */
 /* flat KV k/v [seq_len][n_kv_head*head_dim] (gqa_attention.c:93, cengine_batch_instr.c:141);
    head h uses KV head h / (n_head / n_kv_head); window > 0 attends the last `window`

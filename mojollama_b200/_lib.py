@@ -65,6 +65,10 @@ def core() -> ctypes.CDLL:
     so.mlq_moe_ffn.argtypes = [_vp, _ci, _vp, _vp, _ci]
     so.mlq_forget_model_plans.restype = None
     so.mlq_sizeof_bc.restype = ctypes.c_size_t
+    so.mlq_ep_dispatch.argtypes = [_vp, _ci, _ci, _ci, _ci, _vp, _ci, _vp, _vp, _vp, _vp]
+    so.mlq_moe_rows.argtypes = [_ci, _ci, _ci, _vp, _vp, _vp, ctypes.c_longlong, ctypes.c_longlong,
+                                ctypes.c_longlong, _ci, _vp, _ci, _ci, _ci, _vp, _vp]
+    so.mlq_ep_combine.argtypes = [_vp, _vp, _vp, _ci, _ci, _ci, _vp, _vp]
     so.mlq_attn_decode_flat.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
     so.mlq_attn_decode_paged.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _ci, _vp]
     so.mlq_page_table_init.argtypes = [_vp, _ci, _ci, _ci, _ci, _ci]

@@ -1,0 +1,201 @@
+// Expert-parallel MoE building blocks (the MoE FFN of qwen36_batch_forward / moe_ffn,
+// cengine_batch_instr.c:591-665 and :1113-1207, with the experts split over ranks).
+//
+// A rank owns experts [rank * E_local, (rank + 1) * E_local).  For T local tokens with
+// top-k routing (idx [T][k] global expert ids, w [T][k]):
+//   dispatch: slot s = t*k + i goes to rank idx[s] / E_local; the send buffer groups slots
+//     by destination rank, and inside one destination keeps slot order (stable, so the
+//     result does not depend on thread timing); it carries the token row x[t] and the
+//     destination's local expert id;
+//   experts:  every received row r is run through its one expert (no weight):
+//     y[r] = down_e(silu(clamp(gate_e x_r)) * up_e x_r);
+//   combine:  the rows come back in send order; out[t] = residual[t] + sum_i w[t][i] *
+//     y[pos[t*k + i]], i = 0..k-1 in order.
+// The exchanges themselves (all-to-all of counts, rows and ids) are NCCL collectives issued
+// by the host (mojollama_b200/ep.py).
+#include <cuda_runtime.h>
+
+#include "mlq_internal.h"
+
+namespace mlq {
+
+constexpr int kEpThreads = 1024;
+
+// one CTA: counts[world], pos[T*k], send_eid[T*k] (stable by destination, then slot)
+__global__ void __launch_bounds__(kEpThreads) k_ep_plan(const int *__restrict__ idx, int S, int e_local, int world,
+                                                        int *__restrict__ counts, int *__restrict__ pos,
+                                                        int *__restrict__ send_eid) {
+    __shared__ int warp_cnt[kEpThreads / 32][8];
+    __shared__ int base[8];        // running start of each destination for the current chunk
+    __shared__ int total[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    // pass 1: totals per destination
+    if (tid < 8) total[tid] = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < S; c0 += blockDim.x) {
+        const int s = c0 + tid;
+        const int d = s < S ? idx[s] / e_local : -1;
+        for (int r = 0; r < world; r++) {
+            const unsigned m = __ballot_sync(0xffffffffu, d == r);
+            if (lane == 0 && m) atomicAdd(&total[r], __popc(m));
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int r = 0; r < world; r++) {
+            base[r] = acc;
+            counts[r] = total[r];
+            acc += total[r];
+        }
+    }
+    __syncthreads();
+    // pass 2: positions, chunk by chunk in slot order
+    for (int c0 = 0; c0 < S; c0 += blockDim.x) {
+        const int s = c0 + tid;
+        const int g = s < S ? idx[s] : 0;
+        const int d = s < S ? g / e_local : -1;
+        int my_rank_in_warp = 0;
+        for (int r = 0; r < world; r++) {
+            const unsigned m = __ballot_sync(0xffffffffu, d == r);
+            if (d == r) my_rank_in_warp = __popc(m & ((1u << lane) - 1u));
+            if (lane == 0) warp_cnt[warp][r] = __popc(m);
+        }
+        __syncthreads();
+        if (d >= 0) {
+            int before = base[d] + my_rank_in_warp;
+            for (int w2 = 0; w2 < warp; w2++) before += warp_cnt[w2][d];
+            pos[s] = before;
+            send_eid[before] = g - d * e_local;
+        }
+        __syncthreads();
+        if (tid < world) {
+            int add = 0;
+            for (int w2 = 0; w2 < nw; w2++) add += warp_cnt[w2][tid];
+            base[tid] += add;
+        }
+        __syncthreads();
+    }
+}
+
+// send_x[pos[t*k + i]] = x[t]
+__global__ void k_ep_gather(const float *__restrict__ x, const int *__restrict__ pos, int k, int N,
+                            float *__restrict__ send_x) {
+    const int s = blockIdx.x;
+    const int t = s / k;
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * N);
+    float4 *dst = reinterpret_cast<float4 *>(send_x + (size_t)pos[s] * N);
+    for (int i = threadIdx.x; i < N / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// out[t] = residual[t] + sum_i w[t][i] * y[pos[t*k + i]]   (i in order)
+__global__ void k_ep_combine(const float *__restrict__ y, const int *__restrict__ pos, const float *__restrict__ w,
+                             int k, int N, const float *__restrict__ residual, float *__restrict__ out) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+        float acc = residual ? residual[(size_t)t * N + c] : 0.0f;
+        for (int i = 0; i < k; i++) acc = fmaf(w[t * k + i], y[(size_t)pos[t * k + i] * N + c], acc);
+        out[(size_t)t * N + c] = acc;
+    }
+}
+
+}  // namespace mlq
+
+using namespace mlq;
+
+extern "C" {
+
+int mlq_ep_dispatch(const int *idx, int T, int k, int experts_per_rank, int world, const float *x, int N, int *counts,
+                    int *pos, float *send_x, int *send_eid) {
+    if (!idx || !x || !counts || !pos || !send_x || !send_eid || T <= 0 || k <= 0 || experts_per_rank <= 0 ||
+        world <= 0 || world > 8 || N <= 0 || N % 4) {
+        set_error(MLQ_ERR_ARG, "ep_dispatch: bad arguments (world 1..8, N %% 4 == 0)");
+        return MLQ_ERR_ARG;
+    }
+    if (!is_device_ptr(idx) || !is_device_ptr(x) || !is_device_ptr(send_x)) {
+        set_error(MLQ_ERR_ARG, "ep_dispatch: device pointers only");
+        return MLQ_ERR_ARG;
+    }
+    cudaStream_t s = stream();
+    const int S = T * k;
+    k_ep_plan<<<1, kEpThreads, 0, s>>>(idx, S, experts_per_rank, world, counts, pos, send_eid);
+    k_ep_gather<<<S, 128, 0, s>>>(x, pos, k, N, send_x);
+    count_launch(2);
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int mlq_ep_combine(const float *recv_y, const int *pos, const float *w, int T, int k, int N, const float *residual,
+                   float *out) {
+    if (!recv_y || !pos || !w || !out || T <= 0 || k <= 0 || N <= 0) {
+        set_error(MLQ_ERR_ARG, "ep_combine: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    cudaStream_t s = stream();
+    k_ep_combine<<<T, 256, 0, s>>>(recv_y, pos, w, k, N, residual, out);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// y[r] = down_e(silu(clamp(gate_e x_r, +-80)) * up_e x_r) for the local expert e = eid[r]
+// (0 <= e < n_experts); expert tensors are [n_experts][rows][cols] at the given byte
+// strides (device memory).  Rows are grouped by expert on the device (stable order) and
+// every active expert's three matrices are streamed once for all of its rows.
+int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp, long long gstride,
+                 long long ustride, long long dstride, int n_experts, const int *eid, int R, int n_ff, int N,
+                 const float *x, float *y) {
+    if (R < 0 || !eid || !x || !y || !gexp || !uexp || !dexp || n_ff <= 0 || N <= 0 || n_experts <= 0) {
+        set_error(MLQ_ERR_ARG, "moe_rows: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    if (R == 0) return MLQ_OK;
+    const int tg = grouped_tiles_per_expert(gqt, n_ff, N), tu = grouped_tiles_per_expert(uqt, n_ff, N);
+    const int td = grouped_tiles_per_expert(dqt, N, n_ff);
+    if (!tg || !tu || !td) {
+        set_error(MLQ_ERR_TYPE, "moe_rows: expert types %d/%d/%d", gqt, uqt, dqt);
+        return MLQ_ERR_TYPE;
+    }
+    const int chunks = (R + 7) / 8 + (n_experts < R ? n_experts : R);
+    const int tgu = tg > tu ? tg : tu;
+    CallScope cs;
+    int *offs = (int *)cs.scratch(sizeof(int) * (3 * (size_t)n_experts + 2));
+    int *spos = (int *)cs.scratch(sizeof(int) * (size_t)R);
+    int *nitem = (int *)cs.scratch(sizeof(int) * 4);
+    void *items_gu = cs.scratch(16 * (size_t)chunks * tgu);
+    void *items_d = cs.scratch(16 * (size_t)chunks * (td > tu ? td : tu));
+    float *xs = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
+    float *g = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
+    float *u = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
+    float *ys = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
+    if (cs.failed) return cs.finish();
+    cudaStream_t s = stream();
+    // gate and up share one item list when their tilings agree (the usual case: one type)
+    int rc = MLQ_OK;
+    if (tg == tu) {
+        rc = launch_group_plan(eid, R, n_experts, tg, td, offs, spos, items_gu, items_d, nitem, s);
+        if (rc == MLQ_OK) rc = launch_rows_permute(x, spos, R, N, 1, xs, s);
+        if (rc == MLQ_OK)
+            rc = launch_grouped(gqt, (const uint8_t *)gexp, gstride, items_gu, nitem, chunks * tg, xs, g, n_ff, N, s);
+        if (rc == MLQ_OK)
+            rc = launch_grouped(uqt, (const uint8_t *)uexp, ustride, items_gu, nitem, chunks * tu, xs, u, n_ff, N, s);
+    } else {
+        rc = launch_group_plan(eid, R, n_experts, tg, tu, offs, spos, items_gu, items_d, nitem, s);
+        if (rc == MLQ_OK) rc = launch_rows_permute(x, spos, R, N, 1, xs, s);
+        if (rc == MLQ_OK)
+            rc = launch_grouped(gqt, (const uint8_t *)gexp, gstride, items_gu, nitem, chunks * tg, xs, g, n_ff, N, s);
+        if (rc == MLQ_OK)
+            rc = launch_grouped(uqt, (const uint8_t *)uexp, ustride, items_d, nitem + 1, chunks * tu, xs, u, n_ff, N, s);
+        if (rc == MLQ_OK) rc = launch_group_plan(eid, R, n_experts, td, td, offs, spos, items_d, items_d, nitem, s);
+    }
+    if (rc == MLQ_OK) rc = launch_swiglu(g, g, u, (long long)R * n_ff, s);
+    if (rc == MLQ_OK)
+        rc = launch_grouped(dqt, (const uint8_t *)dexp, dstride, items_d, nitem + 1, chunks * td, g, ys, N, n_ff, s);
+    if (rc == MLQ_OK) rc = launch_rows_permute(ys, spos, R, N, 0, y, s);
+    if (rc != MLQ_OK) {
+        cs.failed = true;
+        cs.finish();
+        return rc;
+    }
+    return cs.finish();
+}
+
+}  // extern "C"

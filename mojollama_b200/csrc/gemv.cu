@@ -596,6 +596,320 @@ int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_ro
     }
 }
 
+// ------------------------------------------------------------------------------ grouped experts
+// Grouped expert GEMV: rows sorted by expert; every active expert's matrix is streamed once
+// for all of its rows (up to 8 per pass).  Work items (expert e, first sorted row m0, row
+// count mc <= 8, row tile t) are listed expert-major; a CTA takes a contiguous range of
+// items, so it re-encodes its activation rows only when (e, m0) changes.  Tiles are the
+// same contiguous byte ranges as in k_gemv_q, at base + e * estride.
+struct GroupItem { int e, m0, mc, tile; };
+
+// Item it of a warp's range, fetched 32 at a time (lane i loads item base + i) and
+// broadcast with shuffles: one global round trip per 32 items.  Call warp-uniformly.
+struct ItemFetcher {
+    GroupItem mine;
+    __device__ __forceinline__ GroupItem get(const GroupItem *items, int i0, int n, int it, int lane) {
+        if ((it & 31) == 0) mine = (it + lane < n) ? items[i0 + it + lane] : GroupItem{0, 0, 0, 0};
+        const int src = it & 31;
+        return GroupItem{__shfl_sync(0xffffffffu, mine.e, src), __shfl_sync(0xffffffffu, mine.m0, src),
+                         __shfl_sync(0xffffffffu, mine.mc, src), __shfl_sync(0xffffffffu, mine.tile, src)};
+    }
+};
+
+struct GroupArgs {
+    GemvArgs g;                 // W = expert 0, n_rows / K / row_bytes of one expert, rpt, wpr, stages
+    long long estride;          // bytes between experts
+    const GroupItem *items;
+    const int *n_items;         // item count, written on the device by the planner
+    int tiles_per_expert;
+};
+
+__device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t *stages, uint64_t *full,
+                                                    uint64_t *empty, volatile int *abort_flag, int i0, int n_iter,
+                                                    int lane) {
+    const GemvArgs &a = ga.g;
+    const uint64_t pol = policy_evict_first();
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    const long long mat_bytes = (long long)a.n_rows * a.row_bytes;
+    ItemFetcher fetch;
+    for (int it = 0; it < n_iter; ++it) {
+        const GroupItem item = fetch.get(ga.items, i0, n_iter, it, lane);
+        const int s = it % a.n_stages;
+        if (it >= a.n_stages) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / a.n_stages) - 1) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok || *abort_flag) {
+                if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
+                return;
+            }
+        }
+        const long long b0 = (long long)item.tile * tile_bytes;
+        const long long b1 = min(b0 + tile_bytes, mat_bytes);
+        const uintptr_t base = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride);
+        const uintptr_t g0 = base + (uintptr_t)b0, g1 = base + (uintptr_t)b1;
+        const uintptr_t gd = g0 & ~uintptr_t(15);
+        const uintptr_t j0 = (g0 + 15) & ~uintptr_t(15);
+        const uintptr_t j1 = g1 & ~uintptr_t(15);
+        uint8_t *st = stages + (size_t)s * a.stage_bytes;
+        if (j1 > j0) {
+            if (g0 + lane < j0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+            if (j1 + lane < g1) st[j1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(j1 + lane));
+        } else {
+            if (g0 + lane < g1) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (j1 > j0) {
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(j1 - j0));
+                bulk_g2s(st + (j0 - gd), reinterpret_cast<const void *>(j0), (uint32_t)(j1 - j0), &full[s], pol);
+            } else {
+                mbar_arrive(&full[s]);
+            }
+        }
+    }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_grouped(GroupArgs ga) {
+    constexpr int M = 8;
+    const GemvArgs &a = ga.g;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvLayout L = gemv_layout(M, a.K, a.stage_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMaxStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_items = *ga.n_items;
+    const int per_cta = (n_items + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int i0 = blockIdx.x * per_cta;
+    const int n_iter = max(0, min(n_items, i0 + per_cta) - i0);
+    init_barriers(full, empty, abort_flag, a.n_stages, kConsumerWarps);
+    if (warp == kConsumerWarps) {
+        produce_group_tiles(ga, smem + L.off_stage, full, empty, abort_flag, i0, n_iter, lane);
+        return;
+    }
+    int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
+    int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
+    float *xs = reinterpret_cast<float *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
+    float *red = reinterpret_cast<float *>(smem + L.off_red);
+    XPlanes xp{xh, xl, xs, xsum, a.K};
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    const int rr = warp / a.wpr, part = warp - rr * a.wpr;
+    const int U = a.K / Fmt<QT>::UE;
+    int cur_e = -1, cur_m0 = -1;
+    ItemFetcher fetch;
+    for (int it = 0; it < n_iter; ++it) {
+        const GroupItem item = fetch.get(ga.items, i0, n_iter, it, lane);
+        if (item.e != cur_e || item.m0 != cur_m0) {
+            named_bar_sync(1, kConsumerWarps * 32);   // every warp is done with the old rows
+            encode_x_planes<M>(a.x + (size_t)item.m0 * a.K, item.mc, a.K, xh, xl, xs, xsum, warp, lane,
+                               kConsumerWarps);
+            named_bar_sync(1, kConsumerWarps * 32);
+            cur_e = item.e;
+            cur_m0 = item.m0;
+        }
+        const int s = it % a.n_stages;
+        const bool ok = consume_wait(a, full, abort_flag, it, lane);
+        const int row0 = item.tile * a.rpt;
+        const int row = row0 + rr;
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[m] = 0.0f;
+        if (ok && row < a.n_rows) {
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride) +
+                                 (uintptr_t)((long long)item.tile * tile_bytes);
+            const uint8_t *rowp = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15) + (size_t)rr * a.row_bytes;
+            for (int u = part * 32 + lane; u < U; u += 32 * a.wpr) {
+                W<QT> w;
+                w.decode(rowp, u);
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    if (m < item.mc) {
+                        XU<QT> xu;
+                        load_xu<QT>(xp, m, u, xu);
+                        acc[m] += w.dot(xu);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&empty[s]);
+        float *out = a.out + (size_t)item.m0 * a.n_rows;
+        if (a.wpr == 1) {
+            if (lane == 0 && ok && row < a.n_rows) {
+#pragma unroll
+                for (int m = 0; m < M; m++)
+                    if (m < item.mc) out[(size_t)m * a.n_rows + row] = acc[m];
+            }
+        } else {
+            float *rd = red + (it & 1) * kConsumerWarps * M;
+            if (lane == 0) {
+#pragma unroll
+                for (int m = 0; m < M; m++) rd[warp * M + m] = acc[m];
+            }
+            named_bar_sync(1, kConsumerWarps * 32);
+            if ((int)threadIdx.x < a.rpt * M && ok) {
+                const int r = threadIdx.x / M, m = threadIdx.x - r * M;
+                float sum = 0.0f;
+                for (int p = 0; p < a.wpr; p++) sum += rd[(r * a.wpr + p) * M + m];
+                if (row0 + r < a.n_rows && m < item.mc) out[(size_t)m * a.n_rows + row0 + r] = sum;
+            }
+        }
+    }
+}
+
+// Host-free grouping: counts per expert, stable sorted order and the work-item lists for
+// two tilings (the gate/up matrices and the down matrix).  Thread 0 counts and orders
+// (deterministic, small loops over rows and experts); the item lists are written in
+// parallel, one expert per thread.
+__global__ void k_group_plan(const int *__restrict__ eid, int R, int E, int tiles_a, int tiles_b,
+                             int *__restrict__ offs, int *__restrict__ sorted_pos, GroupItem *__restrict__ items_a,
+                             GroupItem *__restrict__ items_b, int *__restrict__ n_items) {
+    extern __shared__ int sm_plan[];
+    int *so = sm_plan;              // [E + 1] row offsets
+    int *sc = so + E + 1;           // [E] running positions
+    int *si = sc + E;               // [E + 1] first row-chunk index of each expert
+    int *se = si + E + 1;           // [R] expert ids (read once from global memory)
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) so[e] = 0;
+    for (int r = threadIdx.x; r < R; r += blockDim.x) se[r] = eid[r];
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int e = se[r];
+        if (e >= 0 && e < E) atomicAdd(&so[e + 1], 1);   // counts: order-free
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int e = 0; e < E; e++) so[e + 1] += so[e];
+        si[0] = 0;
+        for (int e = 0; e < E; e++) si[e + 1] = si[e] + (so[e + 1] - so[e] + 7) / 8;
+        n_items[0] = si[E] * tiles_a;
+        n_items[1] = si[E] * tiles_b;
+        for (int e = 0; e < E; e++) sc[e] = so[e];
+        for (int r = 0; r < R; r++) {   // stable positions in arrival order
+            const int e = se[r];
+            sorted_pos[r] = (e >= 0 && e < E) ? sc[e]++ : -1;
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) offs[e] = so[e];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int n = so[e + 1] - so[e];
+        const int *offs_s = so;
+        int c = si[e];
+        for (int m0 = 0; m0 < n; m0 += 8, c++) {
+            const int mc = min(8, n - m0);
+            for (int t = 0; t < tiles_a; t++) items_a[(size_t)c * tiles_a + t] = GroupItem{e, offs_s[e] + m0, mc, t};
+            for (int t = 0; t < tiles_b; t++) items_b[(size_t)c * tiles_b + t] = GroupItem{e, offs_s[e] + m0, mc, t};
+        }
+    }
+}
+
+__global__ void k_rows_permute(const float *__restrict__ src, const int *__restrict__ pos, int K, int to_sorted,
+                               float *__restrict__ dst) {
+    const int r = blockIdx.x;
+    const int p = pos[r];
+    if (p < 0) return;
+    const float *s = src + (size_t)(to_sorted ? r : p) * K;
+    float *d = dst + (size_t)(to_sorted ? p : r) * K;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) d[i] = s[i];
+}
+
+template <int QT>
+static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem *items, const int *n_items_dev,
+                            int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K,
+                            cudaStream_t s) {
+    const LaunchEnv *c = launch_env();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    constexpr int M = 8;
+    const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
+    int rpt = (int)(kStageTarget / rb);
+    rpt = rpt < 1 ? 1 : (rpt > 8 ? 8 : rpt);
+    rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
+    const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
+    const int fixed = gemv_layout(M, K, stage_bytes, 0).total;
+    const int n_stages = stages_for(fixed, stage_bytes);
+    if (n_stages < 2) {
+        set_error(MLQ_ERR_CAPACITY, "grouped experts: K=%d too large for the stage ring", K);
+        return MLQ_ERR_CAPACITY;
+    }
+    GroupArgs ga{};
+    GemvArgs &a = ga.g;
+    a.W = W; a.x = x_sorted; a.out = y_sorted; a.n_rows = n_rows; a.K = K; a.nb_x = M;
+    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = kConsumerWarps / rpt;
+    a.stage_bytes = stage_bytes; a.n_stages = n_stages; a.status = c->d_status;
+    ga.estride = estride;
+    ga.items = items;
+    ga.tiles_per_expert = (n_rows + rpt - 1) / rpt;
+    // the item count is only known on the device: the grid covers the bound and every CTA
+    // takes a contiguous share of the real count
+    ga.n_items = n_items_dev;
+    const int grid = n_items_bound < c->num_sms ? (n_items_bound > 0 ? n_items_bound : 1) : c->num_sms;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemv_grouped<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    k_gemv_grouped<QT><<<grid, kThreads, fixed + n_stages * stage_bytes, s>>>(ga);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int grouped_tiles_per_expert(int qt, int n_rows, int K) {
+    const long long rb = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    if (rb <= 0) return 0;
+    int rpt = (int)(kStageTarget / rb);
+    rpt = rpt < 1 ? 1 : (rpt > 8 ? 8 : rpt);
+    rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
+    return (n_rows + rpt - 1) / rpt;
+}
+
+int launch_grouped(int qt, const uint8_t *W, long long estride, const void *items, const int *n_items_dev,
+                   int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K, cudaStream_t s) {
+    const GroupItem *it = (const GroupItem *)items;
+    switch (qt) {
+        case MLQ_Q4_0: return launch_grouped_t<MLQ_Q4_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q4_1: return launch_grouped_t<MLQ_Q4_1>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q5_0: return launch_grouped_t<MLQ_Q5_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q8_0: return launch_grouped_t<MLQ_Q8_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q4_K: return launch_grouped_t<MLQ_Q4_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q5_K: return launch_grouped_t<MLQ_Q5_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_Q6_K: return launch_grouped_t<MLQ_Q6_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_MXFP4: return launch_grouped_t<MLQ_MXFP4>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        case MLQ_MXFP4_REF: return launch_grouped_t<MLQ_MXFP4_REF>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+        default:
+            set_error(MLQ_ERR_TYPE, "grouped experts: type %d", qt);
+            return MLQ_ERR_TYPE;
+    }
+}
+
+int launch_group_plan(const int *eid, int R, int E, int tiles_a, int tiles_b, int *offs, int *sorted_pos,
+                      void *items_a, void *items_b, int *n_items, cudaStream_t s) {
+    const size_t sm = sizeof(int) * (3 * (size_t)E + 2 + (size_t)R);
+    if (sm > 48 * 1024) {
+        set_error(MLQ_ERR_CAPACITY, "grouped experts: %d experts / %d rows per call", E, R);
+        return MLQ_ERR_CAPACITY;
+    }
+    k_group_plan<<<1, 256, sm, s>>>(eid, R, E, tiles_a, tiles_b, offs, sorted_pos, (GroupItem *)items_a,
+                                    (GroupItem *)items_b, n_items);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_rows_permute(const float *src, const int *pos, int R, int K, int to_sorted, float *dst, cudaStream_t s) {
+    if (R <= 0) return MLQ_OK;
+    k_rows_permute<<<R, 256, 0, s>>>(src, pos, K, to_sorted, dst);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
 // ------------------------------------------------------------------------------ dequantize
 // One thread per output element, bit-exact with the reference's *_dequantize_row and
 // gguf-py: every product/difference is rounded separately (no FMA contraction).

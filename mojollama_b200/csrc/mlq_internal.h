@@ -149,6 +149,13 @@ int launch_moe_experts(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
                        long long gs, long long us, long long ds, const int *idx, const float *w, int top_k,
                        int n_tok, int n_ff, int N, const float *x, float *h, float *h2, float *out,
                        const float *residual, float clamp, cudaStream_t s);
+// grouped expert GEMV (gemv.cu): rows sorted by expert, each active expert streamed once
+int grouped_tiles_per_expert(int qt, int n_rows, int K);
+int launch_group_plan(const int *eid, int R, int E, int tiles_a, int tiles_b, int *offs, int *sorted_pos,
+                      void *items_a, void *items_b, int *n_items, cudaStream_t s);
+int launch_grouped(int qt, const uint8_t *W, long long estride, const void *items, const int *n_items_dev,
+                   int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K, cudaStream_t s);
+int launch_rows_permute(const float *src, const int *pos, int R, int K, int to_sorted, float *dst, cudaStream_t s);
 // batch-engine embedding rows (qwen36.cu)
 int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_tok, float *x, int B, int N, int V,
                  cudaStream_t s);
