@@ -152,6 +152,22 @@ __device__ __forceinline__ void produce_tiles(const GemvArgs &a, uint8_t *stages
     }
 }
 
+// Before waiting on the previous kernel (programmatic dependent launch), the producer
+// warp prefetches this CTA's first tiles into L2: the bytes are only read later, after
+// the wait, so a tile the previous kernel is still writing is read correctly.
+__device__ __forceinline__ void prefetch_first_tiles(const GemvArgs &a, int n_iter, int lane) {
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    const int n = n_iter < a.n_stages ? n_iter : a.n_stages;
+    if (lane < n) {
+        const long long tile = (long long)blockIdx.x + (long long)lane * gridDim.x;
+        const long long b0 = tile * tile_bytes, b1 = min(b0 + tile_bytes, a.total_bytes);
+        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b0;
+        const uintptr_t g1 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)b1;
+        const uintptr_t i0 = (g0 + 15) & ~uintptr_t(15), i1 = g1 & ~uintptr_t(15);
+        if (i1 > i0) prefetch_l2(reinterpret_cast<const void *>(i0), (uint32_t)(i1 - i0));
+    }
+}
+
 // decode warps: bounded wait for stage s of iteration it; false on timeout/abort
 __device__ __forceinline__ bool consume_wait(const GemvArgs &a, uint64_t *full, volatile int *abort_flag, int it,
                                              int lane) {
@@ -187,7 +203,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    if (warp == kConsumerWarps) prefetch_first_tiles(a, n_iter, lane);
     init_barriers(full, empty, abort_flag, a.n_stages, kConsumerWarps);
+    pdl_wait();
+    pdl_trigger();
     if (warp == kConsumerWarps) {
         produce_tiles(a, smem + L.off_stage, full, empty, abort_flag, n_iter, lane);
         return;
@@ -264,7 +283,10 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    if (warp == kFastWarps) prefetch_first_tiles(a, n_iter, lane);
     init_barriers(full, empty, abort_flag, a.n_stages, kFastWarps);
+    pdl_wait();
+    pdl_trigger();
     if (warp == kFastWarps) {
         produce_tiles(a, smem + L.off_stage, full, empty, abort_flag, n_iter, lane);
         return;
@@ -388,6 +410,33 @@ __global__ void __launch_bounds__(256) k_gemv_float(const WT *__restrict__ W, co
 }
 
 // ------------------------------------------------------------------------------ launchers
+// Launch with programmatic stream serialization: the kernel may start while the previous
+// kernel on the stream finishes; it calls pdl_wait() before touching anything that kernel
+// writes.  MLQ_NO_PDL=1 launches normally.
+static bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_NO_PDL");
+        v = (e && atoi(e) != 0) ? 0 : 1;
+    }
+    return v == 1;
+}
+
+template <typename Kern, typename Args>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, int smem, cudaStream_t s, const Args &args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args);
+}
+
 static int stages_for(int fixed, int stage_bytes) {
     int n = (kSmemBudget - fixed) / stage_bytes;
     return n > kMaxStages ? kMaxStages : n;
@@ -408,9 +457,8 @@ static int launch_gemv_kernel(Kern kern, GemvArgs &a, int smem, cudaStream_t s, 
     if (per_sm < 1) per_sm = 1;
     a.status = c->d_status;
     const int grid = a.n_tiles < per_sm * c->num_sms ? a.n_tiles : per_sm * c->num_sms;
-    kern<<<grid, threads, smem, s>>>(a);
     count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl(kern, dim3(grid), dim3(threads), smem, s, a)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 template <int QT, int M>
@@ -680,6 +728,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_grouped(GroupArgs ga) {
     uint64_t *empty = full + kMaxStages;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();   // the item list is the previous kernel's output
+    pdl_trigger();
     const int n_items = *ga.n_items;
     const int per_cta = (n_items + (int)gridDim.x - 1) / (int)gridDim.x;
     const int i0 = blockIdx.x * per_cta;
@@ -693,10 +743,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_grouped(GroupArgs ga) {
     int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
     float *xs = reinterpret_cast<float *>(smem + L.off_xs);
     float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
-    float *red = reinterpret_cast<float *>(smem + L.off_red);
     XPlanes xp{xh, xl, xs, xsum, a.K};
     const long long tile_bytes = (long long)a.rpt * a.row_bytes;
-    const int rr = warp / a.wpr, part = warp - rr * a.wpr;
     const int U = a.K / Fmt<QT>::UE;
     int cur_e = -1, cur_m0 = -1;
     ItemFetcher fetch;
@@ -713,55 +761,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_grouped(GroupArgs ga) {
         const int s = it % a.n_stages;
         const bool ok = consume_wait(a, full, abort_flag, it, lane);
         const int row0 = item.tile * a.rpt;
-        const int row = row0 + rr;
-        float acc[M];
+        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride) +
+                             (uintptr_t)((long long)item.tile * tile_bytes);
+        const uint8_t *stage = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15);
+        float *out = a.out + (size_t)item.m0 * a.n_rows;
+        // warp w takes rows w, w + 8, ... of the tile
+        for (int rr = warp; rr < a.rpt; rr += kConsumerWarps) {
+            const int row = row0 + rr;
+            float acc[M];
 #pragma unroll
-        for (int m = 0; m < M; m++) acc[m] = 0.0f;
-        if (ok && row < a.n_rows) {
-            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride) +
-                                 (uintptr_t)((long long)item.tile * tile_bytes);
-            const uint8_t *rowp = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15) + (size_t)rr * a.row_bytes;
-            for (int u = part * 32 + lane; u < U; u += 32 * a.wpr) {
-                W<QT> w;
-                w.decode(rowp, u);
+            for (int m = 0; m < M; m++) acc[m] = 0.0f;
+            if (ok && row < a.n_rows) {
+                const uint8_t *rowp = stage + (size_t)rr * a.row_bytes;
+                for (int u = lane; u < U; u += 32) {
+                    W<QT> w;
+                    w.decode(rowp, u);
 #pragma unroll
-                for (int m = 0; m < M; m++) {
-                    if (m < item.mc) {
-                        XU<QT> xu;
-                        load_xu<QT>(xp, m, u, xu);
-                        acc[m] += w.dot(xu);
+                    for (int m = 0; m < M; m++) {
+                        if (m < item.mc) {
+                            XU<QT> xu;
+                            load_xu<QT>(xp, m, u, xu);
+                            acc[m] += w.dot(xu);
+                        }
                     }
                 }
             }
-        }
 #pragma unroll
-        for (int m = 0; m < M; m++) {
+            for (int m = 0; m < M; m++) {
+                if (m < item.mc) {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-        }
-        __syncwarp();
-        if (lane == 0 && ok) mbar_arrive(&empty[s]);
-        float *out = a.out + (size_t)item.m0 * a.n_rows;
-        if (a.wpr == 1) {
+                    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                }
+            }
             if (lane == 0 && ok && row < a.n_rows) {
 #pragma unroll
                 for (int m = 0; m < M; m++)
                     if (m < item.mc) out[(size_t)m * a.n_rows + row] = acc[m];
             }
-        } else {
-            float *rd = red + (it & 1) * kConsumerWarps * M;
-            if (lane == 0) {
-#pragma unroll
-                for (int m = 0; m < M; m++) rd[warp * M + m] = acc[m];
-            }
-            named_bar_sync(1, kConsumerWarps * 32);
-            if ((int)threadIdx.x < a.rpt * M && ok) {
-                const int r = threadIdx.x / M, m = threadIdx.x - r * M;
-                float sum = 0.0f;
-                for (int p = 0; p < a.wpr; p++) sum += rd[(r * a.wpr + p) * M + m];
-                if (row0 + r < a.n_rows && m < item.mc) out[(size_t)m * a.n_rows + row0 + r] = sum;
-            }
         }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&empty[s]);
     }
 }
 
@@ -821,6 +860,13 @@ __global__ void k_rows_permute(const float *__restrict__ src, const int *__restr
     for (int i = threadIdx.x; i < K; i += blockDim.x) d[i] = s[i];
 }
 
+// rows per grouped tile: a multiple of the 8 decode warps, about kStageTarget bytes, <= 64
+static int grouped_rpt(long long rb) {
+    long long r = kStageTarget / rb;
+    r = r < 8 ? 8 : (r > 64 ? 64 : r);
+    return (int)(r / 8 * 8);
+}
+
 template <int QT>
 static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem *items, const int *n_items_dev,
                             int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K,
@@ -829,9 +875,7 @@ static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem
     if (!c) return MLQ_ERR_NO_DEVICE;
     constexpr int M = 8;
     const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
-    int rpt = (int)(kStageTarget / rb);
-    rpt = rpt < 1 ? 1 : (rpt > 8 ? 8 : rpt);
-    rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
+    const int rpt = grouped_rpt(rb);
     const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
     const int fixed = gemv_layout(M, K, stage_bytes, 0).total;
     const int n_stages = stages_for(fixed, stage_bytes);
@@ -842,7 +886,7 @@ static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem
     GroupArgs ga{};
     GemvArgs &a = ga.g;
     a.W = W; a.x = x_sorted; a.out = y_sorted; a.n_rows = n_rows; a.K = K; a.nb_x = M;
-    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = kConsumerWarps / rpt;
+    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = 1;
     a.stage_bytes = stage_bytes; a.n_stages = n_stages; a.status = c->d_status;
     ga.estride = estride;
     ga.items = items;
@@ -857,17 +901,16 @@ static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem
             return MLQ_ERR_CUDA;
         attr = true;
     }
-    k_gemv_grouped<QT><<<grid, kThreads, fixed + n_stages * stage_bytes, s>>>(ga);
     count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl(k_gemv_grouped<QT>, dim3(grid), dim3(kThreads), fixed + n_stages * stage_bytes, s, ga))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 int grouped_tiles_per_expert(int qt, int n_rows, int K) {
     const long long rb = (long long)(K / block_elems(qt)) * block_bytes(qt);
     if (rb <= 0) return 0;
-    int rpt = (int)(kStageTarget / rb);
-    rpt = rpt < 1 ? 1 : (rpt > 8 ? 8 : rpt);
-    rpt = rpt >= 8 ? 8 : rpt >= 4 ? 4 : rpt >= 2 ? 2 : 1;
+    const int rpt = grouped_rpt(rb);
     return (n_rows + rpt - 1) / rpt;
 }
 

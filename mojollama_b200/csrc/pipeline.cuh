@@ -79,6 +79,17 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// Programmatic dependent launch: wait until the kernels this grid depends on have
+// completed and their writes are visible (no-op for a normal launch); let the next
+// dependent grid be scheduled as this grid's CTAs finish.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// L2 prefetch of a 16-byte-aligned range (TMA engine); harmless if the bytes change later
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
