@@ -438,8 +438,10 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
+    h0 = time.perf_counter()
     for _ in range(steps):
         out = step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / steps   # host time to issue one step
     b.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -452,7 +454,8 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
     return {"workload": f"config-3 MoE FFN stack: {L} layers, {E} experts top-{k} (renormalised), FF {FF}, "
                         f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), NCCL all-to-all",
             "tokens_per_rank": tokens, "tok_s": round(world * tokens / (t / 1e3), 1), "ms_per_step": round(t, 3),
-            "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite}
+            "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite,
+            "host_issue_ms_per_step": round(host_ms, 3)}
 
 
 SWEEP_SHAPES = [(2048, 2048), (5632, 2048), (2880, 2880), (151936, 2048)]

@@ -137,13 +137,17 @@ int mlq_ep_combine(const float *recv_y, const int *pos, const float *w, int T, i
 }
 
 // y[r] = down_e(silu(clamp(gate_e x_r, +-80)) * up_e x_r) for the local expert e = eid[r]
-// (0 <= e < n_experts); expert tensors are [n_experts][rows][cols] at the given byte
-// strides (device memory).  Rows are grouped by expert on the device (stable order) and
-// every active expert's three matrices are streamed once for all of its rows.
+// (0 <= e < n_experts <= 1024; rows with another id are left unwritten); expert tensors
+// are [n_experts][rows][cols] at the given byte strides (device memory).  The planner
+// orders the rows by expert (stable) and lists the work items; the rows of x are encoded
+// once in that order; the gate and up matrices of every active expert are streamed once
+// for all of its rows (one launch when they share a type); silu(clamp(g)) * u is encoded
+// the same way; the down matrices then write y in the callers' row order.
 int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp, long long gstride,
                  long long ustride, long long dstride, int n_experts, const int *eid, int R, int n_ff, int N,
                  const float *x, float *y) {
-    if (R < 0 || !eid || !x || !y || !gexp || !uexp || !dexp || n_ff <= 0 || N <= 0 || n_experts <= 0) {
+    if (R < 0 || !eid || !x || !y || !gexp || !uexp || !dexp || n_ff <= 0 || N <= 0 || n_experts <= 0 || N % 32 ||
+        n_ff % 32) {
         set_error(MLQ_ERR_ARG, "moe_rows: bad arguments");
         return MLQ_ERR_ARG;
     }
@@ -155,41 +159,48 @@ int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, 
         return MLQ_ERR_TYPE;
     }
     const int chunks = (R + 7) / 8 + (n_experts < R ? n_experts : R);
-    const int tgu = tg > tu ? tg : tu;
+    const bool pair = gqt == uqt;   // one type: one tiling, gate and up in one launch
     CallScope cs;
-    int *offs = (int *)cs.scratch(sizeof(int) * (3 * (size_t)n_experts + 2));
     int *spos = (int *)cs.scratch(sizeof(int) * (size_t)R);
+    int *srow = (int *)cs.scratch(sizeof(int) * (size_t)R);
     int *nitem = (int *)cs.scratch(sizeof(int) * 4);
-    void *items_gu = cs.scratch(16 * (size_t)chunks * tgu);
-    void *items_d = cs.scratch(16 * (size_t)chunks * (td > tu ? td : tu));
-    float *xs = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
+    const int tiles[3] = {pair ? tg + tu : tg, pair ? td : tu, td};
+    const int n_lists = pair ? 2 : 3;
+    void *items[3] = {nullptr, nullptr, nullptr};
+    for (int l = 0; l < n_lists; l++) items[l] = cs.scratch(16 * (size_t)chunks * tiles[l]);
+    uint8_t *px = (uint8_t *)cs.scratch(grouped_packed_bytes(R, N));
+    uint8_t *ph = (uint8_t *)cs.scratch(grouped_packed_bytes(R, n_ff));
     float *g = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
     float *u = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
-    float *ys = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
     if (cs.failed) return cs.finish();
     cudaStream_t s = stream();
-    // gate and up share one item list when their tilings agree (the usual case: one type)
-    int rc = MLQ_OK;
-    if (tg == tu) {
-        rc = launch_group_plan(eid, R, n_experts, tg, td, offs, spos, items_gu, items_d, nitem, s);
-        if (rc == MLQ_OK) rc = launch_rows_permute(x, spos, R, N, 1, xs, s);
-        if (rc == MLQ_OK)
-            rc = launch_grouped(gqt, (const uint8_t *)gexp, gstride, items_gu, nitem, chunks * tg, xs, g, n_ff, N, s);
-        if (rc == MLQ_OK)
-            rc = launch_grouped(uqt, (const uint8_t *)uexp, ustride, items_gu, nitem, chunks * tu, xs, u, n_ff, N, s);
-    } else {
-        rc = launch_group_plan(eid, R, n_experts, tg, tu, offs, spos, items_gu, items_d, nitem, s);
-        if (rc == MLQ_OK) rc = launch_rows_permute(x, spos, R, N, 1, xs, s);
-        if (rc == MLQ_OK)
-            rc = launch_grouped(gqt, (const uint8_t *)gexp, gstride, items_gu, nitem, chunks * tg, xs, g, n_ff, N, s);
-        if (rc == MLQ_OK)
-            rc = launch_grouped(uqt, (const uint8_t *)uexp, ustride, items_d, nitem + 1, chunks * tu, xs, u, n_ff, N, s);
-        if (rc == MLQ_OK) rc = launch_group_plan(eid, R, n_experts, td, td, offs, spos, items_d, items_d, nitem, s);
+    int rc = launch_group_plan(eid, R, n_experts, n_lists, items, tiles, spos, srow, nitem, s);
+    if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, srow, R, N, px, s);
+    GroupedCall gc{};
+    gc.planes = px;
+    gc.n_rows = n_ff;
+    gc.K = N;
+    if (rc == MLQ_OK) {
+        gc.qt = gqt; gc.W = (const uint8_t *)gexp; gc.estride = gstride; gc.out = g;
+        gc.items = items[0]; gc.n_items_dev = nitem; gc.n_items_bound = chunks * tiles[0];
+        if (pair) { gc.W2 = (const uint8_t *)uexp; gc.estride2 = ustride; gc.out2 = u; }
+        rc = launch_grouped(gc, s);
     }
-    if (rc == MLQ_OK) rc = launch_swiglu(g, g, u, (long long)R * n_ff, s);
-    if (rc == MLQ_OK)
-        rc = launch_grouped(dqt, (const uint8_t *)dexp, dstride, items_d, nitem + 1, chunks * td, g, ys, N, n_ff, s);
-    if (rc == MLQ_OK) rc = launch_rows_permute(ys, spos, R, N, 0, y, s);
+    if (rc == MLQ_OK && !pair) {
+        gc.qt = uqt; gc.W = (const uint8_t *)uexp; gc.estride = ustride; gc.out = u;
+        gc.items = items[1]; gc.n_items_dev = nitem + 1; gc.n_items_bound = chunks * tiles[1];
+        rc = launch_grouped(gc, s);
+    }
+    if (rc == MLQ_OK) rc = launch_encode_packed(g, u, nullptr, R, n_ff, ph, s);
+    if (rc == MLQ_OK) {
+        GroupedCall dc{};
+        dc.qt = dqt; dc.W = (const uint8_t *)dexp; dc.estride = dstride; dc.out = y;
+        dc.items = items[n_lists - 1]; dc.n_items_dev = nitem + n_lists - 1; dc.n_items_bound = chunks * td;
+        dc.planes = ph; dc.out_rows = srow;
+        dc.n_rows = N;
+        dc.K = n_ff;
+        rc = launch_grouped(dc, s);
+    }
     if (rc != MLQ_OK) {
         cs.failed = true;
         cs.finish();

@@ -116,13 +116,42 @@ __device__ __forceinline__ void e2m1x2_split(uint32_t sel, uint32_t &pos, uint32
 }
 
 // ---------------------------------------------------------------------------------- x planes
+// Row m of the h / l planes starts at h + m * hs (bytes); its scales and sums at
+// s + m * ss (floats).  Inside a row, the 16-byte chunks of every complete 128-byte
+// group are permuted (plane_swz) so that the three unit load patterns -- lane u reading
+// chunks 2u + i (32-element units), 4u + i (Q4_K/Q5_K) and 8(u/2) + u%2 + 2k (Q6_K) --
+// hit eight different bank groups in each quarter-warp phase of a 128-bit load.
 struct XPlanes {
-    const int8_t *h;      // [M][K]
-    const int8_t *l;      // [M][K]
-    const float *s;       // [M][K/32]   s_b / 254
-    const float *sum;     // [M][K/32]   exact fp32 block sums
+    const int8_t *h;      // [M] rows of K int8, row stride hs
+    const int8_t *l;
+    const float *s;       // [M] rows of K/32: s_b / 254, row stride ss
+    const float *sum;     // [M] rows of K/32: exact fp32 block sums
     int K;
+    int hs, ss;
 };
+
+// byte offset of the 16-byte chunk holding logical byte k (a multiple of 16) of a row of
+// K bytes: chunk c of 128-byte group a -> c ^ f(a & 7), f(a) = a ^ 2a (mod 8); a group
+// cut short by the end of the row keeps its order
+__device__ __forceinline__ int plane_swz(int k, int K) {
+    const int a = (k >> 7) & 7;
+    return ((k | 127) < K) ? (k ^ (((a ^ (a << 1)) & 7) << 4)) : k;
+}
+
+// NW words (NW % 4 == 0, at most 64 bytes) of a plane row from logical byte k (a multiple
+// of 16 with the NW words inside one 128-byte group): one permutation term for all chunks
+template <int NW>
+__device__ __forceinline__ void lds_plane(const int8_t *row, int k, int K, uint32_t *w) {
+    const int sw = plane_swz(k, K) ^ k;
+#pragma unroll
+    for (int i = 0; i < NW / 4; i++) {
+        const int4 v = *reinterpret_cast<const int4 *>(row + ((k + 16 * i) ^ sw));
+        w[4 * i + 0] = (uint32_t)v.x;
+        w[4 * i + 1] = (uint32_t)v.y;
+        w[4 * i + 2] = (uint32_t)v.z;
+        w[4 * i + 3] = (uint32_t)v.w;
+    }
+}
 
 // 254 * dp4a(q, h) + dp4a(q, l) over NW words held in registers
 template <int NW>
@@ -134,19 +163,6 @@ __device__ __forceinline__ int dot_words(const uint32_t *q, const uint32_t *h, c
         b = __dp4a((int)q[i], (int)l[i], b);
     }
     return a * 254 + b;
-}
-
-// copy NW words (NW % 4 == 0) of a plane from 16-byte-aligned shared memory
-template <int NW>
-__device__ __forceinline__ void lds_words(const int8_t *p, uint32_t *w) {
-#pragma unroll
-    for (int i = 0; i < NW / 4; i++) {
-        const int4 v = reinterpret_cast<const int4 *>(p)[i];
-        w[4 * i + 0] = (uint32_t)v.x;
-        w[4 * i + 1] = (uint32_t)v.y;
-        w[4 * i + 2] = (uint32_t)v.z;
-        w[4 * i + 3] = (uint32_t)v.w;
-    }
 }
 
 // ---------------------------------------------------------------------------------- units
@@ -174,10 +190,9 @@ template <> struct XU<MLQ_MXFP4_REF> : XU32 {};
 
 template <int QT>
 __device__ __forceinline__ void load_xu32(const XPlanes &xp, int m, int u, XU32 &x) {
-    const size_t xo = (size_t)m * xp.K + 32 * u;
-    lds_words<8>(xp.h + xo, x.h);
-    lds_words<8>(xp.l + xo, x.l);
-    const size_t so = (size_t)m * (xp.K / 32) + u;
+    lds_plane<8>(xp.h + (size_t)m * xp.hs, 32 * u, xp.K, x.h);
+    lds_plane<8>(xp.l + (size_t)m * xp.hs, 32 * u, xp.K, x.l);
+    const size_t so = (size_t)m * xp.ss + u;
     x.s = xp.s[so];
     x.sum = xp.sum[so];
 }
@@ -321,10 +336,9 @@ template <> struct XU<MLQ_Q5_K> : XU64 {};
 
 __device__ __forceinline__ void load_xu64(const XPlanes &xp, int m, int u, XU64 &x) {
     const int xb0 = 2 * u;                       // = 8*(u/4) + 2*(u%4)
-    const size_t xo = (size_t)m * xp.K + 32 * xb0;
-    lds_words<16>(xp.h + xo, x.h);
-    lds_words<16>(xp.l + xo, x.l);
-    const size_t so = (size_t)m * (xp.K / 32) + xb0;
+    lds_plane<16>(xp.h + (size_t)m * xp.hs, 32 * xb0, xp.K, x.h);
+    lds_plane<16>(xp.l + (size_t)m * xp.hs, 32 * xb0, xp.K, x.l);
+    const size_t so = (size_t)m * xp.ss + xb0;
     x.s[0] = xp.s[so];
     x.s[1] = xp.s[so + 1];
     x.sum[0] = xp.sum[so];
@@ -432,10 +446,9 @@ __device__ __forceinline__ void load_xu_q6k(const XPlanes &xp, int m, int u, XU<
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int xb = 8 * sb + 4 * hh + k;
-        const size_t xo = (size_t)m * xp.K + 32 * xb + l0;
-        lds_words<4>(xp.h + xo, x.h + 4 * k);
-        lds_words<4>(xp.l + xo, x.l + 4 * k);
-        x.s[k] = xp.s[(size_t)m * (xp.K / 32) + xb];
+        lds_plane<4>(xp.h + (size_t)m * xp.hs, 32 * xb + l0, xp.K, x.h + 4 * k);
+        lds_plane<4>(xp.l + (size_t)m * xp.hs, 32 * xb + l0, xp.K, x.l + 4 * k);
+        x.s[k] = xp.s[(size_t)m * xp.ss + xb];
         int hs = 0, ls = 0;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -507,56 +520,80 @@ __device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> 
     }
 }
 
-// Encode activation rows [nb_x][K] (rows >= nb_x of the M read as zero) into the int8
-// planes + scales described at the top of this file; one warp per 32-element block.
-// Each warp takes kEncBatch blocks at a time and issues all their loads before the
-// reductions, so the L2 latency is paid once per batch rather than once per block.
+// Encode activation rows into the int8 planes + scales described at the top of this
+// file; one warp per 32-element block.  src(m, k) gives element k of row m; only rows
+// m < n_rows are written.  Each warp takes kEncBatch blocks at a time and issues all
+// their loads before the reductions, so the L2 latency is paid once per batch rather
+// than once per block.
 constexpr int kEncBatch = 8;
 
-template <int M>
-__device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, int8_t *xh, int8_t *xl,
-                                float *xs, float *xsum, int warp, int lane, int nwarps) {
+// Block kb of row m from its 32 values (one per lane).
+__device__ __forceinline__ void encode_block(float v, int m, int kb, int K, int8_t *xh, int8_t *xl, float *xs,
+                                             float *xsum, int hs, int ss, int lane) {
+    float amax = fabsf(v), sum = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    int h = 0, l = 0;
+    float scale;
+    if (amax > 0.0f && amax <= 3.402823466e38f) {
+        const float sc = amax / 127.0f;
+        const float t = v / sc;
+        const float hh = rintf(t);
+        h = (int)hh;
+        l = (int)rintf((t - hh) * 254.0f);
+        scale = sc / 254.0f;
+    } else {
+        scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
+    }
+    const int k = 32 * kb + lane;
+    const size_t o = (size_t)m * hs + plane_swz(k & ~15, K) + (k & 15);
+    xh[o] = (int8_t)h;
+    xl[o] = (int8_t)l;
+    if (lane == 0) {
+        xs[(size_t)m * ss + kb] = scale;
+        xsum[(size_t)m * ss + kb] = sum;
+    }
+}
+
+template <typename Src>
+__device__ void encode_blocks(const Src &src, int n_rows, int K, int8_t *xh, int8_t *xl, float *xs, float *xsum,
+                              int hs, int ss, int warp, int lane, int nwarps) {
     const int kb_per_row = K / 32;
-    const int total = M * kb_per_row;
+    const int total = n_rows * kb_per_row;
     for (int blk0 = warp * kEncBatch; blk0 < total; blk0 += nwarps * kEncBatch) {
         float v[kEncBatch];
 #pragma unroll
         for (int i = 0; i < kEncBatch; i++) {
             const int blk = blk0 + i;
             const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
-            v[i] = (blk < total && m < nb_x) ? __ldg(x + (size_t)m * K + 32 * kb + lane) : 0.0f;
+            v[i] = blk < total ? src(m, 32 * kb + lane) : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < kEncBatch; i++) {
             const int blk = blk0 + i;
             if (blk >= total) break;
             const int m = blk / kb_per_row, kb = blk - m * kb_per_row;
-            float amax = fabsf(v[i]), sum = v[i];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            }
-            int h = 0, l = 0;
-            float scale;
-            if (amax > 0.0f && amax <= 3.402823466e38f) {
-                const float sc = amax / 127.0f;
-                const float t = v[i] / sc;
-                const float hh = rintf(t);
-                h = (int)hh;
-                l = (int)rintf((t - hh) * 254.0f);
-                scale = sc / 254.0f;
-            } else {
-                scale = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);   // NaN/inf block -> NaN
-            }
-            xh[(size_t)m * K + 32 * kb + lane] = (int8_t)h;
-            xl[(size_t)m * K + 32 * kb + lane] = (int8_t)l;
-            if (lane == 0) {
-                xs[blk] = scale;
-                xsum[blk] = sum;
-            }
+            encode_block(v[i], m, kb, K, xh, xl, xs, xsum, hs, ss, lane);
         }
     }
+}
+
+// rows [nb_x][K] of x; rows nb_x..M-1 read as zero
+struct PlainRows {
+    const float *x;
+    int K, nb;
+    __device__ __forceinline__ float operator()(int m, int k) const {
+        return m < nb ? __ldg(x + (size_t)m * K + k) : 0.0f;
+    }
+};
+
+template <int M>
+__device__ void encode_x_planes(const float *__restrict__ x, int nb_x, int K, int8_t *xh, int8_t *xl, float *xs,
+                                float *xsum, int warp, int lane, int nwarps) {
+    encode_blocks(PlainRows{x, K, nb_x}, M, K, xh, xl, xs, xsum, K, K / 32, warp, lane, nwarps);
 }
 
 // generic path: acc[m] += dot(unit u, x row m), activations from shared memory

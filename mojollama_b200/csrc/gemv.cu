@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
     encode_x_planes<M>(a.x, a.nb_x, a.K, xh, xl, xs, xsum, warp, lane, kConsumerWarps);
     named_bar_sync(1, kConsumerWarps * 32);
 
-    XPlanes xp{xh, xl, xs, xsum, a.K};
+    XPlanes xp{xh, xl, xs, xsum, a.K, a.K, a.K / 32};
     const long long tile_bytes = (long long)a.rpt * a.row_bytes;
     const int rr = warp / a.wpr, part = warp - rr * a.wpr;
     const int U = a.K / Fmt<QT>::UE;
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
     float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
     encode_x_planes<1>(a.x, 1, a.K, xh, xl, xs, xsum, warp, lane, kFastWarps);
     named_bar_sync(1, kFastWarps * 32);
-    const XPlanes xp{xh, xl, xs, xsum, a.K};
+    const XPlanes xp{xh, xl, xs, xsum, a.K, a.K, a.K / 32};
     const int U = a.K / Fmt<QT>::UE;
     XU<QT> xu[UPL];
 #pragma unroll
@@ -645,43 +645,113 @@ int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_ro
 }
 
 // ------------------------------------------------------------------------------ grouped experts
-// Grouped expert GEMV: rows sorted by expert; every active expert's matrix is streamed once
-// for all of its rows (up to 8 per pass).  Work items (expert e, first sorted row m0, row
-// count mc <= 8, row tile t) are listed expert-major; a CTA takes a contiguous range of
-// items, so it re-encodes its activation rows only when (e, m0) changes.  Tiles are the
-// same contiguous byte ranges as in k_gemv_q, at base + e * estride.
+// Grouped expert GEMV: the rows of one call are ordered by expert (stable) and every
+// active expert's matrix is streamed once for all of its rows, up to 8 rows per pass.
+// Work items (expert e, first sorted position m0, row count mc <= 8, tile t) are listed
+// expert-major by the planner.  Tiles are the same contiguous byte ranges as in k_gemv_q,
+// at base + e * estride.  One launch can stream two matrices of one type and shape (gate
+// and up): tiles [0, T) of an item address the first and [T, 2T) the second.
+//
+// The activation rows are encoded once, before the launch, into packed rows in global
+// memory (k_encode_packed); the producer warp bulk-copies an item's mc rows into one of
+// two shared-memory activation slots when (e, m0) changes, next to the weight tiles, so
+// no decode warp ever waits on an encode.  CTAs take groups of G consecutive items
+// round-robin (group g -> CTA g % grid), which spreads the costlier many-row items over
+// all SMs.  The producer hands every tile's item to the decode warps in the stage itself.
 struct GroupItem { int e, m0, mc, tile; };
 
-// Item it of a warp's range, fetched 32 at a time (lane i loads item base + i) and
-// broadcast with shuffles: one global round trip per 32 items.  Call warp-uniformly.
-struct ItemFetcher {
-    GroupItem mine;
-    __device__ __forceinline__ GroupItem get(const GroupItem *items, int i0, int n, int it, int lane) {
-        if ((it & 31) == 0) mine = (it + lane < n) ? items[i0 + it + lane] : GroupItem{0, 0, 0, 0};
-        const int src = it & 31;
-        return GroupItem{__shfl_sync(0xffffffffu, mine.e, src), __shfl_sync(0xffffffffu, mine.m0, src),
-                         __shfl_sync(0xffffffffu, mine.mc, src), __shfl_sync(0xffffffffu, mine.tile, src)};
-    }
-};
+// packed activation row: [K int8 h][K int8 l][K/32 f32 s][K/32 f32 sum], 16-byte multiple
+__host__ __device__ inline int packed_row_bytes(int K) { return align_up(2 * K + (K / 32) * 8, 16); }
+
+__device__ __forceinline__ XPlanes packed_planes(const uint8_t *base, int K) {
+    const int rb = packed_row_bytes(K);
+    const float *s = reinterpret_cast<const float *>(base + 2 * K);
+    return XPlanes{reinterpret_cast<const int8_t *>(base), reinterpret_cast<const int8_t *>(base + K), s, s + K / 32,
+                   K, rb, rb / 4};
+}
 
 struct GroupArgs {
-    GemvArgs g;                 // W = expert 0, n_rows / K / row_bytes of one expert, rpt, wpr, stages
-    long long estride;          // bytes between experts
+    GemvArgs g;                 // W / out: first matrix; n_rows / K / row_bytes of one expert
+    long long estride;          // bytes between experts of the first matrix
+    const uint8_t *W2;          // second matrix (tiles >= tiles_per_expert), or null
+    long long estride2;
+    float *out2;
     const GroupItem *items;
     const int *n_items;         // item count, written on the device by the planner
     int tiles_per_expert;
+    const uint8_t *planes;      // packed activation rows in sorted order
+    int n_xslots;               // shared-memory activation slots (2, or 1 for very long rows)
+    int xslot_bytes;            // 8 packed rows
+    int group;                  // items per round-robin group
+    int lane_group_log;         // log2 of the lanes per weight row (>= min(units per row, 32))
+    const int *out_rows;        // result of sorted position p -> row out_rows[p] (identity if null)
 };
 
-__device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t *stages, uint64_t *full,
-                                                    uint64_t *empty, volatile int *abort_flag, int i0, int n_iter,
+struct GroupLayout {
+    int off_bar, off_flag, off_x, off_stage, total;
+};
+
+__host__ __device__ inline GroupLayout group_layout(int xslot_bytes, int n_xslots, int stage_bytes, int n_stages) {
+    GroupLayout L;
+    int o = 0;
+    L.off_bar = o;   o += (2 * kMaxStages + 4) * 8;   // full, empty, x_full[2], x_empty[2]
+    L.off_flag = o;  o += 16;
+    o = align_up(o, 128);
+    L.off_x = o;     o = align_up(o + n_xslots * xslot_bytes, 128);
+    L.off_stage = o; o += n_stages * stage_bytes;
+    L.total = o;
+    return L;
+}
+
+// item index of a CTA's it-th tile (round-robin groups of G)
+__device__ __forceinline__ int group_item_index(int it, int G) {
+    return ((it / G) * (int)gridDim.x + (int)blockIdx.x) * G + it % G;
+}
+
+// first byte, matrix-local tile and output base of an item's tile
+struct ItemTile {
+    uintptr_t g0;
+    float *out;
+    int tile;
+};
+__device__ __forceinline__ ItemTile item_tile(const GroupArgs &ga, const GroupItem &item, long long tile_bytes) {
+    const bool second = item.tile >= ga.tiles_per_expert;
+    ItemTile t;
+    t.tile = second ? item.tile - ga.tiles_per_expert : item.tile;
+    const uint8_t *W = second ? ga.W2 : ga.g.W;
+    const long long es = second ? ga.estride2 : ga.estride;
+    t.g0 = reinterpret_cast<uintptr_t>(W) + (uintptr_t)((long long)item.e * es) +
+           (uintptr_t)((long long)t.tile * tile_bytes);
+    t.out = second ? ga.out2 : ga.g.out;
+    return t;
+}
+
+// the item travels in the last 16 bytes of its stage (past the tile and the decode slack)
+__device__ __forceinline__ GroupItem *stage_item(uint8_t *stage, int stage_bytes) {
+    return reinterpret_cast<GroupItem *>(stage + stage_bytes - 16);
+}
+
+__device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t *stages, uint8_t *xslots,
+                                                    uint64_t *full, uint64_t *empty, uint64_t *xfull,
+                                                    uint64_t *xempty, volatile int *abort_flag, int n_items,
                                                     int lane) {
     const GemvArgs &a = ga.g;
     const uint64_t pol = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
     const long long tile_bytes = (long long)a.rpt * a.row_bytes;
     const long long mat_bytes = (long long)a.n_rows * a.row_bytes;
-    ItemFetcher fetch;
-    for (int it = 0; it < n_iter; ++it) {
-        const GroupItem item = fetch.get(ga.items, i0, n_iter, it, lane);
+    const int G = ga.group;
+    const int prb = packed_row_bytes(a.K);
+    int run = 0, cur_e = -1, cur_m0 = -1;
+    GroupItem mine{-1, 0, 0, 0};
+    for (int it = 0;; ++it) {
+        const int j = it % G;
+        if (j == 0) {   // lane i < G holds item i of the group
+            const int li = group_item_index(it, G) + lane;
+            mine = (lane < G && li < n_items) ? ga.items[li] : GroupItem{-1, 0, 0, 0};
+        }
+        const GroupItem item{__shfl_sync(0xffffffffu, mine.e, j), __shfl_sync(0xffffffffu, mine.m0, j),
+                             __shfl_sync(0xffffffffu, mine.mc, j), __shfl_sync(0xffffffffu, mine.tile, j)};
         const int s = it % a.n_stages;
         if (it >= a.n_stages) {
             bool ok = true;
@@ -692,14 +762,21 @@ __device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t
                 return;
             }
         }
-        const long long b0 = (long long)item.tile * tile_bytes;
+        uint8_t *st = stages + (size_t)s * a.stage_bytes;
+        if (item.e < 0) {   // end of this CTA's items
+            if (lane == 0) {
+                *stage_item(st, a.stage_bytes) = GroupItem{-1, 0, 0, 0};
+                mbar_arrive(&full[s]);
+            }
+            return;
+        }
+        const ItemTile t = item_tile(ga, item, tile_bytes);
+        const long long b0 = (long long)t.tile * tile_bytes;
         const long long b1 = min(b0 + tile_bytes, mat_bytes);
-        const uintptr_t base = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride);
-        const uintptr_t g0 = base + (uintptr_t)b0, g1 = base + (uintptr_t)b1;
+        const uintptr_t g0 = t.g0, g1 = t.g0 + (uintptr_t)(b1 - b0);
         const uintptr_t gd = g0 & ~uintptr_t(15);
         const uintptr_t j0 = (g0 + 15) & ~uintptr_t(15);
         const uintptr_t j1 = g1 & ~uintptr_t(15);
-        uint8_t *st = stages + (size_t)s * a.stage_bytes;
         if (j1 > j0) {
             if (g0 + lane < j0) st[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
             if (j1 + lane < g1) st[j1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(j1 + lane));
@@ -708,6 +785,7 @@ __device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t
         }
         __syncwarp();
         if (lane == 0) {
+            *stage_item(st, a.stage_bytes) = item;
             if (j1 > j0) {
                 mbar_arrive_expect_tx(&full[s], (uint32_t)(j1 - j0));
                 bulk_g2s(st + (j0 - gd), reinterpret_cast<const void *>(j0), (uint32_t)(j1 - j0), &full[s], pol);
@@ -715,196 +793,399 @@ __device__ __forceinline__ void produce_group_tiles(const GroupArgs &ga, uint8_t
                 mbar_arrive(&full[s]);
             }
         }
-    }
-}
-
-template <int QT>
-__global__ void __launch_bounds__(kThreads, 1) k_gemv_grouped(GroupArgs ga) {
-    constexpr int M = 8;
-    const GemvArgs &a = ga.g;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const GemvLayout L = gemv_layout(M, a.K, a.stage_bytes, a.n_stages);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
-    uint64_t *empty = full + kMaxStages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();   // the item list is the previous kernel's output
-    pdl_trigger();
-    const int n_items = *ga.n_items;
-    const int per_cta = (n_items + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int i0 = blockIdx.x * per_cta;
-    const int n_iter = max(0, min(n_items, i0 + per_cta) - i0);
-    init_barriers(full, empty, abort_flag, a.n_stages, kConsumerWarps);
-    if (warp == kConsumerWarps) {
-        produce_group_tiles(ga, smem + L.off_stage, full, empty, abort_flag, i0, n_iter, lane);
-        return;
-    }
-    int8_t *xh = reinterpret_cast<int8_t *>(smem + L.off_xh);
-    int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
-    float *xs = reinterpret_cast<float *>(smem + L.off_xs);
-    float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
-    XPlanes xp{xh, xl, xs, xsum, a.K};
-    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
-    const int U = a.K / Fmt<QT>::UE;
-    int cur_e = -1, cur_m0 = -1;
-    ItemFetcher fetch;
-    for (int it = 0; it < n_iter; ++it) {
-        const GroupItem item = fetch.get(ga.items, i0, n_iter, it, lane);
+        // a new activation run: its rows into the next slot once the decode warps are done
+        // with the run that used it (issued after the tile, which they need to see first)
         if (item.e != cur_e || item.m0 != cur_m0) {
-            named_bar_sync(1, kConsumerWarps * 32);   // every warp is done with the old rows
-            encode_x_planes<M>(a.x + (size_t)item.m0 * a.K, item.mc, a.K, xh, xl, xs, xsum, warp, lane,
-                               kConsumerWarps);
-            named_bar_sync(1, kConsumerWarps * 32);
+            const int xs = run % ga.n_xslots;
+            bool ok = true;
+            if (run >= ga.n_xslots && lane == 0) ok = mbar_wait_bounded(&xempty[xs], ((run / ga.n_xslots) - 1) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok || *abort_flag) {
+                if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
+                return;
+            }
+            if (lane == 0) {
+                const uint32_t bytes = (uint32_t)(item.mc * prb);
+                mbar_arrive_expect_tx(&xfull[xs], bytes);
+                bulk_g2s(xslots + (size_t)xs * ga.xslot_bytes, ga.planes + (size_t)item.m0 * prb, bytes, &xfull[xs],
+                         pol_x);
+            }
+            ++run;
             cur_e = item.e;
             cur_m0 = item.m0;
         }
-        const int s = it % a.n_stages;
-        const bool ok = consume_wait(a, full, abort_flag, it, lane);
-        const int row0 = item.tile * a.rpt;
-        const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)(item.e * ga.estride) +
-                             (uintptr_t)((long long)item.tile * tile_bytes);
-        const uint8_t *stage = smem + L.off_stage + (size_t)s * a.stage_bytes + (g0 & 15);
-        float *out = a.out + (size_t)item.m0 * a.n_rows;
-        // warp w takes rows w, w + 8, ... of the tile
-        for (int rr = warp; rr < a.rpt; rr += kConsumerWarps) {
-            const int row = row0 + rr;
-            float acc[M];
+    }
+}
+
+// Lanes form groups of GS = 2^gs_log (the units of one weight row, stepping by GS); warp
+// w takes rows w + 16 (j * RPW + gi) of a tile, RPW = 32 / GS rows per pass.
+struct LaneMap {
+    int gs_log, rpw, gi, gl, U;
+};
+
+// One staged tile against MC (>= mc) activation rows: each unit is decoded once and
+// dotted with every activation row from shared memory (conflict-free swizzled planes).
+template <int QT, int MC, bool A16>
+__device__ __forceinline__ void group_tile_rows(const GroupArgs &ga, const uint8_t *stage, const XPlanes &xp,
+                                                const GroupItem &item, const ItemTile &t, const LaneMap &lm,
+                                                int warp) {
+    const GemvArgs &a = ga.g;
+    const int GS = 1 << lm.gs_log;
+    const int row0 = t.tile * a.rpt;
+    const int mc = item.mc;
+    for (int base = 0; warp + kFastWarps * base < a.rpt; base += lm.rpw) {
+        const int r = warp + kFastWarps * (base + lm.gi);
+        const bool v = r < a.rpt && row0 + r < a.n_rows;
+        float acc[MC];
 #pragma unroll
-            for (int m = 0; m < M; m++) acc[m] = 0.0f;
-            if (ok && row < a.n_rows) {
-                const uint8_t *rowp = stage + (size_t)rr * a.row_bytes;
-                for (int u = lane; u < U; u += 32) {
-                    W<QT> w;
-                    w.decode(rowp, u);
+        for (int m = 0; m < MC; m++) acc[m] = 0.0f;
+        if (v) {
+            const uint8_t *pr = stage + (size_t)r * a.row_bytes;
+            for (int u = lm.gl; u < lm.U; u += GS) {
+                W<QT> w;
+                if constexpr (A16) w.decode_a16(pr, u);
+                else w.decode(pr, u);
 #pragma unroll
-                    for (int m = 0; m < M; m++) {
-                        if (m < item.mc) {
-                            XU<QT> xu;
-                            load_xu<QT>(xp, m, u, xu);
-                            acc[m] += w.dot(xu);
-                        }
+                for (int m = 0; m < MC; m++) {
+                    if (m < mc) {
+                        XU<QT> xu;
+                        load_xu<QT>(xp, m, u, xu);
+                        acc[m] += w.dot(xu);
                     }
                 }
             }
+        }
 #pragma unroll
-            for (int m = 0; m < M; m++) {
-                if (m < item.mc) {
+        for (int m = 0; m < MC; m++) {
+            if (m < mc) {
+                for (int o = GS >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+            }
+        }
+        if (lm.gl == 0 && v) {
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+            for (int m = 0; m < MC; m++) {
+                if (m < mc) {
+                    const int p = item.m0 + m;
+                    t.out[(size_t)(ga.out_rows ? __ldg(ga.out_rows + p) : p) * a.n_rows + row0 + r] = acc[m];
                 }
             }
-            if (lane == 0 && ok && row < a.n_rows) {
-#pragma unroll
-                for (int m = 0; m < M; m++)
-                    if (m < item.mc) out[(size_t)m * a.n_rows + row] = acc[m];
-            }
         }
-        __syncwarp();
-        if (lane == 0 && ok) mbar_arrive(&empty[s]);
     }
 }
 
-// Host-free grouping: counts per expert, stable sorted order and the work-item lists for
-// two tilings (the gate/up matrices and the down matrix).  Thread 0 counts and orders
-// (deterministic, small loops over rows and experts); the item lists are written in
-// parallel, one expert per thread.
-__global__ void k_group_plan(const int *__restrict__ eid, int R, int E, int tiles_a, int tiles_b,
-                             int *__restrict__ offs, int *__restrict__ sorted_pos, GroupItem *__restrict__ items_a,
-                             GroupItem *__restrict__ items_b, int *__restrict__ n_items) {
-    extern __shared__ int sm_plan[];
-    int *so = sm_plan;              // [E + 1] row offsets
-    int *sc = so + E + 1;           // [E] running positions
-    int *si = sc + E;               // [E + 1] first row-chunk index of each expert
-    int *se = si + E + 1;           // [R] expert ids (read once from global memory)
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) so[e] = 0;
-    for (int r = threadIdx.x; r < R; r += blockDim.x) se[r] = eid[r];
-    __syncthreads();
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        const int e = se[r];
-        if (e >= 0 && e < E) atomicAdd(&so[e + 1], 1);   // counts: order-free
-    }
-    __syncthreads();
+template <int QT, bool A16>
+__global__ void __launch_bounds__(kFastThreads, 1) k_gemv_grouped(GroupArgs ga) {
+    const GemvArgs &a = ga.g;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GroupLayout L = group_layout(ga.xslot_bytes, ga.n_xslots, a.stage_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMaxStages;
+    uint64_t *xfull = empty + kMaxStages;
+    uint64_t *xempty = xfull + 2;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int e = 0; e < E; e++) so[e + 1] += so[e];
-        si[0] = 0;
-        for (int e = 0; e < E; e++) si[e + 1] = si[e] + (so[e + 1] - so[e] + 7) / 8;
-        n_items[0] = si[E] * tiles_a;
-        n_items[1] = si[E] * tiles_b;
-        for (int e = 0; e < E; e++) sc[e] = so[e];
-        for (int r = 0; r < R; r++) {   // stable positions in arrival order
-            const int e = se[r];
-            sorted_pos[r] = (e >= 0 && e < E) ? sc[e]++ : -1;
+        for (int s = 0; s < a.n_stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kFastWarps);
         }
+        for (int j = 0; j < 2; j++) {
+            mbar_init(&xfull[j], 1);
+            mbar_init(&xempty[j], kFastWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
     }
     __syncthreads();
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) offs[e] = so[e];
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int n = so[e + 1] - so[e];
-        const int *offs_s = so;
-        int c = si[e];
-        for (int m0 = 0; m0 < n; m0 += 8, c++) {
-            const int mc = min(8, n - m0);
-            for (int t = 0; t < tiles_a; t++) items_a[(size_t)c * tiles_a + t] = GroupItem{e, offs_s[e] + m0, mc, t};
-            for (int t = 0; t < tiles_b; t++) items_b[(size_t)c * tiles_b + t] = GroupItem{e, offs_s[e] + m0, mc, t};
+    pdl_wait();   // the item list and the activation rows are earlier kernels' outputs
+    pdl_trigger();
+    if (warp == kFastWarps) {
+        produce_group_tiles(ga, smem + L.off_stage, smem + L.off_x, full, empty, xfull, xempty, abort_flag,
+                            *ga.n_items, lane);
+        return;
+    }
+    int run = 0, cur_e = -1, cur_m0 = -1, xs = 0;
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    LaneMap lm;
+    lm.gs_log = ga.lane_group_log;
+    lm.rpw = 32 >> lm.gs_log;
+    lm.gi = lane >> lm.gs_log;
+    lm.gl = lane & ((1 << lm.gs_log) - 1);
+    lm.U = a.K / Fmt<QT>::UE;
+    for (int it = 0;; ++it) {
+        const int s = it % a.n_stages;
+        if (!consume_wait(a, full, abort_flag, it, lane)) break;
+        uint8_t *st = smem + L.off_stage + (size_t)s * a.stage_bytes;
+        GroupItem v;
+        if (lane == 0) v = *stage_item(st, a.stage_bytes);
+        GroupItem item;
+        item.e = __shfl_sync(0xffffffffu, v.e, 0);
+        item.m0 = __shfl_sync(0xffffffffu, v.m0, 0);
+        item.mc = __shfl_sync(0xffffffffu, v.mc, 0);
+        item.tile = __shfl_sync(0xffffffffu, v.tile, 0);
+        if (item.e < 0) break;
+        if (item.e != cur_e || item.m0 != cur_m0) {
+            // a new run: release the previous run's activation slot, wait for this one's
+            if (run > 0 && lane == 0) mbar_arrive(&xempty[(run - 1) % ga.n_xslots]);
+            xs = run % ga.n_xslots;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded(&xfull[xs], (run / ga.n_xslots) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
+                break;
+            }
+            ++run;
+            cur_e = item.e;
+            cur_m0 = item.m0;
+        }
+        const XPlanes xp = packed_planes(smem + L.off_x + (size_t)xs * ga.xslot_bytes, a.K);
+        const ItemTile t = item_tile(ga, item, tile_bytes);
+        const uint8_t *stage = st + (t.g0 & 15);
+        if (item.mc == 1) group_tile_rows<QT, 1, A16>(ga, stage, xp, item, t, lm, warp);
+        else if (item.mc == 2) group_tile_rows<QT, 2, A16>(ga, stage, xp, item, t, lm, warp);
+        else if (item.mc <= 4) group_tile_rows<QT, 4, A16>(ga, stage, xp, item, t, lm, warp);
+        else group_tile_rows<QT, 8, A16>(ga, stage, xp, item, t, lm, warp);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+// activation element k of sorted row p: x[rows[p]] (or x[p]), or silu(clamp(g, +-80)) * u
+// of rows p of g = x and u = x2 (k_swiglu, quant_kernels_omp.c:2157-2164)
+struct GroupRows {
+    const float *x, *x2;
+    const int *rows;
+    int K;
+    __device__ __forceinline__ float operator()(int p, int k) const {
+        const size_t o = (size_t)(rows ? __ldg(rows + p) : p) * K + k;
+        float v = __ldg(x + o);
+        if (x2) {
+            const float g = fminf(fmaxf(v, -80.0f), 80.0f);
+            v = (g / (1.0f + expf(-g))) * __ldg(x2 + o);
+        }
+        return v;
+    }
+};
+
+// R packed activation rows: one warp per 32-element block (many independent warps: the
+// kernel is latency-bound on its loads, not on work)
+__global__ void __launch_bounds__(256) k_encode_packed(GroupRows src, int R, int K, uint8_t *__restrict__ planes) {
+    const int lane = threadIdx.x & 31;
+    const int kbr = K / 32;
+    const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (blk >= (long long)R * kbr) return;   // warp-uniform
+    const int p = (int)(blk / kbr), kb = (int)(blk - (long long)p * kbr);
+    const int prb = packed_row_bytes(K);
+    float *s = reinterpret_cast<float *>(planes + 2 * K);
+    encode_block(src(p, 32 * kb + lane), p, kb, K, reinterpret_cast<int8_t *>(planes),
+                 reinterpret_cast<int8_t *>(planes + K), s, s + K / 32, prb, prb / 4, lane);
+}
+
+// Host-free grouping: a stable order of the rows by expert and the work-item lists of up
+// to three tilings.  Deterministic and parallel: counts per expert (order-free atomics),
+// block-wide exclusive scans of the row and 8-row-chunk counts, then positions
+// kPlanThreads rows at a time (rank among the warp's rows of the same expert from
+// __match_any_sync, plus the counts of earlier warps and earlier row groups).
+constexpr int kPlanThreads = 256;
+constexpr int kPlanWarps = kPlanThreads / 32;
+constexpr int kPlanMaxE = 1024;
+
+struct PlanLists {
+    GroupItem *items[3];
+    int tiles[3];
+    int n;
+};
+
+__global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restrict__ eid, int R, int E, PlanLists pl,
+                                                             int *__restrict__ sorted_pos, int *__restrict__ src_row,
+                                                             int *__restrict__ n_items) {
+    extern __shared__ int sm_plan[];
+    int *run = sm_plan;          // [E] counts, then running positions
+    int *so = run + E;           // [E + 1] first sorted position of each expert
+    int *si = so + E + 1;        // [E + 1] first 8-row chunk of each expert
+    int *wc = si + E + 1;        // [kPlanWarps][E] counts of the current row group, then bases
+    __shared__ int wsum[2][kPlanWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < E; e += kPlanThreads) run[e] = 0;
+    __syncthreads();
+    for (int r = tid; r < R; r += kPlanThreads) {
+        const int e = eid[r];
+        if (e >= 0 && e < E) atomicAdd(&run[e], 1);
+    }
+    __syncthreads();
+    // exclusive scans; thread tid owns experts [tid * ept, (tid + 1) * ept)
+    const int ept = (E + kPlanThreads - 1) / kPlanThreads;
+    const int e0 = min(E, tid * ept), e1 = min(E, e0 + ept);
+    int own_r = 0, own_c = 0;
+    for (int e = e0; e < e1; e++) {
+        own_r += run[e];
+        own_c += (run[e] + 7) / 8;
+    }
+    int inc_r = own_r, inc_c = own_c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, inc_r, o), b = __shfl_up_sync(0xffffffffu, inc_c, o);
+        if (lane >= o) {
+            inc_r += a;
+            inc_c += b;
+        }
+    }
+    if (lane == 31) {
+        wsum[0][warp] = inc_r;
+        wsum[1][warp] = inc_c;
+    }
+    __syncthreads();
+    int pr = inc_r - own_r, pc = inc_c - own_c;
+    for (int w = 0; w < warp; w++) {
+        pr += wsum[0][w];
+        pc += wsum[1][w];
+    }
+    for (int e = e0; e < e1; e++) {
+        so[e] = pr;
+        si[e] = pc;
+        pr += run[e];
+        pc += (run[e] + 7) / 8;
+    }
+    if (tid == kPlanThreads - 1) {   // the last thread's running sums are the totals
+        so[E] = pr;
+        si[E] = pc;
+    }
+    __syncthreads();
+    if (tid < pl.n) n_items[tid] = si[E] * pl.tiles[tid];
+    for (int e = tid; e < E; e += kPlanThreads) run[e] = so[e];
+    __syncthreads();
+    // stable positions
+    for (int c0 = 0; c0 < R; c0 += kPlanThreads) {
+        const int r = c0 + tid;
+        const int e = r < R ? eid[r] : -1;
+        const bool valid = e >= 0 && e < E;
+        const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+        const int rank = __popc(same & ((1u << lane) - 1u));
+        for (int i = tid; i < kPlanWarps * E; i += kPlanThreads) wc[i] = 0;
+        __syncthreads();
+        if (valid && rank == 0) wc[warp * E + e] = __popc(same);
+        __syncthreads();
+        for (int x = tid; x < E; x += kPlanThreads) {
+            int acc = run[x];
+            for (int w = 0; w < kPlanWarps; w++) {
+                const int n = wc[w * E + x];
+                wc[w * E + x] = acc;
+                acc += n;
+            }
+            run[x] = acc;
+        }
+        __syncthreads();
+        if (valid) {
+            const int p = wc[warp * E + e] + rank;
+            sorted_pos[r] = p;
+            src_row[p] = r;
+        } else if (r < R) {
+            sorted_pos[r] = -1;
+        }
+        __syncthreads();
+    }
+    // positions past the valid rows (rows with an id outside [0, E)) read row 0, so that
+    // consumers of src_row stay in bounds
+    for (int p = so[E] + tid; p < R; p += kPlanThreads) src_row[p] = 0;
+    // items: warp per chunk (ascending), lanes over the tiles; the chunk's expert is found
+    // by advancing over si 32 experts per ballot (si is non-decreasing)
+    const int n_chunks = si[E];
+    int e = 0;
+    for (int c = warp; c < n_chunks; c += kPlanWarps) {
+        for (;;) {
+            const int x = e + 1 + lane;
+            const unsigned b = __ballot_sync(0xffffffffu, x < E && si[x] <= c);
+            e += __popc(b);
+            if (b != 0xffffffffu) break;
+        }
+        const int m0 = (c - si[e]) * 8;
+        const int mc = min(8, so[e + 1] - so[e] - m0);
+        for (int l = 0; l < pl.n; l++) {
+            const int T = pl.tiles[l];
+            GroupItem *dst = pl.items[l] + (size_t)c * T;
+            for (int t = lane; t < T; t += 32) dst[t] = GroupItem{e, so[e] + m0, mc, t};
         }
     }
 }
 
-__global__ void k_rows_permute(const float *__restrict__ src, const int *__restrict__ pos, int K, int to_sorted,
-                               float *__restrict__ dst) {
-    const int r = blockIdx.x;
-    const int p = pos[r];
-    if (p < 0) return;
-    const float *s = src + (size_t)(to_sorted ? r : p) * K;
-    float *d = dst + (size_t)(to_sorted ? p : r) * K;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) d[i] = s[i];
-}
-
-// rows per grouped tile: a multiple of the 8 decode warps, about kStageTarget bytes, <= 64
+// rows per grouped tile: a multiple of the 16 decode warps, about 36 KB (every item then
+// gives each warp one or more whole rows to amortise its bookkeeping over), <= 64
 static int grouped_rpt(long long rb) {
-    long long r = kStageTarget / rb;
-    r = r < 8 ? 8 : (r > 64 ? 64 : r);
-    return (int)(r / 8 * 8);
+    long long r = 36864 / rb;
+    r = r < 16 ? 16 : (r > 64 ? 64 : r);
+    return (int)(r / 16 * 16);
 }
 
-template <int QT>
-static int launch_grouped_t(const uint8_t *W, long long estride, const GroupItem *items, const int *n_items_dev,
-                            int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K,
-                            cudaStream_t s) {
+template <int QT, bool A16>
+static int launch_grouped_t(const GroupedCall &gc, cudaStream_t s) {
     const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
-    constexpr int M = 8;
-    const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
+    const long long rb = (long long)(gc.K / Fmt<QT>::BE) * Fmt<QT>::BB;
     const int rpt = grouped_rpt(rb);
     const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
-    const int fixed = gemv_layout(M, K, stage_bytes, 0).total;
-    const int n_stages = stages_for(fixed, stage_bytes);
+    const int xslot_bytes = 8 * packed_row_bytes(gc.K);
+    const int n_xslots = group_layout(xslot_bytes, 2, stage_bytes, 3).total <= kSmemBudget ? 2 : 1;
+    const int fixed = group_layout(xslot_bytes, n_xslots, stage_bytes, 0).total;
+    const int n_stages = fixed < kSmemBudget ? stages_for(fixed, stage_bytes) : 0;
     if (n_stages < 2) {
-        set_error(MLQ_ERR_CAPACITY, "grouped experts: K=%d too large for the stage ring", K);
+        set_error(MLQ_ERR_CAPACITY, "grouped experts: K=%d too large for the stage ring", gc.K);
         return MLQ_ERR_CAPACITY;
     }
+    const int U = gc.K / Fmt<QT>::UE;
+    int gs_log = 0;
+    while ((1 << gs_log) < U && gs_log < 5) gs_log++;
+    // items per round-robin group: about 128 KB of weights, fewer when the call is small
+    // enough that every SM should still get a couple of groups
+    const long long tb = (long long)rpt * rb;
+    long long G = 131072 / tb;
+    const long long spread = (long long)gc.n_items_bound / (2LL * c->num_sms);
+    if (spread < G) G = spread;
+    G = G < 1 ? 1 : (G > 32 ? 32 : G);
     GroupArgs ga{};
     GemvArgs &a = ga.g;
-    a.W = W; a.x = x_sorted; a.out = y_sorted; a.n_rows = n_rows; a.K = K; a.nb_x = M;
-    a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = 1;
+    a.W = gc.W; a.x = nullptr; a.out = gc.out; a.n_rows = gc.n_rows; a.K = gc.K; a.nb_x = 8;
+    a.row_bytes = rb; a.total_bytes = rb * gc.n_rows; a.rpt = rpt; a.wpr = 1;
     a.stage_bytes = stage_bytes; a.n_stages = n_stages; a.status = c->d_status;
-    ga.estride = estride;
-    ga.items = items;
-    ga.tiles_per_expert = (n_rows + rpt - 1) / rpt;
-    // the item count is only known on the device: the grid covers the bound and every CTA
-    // takes a contiguous share of the real count
-    ga.n_items = n_items_dev;
-    const int grid = n_items_bound < c->num_sms ? (n_items_bound > 0 ? n_items_bound : 1) : c->num_sms;
+    ga.estride = gc.estride;
+    ga.W2 = gc.W2; ga.estride2 = gc.estride2; ga.out2 = gc.out2;
+    ga.items = (const GroupItem *)gc.items;
+    ga.n_items = gc.n_items_dev;
+    ga.tiles_per_expert = (gc.n_rows + rpt - 1) / rpt;
+    ga.planes = gc.planes;
+    ga.n_xslots = n_xslots;
+    ga.xslot_bytes = xslot_bytes;
+    ga.group = (int)G;
+    ga.lane_group_log = gs_log;
+    ga.out_rows = gc.out_rows;
+    // the item count is only known on the device: the grid covers the bound
+    const int groups = (int)((gc.n_items_bound + G - 1) / G);
+    const int grid = groups < c->num_sms ? (groups > 0 ? groups : 1) : c->num_sms;
     static bool attr = false;
     if (!attr) {
-        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemv_grouped<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemv_grouped<QT, A16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kMaxSmem)))
             return MLQ_ERR_CUDA;
         attr = true;
     }
     count_launch();
-    return MLQ_CUDA(launch_pdl(k_gemv_grouped<QT>, dim3(grid), dim3(kThreads), fixed + n_stages * stage_bytes, s, ga))
+    return MLQ_CUDA(launch_pdl(k_gemv_grouped<QT, A16>, dim3(grid), dim3(kFastThreads),
+                               fixed + n_stages * stage_bytes, s, ga))
                ? MLQ_OK
                : MLQ_ERR_CUDA;
+}
+
+// Q4_K / Q5_K rows on 16-byte boundaries (row bytes, expert strides and bases all
+// multiples of 16) decode with 128-bit shared-memory loads
+template <int QT>
+static int launch_grouped_a(const GroupedCall &gc, cudaStream_t s) {
+    if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K) {
+        const long long rb = (long long)(gc.K / Fmt<QT>::BE) * Fmt<QT>::BB;
+        const bool al = rb % 16 == 0 && (reinterpret_cast<uintptr_t>(gc.W) & 15) == 0 && gc.estride % 16 == 0 &&
+                        (!gc.W2 || ((reinterpret_cast<uintptr_t>(gc.W2) & 15) == 0 && gc.estride2 % 16 == 0));
+        if (al) return launch_grouped_t<QT, true>(gc, s);
+    }
+    return launch_grouped_t<QT, false>(gc, s);
 }
 
 int grouped_tiles_per_expert(int qt, int n_rows, int K) {
@@ -914,41 +1195,52 @@ int grouped_tiles_per_expert(int qt, int n_rows, int K) {
     return (n_rows + rpt - 1) / rpt;
 }
 
-int launch_grouped(int qt, const uint8_t *W, long long estride, const void *items, const int *n_items_dev,
-                   int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K, cudaStream_t s) {
-    const GroupItem *it = (const GroupItem *)items;
-    switch (qt) {
-        case MLQ_Q4_0: return launch_grouped_t<MLQ_Q4_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q4_1: return launch_grouped_t<MLQ_Q4_1>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q5_0: return launch_grouped_t<MLQ_Q5_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q8_0: return launch_grouped_t<MLQ_Q8_0>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q4_K: return launch_grouped_t<MLQ_Q4_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q5_K: return launch_grouped_t<MLQ_Q5_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_Q6_K: return launch_grouped_t<MLQ_Q6_K>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_MXFP4: return launch_grouped_t<MLQ_MXFP4>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
-        case MLQ_MXFP4_REF: return launch_grouped_t<MLQ_MXFP4_REF>(W, estride, it, n_items_dev, n_items_bound, x_sorted, y_sorted, n_rows, K, s);
+size_t grouped_packed_bytes(int R, int K) { return (size_t)R * packed_row_bytes(K); }
+
+int launch_grouped(const GroupedCall &gc, cudaStream_t s) {
+    if (!gc.planes || (reinterpret_cast<uintptr_t>(gc.planes) & 15) || gc.K % 32) {
+        set_error(MLQ_ERR_ARG, "grouped experts: packed rows must be 16-byte aligned, K %% 32 == 0");
+        return MLQ_ERR_ARG;
+    }
+    switch (gc.qt) {
+        case MLQ_Q4_0: return launch_grouped_a<MLQ_Q4_0>(gc, s);
+        case MLQ_Q4_1: return launch_grouped_a<MLQ_Q4_1>(gc, s);
+        case MLQ_Q5_0: return launch_grouped_a<MLQ_Q5_0>(gc, s);
+        case MLQ_Q8_0: return launch_grouped_a<MLQ_Q8_0>(gc, s);
+        case MLQ_Q4_K: return launch_grouped_a<MLQ_Q4_K>(gc, s);
+        case MLQ_Q5_K: return launch_grouped_a<MLQ_Q5_K>(gc, s);
+        case MLQ_Q6_K: return launch_grouped_a<MLQ_Q6_K>(gc, s);
+        case MLQ_MXFP4: return launch_grouped_a<MLQ_MXFP4>(gc, s);
+        case MLQ_MXFP4_REF: return launch_grouped_a<MLQ_MXFP4_REF>(gc, s);
         default:
-            set_error(MLQ_ERR_TYPE, "grouped experts: type %d", qt);
+            set_error(MLQ_ERR_TYPE, "grouped experts: type %d", gc.qt);
             return MLQ_ERR_TYPE;
     }
 }
 
-int launch_group_plan(const int *eid, int R, int E, int tiles_a, int tiles_b, int *offs, int *sorted_pos,
-                      void *items_a, void *items_b, int *n_items, cudaStream_t s) {
-    const size_t sm = sizeof(int) * (3 * (size_t)E + 2 + (size_t)R);
-    if (sm > 48 * 1024) {
-        set_error(MLQ_ERR_CAPACITY, "grouped experts: %d experts / %d rows per call", E, R);
-        return MLQ_ERR_CAPACITY;
-    }
-    k_group_plan<<<1, 256, sm, s>>>(eid, R, E, tiles_a, tiles_b, offs, sorted_pos, (GroupItem *)items_a,
-                                    (GroupItem *)items_b, n_items);
+int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
+                         cudaStream_t s) {
+    if (R <= 0) return MLQ_OK;
+    const long long blocks = ((long long)R * (K / 32) + 7) / 8;
+    k_encode_packed<<<(unsigned)blocks, 256, 0, s>>>(GroupRows{x, x2, rows, K}, R, K, planes);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
-int launch_rows_permute(const float *src, const int *pos, int R, int K, int to_sorted, float *dst, cudaStream_t s) {
-    if (R <= 0) return MLQ_OK;
-    k_rows_permute<<<R, 256, 0, s>>>(src, pos, K, to_sorted, dst);
+int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,
+                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s) {
+    if (E <= 0 || E > kPlanMaxE || n_lists < 1 || n_lists > 3) {
+        set_error(MLQ_ERR_CAPACITY, "grouped experts: %d experts (1..%d), %d item lists", E, kPlanMaxE, n_lists);
+        return MLQ_ERR_CAPACITY;
+    }
+    PlanLists pl{};
+    pl.n = n_lists;
+    for (int l = 0; l < n_lists; l++) {
+        pl.items[l] = (GroupItem *)items[l];
+        pl.tiles[l] = tiles[l];
+    }
+    const size_t sm = sizeof(int) * (3 * (size_t)E + 2 + (size_t)kPlanWarps * E);
+    k_group_plan<<<1, kPlanThreads, sm, s>>>(eid, R, E, pl, sorted_pos, src_row, n_items);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }

@@ -149,13 +149,33 @@ int launch_moe_experts(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
                        long long gs, long long us, long long ds, const int *idx, const float *w, int top_k,
                        int n_tok, int n_ff, int N, const float *x, float *h, float *h2, float *out,
                        const float *residual, float clamp, cudaStream_t s);
-// grouped expert GEMV (gemv.cu): rows sorted by expert, each active expert streamed once
+// grouped expert GEMV (gemv.cu): rows ordered by expert, each active expert streamed once
+struct GroupedCall {
+    int qt;
+    const uint8_t *W;          // expert 0 of the first matrix; experts estride bytes apart
+    long long estride;
+    float *out;                // [rows][n_rows]
+    const uint8_t *W2;         // optional second matrix of the same type and shape (tiles >= T)
+    long long estride2;
+    float *out2;
+    const void *items;         // planner item list
+    const int *n_items_dev;    // its length, on the device
+    int n_items_bound;         // host bound of that length (grid size)
+    const uint8_t *planes;     // packed activation rows in sorted order (launch_encode_packed)
+    const int *out_rows;       // sorted position -> row of out / out2 (identity if null)
+    int n_rows, K;             // of one expert's matrix
+};
 int grouped_tiles_per_expert(int qt, int n_rows, int K);
-int launch_group_plan(const int *eid, int R, int E, int tiles_a, int tiles_b, int *offs, int *sorted_pos,
-                      void *items_a, void *items_b, int *n_items, cudaStream_t s);
-int launch_grouped(int qt, const uint8_t *W, long long estride, const void *items, const int *n_items_dev,
-                   int n_items_bound, const float *x_sorted, float *y_sorted, int n_rows, int K, cudaStream_t s);
-int launch_rows_permute(const float *src, const int *pos, int R, int K, int to_sorted, float *dst, cudaStream_t s);
+size_t grouped_packed_bytes(int R, int K);
+int launch_grouped(const GroupedCall &gc, cudaStream_t s);
+// packed activation rows p < R: x[rows[p]] (rows may be null: x[p]); with x2 set,
+// silu(clamp(x[p], +-80)) * x2[p]
+int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
+                         cudaStream_t s);
+// stable order of R rows by expert id (sorted_pos[r], src_row[p]) and the item lists of
+// n_lists tilings (tiles[l] tiles per 8-row chunk; n_items[l] written on the device)
+int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,
+                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s);
 // batch-engine embedding rows (qwen36.cu)
 int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_tok, float *x, int B, int N, int V,
                  cudaStream_t s);

@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
             if (ok && Wg && row0 + r < a.n_rows) {
                 const int xr = (a.nx == 1) ? 0 : g;
                 const XPlanes xp{xh + (size_t)xr * a.K, xl + (size_t)xr * a.K, xs + (size_t)xr * (a.K / 32),
-                                 xsum + (size_t)xr * (a.K / 32), a.K};
+                                 xsum + (size_t)xr * (a.K / 32), a.K, a.K, a.K / 32};
                 const uintptr_t g0 = reinterpret_cast<uintptr_t>(Wg) + (uintptr_t)(tile * tile_bytes);
                 const uint8_t *rowp = smem + L.off_stage + (size_t)s * stage_bytes + (size_t)g * a.slot_bytes +
                                       (g0 & 15) + (size_t)r * a.row_bytes;

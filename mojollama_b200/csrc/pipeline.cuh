@@ -72,6 +72,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// L2 eviction policy for data that many CTAs read again (activation rows)
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // L2 eviction policy for data read exactly once (weights streamed by a GEMV)
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
