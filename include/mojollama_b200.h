@@ -90,6 +90,17 @@ size_t mlq_row_bytes(int qt, int n_cols);  /* 0 if n_cols is not a multiple of t
  * x: [B][n_cols] fp32, out: [B][n_rows] fp32 (the reference's batch layout,
  * cengine_batch_instr.c:251). */
 int mlq_matmul(const void *W, int qt, const float *x, float *out, int n_rows, int n_cols, int B);
+
+/* Decode GEMV of the batch engine's step (B <= 8) over n (1..4) matrices of one type that
+   share the input x [B][K] (device pointers throughout): mode 0 out_i[B][n_rows_i] = x W_i^T;
+   mode 1 out_i = res_i + x W_i^T (residual add folded in); mode 2 (n = 2, equal rows)
+   out_0 = silu(x W_0^T) * (x W_1^T) (gate/up with the SiLU-mul).  The step's projections
+   in batch_forward (cengine_batch_instr.c:1349-1351 q/k/v, :1409 o + residual add,
+   :1463-1467 gate/up/silu/down + residual add, :1492 output head).
+   MLQ_ERR_UNSUPPORTED when the shape or type is outside the kernel (the batch engine then
+   uses mlq_matmul's path). */
+int mlq_gemv_fused(int qt, int n, const void *const *W, const int *n_rows, float *const *out,
+                   const float *const *res, int mode, const float *x, int B, int K);
 /* dequantize n values of type qt to fp32, bit-identical to gguf-py / the reference */
 int mlq_dequantize(const void *W, int qt, float *out, int64_t n);
 /* the reference's Q8_0 activation quantizer, byte-identical (quant_kernels_omp.c:1406) */

@@ -53,6 +53,7 @@ def core() -> ctypes.CDLL:
     so.mlq_row_bytes.argtypes = [_ci, _ci]
     so.mlq_row_bytes.restype = ctypes.c_size_t
     so.mlq_matmul.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
+    so.mlq_gemv_fused.argtypes = [_ci, _ci, _vp, _vp, _vp, _vp, _ci, _vp, _ci, _ci]
     so.mlq_dequantize.argtypes = [_vp, _ci, _vp, ctypes.c_int64]
     so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
     so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]

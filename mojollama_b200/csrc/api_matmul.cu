@@ -44,6 +44,34 @@ int mlq_matmul(const void *W, int qt, const float *x, float *out, int n_rows, in
     return cs.finish();
 }
 
+int mlq_gemv_fused(int qt, int n, const void *const *W, const int *n_rows, float *const *out,
+                   const float *const *res, int mode, const float *x, int B, int K) {
+    if (n < 1 || n > 4 || !W || !n_rows || !out || !x || B < 1 || B > 8 || K <= 0 || mode < 0 || mode > 2 ||
+        (mode == 1 && !res) || (mode == 2 && n != 2)) {
+        set_error(MLQ_ERR_ARG, "mlq_gemv_fused: bad arguments (n 1..4, B 1..8, mode 0..2)");
+        return MLQ_ERR_ARG;
+    }
+    if (!is_device_ptr(x)) {
+        set_error(MLQ_ERR_ARG, "mlq_gemv_fused: device pointers only");
+        return MLQ_ERR_ARG;
+    }
+    CallScope cs;
+    uint8_t *planes = (uint8_t *)cs.scratch(packed_rows_bytes(B, K));
+    if (cs.failed) return cs.finish();
+    cudaStream_t s = stream();
+    int rc = K % 32 ? MLQ_ERR_UNSUPPORTED : launch_encode_packed(x, nullptr, nullptr, B, K, planes, s);
+    if (rc == MLQ_OK)
+        rc = launch_gemv_seg(qt, n, (const uint8_t *const *)W, n_rows, out, mode == 1 ? res : nullptr, mode == 2,
+                             planes, B, K, s);
+    if (rc == MLQ_ERR_UNSUPPORTED) {
+        set_error(rc, "mlq_gemv_fused: type %d, K=%d, B=%d not covered", qt, K, B);
+        cs.finish();
+        return rc;
+    }
+    if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
+    return cs.finish();
+}
+
 int mlq_dequantize(const void *W, int qt, float *out, int64_t n) {
     if (!W || !out || n <= 0) {
         set_error(MLQ_ERR_ARG, "mlq_dequantize: null pointer or non-positive n");

@@ -527,6 +527,20 @@ __device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> 
 // than once per block.
 constexpr int kEncBatch = 8;
 
+// Packed activation row (the x planes of one row in global memory, copied to shared memory
+// as a whole): [K int8 h][K int8 l][K/32 f32 s][K/32 f32 sum], padded to 16 bytes.
+__host__ __device__ inline int packed_row_bytes(int K) { return (2 * K + (K / 32) * 8 + 15) / 16 * 16; }
+
+__device__ __forceinline__ XPlanes packed_planes(const uint8_t *base, int K) {
+    const int rb = packed_row_bytes(K);
+    const float *s = reinterpret_cast<const float *>(base + 2 * K);
+    return XPlanes{reinterpret_cast<const int8_t *>(base), reinterpret_cast<const int8_t *>(base + K), s, s + K / 32,
+                   K, rb, rb / 4};
+}
+
+// encode one 32-element block into row m of a packed buffer
+__device__ __forceinline__ void encode_block_packed(float v, int m, int kb, int K, uint8_t *planes, int lane);
+
 // Block kb of row m from its 32 values (one per lane).
 __device__ __forceinline__ void encode_block(float v, int m, int kb, int K, int8_t *xh, int8_t *xl, float *xs,
                                              float *xsum, int hs, int ss, int lane) {
@@ -556,6 +570,13 @@ __device__ __forceinline__ void encode_block(float v, int m, int kb, int K, int8
         xs[(size_t)m * ss + kb] = scale;
         xsum[(size_t)m * ss + kb] = sum;
     }
+}
+
+__device__ __forceinline__ void encode_block_packed(float v, int m, int kb, int K, uint8_t *planes, int lane) {
+    const int prb = packed_row_bytes(K);
+    float *s = reinterpret_cast<float *>(planes + 2 * K);
+    encode_block(v, m, kb, K, reinterpret_cast<int8_t *>(planes), reinterpret_cast<int8_t *>(planes + K), s,
+                 s + K / 32, prb, prb / 4, lane);
 }
 
 template <typename Src>

@@ -360,6 +360,7 @@ struct StepBufs {
           *v = nullptr, *att = nullptr, *tmp = nullptr, *g = nullptr, *u = nullptr, *h = nullptr, *logits_e = nullptr,
           *e_w = nullptr, *hm = nullptr, *hm2 = nullptr, *score = nullptr, *attn_scr = nullptr, *hfin = nullptr,
           *logits = nullptr, *state = nullptr;
+    uint8_t *px = nullptr, *pa = nullptr, *ph = nullptr;   // packed activation rows (decode GEMV inputs)
     size_t attn_sb = 0;
 };
 
@@ -417,6 +418,9 @@ static size_t carve(StepBufs &b, uint8_t *base, const StepDims &d) {
     b.hfin = (float *)take(B * d.N * 4);
     b.logits = (float *)take(B * (size_t)d.outNR * 4);
     b.state = d.ssm ? (float *)take((size_t)d.L * kSsmGroups * kSsmState * 4) : nullptr;
+    b.px = take(packed_rows_bytes(d.B, d.N));
+    b.pa = take(packed_rows_bytes(d.B, d.inner));
+    b.ph = take(packed_rows_bytes(d.B, wide));
     return o;
 }
 
@@ -477,9 +481,28 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
     float *nout = compat ? x : xn;
     const float *pin = compat ? xin : xn;
     const float inf = HUGE_VALF;
+    // Decode path (B <= 8, outside compatibility mode): every RMSNorm also writes its rows
+    // as packed activation rows, and the projections run as segmented decode GEMVs on them
+    // (Q/K/V of one type in one launch, gate/up with the SiLU-mul, o/down with the residual
+    // add); a shape the decode GEMV does not take falls back to the plain GEMV.
+    const bool fast = !compat && B <= 8 && N % 32 == 0 && inner % 32 == 0 && c->FF % 32 == 0 &&
+                      !getenv("MLQ_NO_DECODE_GEMV");
+    auto norm = [&](const float *w, float *out_fp32) -> int {
+        if (fast && launch_rms_norm_encode(out_fp32, x, w, res, B, N, c->eps, 1, sb.px, s) == MLQ_OK) return MLQ_OK;
+        return launch_rms_norm(out_fp32, x, w, res, B, N, c->eps, 1, s);
+    };
+    // seg GEMV over n matrices sharing input planes; false: not taken (caller falls back)
+    auto seg = [&](int qt, int n, const uint8_t *const *W, const int *rows, float *const *out, const float *const *rs,
+                   int pair, const uint8_t *planes, int K) -> bool {
+        if (!fast || rc != MLQ_OK) return false;
+        const int r2 = launch_gemv_seg(qt, n, W, rows, out, rs, pair, planes, B, K, s);
+        if (r2 == MLQ_ERR_UNSUPPORTED) return false;
+        rc = r2;
+        return true;
+    };
     for (int l = 0; l < L && rc == MLQ_OK; l++) {
         const LayerPlan &lp = P->layers[l];
-        MLQ_TRY(launch_rms_norm(nout, x, lp.an, res, B, N, c->eps, 1, s));
+        MLQ_TRY(norm(lp.an, nout));
         if (lp.ssm) {
             float *st = d_state + (size_t)l * kSsmGroups * kSsmState;
             MLQ_TRY(launch_ssm_decode_step(pin, att, lp.conv, lp.ssm_a, lp.ssm_dt, lp.ssm_alpha, lp.ssm_beta, st, B, N,
@@ -515,9 +538,26 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
                 count_launch(2);
                 MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
             } else {
-                MLQ_TRY(launch_matmul(lp.wq, lp.qq, pin, q, lp.nq, c->nc, B, 0, s));
-                MLQ_TRY(launch_matmul(lp.wk, lp.qk, pin, k, lp.nk, c->nc, B, 0, s));
-                MLQ_TRY(launch_matmul(lp.wv, lp.qv, pin, v, lp.nv, c->nc, B, 0, s));
+                // Q, K, V grouped by type into decode GEMV launches
+                const uint8_t *Wm[3] = {lp.wq, lp.wk, lp.wv};
+                const int qts[3] = {lp.qq, lp.qk, lp.qv}, rows[3] = {lp.nq, lp.nk, lp.nv};
+                float *outs[3] = {q, k, v};
+                bool done[3] = {false, false, false};
+                for (int i = 0; i < 3 && fast && c->nc == N; i++) {
+                    if (done[i]) continue;
+                    const uint8_t *gw[3];
+                    int gr[3], n = 0;
+                    float *go[3];
+                    int idx[3];
+                    for (int j = i; j < 3; j++)
+                        if (!done[j] && qts[j] == qts[i]) {
+                            gw[n] = Wm[j]; gr[n] = rows[j]; go[n] = outs[j]; idx[n++] = j;
+                        }
+                    if (seg(qts[i], n, gw, gr, go, nullptr, 0, sb.px, N))
+                        for (int j = 0; j < n; j++) done[idx[j]] = true;
+                }
+                for (int i = 0; i < 3; i++)
+                    if (!done[i]) MLQ_TRY(launch_matmul(Wm[i], qts[i], pin, outs[i], rows[i], c->nc, B, 0, s));
             }
             MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
             MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
@@ -531,11 +571,22 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
             }
             MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, 0, scale, att, sb.attn_scr,
                                        sb.attn_sb, s));
-            if (lp.wattng) MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, att, tmp, N, inner, B, 0, s));
-            else MLQ_TRY(launch_matmul(lp.wo, lp.qo, att, tmp, lp.no, inner, B, 0, s));
-            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            bool o_done = false;
+            if (fast && !lp.wattng && lp.no == N && rc == MLQ_OK) {   // x = res + W_o att
+                MLQ_TRY(launch_encode_packed(att, nullptr, nullptr, B, inner, sb.pa, s));
+                const uint8_t *wo = lp.wo;
+                const int no = lp.no;
+                float *xo = x;
+                const float *ro = res;
+                o_done = seg(lp.qo, 1, &wo, &no, &xo, &ro, 0, sb.pa, inner);
+            }
+            if (!o_done) {
+                if (lp.wattng) MLQ_TRY(launch_matmul(lp.wattng, lp.qattng, att, tmp, N, inner, B, 0, s));
+                else MLQ_TRY(launch_matmul(lp.wo, lp.qo, att, tmp, lp.no, inner, B, 0, s));
+                MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            }
         }
-        MLQ_TRY(launch_rms_norm(nout, x, lp.fn, res, B, N, c->eps, 1, s));
+        MLQ_TRY(norm(lp.fn, nout));
         if (lp.router) {
             const int E = c->n_experts;
             MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, sb.logits_e, E, N, B, 0, s));
@@ -555,20 +606,46 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
                 count_launch();
             }
         } else if (lp.wg) {
-            MLQ_TRY(launch_matmul(lp.wg, lp.qg, pin, g, lp.ng, c->nc, B, 0, s));
-            MLQ_TRY(launch_matmul(lp.wu, lp.qu, pin, u, lp.nu, c->nc, B, 0, s));
-            k_silu_mul<<<grid1((long long)B * c->FF), 256, 0, s>>>(h, g, u, (long long)B * c->FF);
-            count_launch();
-            MLQ_TRY(launch_matmul(lp.wd, lp.qd, h, tmp, lp.nd, c->FF, B, 0, s));
-            MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            bool h_done = false;
+            if (lp.qg == lp.qu && lp.ng == lp.nu && lp.ng == c->FF && c->nc == N) {   // h = silu(W_g x) * (W_u x)
+                const uint8_t *gu[2] = {lp.wg, lp.wu};
+                const int rows[2] = {lp.ng, lp.nu};
+                float *ho[2] = {h, h};
+                h_done = seg(lp.qg, 2, gu, rows, ho, nullptr, 1, sb.px, N);
+            }
+            if (!h_done) {
+                MLQ_TRY(launch_matmul(lp.wg, lp.qg, pin, g, lp.ng, c->nc, B, 0, s));
+                MLQ_TRY(launch_matmul(lp.wu, lp.qu, pin, u, lp.nu, c->nc, B, 0, s));
+                k_silu_mul<<<grid1((long long)B * c->FF), 256, 0, s>>>(h, g, u, (long long)B * c->FF);
+                count_launch();
+            }
+            bool d_done = false;
+            if (fast && lp.nd == N && rc == MLQ_OK) {   // x = res + W_d h
+                MLQ_TRY(launch_encode_packed(h, nullptr, nullptr, B, c->FF, sb.ph, s));
+                const uint8_t *wd = lp.wd;
+                const int nd = lp.nd;
+                float *xo = x;
+                const float *ro = res;
+                d_done = seg(lp.qd, 1, &wd, &nd, &xo, &ro, 0, sb.ph, c->FF);
+            }
+            if (!d_done) {
+                MLQ_TRY(launch_matmul(lp.wd, lp.qd, h, tmp, lp.nd, c->FF, B, 0, s));
+                MLQ_TRY(launch_add(x, res, tmp, (long long)B * N, s));
+            }
         } else if (!compat) {
             cudaMemcpyAsync(x, res, sizeof(float) * (size_t)B * N, cudaMemcpyDeviceToDevice, s);
         }   // (with no FFN the reference leaves the normalised activations in x)
     }
     // the final normalised hidden state also lands in ws[0 : B*N], where the reference
     // leaves it (its x buffer is the start of the workspace)
-    MLQ_TRY(launch_rms_norm(hfin, x, P->onw, res, B, N, c->eps, 1, s));
-    MLQ_TRY(launch_matmul(P->wout, c->outQuant, hfin, d_logits, c->outNR, c->outNC, B, 0, s));
+    MLQ_TRY(norm(P->onw, hfin));
+    {
+        const uint8_t *wout = P->wout;
+        const int nr = c->outNR;
+        float *lo = d_logits;
+        if (!(c->outNC == N && seg(c->outQuant, 1, &wout, &nr, &lo, nullptr, 0, sb.px, N)))
+            MLQ_TRY(launch_matmul(P->wout, c->outQuant, hfin, d_logits, c->outNR, c->outNC, B, 0, s));
+    }
 #undef MLQ_TRY
     return rc;
 }

@@ -660,16 +660,6 @@ int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_ro
 // all SMs.  The producer hands every tile's item to the decode warps in the stage itself.
 struct GroupItem { int e, m0, mc, tile; };
 
-// packed activation row: [K int8 h][K int8 l][K/32 f32 s][K/32 f32 sum], 16-byte multiple
-__host__ __device__ inline int packed_row_bytes(int K) { return align_up(2 * K + (K / 32) * 8, 16); }
-
-__device__ __forceinline__ XPlanes packed_planes(const uint8_t *base, int K) {
-    const int rb = packed_row_bytes(K);
-    const float *s = reinterpret_cast<const float *>(base + 2 * K);
-    return XPlanes{reinterpret_cast<const int8_t *>(base), reinterpret_cast<const int8_t *>(base + K), s, s + K / 32,
-                   K, rb, rb / 4};
-}
-
 struct GroupArgs {
     GemvArgs g;                 // W / out: first matrix; n_rows / K / row_bytes of one expert
     long long estride;          // bytes between experts of the first matrix
@@ -976,10 +966,7 @@ __global__ void __launch_bounds__(256) k_encode_packed(GroupRows src, int R, int
     const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (blk >= (long long)R * kbr) return;   // warp-uniform
     const int p = (int)(blk / kbr), kb = (int)(blk - (long long)p * kbr);
-    const int prb = packed_row_bytes(K);
-    float *s = reinterpret_cast<float *>(planes + 2 * K);
-    encode_block(src(p, 32 * kb + lane), p, kb, K, reinterpret_cast<int8_t *>(planes),
-                 reinterpret_cast<int8_t *>(planes + K), s, s + K / 32, prb, prb / 4, lane);
+    encode_block_packed(src(p, 32 * kb + lane), p, kb, K, planes, lane);
 }
 
 // Host-free grouping: a stable order of the rows by expert and the work-item lists of up
@@ -1244,6 +1231,364 @@ int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *it
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }
+
+// ------------------------------------------------------------------------------ decode GEMV
+// Segmented decode GEMV for the batch engine's B <= 8 step: up to four matrices of one
+// type sharing one input (Q, K and V; gate and up) in one launch, the input read as
+// packed activation rows that an earlier kernel encoded once (the RMSNorm, or
+// k_encode_packed), and the step's elementwise neighbours folded into the store:
+//   plain     out_s[m][r] = W_s[r] . x_m
+//   residual  out_s[m][r] = res_s[m][r] + W_s[r] . x_m          (o / down + residual add)
+//   pair      out[m][r] = silu(G[r] . x_m) * (U[r] . x_m)        (gate / up + SiLU-mul)
+// The producer warp streams the weight tiles it will need before waiting for the previous
+// kernel (programmatic dependent launch: weights do not depend on it), then bulk-copies the
+// activation rows once; 16 decode warps take the rows of every tile (lane groups for short
+// rows) with each unit decoded once and dotted with all B rows.
+constexpr int kSegMax = 4;
+
+struct SegArgs {
+    const uint8_t *W[kSegMax];
+    float *out[kSegMax];
+    const float *res[kSegMax];    // residual of each segment (null: plain store)
+    int n_rows[kSegMax];
+    int tile0[kSegMax + 1];       // first tile of each segment; tile0[n_seg] = all tiles
+    int n_seg;
+    int pair;                     // segments 0 / 1 are gate / up of one shape; tiles cover both
+    const uint8_t *planes;        // packed activation rows [B]
+    int B, K;
+    long long row_bytes;
+    int rpt, region_bytes, stage_bytes, n_stages, gs_log;
+    int *status;
+};
+
+struct SegLayout {
+    int off_bar, off_flag, off_x, off_stage, total;
+};
+
+__host__ __device__ inline SegLayout seg_layout(int x_bytes, int stage_bytes, int n_stages) {
+    SegLayout L;
+    int o = 0;
+    L.off_bar = o;   o += (2 * kMaxStages + 1) * 8;   // full, empty, x_full
+    L.off_flag = o;  o += 16;
+    o = align_up(o, 128);
+    L.off_x = o;     o = align_up(o + x_bytes, 128);
+    L.off_stage = o; o += n_stages * stage_bytes;
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ int seg_of(const SegArgs &a, int tile) {
+    int s = 0;
+    while (s + 1 < a.n_seg && tile >= a.tile0[s + 1]) s++;
+    return s;
+}
+
+// Stage the byte range of local tile lt of matrix W (n_rows rows) into a region: lanes
+// copy the ragged head / tail, the 16-byte-aligned interior is returned for one bulk copy.
+struct BulkPart {
+    uint8_t *dst;
+    const void *src;
+    uint32_t bytes;
+};
+__device__ __forceinline__ BulkPart stage_tile_bytes(const SegArgs &a, const uint8_t *W, int n_rows, int lt,
+                                                     uint8_t *region, int lane) {
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    const long long b0 = (long long)lt * tile_bytes;
+    const long long b1 = min(b0 + tile_bytes, (long long)n_rows * a.row_bytes);
+    const uintptr_t g0 = reinterpret_cast<uintptr_t>(W) + (uintptr_t)b0;
+    const uintptr_t g1 = reinterpret_cast<uintptr_t>(W) + (uintptr_t)b1;
+    const uintptr_t gd = g0 & ~uintptr_t(15);
+    const uintptr_t j0 = (g0 + 15) & ~uintptr_t(15);
+    const uintptr_t j1 = g1 & ~uintptr_t(15);
+    if (j1 > j0) {
+        if (g0 + lane < j0) region[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+        if (j1 + lane < g1) region[j1 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(j1 + lane));
+        return BulkPart{region + (j0 - gd), reinterpret_cast<const void *>(j0), (uint32_t)(j1 - j0)};
+    }
+    if (g0 + lane < g1) region[g0 + lane - gd] = ldg_u8_nc(reinterpret_cast<const uint8_t *>(g0 + lane));
+    return BulkPart{nullptr, nullptr, 0};
+}
+
+__device__ __forceinline__ void seg_issue(const SegArgs &a, int tile, uint8_t *st, uint64_t *full, uint64_t pol,
+                                          int lane) {
+    BulkPart p0, p1{nullptr, nullptr, 0};
+    if (a.pair) {
+        p0 = stage_tile_bytes(a, a.W[0], a.n_rows[0], tile, st, lane);
+        p1 = stage_tile_bytes(a, a.W[1], a.n_rows[1], tile, st + a.region_bytes, lane);
+    } else {
+        const int s = seg_of(a, tile);
+        p0 = stage_tile_bytes(a, a.W[s], a.n_rows[s], tile - a.tile0[s], st, lane);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        const uint32_t tx = p0.bytes + p1.bytes;
+        if (tx) {
+            mbar_arrive_expect_tx(full, tx);
+            if (p0.bytes) bulk_g2s(p0.dst, p0.src, p0.bytes, full, pol);
+            if (p1.bytes) bulk_g2s(p1.dst, p1.src, p1.bytes, full, pol);
+        } else {
+            mbar_arrive(full);
+        }
+    }
+}
+
+// dot of staged row r (region base + its head offset) with the B activation rows
+template <int QT, int MC, bool A16>
+__device__ __forceinline__ void seg_row_dot(const uint8_t *row, const XPlanes &xp, int B, int U, int GS, int gl,
+                                            float (&acc)[MC]) {
+    for (int u = gl; u < U; u += GS) {
+        W<QT> w;
+        if constexpr (A16) w.decode_a16(row, u);
+        else w.decode(row, u);
+#pragma unroll
+        for (int m = 0; m < MC; m++) {
+            if (m < B) {
+                XU<QT> xu;
+                load_xu<QT>(xp, m, u, xu);
+                acc[m] += w.dot(xu);
+            }
+        }
+    }
+}
+
+template <int QT, int MC, bool A16>
+__global__ void __launch_bounds__(kFastThreads, 1) k_gemv_seg(SegArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int prb = packed_row_bytes(a.K);
+    const SegLayout L = seg_layout(a.B * prb, a.stage_bytes, a.n_stages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
+    uint64_t *empty = full + kMaxStages;
+    uint64_t *xfull = empty + kMaxStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = a.tile0[a.n_seg];
+    const int n_iter = (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.n_stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kFastWarps);
+        }
+        mbar_init(xfull, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    uint8_t *stages = smem + L.off_stage;
+    if (warp == kFastWarps) {
+        const uint64_t pol = policy_evict_first();
+        // the first stages' weights before the wait: they do not depend on the previous kernel
+        const int pre = n_iter < a.n_stages ? n_iter : a.n_stages;
+        for (int it = 0; it < pre; ++it)
+            seg_issue(a, (int)blockIdx.x + it * (int)gridDim.x, stages + (size_t)it * a.stage_bytes, &full[it], pol,
+                      lane);
+        pdl_wait();
+        pdl_trigger();
+        if (lane == 0) {
+            const uint32_t xb = (uint32_t)(a.B * prb);
+            mbar_arrive_expect_tx(xfull, xb);
+            bulk_g2s(smem + L.off_x, a.planes, xb, xfull, policy_evict_last());
+        }
+        for (int it = pre; it < n_iter; ++it) {
+            const int s = it % a.n_stages;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / a.n_stages) - 1) & 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok || *abort_flag) {
+                if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_EMPTY); }
+                return;
+            }
+            seg_issue(a, (int)blockIdx.x + it * (int)gridDim.x, stages + (size_t)s * a.stage_bytes, &full[s], pol,
+                      lane);
+        }
+        return;
+    }
+    pdl_wait();   // the residual rows are an earlier kernel's output too
+    pdl_trigger();
+    {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(xfull, 0);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
+            return;
+        }
+    }
+    const XPlanes xp = packed_planes(smem + L.off_x, a.K);
+    const int GS = 1 << a.gs_log, RPW = 32 >> a.gs_log;
+    const int gi = lane >> a.gs_log, gl = lane & (GS - 1);
+    const int U = a.K / Fmt<QT>::UE;
+    const long long tile_bytes = (long long)a.rpt * a.row_bytes;
+    for (int it = 0; it < n_iter; ++it) {
+        const int s = it % a.n_stages;
+        bool ok = !*abort_flag;
+        if (ok && lane == 0) ok = mbar_wait_bounded(&full[s], (it / a.n_stages) & 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            if (lane == 0) { *abort_flag = 1; raise_status(a.status, DEV_ST_WAIT_FULL); }
+            return;
+        }
+        const int tile = (int)blockIdx.x + it * (int)gridDim.x;
+        const int sg = a.pair ? 0 : seg_of(a, tile);
+        const int lt = a.pair ? tile : tile - a.tile0[sg];
+        const int nr = a.n_rows[sg];
+        const uint8_t *st = stages + (size_t)s * a.stage_bytes;
+        const uint8_t *ra = st + ((reinterpret_cast<uintptr_t>(a.W[sg]) + (uintptr_t)(lt * tile_bytes)) & 15);
+        const uint8_t *rb2 = st + a.region_bytes +
+                             ((reinterpret_cast<uintptr_t>(a.W[1]) + (uintptr_t)(lt * tile_bytes)) & 15);
+        for (int base = 0; warp + kFastWarps * base < a.rpt; base += RPW) {
+            const int r = warp + kFastWarps * (base + gi);
+            const int row = lt * a.rpt + r;
+            const bool v = r < a.rpt && row < nr;
+            float acc[MC];
+#pragma unroll
+            for (int m = 0; m < MC; m++) acc[m] = 0.0f;
+            if (v) seg_row_dot<QT, MC, A16>(ra + (size_t)r * a.row_bytes, xp, a.B, U, GS, gl, acc);
+#pragma unroll
+            for (int m = 0; m < MC; m++) {
+                if (m < a.B) {
+                    for (int o = GS >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                }
+            }
+            if (a.pair) {
+                float acc2[MC];
+#pragma unroll
+                for (int m = 0; m < MC; m++) acc2[m] = 0.0f;
+                if (v) seg_row_dot<QT, MC, A16>(rb2 + (size_t)r * a.row_bytes, xp, a.B, U, GS, gl, acc2);
+#pragma unroll
+                for (int m = 0; m < MC; m++) {
+                    if (m < a.B) {
+                        for (int o = GS >> 1; o > 0; o >>= 1) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                    }
+                }
+                if (gl == 0 && v) {   // h = silu(g) * u, exact (cengine_batch_instr.c:1465)
+#pragma unroll
+                    for (int m = 0; m < MC; m++) {
+                        if (m < a.B) {
+                            const float gv = acc[m];
+                            a.out[0][(size_t)m * nr + row] = (gv / (1.0f + expf(-gv))) * acc2[m];
+                        }
+                    }
+                }
+            } else if (gl == 0 && v) {
+                const float *res = a.res[sg];
+                float *out = a.out[sg];
+#pragma unroll
+                for (int m = 0; m < MC; m++) {
+                    if (m < a.B) {
+                        const size_t o = (size_t)m * nr + row;
+                        out[o] = res ? res[o] + acc[m] : acc[m];
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+template <int QT, int MC, bool A16>
+static int launch_seg_t(const SegArgs &a, int smem, cudaStream_t s) {
+    const LaunchEnv *c = launch_env();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemv_seg<QT, MC, A16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kMaxSmem)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    const int n_tiles = a.tile0[a.n_seg];
+    const int grid = n_tiles < c->num_sms ? n_tiles : c->num_sms;
+    count_launch();
+    return MLQ_CUDA(launch_pdl(k_gemv_seg<QT, MC, A16>, dim3(grid), dim3(kFastThreads), smem, s, a)) ? MLQ_OK
+                                                                                                      : MLQ_ERR_CUDA;
+}
+
+template <int QT>
+static int launch_seg_q(SegArgs &a, cudaStream_t s) {
+    const LaunchEnv *c = launch_env();
+    if (!c) return MLQ_ERR_NO_DEVICE;
+    if (a.K % Fmt<QT>::BE || a.K % 32) return MLQ_ERR_UNSUPPORTED;
+    const long long rb = (long long)(a.K / Fmt<QT>::BE) * Fmt<QT>::BB;
+    const int mats = a.pair ? 2 : 1;
+    long long rpt = 24576 / (rb * mats);
+    rpt = rpt < 16 ? 16 : (rpt > 64 ? 64 : rpt);
+    a.rpt = (int)(rpt / 16 * 16);
+    a.row_bytes = rb;
+    a.region_bytes = align_up((int)(a.rpt * rb), 16) + 32;
+    a.stage_bytes = mats * a.region_bytes;
+    const int x_bytes = a.B * packed_row_bytes(a.K);
+    const int fixed = seg_layout(x_bytes, a.stage_bytes, 0).total;
+    const int n_stages = fixed < kSmemBudget ? stages_for(fixed, a.stage_bytes) : 0;
+    if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
+    a.n_stages = n_stages;
+    const int U = a.K / Fmt<QT>::UE;
+    int gs_log = 0;
+    while ((1 << gs_log) < U && gs_log < 5) gs_log++;
+    a.gs_log = gs_log;
+    a.status = c->d_status;
+    int t = 0;
+    for (int i = 0; i < a.n_seg; i++) {
+        a.tile0[i] = t;
+        if (!a.pair || i == 0) t += (a.n_rows[i] + a.rpt - 1) / a.rpt;
+    }
+    a.tile0[a.n_seg] = t;   // (pair: one tile list covers both matrices)
+    const int smem = fixed + n_stages * a.stage_bytes;
+    bool a16 = false;
+    if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K) {
+        a16 = rb % 16 == 0;
+        for (int i = 0; i < a.n_seg; i++) a16 = a16 && (reinterpret_cast<uintptr_t>(a.W[i]) & 15) == 0;
+    }
+#define MLQ_SEG(MC)                                                                 \
+    do {                                                                            \
+        if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K) {                           \
+            if (a16) return launch_seg_t<QT, MC, true>(a, smem, s);                 \
+        }                                                                           \
+        return launch_seg_t<QT, MC, false>(a, smem, s);                            \
+    } while (0)
+    if (a.B == 1) MLQ_SEG(1);
+    if (a.B == 2) MLQ_SEG(2);
+    if (a.B <= 4) MLQ_SEG(4);
+    MLQ_SEG(8);
+#undef MLQ_SEG
+}
+
+// MLQ_ERR_UNSUPPORTED when the shape or type does not suit the kernel (the caller then
+// uses the plain GEMV path)
+int launch_gemv_seg(int qt, int n_seg, const uint8_t *const *W, const int *n_rows, float *const *out,
+                    const float *const *res, int pair, const uint8_t *planes, int B, int K, cudaStream_t s) {
+    if (n_seg < 1 || n_seg > kSegMax || B < 1 || B > 8 || !planes || (reinterpret_cast<uintptr_t>(planes) & 15) ||
+        (pair && (n_seg != 2 || n_rows[0] != n_rows[1])))
+        return MLQ_ERR_UNSUPPORTED;
+    SegArgs a{};
+    a.n_seg = n_seg;
+    a.pair = pair;
+    a.planes = planes;
+    a.B = B;
+    a.K = K;
+    for (int i = 0; i < n_seg; i++) {
+        if (!W[i] || !out[i] || n_rows[i] <= 0) return MLQ_ERR_UNSUPPORTED;
+        a.W[i] = W[i];
+        a.out[i] = out[i];
+        a.res[i] = res ? res[i] : nullptr;
+        a.n_rows[i] = n_rows[i];
+    }
+    switch (qt) {
+        case MLQ_Q4_0: return launch_seg_q<MLQ_Q4_0>(a, s);
+        case MLQ_Q4_1: return launch_seg_q<MLQ_Q4_1>(a, s);
+        case MLQ_Q5_0: return launch_seg_q<MLQ_Q5_0>(a, s);
+        case MLQ_Q8_0: return launch_seg_q<MLQ_Q8_0>(a, s);
+        case MLQ_Q4_K: return launch_seg_q<MLQ_Q4_K>(a, s);
+        case MLQ_Q5_K: return launch_seg_q<MLQ_Q5_K>(a, s);
+        case MLQ_Q6_K: return launch_seg_q<MLQ_Q6_K>(a, s);
+        case MLQ_MXFP4: return launch_seg_q<MLQ_MXFP4>(a, s);
+        case MLQ_MXFP4_REF: return launch_seg_q<MLQ_MXFP4_REF>(a, s);
+        default: return MLQ_ERR_UNSUPPORTED;
+    }
+}
+
+size_t packed_rows_bytes(int rows, int K) { return (size_t)rows * packed_row_bytes(K); }
+
 
 // ------------------------------------------------------------------------------ dequantize
 // One thread per output element, bit-exact with the reference's *_dequantize_row and

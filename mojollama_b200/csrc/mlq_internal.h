@@ -172,6 +172,16 @@ int launch_grouped(const GroupedCall &gc, cudaStream_t s);
 // silu(clamp(x[p], +-80)) * x2[p]
 int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
                          cudaStream_t s);
+// decode GEMV over up to 4 same-type matrices sharing packed activation rows [B <= 8]:
+// out_i = (res_i +) W_i x, or with pair (2 matrices, same rows) out_0 = silu(W_0 x) * (W_1 x);
+// MLQ_ERR_UNSUPPORTED when the shape or type does not suit it
+int launch_gemv_seg(int qt, int n_seg, const uint8_t *const *W, const int *n_rows, float *const *out,
+                    const float *const *res, int pair, const uint8_t *planes, int B, int K, cudaStream_t s);
+size_t packed_rows_bytes(int rows, int K);
+// RMSNorm of rows (as launch_rms_norm) that also writes the normalised rows as packed
+// activation rows (out may be null when only the packed rows are needed)
+int launch_rms_norm_encode(float *out, const float *x, const float *w, float *res, int rows, int n, float eps,
+                           int flags, uint8_t *planes, cudaStream_t s);
 // stable order of R rows by expert id (sorted_pos[r], src_row[p]) and the item lists of
 // n_lists tilings (tiles[l] tiles per 8-row chunk; n_items[l] written on the device)
 int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,

@@ -12,8 +12,11 @@
 // All are HBM/launch bound; in the fused forward they are folded into neighbours.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdlib.h>
 
+#include "formats.cuh"
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
@@ -79,6 +82,43 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
             v = fminf(fmaxf(v, -1000.0f), 1000.0f);
         }
         orow[i] = (v * inv) * (w ? w[i] : 1.0f);
+    }
+}
+
+// k_rms_norm with the normalised row also written as a packed activation row (the
+// input encoding of the GEMVs that read it): one CTA per row, warp w encodes blocks
+// w, w + 8, ... from the same normalised values k_rms_norm stores.
+__global__ void __launch_bounds__(256) k_rms_norm_encode(float *__restrict__ out, const float *__restrict__ x,
+                                                          const float *__restrict__ w, float *__restrict__ res, int n,
+                                                          float eps, int flags, uint8_t *__restrict__ planes) {
+    __shared__ float sh[32];
+    pdl_wait();
+    pdl_trigger();
+    const float *xr = x + (size_t)blockIdx.x * n;
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = xr[i];
+        if (flags & 1) {
+            if (v != v) v = 0.0f;
+            v = fminf(fmaxf(v, -1000.0f), 1000.0f);
+            if (res) res[(size_t)blockIdx.x * n + i] = v;
+        }
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, sh);
+    const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int kb = warp; kb < n / 32; kb += nw) {
+        const int i = 32 * kb + lane;
+        float v = xr[i];
+        if (flags & 1) {
+            if (v != v) v = 0.0f;
+            v = fminf(fmaxf(v, -1000.0f), 1000.0f);
+        }
+        const float o = (v * inv) * (w ? w[i] : 1.0f);
+        if (out) out[(size_t)blockIdx.x * n + i] = o;
+        encode_block_packed(o, blockIdx.x, kb, n, planes, lane);
     }
 }
 
@@ -195,6 +235,23 @@ int launch_rms_norm(float *out, const float *x, const float *w, float *res, int 
     k_rms_norm<<<rows, 256, 0, s>>>(out, x, w, res, n, eps, flags);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_rms_norm_encode(float *out, const float *x, const float *w, float *res, int rows, int n, float eps,
+                           int flags, uint8_t *planes, cudaStream_t s) {
+    if (n % 32 || !planes) return MLQ_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = getenv("MLQ_NO_PDL") ? 0 : 1;
+    count_launch();
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_rms_norm_encode, out, x, w, res, n, eps, flags, planes)) ? MLQ_OK
+                                                                                                        : MLQ_ERR_CUDA;
 }
 
 int launch_silu(float *out, const float *x, long long n, int mode, cudaStream_t s) {
