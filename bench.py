@@ -43,6 +43,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 FORMATS = [("Q4_0", 2), ("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14), ("Q8_0", 8), ("MXFP4", 39)]
+# the kernel each format's M=1 GEMV runs (mojollama_b200/csrc/gemv.cu, gemv_mxf4_tc.cu)
+KERNEL_OF = {"MXFP4": "k_gemv_mxf4_tc (tcgen05.mma kind::mxf4, UE8M0 block scales)"}
 N_ROWS, K_COLS, DISTINCT = 151936, 2048, 4096
 METRIC = "quant-GEMV HBM GB/s (M=1, 151936x2048, 6 GGUF formats)"
 WORKLOAD = "quant-GEMV sweep Q4_0,Q4_K,Q5_K,Q6_K,Q8_0,MXFP4 at 151936x2048, M=1 (BASELINE config 2)"
@@ -329,7 +331,7 @@ def run_ours(args, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8-dp4a/fp32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 dp4a (Q4_0/K-quants/Q8_0), e2m1 x ue8m0 tcgen05 (MXFP4); fp32 accumulate", "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "every weight matrix (165-331 MB) is larger than L2; no flush"},
@@ -338,7 +340,8 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": K_COLS * 4 * len(FORMATS), "d2h_bytes_per_step": N_ROWS * 4 * len(FORMATS),
                 "api": "combined_engine.so quant_matmul_omp, pinned host x/out, resident weights"},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "hbm", "kernel": f"k_gemv_q1<{dom_name}> (M=1 GEMV)", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": KERNEL_OF.get(dom_name, f"k_gemv_q1<{dom_name}>") + " (M=1 GEMV)",
+                     "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "traffic": traffic, "algorithmic_bytes": alg_bytes(dom_qt),
                      "share_of_step": round(pre_ms[dom_qt] / sum(pre_ms.values()), 3),

@@ -31,6 +31,7 @@
 #include "formats.cuh"
 #include "mlq_internal.h"
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
 
 namespace mlq {
 
@@ -82,14 +83,6 @@ __global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh,
     if (threadIdx.x == 0) scale[t] = s;
 }
 
-// ---------------------------------------------------------------- tcgen05 primitives
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-    // K-major, 128-byte swizzle: start >> 4, LBO 16 B (unused for swizzled K-major),
-    // SBO 1024 B (8-row atoms), version 1 (sm_100), layout type 2 (SWIZZLE_128B)
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           (1ull << 46) | (2ull << 61);
-}
-
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = nt, M = 128
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int nt) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
@@ -102,33 +95,6 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// 8 consecutive fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // ---------------------------------------------------------------- decode of 8 weights
@@ -486,7 +452,9 @@ void forget_tc_scratch() {
     g_tc_retired.clear();
 }
 
-static void *tc_scratch(cudaStream_t s, size_t bytes) {
+void *tc_scratch(cudaStream_t s, size_t bytes) {
+    const LaunchEnv *env = launch_env();
+    if (!env || env->no_alloc) return nullptr;   // a caller that allocates nothing: fall back
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(g_tc_mu);

@@ -564,6 +564,17 @@ static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, in
         const int rc = launch_gemm_tc(W, QT, x, out, n_rows, K, B, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;
     }
+    if constexpr (QT == MLQ_MXFP4) {
+        // block-scaled tensor cores: groups of up to 8 activation rows per weight pass
+        int b = 0, rc = MLQ_OK;
+        const int g = K <= 1024 ? 8 : K <= 2048 ? 4 : K <= 4096 ? 2 : 1;
+        for (; b < B && rc == MLQ_OK; b += g) {
+            const int take = B - b < g ? B - b : g;
+            rc = launch_gemv_mxf4_tc(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
+            if (rc == MLQ_ERR_UNSUPPORTED && b == 0) break;
+        }
+        if (rc != MLQ_ERR_UNSUPPORTED) return rc;
+    }
     if (B == 1) {
         const int rc = launch_q1<QT>(W, x, out, n_rows, K, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;

@@ -37,6 +37,7 @@ Ctx *ctx();                          // current device's context (initialises on
 struct LaunchEnv {
     int num_sms;
     int *d_status;
+    bool no_alloc = false;           // launchers must not allocate (paths needing scratch step aside)
 };
 const LaunchEnv *launch_env();
 struct LaunchEnvScope {
@@ -193,6 +194,12 @@ size_t embed_bytes(int emb_quant, int N, int V);
 bool host_tokens(const int *tokens, int B, std::vector<int> &out);
 void forget_kv_mirrors();
 void forget_tc_scratch();
+// per-(device, stream) scratch of the tensor-core kernels, grown outside graph capture;
+// null inside a capture that would need growth, or under a no-allocation LaunchEnv
+void *tc_scratch(cudaStream_t s, size_t bytes);
+// MXFP4 GEMV on the block-scaled tensor cores (gemv_mxf4_tc.cu), 1 <= M <= 8;
+// MLQ_ERR_UNSUPPORTED when the shape / alignment is outside it
+int launch_gemv_mxf4_tc(const uint8_t *W, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s);
 int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int *idx, float *w, cudaStream_t s);
 
 }  // namespace mlq

@@ -120,7 +120,7 @@ extern "C" int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_
     if (!d.ready && !setup_device(dev, d)) return MLQ_ERR_CUDA;
     if (ref_compat() && qt == MLQ_MXFP4) qt = MLQ_MXFP4_REF;
 
-    const LaunchEnv env{d.num_sms, d.status};
+    const LaunchEnv env{d.num_sms, d.status, true};
     LaunchEnvScope scope(&env);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const long long n = (long long)B * n_cols;
