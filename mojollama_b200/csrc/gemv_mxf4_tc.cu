@@ -57,6 +57,7 @@
 #include "mlq_internal.h"
 #include "pipeline.cuh"
 #include "tcgen05.cuh"
+#include "tc_work.cuh"
 
 namespace mlq {
 
@@ -103,17 +104,6 @@ constexpr int kBarRawFull = 0, kBarRawEmpty = 6, kBarAFull = 12, kBarAFree = 14,
               kBarAccEmpty = 18, kBarDrain = 20, kNumBars = 21;
 constexpr int kBarBytes = kNumBars * 8 + 32;   // + TMEM base slot + flags
 
-__device__ __forceinline__ void set_status(int *status, int code) {
-    if (status) atomicCAS(status, 0, code);
-}
-
-// lane 0 waits (bounded), the verdict is shared by the warp
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int lane) {
-    bool ok = true;
-    if (lane == 0) ok = mbar_wait_bounded(bar, parity);
-    return __shfl_sync(0xffffffffu, ok, 0);
-}
-
 // kind::mxf4 block-scaled instruction descriptor: A and B E2M1, K-major, UE8M0 scales,
 // M = 128, N = n; the scale-factor byte ids of this MMA
 __device__ __forceinline__ uint32_t idesc_mxf4(int n, uint32_t sfa_id, uint32_t sfb_id) {
@@ -132,12 +122,6 @@ __device__ __forceinline__ void umma_mxf4(uint32_t tmem_d, uint64_t adesc, uint6
 }
 
 // ---------------------------------------------------------------- activation planes
-// byte offset of byte kb of plane row n in the swizzled B image (n_pad rows, 128-byte atoms)
-__device__ __forceinline__ int bimg_off(int n, int kb, int n_pad) {
-    const int ac = kb >> 7, o = kb & 127, c = o >> 4;
-    return ac * (n_pad * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4) + (o & 15);
-}
-
 // 2^e as a float for -127 <= e <= 127 (2^-127 is subnormal)
 __device__ __forceinline__ float pow2f(int e) {
     return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x00400000u);
@@ -219,52 +203,6 @@ __device__ void encode_planes(const float *__restrict__ x, int M, int K, uint8_t
         }
     }
 }
-
-// This CTA's chunks in processing order: local index g -> unit u = tile * nc + chunk.
-struct WorkMap {
-    int nc, G, b, dp_rounds, tail_base, tail_units, t0, t1;
-    int dp_rounds_all;   // first tail tile = rounds of whole tiles x grid
-    __device__ WorkMap(int nc_, int n_tiles, int dp, int tail) : nc(nc_), G(gridDim.x), b(blockIdx.x),
-        dp_rounds(dp), tail_base(dp * (int)gridDim.x * nc_), tail_units(tail) {
-        dp_rounds_all = dp * G;
-        const int mine = (n_tiles - b + G - 1) / G;   // round-robin tiles this CTA has at all
-        if (dp_rounds > mine) dp_rounds = mine;
-        t0 = (int)((long long)b * tail / G);
-        t1 = (int)((long long)(b + 1) * tail / G);
-    }
-    __device__ int total() const { return dp_rounds * nc + t1 - t0; }
-    __device__ int unit(int g) const {
-        const int d = dp_rounds * nc;
-        if (g < d) {
-            const int r = g / nc;
-            return (b + r * G) * nc + (g - r * nc);
-        }
-        return tail_base + t0 + (g - d);
-    }
-};
-
-// Walks this CTA's chunks in order without divisions: (tile, chunk c) of local chunk g and
-// whether g starts / ends an accumulation segment (one tile's chunks within this CTA).
-struct UnitWalk {
-    const WorkMap &w;
-    int g = 0, tile, c, d;
-    __device__ explicit UnitWalk(const WorkMap &wm) : w(wm), d(wm.dp_rounds * wm.nc) { at(0); }
-    __device__ void at(int gg) {
-        g = gg;
-        const int u = w.unit(gg);
-        tile = u / w.nc;
-        c = u - tile * w.nc;
-    }
-    __device__ bool seg_start() const { return g == 0 || c == 0 || g == d; }
-    __device__ bool seg_end(int total) const { return g == total - 1 || c == w.nc - 1; }
-    __device__ void next() {
-        if (++g == d) { at(g); return; }   // first tail chunk
-        if (++c == w.nc) {
-            c = 0;
-            tile += g < d ? w.G : 1;
-        }
-    }
-};
 
 // ---------------------------------------------------------------- the GEMV kernel
 __global__ void __launch_bounds__(kThreads, 1) k_gemv_mxf4_tc(const __grid_constant__ CUtensorMap tmap,
@@ -571,6 +509,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mxf4_tc(const __grid_const
     }
 }
 
+int tc_mxf4_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_MXF4_TC");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v;
+}
+
+}  // namespace
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (the library does not
 // link libcuda, so it still loads on a machine without a driver)
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
@@ -596,7 +545,7 @@ std::mutex g_cnt_mu;
 std::map<int, std::pair<int *, int>> g_cnt;
 std::vector<int *> g_cnt_retired;
 
-int *mxf4_counters(int n, cudaStream_t s) {
+int *tc_counters(int n, cudaStream_t s) {
     const LaunchEnv *env = launch_env();
     if (!env || env->no_alloc) return nullptr;
     int dev = 0;
@@ -621,16 +570,47 @@ int *mxf4_counters(int n, cudaStream_t s) {
     return p;
 }
 
-int tc_mxf4_enabled() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("MLQ_MXF4_TC");
-        v = (e && atoi(e) == 0) ? 0 : 1;
-    }
-    return v;
+// 2-D tensor map of a row-major byte matrix viewed as 16-bit elements: [rows][row_bytes / 2]
+// with boxes of box_rows x box_bytes (row_bytes and box_bytes multiples of 16, base 16-aligned)
+bool tc_tensor_map_rows(CUtensorMap *tmap, const void *base, long long rows, long long row_bytes, int box_bytes,
+                        int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = encode_tiled_fn();
+    if (!encode || row_bytes % 16 || box_bytes % 16 || ((uintptr_t)base & 15)) return false;
+    const cuuint64_t gdim[2] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 2), (cuuint32_t)box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    return encode(tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
+// Work split shared by the tensor-core GEMVs: with at least one 128-row tile per SM, whole
+// tiles round-robin (tile b, b + grid, ...); splitting the last uneven round's chunks over
+// all CTAs measured slower (the partial-sum hand-off at the end of a CTA costs more than the
+// imbalance it removes).  With fewer tiles than SMs the chunks are split evenly over up to
+// one CTA per SM, and a split tile's parts are added by the last of its CTAs to finish;
+// mask[t] marks (bit c) the chunks that start a part of tile t.
+bool tc_plan(int n_rows, int nc, int num_sms, TcPlan &p, uint16_t *mask, int max_tiles) {
+    p.n_tiles = (n_rows + 127) / 128;
+    p.nc = nc;
+    const long long n_units = (long long)p.n_tiles * nc;
+    if (n_units >= (1ll << 30) || nc > 16) return false;
+    p.grid = p.n_tiles >= num_sms ? num_sms : (n_units < num_sms ? (int)n_units : num_sms);
+    p.dp_rounds = p.n_tiles >= p.grid ? (p.n_tiles + p.grid - 1) / p.grid : 0;
+    p.tail_units = p.dp_rounds ? 0 : (int)n_units;
+    if (p.tail_units) {
+        if (p.n_tiles > max_tiles) return false;
+        auto owner = [&](long long u) { return (int)(((u + 1) * p.grid - 1) / p.tail_units); };
+        for (int t = 0; t < p.n_tiles; t++) {
+            uint32_t m = 1u;
+            for (int c = 1; c < nc; c++)
+                if (owner((long long)t * nc + c) != owner((long long)t * nc + c - 1)) m |= 1u << c;
+            mask[t] = (uint16_t)m;
+        }
+    }
+    return true;
+}
 
 // out [M][n_rows] = x [M][K] . W^T for GGUF MXFP4 W; MLQ_ERR_UNSUPPORTED outside the kernel's
 // shapes (K % 512, 16-byte-aligned W, 8M * K / 2 bytes of planes in shared memory), under a
@@ -656,38 +636,18 @@ int launch_gemv_mxf4_tc(const uint8_t *W, const float *x, float *out, int n_rows
     if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
     const int smem = 1024 + off_raw + n_stages * kRawBytes;
 
-    // Work split: with at least one tile per CTA, whole tiles round-robin (tile b, b + grid,
-    // ...); splitting the last uneven round's chunks over all CTAs measured slower (the
-    // partial-sum hand-off at the end of a CTA costs more than the imbalance it removes).
-    // With fewer tiles than SMs, every chunk is split evenly over one CTA per chunk (capped
-    // at the SM count) and split tiles are combined through partial sums.
-    const int n_tiles = (n_rows + kRows - 1) / kRows, nc = K / kChunkK;
-    const long long n_units = (long long)n_tiles * nc;
-    if (n_units >= (1ll << 30)) return MLQ_ERR_UNSUPPORTED;
-    const int grid = n_tiles >= env->num_sms ? env->num_sms : (n_units < env->num_sms ? (int)n_units : env->num_sms);
-    const int dp_rounds = n_tiles >= grid ? (n_tiles + grid - 1) / grid : 0;
-    const int tail_units = dp_rounds ? 0 : (int)n_units;
-
+    TcPlan plan;
+    Mxf4Args a{};
+    if (!tc_plan(n_rows, K / kChunkK, env->num_sms, plan, a.tail_mask, kMaxTailTiles)) return MLQ_ERR_UNSUPPORTED;
+    const int n_tiles = plan.n_tiles, nc = plan.nc, grid = plan.grid;
     // partial sums of split tiles (written and read within one launch) and the per-tile
     // arrival counters (zero between launches: each launch's last arrival resets its tile)
-    float *part = tail_units ? (float *)tc_scratch(s, (size_t)n_tiles * nc * M * kRows * sizeof(float)) : nullptr;
-    int *counter = tail_units ? mxf4_counters(n_tiles, s) : nullptr;
-    if (tail_units && (!part || !counter)) return MLQ_ERR_UNSUPPORTED;
-
-    // the weights as a 2-D tensor of 16-bit elements: [n_rows][row_bytes / 2], row pitch
-    // row_bytes (a multiple of 16 since K % 512 == 0); boxes of 128 rows x 272 bytes
+    float *part = plan.tail_units ? (float *)tc_scratch(s, (size_t)n_tiles * nc * M * kRows * sizeof(float)) : nullptr;
+    int *counter = plan.tail_units ? tc_counters(n_tiles, s) : nullptr;
+    if (plan.tail_units && (!part || !counter)) return MLQ_ERR_UNSUPPORTED;
+    // the weights as 16-bit elements [n_rows][row_bytes / 2], boxes of 128 rows x 272 bytes
     CUtensorMap tmap;
-    const cuuint64_t gdim[2] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)n_rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)(kRawRow / 2), (cuuint32_t)kRows};
-    const cuuint32_t estride[2] = {1, 1};
-    PFN_cuTensorMapEncodeTiled_v12000 encode = encode_tiled_fn();
-    if (!encode) return MLQ_ERR_UNSUPPORTED;
-    if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)W, gdim, gstride, box, estride,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return MLQ_ERR_UNSUPPORTED;
+    if (!tc_tensor_map_rows(&tmap, W, n_rows, row_bytes, kRawRow, kRows)) return MLQ_ERR_UNSUPPORTED;
 
     static bool attr = false;
     if (!attr) {
@@ -695,25 +655,13 @@ int launch_gemv_mxf4_tc(const uint8_t *W, const float *x, float *out, int n_rows
             return MLQ_ERR_CUDA;
         attr = true;
     }
-    Mxf4Args a{};
     a.x = x;
     a.out = out;
     a.n_rows = n_rows; a.K = K; a.M = M; a.N = N;
     a.n_tiles = n_tiles;
     a.n_chunks = nc;
-    a.dp_rounds = dp_rounds;
-    a.tail_units = tail_units;
-    if (tail_units) {   // CTA b holds tail chunks [b R / G, (b + 1) R / G)
-        const int tail_tiles = tail_units / nc;
-        if (tail_tiles > kMaxTailTiles || nc > 16) return MLQ_ERR_UNSUPPORTED;
-        auto owner = [&](long long u) { return (int)(((u + 1) * grid - 1) / tail_units); };
-        for (int t = 0; t < tail_tiles; t++) {
-            uint32_t m = 1u;
-            for (int c = 1; c < nc; c++)
-                if (owner((long long)t * nc + c) != owner((long long)t * nc + c - 1)) m |= 1u << c;
-            a.tail_mask[t] = (uint16_t)m;
-        }
-    }
+    a.dp_rounds = plan.dp_rounds;
+    a.tail_units = plan.tail_units;
     a.part = part;
     a.counter = counter;
     a.n_stages = n_stages;

@@ -17,6 +17,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
            (1ull << 46) | (2ull << 61);
 }
 
+// the same with a chosen stride between 8-row groups (SBO); SBO 0 makes an operand of 16
+// rows read rows 0-7 twice (a B operand with only 8 distinct rows)
+__device__ __forceinline__ uint64_t umma_desc_sw128_sbo(uint32_t saddr, uint32_t sbo_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(16 >> 4) << 16) | ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+
 // the mbarrier completes one phase when every MMA this thread issued so far has finished
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
