@@ -1526,11 +1526,16 @@ static int launch_seg_q(SegArgs &a, cudaStream_t s) {
     rpt = rpt < 16 ? 16 : (rpt > 64 ? 64 : rpt);
     a.rpt = (int)(rpt / 16 * 16);
     a.row_bytes = rb;
-    a.region_bytes = align_up((int)(a.rpt * rb), 16) + 32;
-    a.stage_bytes = mats * a.region_bytes;
     const int x_bytes = a.B * packed_row_bytes(a.K);
-    const int fixed = seg_layout(x_bytes, a.stage_bytes, 0).total;
-    const int n_stages = fixed < kSmemBudget ? stages_for(fixed, a.stage_bytes) : 0;
+    int fixed = 0, n_stages = 0;
+    // long rows: fewer rows per tile (down to 4, the other decode warps idle) until two stages fit
+    for (;; a.rpt >>= 1) {
+        a.region_bytes = align_up((int)(a.rpt * rb), 16) + 32;
+        a.stage_bytes = mats * a.region_bytes;
+        fixed = seg_layout(x_bytes, a.stage_bytes, 0).total;
+        n_stages = fixed < kSmemBudget ? stages_for(fixed, a.stage_bytes) : 0;
+        if (n_stages >= 2 || a.rpt <= 4) break;
+    }
     if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
     a.n_stages = n_stages;
     const int U = a.K / Fmt<QT>::UE;
