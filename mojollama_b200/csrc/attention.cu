@@ -24,6 +24,7 @@
 #include <math.h>
 
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
@@ -263,6 +264,71 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
         count_launch();
     }
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// The decode step's RoPE and KV store in one launch, one CTA per sequence b: q and k rotated
+// in place (NeoX halves of the first rope_dim dims of each head, as k_rope_neox, cengine_
+// batch_instr.c:686), then the new k / v rows into the cache at position pos[b] (as
+// k_kv_write) and, when mirror arrays are given, into the KVBlock's own 64-slot arrays
+// ([L][1024][64][row], cengine_batch_instr.c:1349-1350).
+__global__ void __launch_bounds__(256) k_rope_kv(float *__restrict__ q, float *__restrict__ k,
+                                                 const float *__restrict__ v, int nh, int nkh, int hd, int rope_dim,
+                                                 const int *__restrict__ pos, const float *__restrict__ cos_t,
+                                                 const float *__restrict__ sin_t, KVView kv,
+                                                 float *const *__restrict__ mk, float *const *__restrict__ mv) {
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x, p = pos[b], hd2 = rope_dim / 2, row = nkh * hd;
+    float *qb = q + (size_t)b * nh * hd, *kb = k + (size_t)b * row;
+    const float *cs = cos_t + (size_t)p * hd2, *sn = sin_t + (size_t)p * hd2;
+    for (int t = threadIdx.x; t < (nh + nkh) * hd2; t += blockDim.x) {
+        const int hh = t / hd2, j = t - hh * hd2;
+        float *w = hh < nh ? qb + (size_t)hh * hd : kb + (size_t)(hh - nh) * hd;
+        const float c = cs[j], sv = sn[j];
+        const float a0 = w[j], a1 = w[j + hd2];
+        w[j] = a0 * c - a1 * sv;
+        w[j + hd2] = a1 * c + a0 * sv;
+    }
+    __syncthreads();
+    const long long off = kv_offset(kv, b, p);
+    float *kc = const_cast<float *>(kv_kbase(kv, b)), *vc = const_cast<float *>(kv_vbase(kv, b));
+    float *mkb = mk ? mk[b] : nullptr, *mvb = mv ? mv[b] : nullptr;
+    size_t moff = 0;
+    bool mirror = mkb && mvb && kv.table;
+    if (mirror) {
+        const int page = kv.table[(size_t)b * kv.table_stride + p / kv.page_size];
+        mirror = page >= 0 && page < 1024;
+        moff = ((size_t)kv.layer * 1024 * 64 + (size_t)page * 64 + (p % kv.page_size)) * row;
+    }
+    for (int i = threadIdx.x; i < row; i += blockDim.x) {
+        const float kv_k = kb[i], kv_v = v[(size_t)b * row + i];
+        kc[off + i] = kv_k;
+        vc[off + i] = kv_v;
+        if (mirror) {
+            mkb[moff + i] = kv_k;
+            mvb[moff + i] = kv_v;
+        }
+    }
+}
+
+int launch_rope_kv(float *q, float *k, const float *v, int B, int nh, int nkh, int hd, int rope_dim, const int *pos,
+                   const float *cos_t, const float *sin_t, const KVView &kv, float *const *mk, float *const *mv,
+                   cudaStream_t s) {
+    if (!kv.pool_seq || rope_dim > hd || rope_dim % 2 || !pos) return MLQ_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(B);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = getenv("MLQ_NO_PDL") ? 0 : 1;
+    count_launch();
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_rope_kv, q, k, v, nh, nkh, hd, rope_dim, pos, cos_t, sin_t, kv, mk,
+                                       mv))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,

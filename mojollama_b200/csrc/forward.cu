@@ -559,15 +559,21 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
                 for (int i = 0; i < 3; i++)
                     if (!done[i]) MLQ_TRY(launch_matmul(Wm[i], qts[i], pin, outs[i], rows[i], c->nc, B, 0, s));
             }
-            MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
-            MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
             KVView kv{nullptr, nullptr, sb.tab, tab_w, (long long)ps * kvrow, ps, kvrow, sb.pools, layer_stride, l,
                       kv0->pt._n_layers};
-            MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, sb.pos, 0, B, kvrow, s));
-            if (rc == MLQ_OK) {
-                k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(sb.mk, sb.mv, sb.tab, tab_w,
-                                                                                        sb.pos, k, v, kvrow, ps, l);
-                count_launch();
+            // RoPE + KV store (+ KVBlock mirror) in one launch when the row layout allows
+            const bool fused_kv = rc == MLQ_OK && inner == NH * HD && kvrow == NKH * HD &&
+                                  launch_rope_kv(q, k, v, B, NH, NKH, HD, rope_dim, sb.pos, P->cos_t, P->sin_t, kv,
+                                                 sb.mk, sb.mv, s) == MLQ_OK;
+            if (!fused_kv) {
+                MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+                MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+                MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, sb.pos, 0, B, kvrow, s));
+                if (rc == MLQ_OK) {
+                    k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(
+                        sb.mk, sb.mv, sb.tab, tab_w, sb.pos, k, v, kvrow, ps, l);
+                    count_launch();
+                }
             }
             MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, 0, scale, att, sb.attn_scr,
                                        sb.attn_sb, s));

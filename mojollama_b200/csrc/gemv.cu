@@ -1528,7 +1528,9 @@ static int launch_seg_q(SegArgs &a, cudaStream_t s) {
     a.row_bytes = rb;
     const int x_bytes = a.B * packed_row_bytes(a.K);
     int fixed = 0, n_stages = 0;
-    // long rows: fewer rows per tile (down to 4, the other decode warps idle) until two stages fit
+    // long rows: fewer rows per tile (down to 4, the other decode warps idle) until two
+    // stages fit (more stages through smaller tiles measured slower: the kernel is bound by
+    // its decode warps, and smaller tiles leave some of them idle)
     for (;; a.rpt >>= 1) {
         a.region_bytes = align_up((int)(a.rpt * rb), 16) + 32;
         a.stage_bytes = mats * a.region_bytes;

@@ -131,6 +131,11 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
 int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
                     const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s);
 size_t attn_scratch_bytes(int B, int nh, int hd);
+// decode step: RoPE of q and k in place, then k / v into the per-sequence page pools at pos[b]
+// and (mk / mv non-null) the KVBlock mirror arrays; MLQ_ERR_UNSUPPORTED outside that case
+int launch_rope_kv(float *q, float *k, const float *v, int B, int nh, int nkh, int hd, int rope_dim, const int *pos,
+                   const float *cos_t, const float *sin_t, const KVView &kv, float *const *mk, float *const *mv,
+                   cudaStream_t s);
 // bytes of a KVBlock k or v array allocated by kv_init of this library (0 if unknown)
 size_t kv_array_bytes(const void *p);
 

@@ -86,15 +86,18 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
 }
 
 // k_rms_norm with the normalised row also written as a packed activation row (the
-// input encoding of the GEMVs that read it): one CTA per row, warp w encodes blocks
-// w, w + 8, ... from the same normalised values k_rms_norm stores.
+// input encoding of the GEMVs that read it).  CTA (slice, row): every CTA of a row sums the
+// squares of the whole row (one pass over n floats), then normalises and encodes only its
+// slice of 32-element blocks, warp w taking blocks w, w + 8, ... of the slice -- several
+// CTAs per row keep this latency-bound step short.
 __global__ void __launch_bounds__(256) k_rms_norm_encode(float *__restrict__ out, const float *__restrict__ x,
                                                           const float *__restrict__ w, float *__restrict__ res, int n,
                                                           float eps, int flags, uint8_t *__restrict__ planes) {
     __shared__ float sh[32];
     pdl_wait();
     pdl_trigger();
-    const float *xr = x + (size_t)blockIdx.x * n;
+    const int row = blockIdx.y;
+    const float *xr = x + (size_t)row * n;
     float ss = 0.0f;
 #pragma unroll 8
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -102,23 +105,25 @@ __global__ void __launch_bounds__(256) k_rms_norm_encode(float *__restrict__ out
         if (flags & 1) {
             if (v != v) v = 0.0f;
             v = fminf(fmaxf(v, -1000.0f), 1000.0f);
-            if (res) res[(size_t)blockIdx.x * n + i] = v;
         }
         ss = fmaf(v, v, ss);
     }
     ss = block_sum(ss, sh);
     const float inv = 1.0f / sqrtf(ss / (float)n + eps);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int kb = warp; kb < n / 32; kb += nw) {
+    const int nb = n / 32, per = (nb + gridDim.x - 1) / gridDim.x;
+    const int kb0 = blockIdx.x * per, kb1 = min(nb, kb0 + per);
+    for (int kb = kb0 + warp; kb < kb1; kb += nw) {
         const int i = 32 * kb + lane;
         float v = xr[i];
         if (flags & 1) {
             if (v != v) v = 0.0f;
             v = fminf(fmaxf(v, -1000.0f), 1000.0f);
+            if (res) res[(size_t)row * n + i] = v;
         }
         const float o = (v * inv) * (w ? w[i] : 1.0f);
-        if (out) out[(size_t)blockIdx.x * n + i] = o;
-        encode_block_packed(o, blockIdx.x, kb, n, planes, lane);
+        if (out) out[(size_t)row * n + i] = o;
+        encode_block_packed(o, row, kb, n, planes, lane);
     }
 }
 
@@ -241,7 +246,10 @@ int launch_rms_norm_encode(float *out, const float *x, const float *w, float *re
                            int flags, uint8_t *planes, cudaStream_t s) {
     if (n % 32 || !planes) return MLQ_ERR_UNSUPPORTED;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows);
+    // one 32-element block per warp; a single CTA per row when normalising in place (the
+    // other CTAs of the row would still be reading x)
+    const int slices = out == x ? 1 : (n / 32 + 7) / 8;
+    cfg.gridDim = dim3(slices, rows);
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
