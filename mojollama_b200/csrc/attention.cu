@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include "formats.cuh"
 #include "mlq_internal.h"
 #include "pipeline.cuh"
 
@@ -50,7 +51,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
                                                               const int *__restrict__ seq_lens, int seq_len_scalar,
                                                               int nh, int nkh, int window, float scale,
                                                               int chunk, float *__restrict__ out,
-                                                              float *__restrict__ part_ml, float *__restrict__ part_acc) {
+                                                              float *__restrict__ part_ml, float *__restrict__ part_acc,
+                                                              uint8_t *__restrict__ planes) {
     extern __shared__ float sm[];
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int rep = nh / nkh;
@@ -169,12 +171,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
             part_ml[o] = ms[h];
             part_ml[o + 1] = ls[h];
         }
+    } else if (planes) {
+        // the output rows also as packed activation rows (the next GEMV's input encoding):
+        // this CTA's rep heads are rep * HD / 32 whole 32-element blocks of row b
+        __syncthreads();
+        const int warp = tid >> 5, lane = tid & 31, K = nh * HD;
+        const int kb0 = g * rep * HD / 32;
+        for (int j = warp; j < rep * HD / 32; j += kAttnThreads / 32) {
+            const int kb = kb0 + j;
+            encode_block_packed(out[(size_t)b * K + 32 * kb + lane], b, kb, K, planes, lane);
+        }
     }
 }
 
 // combine splits: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s
 __global__ void k_attn_merge(const float *__restrict__ part_ml, const float *__restrict__ part_acc, int n_splits,
-                             int hd, float *__restrict__ out) {
+                             int hd, float *__restrict__ out, int nh, uint8_t *__restrict__ planes) {
     const int bh = blockIdx.x;   // b * nh + head
     float M = -INFINITY;
     for (int s = 0; s < n_splits; s++) M = fmaxf(M, part_ml[((size_t)bh * n_splits + s) * 2]);
@@ -190,6 +202,14 @@ __global__ void k_attn_merge(const float *__restrict__ part_ml, const float *__r
             if (m != -INFINITY) a += expf(m - M) * part_acc[((size_t)bh * n_splits + s) * hd + d];
         }
         out[(size_t)bh * hd + d] = (L > 0.0f) ? a / L : 0.0f;
+    }
+    if (planes && hd % 32 == 0) {   // this head's hd / 32 blocks as packed activation rows
+        __syncthreads();
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, b = bh / nh, K = nh * hd;
+        for (int j = warp; j < hd / 32; j += blockDim.x / 32) {
+            const int kb = (bh - b * nh) * hd / 32 + j;
+            encode_block_packed(out[(size_t)b * K + 32 * kb + lane], b, kb, K, planes, lane);
+        }
     }
 }
 
@@ -214,7 +234,8 @@ static size_t attn_smem(int rep, int hd) {
 // q [B][nh][hd] -> out [B][nh][hd]; scratch holds the split partials when needed
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
                        int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
-                       float *scratch, size_t scratch_bytes, cudaStream_t s) {
+                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes) {
+    if (planes && ((nh / (nkh > 0 ? nkh : 1)) * hd % 32 || hd % 32)) planes = nullptr;   // caller encodes
     const LaunchEnv *env = launch_env();
     if (!env) return MLQ_ERR_NO_DEVICE;
     if (nkh <= 0 || nh % nkh) { set_error(MLQ_ERR_ARG, "attention: n_head %d not a multiple of n_kv_head %d", nh, nkh); return MLQ_ERR_ARG; }
@@ -245,7 +266,8 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
             attr = true;                                                                                      \
         }                                                                                                     \
         k_attn_decode<HD_><<<grid, kAttnThreads, smem, s>>>(q, kv, seq_lens_dev, seq_len_scalar, nh, nkh,     \
-                                                            window, scale, chunk1, out, part_ml, part_acc);   \
+                                                            window, scale, chunk1, out, part_ml, part_acc,    \
+                                                            planes);                                          \
     } break;
     switch (hd) {
         MLQ_ATTN_CASE(64)
@@ -260,7 +282,7 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
 #undef MLQ_ATTN_CASE
     count_launch();
     if (n_splits > 1) {
-        k_attn_merge<<<B * nh, 128, 0, s>>>(part_ml, part_acc, n_splits, hd, out);
+        k_attn_merge<<<B * nh, 128, 0, s>>>(part_ml, part_acc, n_splits, hd, out, nh, planes);
         count_launch();
     }
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;

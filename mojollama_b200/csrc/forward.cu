@@ -575,11 +575,14 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
                     count_launch();
                 }
             }
+            // the attention output also as packed rows for the o projection (decode path)
+            const bool o_fast = fast && !lp.wattng && lp.no == N;
+            const bool att_packed = o_fast && inner == NH * HD && attn_packs_output(NH, NKH, HD);
             MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, 0, scale, att, sb.attn_scr,
-                                       sb.attn_sb, s));
+                                       sb.attn_sb, s, att_packed ? sb.pa : nullptr));
             bool o_done = false;
-            if (fast && !lp.wattng && lp.no == N && rc == MLQ_OK) {   // x = res + W_o att
-                MLQ_TRY(launch_encode_packed(att, nullptr, nullptr, B, inner, sb.pa, s));
+            if (o_fast && rc == MLQ_OK) {   // x = res + W_o att
+                if (!att_packed) MLQ_TRY(launch_encode_packed(att, nullptr, nullptr, B, inner, sb.pa, s));
                 const uint8_t *wo = lp.wo;
                 const int no = lp.no;
                 float *xo = x;

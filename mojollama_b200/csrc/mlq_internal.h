@@ -125,9 +125,12 @@ struct KVView {
     int tail_stride = 0;
 };
 
+// planes non-null: the output rows [B][nh*hd] also written as packed activation rows, when
+// attn_packs_output(nh, nkh, hd) (otherwise planes is ignored)
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
                        int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
-                       float *scratch, size_t scratch_bytes, cudaStream_t s);
+                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes = nullptr);
+inline bool attn_packs_output(int nh, int nkh, int hd) { return nkh > 0 && (nh / nkh) * hd % 32 == 0 && hd % 32 == 0; }
 int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
                     const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s);
 size_t attn_scratch_bytes(int B, int nh, int hd);
