@@ -36,6 +36,10 @@ template <> struct Fmt<MLQ_Q5_0>      { static constexpr int BE = 32,  BB = 22, 
 template <> struct Fmt<MLQ_Q8_0>      { static constexpr int BE = 32,  BB = 34,  UE = 32; };
 template <> struct Fmt<MLQ_MXFP4>     { static constexpr int BE = 32,  BB = 17,  UE = 32; };
 template <> struct Fmt<MLQ_MXFP4_REF> { static constexpr int BE = 32,  BB = 17,  UE = 32; };
+// Q4_0 read as block pairs (64 elements, 36 bytes) where rows start on 4-byte boundaries:
+// an internal unit variant of MLQ_Q4_0, not an ABI type id
+constexpr int kQ4_0Pair = 2002;
+template <> struct Fmt<kQ4_0Pair>     { static constexpr int BE = 32,  BB = 18,  UE = 64; };
 template <> struct Fmt<MLQ_Q4_K>      { static constexpr int BE = 256, BB = 144, UE = 64; };
 template <> struct Fmt<MLQ_Q5_K>      { static constexpr int BE = 256, BB = 176, UE = 64; };
 template <> struct Fmt<MLQ_Q6_K>      { static constexpr int BE = 256, BB = 210, UE = 64; };
@@ -75,20 +79,20 @@ __device__ __forceinline__ int sbyte16(const uint32_t (&w)[4], int idx) {
     const uint32_t word = (idx < 4) ? w[0] : (idx < 8) ? w[1] : (idx < 12) ? w[2] : w[3];
     return (int)(int8_t)(__byte_perm(word, 0, (unsigned)(idx & 3)) & 0xFF);
 }
-__device__ __forceinline__ uint32_t ubyte12(const uint32_t (&w)[3], int idx) {
-    const uint32_t word = (idx < 4) ? w[0] : (idx < 8) ? w[1] : w[2];
-    return __byte_perm(word, 0, (unsigned)(idx & 3)) & 0xFF;
-}
 
-// K-quant 6-bit (scale, min) pair j of the 12 packed bytes (get_scale_min_k4)
-__device__ __forceinline__ void scale_min_k4(const uint32_t (&s)[3], int j, uint32_t &sc, uint32_t &m) {
-    if (j < 4) {
-        sc = ubyte12(s, j) & 63u;
-        m = ubyte12(s, j + 4) & 63u;
-    } else {
-        sc = (ubyte12(s, j + 4) & 0xFu) | ((ubyte12(s, j - 4) >> 6) << 4);
-        m = (ubyte12(s, j + 4) >> 4) | ((ubyte12(s, j) >> 6) << 4);
-    }
+// (scale, min) of sub-blocks 2g and 2g+1 (get_scale_min_k4 for j = 2g, 2g+1) as floats.
+// All eight pairs are built bytewise at once: j < 4 from the low 6 bits of bytes j and
+// j+4; j >= 4 from the nibbles of byte j+4 and the top 2 bits of bytes j-4 and j.  The
+// chosen byte becomes the float 2^23 + b (PRMT into 0x4B000000) minus 2^23, exactly.
+__device__ __forceinline__ void scale_min_pair_k4(const uint32_t (&s)[3], int g, float &sc0, float &m0, float &sc1,
+                                                  float &m1) {
+    const uint32_t sc = g < 2 ? (s[0] & 0x3F3F3F3Fu) : ((s[2] & 0x0F0F0F0Fu) | ((s[0] >> 2) & 0x30303030u));
+    const uint32_t mn = g < 2 ? (s[1] & 0x3F3F3F3Fu) : (((s[2] >> 4) & 0x0F0F0F0Fu) | ((s[1] >> 2) & 0x30303030u));
+    const uint32_t k0 = 0x7540u | (uint32_t)(2 * (g & 1)), k1 = k0 + 1u;
+    sc0 = __uint_as_float(__byte_perm(sc, 0x4B000000u, k0)) - 8388608.0f;
+    sc1 = __uint_as_float(__byte_perm(sc, 0x4B000000u, k1)) - 8388608.0f;
+    m0 = __uint_as_float(__byte_perm(mn, 0x4B000000u, k0)) - 8388608.0f;
+    m1 = __uint_as_float(__byte_perm(mn, 0x4B000000u, k1)) - 8388608.0f;
 }
 
 // spread 4 bits (t & 0xF) to bit 4 of each byte: element i gets +16 when bit i is set
@@ -332,6 +336,7 @@ struct XU64 {
     float s[2], sum[2];
 };
 template <> struct XU<MLQ_Q4_K> : XU64 {};
+template <> struct XU<kQ4_0Pair> : XU64 {};
 template <> struct XU<MLQ_Q5_K> : XU64 {};
 
 __device__ __forceinline__ void load_xu64(const XPlanes &xp, int m, int u, XU64 &x) {
@@ -345,6 +350,35 @@ __device__ __forceinline__ void load_xu64(const XPlanes &xp, int m, int u, XU64 
     x.sum[1] = xp.sum[so + 1];
 }
 
+// Q4_0 block pair u (blocks 2u, 2u+1) of a row that starts on a 4-byte boundary: the
+// pair's 9 words are aligned, so they load without shifts, and lanes reading
+// consecutive pairs (9 words apart) touch 32 different banks.
+template <> struct W<kQ4_0Pair> {
+    uint32_t q[16];          // words 0..7 block 2u, 8..15 block 2u+1 (element order)
+    float d0, d1;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
+        const uint32_t *p = reinterpret_cast<const uint32_t *>(row + 36 * u);
+        uint32_t w[9];
+#pragma unroll
+        for (int i = 0; i < 9; i++) w[i] = p[i];
+        d0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(w[4] >> 16)));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t qa = __byte_perm(w[i], w[i + 1], 0x5432);   // block 2u bytes 2+4i..5+4i
+            q[i] = qa & 0x0F0F0F0Fu;
+            q[4 + i] = (qa >> 4) & 0x0F0F0F0Fu;
+            q[8 + i] = w[5 + i] & 0x0F0F0F0Fu;
+            q[12 + i] = (w[5 + i] >> 4) & 0x0F0F0F0Fu;
+        }
+    }
+    __device__ __forceinline__ float dot(const XU64 &x) const {
+        const int c0 = dot_words<8>(q, x.h, x.l);
+        const int c1 = dot_words<8>(q + 8, x.h + 8, x.l + 8);
+        return fmaf(d0, fmaf(x.s[0], (float)c0, -8.0f * x.sum[0]), d1 * fmaf(x.s[1], (float)c1, -8.0f * x.sum[1]));
+    }
+};
+
 template <int QT> struct WK45 {
     uint32_t q[16];          // words 0..7 sub-block 2g (lo nibbles), 8..15 sub-block 2g+1
     float ds0, dm0, ds1, dm1;
@@ -357,9 +391,8 @@ template <int QT> struct WK45 {
         const float d = __half2float(__ushort_as_half((unsigned short)(hdr[0] & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[0] >> 16)));
         const uint32_t sw[3] = {hdr[1], hdr[2], hdr[3]};
-        uint32_t sc0, m0, sc1, m1;
-        scale_min_k4(sw, 2 * g, sc0, m0);
-        scale_min_k4(sw, 2 * g + 1, sc1, m1);
+        float sc0, m0, sc1, m1;
+        scale_min_pair_k4(sw, g, sc0, m0, sc1, m1);
         uint32_t w[8];
         if (QT == MLQ_Q4_K) {
             load_words<8>(blk + 16 + 32 * g, w);
@@ -378,10 +411,10 @@ template <int QT> struct WK45 {
                 q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
             }
         }
-        ds0 = d * (float)sc0;
-        dm0 = dmin * (float)m0;
-        ds1 = d * (float)sc1;
-        dm1 = dmin * (float)m1;
+        ds0 = d * sc0;
+        dm0 = dmin * m0;
+        ds1 = d * sc1;
+        dm1 = dmin * m1;
     }
     // same, for a row that starts on a 16-byte boundary of shared memory: the block
     // header and qs/qh are then 16-byte aligned (144 and 176 are multiples of 16),
@@ -394,9 +427,8 @@ template <int QT> struct WK45 {
         const float d = __half2float(__ushort_as_half((unsigned short)(hv.x & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hv.x >> 16)));
         const uint32_t sw[3] = {hv.y, hv.z, hv.w};
-        uint32_t sc0, m0, sc1, m1;
-        scale_min_k4(sw, 2 * g, sc0, m0);
-        scale_min_k4(sw, 2 * g + 1, sc1, m1);
+        float sc0, m0, sc1, m1;
+        scale_min_pair_k4(sw, g, sc0, m0, sc1, m1);
         const uint4 *qp = reinterpret_cast<const uint4 *>(blk + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g);
         const uint4 v0 = qp[0], v1 = qp[1];
         const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -416,10 +448,10 @@ template <int QT> struct WK45 {
                 q[8 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
             }
         }
-        ds0 = d * (float)sc0;
-        dm0 = dmin * (float)m0;
-        ds1 = d * (float)sc1;
-        dm1 = dmin * (float)m1;
+        ds0 = d * sc0;
+        dm0 = dmin * m0;
+        ds1 = d * sc1;
+        dm1 = dmin * m1;
     }
     __device__ __forceinline__ float dot(const XU64 &x) const {
         const int c0 = dot_words<8>(q, x.h, x.l);
@@ -509,7 +541,7 @@ template <int QT>
 __device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> &x) {
     if constexpr (QT == MLQ_Q6_K) {
         load_xu_q6k(xp, m, u, x);
-    } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K) {
+    } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == kQ4_0Pair) {
         load_xu64(xp, m, u, x);
     } else {
         load_xu32<QT>(xp, m, u, x);

@@ -268,14 +268,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_q(GemvArgs a) {
 }
 
 // ---------------------------------------------------------------- M = 1 decode kernel
-// kFastWarps decode warps each own RW rows of every tile (rows w, w+16, ...), and
-// each lane always handles units lane, lane+32, ... of a row, so the lane's
-// activation slices XU are loaded into registers once and reused for every row the
-// CTA streams.  UPL = units per lane (ceil(K/UE/32)); A16 = rows start on 16-byte
-// boundaries in shared memory (Q4_K/Q5_K then use 128-bit loads); RW = rows per
-// warp per tile (independent decode chains for latency hiding).
-template <int QT, int UPL, bool A16, int RW>
-__global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
+// NW decode warps each own RW rows of every tile (rows w, w+NW, ...), and each lane
+// always handles units lane, lane+32, ... of a row, so the lane's activation slices XU
+// are loaded into registers once and reused for every row the CTA streams.  UPL = units
+// per lane (ceil(K/UE/32)); A16 = rows start on 16-byte boundaries in shared memory
+// (Q4_K/Q5_K then use 128-bit loads); RW = rows per warp per tile (independent decode
+// chains for latency hiding).  With RW = 2 the two row sums are reduced together: one
+// exchange across the half-warps leaves each half with one row, then four levels.
+template <int QT, int UPL, bool A16, int RW, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_q1(GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvLayout L = gemv_layout(1, a.K, a.stage_bytes, a.n_stages);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_bar);
@@ -283,11 +284,11 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.off_flag);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_iter = (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    if (warp == kFastWarps) prefetch_first_tiles(a, n_iter, lane);
-    init_barriers(full, empty, abort_flag, a.n_stages, kFastWarps);
+    if (warp == NW) prefetch_first_tiles(a, n_iter, lane);
+    init_barriers(full, empty, abort_flag, a.n_stages, NW);
     pdl_wait();
     pdl_trigger();
-    if (warp == kFastWarps) {
+    if (warp == NW) {
         produce_tiles(a, smem + L.off_stage, full, empty, abort_flag, n_iter, lane);
         return;
     }
@@ -295,8 +296,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
     int8_t *xl = reinterpret_cast<int8_t *>(smem + L.off_xl);
     float *xs = reinterpret_cast<float *>(smem + L.off_xs);
     float *xsum = reinterpret_cast<float *>(smem + L.off_xsum);
-    encode_x_planes<1>(a.x, 1, a.K, xh, xl, xs, xsum, warp, lane, kFastWarps);
-    named_bar_sync(1, kFastWarps * 32);
+    encode_x_planes<1>(a.x, 1, a.K, xh, xl, xs, xsum, warp, lane, NW);
+    named_bar_sync(1, NW * 32);
     const XPlanes xp{xh, xl, xs, xsum, a.K, a.K, a.K / 32};
     const int U = a.K / Fmt<QT>::UE;
     XU<QT> xu[UPL];
@@ -323,9 +324,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
                 if (u < U) {
 #pragma unroll
                     for (int r = 0; r < RW; r++) {
-                        // rows warp, warp + 16, ...: row r of this warp within the tile
-                        if (row0 + kFastWarps * r < a.n_rows) {
-                            const uint8_t *rowp = st + (size_t)(warp + kFastWarps * r) * a.row_bytes;
+                        // rows warp, warp + NW, ...: row r of this warp within the tile
+                        if (row0 + NW * r < a.n_rows) {
+                            const uint8_t *rowp = st + (size_t)(warp + NW * r) * a.row_bytes;
                             W<QT> w;
                             if constexpr (A16) w.decode_a16(rowp, u);
                             else w.decode(rowp, u);
@@ -335,17 +336,30 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_q1(GemvArgs a) {
                 }
             }
         }
+        if constexpr (RW == 2) {
+            const bool up = (lane & 16) != 0;
+            float v = (up ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, up ? acc[0] : acc[1], 16);
 #pragma unroll
-        for (int r = 0; r < RW; r++) {
+            for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            __syncwarp();
+            if (ok) {
+                if (lane == 0) mbar_arrive(&empty[s]);
+                const int r = lane >> 4;
+                if ((lane & 15) == 0 && row0 + NW * r < a.n_rows) a.out[row0 + NW * r] = v;
+            }
+        } else {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-        }
-        __syncwarp();
-        if (lane == 0 && ok) {
-            mbar_arrive(&empty[s]);
+            for (int r = 0; r < RW; r++) {
 #pragma unroll
-            for (int r = 0; r < RW; r++)
-                if (row0 + kFastWarps * r < a.n_rows) a.out[row0 + kFastWarps * r] = acc[r];
+                for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            }
+            __syncwarp();
+            if (lane == 0 && ok) {
+                mbar_arrive(&empty[s]);
+#pragma unroll
+                for (int r = 0; r < RW; r++)
+                    if (row0 + NW * r < a.n_rows) a.out[row0 + NW * r] = acc[r];
+            }
         }
     }
 }
@@ -489,10 +503,22 @@ template <int QT> static int fast_rw() {
     return 2;
 }
 
-template <int QT, int UPL, int RW>
+// decode warps of the M=1 kernel (MLQ_GEMV_WARPS = 16, 20 or 24 overrides); more warps
+// hide more of the dp4a / shared-load latency but cap the registers per thread
+// (20 warps + producer: 96, 24 + producer: 80).  Per format, the fastest measured at
+// 151936 x 2048 on B200.
+template <int QT> static int fast_nw() {
+    const char *e = getenv("MLQ_GEMV_WARPS");
+    if (e && (atoi(e) == 16 || atoi(e) == 20 || atoi(e) == 24)) return atoi(e);
+    if constexpr (QT == kQ4_0Pair) return 24;
+    if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == MLQ_Q6_K) return 20;
+    return kFastWarps;
+}
+
+template <int QT, int UPL, int RW, int NW>
 static int launch_q1_rw(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
     const long long rb = (long long)(K / Fmt<QT>::BE) * Fmt<QT>::BB;
-    const int rpt = kFastWarps * RW;
+    const int rpt = NW * RW;
     const int stage_bytes = align_up((int)(rpt * rb), 16) + 48;
     const int fixed = gemv_layout(1, K, stage_bytes, 0).total;
     const int n_stages = stages_for(fixed, stage_bytes);
@@ -502,21 +528,37 @@ static int launch_q1_rw(const uint8_t *W, const float *x, float *out, int n_rows
     a.row_bytes = rb; a.total_bytes = rb * n_rows; a.rpt = rpt; a.wpr = 1;
     a.n_tiles = (n_rows + rpt - 1) / rpt; a.stage_bytes = stage_bytes; a.n_stages = n_stages;
     const int smem = fixed + n_stages * stage_bytes;
+    constexpr int kThr = (NW + 1) * 32;
     constexpr bool kCanAlign = (QT == MLQ_Q4_K || QT == MLQ_Q5_K);
     if constexpr (kCanAlign) {
         if (rb % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
             static bool attr_a = false;
-            return launch_gemv_kernel(k_gemv_q1<QT, UPL, true, RW>, a, smem, s, attr_a, kFastThreads);
+            return launch_gemv_kernel(k_gemv_q1<QT, UPL, true, RW, NW>, a, smem, s, attr_a, kThr);
         }
     }
     static bool attr_set = false;
-    return launch_gemv_kernel(k_gemv_q1<QT, UPL, false, RW>, a, smem, s, attr_set, kFastThreads);
+    return launch_gemv_kernel(k_gemv_q1<QT, UPL, false, RW, NW>, a, smem, s, attr_set, kThr);
 }
+
+// formats whose M=1 kernel is built with 20 and 24 decode warps as well as 16
+template <int QT> constexpr bool kWarpVariants = QT == kQ4_0Pair || QT == MLQ_Q4_K || QT == MLQ_Q5_K ||
+                                                 QT == MLQ_Q6_K || QT == MLQ_Q8_0;
 
 template <int QT, int UPL>
 static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
-    if (fast_rw<QT>() == 2) return launch_q1_rw<QT, UPL, 2>(W, x, out, n_rows, K, s);
-    return launch_q1_rw<QT, UPL, 1>(W, x, out, n_rows, K, s);
+    const int rw = fast_rw<QT>();
+    if constexpr (kWarpVariants<QT>) {
+        // a tile of NW * RW rows that leaves fewer than 3 stages falls back to 16 warps
+        const int nw = fast_nw<QT>();
+        int rc = MLQ_ERR_CAPACITY;
+        if (nw == 24) rc = rw == 2 ? launch_q1_rw<QT, UPL, 2, 24>(W, x, out, n_rows, K, s)
+                                   : launch_q1_rw<QT, UPL, 1, 24>(W, x, out, n_rows, K, s);
+        else if (nw == 20) rc = rw == 2 ? launch_q1_rw<QT, UPL, 2, 20>(W, x, out, n_rows, K, s)
+                                        : launch_q1_rw<QT, UPL, 1, 20>(W, x, out, n_rows, K, s);
+        if (rc != MLQ_ERR_CAPACITY) return rc;
+    }
+    if (rw == 2) return launch_q1_rw<QT, UPL, 2, kFastWarps>(W, x, out, n_rows, K, s);
+    return launch_q1_rw<QT, UPL, 1, kFastWarps>(W, x, out, n_rows, K, s);
 }
 
 // M = 1 over many rows: the register-resident kernel; returns MLQ_ERR_UNSUPPORTED
@@ -528,6 +570,11 @@ static int launch_q1(const uint8_t *W, const float *x, float *out, int n_rows, i
     const int U = K / Fmt<QT>::UE;
     const int upl = (U + 31) / 32;
     if (n_rows < 8 * c->num_sms * kFastWarps || getenv("MLQ_GEMV_GENERIC")) return MLQ_ERR_UNSUPPORTED;
+    if constexpr (QT == MLQ_Q4_0) {
+        // block pairs: rows of 36-byte pairs on 4-byte boundaries
+        if (K % 64 == 0 && K <= 2048 && (reinterpret_cast<uintptr_t>(W) & 3) == 0)
+            return launch_q1<kQ4_0Pair>(W, x, out, n_rows, K, s);
+    }
     // only the variants that stay inside the 96 registers a 544-thread CTA allows:
     // 64-element units at 1 per lane (K <= 2048), 32-element units at <= 3 (K <= 3072)
     if constexpr (Fmt<QT>::UE == 64) {
