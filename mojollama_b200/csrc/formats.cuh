@@ -74,12 +74,6 @@ __device__ __forceinline__ float e8m0_half(uint32_t e) {
     return __uint_as_float(e < 2 ? (0x00200000u << e) : ((e - 1u) << 23));
 }
 
-// signed byte idx (0..15) of a 16-byte array held in 4 words
-__device__ __forceinline__ int sbyte16(const uint32_t (&w)[4], int idx) {
-    const uint32_t word = (idx < 4) ? w[0] : (idx < 8) ? w[1] : (idx < 12) ? w[2] : w[3];
-    return (int)(int8_t)(__byte_perm(word, 0, (unsigned)(idx & 3)) & 0xFF);
-}
-
 // (scale, min) of sub-blocks 2g and 2g+1 (get_scale_min_k4 for j = 2g, 2g+1) as floats.
 // All eight pairs are built bytewise at once: j < 4 from the low 6 bits of bytes j and
 // j+4; j >= 4 from the nibbles of byte j+4 and the top 2 bits of bytes j-4 and j.  The
@@ -491,19 +485,33 @@ __device__ __forceinline__ void load_xu_q6k(const XPlanes &xp, int m, int u, XU<
     }
 }
 
-// codes stay unsigned (0..63); the -32 offset is applied through XU::off
+// codes stay unsigned (0..63); the -32 offset is applied through XU::off.  The unit's
+// eight scale bytes (8h..8h+7) and d come from one aligned window of the 18-byte
+// scales + d tail; the signed scales become floats exactly through the 2^23 trick on
+// the sign-flipped bytes, and d multiplies the unit's sum once.
 template <> struct W<MLQ_Q6_K> {
     uint32_t q[16];
-    float ds[4];
+    float d, sc[4];
     __device__ __forceinline__ void decode(const uint8_t *row, int u) {
         const int sb = u >> 2, h = (u >> 1) & 1, lr = u & 1, l0 = 16 * lr;
         const uint8_t *blk = row + 210 * sb;
-        uint32_t a[4], b[4], qh[4], scw[4];
+        uint32_t a[4], b[4], qh[4];
         load_words<4>(blk + 64 * h + l0, a);
         load_words<4>(blk + 64 * h + 32 + l0, b);
         load_words<4>(blk + 128 + 32 * h + l0, qh);
-        load_words<4>(blk + 192, scw);
-        const float d = f16_at(blk + 208);
+        const uintptr_t ta = reinterpret_cast<uintptr_t>(blk + 192);
+        const uint32_t *tw = reinterpret_cast<const uint32_t *>(ta & ~uintptr_t(3));
+        const uint32_t sh = (uint32_t)(ta & 3) * 8u;
+        const uint32_t r0 = tw[2 * h], r1 = tw[2 * h + 1], r2 = tw[2 * h + 2];
+        const uint32_t dw = __funnelshift_r(tw[4], tw[5], sh);   // tail bytes 16, 17 = d
+        d = __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu)));
+        const uint32_t wa = __funnelshift_r(r0, r1, sh) ^ 0x80808080u;   // scales 8h..8h+3
+        const uint32_t wb = __funnelshift_r(r1, r2, sh) ^ 0x80808080u;   // scales 8h+4..8h+7
+        const uint32_t k0 = 0x7540u | (uint32_t)lr, k1 = k0 + 2u;
+        sc[0] = __uint_as_float(__byte_perm(wa, 0x4B000000u, k0)) - 8388736.0f;
+        sc[1] = __uint_as_float(__byte_perm(wa, 0x4B000000u, k1)) - 8388736.0f;
+        sc[2] = __uint_as_float(__byte_perm(wb, 0x4B000000u, k0)) - 8388736.0f;
+        sc[3] = __uint_as_float(__byte_perm(wb, 0x4B000000u, k1)) - 8388736.0f;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             q[i] = (a[i] & 0x0F0F0F0Fu) | ((qh[i] & 0x03030303u) << 4);
@@ -511,17 +519,20 @@ template <> struct W<MLQ_Q6_K> {
             q[8 + i] = ((a[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 4) & 0x03030303u) << 4);
             q[12 + i] = ((b[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> 6) & 0x03030303u) << 4);
         }
-#pragma unroll
-        for (int k = 0; k < 4; k++) ds[k] = d * (float)sbyte16(scw, 8 * h + lr + 2 * k);
     }
     __device__ __forceinline__ float dot(const XU<MLQ_Q6_K> &x) const {
         float a = 0.0f;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const int c = dot_words<4>(q + 4 * k, x.h + 4 * k, x.l + 4 * k) - x.off[k];
-            a = fmaf(ds[k] * x.s[k], (float)c, a);
+            int hi = 0, lo = -x.off[k];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                hi = __dp4a((int)q[4 * k + i], (int)x.h[4 * k + i], hi);
+                lo = __dp4a((int)q[4 * k + i], (int)x.l[4 * k + i], lo);
+            }
+            a = fmaf(sc[k], x.s[k] * (float)(hi * 254 + lo), a);
         }
-        return a;
+        return d * a;
     }
 };
 
