@@ -338,7 +338,8 @@ def run_ours(args, rank, world, local_rank):
         "per_format_gbs": None,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": K_COLS * 4 * len(FORMATS), "d2h_bytes_per_step": N_ROWS * 4 * len(FORMATS),
-                "api": "combined_engine.so quant_matmul_omp, pinned host x/out, resident weights"},
+                "api": "combined_engine.so quant_matmul_omp, pinned host x/out, resident weights; x copied in, "
+                       "out written into the pinned buffer by the GEMV kernel (d2h bytes cross PCIe in the kernel)"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": KERNEL_OF.get(dom_name, f"k_gemv_q1<{dom_name}>") + " (M=1 GEMV)",
                      "achieved": round(achieved, 1),

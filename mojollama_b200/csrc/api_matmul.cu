@@ -37,9 +37,22 @@ int mlq_matmul(const void *W, int qt, const float *x, float *out, int n_rows, in
     const size_t wb = rb * (size_t)n_rows;
     const uint8_t *dW = (const uint8_t *)cs.weights(W, wb);
     const float *dx = (const float *)cs.in(x, sizeof(float) * (size_t)B * n_cols);
-    float *dout = (float *)cs.out(out, sizeof(float) * (size_t)B * n_rows);
+    // one activation row of a quantized matrix: the GEMV kernels store each output once
+    // (the many-row kernels in one contiguous run per tile), so a pinned host `out` is
+    // written in place instead of through a staging buffer and a copy after the kernel
+    bool host_mapped = false;
+    float *dout = (float *)(B == 1 && is_quant_type(qt) ? cs.out_direct(out, sizeof(float) * (size_t)n_rows, &host_mapped)
+                                                        : cs.out(out, sizeof(float) * (size_t)B * n_rows));
     if (cs.failed) return cs.finish();
-    int rc = launch_matmul(dW, qt, dx, dout, n_rows, n_cols, B, wb, stream());
+    int rc;
+    if (host_mapped && launch_env()) {
+        LaunchEnv env = *launch_env();
+        env.out_host = true;
+        LaunchEnvScope scope(&env);
+        rc = launch_matmul(dW, qt, dx, dout, n_rows, n_cols, B, wb, stream());
+    } else {
+        rc = launch_matmul(dW, qt, dx, dout, n_rows, n_cols, B, wb, stream());
+    }
     if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }
     return cs.finish();
 }

@@ -38,6 +38,8 @@ struct LaunchEnv {
     int num_sms;
     int *d_status;
     bool no_alloc = false;           // launchers must not allocate (paths needing scratch step aside)
+    bool out_host = false;           // outputs are host memory written over PCIe: kernels that can
+                                     // gather a tile's outputs and write them as one run
 };
 const LaunchEnv *launch_env();
 struct LaunchEnvScope {
@@ -61,6 +63,10 @@ struct CallScope {
     const void *in(const void *p, size_t bytes);
     // device view of an output; host outputs are copied back in finish()
     void *out(void *p, size_t bytes);
+    // device view of an output that the kernels only store to, once per element, in
+    // contiguous runs: pinned host memory the device can reach is written in place (no
+    // staging copy); anything else as out()
+    void *out_direct(void *p, size_t bytes, bool *host_mapped);
     // device view of an in/out buffer (copied in and back)
     void *inout(void *p, size_t bytes);
     // device scratch (uninitialised) for this call

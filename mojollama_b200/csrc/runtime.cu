@@ -324,6 +324,25 @@ void *CallScope::out(void *p, size_t bytes) {
     return d;
 }
 
+void *CallScope::out_direct(void *p, size_t bytes, bool *host_mapped) {
+    *host_mapped = false;
+    if (failed || !p) return nullptr;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return out(p, bytes);
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return p;
+    void *d = nullptr;
+    if (a.type == cudaMemoryTypeHost && cudaHostGetDevicePointer(&d, p, 0) == cudaSuccess && d) {
+        any_host = true;   // finish() synchronises before the caller reads it
+        *host_mapped = true;
+        return d;
+    }
+    cudaGetLastError();
+    return out(p, bytes);
+}
+
 void *CallScope::inout(void *p, size_t bytes) {
     if (failed || !p) return nullptr;
     if (is_device_ptr(p)) return p;

@@ -238,3 +238,24 @@ def test_host_weight_cache_follows_buffer_contents(cuda_device):
     w[:] = make_w(F.Q4_0, n, k, 2)                   # same address, same size, new contents
     assert lib.mlq_matmul(w.ctypes.data, F.Q4_0, x.ctypes.data, out.ctypes.data, n, k, 1) == 0
     assert O.rel_l2(out, O.gemv(w, F.Q4_0, x, n, k)[0]) < TOL
+
+
+@pytest.mark.parametrize("qt", [F.Q4_0, F.Q4_K, F.Q5_K, F.Q6_K, F.Q8_0, F.MXFP4, F.Q4_1])
+@pytest.mark.parametrize("n", [151899, 20000, 300])
+def test_pinned_host_output_written_in_place(cuda_device, qt, n):
+    """A pinned host `out` of a one-row product is written by the kernel itself (the
+    many-row kernel in one contiguous run per tile).  Every element must be written,
+    ragged last tiles included, and equal the device-buffer result bit for bit."""
+    import torch
+    lib = cuda_device
+    k = 2048
+    rng = np.random.default_rng(qt * 7 + n)
+    wd = torch.from_numpy(F.random_blocks(qt, n * k, rng)).cuda()
+    xd = torch.from_numpy(rng.standard_normal(k).astype(np.float32)).cuda()
+    od = torch.zeros(n, device="cuda")
+    assert lib.mlq_matmul(wd.data_ptr(), qt, xd.data_ptr(), od.data_ptr(), n, k, 1) == 0
+    lib.mlq_sync()
+    for _ in range(2):   # twice: the second call must not depend on what the first left
+        hp = torch.full((n,), float("nan")).pin_memory()
+        assert lib.mlq_matmul(wd.data_ptr(), qt, xd.data_ptr(), hp.data_ptr(), n, k, 1) == 0
+        assert torch.equal(hp, od.cpu())
