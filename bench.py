@@ -412,6 +412,10 @@ def _random_kquant(torch, qt, n_blocks, gen):
 def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None):
     import torch.distributed as dist
     from mojollama_b200.ep import EPMoELayer, row_bytes as rbytes
+    # the library's kernels, the NCCL exchanges and the timing events all on torch's
+    # current stream: the exchanges then follow the dispatch kernels, and the events
+    # bracket the device work (not just its issue)
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     c = dict(MOE)
     L = layers or c["L"]
     E, k, N, FF = c["E"], c["k"], c["N"], c["FF"]
