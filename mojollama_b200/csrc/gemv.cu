@@ -501,6 +501,72 @@ __global__ void __launch_bounds__(256) k_gemv_float(const WT *__restrict__ W, co
     }
 }
 
+// fp32 / fp16 / bf16 weights, few rows (a router): one CTA per row, the row split over
+// its 8 warps, up to 16 activation rows per launch; the row is read once for all of them
+// and the per-warp partial sums meet in shared memory
+constexpr int kFewRowsMaxB = 16;
+
+template <typename WT>
+__global__ void __launch_bounds__(256) k_gemv_float_rows(const WT *__restrict__ W, const float *__restrict__ x,
+                                                         float *__restrict__ out, int n_rows, int K, int nb_x,
+                                                         int vec_ok) {
+    constexpr int V = 16 / sizeof(WT);
+    __shared__ float part[8][kFewRowsMaxB];
+    const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const WT *wr = W + (size_t)row * K;
+    float acc[kFewRowsMaxB];
+#pragma unroll
+    for (int m = 0; m < kFewRowsMaxB; m++) acc[m] = 0.0f;
+    if (vec_ok) {
+        for (int k0 = threadIdx.x * V; k0 < K; k0 += 256 * V) {
+            union { int4 v; WT e[V]; } wv;
+            wv.v = __ldg(reinterpret_cast<const int4 *>(wr + k0));
+            float wf[V];
+#pragma unroll
+            for (int j = 0; j < V; j++) wf[j] = to_f<WT>(wv.e[j]);
+#pragma unroll
+            for (int m = 0; m < kFewRowsMaxB; m++) {
+                if (m < nb_x) {
+                    const float *xr = x + (size_t)m * K + k0;
+#pragma unroll
+                    for (int j = 0; j < V; j += 4) {
+                        const float4 xv = __ldg(reinterpret_cast<const float4 *>(xr + j));
+                        acc[m] = fmaf(wf[j + 0], xv.x, acc[m]);
+                        acc[m] = fmaf(wf[j + 1], xv.y, acc[m]);
+                        acc[m] = fmaf(wf[j + 2], xv.z, acc[m]);
+                        acc[m] = fmaf(wf[j + 3], xv.w, acc[m]);
+                    }
+                }
+            }
+        }
+    } else {
+        for (int k = threadIdx.x; k < K; k += 256) {
+            const float wv = to_f<WT>(wr[k]);
+#pragma unroll
+            for (int m = 0; m < kFewRowsMaxB; m++)
+                if (m < nb_x) acc[m] = fmaf(wv, __ldg(x + (size_t)m * K + k), acc[m]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kFewRowsMaxB; m++) {
+        if (m < nb_x) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < kFewRowsMaxB; m++) part[warp][m] = acc[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < nb_x) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) sum += part[w][threadIdx.x];
+        out[(size_t)threadIdx.x * n_rows + row] = sum;
+    }
+}
+
 // ------------------------------------------------------------------------------ launchers
 // Launch with programmatic stream serialization: the kernel may start while the previous
 // kernel on the stream finishes; it calls pdl_wait() before touching anything that kernel
@@ -749,6 +815,16 @@ static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows
     const int V = 16 / sizeof(WT);
     const int vec_ok = (K % V == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
                        ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((K * 4) % 16 == 0);
+    if (n_rows < c->num_sms * 8) {
+        // too few rows for a warp each to fill the GPU: a CTA per row
+        for (int b = 0; b < B; b += kFewRowsMaxB) {
+            const int take = (B - b) < kFewRowsMaxB ? (B - b) : kFewRowsMaxB;
+            k_gemv_float_rows<WT><<<n_rows, 256, 0, s>>>(w, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K,
+                                                         take, vec_ok);
+            count_launch();
+        }
+        return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    }
     const int warps = n_rows;
     int grid = (warps * 32 + 255) / 256;
     const int cap = c->num_sms * 8;

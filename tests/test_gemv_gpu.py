@@ -259,3 +259,18 @@ def test_pinned_host_output_written_in_place(cuda_device, qt, n):
         hp = torch.full((n,), float("nan")).pin_memory()
         assert lib.mlq_matmul(wd.data_ptr(), qt, xd.data_ptr(), hp.data_ptr(), n, k, 1) == 0
         assert torch.equal(hp, od.cpu())
+
+
+@pytest.mark.parametrize("qt", [F.F32, F.F16, F.BF16], ids=lambda q: F.NAMES[q])
+@pytest.mark.parametrize("n,k,B", [(128, 2048, 16), (128, 2048, 37), (7, 100, 3), (1000, 512, 1), (3000, 256, 5)])
+def test_float_weights_batch(cuda_device, qt, n, k, B):
+    """fp32/fp16/bf16 weights (routers, small heads): few rows take one CTA per row for
+    up to 16 activation rows per launch (B = 37: three launches), many rows a warp per row;
+    K = 100 exercises the scalar path."""
+    lib = cuda_device
+    w = make_w(qt, n, k, 31 + B)
+    x = np.random.default_rng(B + n).standard_normal(B * k).astype(np.float32)
+    out = np.full(B * n, np.nan, np.float32)
+    rc = lib.mlq_matmul(w.ctypes.data, qt, x.ctypes.data, out.ctypes.data, n, k, B)
+    assert rc == 0, lib.mlq_last_error_message()
+    assert O.rel_l2(out.reshape(B, n), O.gemv(w, qt, x, n, k)) < TOL
