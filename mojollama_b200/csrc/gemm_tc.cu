@@ -20,7 +20,9 @@
 // Error model: weights rounded once to fp16 (relative 2^-11), activations once (2^-11),
 // products and sums exact / fp32 -- relative L2 of the outputs ~3e-4.
 // Formats: Q8_0, Q4_0, Q4_1, Q5_0, Q4_K, Q5_K with K % 256 == 0 and 16-byte aligned rows
-// and chunks; others (Q6_K, MXFP4, odd K) stay on the dp4a kernels.
+// and chunks; Q6_K (210-byte super-blocks, only 2-byte aligned) with K % 256 == 0, copied
+// in 4-byte pieces from the 4-byte boundary at or below each super-block; MXFP4 and odd K
+// stay on their GEMV kernels.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -99,12 +101,17 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
 
 // ---------------------------------------------------------------- decode of 8 weights
 template <int QT> struct TcFmt;
-template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34; };
-template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18; };
-template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20; };
-template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22; };
-template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144; };
-template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176; };
+//   chunk_bytes  GGUF bytes of one row's 256-element chunk
+//   raw_row      shared-memory bytes per row of a raw stage
+template <int QT> struct TcFmt { static constexpr int chunk_bytes = 0, raw_row = 0; };
+template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34, raw_row = chunk_bytes; };
+template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18, raw_row = chunk_bytes; };
+template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20, raw_row = chunk_bytes; };
+template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22, raw_row = chunk_bytes; };
+template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144, raw_row = chunk_bytes; };
+template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176, raw_row = chunk_bytes; };
+// a super-block and the 2 bytes before it when it starts 2 bytes past a 4-byte boundary
+template <> struct TcFmt<MLQ_Q6_K> { static constexpr int chunk_bytes = 210, raw_row = 212; };
 
 // elements 8j .. 8j+7 of a 256-element row chunk (raw bytes `c`), the GGUF dequantization
 // of each format in fp32, rounded to fp16
@@ -132,6 +139,20 @@ __device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
             if constexpr (QT == MLQ_Q4_0) v[i] = d * (float)(q - 8);
             else if constexpr (QT == MLQ_Q4_1) v[i] = d * (float)q + f16_at(bp + 2);
             else v[i] = d * (float)((q | (int)(((qh >> e) & 1u) << 4)) - 16);
+        }
+    } else if constexpr (QT == MLQ_Q6_K) {
+        // ggml's dequantize_row_q6_K: element n = 128h + 32k + l (l < 32) is
+        // d * sc[8h + l/16 + 2k] * ((ql nibble | qh bits 2k..2k+1 << 4) - 32), the ql byte
+        // being ql[64h + l + 32(k & 1)] (low nibble for k < 2) and the qh byte qh[32h + l]
+        const int n0 = 8 * j, h = n0 >> 7, k = (n0 >> 5) & 3, l0 = n0 & 31;
+        const float ds = f16_at(c + 208) * (float)(int8_t)c[192 + 8 * h + (l0 >> 4) + 2 * k];
+        const uint8_t *ql = c + 64 * h + 32 * (k & 1), *qh = c + 128 + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int l = l0 + i;
+            const int lo = (k < 2) ? (ql[l] & 0xF) : (ql[l] >> 4);
+            const int q = lo | (((qh[l] >> (2 * k)) & 3) << 4);
+            v[i] = ds * (float)(q - 32);
         }
     } else {   // Q4_K, Q5_K: one 256-element super-block per chunk
         const int sub = j >> 2, g = sub >> 1, l0 = (j & 3) * 8;
@@ -236,7 +257,7 @@ struct TcSmem {
     static constexpr int a_bytes = 4 * kTcAtomBytes;                          // 64 KB
     static constexpr int b_atom = NT * 128;
     static constexpr int b_bytes = 4 * b_atom;                                // NT * 512
-    static constexpr int raw_bytes = kTcRows * TcFmt<QT>::chunk_bytes;
+    static constexpr int raw_bytes = kTcRows * TcFmt<QT>::raw_row;
     static constexpr int off_a = 0;
     static constexpr int off_b = a_bytes;                                     // 2 stages
     static constexpr int off_raw = off_b + 2 * b_bytes;                       // 2 stages
@@ -301,11 +322,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
     auto issue_copies = [&](int rt, int ci, int st) {
         const int r0 = rt * kTcRows;
         uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
-        for (int p = tid; p < kTcRows * pieces; p += kTcThreads) {
-            const int r = p / pieces, i = p - r * pieces;
-            if (r0 + r < a.n_rows)
-                cp_async16(raw + r * chunk_bytes + 16 * i,
-                           a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
+        if constexpr (QT == MLQ_Q6_K) {
+            // 4-byte pieces from the boundary at or below the super-block: 53 when it starts
+            // 2 bytes past one, else 52 pieces and its last 2 bytes (d) by a plain load, so
+            // that nothing past the super-block is read
+            for (int p = tid; p < kTcRows * 53; p += kTcThreads) {
+                const int r = p / 53, i = p - r * 53;
+                if (r0 + r >= a.n_rows) continue;
+                const uint8_t *src = a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210;
+                const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 3;
+                const uint8_t *base = src - off;
+                if (i < 52 || off) cp_async4(raw + r * 212 + 4 * i, base + 4 * i);
+                else *reinterpret_cast<uint16_t *>(raw + r * 212 + 208) = *reinterpret_cast<const uint16_t *>(src + 208);
+            }
+        } else {
+            for (int p = tid; p < kTcRows * pieces; p += kTcThreads) {
+                const int r = p / pieces, i = p - r * pieces;
+                if (r0 + r < a.n_rows)
+                    cp_async16(raw + r * chunk_bytes + 16 * i,
+                               a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
+            }
         }
         uint8_t *sb = smem + S::off_b + st * S::b_bytes;
         for (int p = tid; p < NT * 32; p += kTcThreads) {
@@ -349,7 +385,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             } else {
                 for (int p = tid; p < kTcRows * 32; p += kTcThreads) {
                     const int r = p >> 5, j = p & 31;
-                    const uint4 h = (r0 + r < a.n_rows) ? deq8<QT>(raw + r * chunk_bytes, j) : make_uint4(0, 0, 0, 0);
+                    uint4 h = make_uint4(0, 0, 0, 0);
+                    if (r0 + r < a.n_rows) {
+                        if constexpr (QT == MLQ_Q6_K) {
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                                                  (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
+                            h = deq8<QT>(raw + r * 212 + (src & 3), j);
+                        } else {
+                            h = deq8<QT>(raw + r * chunk_bytes, j);
+                        }
+                    }
                     *reinterpret_cast<uint4 *>(sa + sw128_off(r, j, kTcAtomBytes)) = h;
                 }
             }
@@ -486,6 +531,7 @@ bool tc_supported(int qt, const uint8_t *W, int K, long long row_bytes) {
         case MLQ_Q5_0: cb = TcFmt<MLQ_Q5_0>::chunk_bytes; break;
         case MLQ_Q4_K: cb = TcFmt<MLQ_Q4_K>::chunk_bytes; break;
         case MLQ_Q5_K: cb = TcFmt<MLQ_Q5_K>::chunk_bytes; break;
+        case MLQ_Q6_K: return K % kTcKC == 0 && ((uintptr_t)W & 3) == 0;
         default: return false;
     }
     return K % kTcKC == 0 && cb % 16 == 0 && row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
@@ -561,6 +607,7 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
         case MLQ_Q5_0: return launch_tc_q<MLQ_Q5_0>(a, NT, n_tok_tiles, s);
         case MLQ_Q4_K: return launch_tc_q<MLQ_Q4_K>(a, NT, n_tok_tiles, s);
         case MLQ_Q5_K: return launch_tc_q<MLQ_Q5_K>(a, NT, n_tok_tiles, s);
+        case MLQ_Q6_K: return launch_tc_q<MLQ_Q6_K>(a, NT, n_tok_tiles, s);
         default: return MLQ_ERR_UNSUPPORTED;
     }
 }

@@ -758,7 +758,10 @@ static int tc_min_m() {
 
 template <int QT>
 static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
-    if (tc_min_m() > 0 && B >= tc_min_m()) {
+    // Q6_K from 32 rows: at 16 its tensor-core decode (per element, 210-byte super-blocks
+    // in 4-byte pieces) measured slower than two passes of the 8-row GEMV
+    const int tc_from = QT == MLQ_Q6_K && tc_min_m() > 0 && tc_min_m() < 32 ? 32 : tc_min_m();
+    if (tc_from > 0 && B >= tc_from) {
         const int rc = launch_gemm_tc(W, QT, x, out, n_rows, K, B, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;
     }

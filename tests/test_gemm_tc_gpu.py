@@ -17,7 +17,7 @@ from oracle import ops as O
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
-TC_FORMATS = [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.Q4_K, F.Q5_K]
+TC_FORMATS = [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.Q4_K, F.Q5_K, F.Q6_K]
 
 
 def _mm(lib, torch, w, qt, x, n, k):
@@ -76,3 +76,25 @@ def test_tc_through_batch_matmul_abi(cuda_device, name, qt):
                                           out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n, k, b)
     want = O.gemv(w, qt, x, n, k)
     assert O.rel_l2(out.reshape(b, n), want) < TOL
+
+
+def test_q6k_batch_takes_tensor_cores(cuda_device):
+    """Q6_K at 64 tokens runs as one activation conversion + one tensor-core launch (not
+    8 passes of the 8-row GEMV), rows of 630 bytes (K = 768) included."""
+    import torch
+    lib = cuda_device
+    for n, k in [(1000, 2048), (300, 768)]:
+        rng = np.random.default_rng(n + k)
+        w = F.quantize(F.Q6_K, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+        x = rng.standard_normal((64, k)).astype(np.float32)
+        dw = torch.from_numpy(w).cuda()
+        dx = torch.from_numpy(x).cuda()
+        do = torch.empty(64 * n, device="cuda")
+        torch.cuda.synchronize()
+        l0 = lib.mlq_launch_count()
+        assert lib.mlq_matmul(ctypes.c_void_p(dw.data_ptr()), F.Q6_K, ctypes.c_void_p(dx.data_ptr()),
+                              ctypes.c_void_p(do.data_ptr()), n, k, 64) == 0
+        torch.cuda.synchronize()
+        assert lib.mlq_launch_count() - l0 == 2
+        got = do.cpu().numpy().reshape(64, n)
+        assert O.rel_l2(got, O.gemv(w, F.Q6_K, x, n, k)) < TOL
