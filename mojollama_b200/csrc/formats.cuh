@@ -40,6 +40,9 @@ template <> struct Fmt<MLQ_MXFP4_REF> { static constexpr int BE = 32,  BB = 17, 
 // an internal unit variant of MLQ_Q4_0, not an ABI type id
 constexpr int kQ4_0Pair = 2002;
 template <> struct Fmt<kQ4_0Pair>     { static constexpr int BE = 32,  BB = 18,  UE = 64; };
+// Q8_0 read as block pairs (64 elements, 68 bytes = 17 aligned words) likewise
+constexpr int kQ8_0Pair = 2008;
+template <> struct Fmt<kQ8_0Pair>     { static constexpr int BE = 32,  BB = 34,  UE = 64; };
 template <> struct Fmt<MLQ_Q4_K>      { static constexpr int BE = 256, BB = 144, UE = 64; };
 template <> struct Fmt<MLQ_Q5_K>      { static constexpr int BE = 256, BB = 176, UE = 64; };
 template <> struct Fmt<MLQ_Q6_K>      { static constexpr int BE = 256, BB = 210, UE = 64; };
@@ -331,6 +334,7 @@ struct XU64 {
 };
 template <> struct XU<MLQ_Q4_K> : XU64 {};
 template <> struct XU<kQ4_0Pair> : XU64 {};
+template <> struct XU<kQ8_0Pair> : XU64 {};
 template <> struct XU<MLQ_Q5_K> : XU64 {};
 
 __device__ __forceinline__ void load_xu64(const XPlanes &xp, int m, int u, XU64 &x) {
@@ -370,6 +374,32 @@ template <> struct W<kQ4_0Pair> {
         const int c0 = dot_words<8>(q, x.h, x.l);
         const int c1 = dot_words<8>(q + 8, x.h + 8, x.l + 8);
         return fmaf(d0, fmaf(x.s[0], (float)c0, -8.0f * x.sum[0]), d1 * fmaf(x.s[1], (float)c1, -8.0f * x.sum[1]));
+    }
+};
+
+// Q8_0 block pair u (blocks 2u, 2u+1) of a row that starts on a 4-byte boundary: 17
+// aligned words, an odd stride between lanes (conflict-free shared loads); the first
+// block's codes are bytes 2..33 (one PRMT per word), the second's words 9..16 as they are.
+template <> struct W<kQ8_0Pair> {
+    uint32_t q[16];
+    float d0, d1;
+    __device__ __forceinline__ void decode(const uint8_t *row, int u) {
+        const uint32_t *p = reinterpret_cast<const uint32_t *>(row + 68 * u);
+        uint32_t w[17];
+#pragma unroll
+        for (int i = 0; i < 17; i++) w[i] = p[i];
+        d0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            q[i] = __byte_perm(w[i], w[i + 1], 0x5432);
+            q[8 + i] = w[9 + i];
+        }
+    }
+    __device__ __forceinline__ float dot(const XU64 &x) const {
+        const int c0 = dot_words<8>(q, x.h, x.l);
+        const int c1 = dot_words<8>(q + 8, x.h + 8, x.l + 8);
+        return fmaf(d0 * x.s[0], (float)c0, d1 * x.s[1] * (float)c1);
     }
 };
 
@@ -552,7 +582,7 @@ template <int QT>
 __device__ __forceinline__ void load_xu(const XPlanes &xp, int m, int u, XU<QT> &x) {
     if constexpr (QT == MLQ_Q6_K) {
         load_xu_q6k(xp, m, u, x);
-    } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == kQ4_0Pair) {
+    } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == kQ4_0Pair || QT == kQ8_0Pair) {
         load_xu64(xp, m, u, x);
     } else {
         load_xu32<QT>(xp, m, u, x);

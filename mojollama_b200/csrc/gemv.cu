@@ -657,7 +657,7 @@ template <int QT> static int fast_rw() {
 template <int QT> static int fast_nw() {
     const char *e = getenv("MLQ_GEMV_WARPS");
     if (e && (atoi(e) == 16 || atoi(e) == 20 || atoi(e) == 24)) return atoi(e);
-    if constexpr (QT == kQ4_0Pair) return 24;
+    if constexpr (QT == kQ4_0Pair || QT == kQ8_0Pair) return 24;
     if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == MLQ_Q6_K || QT == MLQ_Q8_0) return 20;
     return kFastWarps;
 }
@@ -693,7 +693,17 @@ static int launch_q1_rw(const uint8_t *W, const float *x, float *out, int n_rows
 
 // formats whose M=1 kernel is built with 20 and 24 decode warps as well as 16
 template <int QT> constexpr bool kWarpVariants = QT == kQ4_0Pair || QT == MLQ_Q4_K || QT == MLQ_Q5_K ||
-                                                 QT == MLQ_Q6_K || QT == MLQ_Q8_0;
+                                                 QT == MLQ_Q6_K || QT == MLQ_Q8_0 || QT == kQ8_0Pair;
+
+// Q8_0 as block pairs where rows allow it (MLQ_Q8_0_PAIRS=0: single blocks)
+static bool q8_0_pairs() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_Q8_0_PAIRS");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v == 1;
+}
 
 template <int QT, int UPL>
 static int launch_q1_fast(const uint8_t *W, const float *x, float *out, int n_rows, int K, cudaStream_t s) {
@@ -725,6 +735,10 @@ static int launch_q1(const uint8_t *W, const float *x, float *out, int n_rows, i
         // block pairs: rows of 36-byte pairs on 4-byte boundaries
         if (K % 64 == 0 && K <= 2048 && (reinterpret_cast<uintptr_t>(W) & 3) == 0)
             return launch_q1<kQ4_0Pair>(W, x, out, n_rows, K, s);
+    }
+    if constexpr (QT == MLQ_Q8_0) {
+        if (q8_0_pairs() && K % 64 == 0 && K <= 2048 && (reinterpret_cast<uintptr_t>(W) & 3) == 0)
+            return launch_q1<kQ8_0Pair>(W, x, out, n_rows, K, s);
     }
     // only the variants that stay inside the 96 registers a 544-thread CTA allows:
     // 64-element units at 1 per lane (K <= 2048), 32-element units at <= 3 (K <= 3072)
@@ -1800,7 +1814,11 @@ int launch_gemv_seg(int qt, int n_seg, const uint8_t *const *W, const int *n_row
         case MLQ_Q4_0: return launch_seg_q<MLQ_Q4_0>(a, s);
         case MLQ_Q4_1: return launch_seg_q<MLQ_Q4_1>(a, s);
         case MLQ_Q5_0: return launch_seg_q<MLQ_Q5_0>(a, s);
-        case MLQ_Q8_0: return launch_seg_q<MLQ_Q8_0>(a, s);
+        case MLQ_Q8_0: {
+            bool pairs = q8_0_pairs() && K % 64 == 0;
+            for (int i = 0; i < n_seg; i++) pairs = pairs && (reinterpret_cast<uintptr_t>(W[i]) & 3) == 0;
+            return pairs ? launch_seg_q<kQ8_0Pair>(a, s) : launch_seg_q<MLQ_Q8_0>(a, s);
+        }
         case MLQ_Q4_K: return launch_seg_q<MLQ_Q4_K>(a, s);
         case MLQ_Q5_K: return launch_seg_q<MLQ_Q5_K>(a, s);
         case MLQ_Q6_K: return launch_seg_q<MLQ_Q6_K>(a, s);
