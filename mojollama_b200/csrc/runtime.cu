@@ -300,12 +300,53 @@ void *CallScope::stage(size_t bytes) {
     return p;
 }
 
+// Small inputs in pinned host memory: one kernel reads them over PCIe into the staging
+// buffer.  It lets the next kernel launch at once (programmatic dependent launch), so a
+// GEMV starts streaming its weights while the input is still crossing; the GEMV reads the
+// input only after its dependency wait.  A copy-engine transfer can overlap nothing.
+static constexpr size_t kPinnedKernelCopyMax = 256 * 1024;
+
+__global__ void __launch_bounds__(256) k_copy_pinned(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src,
+                                                     size_t n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
+    if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
+        for (size_t i = i0; 16 * i < n; i += step) {
+            if (16 * i + 16 <= n) {
+                reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+            } else {
+                for (size_t b = 16 * i; b < n; b++) dst[b] = src[b];
+            }
+        }
+    } else {
+        for (size_t b = i0; b < n; b += step) dst[b] = src[b];
+    }
+}
+
 const void *CallScope::in(const void *p, size_t bytes) {
     if (failed || !p) return nullptr;
-    if (is_device_ptr(p)) return p;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
+        cudaGetLastError();
+        pa.type = cudaMemoryTypeUnregistered;
+    }
+    if (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) return p;
     any_host = true;
     void *d = stage(bytes);
     if (!d) return nullptr;
+    void *hp = nullptr;
+    if (bytes && bytes <= kPinnedKernelCopyMax && pa.type == cudaMemoryTypeHost &&
+        cudaHostGetDevicePointer(&hp, const_cast<void *>(p), 0) == cudaSuccess && hp) {
+        const unsigned grid = (unsigned)((bytes + 4095) / 4096);
+        k_copy_pinned<<<grid, 256, 0, stream()>>>((uint8_t *)d, (const uint8_t *)hp, bytes);
+        count_launch();
+        if (!MLQ_CUDA(cudaGetLastError())) {
+            failed = true;
+            return nullptr;
+        }
+        return d;
+    }
+    cudaGetLastError();
     if (bytes && !MLQ_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, stream()))) {
         failed = true;
         return nullptr;

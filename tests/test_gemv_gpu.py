@@ -274,3 +274,26 @@ def test_float_weights_batch(cuda_device, qt, n, k, B):
     rc = lib.mlq_matmul(w.ctypes.data, qt, x.ctypes.data, out.ctypes.data, n, k, B)
     assert rc == 0, lib.mlq_last_error_message()
     assert O.rel_l2(out.reshape(B, n), O.gemv(w, qt, x, n, k)) < TOL
+
+
+@pytest.mark.parametrize("m,shift", [(1, 0), (1, 1), (3, 0), (40, 0)])
+def test_pinned_host_input(cuda_device, m, shift):
+    """Activations in pinned host memory: up to 256 KB are read over PCIe by a copy kernel
+    (16-byte pieces, or bytes when the buffer is not 16-byte aligned: shift), larger ones by
+    the copy engine; the result equals the device-buffer result bit for bit."""
+    import torch
+    lib = cuda_device
+    n, k = 20000, 2048
+    rng = np.random.default_rng(m + 10 * shift)
+    wd = torch.from_numpy(F.random_blocks(F.Q4_K, n * k, rng)).cuda()
+    x = rng.standard_normal(m * k).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.zeros(m * n, device="cuda")
+    assert lib.mlq_matmul(wd.data_ptr(), F.Q4_K, xd.data_ptr(), od.data_ptr(), n, k, m) == 0
+    lib.mlq_sync()
+    hx = torch.zeros(m * k + 4).pin_memory()
+    hx[shift:shift + m * k] = torch.from_numpy(x)
+    for _ in range(2):
+        ho = torch.full((m * n,), float("nan")).pin_memory()
+        assert lib.mlq_matmul(wd.data_ptr(), F.Q4_K, hx.data_ptr() + 4 * shift, ho.data_ptr(), n, k, m) == 0
+        assert torch.equal(ho, od.cpu())
