@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
                                                               float *__restrict__ part_ml, float *__restrict__ part_acc,
                                                               uint8_t *__restrict__ planes) {
     extern __shared__ float sm[];
+    pdl_wait();   // q, the KV rows and the split scratch follow earlier kernels
+    pdl_trigger();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int rep = nh / nkh;
     const int n_splits = gridDim.x;
@@ -187,6 +189,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
 // combine splits: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s
 __global__ void k_attn_merge(const float *__restrict__ part_ml, const float *__restrict__ part_acc, int n_splits,
                              int hd, float *__restrict__ out, int nh, uint8_t *__restrict__ planes) {
+    pdl_wait();
+    pdl_trigger();
     const int bh = blockIdx.x;   // b * nh + head
     float M = -INFINITY;
     for (int s = 0; s < n_splits; s++) M = fmaxf(M, part_ml[((size_t)bh * n_splits + s) * 2]);
@@ -232,6 +236,24 @@ static size_t attn_smem(int rep, int hd) {
 }
 
 // q [B][nh][hd] -> out [B][nh][hd]; scratch holds the split partials when needed
+// programmatic dependent launch (the kernel waits on its predecessor itself, pdl_wait());
+// MLQ_NO_PDL=1 launches normally
+template <typename... KArgs, typename... Args>
+static cudaError_t attn_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                   Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = getenv("MLQ_NO_PDL") ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
                        int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
                        float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes) {
@@ -265,9 +287,10 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
             cudaFuncSetAttribute(k_attn_decode<HD_>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024); \
             attr = true;                                                                                      \
         }                                                                                                     \
-        k_attn_decode<HD_><<<grid, kAttnThreads, smem, s>>>(q, kv, seq_lens_dev, seq_len_scalar, nh, nkh,     \
-                                                            window, scale, chunk1, out, part_ml, part_acc,    \
-                                                            planes);                                          \
+        if (!MLQ_CUDA(attn_launch_pdl(k_attn_decode<HD_>, grid, dim3(kAttnThreads), smem, s, q, kv,           \
+                                      seq_lens_dev, seq_len_scalar, nh, nkh, window, scale, chunk1, out,      \
+                                      part_ml, part_acc, planes)))                                            \
+            return MLQ_ERR_CUDA;                                                                              \
     } break;
     switch (hd) {
         MLQ_ATTN_CASE(64)
@@ -282,7 +305,9 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
 #undef MLQ_ATTN_CASE
     count_launch();
     if (n_splits > 1) {
-        k_attn_merge<<<B * nh, 128, 0, s>>>(part_ml, part_acc, n_splits, hd, out, nh, planes);
+        if (!MLQ_CUDA(attn_launch_pdl(k_attn_merge, dim3(B * nh), dim3(128), 0, s, (const float *)part_ml,
+                                      (const float *)part_acc, n_splits, hd, out, nh, planes)))
+            return MLQ_ERR_CUDA;
         count_launch();
     }
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;

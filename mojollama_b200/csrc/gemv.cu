@@ -595,6 +595,23 @@ static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, int smem, cudaSt
     return cudaLaunchKernelEx(&cfg, kern, args);
 }
 
+// the same for a kernel of several parameters
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_n(void (*kern)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t s,
+                                Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 static int stages_for(int fixed, int stage_bytes) {
     int n = (kSmemBudget - fixed) / stage_bytes;
     return n > kMaxStages ? kMaxStages : n;
@@ -1191,6 +1208,8 @@ struct GroupRows {
 // R packed activation rows: one warp per 32-element block (many independent warps: the
 // kernel is latency-bound on its loads, not on work)
 __global__ void __launch_bounds__(256) k_encode_packed(GroupRows src, int R, int K, uint8_t *__restrict__ planes) {
+    pdl_wait();   // the rows are an earlier kernel's output
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int kbr = K / 32;
     const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -1439,9 +1458,11 @@ int launch_encode_packed(const float *x, const float *x2, const int *rows, int R
                          cudaStream_t s) {
     if (R <= 0) return MLQ_OK;
     const long long blocks = ((long long)R * (K / 32) + 7) / 8;
-    k_encode_packed<<<(unsigned)blocks, 256, 0, s>>>(GroupRows{x, x2, rows, K}, R, K, planes);
     count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_n(k_encode_packed, dim3((unsigned)blocks), dim3(256), 0, s, GroupRows{x, x2, rows, K},
+                                 R, K, planes))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,
