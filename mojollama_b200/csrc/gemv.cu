@@ -1345,10 +1345,17 @@ __global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restri
     }
 }
 
-// rows per grouped tile: a multiple of the 16 decode warps, about 36 KB (every item then
-// gives each warp one or more whole rows to amortise its bookkeeping over), <= 64
+// rows per grouped tile: a multiple of the 16 decode warps, about 48 KB (every item then
+// gives each warp several whole rows to amortise its bookkeeping over), <= 64.  Config-3
+// MoE layers (16 tokens) measured 12.7 ms per 48-layer step at 36 KB tiles and 128 KB
+// groups, 10.85 ms at 48 KB tiles and 64 KB groups (MLQ_GROUP_TILE_KB, MLQ_GROUP_KB override)
 static int grouped_rpt(long long rb) {
-    long long r = 36864 / rb;
+    static int tile_kb = -1;
+    if (tile_kb < 0) {
+        const char *e = getenv("MLQ_GROUP_TILE_KB");
+        tile_kb = e && atoi(e) > 0 ? atoi(e) : 48;
+    }
+    long long r = (long long)tile_kb * 1024 / rb;
     r = r < 16 ? 16 : (r > 64 ? 64 : r);
     return (int)(r / 16 * 16);
 }
@@ -1371,10 +1378,15 @@ static int launch_grouped_t(const GroupedCall &gc, cudaStream_t s) {
     const int U = gc.K / Fmt<QT>::UE;
     int gs_log = 0;
     while ((1 << gs_log) < U && gs_log < 5) gs_log++;
-    // items per round-robin group: about 128 KB of weights, fewer when the call is small
+    // items per round-robin group: about 64 KB of weights, fewer when the call is small
     // enough that every SM should still get a couple of groups
     const long long tb = (long long)rpt * rb;
-    long long G = 131072 / tb;
+    static int group_kb = -1;
+    if (group_kb < 0) {
+        const char *e = getenv("MLQ_GROUP_KB");
+        group_kb = e && atoi(e) > 0 ? atoi(e) : 64;
+    }
+    long long G = (long long)group_kb * 1024 / tb;
     const long long spread = (long long)gc.n_items_bound / (2LL * c->num_sms);
     if (spread < G) G = spread;
     G = G < 1 ? 1 : (G > 32 ? 32 : G);
