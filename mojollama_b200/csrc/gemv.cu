@@ -674,7 +674,7 @@ template <int QT> static int fast_rw() {
 template <int QT> static int fast_nw() {
     const char *e = getenv("MLQ_GEMV_WARPS");
     if (e && (atoi(e) == 16 || atoi(e) == 20 || atoi(e) == 24)) return atoi(e);
-    if constexpr (QT == kQ4_0Pair || QT == kQ8_0Pair) return 24;
+    if constexpr (QT == kQ4_0Pair) return 24;   // Q8_0 pairs: 16 (larger tiles leave < 3 stages)
     if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == MLQ_Q6_K || QT == MLQ_Q8_0) return 20;
     return kFastWarps;
 }
