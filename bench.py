@@ -1,4 +1,4 @@
-"""Benchmark: quantized GEMV sweep (BASELINE config 2 at its largest shape).
+"""Benchmark: quantized GEMV sweep (benchmark config 2 at its largest shape).
 
 One step = one M=1 matrix-vector product over a 151936 x 2048 weight matrix in each
 of the six swept GGUF formats (Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, MXFP4) -- the decode
@@ -47,7 +47,7 @@ FORMATS = [("Q4_0", 2), ("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14), ("Q8_0", 8), (
 KERNEL_OF = {"MXFP4": "k_gemv_mxf4_tc (tcgen05.mma kind::mxf4, UE8M0 block scales)"}
 N_ROWS, K_COLS, DISTINCT = 151936, 2048, 4096
 METRIC = "quant-GEMV HBM GB/s (M=1, 151936x2048, 6 GGUF formats)"
-WORKLOAD = "quant-GEMV sweep Q4_0,Q4_K,Q5_K,Q6_K,Q8_0,MXFP4 at 151936x2048, M=1 (BASELINE config 2)"
+WORKLOAD = "quant-GEMV sweep Q4_0,Q4_K,Q5_K,Q6_K,Q8_0,MXFP4 at 151936x2048, M=1 (config 2)"
 BLOCK = {2: (32, 18), 12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 39: (32, 17)}
 
 
@@ -73,16 +73,34 @@ def make_weights(qt, seed=0, ref_layout=False):
 
 
 class Clocks:
-    """nvidia-smi sampler for the timed region."""
+    """nvidia-smi sampler for the timed region (CSV in a temporary directory).
+
+    start() returns once the first sample row exists (the sampler takes a few hundred ms
+    to start), so samples cover the timed region that follows; `busy` (optional) keeps
+    the GPU loaded while waiting, so the clocks seen are the clocks under load."""
 
     def __init__(self, index):
+        import tempfile
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"mlq_clocks_{os.getpid()}_{index}.csv")
 
-    def start(self):
+    def _rows(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            return sum(1 for line in open(self.path) if line.strip())
+        except OSError:
+            return 0
+
+    def wait_first(self, busy=None, limit_s=3.0):
+        t0 = time.perf_counter()
+        while self.proc and self._rows() < 1 and time.perf_counter() - t0 < limit_s:
+            if busy:
+                busy()
+            else:
+                time.sleep(0.02)
+
+    def start(self, busy=None):
+        try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
@@ -92,11 +110,15 @@ class Clocks:
                  "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        self.wait_first(busy)
 
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        time.sleep(0.25)
+        n0 = self._rows()
+        t0 = time.perf_counter()
+        while self._rows() <= n0 and time.perf_counter() - t0 < 1.0:   # one sample after the region
+            time.sleep(0.02)
         self.proc.terminate()
         self.proc.wait(timeout=5)
         self.f.close()
@@ -120,6 +142,14 @@ class Clocks:
             pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def our_config(world):
+    """the workload description both arms print (the reference arm runs the same workload
+    on the host cores)"""
+    return {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": "every weight matrix (165-331 MB) is larger than L2; no flush"}
 
 
 # ------------------------------------------------------------------------------ reference arm
@@ -154,7 +184,7 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "cpu"},
+            "data": "synthetic", "config": our_config(world),
             "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "reference",
                              "sample": "the full step (6 formats x 151936x2048 GEMV) per step"},
             "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -263,7 +293,7 @@ def run_ours(args, rank, world, local_rank):
     dom_name, dom_qt = max(FORMATS, key=lambda f: pre_ms[f[1]])
 
     clocks = Clocks(local_rank)
-    clocks.start()
+    clocks.start(busy=lambda: (step_dev(), stream.synchronize()))
     barrier()
     torch.cuda.synchronize()
     launches0 = lib.mlq_launch_count()
@@ -306,11 +336,34 @@ def run_ours(args, rank, world, local_rank):
     stream.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
 
+    # the same calls with pageable numpy x/out: the reference Python's own call shape
+    # (x staged through the library's arena by a copy, out copied back after the kernel)
+    px = np.ascontiguousarray(hx_np.copy())
+    pout = np.zeros(N_ROWS, np.float32)
+
+    def step_e2e_pageable():
+        for name, qt in FORMATS:
+            kern.quant_matmul_omp(host_w[qt].ctypes.data_as(cu), px.ctypes.data_as(cf),
+                                  pout.ctypes.data_as(cf), N_ROWS, K_COLS, qt)
+
+    for _ in range(max(3, args.warmup)):
+        step_e2e_pageable()
+    barrier()
+    torch.cuda.synchronize()
+    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start.record(stream)
+    for _ in range(args.steps):
+        step_e2e_pageable()
+    p_end.record(stream)
+    stream.synchronize()
+    e2e_pageable_ms = p_start.elapsed_time(p_end)
+    assert lib.mlq_last_error() == 0, lib.mlq_last_error_message()
+
     # max over ranks
-    t = torch.tensor([ms, e2e_ms, dom_ms], device="cuda")
+    t = torch.tensor([ms, e2e_ms, dom_ms, e2e_pageable_ms], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, dom_ms = (float(v) for v in t.tolist())
+    ms, e2e_ms, dom_ms, e2e_pageable_ms = (float(v) for v in t.tolist())
 
     step_bytes = sum(alg_bytes(qt) for _, qt in FORMATS)
     value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
@@ -332,14 +385,16 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 dp4a (Q4_0/K-quants/Q8_0), e2m1 x ue8m0 tcgen05 (MXFP4); fp32 accumulate", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "every weight matrix (165-331 MB) is larger than L2; no flush"},
+        "config": our_config(world),
         "per_format_gbs": None,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": K_COLS * 4 * len(FORMATS), "d2h_bytes_per_step": N_ROWS * 4 * len(FORMATS),
                 "api": "combined_engine.so quant_matmul_omp, pinned host x/out, resident weights; x copied in, "
-                       "out written into the pinned buffer by the GEMV kernel (d2h bytes cross PCIe in the kernel)"},
+                       "out written into the pinned buffer by the GEMV kernel (d2h bytes cross PCIe in the kernel)",
+                "pageable": {"value": round(world * step_bytes * args.steps / (e2e_pageable_ms / 1e3) / 1e9, 2),
+                             "unit": "GB/s",
+                             "api": "the same calls with pageable numpy x/out (the reference Python's call shape): "
+                                    "x staged by a copy, out copied back after the kernel"}},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": KERNEL_OF.get(dom_name, f"k_gemv_q1<{dom_name}>") + " (M=1 GEMV)",
                      "achieved": round(achieved, 1),
@@ -388,7 +443,7 @@ def run_decode_profile(args):
 
 
 # ------------------------------------------------------------------------------ MoE expert parallelism
-# BASELINE config 3's MoE FFN: 48 layers, d_model 2048, 128 experts, softmax top-8 with
+# Config 3's MoE FFN: 48 layers, d_model 2048, 128 experts, softmax top-8 with
 # renormalised weights, expert FFN 768, gate/up Q4_K and down Q6_K; the experts are split
 # over the ranks (expert parallelism), the router replicated.  Tokens per rank fixed (weak
 # scaling); each layer runs on the same N(0,1) token rows so the routing stays the one of
@@ -471,7 +526,7 @@ SWEEP_M = [1, 4, 16, 64, 256]
 
 
 def run_sweep(args):
-    """BASELINE config 2 in full: every format x shape x M, device-resident, CUDA events,
+    """Config 2 in full: every format x shape x M, device-resident, CUDA events,
     weights rotated over enough distinct copies that each launch reads from HBM (the set
     of copies is > 2x L2).  Prints one JSON object with GB/s (algorithmic bytes) and
     TFLOP/s (2*M*N*K) per case."""
@@ -563,7 +618,7 @@ def run_decode_only(args):
 
 
 # ------------------------------------------------------------------------------ model decode
-# TinyLlama-1.1B architecture, Q8_0 weights N(0, 0.02) from seed 0,
+# Config 1: TinyLlama-1.1B architecture, Q8_0 weights N(0, 0.02) from seed 0,
 # norms 1.0, B = 4 sequences, 16 prompt tokens each uniform in [0, 32000) from seed 0, then
 # 32 greedy tokens -- one batch_forward call per position (the batch engine's decode step).
 TL = dict(L=22, N=2048, NH=32, NKH=4, HD=64, FF=5632, V=32000, eps=1e-5, B=4, prompt=16, gen=32)

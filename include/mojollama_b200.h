@@ -64,6 +64,11 @@ int   mlq_set_stream(void *cuda_stream);
 int   mlq_use_own_stream(void);
 int   mlq_sync(void);                     /* wait for the stream; also reports device-side errors */
 int   mlq_device_status(void);            /* reads and clears the device error word */
+/* Self-test of the device-side bounded-wait error path (no counterpart in the reference):
+   one thread waits on a barrier nothing arrives on, gives up after limit_us (1..1e6)
+   microseconds and reports it; returns what mlq_sync() then returns, MLQ_ERR_TIMEOUT.
+   Nothing faults or hangs; the context stays usable. */
+int   mlq_selftest_wait_timeout(int limit_us);
 /* optional pre-residency of a whole host tensor (e.g. a 3-D expert tensor): every pointer
    inside it then maps to its device copy; unregister before freeing the host memory */
 int   mlq_register_weights(const void *host_ptr, size_t bytes);
@@ -119,6 +124,11 @@ int mlq_matmul_q8act(const void *W, int qt, const uint8_t *x_q8, float *out, int
    capture. */
 int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_q8, float *out, int n_rows, int n_cols,
                              int B, void *stream);
+/* Status of the mlq_matmul_q8act_noalloc calls on the current device (no counterpart in
+   the reference): waits for `stream`, then reads and clears the status word their
+   device-side bounded waits write.  MLQ_ERR_TIMEOUT when a wait gave up since the last
+   query (that call's output is incomplete), else MLQ_OK.  Allocates nothing. */
+int mlq_noalloc_status(void *stream);
 
 /* ---- row / elementwise ops (out may equal x: in place) ---- */
 /* out = x * w / sqrt(mean(x^2) + eps) per row (w may be NULL = ones).  sanitize = 1

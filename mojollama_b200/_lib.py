@@ -58,6 +58,8 @@ def core() -> ctypes.CDLL:
     so.mlq_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64]
     so.mlq_matmul_q8act.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci]
     so.mlq_matmul_q8act_noalloc.argtypes = [_vp, _ci, _vp, _vp, _ci, _ci, _ci, _vp]
+    so.mlq_noalloc_status.argtypes = [_vp]
+    so.mlq_selftest_wait_timeout.argtypes = [_ci]
     so.mlq_moe_forward.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _vp, _vp, _ci, _vp]
     so.mlq_moe_router.argtypes = [_vp, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _vp, _vp]
     so.mlq_ssm_decode_step.argtypes = [_vp] * 9 + [_ci] * 7

@@ -36,9 +36,11 @@ __device__ __forceinline__ const float *kv_vbase(const KVView &kv, int b) {
     return kv.pool_seq ? kv.pool_seq[b] + (long long)(kv.n_layers + kv.layer) * kv.layer_stride : kv.v;
 }
 
+// float offset of slot t of sequence b, or -1 when its page id lies outside a checked pool
 __device__ __forceinline__ long long kv_offset(const KVView &kv, int b, int t) {
     if (!kv.table) return (long long)t * kv.row_stride;
     const int page = kv.table[(size_t)b * kv.table_stride + t / kv.page_size];
+    if (kv.n_pages > 0 && (unsigned)page >= (unsigned)kv.n_pages) return -1;
     return (long long)page * kv.page_stride + (long long)(t % kv.page_size) * kv.row_stride;
 }
 
@@ -97,7 +99,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
                 vs[t * HD + d] = kv.tail_v[o];
                 continue;
             }
-            const long long off = kv_offset(kv, b, base + t) + (long long)g * HD + d;
+            const long long slot = kv_offset(kv, b, base + t);
+            if (slot < 0) {   // corrupt page id in a checked pool: zeros, no access
+                ks[t * (HD + 1) + d] = 0.0f;
+                vs[t * HD + d] = 0.0f;
+                continue;
+            }
+            const long long off = slot + (long long)g * HD + d;
             ks[t * (HD + 1) + d] = kb[off];
             vs[t * HD + d] = vb[off];
         }
@@ -223,6 +231,7 @@ __global__ void k_kv_write(KVView kv, float *k_base, float *v_base, const float 
     const int b = blockIdx.y;
     const int t = pos ? pos[b] : pos_scalar;
     const long long off = kv_offset(kv, b, t);
+    if (off < 0) return;
     float *kb = kv.pool_seq ? const_cast<float *>(kv_kbase(kv, b)) : k_base;
     float *vb = kv.pool_seq ? const_cast<float *>(kv_vbase(kv, b)) : v_base;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
@@ -338,6 +347,7 @@ __global__ void __launch_bounds__(256) k_rope_kv(float *__restrict__ q, float *_
     }
     __syncthreads();
     const long long off = kv_offset(kv, b, p);
+    if (off < 0) return;   // after the block-wide RoPE above; nothing below synchronises
     float *kc = const_cast<float *>(kv_kbase(kv, b)), *vc = const_cast<float *>(kv_vbase(kv, b));
     float *mkb = mk ? mk[b] : nullptr, *mvb = mv ? mv[b] : nullptr;
     size_t moff = 0;
@@ -429,7 +439,8 @@ int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_p
         return MLQ_ERR_ARG;
     }
     int max_len = 0;
-    if (!is_device_ptr(seq_lens)) {
+    const bool host_lens = !is_device_ptr(seq_lens);
+    if (host_lens) {
         for (int b = 0; b < B; b++) {
             if (seq_lens[b] < 0 || seq_lens[b] > table_stride * page_size) {
                 set_error(MLQ_ERR_CAPACITY, "mlq_attn_decode_paged: seq_len %d beyond the page table", seq_lens[b]);
@@ -439,6 +450,22 @@ int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_p
         }
     } else {
         max_len = table_stride * page_size;
+    }
+    // a host table is checked here, before anything is launched: every page a sequence
+    // reads (its first ceil(seq_len / page_size) entries; all of them when the lengths
+    // are on the device) must name a page of the pool
+    if (!is_device_ptr(table)) {
+        for (int b = 0; b < B; b++) {
+            const int used = host_lens ? (seq_lens[b] + page_size - 1) / page_size : table_stride;
+            for (int i = 0; i < used; i++) {
+                const int pg = table[(size_t)b * table_stride + i];
+                if (pg < 0 || pg >= n_pages) {
+                    set_error(MLQ_ERR_ARG, "mlq_attn_decode_paged: sequence %d, logical page %d -> page %d outside "
+                              "the pool of %d pages", b, i, pg, n_pages);
+                    return MLQ_ERR_ARG;
+                }
+            }
+        }
     }
     CallScope cs;
     const size_t pool = sizeof(float) * (size_t)n_pages * page_size * n_kv_head * head_dim;
@@ -453,6 +480,7 @@ int mlq_attn_decode_paged(const float *q, const float *k_pages, const float *v_p
     if (cs.failed) return cs.finish();
     KVView kv{dk, dv, dt, table_stride, (long long)page_size * n_kv_head * head_dim, page_size,
               n_kv_head * head_dim, nullptr, 0, 0, 0};
+    kv.n_pages = n_pages;   // device tables: a corrupt entry reads zeros, never outside the pool
     int rc = launch_attn_decode(dq, kv, dl, 0, max_len, B, n_head, n_kv_head, head_dim, window,
                                 1.0f / sqrtf((float)head_dim), dout, scr, sb, stream());
     if (rc != MLQ_OK) { cs.failed = true; cs.finish(); return rc; }

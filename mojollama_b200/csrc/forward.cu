@@ -561,6 +561,7 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
             }
             KVView kv{nullptr, nullptr, sb.tab, tab_w, (long long)ps * kvrow, ps, kvrow, sb.pools, layer_stride, l,
                       kv0->pt._n_layers};
+            kv.n_pages = kv0->pt.n_pages;
             // RoPE + KV store (+ KVBlock mirror) in one launch when the row layout allows
             const bool fused_kv = rc == MLQ_OK && inner == NH * HD && kvrow == NKH * HD &&
                                   launch_rope_kv(q, k, v, B, NH, NKH, HD, rope_dim, sb.pos, P->cos_t, P->sin_t, kv,

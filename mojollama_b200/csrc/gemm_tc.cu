@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             while (waited < issued) {
                 if (!mbar_wait_bounded(mma_bar, waited & 1)) {
                     *abort_flag = 1;
-                    atomicCAS(a.status, 0, DEV_ST_WAIT_FULL);
+                    report_status(a.status, DEV_ST_WAIT_FULL);
                     break;
                 }
                 waited++;

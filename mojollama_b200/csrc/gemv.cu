@@ -110,7 +110,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int M, int K, int stage_bytes,
 }
 
 __device__ __forceinline__ void raise_status(int *status, int code) {
-    if (status) atomicCAS(status, 0, code);
+    report_status(status, code);
 }
 
 struct NoFlush {

@@ -27,7 +27,9 @@ struct Ctx {
     int num_sms = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;   // where launches go (own or user-bound)
-    int *d_status = nullptr;         // device error word (0 = ok), written by bounded waits
+    int *d_status = nullptr;         // device view of the error word (0 = ok), written by bounded waits
+    volatile int *h_status = nullptr;  // the same word in mapped pinned host memory: read after a
+                                       // synchronisation at no cost
 };
 Ctx *ctx();                          // current device's context (initialises on first use)
 
@@ -129,6 +131,9 @@ struct KVView {
     // [B][tail_stride] instead of the cache (sequences that share one cache slot)
     const float *tail_k = nullptr, *tail_v = nullptr;
     int tail_stride = 0;
+    // physical pages in the pool (> 0: a table entry outside [0, n_pages) reads as zeros
+    // and is never written, instead of addressing memory outside the pool; 0: unchecked)
+    int n_pages = 0;
 };
 
 // planes non-null: the output rows [B][nh*hd] also written as packed activation rows, when

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
                 if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((it / a.n_stages) - 1) & 1);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok || *abort_flag) {
-                    if (lane == 0) { *abort_flag = 1; if (a.status) atomicCAS(a.status, 0, DEV_ST_WAIT_EMPTY); }
+                    if (lane == 0) { *abort_flag = 1; report_status(a.status, DEV_ST_WAIT_EMPTY); }
                     return;
                 }
             }
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) k_moe_gemv(MoeArgs a) {
         if (!*abort_flag) {
             if (lane == 0) ok = mbar_wait_bounded(&full[s], (it / a.n_stages) & 1);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok && lane == 0) { *abort_flag = 1; if (a.status) atomicCAS(a.status, 0, DEV_ST_WAIT_FULL); }
+            if (!ok && lane == 0) { *abort_flag = 1; report_status(a.status, DEV_ST_WAIT_FULL); }
         }
         const long long tile = (long long)blockIdx.x + (long long)it * gridDim.x;
         const int row0 = (int)(tile * a.rpt);

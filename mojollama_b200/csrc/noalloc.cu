@@ -21,8 +21,13 @@
 //   - the first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call before
 //     any stream capture.
+//   - the kernels' bounded waits report a wait that gave up in a status word of the same
+//     static kind (not in the context status word mlq_device_status reads, which would
+//     need an allocation to exist).  mlq_noalloc_status(stream) reads and clears it; it
+//     allocates nothing either.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "mlq_internal.h"
@@ -37,7 +42,7 @@ static __device__ __align__(256) float g_noalloc_act[kNoAllocMaxElems];
 static __device__ __align__(256) int g_noalloc_status[64];
 
 struct NoAllocDev {
-    bool ready = false;
+    std::atomic<bool> ready{false};   // stored with release after the fields below are set
     float *act = nullptr;
     int *status = nullptr;
     int num_sms = 0;
@@ -50,7 +55,7 @@ std::mutex g_mu;
 // and status word, and the SM count the launchers size their grids with.
 bool setup_device(int dev, NoAllocDev &d) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (d.ready) return true;
+    if (d.ready.load(std::memory_order_acquire)) return true;
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_act);
     if (e != cudaSuccess) {
@@ -74,8 +79,21 @@ bool setup_device(int dev, NoAllocDev &d) {
     d.act = static_cast<float *>(p);
     d.status = static_cast<int *>(q);
     d.num_sms = sms;
-    d.ready = true;
+    d.ready.store(true, std::memory_order_release);
     return true;
+}
+
+// The current device's set-up record (set up on first use), or null with the error set.
+NoAllocDev *current_device(const char *who) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+        cudaGetLastError();
+        mlq::set_error(MLQ_ERR_NO_DEVICE, "%s: no current device", who);
+        return nullptr;
+    }
+    NoAllocDev &d = g_dev[dev];
+    if (!d.ready.load(std::memory_order_acquire) && !setup_device(dev, d)) return nullptr;
+    return &d;
 }
 
 bool device_memory(const void *p) {
@@ -102,7 +120,8 @@ extern "C" int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_
                   (long long)B * n_cols, kNoAllocMaxElems);
         return MLQ_ERR_CAPACITY;
     }
-    if (block_elems(qt) <= 0 || n_cols % block_elems(qt)) {
+    // the same type check as mlq_matmul_q8act, before anything is launched
+    if (mlq_row_bytes(qt, n_cols) == 0) {
         set_error(MLQ_ERR_TYPE, "mlq_matmul_q8act_noalloc: type %d with n_cols %d", qt, n_cols);
         return MLQ_ERR_TYPE;
     }
@@ -110,14 +129,9 @@ extern "C" int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_
         set_error(MLQ_ERR_ARG, "mlq_matmul_q8act_noalloc: W, x_q8 and out must be device memory");
         return MLQ_ERR_ARG;
     }
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
-        cudaGetLastError();
-        set_error(MLQ_ERR_NO_DEVICE, "mlq_matmul_q8act_noalloc: no current device");
-        return MLQ_ERR_NO_DEVICE;
-    }
-    NoAllocDev &d = g_dev[dev];
-    if (!d.ready && !setup_device(dev, d)) return MLQ_ERR_CUDA;
+    NoAllocDev *dp = current_device("mlq_matmul_q8act_noalloc");
+    if (!dp) return mlq_last_error();
+    NoAllocDev &d = *dp;
     if (ref_compat() && qt == MLQ_MXFP4) qt = MLQ_MXFP4_REF;
 
     const LaunchEnv env{d.num_sms, d.status, true};
@@ -129,4 +143,24 @@ extern "C" int mlq_matmul_q8act_noalloc(const void *W, int qt, const uint8_t *x_
         rc = launch_matmul(static_cast<const uint8_t *>(W), qt, d.act, out, n_rows, n_cols, B,
                            mlq_row_bytes(qt, n_cols) * (size_t)n_rows, s);
     return rc;
+}
+
+// Status of the no-allocation calls on the current device: waits for `stream`, reads the
+// status word their bounded waits write, clears it, and returns MLQ_ERR_TIMEOUT when a
+// wait gave up (that call's output is then incomplete).  Allocates nothing.
+extern "C" int mlq_noalloc_status(void *stream) {
+    using namespace mlq;
+    NoAllocDev *dp = current_device("mlq_noalloc_status");
+    if (!dp) return mlq_last_error();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (!MLQ_CUDA(cudaMemcpyAsync(&h, dp->status, sizeof(int), cudaMemcpyDeviceToHost, s))) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(cudaStreamSynchronize(s))) return MLQ_ERR_CUDA;
+    if (h != 0) {
+        if (!MLQ_CUDA(cudaMemsetAsync(dp->status, 0, sizeof(int), s))) return MLQ_ERR_CUDA;
+        if (!MLQ_CUDA(cudaStreamSynchronize(s))) return MLQ_ERR_CUDA;
+        set_error(MLQ_ERR_TIMEOUT, "mlq_noalloc_status: a device-side bounded wait gave up (code %d)", h);
+        return MLQ_ERR_TIMEOUT;
+    }
+    return MLQ_OK;
 }

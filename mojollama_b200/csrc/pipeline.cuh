@@ -11,6 +11,14 @@ enum { DEV_ST_OK = 0, DEV_ST_WAIT_FULL = 0x101, DEV_ST_WAIT_EMPTY = 0x102, DEV_S
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 static constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
 
+// Report a wait that gave up: a plain store of a nonzero code (the word may be mapped
+// pinned host memory, where device atomics are not guaranteed), made visible system-wide.
+__device__ __forceinline__ void report_status(int *status, int code) {
+    if (!status) return;
+    *reinterpret_cast<volatile int *>(status) = code;
+    __threadfence_system();
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -50,14 +58,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for phase `parity` to complete; false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+// Wait for phase `parity` to complete; false after limit_ns (default kWaitLimitNs).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (;;) {
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > kWaitLimitNs) return false;
+        if (globaltimer() - t0 > limit_ns) return false;
     }
 }
 

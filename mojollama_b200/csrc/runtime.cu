@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
@@ -73,15 +74,29 @@ static bool init_device(int dev) {
     if (!MLQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return false;
     cudaStream_t s = nullptr;
     if (!MLQ_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking))) return false;
-    int *st = nullptr;
-    if (!MLQ_CUDA(cudaMalloc(&st, 64))) return false;
-    if (!MLQ_CUDA(cudaMemset(st, 0, 64))) return false;
+    // the status word lives in mapped pinned host memory: kernels write it over PCIe (only
+    // when a bounded wait gives up) and the host reads it after any synchronisation
+    int *hst = nullptr, *st = nullptr;
+    if (!MLQ_CUDA(cudaHostAlloc((void **)&hst, 64, cudaHostAllocMapped | cudaHostAllocPortable))) return false;
+    memset(hst, 0, 64);
+    if (!MLQ_CUDA(cudaHostGetDevicePointer((void **)&st, hst, 0))) return false;
     c.num_sms = sms;
     c.own_stream = s;
     c.stream = s;
     c.d_status = st;
+    c.h_status = hst;
     c.device = dev;
     return true;
+}
+
+// After a synchronisation: MLQ_ERR_TIMEOUT (and the word cleared) when a device-side
+// bounded wait gave up since the last check, else MLQ_OK.
+static int take_device_status(Ctx *c) {
+    const int h = c->h_status[0];
+    if (h == 0) return MLQ_OK;
+    c->h_status[0] = 0;
+    set_error(MLQ_ERR_TIMEOUT, "device-side bounded wait gave up (code 0x%x)", h);
+    return MLQ_ERR_TIMEOUT;
 }
 
 Ctx *ctx() {
@@ -423,6 +438,8 @@ int CallScope::finish() {
     }
     if (any_host) {
         if (!MLQ_CUDA(cudaStreamSynchronize(s))) return MLQ_ERR_CUDA;
+        // the call waited for its kernels anyway: report a bounded wait that gave up
+        if (Ctx *c = ctx()) return take_device_status(c);
     }
     return MLQ_OK;
 }
@@ -468,17 +485,33 @@ int mlq_use_own_stream(void) {
 int mlq_device_status(void) {
     Ctx *c = ctx();
     if (!c) return mlq_last_error();
-    int h = 0;
-    if (!MLQ_CUDA(cudaMemcpyAsync(&h, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream)))
-        return MLQ_ERR_CUDA;
     if (!MLQ_CUDA(cudaStreamSynchronize(c->stream))) return MLQ_ERR_CUDA;
-    if (h != 0) {
-        cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);
-        cudaStreamSynchronize(c->stream);
-        set_error(MLQ_ERR_TIMEOUT, "device-side bounded wait gave up (code %d)", h);
-        return MLQ_ERR_TIMEOUT;
+    return take_device_status(c);
+}
+
+// Self-test of the bounded-wait error path: one thread waits on a shared-memory mbarrier
+// that nothing ever arrives on, gives up after limit_us microseconds of %globaltimer and
+// writes DEV_ST_WAIT_FULL to the status word -- the path every pipeline wait of the
+// library takes when its producer never delivers.  Nothing faults or hangs.
+__global__ void k_wait_selftest(int *status, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (!mbar_wait_bounded(&bar, 0, limit_ns)) report_status(status, DEV_ST_WAIT_FULL);
+}
+
+int mlq_selftest_wait_timeout(int limit_us) {
+    if (limit_us <= 0 || limit_us > 1000000) {
+        set_error(MLQ_ERR_ARG, "mlq_selftest_wait_timeout: limit %d us outside 1..1000000", limit_us);
+        return MLQ_ERR_ARG;
     }
-    return MLQ_OK;
+    Ctx *c = ctx();
+    if (!c) return mlq_last_error();
+    k_wait_selftest<<<1, 32, 0, c->stream>>>(c->d_status, 1000ull * (unsigned long long)limit_us);
+    count_launch();
+    if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
+    return mlq_sync();
 }
 
 int mlq_sync(void) {

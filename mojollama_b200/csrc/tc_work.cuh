@@ -19,7 +19,7 @@ bool tc_tensor_map_rows(CUtensorMap *tmap, const void *base, long long rows, lon
 int *tc_counters(int n, cudaStream_t s);   // zeroed per-tile arrival counters (see gemv_mxf4_tc.cu)
 
 __device__ __forceinline__ void set_status(int *status, int code) {
-    if (status) atomicCAS(status, 0, code);
+    report_status(status, code);
 }
 
 // lane 0 waits (bounded), the verdict is shared by the warp
