@@ -410,7 +410,7 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
     if not args.no_decode and world == 1:
         line["decode"] = run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
-                                    cpu_seconds=args.cpu_seconds)
+                                    cpu_seconds=args.cpu_seconds, with_parity=not args.no_parity)
     if not args.no_moe_ep:
         line["moe_ep"] = run_moe_ep(torch, lib, rank, world)
     print(json.dumps(line), flush=True)
@@ -464,7 +464,7 @@ def _random_kquant(torch, qt, n_blocks, gen):
     return w.reshape(-1)
 
 
-def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None):
+def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None, with_parity=True):
     import torch.distributed as dist
     from mojollama_b200.ep import EPMoELayer, row_bytes as rbytes
     # the library's kernels, the NCCL exchanges and the timing events all on torch's
@@ -477,13 +477,24 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
     el = E // world
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     rgen = torch.Generator(device="cuda").manual_seed(99)   # same router on every rank
+    from mojollama_b200.ep import expert_slice
     layer_objs = []
     exp_bytes = FF * rbytes(c["gq"], N) * 2 + N * rbytes(c["dq"], FF)
-    for _ in range(L):
-        g = _random_kquant(torch, c["gq"], el * FF * N // 256, gen)
-        u = _random_kquant(torch, c["uq"], el * FF * N // 256, gen)
-        d = _random_kquant(torch, c["dq"], el * N * FF // 256, gen)
+    full0 = None
+    for li in range(L):
         router = torch.randn(E, N, device="cuda", generator=rgen) * 0.02
+        if li == 0 and with_parity:
+            # layer 0: every expert from one seed shared by the ranks, so that each rank can
+            # also run the whole layer alone (all E experts resident) as the parity check
+            g0 = torch.Generator(device="cuda").manual_seed(4321)
+            full0 = [_random_kquant(torch, c["gq"], E * FF * N // 256, g0),
+                     _random_kquant(torch, c["uq"], E * FF * N // 256, g0),
+                     _random_kquant(torch, c["dq"], E * N * FF // 256, g0), router]
+            g, u, d = (expert_slice(t, rank, world, E) for t in full0[:3])
+        else:
+            g = _random_kquant(torch, c["gq"], el * FF * N // 256, gen)
+            u = _random_kquant(torch, c["uq"], el * FF * N // 256, gen)
+            d = _random_kquant(torch, c["dq"], el * N * FF // 256, gen)
         layer_objs.append(EPMoELayer(rank, world, E, k, N, FF, c["gq"], c["uq"], c["dq"], g, u, d, router,
                                      renorm=True))
     x = torch.randn(tokens, N, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7 + rank))
@@ -514,10 +525,31 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     t = float(ms.item()) / steps
     finite = bool(torch.isfinite(out).all().item())
+    parity = None
+    if full0 is not None:
+        # expert-parallel layer 0 against the same layer with every expert on this rank
+        # (world 1: no exchange) on the same tokens: the dispatch and combine move rows
+        # without arithmetic, so the two must agree bit for bit
+        alone = EPMoELayer(0, 1, E, k, N, FF, c["gq"], c["uq"], c["dq"], full0[0], full0[1], full0[2], full0[3],
+                           renorm=True)
+        y_ep = layer_objs[0].forward(x, residual=x)
+        y_1 = alone.forward(x, residual=x)
+        torch.cuda.synchronize()
+        num = float(torch.linalg.vector_norm((y_ep - y_1).double()).item())
+        den = float(torch.linalg.vector_norm(y_1.double()).item())
+        res = torch.tensor([num / max(den, 1e-30), 0.0 if torch.equal(y_ep, y_1) else 1.0], device="cuda")
+        if world > 1:
+            dist.all_reduce(res, op=dist.ReduceOp.MAX)
+        parity = {"check": "expert-parallel layer 0 vs the same layer with all experts on one GPU, same tokens, "
+                           "every rank (max over ranks)",
+                  "ep_parity_rel_l2": float(res[0].item()), "dispatch_combine_bit_exact": res[1].item() == 0.0,
+                  "tolerance": 1e-3, "ok": float(res[0].item()) <= 1e-3}
+        del alone, full0
     return {"workload": f"config-3 MoE FFN stack: {L} layers, {E} experts top-{k} (renormalised), FF {FF}, "
                         f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), NCCL all-to-all",
             "tokens_per_rank": tokens, "tok_s": round(world * tokens / (t / 1e3), 1), "ms_per_step": round(t, 3),
             "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite,
+            "parity": parity,
             "host_issue_ms_per_step": round(host_ms, 3)}
 
 
@@ -613,7 +645,8 @@ def run_decode_only(args):
     stream = torch.cuda.Stream()
     lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
     print(json.dumps({"decode": run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
-                                           cpu_seconds=args.cpu_seconds)}), flush=True)
+                                           cpu_seconds=args.cpu_seconds, with_parity=not args.no_parity)}),
+          flush=True)
     return 0
 
 
@@ -691,7 +724,66 @@ def build_tinyllama(torch, lib, max_ctx):
     return b, keep, caches
 
 
-def run_decode(torch, lib, stream, with_cpu=True, cpu_seconds=10.0):
+def tinyllama_oracle_model(keep, b):
+    """The oracle's model description (oracle/model.py) of the bench's TinyLlama-shape
+    model: host copies of the same device bytes the library computes with."""
+    c = TL
+    L, N, NH, NKH, HD, FF, V = c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["FF"], c["V"]
+    import torch
+    src = b.bc
+
+    def host(ptr, nbytes, dtype=np.uint8):
+        t = next(k for k in keep if k.data_ptr() <= ptr < k.data_ptr() + k.numel() * k.element_size())
+        off = ptr - t.data_ptr()
+        return t.view(-1).view(torch.uint8)[off:off + nbytes].cpu().numpy().view(dtype).copy()
+
+    kv = NKH * HD
+    shapes = {"q": ("wQ", N, N), "k": ("wK", kv, N), "v": ("wV", kv, N), "o": ("wO", N, N), "gate": ("wG", FF, N),
+              "up": ("wU", FF, N), "down": ("wD", N, FF)}
+    layers = []
+    for l in range(L):
+        ly = {"type": "attn", "an": host(src.wAN[l], N * 4, np.float32), "fn": host(src.wFN[l], N * 4, np.float32)}
+        for key, (fld, r, k) in shapes.items():
+            ly[key] = (host(getattr(src, fld)[l], r * k // 32 * 34), 8)
+        layers.append(ly)
+    from oracle import ops as O
+    cos_t, sin_t = O.rope_tables(src.max_ctx, HD, HD)
+    return dict(L=L, N=N, NH=NH, NKH=NKH, HD=HD, FF=FF, V=V, eps=c["eps"], rope_dim=HD, max_ctx=src.max_ctx,
+                emb=host(src.emb, V * N * 4, np.float32).reshape(V, N), onw=host(src.onw, N * 4, np.float32),
+                wout=(host(src.wOut, V * N // 32 * 34), 8), cos=cos_t, sin=sin_t, moe=None, layers=layers)
+
+
+def decode_parity(keep, b, fed, logits, tol=3e-3, margin=1e-2):
+    """Config-1 parity at full size: the oracle (oracle/model.py forward_sequence, float64
+    accumulation over the exactly decoded Q8_0 weights) fed the tokens the library was fed
+    (prompts, then its own greedy tokens), position by position.  Reports the relative L2
+    of every position's logits (bar: 3e-3, three layers of 1e-3-bounded ops) and the
+    greedy tokens: where the oracle's top-2 margin exceeds 1e-2 the argmax must agree."""
+    try:
+        from oracle import model as OM
+        from oracle import ops as O
+        t0 = time.perf_counter()
+        m = tinyllama_oracle_model(keep, b)
+        want = OM.forward_sequence(m, fed)
+        P, B, V = logits.shape
+        rel = [O.rel_l2(logits[p], want[p]) for p in range(P)]
+        top2 = np.sort(want, axis=-1)[..., -2:]
+        decided = (top2[..., 1] - top2[..., 0]) > margin
+        agree = np.argmax(logits, -1) == np.argmax(want, -1)
+        return {"oracle": "oracle/model.py forward_sequence (numpy, float64 accumulation; pinned to the "
+                          "reference C build on small models)",
+                "positions": int(P), "sequences": int(B),
+                "logits_rel_l2_vs_oracle": float(max(rel)), "logits_rel_l2_median": float(np.median(rel)),
+                "tolerance": tol, "greedy_margin": margin,
+                "greedy_decided": int(decided.sum()), "greedy_agree_where_decided": int((agree & decided).sum()),
+                "greedy_agree_all": int(agree.sum()),
+                "ok": bool(max(rel) <= tol and bool(np.all(agree[decided]))),
+                "oracle_seconds": round(time.perf_counter() - t0, 1)}
+    except Exception as e:  # never let the checker break the bench line
+        return {"ok": False, "failed": f"{type(e).__name__}: {e}"}
+
+
+def run_decode(torch, lib, stream, with_cpu=True, cpu_seconds=10.0, with_parity=True):
     """Config 1 through batch_forward: device-resident (logits and tokens in HBM, greedy
     argmax on the device) and end to end (host tokens and logits, the reference's usage)."""
     c = TL
@@ -764,6 +856,26 @@ def run_decode(torch, lib, stream, with_cpu=True, cpu_seconds=10.0):
     assert lib.mlq_last_error() == 0, lib.mlq_last_error_message()
     greedy_host = np.argmax(h_logits.reshape(B, V), axis=1)
     step_bytes = sum(tinyllama_step_bytes(P + t) for t in range(G)) / G
+
+    parity = None
+    if with_parity:
+        # untimed: the same generation with every position's logits kept, then the oracle
+        # fed the same tokens (teacher-forced) on host copies of the same weights
+        reset()
+        bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        all_logits = torch.empty((P + G, B, V), device="cuda")
+        fed = torch.empty((P + G, B), dtype=torch.int32, device="cuda")
+        with torch.cuda.stream(stream):
+            for t in range(P + G):
+                if t < P:
+                    d_tok.copy_(d_prompts[t])
+                else:
+                    d_tok.copy_(torch.argmax(all_logits[t - 1], dim=1).to(torch.int32))
+                fed[t].copy_(d_tok)
+                fwd()
+                all_logits[t].copy_(d_logits.view(B, V))
+        stream.synchronize()
+        parity = decode_parity(keep, b, fed.cpu().numpy(), all_logits.cpu().numpy())
     out = {
         "workload": "TinyLlama-1.1B shape, Q8_0, B=4 x (16 prompt + 32 greedy) through batch_forward (config 1)",
         "tok_s": round(B * G / (dec_ms / 1e3), 1), "ms_per_step": round(dec_ms / G, 3),
@@ -771,7 +883,10 @@ def run_decode(torch, lib, stream, with_cpu=True, cpu_seconds=10.0):
         "e2e_tok_s": round(B * G / (t2 - t1), 1), "e2e_ms_per_step": round((t2 - t1) * 1e3 / G, 3),
         "e2e_io": {"h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * V * 4 + B * N * 4},
         "launches_per_step": int(launches),
-        "greedy_tokens_agree": bool(np.array_equal(greedy_dev, greedy_host)),
+        # self-consistency of the library (device argmax loop vs host argmax loop);
+        # the comparison with the oracle is `parity`
+        "device_and_host_loop_tokens_agree": bool(np.array_equal(greedy_dev, greedy_host)),
+        "parity": parity,
         "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
                      "achieved_gbs": round(step_bytes / (dec_ms / G / 1e3) / 1e9, 1)},
     }
@@ -910,6 +1025,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle checks of the model sections")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the config-1 model decode section")
     ap.add_argument("--decode-only", action="store_true", help="run only the config-1 model decode section")

@@ -129,6 +129,66 @@ def forward_step(model, state, seqs, tokens, compat_xn=None):
     return _mv(model["wout"], h, model["V"], N), h
 
 
+def forward_sequence(model, tokens):
+    """Teacher-forced decode of a dense-attention model: ``tokens`` [P][B] are fed one
+    position at a time from an empty cache, exactly as P consecutive ``forward_step``
+    calls (cengine_batch_instr.c:1233-1493, default data flow) would; returns the logits
+    of every position [P][B][V].  Each layer is computed for all P*B rows at once
+    (position p attends to positions 0..p of its own sequence), so every weight matrix is
+    decoded once per call instead of once per position.  Attention layers with
+    separate / QK-fused / QKV-fused projections and dense SwiGLU FFNs only (no SSM, no
+    MoE).  Checked against forward_step in tests/test_model_oracle.py."""
+    L, N, NH, NKH, HD = model["L"], model["N"], model["NH"], model["NKH"], model["HD"]
+    inner, kvrow = NH * HD, NKH * HD
+    eps = model["eps"]
+    rope_dim = model.get("rope_dim") or HD
+    tok = np.asarray(tokens, np.int64)
+    P, B = tok.shape
+    R = P * B                                                  # row r = p * B + b
+    x = model["emb"][tok.reshape(-1)].astype(np.float32)
+    if model.get("moe"):
+        raise ValueError("forward_sequence: dense models only")
+    for l in range(L):
+        ly = model["layers"][l]
+        if ly["type"] != "attn":
+            raise ValueError("forward_sequence: attention layers only")
+        xn, res = O.rms_norm(x, ly["an"], eps, sanitize=True)
+        if ly.get("qkv"):
+            qkv = _mv(ly["qkv"], xn, inner + 2 * N, N)
+            q, k, v = qkv[:, :inner], qkv[:, inner:inner + kvrow], qkv[:, inner + N:inner + N + kvrow]
+        elif ly.get("qk"):
+            qk = _mv(ly["qk"], xn, inner + kvrow, N)
+            q, k = qk[:, :inner], qk[:, inner:]
+            v = _mv(ly["v"], xn, kvrow, N)
+        else:
+            q, k, v = _mv(ly["q"], xn, inner, N), _mv(ly["k"], xn, kvrow, N), _mv(ly["v"], xn, kvrow, N)
+        qr = np.empty((R, inner), np.float32)
+        kr = np.empty((R, kvrow), np.float32)
+        for r in range(R):
+            pos = r // B
+            qr[r] = O.rope_neox(q[r], NH, HD, pos, model["cos"], model["sin"], rope_dim)
+            kr[r] = O.rope_neox(k[r], NKH, HD, pos, model["cos"], model["sin"], rope_dim)
+        vr = np.asarray(v, np.float32)
+        att = np.zeros((R, inner), np.float32)
+        for b in range(B):
+            ks, vs = kr[b::B], vr[b::B]                        # positions 0..P-1 of sequence b
+            for p in range(P):
+                att[p * B + b] = O.gqa_decode(qr[p * B + b], ks[:p + 1], vs[:p + 1], NH, NKH, HD)
+        wo = ly["attn_gate"] if ly.get("attn_gate") else ly["o"]
+        x = (res + _mv(wo, att, N, inner)).astype(np.float32)
+        xn, res = O.rms_norm(x, ly["fn"], eps, sanitize=True)
+        if ly.get("gate"):
+            FF = model["FF"]
+            g = _mv(ly["gate"], xn, FF, N).astype(np.float64)
+            u = _mv(ly["up"], xn, FF, N).astype(np.float64)
+            h = (g / (1 + np.exp(-g))) * u
+            x = (res + _mv(ly["down"], h, N, FF)).astype(np.float32)
+        else:
+            x = res
+    h, _ = O.rms_norm(x, model["onw"], eps, sanitize=True)
+    return _mv(model["wout"], h, model["V"], N).reshape(P, B, model["V"])
+
+
 # ------------------------------------------------------------------ qwen36_batch_forward
 def qwen36_new_state(model):
     L, n_kv = model["L"], model["NKH"] * model["HD"]

@@ -17,7 +17,7 @@ from oracle import ref as R
 
 from model_fixture import fill_bc, make_model, ws_stride
 
-pytestmark = pytest.mark.skipif(not R.available(), reason="reference build (oracle/_ref) not present")
+needs_ref = pytest.mark.skipif(not R.available(), reason="reference build (oracle/_ref) not present")
 
 
 @pytest.mark.parametrize("kind,kw,B,steps", [
@@ -25,6 +25,7 @@ pytestmark = pytest.mark.skipif(not R.available(), reason="reference build (orac
     ("hybrid", {}, 3, 2),
     ("qkv8192", {}, 2, 2),
 ], ids=["dense", "hybrid_ssm_moe", "fused_qkv"])
+@needs_ref
 def test_oracle_compat_step_matches_reference_build(kind, kw, B, steps):
     ref = R.RefEngine()
     m = make_model(kind, seed=21, **kw)
@@ -56,6 +57,7 @@ def test_oracle_compat_step_matches_reference_build(kind, kw, B, steps):
 
 
 @pytest.mark.parametrize("B", [1, 2])
+@needs_ref
 def test_oracle_qwen36_step_matches_reference_build(B):
     """qwen36_batch_forward (cengine_batch_instr.c:859-1231) on a 3 SSM + 1 attention layer
     MoE model whose fused QKV uses the layout the reference's split reads (N-wide K and V
@@ -88,3 +90,18 @@ def test_oracle_qwen36_step_matches_reference_build(B):
         assert O.rel_l2(kv_v[:, :step + 1], st["kv_v"][:, :step + 1]) < 1e-5
         kv_lens += 1
         st["kv_lens"] += 1
+
+
+@pytest.mark.parametrize("modes", [["sep", "qk", "qkv"], ["sep", "sep", "sep"]])
+def test_forward_sequence_equals_stepwise_forward(modes):
+    """The teacher-forced layer-outer restatement (used at full model size, where one
+    decode per position would take minutes) computes the same logits as P consecutive
+    forward_step calls."""
+    m = make_model("dense", seed=3, attn_modes=modes)
+    P, B = 5, 3
+    tok = np.random.default_rng(4).integers(0, m["V"], (P, B))
+    seq = OM.forward_sequence(m, tok)
+    st = OM.new_state(m, B)
+    for p in range(P):
+        lg, _ = OM.forward_step(m, st, list(range(B)), list(tok[p]))
+        assert O.rel_l2(seq[p], lg) < 1e-6, p
