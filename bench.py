@@ -587,6 +587,7 @@ def run_sweep(args):
             for m in ms:
                 x = torch.randn(m * k, device="cuda")
                 o = torch.empty(m * n, device="cuda")
+                torch.cuda.synchronize()   # x and the weights were written on torch's stream
 
                 def launch(i):
                     rc = lib.mlq_matmul(ctypes.c_void_p(dev.data_ptr() + (i % copies) * mat), qt,
@@ -686,6 +687,11 @@ def build_tinyllama(torch, lib, max_ctx):
         keep.append(q)
         return q.data_ptr()
 
+    # the library quantizes on torch's current stream while the model is built, so that each
+    # quantize kernel follows the torch.randn that fills its input and the temporary input
+    # is not reused by the caching allocator before the kernel has read it
+    prev_stream = lib.mlq_get_stream()
+    assert lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
     b = BCm.BCBuilder()
     bc = b.bc
     bc.L, bc.N, bc.NH, bc.NKH, bc.HD, bc.FF, bc.V, bc.eps, bc.nc = L, N, NH, NKH, HD, FF, V, c["eps"], N
@@ -721,6 +727,7 @@ def build_tinyllama(torch, lib, max_ctx):
     caches = [BCm.KVCache(L, NKH, HD) for _ in range(c["B"])]
     b.kv_array([kv.block for kv in caches])
     torch.cuda.synchronize()
+    assert lib.mlq_set_stream(ctypes.c_void_p(prev_stream)) == 0
     return b, keep, caches
 
 
@@ -778,6 +785,7 @@ def decode_parity(keep, b, fed, logits, tol=3e-3, margin=1e-2):
                 "greedy_decided": int(decided.sum()), "greedy_agree_where_decided": int((agree & decided).sum()),
                 "greedy_agree_all": int(agree.sum()),
                 "ok": bool(max(rel) <= tol and bool(np.all(agree[decided]))),
+                "rel_l2_per_position": [float(f"{r:.3g}") for r in rel],
                 "oracle_seconds": round(time.perf_counter() - t0, 1)}
     except Exception as e:  # never let the checker break the bench line
         return {"ok": False, "failed": f"{type(e).__name__}: {e}"}

@@ -184,6 +184,23 @@ int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, co
    tokens [B] (B <= 64), one new token per sequence; c->logits [B][outNR] is written and
    every kv_array[b]->seq_len[0] advances by one.  ws is accepted and unused. */
 int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws);
+
+/* ---- next-token selection on the device ----
+   The reference picks each next token on the host with np.argmax over the logits
+   (turbo_engine_v7_moe.py:2101-2114); these keep logits and tokens on the device.
+   mlq_sample: logits [B][V] -> tokens [B].  temperature <= 0: greedy, exactly np.argmax
+   (first maximum; a NaN counts as the maximum).  temperature > 0: a draw from
+   softmax(logits / temperature) by the Gumbel-max rule argmax(logit/T - log(-log u)),
+   u from a counter-based generator keyed by (seed, step, row, index) -- reproducible,
+   restated in numpy by oracle/sampling.py.  B <= 1024.  Calls on one device share a small
+   per-device state: calls that may overlap on the GPU (unordered streams) race. */
+int mlq_sample(const float *logits, int B, int V, float temperature, unsigned long long seed,
+               unsigned long long step, int *tokens);
+int mlq_argmax(const float *logits, int B, int V, int *tokens);   /* mlq_sample with temperature 0 */
+/* one batch_forward step, then mlq_sample on its logits into next_tokens (which may be the
+   tokens buffer itself); with device tokens / logits / next_tokens nothing reaches the host */
+int mlq_batch_forward_sample(const void *bc, const int *tokens, int B, float *ws, float temperature,
+                             unsigned long long seed, unsigned long long step, int *next_tokens);
 /* moe_ffn: layer l's routed experts for x [B][N] -> ffn [B][N] (cengine_batch_instr.c:591) */
 int mlq_moe_ffn(const void *bc, int l, const float *x, float *ffn, int B);
 /* forget the cached per-model device plans (also done by mlq_cache_clear) */

@@ -65,6 +65,10 @@ def core() -> ctypes.CDLL:
     so.mlq_ssm_decode_step.argtypes = [_vp] * 9 + [_ci] * 7
     so.mlq_ssm_layer_fused.argtypes = [_vp] * 10 + [_vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci] + [_ci] * 7
     so.mlq_batch_forward.argtypes = [_vp, _vp, _ci, _vp]
+    so.mlq_sample.argtypes = [_vp, _ci, _ci, ctypes.c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]
+    so.mlq_argmax.argtypes = [_vp, _ci, _ci, _vp]
+    so.mlq_batch_forward_sample.argtypes = [_vp, _vp, _ci, _vp, ctypes.c_float, ctypes.c_ulonglong,
+                                            ctypes.c_ulonglong, _vp]
     so.mlq_moe_ffn.argtypes = [_vp, _ci, _vp, _vp, _ci]
     so.mlq_forget_model_plans.restype = None
     so.mlq_sizeof_bc.restype = ctypes.c_size_t

@@ -96,3 +96,36 @@ def test_short_and_odd_rows(cuda_device, qt, K):
     out = torch.full((B, n), float("nan"), device="cuda")
     _call(cuda_device, qt, [torch.from_numpy(raw).cuda()], [out], None, 0, x)
     _check(out.cpu().numpy(), x.astype(np.float64) @ Wm.T)
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_config1_layer_shapes(cuda_device, B):
+    """The config-1 (TinyLlama-1.1B shape, Q8_0) decode projections at their full sizes:
+    q/k/v (2048 + 256 + 256 rows, K 2048) in one launch, o + residual (2048 x 2048),
+    gate/up + SiLU-mul (5632 x 2048) and down + residual (2048 x 5632, the long rows)."""
+    qt = F.Q8_0
+    rng = np.random.default_rng(40 + B)
+    N, FF, kv = 2048, 5632, 256
+    x = rng.standard_normal((B, N)).astype(np.float32)
+    xd = x.astype(np.float64)
+    parts = [_mat(qt, r, N, rng) for r in (N, kv, kv)]
+    outs = [torch.full((B, p[1].shape[0]), float("nan"), device="cuda") for p in parts]
+    _call(cuda_device, qt, [torch.from_numpy(p[0]).cuda() for p in parts], outs, None, 0, x)
+    for o, p in zip(outs, parts):
+        _check(o.cpu().numpy(), xd @ p[1].T)
+    raw, Wm = _mat(qt, N, N, rng)
+    r = rng.standard_normal((B, N)).astype(np.float32)
+    out = torch.full((B, N), float("nan"), device="cuda")
+    _call(cuda_device, qt, [torch.from_numpy(raw).cuda()], [out], [torch.from_numpy(r).cuda()], 1, x)
+    _check(out.cpu().numpy(), r.astype(np.float64) + xd @ Wm.T)
+    g, Gm = _mat(qt, FF, N, rng)
+    u, Um = _mat(qt, FF, N, rng)
+    out = torch.full((B, FF), float("nan"), device="cuda")
+    _call(cuda_device, qt, [torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()], [out, out], None, 2, x)
+    gv, uv = xd @ Gm.T, xd @ Um.T
+    _check(out.cpu().numpy(), gv / (1 + np.exp(-gv)) * uv)
+    h = rng.standard_normal((B, FF)).astype(np.float32)
+    raw, Wm = _mat(qt, N, FF, rng)
+    out = torch.full((B, N), float("nan"), device="cuda")
+    _call(cuda_device, qt, [torch.from_numpy(raw).cuda()], [out], [torch.from_numpy(r).cuda()], 1, h)
+    _check(out.cpu().numpy(), r.astype(np.float64) + h.astype(np.float64) @ Wm.T)
