@@ -185,6 +185,28 @@ int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, co
    every kv_array[b]->seq_len[0] advances by one.  ws is accepted and unused. */
 int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws);
 
+/* ---- Mamba-2 decode step (no counterpart in the reference) ----
+   The reference's ssm_decode_step (cengine_batch_instr.c:736-797) is a toy kept byte-
+   compatible above; these are the published Mamba-2 recurrence (Dao & Gu 2024), one token
+   per sequence, for config 5's hybrid model.  H heads of P channels, state size S, G groups
+   of B/C (H % G == 0), conv width d_conv (<= 8).  Layouts: xbc [B][H*P + 2*G*S] (x | B | C),
+   z [B][H*P] (NULL: no gate), dt [B][H], conv_state [B][conv_dim][d_conv] (last d_conv
+   inputs, newest last), conv_w [conv_dim][d_conv], conv_b [conv_dim] (NULL: none), A_log /
+   dt_bias / D [H] (A = -exp(A_log); D NULL: none), norm_w [H*P] (NULL: no norm), ssm_state
+   [B][H][P][S]; both states are updated in place.  y [B][H*P] = norm_w * rmsnorm(y * silu(z))
+   over groups of norm_group elements (0: the whole H*P).  P % 32 == 0; S in {16, 32, 64} or
+   a multiple of 128. */
+int mlq_mamba2_step(const float *xbc, const float *z, const float *dt, float *conv_state, const float *conv_w,
+                    const float *conv_b, const float *A_log, const float *dt_bias, const float *D,
+                    const float *norm_w, float *ssm_state, float *y, int B, int H, int P, int S, int G, int d_conv,
+                    float eps, int norm_group);
+/* the mixer: proj = W_in u (rows z | xBC | dt; W_in [H*P + conv_dim + H][hidden] of type
+   qt_in), the step, out [B][hidden] = W_out y (W_out [hidden][H*P] of type qt_out) */
+int mlq_mamba2_layer(const float *u, int B, int hidden, const void *W_in, int qt_in, const void *W_out, int qt_out,
+                     float *conv_state, const float *conv_w, const float *conv_b, const float *A_log,
+                     const float *dt_bias, const float *D, const float *norm_w, float *ssm_state, float *out, int H,
+                     int P, int S, int G, int d_conv, float eps, int norm_group);
+
 /* ---- next-token selection on the device ----
    The reference picks each next token on the host with np.argmax over the logits
    (turbo_engine_v7_moe.py:2101-2114); these keep logits and tokens on the device.

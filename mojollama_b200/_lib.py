@@ -67,6 +67,8 @@ def core() -> ctypes.CDLL:
     so.mlq_batch_forward.argtypes = [_vp, _vp, _ci, _vp]
     so.mlq_sample.argtypes = [_vp, _ci, _ci, ctypes.c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]
     so.mlq_argmax.argtypes = [_vp, _ci, _ci, _vp]
+    so.mlq_mamba2_step.argtypes = [_vp] * 12 + [_ci] * 6 + [ctypes.c_float, _ci]
+    so.mlq_mamba2_layer.argtypes = [_vp, _ci, _ci, _vp, _ci, _vp, _ci] + [_vp] * 9 + [_ci] * 5 + [ctypes.c_float, _ci]
     so.mlq_batch_forward_sample.argtypes = [_vp, _vp, _ci, _vp, ctypes.c_float, ctypes.c_ulonglong,
                                             ctypes.c_ulonglong, _vp]
     so.mlq_moe_ffn.argtypes = [_vp, _ci, _vp, _vp, _ci]
