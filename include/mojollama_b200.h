@@ -185,6 +185,39 @@ int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, co
    every kv_array[b]->seq_len[0] advances by one.  ws is accepted and unused. */
 int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws);
 
+/* ---- GGUF reader and device weight loader ----
+   Replaces the reference's gguf-py load path (turbo_engine_v7_moe.py:425-618: GGUFReader,
+   numpy views of the mmapped file, host F32 copies).  The file is parsed natively (GGUF
+   versions 2 and 3) and mapped; mlq_gguf_upload streams its whole data section into HBM
+   unchanged (mmap -> two pinned buffers -> copy engine), so tensor i is at dev + its offset
+   in GGUF block layout, ready for mlq_matmul / batch_forward device pointers. */
+typedef struct {
+    char name[128];
+    int n_dims;
+    int64_t dims[4];      /* as stored: dims[0] is the contiguous (fastest) dimension */
+    int type;             /* ggml type code */
+    uint64_t offset;      /* inside the data section */
+    uint64_t bytes;       /* 0 when the type's block layout is not known to this library */
+} MlqGgufTensor;
+void *mlq_gguf_open(const char *path);      /* NULL on error (mlq_last_error_message) */
+int mlq_gguf_close(void *h);
+int mlq_gguf_version(void *h);
+int64_t mlq_gguf_n_tensors(void *h);
+int64_t mlq_gguf_n_kv(void *h);
+uint64_t mlq_gguf_alignment(void *h);
+uint64_t mlq_gguf_data_offset(void *h);     /* file offset of the data section */
+uint64_t mlq_gguf_data_bytes(void *h);
+int mlq_gguf_tensor(void *h, int64_t i, MlqGgufTensor *out);
+int64_t mlq_gguf_find(void *h, const char *name);            /* -1 if absent */
+int mlq_gguf_kv_type(void *h, const char *key);              /* GGUF value type 0..12, -1 if absent */
+int mlq_gguf_kv_int(void *h, const char *key, int64_t *out); /* integer and bool values */
+int mlq_gguf_kv_float(void *h, const char *key, double *out);
+int64_t mlq_gguf_kv_str(void *h, const char *key, char *buf, size_t len);   /* full length, -1 if absent */
+int64_t mlq_gguf_kv_array(void *h, const char *key, int *item_type);       /* count, -1 if not an array */
+const void *mlq_gguf_tensor_data(void *h, int64_t i);        /* host view in the mapping */
+int mlq_gguf_upload(void *h, void *dev, uint64_t dev_bytes);               /* whole data section */
+int mlq_gguf_upload_tensor(void *h, int64_t i, void *dev, uint64_t dev_bytes);
+
 /* ---- Mamba-2 decode step (no counterpart in the reference) ----
    The reference's ssm_decode_step (cengine_batch_instr.c:736-797) is a toy kept byte-
    compatible above; these are the published Mamba-2 recurrence (Dao & Gu 2024), one token

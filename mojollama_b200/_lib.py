@@ -67,6 +67,30 @@ def core() -> ctypes.CDLL:
     so.mlq_batch_forward.argtypes = [_vp, _vp, _ci, _vp]
     so.mlq_sample.argtypes = [_vp, _ci, _ci, ctypes.c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]
     so.mlq_argmax.argtypes = [_vp, _ci, _ci, _vp]
+    so.mlq_gguf_open.restype = _vp
+    so.mlq_gguf_open.argtypes = [ctypes.c_char_p]
+    for fn in ("mlq_gguf_close", "mlq_gguf_version"):
+        getattr(so, fn).argtypes = [_vp]
+    for fn in ("mlq_gguf_n_tensors", "mlq_gguf_n_kv"):
+        getattr(so, fn).argtypes = [_vp]
+        getattr(so, fn).restype = ctypes.c_int64
+    for fn in ("mlq_gguf_alignment", "mlq_gguf_data_offset", "mlq_gguf_data_bytes"):
+        getattr(so, fn).argtypes = [_vp]
+        getattr(so, fn).restype = ctypes.c_uint64
+    so.mlq_gguf_tensor.argtypes = [_vp, ctypes.c_int64, _vp]
+    so.mlq_gguf_find.argtypes = [_vp, ctypes.c_char_p]
+    so.mlq_gguf_find.restype = ctypes.c_int64
+    so.mlq_gguf_kv_type.argtypes = [_vp, ctypes.c_char_p]
+    so.mlq_gguf_kv_int.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+    so.mlq_gguf_kv_float.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
+    so.mlq_gguf_kv_str.argtypes = [_vp, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
+    so.mlq_gguf_kv_str.restype = ctypes.c_int64
+    so.mlq_gguf_kv_array.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(_ci)]
+    so.mlq_gguf_kv_array.restype = ctypes.c_int64
+    so.mlq_gguf_tensor_data.argtypes = [_vp, ctypes.c_int64]
+    so.mlq_gguf_tensor_data.restype = _vp
+    so.mlq_gguf_upload.argtypes = [_vp, _vp, ctypes.c_uint64]
+    so.mlq_gguf_upload_tensor.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_uint64]
     so.mlq_mamba2_step.argtypes = [_vp] * 12 + [_ci] * 6 + [ctypes.c_float, _ci]
     so.mlq_mamba2_layer.argtypes = [_vp, _ci, _ci, _vp, _ci, _vp, _ci] + [_vp] * 9 + [_ci] * 5 + [ctypes.c_float, _ci]
     so.mlq_batch_forward_sample.argtypes = [_vp, _vp, _ci, _vp, ctypes.c_float, ctypes.c_ulonglong,

@@ -113,8 +113,11 @@ def test_mamba2_step_matches_oracle(cuda_device, B, H, P, S, G, gated, norm_grou
         z = rng.standard_normal((B, d_inner)).astype(np.float32) if gated else None
         dt = rng.standard_normal((B, H)).astype(np.float32)              # dt softplus of N(0, 1) + bias
         y = torch.full((B, d_inner), float("nan"), device="cuda")
+        # device copies held in names until the call has run (a temporary's memory could be
+        # handed to the next allocation before the kernels read it)
+        dx, ddt = _dev(xbc), _dev(dt)
         dz = _dev(z) if gated else None
-        rc = lib.mlq_mamba2_step(_vp(_dev(xbc)), _vp(dz), _vp(_dev(dt)), _vp(cs), *[_vp(x) for x in prm], _vp(ss),
+        rc = lib.mlq_mamba2_step(_vp(dx), _vp(dz), _vp(ddt), _vp(cs), *[_vp(x) for x in prm], _vp(ss),
                                  _vp(y), B, H, P, S, G, K, ctypes.c_float(1e-5), norm_group)
         assert rc == 0, lib.mlq_last_error_message()
         want = M2.mamba2_step(xbc, z, dt, cs_o, conv_w, conv_b, A_log, dt_bias, D, norm_w, ss_o, H, P, S, G,
