@@ -356,6 +356,16 @@ void mlq_page_table_destroy(MlqPageTable *pt);               /* frees pool, tabl
 int  mlq_kv_init(MlqKVBlock *kv, int L, int nkh, int hd);
 int  mlq_kv_alloc(MlqKVBlock *kv);
 void mlq_kv_free(MlqKVBlock *kv);
+
+/* ---- KV snapshots for the prefix cache (no counterpart in the C engine; the reference's
+   Python prefix cache copies whole host KV arrays, prefix_cache.py:164-222) ----
+   mlq_kv_snapshot: positions [0, len) (len <= seq_len) of every layer's K and V rows out of
+   a KVBlock's page pool, packed as [2][n_layers][len][nkh*hd] floats at dst.
+   mlq_kv_restore: the reverse; maps pages from the block's free list where its table has
+   none, copies src in, sets seq_len = len.  dst / src may be device or host memory. */
+int mlq_kv_snapshot(const MlqKVBlock *kv, int len, float *dst);
+int mlq_kv_restore(MlqKVBlock *kv, int len, const float *src);
+
 size_t mlq_sizeof_page_table(void);
 size_t mlq_sizeof_kv_block(void);
 /* simd_ops.c:209: copy one position's rows to offset n_past*nkh*hd (layer ignored) */

@@ -67,6 +67,8 @@ def core() -> ctypes.CDLL:
     so.mlq_batch_forward.argtypes = [_vp, _vp, _ci, _vp]
     so.mlq_sample.argtypes = [_vp, _ci, _ci, ctypes.c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]
     so.mlq_argmax.argtypes = [_vp, _ci, _ci, _vp]
+    so.mlq_kv_snapshot.argtypes = [_vp, _ci, _vp]
+    so.mlq_kv_restore.argtypes = [_vp, _ci, _vp]
     so.mlq_gguf_open.restype = _vp
     so.mlq_gguf_open.argtypes = [ctypes.c_char_p]
     for fn in ("mlq_gguf_close", "mlq_gguf_version"):

@@ -11,6 +11,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -125,6 +126,82 @@ void mlq_kv_free(MlqKVBlock *kv) {
     if (kv->v) cudaFree(kv->v);
     kv->k = kv->v = nullptr;
     mlq_page_table_destroy(&kv->pt);
+}
+
+// ------------------------------------------------------------------ snapshots (prefix cache)
+// packed [2][L][len][row]: K of every layer, then V; element (kind, layer, pos, i) lives in
+// the pool at ((kind * L + layer) * n_pages + table[pos / ps]) * ps + pos % ps, row i
+__global__ void k_kv_pack(float *__restrict__ pool, const int *__restrict__ table, float *__restrict__ packed,
+                          int L, int n_pages, int ps, int row, int len, int to_pool) {
+    const int layer = blockIdx.y, kind = blockIdx.z;
+    const long long n = (long long)len * row;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+        const int pos = (int)(e / row), i = (int)(e - (long long)pos * row);
+        const long long slot = ((long long)(kind * L + layer) * n_pages + table[pos / ps]) * ps + pos % ps;
+        float *pp = pool + slot * row + i;
+        float *qq = packed + ((long long)(kind * L + layer) * len + pos) * row + i;
+        if (to_pool) *pp = *qq;
+        else *qq = *pp;
+    }
+}
+
+static int kv_pack(MlqKVBlock *kv, int len, float *packed, int to_pool, const char *who) {
+    const MlqPageTable &pt = kv->pt;
+    const int row = pt._nkh * pt._hd, L = pt._n_layers;
+    const int used = (len + pt.page_size - 1) / pt.page_size;
+    for (int i = 0; i < used; i++) {
+        if (pt.table[i] < 0 || pt.table[i] >= pt.n_pages) {
+            set_error(MLQ_ERR_ARG, "%s: logical page %d unmapped or outside the pool (%d)", who, i, pt.table[i]);
+            return MLQ_ERR_ARG;
+        }
+    }
+    if (len == 0) return MLQ_OK;
+    CallScope cs;
+    const int *dt = (const int *)cs.in(pt.table, sizeof(int) * (size_t)used);
+    float *dp = to_pool ? (float *)cs.in(packed, sizeof(float) * 2 * (size_t)L * len * row)
+                        : (float *)cs.out(packed, sizeof(float) * 2 * (size_t)L * len * row);
+    if (cs.failed) return cs.finish();
+    const long long n = (long long)len * row;
+    const unsigned gx = (unsigned)std::min<long long>((n + 255) / 256, 1024);
+    k_kv_pack<<<dim3(gx, L, 2), 256, 0, stream()>>>(pt.pages, dt, dp, L, pt.n_pages, pt.page_size, row, len, to_pool);
+    count_launch();
+    if (!MLQ_CUDA(cudaGetLastError())) { cs.failed = true; cs.finish(); return MLQ_ERR_CUDA; }
+    return cs.finish();
+}
+
+// Positions [0, len) of every layer's K and V rows out of a KVBlock's page pool, packed as
+// [2][L][len][nkh*hd] floats at dst (device or host), following its page table.
+int mlq_kv_snapshot(const MlqKVBlock *kv, int len, float *dst) {
+    if (!kv || !dst || len < 0 || !kv->pt.pages || !kv->pt.table || len > kv->seq_len[0] ||
+        len > kMaxBlocks * kv->pt.page_size) {
+        set_error(MLQ_ERR_ARG, "mlq_kv_snapshot: bad block, destination or length (len <= seq_len)");
+        return MLQ_ERR_ARG;
+    }
+    return kv_pack(const_cast<MlqKVBlock *>(kv), len, dst, 0, "mlq_kv_snapshot");
+}
+
+// The reverse: maps a page (from the block's free list) to every logical page of [0, len)
+// that has none, copies src [2][L][len][nkh*hd] into those positions and sets seq_len to
+// len.  The block then continues at position len as if it had run those tokens itself.
+int mlq_kv_restore(MlqKVBlock *kv, int len, const float *src) {
+    if (!kv || !src || len < 0 || !kv->pt.pages || !kv->pt.table || len > kMaxBlocks * kv->pt.page_size) {
+        set_error(MLQ_ERR_ARG, "mlq_kv_restore: bad block, source or length");
+        return MLQ_ERR_ARG;
+    }
+    const int used = (len + kv->pt.page_size - 1) / kv->pt.page_size;
+    for (int i = 0; i < used; i++) {
+        if (kv->pt.table[i] < 0) {
+            const int page = mlq_page_table_alloc(&kv->pt);
+            if (page < 0) {
+                set_error(MLQ_ERR_CAPACITY, "mlq_kv_restore: page pool full at logical page %d", i);
+                return MLQ_ERR_CAPACITY;
+            }
+            kv->pt.table[i] = page;
+        }
+    }
+    const int rc = kv_pack(kv, len, const_cast<float *>(src), 1, "mlq_kv_restore");
+    if (rc == MLQ_OK) kv->seq_len[0] = len;
+    return rc;
 }
 
 size_t mlq_sizeof_page_table(void) { return sizeof(MlqPageTable); }
