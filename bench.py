@@ -411,6 +411,9 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_decode and world == 1:
         line["decode"] = run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                     cpu_seconds=args.cpu_seconds, with_parity=not args.no_parity)
+    if not args.no_qwen3moe and world == 1:
+        line["qwen3moe"] = run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
+                                        cpu_seconds=args.cpu_seconds)
     if not args.no_moe_ep:
         line["moe_ep"] = run_moe_ep(torch, lib, rank, world)
     print(json.dumps(line), flush=True)
@@ -551,6 +554,296 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
             "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite,
             "parity": parity,
             "host_issue_ms_per_step": round(host_ms, 3)}
+
+
+# ------------------------------------------------------------------------------ config-3 whole model
+# Qwen3-30B-A3B shape in Q4_K_M through batch_forward: 48 layers, d_model 2048, 32 / 4 heads
+# of 128, 128 experts top-8 (FF 768; gate/up Q4_K, down Q6_K), router F32, attention Q4_K
+# with V in Q6_K, output head 151936 x 2048 Q6_K, vocab 151936.  Prompt 128 tokens, then
+# 64 decode steps, B = 1 and 16.  The batch engine's step (cengine_batch_instr.c:1233-1493)
+# has no QK-RMSNorm and routes with moe_ffn's rule (no renormalisation); neither changes
+# the bytes a step reads.  Synthetic weights: random K-quant blocks with small fp16 scales
+# (finite, bounded values), router N(0, 1/N) so that its logits are ~N(0, 1).
+Q3 = dict(L=48, N=2048, NH=32, NKH=4, HD=128, V=151936, E=128, k=8, M=768, eps=1e-6, prompt=128, gen=64)
+
+
+def _kq_bytes(qt, rows, cols):
+    be, bb = {12: (256, 144), 14: (256, 210), 8: (32, 34)}[qt]
+    return rows * cols // be * bb
+
+
+def qwen3moe_step_bytes(B, pos):
+    """Algorithmic HBM bytes of one decode step: attention and router weights of every
+    layer, the experts the step's tokens select (expected number of distinct experts under
+    near-uniform routing, E (1 - (1 - k/E)^B)), the head, the embedding rows and the K/V rows
+    read and written."""
+    c = Q3
+    N, inner, kv = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"]
+    attn = _kq_bytes(12, inner, N) + _kq_bytes(12, kv, N) + _kq_bytes(14, kv, N) + _kq_bytes(12, N, inner)
+    router = c["E"] * N * 4
+    expert = 2 * _kq_bytes(12, c["M"], N) + _kq_bytes(14, N, c["M"])
+    distinct = c["E"] * (1 - (1 - c["k"] / c["E"]) ** B)
+    head = _kq_bytes(14, c["V"], N)
+    kv_bytes = B * c["L"] * 2 * kv * 4 * (pos + 2)
+    return int(c["L"] * (attn + router + distinct * expert) + head + kv_bytes + B * (N * 4 + c["V"] * 4)), distinct
+
+
+def build_qwen3moe(torch, lib, layers=None):
+    from mojollama_b200 import bc as BCm
+    c = Q3
+    L, N, NH, NKH, HD, V, E, M = layers or c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["V"], c["E"], c["M"]
+    inner, kv = NH * HD, NKH * HD
+    g = torch.Generator(device="cuda").manual_seed(3)
+    keep = []
+
+    def kq(qt, rows, cols):
+        t = _random_kquant(torch, qt, rows * cols // 256, g)
+        keep.append(t)
+        return t.data_ptr()
+
+    b = BCm.BCBuilder()
+    bc = b.bc
+    bc.L, bc.N, bc.NH, bc.NKH, bc.HD, bc.FF, bc.V, bc.eps, bc.nc = L, N, NH, NKH, HD, 0, V, c["eps"], N
+    for nm, qt, r, k in (("wQ", 12, inner, N), ("wK", 12, kv, N), ("wV", 14, kv, N), ("wO", 12, N, inner)):
+        b.layers(nm, [kq(qt, r, k) for _ in range(L)])
+    for f, v in (("nQ", inner), ("nK", kv), ("nV", kv), ("nO", N)):
+        b.ints(f, [v] * L)
+    for f, v in (("q_quant", 12), ("k_quant", 12), ("v_quant", 14), ("o_quant", 12)):
+        b.ints(f, [v] * L)
+    ones = torch.ones(N, device="cuda")
+    keep.append(ones)
+    b.layers("wAN", [ones.data_ptr()] * L)
+    b.layers("wFN", [ones.data_ptr()] * L)
+    routers = [torch.randn(E * N, generator=g, device="cuda") * (1.0 / np.sqrt(N)) for _ in range(L)]
+    keep.extend(routers)
+    b.layers("w_gate_inp", [r.data_ptr() for r in routers])
+    b.layers("w_gate_exps", [kq(12, E * M, N) for _ in range(L)])
+    b.layers("w_up_exps", [kq(12, E * M, N) for _ in range(L)])
+    b.layers("w_down_exps", [kq(14, E * N, M) for _ in range(L)])
+    bc.n_experts, bc.n_experts_per_tok, bc.moe_intermediate = E, c["k"], M
+    bc.gate_exp_quant, bc.up_exp_quant, bc.down_exp_quant = 12, 12, 14
+    emb = torch.randn(V * N, generator=g, device="cuda") * 0.02
+    keep.append(emb)
+    bc.emb, bc.emb_quant = emb.data_ptr(), 0
+    bc.onw = ones.data_ptr()
+    bc.wOut = kq(14, V, N)
+    bc.outNR, bc.outNC, bc.outQuant = V, N, 14
+    max_ctx = c["prompt"] + c["gen"] + 8
+    j = np.arange(HD // 2)
+    theta = np.arange(max_ctx)[:, None] / np.power(1e6, 2.0 * j / HD)   # rope_freq_base 1e6 (Qwen3)
+    b.ptr("cos_table", np.cos(theta).astype(np.float32))
+    b.ptr("sin_table", np.sin(theta).astype(np.float32))
+    bc.max_ctx, bc.rope_dim = max_ctx, HD
+    torch.cuda.synchronize()
+    return b, keep
+
+
+def run_qwen3moe(torch, lib, stream, with_cpu=True, cpu_seconds=10.0):
+    """Config 3 decode through the library's batch_forward with on-device greedy sampling
+    (mlq_batch_forward_sample: tokens never leave the device), per batch size: tok/s,
+    bytes per step and achieved bandwidth, and end to end through the reference-named
+    batch_forward of cengine_batch_instr.so with host tokens and host logits."""
+    from mojollama_b200.serving import PagedKV
+    from mojollama_b200.kernels import load_kernels
+    c = Q3
+    V, P, G = c["V"], c["prompt"], c["gen"]
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    prev = lib.mlq_get_stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    b, keep = build_qwen3moe(torch, lib)
+    lib.mlq_set_stream(ctypes.c_void_p(prev))
+    ce = load_kernels().cengine
+    out = {"workload": "Qwen3-30B-A3B shape, Q4_K_M (Q4_K + Q6_K attn_v / ffn_down / output), 48 layers, "
+                       "128 experts top-8, 128-token prompt then 64 greedy decode steps, through batch_forward "
+                       "(config 3)", "batches": {}}
+    for B in (1, 16):
+        kvs = [PagedKV(c["L"], c["NKH"], c["HD"], 64, (P + G) // 64 + 2) for _ in range(B)]
+        b.kv_array([k.block for k in kvs])
+        d_logits = torch.empty(B * V, device="cuda")
+        b.bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        prompts = torch.from_numpy(np.random.default_rng(B).integers(0, V, (P, B)).astype(np.int32)).cuda()
+        d_tok = torch.empty(B, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+
+        def fwd_sample(t):
+            rc = lib.mlq_batch_forward_sample(ctypes.byref(b.bc), ctypes.c_void_p(d_tok.data_ptr()), B, None,
+                                              ctypes.c_float(0.0), 0, t, ctypes.c_void_p(d_tok.data_ptr()))
+            if rc:
+                raise RuntimeError(lib.mlq_last_error_message())
+
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with torch.cuda.stream(stream):
+            evs[0].record(stream)
+            for t in range(P):
+                d_tok.copy_(prompts[t])
+                fwd_sample(t)
+            evs[1].record(stream)
+            l0 = lib.mlq_launch_count()
+            for t in range(G):
+                fwd_sample(P + t)       # the sampled tokens feed the next step in place
+            evs[2].record(stream)
+        stream.synchronize()
+        launches = (lib.mlq_launch_count() - l0) // G
+        pre_ms, dec_ms = evs[0].elapsed_time(evs[1]), evs[1].elapsed_time(evs[2])
+        sb = [qwen3moe_step_bytes(B, P + t) for t in range(G)]
+        step_bytes = sum(x[0] for x in sb) / G
+        ms = dec_ms / G
+        # end to end: the reference's call shape (host tokens, host logits), 8 steps
+        for k in kvs:
+            k.block.seq_len[0] = P     # continue from the prompt (the positions already hold K/V rows)
+        h_logits = np.zeros(B * V, np.float32)
+        b.bc.logits = h_logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        tok = np.zeros(B, np.int32)
+        n_e2e = 8
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            ce.batch_forward(ctypes.byref(b.bc), tok.ctypes.data, B, None)
+            tok = np.argmax(h_logits.reshape(B, V), axis=1).astype(np.int32)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+        assert lib.mlq_last_error() == 0, lib.mlq_last_error_message()
+        achieved = step_bytes / (ms / 1e3) / 1e9
+        out["batches"][str(B)] = {
+            "tok_s": round(B * G / (dec_ms / 1e3), 1), "ms_per_step": round(ms, 3),
+            "prefill_tok_s": round(B * P / (pre_ms / 1e3), 1), "launches_per_step": int(launches),
+            "e2e_tok_s": round(B / (e2e_ms / 1e3), 1), "e2e_ms_per_step": round(e2e_ms, 3),
+            "e2e_io": {"h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * V * 4},
+            "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                         "expected_distinct_experts_per_layer": round(sb[0][1], 1),
+                         "achieved_gbs": round(achieved, 1), "peak": hbm, "frac": round(achieved / hbm, 4)}}
+        for k in kvs:
+            k.free()
+        del d_logits
+    if with_cpu:
+        out["cpu_baseline"] = qwen3moe_cpu_baseline(torch, b, keep, cpu_seconds)
+    del keep
+    torch.cuda.empty_cache()
+    return out
+
+
+def qwen3moe_cpu_baseline(torch, b, keep, seconds):
+    """The reference C engine's ops for one config-3 decode token on the host cores, the way
+    TurboEngineV7MoE.forward composes them (turbo_engine_v7_moe.py:1540-2120): per layer
+    quant_matmul_omp for q / k / v / o, the F32 router (f32_matmul_omp) and moe_forward_omp
+    over the 8 selected experts; the output head is the reference's Q8_0 requantization of
+    the Q6_K head (turbo_engine_v7_moe.py:515-518) through quant_matmul_omp.  One layer is
+    timed and counted 48 times (the layers are the same work); attention over a 128-token
+    context and the norms are left out (small next to the weight streaming)."""
+    try:
+        from oracle import ref as R
+        if not R.available():
+            return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+        eng = R.RefEngine()
+        threads = os.cpu_count() or 1
+        eng.set_num_threads(threads)
+        c = Q3
+        N, inner, kv, E, M, V = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"], c["E"], c["M"], c["V"]
+        src = b.bc
+
+        def host(ptr, nbytes):
+            t = next(k for k in keep if k.data_ptr() <= ptr < k.data_ptr() + k.numel() * k.element_size())
+            off = ptr - t.data_ptr()
+            return t.view(-1).view(torch.uint8)[off:off + nbytes].cpu().numpy().copy()
+
+        wq, wk = host(src.wQ[0], _kq_bytes(12, inner, N)), host(src.wK[0], _kq_bytes(12, kv, N))
+        wv, wo = host(src.wV[0], _kq_bytes(14, kv, N)), host(src.wO[0], _kq_bytes(12, N, inner))
+        router = host(src.w_gate_inp[0], E * N * 4).view(np.float32)
+        ge = host(src.w_gate_exps[0], _kq_bytes(12, E * M, N))
+        ue = host(src.w_up_exps[0], _kq_bytes(12, E * M, N))
+        de = host(src.w_down_exps[0], _kq_bytes(14, E * N, M))
+        head = np.ascontiguousarray(np.tile(host(src.wOut, _kq_bytes(8, 4096, N)), V // 4096 + 1)[: _kq_bytes(8, V, N)])
+        x = np.random.default_rng(0).standard_normal(N).astype(np.float32)
+        xa = np.random.default_rng(1).standard_normal(inner).astype(np.float32)
+        q, k_, v_, o = (np.zeros(n, np.float32) for n in (inner, kv, kv, N))
+        lg, comb = np.zeros(E, np.float32), np.zeros(N, np.float32)
+        logits = np.zeros(V, np.float32)
+        sel = np.arange(0, E, E // c["k"], dtype=np.int32)[: c["k"]]
+        wts = np.full(c["k"], 1.0 / c["k"], np.float32)
+        cu = ctypes.POINTER(ctypes.c_uint8)
+        gs, us, ds = _kq_bytes(12, M, N), _kq_bytes(12, M, N), _kq_bytes(14, N, M)
+        gp = (cu * E)(*[ctypes.cast(ge.ctypes.data + e * gs, cu) for e in range(E)])
+        up = (cu * E)(*[ctypes.cast(ue.ctypes.data + e * us, cu) for e in range(E)])
+        dp = (cu * E)(*[ctypes.cast(de.ctypes.data + e * ds, cu) for e in range(E)])
+        pre = np.zeros(3 * c["k"] * M, np.float32)   # moe_forward_omp's 3 x top_k x n_ff scratch
+        pre_q8 = np.zeros(M // 32 * 34 + N // 32 * 34, np.uint8)
+
+        def layer():
+            eng.so.quant_matmul_omp(R.uptr(wq), R.fptr(x), R.fptr(q), inner, N, 12)
+            eng.so.quant_matmul_omp(R.uptr(wk), R.fptr(x), R.fptr(k_), kv, N, 12)
+            eng.so.quant_matmul_omp(R.uptr(wv), R.fptr(x), R.fptr(v_), kv, N, 14)
+            eng.so.quant_matmul_omp(R.uptr(wo), R.fptr(xa), R.fptr(o), N, inner, 12)
+            eng.so.f32_matmul_omp(R.fptr(router), R.fptr(x), R.fptr(lg), E, N)
+            eng.so.moe_forward_omp(gp, up, dp, R.fptr(x), M, N, 12, 12, 14, sel.ctypes.data_as(ctypes.POINTER(ctypes.c_int)),
+                                   R.fptr(wts), c["k"], R.fptr(comb), R.fptr(pre), R.uptr(pre_q8))
+
+        layer()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 2 or n < 3:
+            layer()
+            n += 1
+        t_layer = (time.perf_counter() - t0) / n
+        eng.so.quant_matmul_omp(R.uptr(head), R.fptr(x), R.fptr(logits), V, N, 8)
+        m, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 4 or m < 2:
+            eng.so.quant_matmul_omp(R.uptr(head), R.fptr(x), R.fptr(logits), V, N, 8)
+            m += 1
+        t_head = (time.perf_counter() - t0) / m
+        t_tok = c["L"] * t_layer + t_head
+        return {"value": round(1.0 / t_tok, 2), "unit": "tok/s", "cores": threads, "kind": "reference",
+                "sample": f"{n} timings of one layer's reference C ops (4 quant_matmul_omp, f32_matmul_omp router, "
+                          f"moe_forward_omp over 8 experts) x 48 + {m} timings of the Q8_0 head, B=1",
+                "ms_per_layer": round(t_layer * 1e3, 3), "ms_head": round(t_head * 1e3, 3)}
+    except Exception as e:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": f"failed: {e}"}
+
+
+def run_qwen3moe_profile(args):
+    """Small case for an ncu launch list of config-3 decode steps: `--profile-steps` layers,
+    a 4-token prompt, then 2 decode steps at B = 1 and 2 at B = 16 (weights ~1.9 GB)."""
+    import torch
+    from mojollama_b200 import core
+    from mojollama_b200.serving import PagedKV
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    b, keep = build_qwen3moe(torch, lib, layers=args.profile_steps)
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    V = Q3["V"]
+    for B in (1, 16):
+        kvs = [PagedKV(args.profile_steps, Q3["NKH"], Q3["HD"], 64, 2) for _ in range(B)]
+        b.kv_array([k.block for k in kvs])
+        d_logits = torch.empty(B * V, device="cuda")
+        b.bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        d_tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for t in range(6):
+                rc = lib.mlq_batch_forward_sample(ctypes.byref(b.bc), ctypes.c_void_p(d_tok.data_ptr()), B, None,
+                                                  ctypes.c_float(0.0), 0, t, ctypes.c_void_p(d_tok.data_ptr()))
+                assert rc == 0, lib.mlq_last_error_message()
+        stream.synchronize()
+        for k in kvs:
+            k.free()
+    print(json.dumps({"qwen3moe_profile_layers": args.profile_steps}))
+    return 0
+
+
+def run_qwen3moe_only(args):
+    import torch
+    from mojollama_b200 import core
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    print(json.dumps({"qwen3moe": run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
+                                               cpu_seconds=args.cpu_seconds)}), flush=True)
+    return 0
 
 
 SWEEP_SHAPES = [(2048, 2048), (5632, 2048), (2880, 2880), (151936, 2048)]
@@ -1040,6 +1333,9 @@ def main():
     ap.add_argument("--decode-profile", action="store_true", help="small decode case for an ncu launch list")
     ap.add_argument("--no-moe-ep", action="store_true", help="skip the config-3 expert-parallel MoE section")
     ap.add_argument("--moe-ep-only", action="store_true", help="run only the expert-parallel MoE section")
+    ap.add_argument("--qwen3moe-only", action="store_true", help="run only the config-3 whole-model section")
+    ap.add_argument("--no-qwen3moe", action="store_true", help="skip the config-3 whole-model section")
+    ap.add_argument("--qwen3moe-profile", action="store_true", help="small config-3 case for an ncu launch list")
     ap.add_argument("--moe-layers", type=int, default=None)
     ap.add_argument("--moe-tokens", type=int, default=16)
     ap.add_argument("--moe-steps", type=int, default=5)
@@ -1061,6 +1357,10 @@ def main():
         return run_decode_profile(args)
     if args.moe_ep_only:
         return run_moe_ep_only(args, rank, world, local_rank)
+    if args.qwen3moe_only:
+        return run_qwen3moe_only(args)
+    if args.qwen3moe_profile:
+        return run_qwen3moe_profile(args)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":

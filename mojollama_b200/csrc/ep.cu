@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
@@ -91,12 +92,120 @@ __global__ void k_ep_gather(const float *__restrict__ x, const int *__restrict__
 // out[t] = residual[t] + sum_i w[t][i] * y[pos[t*k + i]]   (i in order)
 __global__ void k_ep_combine(const float *__restrict__ y, const int *__restrict__ pos, const float *__restrict__ w,
                              int k, int N, const float *__restrict__ residual, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
         float acc = residual ? residual[(size_t)t * N + c] : 0.0f;
-        for (int i = 0; i < k; i++) acc = fmaf(w[t * k + i], y[(size_t)pos[t * k + i] * N + c], acc);
+        for (int i = 0; i < k; i++) {
+            const int r = pos ? pos[t * k + i] : t * k + i;
+            acc = fmaf(w[t * k + i], y[(size_t)r * N + c], acc);
+        }
         out[(size_t)t * N + c] = acc;
     }
+}
+
+int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
+                      float *out, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    count_launch();
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_ep_combine, y, pos, w, k, N, residual, out)) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ grouped routed experts
+static void moe_grouped_tiles(int gqt, int uqt, int dqt, int n_ff, int N, int tiles[3], int &n_lists) {
+    const int tg = grouped_tiles_per_expert(gqt, n_ff, N), tu = grouped_tiles_per_expert(uqt, n_ff, N);
+    const int td = grouped_tiles_per_expert(dqt, N, n_ff);
+    const bool pair = gqt == uqt;   // one type: one tiling, gate and up in one launch
+    tiles[0] = pair ? tg + tu : tg;
+    tiles[1] = pair ? td : tu;
+    tiles[2] = td;
+    n_lists = pair ? 2 : 3;
+}
+
+static size_t moe_grouped_layout(MoeGroupedScratch *m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E,
+                                 int n_ff, int N) {
+    size_t o = 0;
+    auto take = [&](size_t bytes) -> uint8_t * {
+        uint8_t *p = base ? base + o : nullptr;
+        o += (bytes + 255) & ~(size_t)255;
+        return p;
+    };
+    int tiles[3], n_lists;
+    moe_grouped_tiles(gqt, uqt, dqt, n_ff, N, tiles, n_lists);
+    const int chunks = (R + 7) / 8 + (E < R ? E : R);
+    MoeGroupedScratch t{};
+    t.spos = (int *)take(sizeof(int) * (size_t)R);
+    t.srow = (int *)take(sizeof(int) * (size_t)R);
+    t.nitem = (int *)take(sizeof(int) * 4);
+    for (int l = 0; l < 3; l++) t.items[l] = l < n_lists ? take(16 * (size_t)chunks * tiles[l]) : nullptr;
+    t.px = take(grouped_packed_bytes(R, N));
+    t.ph = take(grouped_packed_bytes(R, n_ff));
+    t.g = (float *)take(sizeof(float) * (size_t)R * n_ff);
+    t.u = (float *)take(sizeof(float) * (size_t)R * n_ff);
+    if (m) *m = t;
+    return o;
+}
+
+size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_ff, int N) {
+    return moe_grouped_layout(nullptr, nullptr, gqt, uqt, dqt, R, E, n_ff, N);
+}
+
+void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff,
+                       int N) {
+    moe_grouped_layout(&m, base, gqt, uqt, dqt, R, E, n_ff, N);
+}
+
+int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
+                       long long gstride, long long ustride, long long dstride, int E, const int *eid, int R,
+                       int row_div, int n_ff, int N, const float *x, float *y, float clamp, const MoeGroupedScratch &m,
+                       cudaStream_t s) {
+    if (R <= 0) return MLQ_OK;
+    int tiles[3], n_lists;
+    moe_grouped_tiles(gqt, uqt, dqt, n_ff, N, tiles, n_lists);
+    if (!tiles[0] || !tiles[1] || !tiles[2]) {
+        set_error(MLQ_ERR_UNSUPPORTED, "grouped experts: types %d/%d/%d with %d x %d", gqt, uqt, dqt, n_ff, N);
+        return MLQ_ERR_UNSUPPORTED;
+    }
+    const bool pair = gqt == uqt;
+    const int chunks = (R + 7) / 8 + (E < R ? E : R);
+    void *items[3] = {m.items[0], m.items[1], m.items[2]};
+    int rc = launch_group_plan(eid, R, E, n_lists, items, tiles, m.spos, m.srow, m.nitem, s);
+    if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, m.srow, R, N, m.px, s, row_div);
+    GroupedCall gc{};
+    gc.planes = m.px;
+    gc.n_rows = n_ff;
+    gc.K = N;
+    if (rc == MLQ_OK) {
+        gc.qt = gqt; gc.W = gexp; gc.estride = gstride; gc.out = m.g;
+        gc.items = items[0]; gc.n_items_dev = m.nitem; gc.n_items_bound = chunks * tiles[0];
+        if (pair) { gc.W2 = uexp; gc.estride2 = ustride; gc.out2 = m.u; }
+        rc = launch_grouped(gc, s);
+    }
+    if (rc == MLQ_OK && !pair) {
+        gc.qt = uqt; gc.W = uexp; gc.estride = ustride; gc.out = m.u;
+        gc.items = items[1]; gc.n_items_dev = m.nitem + 1; gc.n_items_bound = chunks * tiles[1];
+        rc = launch_grouped(gc, s);
+    }
+    if (rc == MLQ_OK) rc = launch_encode_packed(m.g, m.u, nullptr, R, n_ff, m.ph, s, 1, clamp);
+    if (rc == MLQ_OK) {
+        GroupedCall dc{};
+        dc.qt = dqt; dc.W = dexp; dc.estride = dstride; dc.out = y;
+        dc.items = items[n_lists - 1]; dc.n_items_dev = m.nitem + n_lists - 1; dc.n_items_bound = chunks * tiles[n_lists - 1];
+        dc.planes = m.ph; dc.out_rows = m.srow;
+        dc.n_rows = N;
+        dc.K = n_ff;
+        rc = launch_grouped(dc, s);
+    }
+    return rc;
 }
 
 }  // namespace mlq
@@ -130,10 +239,7 @@ int mlq_ep_combine(const float *recv_y, const int *pos, const float *w, int T, i
         set_error(MLQ_ERR_ARG, "ep_combine: bad arguments");
         return MLQ_ERR_ARG;
     }
-    cudaStream_t s = stream();
-    k_ep_combine<<<T, 256, 0, s>>>(recv_y, pos, w, k, N, residual, out);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return launch_ep_combine(recv_y, pos, w, T, k, N, residual, out, stream());
 }
 
 // y[r] = down_e(silu(clamp(gate_e x_r, +-80)) * up_e x_r) for the local expert e = eid[r]
@@ -152,55 +258,18 @@ int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, 
         return MLQ_ERR_ARG;
     }
     if (R == 0) return MLQ_OK;
-    const int tg = grouped_tiles_per_expert(gqt, n_ff, N), tu = grouped_tiles_per_expert(uqt, n_ff, N);
-    const int td = grouped_tiles_per_expert(dqt, N, n_ff);
-    if (!tg || !tu || !td) {
+    if (!grouped_tiles_per_expert(gqt, n_ff, N) || !grouped_tiles_per_expert(uqt, n_ff, N) ||
+        !grouped_tiles_per_expert(dqt, N, n_ff)) {
         set_error(MLQ_ERR_TYPE, "moe_rows: expert types %d/%d/%d", gqt, uqt, dqt);
         return MLQ_ERR_TYPE;
     }
-    const int chunks = (R + 7) / 8 + (n_experts < R ? n_experts : R);
-    const bool pair = gqt == uqt;   // one type: one tiling, gate and up in one launch
     CallScope cs;
-    int *spos = (int *)cs.scratch(sizeof(int) * (size_t)R);
-    int *srow = (int *)cs.scratch(sizeof(int) * (size_t)R);
-    int *nitem = (int *)cs.scratch(sizeof(int) * 4);
-    const int tiles[3] = {pair ? tg + tu : tg, pair ? td : tu, td};
-    const int n_lists = pair ? 2 : 3;
-    void *items[3] = {nullptr, nullptr, nullptr};
-    for (int l = 0; l < n_lists; l++) items[l] = cs.scratch(16 * (size_t)chunks * tiles[l]);
-    uint8_t *px = (uint8_t *)cs.scratch(grouped_packed_bytes(R, N));
-    uint8_t *ph = (uint8_t *)cs.scratch(grouped_packed_bytes(R, n_ff));
-    float *g = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
-    float *u = (float *)cs.scratch(sizeof(float) * (size_t)R * n_ff);
+    uint8_t *scr = (uint8_t *)cs.scratch(moe_grouped_scratch_bytes(gqt, uqt, dqt, R, n_experts, n_ff, N));
     if (cs.failed) return cs.finish();
-    cudaStream_t s = stream();
-    int rc = launch_group_plan(eid, R, n_experts, n_lists, items, tiles, spos, srow, nitem, s);
-    if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, srow, R, N, px, s);
-    GroupedCall gc{};
-    gc.planes = px;
-    gc.n_rows = n_ff;
-    gc.K = N;
-    if (rc == MLQ_OK) {
-        gc.qt = gqt; gc.W = (const uint8_t *)gexp; gc.estride = gstride; gc.out = g;
-        gc.items = items[0]; gc.n_items_dev = nitem; gc.n_items_bound = chunks * tiles[0];
-        if (pair) { gc.W2 = (const uint8_t *)uexp; gc.estride2 = ustride; gc.out2 = u; }
-        rc = launch_grouped(gc, s);
-    }
-    if (rc == MLQ_OK && !pair) {
-        gc.qt = uqt; gc.W = (const uint8_t *)uexp; gc.estride = ustride; gc.out = u;
-        gc.items = items[1]; gc.n_items_dev = nitem + 1; gc.n_items_bound = chunks * tiles[1];
-        rc = launch_grouped(gc, s);
-    }
-    if (rc == MLQ_OK) rc = launch_encode_packed(g, u, nullptr, R, n_ff, ph, s);
-    if (rc == MLQ_OK) {
-        GroupedCall dc{};
-        dc.qt = dqt; dc.W = (const uint8_t *)dexp; dc.estride = dstride; dc.out = y;
-        dc.items = items[n_lists - 1]; dc.n_items_dev = nitem + n_lists - 1; dc.n_items_bound = chunks * td;
-        dc.planes = ph; dc.out_rows = srow;
-        dc.n_rows = N;
-        dc.K = n_ff;
-        rc = launch_grouped(dc, s);
-    }
+    MoeGroupedScratch m;
+    moe_grouped_carve(m, scr, gqt, uqt, dqt, R, n_experts, n_ff, N);
+    int rc = launch_moe_grouped(gqt, uqt, dqt, (const uint8_t *)gexp, (const uint8_t *)uexp, (const uint8_t *)dexp,
+                                gstride, ustride, dstride, n_experts, eid, R, 1, n_ff, N, x, y, 80.0f, m, stream());
     if (rc != MLQ_OK) {
         cs.failed = true;
         cs.finish();

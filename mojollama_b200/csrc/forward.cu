@@ -346,7 +346,15 @@ static int fwd_fail(CallScope &cs, int rc) {
 struct StepDims {
     int B, N, inner, kvrow, FF, E, topk, M, outNR, NH, HD, L;
     bool ssm;
+    int gq = 0, uq = 0, dq = 0;   // routed expert types (grouped expert scratch)
 };
+
+// routed experts run through the grouped expert GEMV when its tilings cover their types
+static bool moe_grouped_ok(const StepDims &d) {
+    return d.E > 0 && d.topk > 0 && d.M > 0 && d.N % 32 == 0 && d.M % 32 == 0 && d.E <= 1024 &&
+           grouped_tiles_per_expert(d.gq, d.M, d.N) && grouped_tiles_per_expert(d.uq, d.M, d.N) &&
+           grouped_tiles_per_expert(d.dq, d.N, d.M) && !getenv("MLQ_NO_GROUPED_MOE");
+}
 
 // Device buffers of one decode step.  The head (pos, len, KV pointer arrays, page tables)
 // is one contiguous block so the per-step host inputs go up in one copy.
@@ -362,6 +370,8 @@ struct StepBufs {
           *logits = nullptr, *state = nullptr;
     uint8_t *px = nullptr, *pa = nullptr, *ph = nullptr;   // packed activation rows (decode GEMV inputs)
     size_t attn_sb = 0;
+    MoeGroupedScratch moe{};   // grouped routed experts (when moe_grouped_ok)
+    float *y_moe = nullptr;    // [B * topk][N] expert outputs before the weighted combine
 };
 
 static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -421,6 +431,12 @@ static size_t carve(StepBufs &b, uint8_t *base, const StepDims &d) {
     b.px = take(packed_rows_bytes(d.B, d.N));
     b.pa = take(packed_rows_bytes(d.B, d.inner));
     b.ph = take(packed_rows_bytes(d.B, wide));
+    if (moe_grouped_ok(d)) {
+        const int R = d.B * d.topk;
+        uint8_t *m = take(moe_grouped_scratch_bytes(d.gq, d.uq, d.dq, R, d.E, d.M, d.N));
+        if (m) moe_grouped_carve(b.moe, m, d.gq, d.uq, d.dq, R, d.E, d.M, d.N);
+        b.y_moe = (float *)take((size_t)R * d.N * 4);
+    }
     return o;
 }
 
@@ -601,9 +617,18 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
             const int E = c->n_experts;
             MLQ_TRY(launch_matmul((const uint8_t *)lp.router, MLQ_F32, pin, sb.logits_e, E, N, B, 0, s));
             MLQ_TRY(launch_router_topk(sb.logits_e, B, E, topk, 0, sb.e_idx, sb.e_w, s));
-            MLQ_TRY(launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
-                                       lp.dexp, lp.gstride, lp.ustride, lp.dstride, sb.e_idx, sb.e_w, topk, B, M, N,
-                                       pin, sb.hm, sb.hm2, x, res, inf, s));
+            if (sb.y_moe) {
+                // every active expert streamed once for all of its (token, slot) rows, then
+                // x = res + sum_i w_i y_i in slot order
+                MLQ_TRY(launch_moe_grouped(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
+                                           lp.dexp, lp.gstride, lp.ustride, lp.dstride, E, sb.e_idx, B * topk, topk,
+                                           M, N, pin, sb.y_moe, inf, sb.moe, s));
+                MLQ_TRY(launch_ep_combine(sb.y_moe, nullptr, sb.e_w, B, topk, N, res, x, s));
+            } else {
+                MLQ_TRY(launch_moe_experts(c->gate_exp_quant, c->up_exp_quant, c->down_exp_quant, lp.gexp, lp.uexp,
+                                           lp.dexp, lp.gstride, lp.ustride, lp.dstride, sb.e_idx, sb.e_w, topk, B, M,
+                                           N, pin, sb.hm, sb.hm2, x, res, inf, s));
+            }
             if (lp.shg && lp.shrouter) {
                 k_dot_rows<<<B, 256, 0, s>>>(pin, lp.shrouter, sb.score, N);
                 count_launch();
@@ -922,6 +947,9 @@ int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws) {
     }
     StepDims d{B, N, inner, kvrow, c->FF, c->n_experts, c->n_experts_per_tok, c->moe_intermediate, c->outNR, NH, HD,
                L, any_ssm};
+    d.gq = c->gate_exp_quant;
+    d.uq = c->up_exp_quant;
+    d.dq = c->down_exp_quant;
     const int tab_w = max_blocks_used(pos, kv0->pt.page_size);
     const float *ws_xn = compat ? ws + (size_t)B * S : nullptr;
     const bool graphable = graphs_enabled() && !(c->emb_quant == MLQ_Q4_K && !compat) && capturable(s);

@@ -1194,11 +1194,15 @@ struct GroupRows {
     const float *x, *x2;
     const int *rows;
     int K;
+    int row_div;      // source row = rows[p] / row_div (several rows reading one token's activations)
+    float clamp;      // silu(clamp(x, +-clamp)) * x2 when x2 is set (HUGE_VALF: no clamp)
     __device__ __forceinline__ float operator()(int p, int k) const {
-        const size_t o = (size_t)(rows ? __ldg(rows + p) : p) * K + k;
+        int r = rows ? __ldg(rows + p) : p;
+        if (row_div > 1) r /= row_div;
+        const size_t o = (size_t)r * K + k;
         float v = __ldg(x + o);
         if (x2) {
-            const float g = fminf(fmaxf(v, -80.0f), 80.0f);
+            const float g = fminf(fmaxf(v, -clamp), clamp);
             v = (g / (1.0f + expf(-g))) * __ldg(x2 + o);
         }
         return v;
@@ -1467,11 +1471,12 @@ int launch_grouped(const GroupedCall &gc, cudaStream_t s) {
 }
 
 int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
-                         cudaStream_t s) {
+                         cudaStream_t s, int row_div, float clamp) {
     if (R <= 0) return MLQ_OK;
     const long long blocks = ((long long)R * (K / 32) + 7) / 8;
     count_launch();
-    return MLQ_CUDA(launch_pdl_n(k_encode_packed, dim3((unsigned)blocks), dim3(256), 0, s, GroupRows{x, x2, rows, K},
+    return MLQ_CUDA(launch_pdl_n(k_encode_packed, dim3((unsigned)blocks), dim3(256), 0, s,
+                                 GroupRows{x, x2, rows, K, row_div, clamp},
                                  R, K, planes))
                ? MLQ_OK
                : MLQ_ERR_CUDA;

@@ -188,10 +188,30 @@ struct GroupedCall {
 int grouped_tiles_per_expert(int qt, int n_rows, int K);
 size_t grouped_packed_bytes(int R, int K);
 int launch_grouped(const GroupedCall &gc, cudaStream_t s);
-// packed activation rows p < R: x[rows[p]] (rows may be null: x[p]); with x2 set,
-// silu(clamp(x[p], +-80)) * x2[p]
+// packed activation rows p < R: x[rows[p] / row_div] (rows may be null: x[p / row_div]);
+// with x2 set, silu(clamp(x, +-clamp)) * x2 of that row
 int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
-                         cudaStream_t s);
+                         cudaStream_t s, int row_div = 1, float clamp = 80.0f);
+// Routed experts of R = T * k rows (row t * k + i: token t, slot i, expert eid[row]) over
+// the grouped expert GEMV: a stable plan by expert, each active expert's gate / up / down
+// matrices streamed once for all of its rows.  x holds one row per token when row_div = k
+// (or one per row when row_div = 1); y [R][N] = down_e(silu(clamp(gate_e x)) * up_e x).
+// Scratch: MoeGroupedScratch of moe_grouped_scratch_bytes.
+struct MoeGroupedScratch {
+    int *spos, *srow, *nitem;
+    void *items[3];
+    uint8_t *px, *ph;
+    float *g, *u;
+};
+size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
+void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
+int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
+                       long long gstride, long long ustride, long long dstride, int E, const int *eid, int R,
+                       int row_div, int n_ff, int N, const float *x, float *y, float clamp, const MoeGroupedScratch &m,
+                       cudaStream_t s);
+// out[t] = residual[t] (if set) + sum_i w[t * k + i] * y[pos[t * k + i]] (pos null: identity)
+int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
+                      float *out, cudaStream_t s);
 // decode GEMV over up to 4 same-type matrices sharing packed activation rows [B <= 8]:
 // out_i = (res_i +) W_i x, or with pair (2 matrices, same rows) out_0 = silu(W_0 x) * (W_1 x);
 // MLQ_ERR_UNSUPPORTED when the shape or type does not suit it
