@@ -15,9 +15,16 @@ roofline  the dominant kernel (the format whose GEMV takes the largest share of 
           each launch timed with CUDA events inside the timed region.
 decode    config 1 (TinyLlama-1.1B shape, Q8_0, B=4) through batch_forward: tok/s device
           resident and end to end, with the reference C engine's batch_forward on the host
-          cores as its CPU baseline (N = 1 only).
+          cores as its CPU baseline (N = 1 only), and the logits of all 48 positions checked
+          against the oracle (greedy tokens where the top-2 margin exceeds 1e-2).
+qwen3moe  config 3 (Qwen3-30B-A3B shape, Q4_K_M, 48 layers, 128 experts top-8) through
+          batch_forward at B = 1 and 16: decode tok/s, bytes per step and achieved bandwidth,
+          end to end through the reference-named entry, the reference C ops on the host cores.
+hybrid    config 5 (hybrid [3 SSM + 1 GQA] x 10, 256 MXFP4 experts) through
+          qwen36_batch_forward at B = 10; N > 1: one independent replica per GPU.
 moe_ep    config 3's MoE FFN stack (48 layers, 128 experts top-8) with the experts split over
-          the N GPUs and NCCL all-to-all dispatch/combine: tok/s (weak scaling).
+          the N GPUs and NCCL all-to-all dispatch/combine: tok/s (weak scaling), with the
+          expert-parallel layer checked against the same layer on one GPU.
 cpu_baseline  the reference C engine (compiled from its own sources into oracle/_ref)
           on the host cores, on the same weights (MXFP4 re-encoded in the reference's
           own layout), with all host threads.
@@ -368,6 +375,14 @@ def run_ours(args, rank, world, local_rank):
     step_bytes = sum(alg_bytes(qt) for _, qt in FORMATS)
     value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
     e2e_value = world * step_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+    hyb = None
+    if not args.no_hybrid:
+        # config 5 as independent replicas: every rank runs its own, the slowest one counts
+        hyb = run_hybrid(torch, lib, stream, rank, world)
+        ht = torch.tensor([hyb["dec_ms"], hyb["pre_ms"]], device="cuda")
+        if world > 1:
+            dist.all_reduce(ht, op=dist.ReduceOp.MAX)
+        hyb["dec_ms"], hyb["pre_ms"] = (float(v) for v in ht.tolist())
     if rank != 0:
         if not args.no_moe_ep:
             run_moe_ep(torch, lib, rank, world)   # every rank takes part in the collectives
@@ -411,6 +426,8 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_decode and world == 1:
         line["decode"] = run_decode(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                     cpu_seconds=args.cpu_seconds, with_parity=not args.no_parity)
+    if hyb is not None:
+        line["hybrid"] = hybrid_line(hyb, world)
     if not args.no_qwen3moe and world == 1:
         line["qwen3moe"] = run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                         cpu_seconds=args.cpu_seconds)
@@ -843,6 +860,242 @@ def run_qwen3moe_only(args):
     lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
     print(json.dumps({"qwen3moe": run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                                cpu_seconds=args.cpu_seconds)}), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ config-5 whole model
+# Hybrid attention/SSM MoE (Qwen3.6-35B style) through the reference-named 76-argument
+# qwen36_batch_forward (cengine_batch_instr.c:859-1231) of cengine_batch_instr.so: 40 layers
+# in a repeating [3 SSM + 1 GQA] pattern, d_model 2048; GQA 16 / 2 heads of 256 with a fused
+# QKV projection; SSM layers as that entry point defines them (its own ssm_decode_step,
+# groups 32, state 128, inner 2048, conv 4); every layer an MoE of 256 MXFP4 experts (FF
+# 512) top-8 renormalised plus a shared expert; vocab 151936.  B = 10 sequences, 128 prompt
+# steps then 64 decode steps.  Attention / SSM projections and the head in Q8_0.  Synthetic
+# weights: random blocks with small scales.  The entry point's own semantics (one shared
+# KV slot per layer and step, cengine_batch_instr.c:1069-1072) are kept; the work per step
+# -- the weights streamed -- is that of the model.  N > 1: independent replicas per GPU.
+Q5 = dict(L=40, N=2048, NH=16, NKH=2, HD=256, V=151936, E=256, k=8, M=512, SI=512, IN=2048, G=32, S=128, DR=32,
+          eps=1e-6, B=10, prompt=128, gen=64)
+QWEN36_ARGTYPES = ([ctypes.c_int] * 10 + [ctypes.c_float] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_int] +
+                   [ctypes.c_void_p] * 39 + [ctypes.c_int] * 3 + [ctypes.c_void_p] * 14)
+
+
+def _random_blocks(torch, qt, n_blocks, gen):
+    """random Q8_0 / MXFP4 blocks on the device with small scales: Q8_0 d = 2^-12 (values
+    up to 0.031), MXFP4 e = 119 (values up to 6 * 2^-8)"""
+    bb = {8: 34, 39: 17}[qt]
+    w = torch.randint(0, 256, (n_blocks, bb), dtype=torch.uint8, device="cuda", generator=gen)
+    if qt == 8:
+        w[:, 0], w[:, 1] = 0x00, 0x0C
+    else:
+        w[:, 0] = 119
+    return w.reshape(-1)
+
+
+def hybrid_step_bytes(B):
+    c = Q5
+    N, inner, n_kv, IN = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"], c["IN"]
+    q8 = lambda r, k: r * k // 32 * 34
+    mx = lambda r, k: r * k // 32 * 17
+    attn = q8(inner + 2 * n_kv, N) + q8(N, inner)
+    ssm = q8(IN, N) + q8(N, IN)
+    expert = 2 * mx(c["M"], N) + mx(N, c["M"])
+    distinct = c["E"] * (1 - (1 - c["k"] / c["E"]) ** B)
+    moe = c["E"] * N * 4 + expert * (distinct + 1) + N * 4
+    n_attn = c["L"] // 4
+    return int(n_attn * attn + (c["L"] - n_attn) * ssm + c["L"] * moe + q8(c["V"], N)), distinct
+
+
+def build_hybrid(torch, L):
+    c = Q5
+    N, inner, n_kv, IN, E, M, SI, V = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"], c["IN"], c["E"], c["M"], c["SI"], c["V"]
+    g = torch.Generator(device="cuda").manual_seed(5)
+    keep = []
+
+    def blk(qt, rows, cols):
+        t = _random_blocks(torch, qt, rows * cols // 32, g)
+        keep.append(t)
+        return t.data_ptr()
+
+    def dev(t):
+        keep.append(t)
+        return t.data_ptr()
+
+    types = [1 if l % 4 != 3 else 0 for l in range(L)]
+    m = {"types": types, "keep": keep}
+    m["an"] = [dev(torch.ones(N, device="cuda")) for _ in range(L)]
+    m["fn"] = [dev(torch.ones(N, device="cuda")) for _ in range(L)]
+    m["qkv"] = [blk(8, inner + 2 * n_kv, N) if t == 0 else None for t in types]
+    m["o"] = [blk(8, N, inner) if t == 0 else None for t in types]
+    m["gate"] = [blk(8, IN, N) if t == 1 else None for t in types]
+    m["sout"] = [blk(8, N, IN) if t == 1 else None for t in types]
+    m["gexp"] = [blk(39, E * M, N) for _ in range(L)]
+    m["uexp"] = [blk(39, E * M, N) for _ in range(L)]
+    m["dexp"] = [blk(39, E * N, M) for _ in range(L)]
+    m["shg"] = [blk(39, SI, N) for _ in range(L)]
+    m["shu"] = [blk(39, SI, N) for _ in range(L)]
+    m["shd"] = [blk(39, N, SI) for _ in range(L)]
+    m["shr"] = [dev(torch.randn(N, generator=g, device="cuda") * (1.0 / np.sqrt(N))) for _ in range(L)]
+    m["router"] = [dev(torch.randn(E * N, generator=g, device="cuda") * (1.0 / np.sqrt(N))) for _ in range(L)]
+    G, DR = c["G"], c["DR"]
+    m["conv"] = [dev(torch.randn(2 * IN, generator=g, device="cuda") * 0.5) if t == 1 else None for t in types]
+    m["sa"] = [dev(-0.5 * torch.rand(G, generator=g, device="cuda")) if t == 1 else None for t in types]
+    m["sdt"] = [dev(0.1 * torch.randn(G, generator=g, device="cuda")) if t == 1 else None for t in types]
+    m["sal"] = [dev(0.1 * torch.randn(G * DR, generator=g, device="cuda")) if t == 1 else None for t in types]
+    m["sbe"] = [dev(0.1 * torch.randn(G * DR, generator=g, device="cuda")) if t == 1 else None for t in types]
+    m["snorm"] = [dev(torch.ones(IN, device="cuda")) if t == 1 else None for t in types]
+    m["emb"] = dev(torch.randn(V * N, generator=g, device="cuda") * 0.02)
+    m["onw"] = dev(torch.ones(N, device="cuda"))
+    m["wout"] = blk(8, V, N)
+    max_ctx = c["prompt"] + c["gen"] + 8
+    j = np.arange(c["HD"] // 2)
+    theta = np.arange(max_ctx)[:, None] / np.power(1e7, 2.0 * j / c["HD"])
+    m["cos"] = dev(torch.from_numpy(np.cos(theta).astype(np.float32)).cuda())
+    m["sin"] = dev(torch.from_numpy(np.sin(theta).astype(np.float32)).cuda())
+    m["max_ctx"] = max_ctx
+    m["kv_k"] = dev(torch.zeros(L * max_ctx * n_kv, device="cuda"))
+    m["kv_v"] = dev(torch.zeros(L * max_ctx * n_kv, device="cuda"))
+    m["ssm_state"] = dev(torch.zeros(L * G * c["S"], device="cuda"))
+    torch.cuda.synchronize()
+    return m
+
+
+class HybridCall:
+    """qwen36_batch_forward's 76 arguments for the config-5 model (host arrays of device
+    pointers and sizes kept alive here)."""
+
+    def __init__(self, m, L):
+        c = Q5
+        self.m, self.L, self.keep = m, L, []
+        N, inner, n_kv, IN = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"], c["IN"]
+
+        def P(items):
+            arr = (ctypes.c_void_p * L)(*items)
+            self.keep.append(arr)
+            return ctypes.cast(arr, ctypes.c_void_p).value
+
+        def I(vals):
+            arr = np.ascontiguousarray(vals, dtype=np.int32)
+            self.keep.append(arr)
+            return arr.ctypes.data
+
+        t = m["types"]
+        self.kv_lens = np.zeros(L, np.int32)
+        self.f = [P(m["an"]), P(m["fn"]),
+                  P(m["qkv"]), I([inner + 2 * n_kv] * L), I([N] * L), I([8] * L),
+                  P(m["gate"]), I([IN] * L), I([N] * L), I([8] * L),
+                  P(m["sout"]), I([N] * L), I([IN] * L), I([8] * L),
+                  P(m["o"]), I([N] * L), I([inner] * L), I([8] * L),
+                  P(m["gexp"]), I([39] * L), P(m["uexp"]), I([39] * L), P(m["dexp"]), I([39] * L),
+                  P(m["shg"]), P(m["shu"]), P(m["shd"]), P(m["shr"]), I([c["SI"]] * L),
+                  P(m["router"]), I([0] * L), I([39] * L), I([39] * L), I([39] * L)]
+        self.tail = [P(m["conv"]), P(m["sa"]), P(m["sdt"]), P(m["sal"]), P(m["sbe"]), P(m["snorm"])]
+        self.types = I(t)
+
+    def __call__(self, fn, tokens_ptr, B, logits_ptr, ws_ptr):
+        c, m = Q5, self.m
+        fn.argtypes = QWEN36_ARGTYPES
+        fn.restype = None
+        fn(B, self.L, c["N"], c["NH"], c["NKH"], c["HD"], 0, c["E"], c["k"], c["M"], c["eps"], c["HD"],
+           m["max_ctx"], c["IN"], c["G"], c["S"], 4, c["DR"], m["emb"], 0, self.types, tokens_ptr, logits_ptr,
+           *self.f, m["onw"], m["wout"], c["V"], c["N"], 8, *self.tail, m["ssm_state"], m["kv_k"], m["kv_v"],
+           self.kv_lens.ctypes.data, m["cos"], m["sin"], ws_ptr, None)
+
+
+def run_hybrid(torch, lib, stream, rank=0, world=1):
+    """Config 5: B = 10 sequences through qwen36_batch_forward with device weights, tokens
+    and logits (the drop-in's asynchronous form: every pointer is device memory), greedy
+    next tokens on the device (mlq_argmax); timed over the 64 decode steps after a 128-step
+    prompt.  Returns this rank's numbers (the caller takes the max over ranks)."""
+    from mojollama_b200.kernels import load_kernels
+    c = Q5
+    B, V, P, G = c["B"], c["V"], c["prompt"], c["gen"]
+    prev = lib.mlq_get_stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    m = build_hybrid(torch, c["L"])
+    lib.mlq_set_stream(ctypes.c_void_p(prev))
+    call = HybridCall(m, c["L"])
+    fn = load_kernels().cengine.qwen36_batch_forward
+    d_logits = torch.empty(B * V, device="cuda")
+    d_tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+    prompts = torch.from_numpy(np.random.default_rng(7 + rank).integers(0, V, (P, B)).astype(np.int32)).cuda()
+    ws = torch.empty(12 * B * 8192 + 8, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(t):
+        call(fn, d_tok.data_ptr(), B, d_logits.data_ptr(), ws.data_ptr())
+        call.kv_lens += 1            # the caller advances the per-layer cache lengths
+        rc = lib.mlq_argmax(ctypes.c_void_p(d_logits.data_ptr()), B, V, ctypes.c_void_p(d_tok.data_ptr()))
+        if rc or lib.mlq_last_error():
+            raise RuntimeError(lib.mlq_last_error_message())
+
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.cuda.stream(stream):
+        evs[0].record(stream)
+        for t in range(P):
+            d_tok.copy_(prompts[t])
+            step(t)
+        evs[1].record(stream)
+        l0 = lib.mlq_launch_count()
+        for t in range(G):
+            step(P + t)
+        evs[2].record(stream)
+    stream.synchronize()
+    launches = (lib.mlq_launch_count() - l0) // G
+    pre_ms, dec_ms = evs[0].elapsed_time(evs[1]), evs[1].elapsed_time(evs[2])
+    del m, call
+    torch.cuda.empty_cache()
+    return {"dec_ms": dec_ms, "pre_ms": pre_ms, "launches": launches}
+
+
+def hybrid_line(res, world):
+    c = Q5
+    B, G, P = c["B"], c["gen"], c["prompt"]
+    bytes_step, distinct = hybrid_step_bytes(B)
+    ms = res["dec_ms"] / G
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    achieved = bytes_step / (ms / 1e3) / 1e9
+    return {"workload": "hybrid [3 SSM + 1 GQA] x 10, 256 MXFP4 experts top-8 + shared expert, Q8_0 projections, "
+                        "B=10 x (128 prompt + 64 greedy) through qwen36_batch_forward (config 5); N > 1: one "
+                        "independent replica per GPU",
+            "replicas": world, "tok_s": round(world * B * G / (res["dec_ms"] / 1e3), 1),
+            "tok_s_per_replica": round(B * G / (res["dec_ms"] / 1e3), 1), "ms_per_step": round(ms, 3),
+            "prefill_tok_s": round(world * B * P / (res["pre_ms"] / 1e3), 1), "launches_per_step": res["launches"],
+            "roofline": {"bound": "hbm", "bytes_per_step": bytes_step,
+                         "expected_distinct_experts_per_layer": round(distinct, 1),
+                         "achieved_gbs": round(achieved, 1), "peak": hbm, "frac": round(achieved / hbm, 4)}}
+
+
+def run_hybrid_only(args, rank, world, local_rank):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from mojollama_b200 import core
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        lib = core()
+        assert lib.mlq_init(local_rank) == 0
+        stream = torch.cuda.Stream()
+        lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+        res = run_hybrid(torch, lib, stream, rank, world)
+        t = torch.tensor([res["dec_ms"], res["pre_ms"]], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res["dec_ms"], res["pre_ms"] = (float(v) for v in t.tolist())
+        if rank == 0:
+            print(json.dumps({"hybrid": hybrid_line(res, world)}), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
     return 0
 
 
@@ -1336,6 +1589,8 @@ def main():
     ap.add_argument("--qwen3moe-only", action="store_true", help="run only the config-3 whole-model section")
     ap.add_argument("--no-qwen3moe", action="store_true", help="skip the config-3 whole-model section")
     ap.add_argument("--qwen3moe-profile", action="store_true", help="small config-3 case for an ncu launch list")
+    ap.add_argument("--hybrid-only", action="store_true", help="run only the config-5 whole-model section")
+    ap.add_argument("--no-hybrid", action="store_true", help="skip the config-5 whole-model section")
     ap.add_argument("--moe-layers", type=int, default=None)
     ap.add_argument("--moe-tokens", type=int, default=16)
     ap.add_argument("--moe-steps", type=int, default=5)
@@ -1361,6 +1616,8 @@ def main():
         return run_qwen3moe_only(args)
     if args.qwen3moe_profile:
         return run_qwen3moe_profile(args)
+    if args.hybrid_only:
+        return run_hybrid_only(args, rank, world, local_rank)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":

@@ -500,8 +500,25 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
         if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
         MLQ_TRY(launch_matmul(wr, rqt, xn, lg, E, N, B, 0, s));
         MLQ_TRY(launch_router_topk(lg, B, E, topk, 1, e_idx, e_w, s));
-        MLQ_TRY(launch_moe_experts(gqt, uqt, dqt, ge, ue, de, gs, us, ds, e_idx, e_w, topk, B, M, N, xn, hm, hm2, x, x,
-                                   80.0f, s));
+        const bool grouped = N % 32 == 0 && M % 32 == 0 && E <= 1024 && grouped_tiles_per_expert(gqt, M, N) &&
+                             grouped_tiles_per_expert(uqt, M, N) && grouped_tiles_per_expert(dqt, N, M) &&
+                             !getenv("MLQ_NO_GROUPED_MOE");
+        if (grouped && rc == MLQ_OK) {
+            // every active expert streamed once for all of its (token, slot) rows, then
+            // x += sum_i w_i y_i in slot order (moe_forward_omp's +-80 SiLU clamp)
+            const int R = B * topk;
+            uint8_t *mscr = (uint8_t *)cs.scratch(moe_grouped_scratch_bytes(gqt, uqt, dqt, R, E, M, N));
+            float *ym = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
+            if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_CUDA; break; }
+            MoeGroupedScratch ms;
+            moe_grouped_carve(ms, mscr, gqt, uqt, dqt, R, E, M, N);
+            MLQ_TRY(launch_moe_grouped(gqt, uqt, dqt, ge, ue, de, gs, us, ds, E, e_idx, R, topk, M, N, xn, ym, 80.0f,
+                                       ms, s));
+            MLQ_TRY(launch_ep_combine(ym, nullptr, e_w, B, topk, N, x, x, s));
+        } else {
+            MLQ_TRY(launch_moe_experts(gqt, uqt, dqt, ge, ue, de, gs, us, ds, e_idx, e_w, topk, B, M, N, xn, hm, hm2, x,
+                                       x, 80.0f, s));
+        }
         if (a->shexp_router && a->shexp_router[l]) {
             const int si = a->shexp_int ? a->shexp_int[l] : 512;
             const int sgq = a->shexp_gate_qt ? a->shexp_gate_qt[l] : MLQ_MXFP4;
