@@ -516,7 +516,7 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
             u = _random_kquant(torch, c["uq"], el * FF * N // 256, gen)
             d = _random_kquant(torch, c["dq"], el * N * FF // 256, gen)
         layer_objs.append(EPMoELayer(rank, world, E, k, N, FF, c["gq"], c["uq"], c["dq"], g, u, d, router,
-                                     renorm=True))
+                                     renorm=True, max_tokens=tokens))
     x = torch.randn(tokens, N, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7 + rank))
 
     def step():
@@ -551,7 +551,7 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
         # (world 1: no exchange) on the same tokens: the dispatch and combine move rows
         # without arithmetic, so the two must agree bit for bit
         alone = EPMoELayer(0, 1, E, k, N, FF, c["gq"], c["uq"], c["dq"], full0[0], full0[1], full0[2], full0[3],
-                           renorm=True)
+                           renorm=True, max_tokens=tokens)
         y_ep = layer_objs[0].forward(x, residual=x)
         y_1 = alone.forward(x, residual=x)
         torch.cuda.synchronize()
@@ -566,7 +566,8 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
                   "tolerance": 1e-3, "ok": float(res[0].item()) <= 1e-3}
         del alone, full0
     return {"workload": f"config-3 MoE FFN stack: {L} layers, {E} experts top-{k} (renormalised), FF {FF}, "
-                        f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), NCCL all-to-all",
+                        f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), fixed-capacity NCCL "
+                        f"all-to-all (no host synchronisation in a step)",
             "tokens_per_rank": tokens, "tok_s": round(world * tokens / (t / 1e3), 1), "ms_per_step": round(t, 3),
             "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite,
             "parity": parity,

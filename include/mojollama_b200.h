@@ -313,6 +313,15 @@ int mlq_ep_dispatch(const int *idx, int T, int k, int experts_per_rank, int worl
 int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp, long long gstride,
                  long long ustride, long long dstride, int n_experts, const int *eid, int R, int n_ff, int N,
                  const float *x, float *y);
+/* Fixed-capacity forms for an exchange with equal splits (no count read back to the host):
+   send / recv [world][cap][N + 4] floats, the destination-local expert id in-band at column
+   N of each row (int bits; -1 = unused row).  Rows for destination d sit at d * cap + j in
+   slot order; pos[t*k + i] = d * cap + j.  cap >= T * min(k, experts_per_rank). */
+int mlq_ep_dispatch_packed(const int *idx, int T, int k, int experts_per_rank, int world, int cap, const float *x,
+                           int N, int *pos, float *send);
+int mlq_moe_rows_packed(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp,
+                        long long gstride, long long ustride, long long dstride, int n_experts, const float *recv,
+                        int R, int n_ff, int N, float *y);
 int mlq_ep_combine(const float *recv_y, const int *pos, const float *w, int T, int k, int N, const float *residual,
                    float *out);
 

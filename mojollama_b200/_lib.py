@@ -103,6 +103,9 @@ def core() -> ctypes.CDLL:
     so.mlq_ep_dispatch.argtypes = [_vp, _ci, _ci, _ci, _ci, _vp, _ci, _vp, _vp, _vp, _vp]
     so.mlq_moe_rows.argtypes = [_ci, _ci, _ci, _vp, _vp, _vp, ctypes.c_longlong, ctypes.c_longlong,
                                 ctypes.c_longlong, _ci, _vp, _ci, _ci, _ci, _vp, _vp]
+    so.mlq_ep_dispatch_packed.argtypes = [_vp, _ci, _ci, _ci, _ci, _ci, _vp, _ci, _vp, _vp]
+    so.mlq_moe_rows_packed.argtypes = [_ci, _ci, _ci, _vp, _vp, _vp, ctypes.c_longlong, ctypes.c_longlong,
+                                       ctypes.c_longlong, _ci, _vp, _ci, _ci, _ci, _vp]
     so.mlq_ep_combine.argtypes = [_vp, _vp, _vp, _ci, _ci, _ci, _vp, _vp]
     so.mlq_attn_decode_flat.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci]
     so.mlq_attn_decode_paged.argtypes = [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci, _ci, _ci, _vp]

@@ -23,9 +23,11 @@ namespace mlq {
 constexpr int kEpThreads = 1024;
 
 // one CTA: counts[world], pos[T*k], send_eid[T*k] (stable by destination, then slot)
+// cap > 0: fixed-capacity layout -- destination d's rows start at d * cap, and the slots
+// beyond its count get id -1 (send_eid then has world * cap entries, eid_stride apart)
 __global__ void __launch_bounds__(kEpThreads) k_ep_plan(const int *__restrict__ idx, int S, int e_local, int world,
                                                         int *__restrict__ counts, int *__restrict__ pos,
-                                                        int *__restrict__ send_eid) {
+                                                        int *__restrict__ send_eid, int cap, int eid_stride) {
     __shared__ int warp_cnt[kEpThreads / 32][8];
     __shared__ int base[8];        // running start of each destination for the current chunk
     __shared__ int total[8];
@@ -45,8 +47,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_plan(const int *__restrict__ 
     if (tid == 0) {
         int acc = 0;
         for (int r = 0; r < world; r++) {
-            base[r] = acc;
-            counts[r] = total[r];
+            base[r] = cap > 0 ? r * cap : acc;
+            if (counts) counts[r] = total[r];
             acc += total[r];
         }
     }
@@ -67,7 +69,7 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_plan(const int *__restrict__ 
             int before = base[d] + my_rank_in_warp;
             for (int w2 = 0; w2 < warp; w2++) before += warp_cnt[w2][d];
             pos[s] = before;
-            send_eid[before] = g - d * e_local;
+            send_eid[(size_t)before * eid_stride] = g - d * e_local;
         }
         __syncthreads();
         if (tid < world) {
@@ -77,15 +79,19 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_plan(const int *__restrict__ 
         }
         __syncthreads();
     }
+    if (cap > 0) {   // unused rows of every destination: id -1 (the experts skip them)
+        for (int r = 0; r < world; r++)
+            for (int j = total[r] + tid; j < cap; j += blockDim.x) send_eid[((size_t)r * cap + j) * eid_stride] = -1;
+    }
 }
 
-// send_x[pos[t*k + i]] = x[t]
+// send_x[pos[t*k + i]] = x[t]   (row stride `stride` floats in send_x)
 __global__ void k_ep_gather(const float *__restrict__ x, const int *__restrict__ pos, int k, int N,
-                            float *__restrict__ send_x) {
+                            float *__restrict__ send_x, int stride) {
     const int s = blockIdx.x;
     const int t = s / k;
     const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * N);
-    float4 *dst = reinterpret_cast<float4 *>(send_x + (size_t)pos[s] * N);
+    float4 *dst = reinterpret_cast<float4 *>(send_x + (size_t)pos[s] * stride);
     for (int i = threadIdx.x; i < N / 4; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -167,7 +173,7 @@ void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, in
 int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
                        long long gstride, long long ustride, long long dstride, int E, const int *eid, int R,
                        int row_div, int n_ff, int N, const float *x, float *y, float clamp, const MoeGroupedScratch &m,
-                       cudaStream_t s) {
+                       cudaStream_t s, int eid_stride, int x_stride) {
     if (R <= 0) return MLQ_OK;
     int tiles[3], n_lists;
     moe_grouped_tiles(gqt, uqt, dqt, n_ff, N, tiles, n_lists);
@@ -178,8 +184,8 @@ int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
     const bool pair = gqt == uqt;
     const int chunks = (R + 7) / 8 + (E < R ? E : R);
     void *items[3] = {m.items[0], m.items[1], m.items[2]};
-    int rc = launch_group_plan(eid, R, E, n_lists, items, tiles, m.spos, m.srow, m.nitem, s);
-    if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, m.srow, R, N, m.px, s, row_div);
+    int rc = launch_group_plan(eid, R, E, n_lists, items, tiles, m.spos, m.srow, m.nitem, s, eid_stride);
+    if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, m.srow, R, N, m.px, s, row_div, 80.0f, x_stride);
     GroupedCall gc{};
     gc.planes = m.px;
     gc.n_rows = n_ff;
@@ -227,8 +233,34 @@ int mlq_ep_dispatch(const int *idx, int T, int k, int experts_per_rank, int worl
     }
     cudaStream_t s = stream();
     const int S = T * k;
-    k_ep_plan<<<1, kEpThreads, 0, s>>>(idx, S, experts_per_rank, world, counts, pos, send_eid);
-    k_ep_gather<<<S, 128, 0, s>>>(x, pos, k, N, send_x);
+    k_ep_plan<<<1, kEpThreads, 0, s>>>(idx, S, experts_per_rank, world, counts, pos, send_eid, 0, 1);
+    k_ep_gather<<<S, 128, 0, s>>>(x, pos, k, N, send_x, N);
+    count_launch(2);
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// Fixed-capacity dispatch for an exchange with equal splits (no count read back to the
+// host): send [world][cap][N + 4] floats; the rows for destination d are at d * cap + j in
+// slot order (stable), each row carries the destination-local expert id in-band at column
+// N (as int bits), rows beyond d's count carry id -1.  pos[t*k + i] = d * cap + j, where the
+// result of that slot comes back after the return exchange.  cap >= T * min(k, experts
+// per rank) always suffices (a token sends at most one row per local expert of a peer).
+int mlq_ep_dispatch_packed(const int *idx, int T, int k, int experts_per_rank, int world, int cap, const float *x,
+                           int N, int *pos, float *send) {
+    if (!idx || !x || !pos || !send || T <= 0 || k <= 0 || experts_per_rank <= 0 || world <= 0 || world > 8 ||
+        N <= 0 || N % 4 || cap < T * (k < experts_per_rank ? k : experts_per_rank)) {
+        set_error(MLQ_ERR_ARG, "ep_dispatch_packed: bad arguments (world 1..8, N %% 4 == 0, cap >= T * min(k, E/world))");
+        return MLQ_ERR_ARG;
+    }
+    if (!is_device_ptr(idx) || !is_device_ptr(x) || !is_device_ptr(send)) {
+        set_error(MLQ_ERR_ARG, "ep_dispatch_packed: device pointers only");
+        return MLQ_ERR_ARG;
+    }
+    cudaStream_t s = stream();
+    const int S = T * k, stride = N + 4;
+    k_ep_plan<<<1, kEpThreads, 0, s>>>(idx, S, experts_per_rank, world, nullptr, pos,
+                                       reinterpret_cast<int *>(send) + N, cap, stride);
+    k_ep_gather<<<S, 128, 0, s>>>(x, pos, k, N, send, stride);
     count_launch(2);
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }
@@ -270,6 +302,39 @@ int mlq_moe_rows(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, 
     moe_grouped_carve(m, scr, gqt, uqt, dqt, R, n_experts, n_ff, N);
     int rc = launch_moe_grouped(gqt, uqt, dqt, (const uint8_t *)gexp, (const uint8_t *)uexp, (const uint8_t *)dexp,
                                 gstride, ustride, dstride, n_experts, eid, R, 1, n_ff, N, x, y, 80.0f, m, stream());
+    if (rc != MLQ_OK) {
+        cs.failed = true;
+        cs.finish();
+        return rc;
+    }
+    return cs.finish();
+}
+
+// mlq_moe_rows over packed exchange rows: recv [R][N + 4] floats, the local expert id
+// in-band at column N (rows with id -1, or any id outside [0, n_experts), are skipped).
+int mlq_moe_rows_packed(int gqt, int uqt, int dqt, const void *gexp, const void *uexp, const void *dexp,
+                        long long gstride, long long ustride, long long dstride, int n_experts, const float *recv,
+                        int R, int n_ff, int N, float *y) {
+    if (R < 0 || !recv || !y || !gexp || !uexp || !dexp || n_ff <= 0 || N <= 0 || n_experts <= 0 || N % 32 ||
+        n_ff % 32) {
+        set_error(MLQ_ERR_ARG, "moe_rows_packed: bad arguments");
+        return MLQ_ERR_ARG;
+    }
+    if (R == 0) return MLQ_OK;
+    if (!grouped_tiles_per_expert(gqt, n_ff, N) || !grouped_tiles_per_expert(uqt, n_ff, N) ||
+        !grouped_tiles_per_expert(dqt, N, n_ff)) {
+        set_error(MLQ_ERR_TYPE, "moe_rows_packed: expert types %d/%d/%d", gqt, uqt, dqt);
+        return MLQ_ERR_TYPE;
+    }
+    CallScope cs;
+    uint8_t *scr = (uint8_t *)cs.scratch(moe_grouped_scratch_bytes(gqt, uqt, dqt, R, n_experts, n_ff, N));
+    if (cs.failed) return cs.finish();
+    MoeGroupedScratch m;
+    moe_grouped_carve(m, scr, gqt, uqt, dqt, R, n_experts, n_ff, N);
+    const int stride = N + 4;
+    int rc = launch_moe_grouped(gqt, uqt, dqt, (const uint8_t *)gexp, (const uint8_t *)uexp, (const uint8_t *)dexp,
+                                gstride, ustride, dstride, n_experts, reinterpret_cast<const int *>(recv) + N, R, 1,
+                                n_ff, N, recv, y, 80.0f, m, stream(), stride, stride);
     if (rc != MLQ_OK) {
         cs.failed = true;
         cs.finish();

@@ -1196,10 +1196,11 @@ struct GroupRows {
     int K;
     int row_div;      // source row = rows[p] / row_div (several rows reading one token's activations)
     float clamp;      // silu(clamp(x, +-clamp)) * x2 when x2 is set (HUGE_VALF: no clamp)
+    int stride;       // floats between source rows (K for dense rows)
     __device__ __forceinline__ float operator()(int p, int k) const {
         int r = rows ? __ldg(rows + p) : p;
         if (row_div > 1) r /= row_div;
-        const size_t o = (size_t)r * K + k;
+        const size_t o = (size_t)r * stride + k;
         float v = __ldg(x + o);
         if (x2) {
             const float g = fminf(fmaxf(v, -clamp), clamp);
@@ -1237,9 +1238,9 @@ struct PlanLists {
     int n;
 };
 
-__global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restrict__ eid, int R, int E, PlanLists pl,
-                                                             int *__restrict__ sorted_pos, int *__restrict__ src_row,
-                                                             int *__restrict__ n_items) {
+__global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restrict__ eid, int eid_stride, int R, int E,
+                                                             PlanLists pl, int *__restrict__ sorted_pos,
+                                                             int *__restrict__ src_row, int *__restrict__ n_items) {
     extern __shared__ int sm_plan[];
     int *run = sm_plan;          // [E] counts, then running positions
     int *so = run + E;           // [E + 1] first sorted position of each expert
@@ -1250,7 +1251,7 @@ __global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restri
     for (int e = tid; e < E; e += kPlanThreads) run[e] = 0;
     __syncthreads();
     for (int r = tid; r < R; r += kPlanThreads) {
-        const int e = eid[r];
+        const int e = eid[(size_t)r * eid_stride];
         if (e >= 0 && e < E) atomicAdd(&run[e], 1);
     }
     __syncthreads();
@@ -1298,7 +1299,7 @@ __global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restri
     // stable positions
     for (int c0 = 0; c0 < R; c0 += kPlanThreads) {
         const int r = c0 + tid;
-        const int e = r < R ? eid[r] : -1;
+        const int e = r < R ? eid[(size_t)r * eid_stride] : -1;
         const bool valid = e >= 0 && e < E;
         const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
         const int rank = __popc(same & ((1u << lane) - 1u));
@@ -1471,19 +1472,19 @@ int launch_grouped(const GroupedCall &gc, cudaStream_t s) {
 }
 
 int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
-                         cudaStream_t s, int row_div, float clamp) {
+                         cudaStream_t s, int row_div, float clamp, int x_stride) {
     if (R <= 0) return MLQ_OK;
     const long long blocks = ((long long)R * (K / 32) + 7) / 8;
     count_launch();
     return MLQ_CUDA(launch_pdl_n(k_encode_packed, dim3((unsigned)blocks), dim3(256), 0, s,
-                                 GroupRows{x, x2, rows, K, row_div, clamp},
+                                 GroupRows{x, x2, rows, K, row_div, clamp, x_stride > 0 ? x_stride : K},
                                  R, K, planes))
                ? MLQ_OK
                : MLQ_ERR_CUDA;
 }
 
 int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,
-                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s) {
+                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s, int eid_stride) {
     if (E <= 0 || E > kPlanMaxE || n_lists < 1 || n_lists > 3) {
         set_error(MLQ_ERR_CAPACITY, "grouped experts: %d experts (1..%d), %d item lists", E, kPlanMaxE, n_lists);
         return MLQ_ERR_CAPACITY;
@@ -1495,7 +1496,7 @@ int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *it
         pl.tiles[l] = tiles[l];
     }
     const size_t sm = sizeof(int) * (3 * (size_t)E + 2 + (size_t)kPlanWarps * E);
-    k_group_plan<<<1, kPlanThreads, sm, s>>>(eid, R, E, pl, sorted_pos, src_row, n_items);
+    k_group_plan<<<1, kPlanThreads, sm, s>>>(eid, eid_stride, R, E, pl, sorted_pos, src_row, n_items);
     count_launch();
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
 }

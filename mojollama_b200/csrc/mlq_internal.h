@@ -191,7 +191,7 @@ int launch_grouped(const GroupedCall &gc, cudaStream_t s);
 // packed activation rows p < R: x[rows[p] / row_div] (rows may be null: x[p / row_div]);
 // with x2 set, silu(clamp(x, +-clamp)) * x2 of that row
 int launch_encode_packed(const float *x, const float *x2, const int *rows, int R, int K, uint8_t *planes,
-                         cudaStream_t s, int row_div = 1, float clamp = 80.0f);
+                         cudaStream_t s, int row_div = 1, float clamp = 80.0f, int x_stride = 0);
 // Routed experts of R = T * k rows (row t * k + i: token t, slot i, expert eid[row]) over
 // the grouped expert GEMV: a stable plan by expert, each active expert's gate / up / down
 // matrices streamed once for all of its rows.  x holds one row per token when row_div = k
@@ -205,10 +205,12 @@ struct MoeGroupedScratch {
 };
 size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
 void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
+// eid_stride / x_stride: ints / floats between rows of eid and x (packed exchange rows keep
+// the expert id in-band at column N of an (N + 4)-float row); 0 = dense (1 / N)
 int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
                        long long gstride, long long ustride, long long dstride, int E, const int *eid, int R,
                        int row_div, int n_ff, int N, const float *x, float *y, float clamp, const MoeGroupedScratch &m,
-                       cudaStream_t s);
+                       cudaStream_t s, int eid_stride = 1, int x_stride = 0);
 // out[t] = residual[t] (if set) + sum_i w[t * k + i] * y[pos[t * k + i]] (pos null: identity)
 int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
                       float *out, cudaStream_t s);
@@ -225,7 +227,7 @@ int launch_rms_norm_encode(float *out, const float *x, const float *w, float *re
 // stable order of R rows by expert id (sorted_pos[r], src_row[p]) and the item lists of
 // n_lists tilings (tiles[l] tiles per 8-row chunk; n_items[l] written on the device)
 int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *items, const int *tiles,
-                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s);
+                      int *sorted_pos, int *src_row, int *n_items, cudaStream_t s, int eid_stride = 1);
 // batch-engine embedding rows (qwen36.cu)
 int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_tok, float *x, int B, int N, int V,
                  cudaStream_t s);

@@ -6,15 +6,20 @@ renormalised), per expert silu(clamp(gate x, +-80)) * (up x) -> down, weighted s
 to the residual.  Here the E experts are split into contiguous slices of E / world per
 rank; attention, the router and the shared expert stay replicated.
 
-One forward, per rank (T local tokens):
+One forward, per rank (T local tokens, at most ``max_tokens``):
   1. route:    idx, w = top-k(softmax(W_r x))                          (device)
-  2. dispatch: slots grouped by destination rank, slot order kept        (device)
-  3. exchange: all-to-all of the per-destination counts, then of the token rows and the
-               destination-local expert ids (NCCL over NVLink on GPUs)
-  4. experts:  every received row through its one local expert          (device)
-  5. exchange: the expert outputs go back along the same splits
+  2. dispatch: every destination rank d gets a fixed block of cap = max_tokens * min(k, E/world)
+               rows [d * cap, (d + 1) * cap), slot order kept, the destination-local expert id
+               carried in-band in each row (-1 marks an unused row)       (device)
+  3. exchange: one all-to-all with equal splits (NCCL over NVLink on GPUs); no counts
+               travel to the host, so nothing in a forward waits for the host
+  4. experts:  every received row through its one local expert, unused rows skipped (device)
+  5. exchange: the expert outputs go back, equal splits again
   6. combine:  out[t] = residual[t] + sum_i w[t][i] * y[t, i], i in order (device)
-Every step is deterministic: positions are stable, the combine adds slots in order.
+Every step is deterministic: positions are stable, the combine adds slots in order.  The
+fixed blocks move more bytes than a variable split when routing is uneven (the blocks are
+sized for the worst case), and in exchange the layer issues no host synchronisation, so a
+stack of layers is enqueued as fast as the host can launch and can be captured whole.
 
 The device work goes through a backend object.  `CudaBackend` is the product path (the
 kernels of libmojollama_b200; there is no other implementation).  The collective logic is
@@ -62,24 +67,24 @@ class CudaBackend:
         return idx, w
 
     def dispatch(self, layer: "EPMoELayer", idx: torch.Tensor, x: torch.Tensor):
+        """pos [T*k] and the packed send rows [world * cap][N + 4] (ids in-band at column N)"""
         T, k = idx.shape
-        counts = torch.empty(layer.world, dtype=torch.int32, device=x.device)
+        cap = layer.cap
         pos = torch.empty(T * k, dtype=torch.int32, device=x.device)
-        send_x = torch.empty((T * k, layer.N), dtype=torch.float32, device=x.device)
-        send_eid = torch.empty(T * k, dtype=torch.int32, device=x.device)
-        self._ok(self.lib.mlq_ep_dispatch(_vp(idx), T, k, layer.e_local, layer.world, _vp(x), layer.N, _vp(counts),
-                                          _vp(pos), _vp(send_x), _vp(send_eid)), "mlq_ep_dispatch")
-        return counts, pos, send_x, send_eid
+        send = torch.empty((layer.world * cap, layer.N + 4), dtype=torch.float32, device=x.device)
+        self._ok(self.lib.mlq_ep_dispatch_packed(_vp(idx), T, k, layer.e_local, layer.world, cap, _vp(x), layer.N,
+                                                 _vp(pos), _vp(send)), "mlq_ep_dispatch_packed")
+        return pos, send
 
-    def experts(self, layer: "EPMoELayer", recv_x: torch.Tensor, recv_eid: torch.Tensor):
-        R = recv_x.shape[0]
-        y = torch.empty((R, layer.N), dtype=torch.float32, device=recv_x.device)
+    def experts(self, layer: "EPMoELayer", recv: torch.Tensor):
+        """y [R][N] for the packed received rows (rows with id -1 are left unwritten)"""
+        R = recv.shape[0]
+        y = torch.empty((R, layer.N), dtype=torch.float32, device=recv.device)
         if R:
-            self._ok(self.lib.mlq_moe_rows(layer.gq, layer.uq, layer.dq, _vp(layer.gate), _vp(layer.up),
-                                           _vp(layer.down), layer.gstride, layer.ustride, layer.dstride,
-                                           layer.e_local, _vp(recv_eid), R, layer.n_ff, layer.N, _vp(recv_x),
-                                           _vp(y)),
-                     "mlq_moe_rows")
+            self._ok(self.lib.mlq_moe_rows_packed(layer.gq, layer.uq, layer.dq, _vp(layer.gate), _vp(layer.up),
+                                                  _vp(layer.down), layer.gstride, layer.ustride, layer.dstride,
+                                                  layer.e_local, _vp(recv), R, layer.n_ff, layer.N, _vp(y)),
+                     "mlq_moe_rows_packed")
         return y
 
     def combine(self, layer: "EPMoELayer", recv_y: torch.Tensor, pos: torch.Tensor, w: torch.Tensor,
@@ -100,11 +105,14 @@ class EPMoELayer:
     (moe_ffn)."""
 
     def __init__(self, rank, world, E, k, N, n_ff, gq, uq, dq, gate, up, down, router, router_qt=0, renorm=True,
-                 backend=None, group=None):
+                 backend=None, group=None, max_tokens=64):
         if E % world:
             raise ValueError(f"{E} experts do not split over {world} ranks")
         self.rank, self.world, self.E, self.k, self.N, self.n_ff = rank, world, E, k, N, n_ff
         self.e_local = E // world
+        # rows one rank may send one peer: a token sends at most one row per local expert
+        self.max_tokens = max_tokens
+        self.cap = max_tokens * min(k, self.e_local)
         self.gq, self.uq, self.dq = gq, uq, dq
         self.gate, self.up, self.down, self.router, self.router_qt = gate, up, down, router, router_qt
         self.gstride = n_ff * row_bytes(gq, N)
@@ -114,26 +122,24 @@ class EPMoELayer:
         self.backend = backend if backend is not None else CudaBackend()
         self.group = group
 
-    def exchange(self, send: torch.Tensor, in_splits, out_splits) -> torch.Tensor:
-        out = send.new_empty((sum(out_splits),) + tuple(send.shape[1:]))
-        dist.all_to_all_single(out, send, out_splits, in_splits, group=self.group)
+    def exchange(self, send: torch.Tensor) -> torch.Tensor:
+        """all-to-all with equal splits: block d of `send` goes to rank d, block r of the
+        result came from rank r"""
+        out = torch.empty_like(send)
+        dist.all_to_all_single(out, send, group=self.group)
         return out
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if x.shape[0] > self.max_tokens:
+            raise ValueError(f"{x.shape[0]} tokens > max_tokens {self.max_tokens}")
         b = self.backend
         idx, w = b.route(self, x)
-        counts, pos, send_x, send_eid = b.dispatch(self, idx, x)
+        pos, send = b.dispatch(self, idx, x)
         if self.world == 1:
-            y = b.experts(self, send_x, send_eid)
-            return b.combine(self, y, pos, w, residual)
-        in_splits = [int(v) for v in counts.cpu().tolist()]
-        peer_counts = torch.empty_like(counts)
-        dist.all_to_all_single(peer_counts, counts, group=self.group)
-        out_splits = [int(v) for v in peer_counts.cpu().tolist()]
-        recv_x = self.exchange(send_x, in_splits, out_splits)
-        recv_eid = self.exchange(send_eid, in_splits, out_splits)
-        y = b.experts(self, recv_x, recv_eid)
-        back = self.exchange(y, out_splits, in_splits)
+            return b.combine(self, b.experts(self, send), pos, w, residual)
+        recv = self.exchange(send)
+        y = b.experts(self, recv)
+        back = self.exchange(y)
         return b.combine(self, back, pos, w, residual)
 
 

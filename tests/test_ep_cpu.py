@@ -1,7 +1,8 @@
 """Expert parallelism on CPU ranks (gloo, world size 2 and 4): the collective logic of
-mojollama_b200/ep.py -- splits, the three all-to-all exchanges, the return path and the
-ordered combine -- driven by an oracle backend (numpy, fp64), against the single-rank MoE
-FFN of the oracle over all experts (moe_forward, cengine_batch_instr.c:1113-1207 math).
+mojollama_b200/ep.py -- the fixed-capacity blocks, the two equal-split all-to-all exchanges,
+the return path and the ordered combine -- driven by an oracle backend (numpy, fp64), against
+the single-rank MoE FFN of the oracle over all experts (moe_forward,
+cengine_batch_instr.c:1113-1207 math).
 
 The device kernels behind the product backend are checked against the same oracle in
 tests/test_ep_gpu.py."""
@@ -37,21 +38,34 @@ class OracleBackend:
         return torch.from_numpy(np.array(idx, np.int32)), torch.from_numpy(np.array(w, np.float32))
 
     def dispatch(self, layer, idx, x):
+        """fixed-capacity layout: destination d's rows at d * cap + j in slot order, the
+        destination-local expert id in-band at column N (int bits), -1 for unused rows"""
         flat = idx.reshape(-1).numpy()
         dest = flat // layer.e_local
-        order = np.argsort(dest, kind="stable")
-        pos = np.empty_like(order)
-        pos[order] = np.arange(len(order))
-        counts = np.bincount(dest, minlength=layer.world).astype(np.int32)
-        send_x = x.numpy()[order // layer.k]
-        send_eid = (flat[order] - dest[order] * layer.e_local).astype(np.int32)
-        return (torch.from_numpy(counts), torch.from_numpy(pos.astype(np.int32)),
-                torch.from_numpy(np.ascontiguousarray(send_x)), torch.from_numpy(send_eid))
+        cap, n = layer.cap, layer.N
+        send = np.zeros((layer.world * cap, n + 4), np.float32)
+        ids = send[:, n].view(np.int32)
+        ids[:] = -1
+        pos = np.empty(len(flat), np.int32)
+        fill = np.zeros(layer.world, np.int64)
+        xs = x.numpy()
+        for s_, d in enumerate(dest):
+            p = d * cap + fill[d]
+            fill[d] += 1
+            pos[s_] = p
+            send[p, :n] = xs[s_ // layer.k]
+            ids[p] = flat[s_] - d * layer.e_local
+        return torch.from_numpy(pos), torch.from_numpy(send)
 
-    def experts(self, layer, recv_x, recv_eid):
-        y = np.zeros((recv_x.shape[0], layer.N), np.float32)
+    def experts(self, layer, recv):
+        rv = recv.numpy()
+        n = layer.N
+        eids = np.ascontiguousarray(rv[:, n]).view(np.int32)
+        y = np.zeros((rv.shape[0], n), np.float32)
         g_all, u_all, d_all = layer.gate.numpy(), layer.up.numpy(), layer.down.numpy()
-        for r, (xr, e) in enumerate(zip(recv_x.numpy(), recv_eid.numpy())):
+        for r, (xr, e) in enumerate(zip(rv[:, :n], eids)):
+            if not 0 <= e < layer.e_local:
+                continue
             g = O.gemv(g_all[e * layer.gstride:(e + 1) * layer.gstride], layer.gq, xr, layer.n_ff, layer.N)[0]
             u = O.gemv(u_all[e * layer.ustride:(e + 1) * layer.ustride], layer.uq, xr, layer.n_ff, layer.N)[0]
             h = O.silu_clamped(g) * u
@@ -95,7 +109,7 @@ def _rank(rank, world, port, renorm, q):
         mats, router = _model()
         sl = {n: expert_slice(torch.from_numpy(m), rank, world, E) for n, m in mats.items()}
         layer = EPMoELayer(rank, world, E, K_TOP, N, FF, F.Q8_0, F.Q8_0, F.Q8_0, sl["gate"], sl["up"], sl["down"],
-                           torch.from_numpy(router), renorm=renorm, backend=OracleBackend())
+                           torch.from_numpy(router), renorm=renorm, backend=OracleBackend(), max_tokens=T + world)
         rng = np.random.default_rng(100 + rank)
         x = rng.standard_normal((T + rank, N)).astype(np.float32)   # ranks hold different token counts
         res = rng.standard_normal((T + rank, N)).astype(np.float32)

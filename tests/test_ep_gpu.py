@@ -25,20 +25,27 @@ class _L:   # the fields the oracle dispatch reads
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_ep_dispatch_matches_oracle(cuda_device, world):
+    """fixed-capacity dispatch: positions, in-band expert ids (-1 for unused rows) and the
+    used rows' data bit for bit"""
     from mojollama_b200.ep import CudaBackend
     rng = np.random.default_rng(world)
     T, k, e_local, n = 300, 8, 16, 128
-    idx = rng.integers(0, e_local * world, (T, k)).astype(np.int32)
+    idx = np.stack([rng.choice(e_local * world, k, replace=False) for _ in range(T)]).astype(np.int32)
     x = rng.standard_normal((T, n)).astype(np.float32)
     lay = _L(world, e_local, k)
     lay.N = n
-    counts, pos, send_x, send_eid = CudaBackend().dispatch(lay, torch.from_numpy(idx).cuda(), torch.from_numpy(x).cuda())
+    lay.cap = T * min(k, e_local)
+    pos, send = CudaBackend().dispatch(lay, torch.from_numpy(idx).cuda(), torch.from_numpy(x).cuda())
     torch.cuda.synchronize()
-    wc, wp, wx, we = OracleBackend().dispatch(lay, torch.from_numpy(idx), torch.from_numpy(x))
-    assert np.array_equal(counts.cpu().numpy(), wc.numpy())
+    wp, ws = OracleBackend().dispatch(lay, torch.from_numpy(idx), torch.from_numpy(x))
+    got, want = send.cpu().numpy(), ws.numpy()
     assert np.array_equal(pos.cpu().numpy(), wp.numpy())
-    assert np.array_equal(send_eid.cpu().numpy(), we.numpy())
-    assert np.array_equal(send_x.cpu().numpy(), wx.numpy())
+    gid = np.ascontiguousarray(got[:, n]).view(np.int32)
+    wid = np.ascontiguousarray(want[:, n]).view(np.int32)
+    assert np.array_equal(gid, wid)
+    used = wid >= 0
+    assert used.sum() == T * k
+    assert np.array_equal(got[used, :n], want[used, :n])
 
 
 @pytest.mark.parametrize("renorm", [True, False])
@@ -47,7 +54,7 @@ def test_ep_layer_one_rank_matches_oracle(cuda_device, renorm):
     mats, router = _model()
     d = {n: torch.from_numpy(m).cuda() for n, m in mats.items()}
     layer = EPMoELayer(0, 1, E, K_TOP, N, FF, F.Q8_0, F.Q8_0, F.Q8_0, d["gate"], d["up"], d["down"],
-                       torch.from_numpy(router).cuda(), renorm=renorm)
+                       torch.from_numpy(router).cuda(), renorm=renorm, max_tokens=16)
     rng = np.random.default_rng(7)
     x = rng.standard_normal((9, N)).astype(np.float32)
     res = rng.standard_normal((9, N)).astype(np.float32)
@@ -81,7 +88,7 @@ def _nccl_rank(rank, world, port, q):
         mats, router = _model()
         sl = {n: expert_slice(torch.from_numpy(m), rank, world, E).cuda() for n, m in mats.items()}
         layer = EPMoELayer(rank, world, E, K_TOP, N, FF, F.Q8_0, F.Q8_0, F.Q8_0, sl["gate"], sl["up"], sl["down"],
-                           torch.from_numpy(router).cuda(), renorm=True)
+                           torch.from_numpy(router).cuda(), renorm=True, max_tokens=8)
         rng = np.random.default_rng(200 + rank)
         x = rng.standard_normal((6 + rank, N)).astype(np.float32)
         res = rng.standard_normal((6 + rank, N)).astype(np.float32)
