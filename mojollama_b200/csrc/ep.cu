@@ -101,7 +101,7 @@ __global__ void k_ep_combine(const float *__restrict__ y, const int *__restrict_
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < N; c += gridDim.y * blockDim.x) {
         float acc = residual ? residual[(size_t)t * N + c] : 0.0f;
         for (int i = 0; i < k; i++) {
             const int r = pos ? pos[t * k + i] : t * k + i;
@@ -114,7 +114,7 @@ __global__ void k_ep_combine(const float *__restrict__ y, const int *__restrict_
 int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
                       float *out, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(T);
+    cfg.gridDim = dim3(T, (N + 255) / 256);   // columns spread over CTAs: one token is 8 CTAs at N = 2048
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute at[1];

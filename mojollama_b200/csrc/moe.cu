@@ -421,24 +421,36 @@ __global__ void k_router_topk(const float *__restrict__ logits, int B, int E, in
     const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (b >= B) return;
     const float *lg = logits + (size_t)b * E;
+    // lane holds experts lane + 32 j (j < 8: up to 256 experts) in registers
+    float p[8];
     float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int e = lane + 32 * j;
+        p[j] = e < E ? lg[e] : -INFINITY;
+        mx = fmaxf(mx, p[j]);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.0f;
-    for (int e = lane; e < E; e += 32) sum += expf(lg[e] - mx);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        p[j] = (lane + 32 * j) < E ? expf(p[j] - mx) : 0.0f;
+        sum += p[j];
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float inv = 1.0f / (sum + 1e-10f);
-    unsigned long long taken[4] = {0, 0, 0, 0};   // up to 256 experts
+#pragma unroll
+    for (int j = 0; j < 8; j++) p[j] = (lane + 32 * j) < E ? p[j] * inv : -INFINITY;
     float tsum = 0.0f;
-    for (int j = 0; j < k; j++) {
+    for (int s = 0; s < k; s++) {
+        // this lane's best remaining expert (strictly greater wins: ties keep the lower index)
         float best = -INFINITY;
         int bi = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            if ((taken[e >> 6] >> (e & 63)) & 1ull) continue;
-            const float p = expf(lg[e] - mx) * inv;
-            if (p > best || (p == best && e < bi)) { best = p; bi = e; }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (p[j] > best) { best = p[j]; bi = lane + 32 * j; }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -446,16 +458,20 @@ __global__ void k_router_topk(const float *__restrict__ logits, int B, int E, in
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
         }
-        if (bi >= 0 && bi < E) taken[bi >> 6] |= 1ull << (bi & 63);
+        if (bi >= 0 && bi < E && (bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (lane + 32 * j == bi) p[j] = -INFINITY;   // taken
+        }
         if (lane == 0) {
-            idx[(size_t)b * k + j] = (bi < E) ? bi : -1;
-            w[(size_t)b * k + j] = best;
+            idx[(size_t)b * k + s] = (bi < E) ? bi : -1;
+            w[(size_t)b * k + s] = best;
         }
         tsum += best;
     }
     if (renorm && lane == 0) {
         const float ti = 1.0f / (tsum + 1e-10f);
-        for (int j = 0; j < k; j++) w[(size_t)b * k + j] *= ti;
+        for (int s = 0; s < k; s++) w[(size_t)b * k + s] *= ti;
     }
 }
 
