@@ -25,6 +25,7 @@ hybrid    config 5 (hybrid [3 SSM + 1 GQA] x 10, 256 MXFP4 experts) through
 moe_ep    config 3's MoE FFN stack (48 layers, 128 experts top-8) with the experts split over
           the N GPUs and NCCL all-to-all dispatch/combine: tok/s (weak scaling), with the
           expert-parallel layer checked against the same layer on one GPU.
+sweep     config 2 in full (6 formats x 4 shapes x M in {1, 4, 16, 64, 256}), one row per case.
 cpu_baseline  the reference C engine (compiled from its own sources into oracle/_ref)
           on the host cores, on the same weights (MXFP4 re-encoded in the reference's
           own layout), with all host threads.
@@ -428,6 +429,12 @@ def run_ours(args, rank, world, local_rank):
                                     cpu_seconds=args.cpu_seconds, with_parity=not args.no_parity)
     if hyb is not None:
         line["hybrid"] = hybrid_line(hyb, world)
+    if not args.no_sweep and world == 1:
+        # config 2 in full: one compact row per case, [format, N, K, M, us, GB/s, TFLOP/s]
+        sw = sweep_cases(torch, lib, stream, SWEEP_M)
+        line["sweep"] = {"metric": sw["metric"], "columns": ["fmt", "N", "K", "M", "us", "gbs", "tflops"],
+                         "cases": [[c["fmt"], c["N"], c["K"], c["M"], c["us"], c["gbs"], c["tflops"]]
+                                   for c in sw["cases"]]}
     if not args.no_qwen3moe and world == 1:
         line["qwen3moe"] = run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                         cpu_seconds=args.cpu_seconds)
@@ -1105,18 +1112,23 @@ SWEEP_M = [1, 4, 16, 64, 256]
 
 
 def run_sweep(args):
-    """Config 2 in full: every format x shape x M, device-resident, CUDA events,
-    weights rotated over enough distinct copies that each launch reads from HBM (the set
-    of copies is > 2x L2).  Prints one JSON object with GB/s (algorithmic bytes) and
-    TFLOP/s (2*M*N*K) per case."""
+    """Config 2 in full as its own JSON object (see sweep_cases)."""
     import torch
     from mojollama_b200 import core
     lib = core()
     assert lib.mlq_init(0) == 0
     stream = torch.cuda.Stream()
     lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
-    from mojollama_b200 import gguf_quant as Q
     ms = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else SWEEP_M
+    print(json.dumps(sweep_cases(torch, lib, stream, ms)), flush=True)
+    return 0
+
+
+def sweep_cases(torch, lib, stream, ms):
+    """Config 2 in full: every format x shape x M, device-resident, CUDA events,
+    weights rotated over enough distinct copies that each launch reads from HBM (the set
+    of copies is > 2x L2).  GB/s (algorithmic bytes) and TFLOP/s (2*M*N*K) per case."""
+    from mojollama_b200 import gguf_quant as Q
     out = {"metric": "config-2 sweep: GB/s = (N*row_bytes + M*K*4 + M*N*4)/t, TFLOP/s = 2*M*N*K/t", "cases": []}
     for name, qt in FORMATS:
         be, bb = BLOCK[qt]
@@ -1157,8 +1169,7 @@ def run_sweep(args):
                                      "gbs": round(byts / t / 1e9, 1), "tflops": round(2 * m * n * k / t / 1e12, 2)})
             del dev
             torch.cuda.empty_cache()
-    print(json.dumps(out), flush=True)
-    return 0
+    return out
 
 
 def run_moe_ep_only(args, rank, world, local_rank):
@@ -1599,6 +1610,7 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=3)
     ap.add_argument("--sweep", action="store_true", help="config-2 sweep (formats x shapes x M), one JSON object")
     ap.add_argument("--sweep-m", default=None, help="comma-separated M values for --sweep")
+    ap.add_argument("--no-sweep", action="store_true", help="leave the config-2 sweep out of the bench line")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
