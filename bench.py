@@ -20,6 +20,8 @@ decode    config 1 (TinyLlama-1.1B shape, Q8_0, B=4) through batch_forward: tok/
 qwen3moe  config 3 (Qwen3-30B-A3B shape, Q4_K_M, 48 layers, 128 experts top-8) through
           batch_forward at B = 1 and 16: decode tok/s, bytes per step and achieved bandwidth,
           end to end through the reference-named entry, the reference C ops on the host cores.
+gptoss    config 4 (GPT-OSS-20B shape: bf16 attention alternating full / 128-token windows,
+          32 MXFP4 experts top-4, 16-token pages) through batch_forward at B = 1, 16, 64.
 hybrid    config 5 (hybrid [3 SSM + 1 GQA] x 10, 256 MXFP4 experts) through
           qwen36_batch_forward at B = 10; N > 1: one independent replica per GPU.
 moe_ep    config 3's MoE FFN stack (48 layers, 128 experts top-8) with the experts split over
@@ -435,6 +437,8 @@ def run_ours(args, rank, world, local_rank):
         line["sweep"] = {"metric": sw["metric"], "columns": ["fmt", "N", "K", "M", "us", "gbs", "tflops"],
                          "cases": [[c["fmt"], c["N"], c["K"], c["M"], c["us"], c["gbs"], c["tflops"]]
                                    for c in sw["cases"]]}
+    if not args.no_gptoss and world == 1:
+        line["gptoss"] = run_gptoss(torch, lib, stream)
     if not args.no_qwen3moe and world == 1:
         line["qwen3moe"] = run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                         cpu_seconds=args.cpu_seconds)
@@ -868,6 +872,164 @@ def run_qwen3moe_only(args):
     lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
     print(json.dumps({"qwen3moe": run_qwen3moe(torch, lib, stream, with_cpu=not args.no_cpu_baseline,
                                                cpu_seconds=args.cpu_seconds)}), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ config-4 whole model
+# GPT-OSS-20B shape through batch_forward: 24 layers, d_model 2880, 64 / 8 heads of 64, bf16
+# attention projections, layers alternating full and 128-token sliding-window attention
+# (mlq_set_attention_windows), 32 MXFP4 experts top-4 with SwiGLU FFN 2880, F32 router, bf16
+# head over 201088 tokens, KV in 16-token pages.  Decode 128 steps after a 1024-token
+# context at B = 1, 16 and 64.  The context's K/V rows are not computed (no prefill is
+# timed): the pages are mapped zero-filled, which leaves the decode step's work -- weights
+# and K/V rows read -- what it is at that context.  The batch engine's MoE rule (moe_ffn: no
+# renormalisation, exact SiLU) and no attention sinks.
+Q4 = dict(L=24, N=2880, NH=64, NKH=8, HD=64, V=201088, E=32, k=4, M=2880, eps=1e-5, ctx=1024, gen=128, window=128)
+
+
+def gptoss_step_bytes(B, pos):
+    c = Q4
+    N, inner, kv, M = c["N"], c["NH"] * c["HD"], c["NKH"] * c["HD"], c["M"]
+    attn = 2 * (inner * N + 2 * kv * N + N * inner)
+    expert = 3 * M * N // 32 * 17
+    distinct = c["E"] * (1 - (1 - c["k"] / c["E"]) ** B)
+    n_full = c["L"] // 2
+    kv_rows = n_full * (pos + 1) + (c["L"] - n_full) * min(pos + 1, c["window"])
+    kv_bytes = B * kv_rows * 2 * kv * 4 + B * c["L"] * 2 * kv * 4
+    return int(c["L"] * (attn + c["E"] * N * 4 + distinct * expert) + 2 * c["V"] * N + kv_bytes +
+               B * (N * 4 + c["V"] * 4)), distinct
+
+
+def build_gptoss(torch, lib):
+    from mojollama_b200 import bc as BCm
+    c = Q4
+    L, N, NH, NKH, HD, V, E, M = c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["V"], c["E"], c["M"]
+    inner, kv = NH * HD, NKH * HD
+    g = torch.Generator(device="cuda").manual_seed(4)
+    keep = []
+
+    def bf16(rows, cols):
+        t = (torch.randn(rows * cols, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        keep.append(t)
+        return t.data_ptr()
+
+    def mx(rows, cols):
+        t = _random_blocks(torch, 39, rows * cols // 32, g)
+        keep.append(t)
+        return t.data_ptr()
+
+    b = BCm.BCBuilder()
+    bc = b.bc
+    bc.L, bc.N, bc.NH, bc.NKH, bc.HD, bc.FF, bc.V, bc.eps, bc.nc = L, N, NH, NKH, HD, 0, V, c["eps"], N
+    for nm, r, k in (("wQ", inner, N), ("wK", kv, N), ("wV", kv, N), ("wO", N, inner)):
+        b.layers(nm, [bf16(r, k) for _ in range(L)])
+    for f, v in (("nQ", inner), ("nK", kv), ("nV", kv), ("nO", N)):
+        b.ints(f, [v] * L)
+    for f in ("q_quant", "k_quant", "v_quant", "o_quant"):
+        b.ints(f, [30] * L)
+    ones = torch.ones(N, device="cuda")
+    keep.append(ones)
+    b.layers("wAN", [ones.data_ptr()] * L)
+    b.layers("wFN", [ones.data_ptr()] * L)
+    routers = [torch.randn(E * N, generator=g, device="cuda") * (1.0 / np.sqrt(N)) for _ in range(L)]
+    keep.extend(routers)
+    b.layers("w_gate_inp", [r.data_ptr() for r in routers])
+    b.layers("w_gate_exps", [mx(E * M, N) for _ in range(L)])
+    b.layers("w_up_exps", [mx(E * M, N) for _ in range(L)])
+    b.layers("w_down_exps", [mx(E * N, M) for _ in range(L)])
+    bc.n_experts, bc.n_experts_per_tok, bc.moe_intermediate = E, c["k"], M
+    bc.gate_exp_quant, bc.up_exp_quant, bc.down_exp_quant = 39, 39, 39
+    emb = torch.randn(V * N, generator=g, device="cuda") * 0.02
+    keep.append(emb)
+    bc.emb, bc.emb_quant = emb.data_ptr(), 0
+    bc.onw = ones.data_ptr()
+    bc.wOut = bf16(V, N)
+    bc.outNR, bc.outNC, bc.outQuant = V, N, 30
+    max_ctx = c["ctx"] + c["gen"] + 8
+    j = np.arange(HD // 2)
+    theta = np.arange(max_ctx)[:, None] / np.power(150000.0, 2.0 * j / HD)
+    b.ptr("cos_table", np.cos(theta).astype(np.float32))
+    b.ptr("sin_table", np.sin(theta).astype(np.float32))
+    bc.max_ctx, bc.rope_dim = max_ctx, HD
+    win = np.array([0 if l % 2 == 0 else c["window"] for l in range(L)], np.int32)
+    assert lib.mlq_set_attention_windows(ctypes.byref(bc), win.ctypes.data, L) == 0
+    torch.cuda.synchronize()
+    return b, keep
+
+
+def run_gptoss(torch, lib, stream):
+    """Config 4 decode through batch_forward with device sampling, per batch size."""
+    from mojollama_b200.serving import PagedKV
+    c = Q4
+    V, P, G = c["V"], c["ctx"], c["gen"]
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    prev = lib.mlq_get_stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    b, keep = build_gptoss(torch, lib)
+    lib.mlq_set_stream(ctypes.c_void_p(prev))
+    out = {"workload": "GPT-OSS-20B shape: 24 layers, bf16 attention alternating full / 128-token window, 32 MXFP4 "
+                       "experts top-4, bf16 head over 201088 tokens, 16-token KV pages; 128 greedy decode steps after "
+                       "a 1024-token context (config 4)", "context_kv": "zero-filled pages (prefill not timed)",
+           "batches": {}}
+    for B in (1, 16, 64):
+        kvs = [PagedKV(c["L"], c["NKH"], c["HD"], 16, (P + G) // 16 + 2) for _ in range(B)]
+        for k in kvs:
+            k.fast_forward(P)
+        b.kv_array([k.block for k in kvs])
+        d_logits = torch.empty(B * V, device="cuda")
+        b.bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        d_tok = torch.from_numpy(np.random.default_rng(B).integers(0, V, B).astype(np.int32)).cuda()
+        torch.cuda.synchronize()
+
+        def fwd(t):
+            rc = lib.mlq_batch_forward_sample(ctypes.byref(b.bc), ctypes.c_void_p(d_tok.data_ptr()), B, None,
+                                              ctypes.c_float(0.0), 0, t, ctypes.c_void_p(d_tok.data_ptr()))
+            if rc:
+                raise RuntimeError(lib.mlq_last_error_message())
+
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        with torch.cuda.stream(stream):
+            for t in range(3):          # warm-up (plan, first eager step, graph capture)
+                fwd(t)
+            ev[0].record(stream)
+            l0 = lib.mlq_launch_count()
+            for t in range(3, G):
+                fwd(t)
+            ev[1].record(stream)
+        stream.synchronize()
+        steps = G - 3
+        launches = (lib.mlq_launch_count() - l0) // steps
+        ms = ev[0].elapsed_time(ev[1]) / steps
+        sb = [gptoss_step_bytes(B, P + t) for t in range(3, G)]
+        step_bytes = sum(x[0] for x in sb) / steps
+        achieved = step_bytes / (ms / 1e3) / 1e9
+        out["batches"][str(B)] = {
+            "tok_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 3), "launches_per_step": int(launches),
+            "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                         "expected_distinct_experts_per_layer": round(sb[0][1], 1),
+                         "achieved_gbs": round(achieved, 1), "peak": hbm, "frac": round(achieved / hbm, 4)}}
+        for k in kvs:
+            k.free()
+        del d_logits
+    lib.mlq_set_attention_windows(ctypes.byref(b.bc), None, 0)
+    del keep
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_gptoss_only(args):
+    import torch
+    from mojollama_b200 import core
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    print(json.dumps({"gptoss": run_gptoss(torch, lib, stream)}), flush=True)
     return 0
 
 
@@ -1602,6 +1764,8 @@ def main():
     ap.add_argument("--no-qwen3moe", action="store_true", help="skip the config-3 whole-model section")
     ap.add_argument("--qwen3moe-profile", action="store_true", help="small config-3 case for an ncu launch list")
     ap.add_argument("--hybrid-only", action="store_true", help="run only the config-5 whole-model section")
+    ap.add_argument("--gptoss-only", action="store_true", help="run only the config-4 whole-model section")
+    ap.add_argument("--no-gptoss", action="store_true", help="skip the config-4 whole-model section")
     ap.add_argument("--no-hybrid", action="store_true", help="skip the config-5 whole-model section")
     ap.add_argument("--moe-layers", type=int, default=None)
     ap.add_argument("--moe-tokens", type=int, default=16)
@@ -1631,6 +1795,8 @@ def main():
         return run_qwen3moe_profile(args)
     if args.hybrid_only:
         return run_hybrid_only(args, rank, world, local_rank)
+    if args.gptoss_only:
+        return run_gptoss_only(args)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":

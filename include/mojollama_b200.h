@@ -184,6 +184,10 @@ int mlq_ssm_layer_fused(const float *x, const float *residual, float *output, co
    tokens [B] (B <= 64), one new token per sequence; c->logits [B][outNR] is written and
    every kv_array[b]->seq_len[0] advances by one.  ws is accepted and unused. */
 int mlq_batch_forward(const void *bc, const int *tokens, int B, float *ws);
+/* Sliding-window attention per layer for batch_forward on the model described by bc (no
+   counterpart in the reference, whose engine attends to every position): layer l attends to
+   its last windows[l] positions, 0 = all.  Kept per BC address; L = 0 clears it. */
+int mlq_set_attention_windows(const void *bc, const int *windows, int L);
 
 /* ---- GGUF reader and device weight loader ----
    Replaces the reference's gguf-py load path (turbo_engine_v7_moe.py:425-618: GGUFReader,

@@ -65,6 +65,7 @@ def core() -> ctypes.CDLL:
     so.mlq_ssm_decode_step.argtypes = [_vp] * 9 + [_ci] * 7
     so.mlq_ssm_layer_fused.argtypes = [_vp] * 10 + [_vp, _ci, _ci, _ci, _vp, _ci, _ci, _ci] + [_ci] * 7
     so.mlq_batch_forward.argtypes = [_vp, _vp, _ci, _vp]
+    so.mlq_set_attention_windows.argtypes = [_vp, _vp, _ci]
     so.mlq_sample.argtypes = [_vp, _ci, _ci, ctypes.c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]
     so.mlq_argmax.argtypes = [_vp, _ci, _ci, _vp]
     so.mlq_kv_snapshot.argtypes = [_vp, _ci, _vp]

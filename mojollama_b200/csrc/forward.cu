@@ -130,7 +130,19 @@ struct LayerPlan {
     const float *conv = nullptr, *ssm_a = nullptr, *ssm_dt = nullptr, *ssm_alpha = nullptr, *ssm_beta = nullptr;
     const uint8_t *wssmout = nullptr;
     int qssmout = 0;
+    int window = 0;   // attention over the last `window` positions only (0: all)
 };
+
+// Per-layer sliding windows of a model description (mlq_set_attention_windows), keyed by
+// the BC's address; part of the plan's fingerprint, so changing them rebuilds the plan
+static std::mutex g_win_mu;
+static std::map<uintptr_t, std::vector<int>> g_windows;
+
+static std::vector<int> windows_of(const BC *c) {
+    std::lock_guard<std::mutex> lk(g_win_mu);
+    auto it = g_windows.find((uintptr_t)c);
+    return it == g_windows.end() ? std::vector<int>() : it->second;
+}
 
 struct ModelPlan {
     unsigned long long gen = 0;   // distinguishes rebuilt plans of one BC address
@@ -172,6 +184,10 @@ static std::vector<uint8_t> fingerprint(const BC *c) {
     std::vector<uint8_t> f(reinterpret_cast<const uint8_t *>(&k), reinterpret_cast<const uint8_t *>(&k) + sizeof(BC));
     const int L = c->L;
     f.push_back(ref_compat() ? 1 : 0);
+    for (int w : windows_of(c)) {
+        const uint8_t *wb = reinterpret_cast<const uint8_t *>(&w);
+        f.insert(f.end(), wb, wb + sizeof(int));
+    }
     fp_push(f, c->wQ, L); fp_push(f, c->wK, L); fp_push(f, c->wV, L); fp_push(f, c->wO, L);
     fp_push(f, c->wG, L); fp_push(f, c->wU, L); fp_push(f, c->wD, L); fp_push(f, c->wAN, L); fp_push(f, c->wFN, L);
     fp_push(f, c->q_quant, L); fp_push(f, c->k_quant, L); fp_push(f, c->v_quant, L); fp_push(f, c->o_quant, L);
@@ -228,8 +244,10 @@ static size_t expert_extent(long long stride, int E, int qt, int rows, int cols)
 static bool build_plan(const BC *c, CallScope &cs, ModelPlan &P) {
     const int L = c->L, N = c->N, NH = c->NH, NKH = c->NKH, HD = c->HD, inner = NH * HD;
     P.layers.assign(L, LayerPlan{});
+    const std::vector<int> win = windows_of(c);
     for (int l = 0; l < L; l++) {
         LayerPlan &lp = P.layers[l];
+        lp.window = l < (int)win.size() ? win[l] : 0;
         lp.an = Fv(cs, c->wAN ? c->wAN[l] : nullptr, N);
         lp.fn = Fv(cs, c->wFN ? c->wFN[l] : nullptr, N);
         lp.ssm = c->layer_types && c->layer_types[l] == 1 && c->ssm_conv1d && c->ssm_conv1d[l];
@@ -595,7 +613,7 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
             // the attention output also as packed rows for the o projection (decode path)
             const bool o_fast = fast && !lp.wattng && lp.no == N;
             const bool att_packed = o_fast && inner == NH * HD && attn_packs_output(NH, NKH, HD);
-            MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, 0, scale, att, sb.attn_scr,
+            MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, lp.window, scale, att, sb.attn_scr,
                                        sb.attn_sb, s, att_packed ? sb.pa : nullptr));
             bool o_done = false;
             if (o_fast && rc == MLQ_OK) {   // x = res + W_o att
@@ -827,6 +845,27 @@ using namespace mlq;
 extern "C" {
 
 size_t mlq_sizeof_bc(void) { return sizeof(BC); }
+
+// Sliding-window attention per layer for batch_forward on this model description: layer l
+// attends to its last windows[l] positions (0 = all of them).  The reference's engine has no
+// windowed attention; GPT-OSS-style models alternate full and 128-token windows.  The setting
+// belongs to the BC address; windows == NULL or L == 0 clears it.
+int mlq_set_attention_windows(const void *bc, const int *windows, int L) {
+    if (!bc || L < 0 || (L > 0 && !windows)) {
+        set_error(MLQ_ERR_ARG, "mlq_set_attention_windows: null model or windows");
+        return MLQ_ERR_ARG;
+    }
+    for (int l = 0; l < L; l++) {
+        if (windows[l] < 0) {
+            set_error(MLQ_ERR_ARG, "mlq_set_attention_windows: layer %d window %d < 0", l, windows[l]);
+            return MLQ_ERR_ARG;
+        }
+    }
+    std::lock_guard<std::mutex> lk(g_win_mu);
+    if (L == 0) g_windows.erase((uintptr_t)bc);
+    else g_windows[(uintptr_t)bc] = std::vector<int>(windows, windows + L);
+    return MLQ_OK;
+}
 
 void mlq_forget_model_plans(void) {
     destroy_graphs();

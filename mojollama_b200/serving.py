@@ -69,6 +69,19 @@ class PagedKV:
         pt.free_count = pt.n_pages
         self.block.seq_len[0] = 0
 
+    def fast_forward(self, n: int):
+        """map pages for positions [0, n) and continue at position n; the rows keep whatever
+        the pool holds (zeros for a fresh pool), which is what a decode-throughput
+        measurement at context n needs (the values do not change the work)"""
+        pt = self.block.pt
+        for i in range((n + pt.page_size - 1) // pt.page_size):
+            if pt.table[i] < 0:
+                page = self.lib.mlq_page_table_alloc(ctypes.byref(pt))
+                if page < 0:
+                    raise RuntimeError("page pool full")
+                pt.table[i] = page
+        self.block.seq_len[0] = n
+
     def free(self):
         if self.block.pt.pages:
             self.lib.mlq_page_table_destroy(ctypes.byref(self.block.pt))

@@ -94,7 +94,7 @@ def forward_step(model, state, seqs, tokens, compat_xn=None):
                 kb = O.rope_neox(k[b], NKH, HD, pos, model["cos"], model["sin"], rope_dim)
                 ks.append(kb)
                 vs.append(np.asarray(v[b], np.float32))
-                att[b] = O.gqa_decode(qb, np.stack(ks), np.stack(vs), NH, NKH, HD)
+                att[b] = O.gqa_decode(qb, np.stack(ks), np.stack(vs), NH, NKH, HD, ly.get("window", 0))
             wo = ly["attn_gate"] if ly.get("attn_gate") else ly["o"]
             x = (res + _mv(wo, att, N, inner)).astype(np.float32)
         xn, res = O.rms_norm(x, ly["fn"], eps, sanitize=True)        # :1408-1427
