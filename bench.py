@@ -900,10 +900,10 @@ def gptoss_step_bytes(B, pos):
                B * (N * 4 + c["V"] * 4)), distinct
 
 
-def build_gptoss(torch, lib):
+def build_gptoss(torch, lib, layers=None):
     from mojollama_b200 import bc as BCm
     c = Q4
-    L, N, NH, NKH, HD, V, E, M = c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["V"], c["E"], c["M"]
+    L, N, NH, NKH, HD, V, E, M = layers or c["L"], c["N"], c["NH"], c["NKH"], c["HD"], c["V"], c["E"], c["M"]
     inner, kv = NH * HD, NKH * HD
     g = torch.Generator(device="cuda").manual_seed(4)
     keep = []
@@ -1020,6 +1020,41 @@ def run_gptoss(torch, lib, stream):
     del keep
     torch.cuda.empty_cache()
     return out
+
+
+def run_gptoss_profile(args):
+    """Small case for an ncu launch list of config-4 decode steps: `--profile-steps` layers,
+    a 256-token context, 4 steps at B = 16 and 4 at B = 64 (weights ~2.7 GB)."""
+    import torch
+    from mojollama_b200 import core
+    from mojollama_b200.serving import PagedKV
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    L = args.profile_steps
+    b, keep = build_gptoss(torch, lib, layers=L)
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    V = Q4["V"]
+    for B in (16, 64):
+        kvs = [PagedKV(L, Q4["NKH"], Q4["HD"], 16, 24) for _ in range(B)]
+        for k in kvs:
+            k.fast_forward(256)
+        b.kv_array([k.block for k in kvs])
+        d_logits = torch.empty(B * V, device="cuda")
+        b.bc.logits = ctypes.cast(ctypes.c_void_p(d_logits.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        d_tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for t in range(4):
+                rc = lib.mlq_batch_forward_sample(ctypes.byref(b.bc), ctypes.c_void_p(d_tok.data_ptr()), B, None,
+                                                  ctypes.c_float(0.0), 0, t, ctypes.c_void_p(d_tok.data_ptr()))
+                assert rc == 0, lib.mlq_last_error_message()
+        stream.synchronize()
+        for k in kvs:
+            k.free()
+    print(json.dumps({"gptoss_profile_layers": L}))
+    return 0
 
 
 def run_gptoss_only(args):
@@ -1766,6 +1801,7 @@ def main():
     ap.add_argument("--hybrid-only", action="store_true", help="run only the config-5 whole-model section")
     ap.add_argument("--gptoss-only", action="store_true", help="run only the config-4 whole-model section")
     ap.add_argument("--no-gptoss", action="store_true", help="skip the config-4 whole-model section")
+    ap.add_argument("--gptoss-profile", action="store_true", help="small config-4 case for an ncu launch list")
     ap.add_argument("--no-hybrid", action="store_true", help="skip the config-5 whole-model section")
     ap.add_argument("--moe-layers", type=int, default=None)
     ap.add_argument("--moe-tokens", type=int, default=16)
@@ -1797,6 +1833,8 @@ def main():
         return run_hybrid_only(args, rank, world, local_rank)
     if args.gptoss_only:
         return run_gptoss_only(args)
+    if args.gptoss_profile:
+        return run_gptoss_profile(args)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":

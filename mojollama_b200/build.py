@@ -85,7 +85,7 @@ def build(verbose: bool = False, jobs: int = 0) -> str:
                 print(f"  nvcc {os.path.relpath(s, PKG)}", flush=True)
     core = os.path.join(LIB, "libmojollama_b200.so")
     if _stale(core, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", core] + objs + ["-lcudart", "-lcuda"])
+        _run([NVCC] + ARCH + ["-shared", "-o", core] + objs + ["-lcudart", "-lcuda", "-lcublas"])
         print(f"  link {os.path.relpath(core, PKG)}", flush=True)
     for name, src in ALIASES.items():
         out = os.path.join(LIB, name)

@@ -25,6 +25,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <type_traits>
 #include <math.h>
 #include <stdint.h>
 
@@ -859,6 +860,13 @@ template <typename WT>
 static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
     const LaunchEnv *c = launch_env();
     if (!c) return MLQ_ERR_NO_DEVICE;
+    if constexpr (sizeof(WT) == 2) {
+        // more than four activation rows: one GEMM instead of passes of four over the matrix
+        if (B > 4 && !getenv("MLQ_NO_GEMM16")) {
+            const int rc = launch_gemm16(W, std::is_same<WT, __nv_bfloat16>::value ? 1 : 0, x, out, n_rows, K, B, s);
+            if (rc != MLQ_ERR_UNSUPPORTED) return rc;
+        }
+    }
     const WT *w = reinterpret_cast<const WT *>(W);
     const int V = 16 / sizeof(WT);
     const int vec_ok = (K % V == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&

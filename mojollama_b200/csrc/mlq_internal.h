@@ -97,6 +97,9 @@ bool is_quant_type(int qt);
 int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int n_cols,
                   int B, size_t w_bytes, cudaStream_t s);
 int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStream_t s);
+// 16-bit float weights (bf16 = 1 / f16 = 0) times B fp32 activation rows through cuBLAS
+// (blas.cu); MLQ_ERR_UNSUPPORTED when unavailable
+int launch_gemm16(const void *W, int bf16, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s);
 // tensor-core GEMM (gemm_tc.cu); MLQ_ERR_UNSUPPORTED for formats/shapes it does not cover
 int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s);
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);

@@ -297,3 +297,23 @@ def test_pinned_host_input(cuda_device, m, shift):
         ho = torch.full((m * n,), float("nan")).pin_memory()
         assert lib.mlq_matmul(wd.data_ptr(), F.Q4_K, hx.data_ptr() + 4 * shift, ho.data_ptr(), n, k, m) == 0
         assert torch.equal(ho, od.cpu())
+
+
+@pytest.mark.parametrize("qt", [F.BF16, F.F16])
+@pytest.mark.parametrize("B", [5, 16, 64])
+def test_16bit_weights_many_rows(cuda_device, qt, B):
+    """bf16 / f16 weights with more than four activation rows (the GPT-OSS attention and head
+    shapes at batch 16 / 64): one GEMM over the matrix, activations as two 16-bit parts."""
+    import torch
+    rng = np.random.default_rng(qt * 100 + B)
+    n, k = 4096, 2880
+    w = F.quantize(qt, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
+    x = rng.standard_normal((B, k)).astype(np.float32)
+    dw, dx = torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()
+    out = torch.full((B, n), float("nan"), device="cuda")
+    lib = cuda_device
+    assert lib.mlq_matmul(dw.data_ptr(), qt, dx.data_ptr(), out.data_ptr(), n, k, B) == 0, \
+        lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    want = O.gemv(w, qt, x, n, k)
+    assert O.rel_l2(out.cpu().numpy(), want) < TOL, O.rel_l2(out.cpu().numpy(), want)
