@@ -495,7 +495,7 @@ def _random_kquant(torch, qt, n_blocks, gen):
     return w.reshape(-1)
 
 
-def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None, with_parity=True):
+def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=None, with_parity=True, use_graph=True):
     import torch.distributed as dist
     from mojollama_b200.ep import EPMoELayer, row_bytes as rbytes
     # the library's kernels, the NCCL exchanges and the timing events all on torch's
@@ -539,13 +539,44 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    # The step issues no host synchronisation (fixed-capacity exchanges), so it is captured
+    # whole -- kernels and NCCL all-to-alls -- into one CUDA graph and replayed; the library
+    # launches on the capture stream while capturing.  Eager timing if capture is refused.
+    graph, graph_err = None, None
+    if use_graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(torch.cuda.current_stream())
+            # bound before the capture starts: rebinding inside it would synchronise the old stream
+            lib.mlq_set_stream(ctypes.c_void_p(cap.cuda_stream))
+            with torch.cuda.graph(g, stream=cap):
+                g_out = step()
+            lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            graph = g
+            graph.replay()
+            torch.cuda.synchronize()
+        except Exception as e:   # keep the eager path
+            graph_err = f"{type(e).__name__}: {e}"[:200]
+            graph = None
+            lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            torch.cuda.synchronize()
+    ok = torch.tensor([0 if graph is None else 1], device="cuda")
+    if world > 1:   # every rank takes the same path (the collectives must match)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if graph is not None and int(ok.item()) == 0:
+        graph = None
     if world > 1:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     h0 = time.perf_counter()
     for _ in range(steps):
-        out = step()
+        if graph is not None:
+            graph.replay()
+            out = g_out
+        else:
+            out = step()
     host_ms = (time.perf_counter() - h0) * 1e3 / steps   # host time to issue one step
     b.record()
     torch.cuda.synchronize()
@@ -572,15 +603,20 @@ def run_moe_ep(torch, lib, rank, world, tokens=16, steps=5, warmup=3, layers=Non
         if world > 1:
             dist.all_reduce(res, op=dist.ReduceOp.MAX)
         parity = {"check": "expert-parallel layer 0 vs the same layer with all experts on one GPU, same tokens, "
-                           "every rank (max over ranks)",
+                           "every rank (max over ranks; eager)",
                   "ep_parity_rel_l2": float(res[0].item()), "dispatch_combine_bit_exact": res[1].item() == 0.0,
                   "tolerance": 1e-3, "ok": float(res[0].item()) <= 1e-3}
         del alone, full0
+    used_graph = graph is not None
+    if graph is not None:
+        del graph, g_out   # a graph holding NCCL work is released before the process group goes
+        torch.cuda.synchronize()
     return {"workload": f"config-3 MoE FFN stack: {L} layers, {E} experts top-{k} (renormalised), FF {FF}, "
                         f"Q4_K gate/up + Q6_K down, experts split over {world} GPU(s), fixed-capacity NCCL "
                         f"all-to-all (no host synchronisation in a step)",
             "tokens_per_rank": tokens, "tok_s": round(world * tokens / (t / 1e3), 1), "ms_per_step": round(t, 3),
             "expert_bytes_per_rank": L * el * exp_bytes, "scaling": "weak", "outputs_finite": finite,
+            "cuda_graph": used_graph, **({"graph_error": graph_err} if graph_err else {}),
             "parity": parity,
             "host_issue_ms_per_step": round(host_ms, 3)}
 
