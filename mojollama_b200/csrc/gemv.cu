@@ -1642,6 +1642,32 @@ __device__ __forceinline__ void seg_row_dot(const uint8_t *row, const XPlanes &x
     }
 }
 
+// the same for a gate row and an up row at once: each activation slice is loaded once
+// for both (the pair's rows share their input)
+template <int QT, int MC, bool A16>
+__device__ __forceinline__ void seg_row_dot2(const uint8_t *row_a, const uint8_t *row_b, const XPlanes &xp, int B,
+                                             int U, int GS, int gl, float (&acc)[MC], float (&acc2)[MC]) {
+    for (int u = gl; u < U; u += GS) {
+        W<QT> wa, wb;
+        if constexpr (A16) {
+            wa.decode_a16(row_a, u);
+            wb.decode_a16(row_b, u);
+        } else {
+            wa.decode(row_a, u);
+            wb.decode(row_b, u);
+        }
+#pragma unroll
+        for (int m = 0; m < MC; m++) {
+            if (m < B) {
+                XU<QT> xu;
+                load_xu<QT>(xp, m, u, xu);
+                acc[m] += wa.dot(xu);
+                acc2[m] += wb.dot(xu);
+            }
+        }
+    }
+}
+
 template <int QT, int MC, bool A16>
 __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_seg(SegArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1733,22 +1759,20 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_seg(SegArgs a) {
             float acc[MC];
 #pragma unroll
             for (int m = 0; m < MC; m++) acc[m] = 0.0f;
-            if (v) seg_row_dot<QT, MC, A16>(ra + (size_t)r * a.row_bytes, xp, a.B, U, GS, gl, acc);
-#pragma unroll
-            for (int m = 0; m < MC; m++) {
-                if (m < a.B) {
-                    for (int o = GS >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-                }
-            }
             if (a.pair) {
                 float acc2[MC];
 #pragma unroll
                 for (int m = 0; m < MC; m++) acc2[m] = 0.0f;
-                if (v) seg_row_dot<QT, MC, A16>(rb2 + (size_t)r * a.row_bytes, xp, a.B, U, GS, gl, acc2);
+                if (v)
+                    seg_row_dot2<QT, MC, A16>(ra + (size_t)r * a.row_bytes, rb2 + (size_t)r * a.row_bytes, xp, a.B,
+                                              U, GS, gl, acc, acc2);
 #pragma unroll
                 for (int m = 0; m < MC; m++) {
                     if (m < a.B) {
-                        for (int o = GS >> 1; o > 0; o >>= 1) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                        for (int o = GS >> 1; o > 0; o >>= 1) {
+                            acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                            acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                        }
                     }
                 }
                 if (gl == 0 && v) {   // h = silu(g) * u, exact (cengine_batch_instr.c:1465)
@@ -1760,7 +1784,16 @@ __global__ void __launch_bounds__(kFastThreads, 1) k_gemv_seg(SegArgs a) {
                         }
                     }
                 }
-            } else if (gl == 0 && v) {
+            } else {
+                if (v) seg_row_dot<QT, MC, A16>(ra + (size_t)r * a.row_bytes, xp, a.B, U, GS, gl, acc);
+#pragma unroll
+                for (int m = 0; m < MC; m++) {
+                    if (m < a.B) {
+                        for (int o = GS >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                    }
+                }
+            }
+            if (!a.pair && gl == 0 && v) {
                 const float *res = a.res[sg];
                 float *out = a.out[sg];
 #pragma unroll
