@@ -47,14 +47,15 @@ __device__ __forceinline__ long long kv_offset(const KVView &kv, int b, int t) {
 constexpr int kTile = 32;          // positions per shared-memory tile
 constexpr int kAttnThreads = 128;
 
-// smem: q [rep][HD], K tile [kTile][HD+1], V tile [kTile][HD], p [rep][kTile]
+// smem: q [rep][HD], K tile [kTile][HD+1], V tile [kTile][HD], p [rep][kTile], m / l / c
+// [rep], and with a fused RoPE the new k / v rows of this CTA's KV head [2][HD]
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__restrict__ q, KVView kv,
                                                               const int *__restrict__ seq_lens, int seq_len_scalar,
                                                               int nh, int nkh, int window, float scale,
                                                               int chunk, float *__restrict__ out,
                                                               float *__restrict__ part_ml, float *__restrict__ part_acc,
-                                                              uint8_t *__restrict__ planes) {
+                                                              uint8_t *__restrict__ planes, AttnRope rp) {
     extern __shared__ float sm[];
     pdl_wait();   // q, the KV rows and the split scratch follow earlier kernels
     pdl_trigger();
@@ -72,9 +73,34 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
     float *ms = ps + rep * kTile;                    // rep running max
     float *ls = ms + rep;                            // rep running sum
     float *cs = ls + rep;                            // rep correction factor of this tile
+    float *nk = cs + rep;                            // fused RoPE: new k row of head g [HD]
+    float *nv = nk + HD;                             //             new v row [HD]
     const int tid = threadIdx.x;
-    for (int i = tid; i < rep * HD; i += blockDim.x)
-        qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i] * scale;
+    const int p_new = rp.pos ? rp.pos[b] : -1;
+    if (rp.pos) {
+        // q heads g*rep.. and the new k row of head g, rotated as k_rope_kv does, then q scaled
+        const int hd2 = rp.rope_dim / 2, row = nkh * HD;
+        for (int i = tid; i < rep * HD; i += blockDim.x) qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i];
+        for (int d = tid; d < HD; d += blockDim.x) {
+            nk[d] = rp.k_new[(size_t)b * row + (size_t)g * HD + d];
+            nv[d] = rp.v_new[(size_t)b * row + (size_t)g * HD + d];
+        }
+        __syncthreads();
+        const float *cst = rp.cos_t + (size_t)p_new * hd2, *snt = rp.sin_t + (size_t)p_new * hd2;
+        for (int t = tid; t < (rep + 1) * hd2; t += blockDim.x) {
+            const int hh = t / hd2, j = t - hh * hd2;
+            float *w = hh < rep ? qs + hh * HD : nk;
+            const float c = cst[j], sv = snt[j];
+            const float a0 = w[j], a1 = w[j + hd2];
+            w[j] = a0 * c - a1 * sv;
+            w[j + hd2] = a1 * c + a0 * sv;
+        }
+        __syncthreads();
+        for (int i = tid; i < rep * HD; i += blockDim.x) qs[i] *= scale;
+    } else {
+        for (int i = tid; i < rep * HD; i += blockDim.x)
+            qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i] * scale;
+    }
     for (int h = tid; h < rep; h += blockDim.x) {
         ms[h] = -INFINITY;
         ls[h] = 0.0f;
@@ -88,11 +114,40 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
 
     const float *kb = kv_kbase(kv, b);
     const float *vb = kv_vbase(kv, b);
+    if (rp.pos && p_new >= t0 && p_new < t1) {
+        // this CTA's positions include the new one: store its k / v rows of head g
+        const long long off = kv_offset(kv, b, p_new);
+        if (off >= 0) {
+            const int row = nkh * HD;
+            float *kc = const_cast<float *>(kb), *vc = const_cast<float *>(vb);
+            float *mkb = rp.mk ? rp.mk[b] : nullptr, *mvb = rp.mv ? rp.mv[b] : nullptr;
+            size_t moff = 0;
+            bool mirror = mkb && mvb && kv.table;
+            if (mirror) {
+                const int page = kv.table[(size_t)b * kv.table_stride + p_new / kv.page_size];
+                mirror = page >= 0 && page < 1024;
+                moff = ((size_t)kv.layer * 1024 * 64 + (size_t)page * 64 + (p_new % kv.page_size)) * row;
+            }
+            for (int d = tid; d < HD; d += blockDim.x) {
+                kc[off + (long long)g * HD + d] = nk[d];
+                vc[off + (long long)g * HD + d] = nv[d];
+                if (mirror) {
+                    mkb[moff + (size_t)g * HD + d] = nk[d];
+                    mvb[moff + (size_t)g * HD + d] = nv[d];
+                }
+            }
+        }
+    }
     for (int base = t0; base < t1; base += kTile) {
         const int nt = min(kTile, t1 - base);
         // stage K and V rows of this tile (coalesced along HD)
         for (int i = tid; i < nt * HD; i += blockDim.x) {
             const int t = i / HD, d = i - t * HD;
+            if (base + t == p_new) {   // fused RoPE: the new row from shared memory
+                ks[t * (HD + 1) + d] = nk[d];
+                vs[t * HD + d] = nv[d];
+                continue;
+            }
             if (kv.tail_k && base + t == sl - 1) {
                 const size_t o = (size_t)b * kv.tail_stride + (size_t)g * HD + d;
                 ks[t * (HD + 1) + d] = kv.tail_k[o];
@@ -241,7 +296,7 @@ __global__ void k_kv_write(KVView kv, float *k_base, float *v_base, const float 
 }
 
 static size_t attn_smem(int rep, int hd) {
-    return sizeof(float) * ((size_t)rep * hd + kTile * (hd + 1) + kTile * hd + rep * kTile + 3 * rep);
+    return sizeof(float) * ((size_t)rep * hd + kTile * (hd + 1) + kTile * hd + rep * kTile + 3 * rep + 2 * hd);
 }
 
 // q [B][nh][hd] -> out [B][nh][hd]; scratch holds the split partials when needed
@@ -265,8 +320,16 @@ static cudaError_t attn_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block
 
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
                        int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
-                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes) {
+                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes,
+                       const AttnRope *rope) {
     if (planes && ((nh / (nkh > 0 ? nkh : 1)) * hd % 32 || hd % 32)) planes = nullptr;   // caller encodes
+    AttnRope rp;
+    if (rope && rope->pos) {
+        if (!kv.pool_seq || rope->rope_dim > hd || rope->rope_dim % 2 || rope->rope_dim <= 0 || !rope->cos_t ||
+            !rope->sin_t || !rope->k_new || !rope->v_new)
+            return MLQ_ERR_UNSUPPORTED;
+        rp = *rope;
+    }
     const LaunchEnv *env = launch_env();
     if (!env) return MLQ_ERR_NO_DEVICE;
     if (nkh <= 0 || nh % nkh) { set_error(MLQ_ERR_ARG, "attention: n_head %d not a multiple of n_kv_head %d", nh, nkh); return MLQ_ERR_ARG; }
@@ -298,7 +361,7 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
         }                                                                                                     \
         if (!MLQ_CUDA(attn_launch_pdl(k_attn_decode<HD_>, grid, dim3(kAttnThreads), smem, s, q, kv,           \
                                       seq_lens_dev, seq_len_scalar, nh, nkh, window, scale, chunk1, out,      \
-                                      part_ml, part_acc, planes)))                                            \
+                                      part_ml, part_acc, planes, rp)))                                        \
             return MLQ_ERR_CUDA;                                                                              \
     } break;
     switch (hd) {

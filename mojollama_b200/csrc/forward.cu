@@ -596,25 +596,46 @@ static int enqueue_step(const BC *c, const ModelPlan *P, const StepBufs &sb, con
             KVView kv{nullptr, nullptr, sb.tab, tab_w, (long long)ps * kvrow, ps, kvrow, sb.pools, layer_stride, l,
                       kv0->pt._n_layers};
             kv.n_pages = kv0->pt.n_pages;
-            // RoPE + KV store (+ KVBlock mirror) in one launch when the row layout allows
-            const bool fused_kv = rc == MLQ_OK && inner == NH * HD && kvrow == NKH * HD &&
-                                  launch_rope_kv(q, k, v, B, NH, NKH, HD, rope_dim, sb.pos, P->cos_t, P->sin_t, kv,
-                                                 sb.mk, sb.mv, s) == MLQ_OK;
-            if (!fused_kv) {
-                MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
-                MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
-                MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, sb.pos, 0, B, kvrow, s));
-                if (rc == MLQ_OK) {
-                    k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(
-                        sb.mk, sb.mv, sb.tab, tab_w, sb.pos, k, v, kvrow, ps, l);
-                    count_launch();
-                }
-            }
             // the attention output also as packed rows for the o projection (decode path)
             const bool o_fast = fast && !lp.wattng && lp.no == N;
             const bool att_packed = o_fast && inner == NH * HD && attn_packs_output(NH, NKH, HD);
-            MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, lp.window, scale, att, sb.attn_scr,
-                                       sb.attn_sb, s, att_packed ? sb.pa : nullptr));
+            // RoPE + KV store (+ KVBlock mirror) inside the attention kernel when the row layout
+            // allows; otherwise in one launch before it, or as separate steps
+            bool attn_done = false;
+            if (rc == MLQ_OK && inner == NH * HD && kvrow == NKH * HD && !getenv("MLQ_NO_ATTN_ROPE")) {
+                AttnRope ar;
+                ar.pos = sb.pos;
+                ar.cos_t = P->cos_t;
+                ar.sin_t = P->sin_t;
+                ar.rope_dim = rope_dim;
+                ar.k_new = k;
+                ar.v_new = v;
+                ar.mk = sb.mk;
+                ar.mv = sb.mv;
+                const int ra = launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, lp.window, scale, att,
+                                                  sb.attn_scr, sb.attn_sb, s, att_packed ? sb.pa : nullptr, &ar);
+                if (ra != MLQ_ERR_UNSUPPORTED) {
+                    rc = ra;
+                    attn_done = true;
+                }
+            }
+            if (!attn_done) {
+                const bool fused_kv = rc == MLQ_OK && inner == NH * HD && kvrow == NKH * HD &&
+                                      launch_rope_kv(q, k, v, B, NH, NKH, HD, rope_dim, sb.pos, P->cos_t, P->sin_t,
+                                                     kv, sb.mk, sb.mv, s) == MLQ_OK;
+                if (!fused_kv) {
+                    MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+                    MLQ_TRY(launch_rope_neox(k, B, kvrow, NKH, HD, sb.pos, 0, P->cos_t, P->sin_t, rope_dim, s));
+                    MLQ_TRY(launch_kv_write(kv, nullptr, nullptr, k, v, sb.pos, 0, B, kvrow, s));
+                    if (rc == MLQ_OK) {
+                        k_kv_mirror<<<dim3(grid1(kvrow) > 16 ? 16 : grid1(kvrow), B), 256, 0, s>>>(
+                            sb.mk, sb.mv, sb.tab, tab_w, sb.pos, k, v, kvrow, ps, l);
+                        count_launch();
+                    }
+                }
+                MLQ_TRY(launch_attn_decode(q, kv, sb.len, 0, attn_len, B, NH, NKH, HD, lp.window, scale, att,
+                                           sb.attn_scr, sb.attn_sb, s, att_packed ? sb.pa : nullptr));
+            }
             bool o_done = false;
             if (o_fast && rc == MLQ_OK) {   // x = res + W_o att
                 if (!att_packed) MLQ_TRY(launch_encode_packed(att, nullptr, nullptr, B, inner, sb.pa, s));

@@ -139,11 +139,27 @@ struct KVView {
     int n_pages = 0;
 };
 
+// The decode step's RoPE and KV store done by the attention kernel itself (instead of a
+// k_rope_kv launch before it): q [B][nh][hd] and the new rows k_new / v_new [B][nkh*hd]
+// arrive unrotated; each CTA rotates its own query heads and its KV head's new k row (NeoX
+// halves of the first rope_dim dims at position pos[b]), and the CTA whose positions
+// include pos[b] stores the new k / v rows of its head into the cache and, when mk / mv are
+// given, into the KVBlock mirrors.  Requires per-sequence pools (kv.pool_seq).
+struct AttnRope {
+    const int *pos = nullptr;
+    const float *cos_t = nullptr, *sin_t = nullptr;
+    int rope_dim = 0;
+    const float *k_new = nullptr, *v_new = nullptr;
+    float *const *mk = nullptr;
+    float *const *mv = nullptr;
+};
 // planes non-null: the output rows [B][nh*hd] also written as packed activation rows, when
-// attn_packs_output(nh, nkh, hd) (otherwise planes is ignored)
+// attn_packs_output(nh, nkh, hd) (otherwise planes is ignored); rope non-null: see AttnRope
+// (MLQ_ERR_UNSUPPORTED when its requirements are not met; nothing is launched then)
 int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev, int seq_len_scalar,
                        int max_seq_len, int B, int nh, int nkh, int hd, int window, float scale, float *out,
-                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes = nullptr);
+                       float *scratch, size_t scratch_bytes, cudaStream_t s, uint8_t *planes = nullptr,
+                       const AttnRope *rope = nullptr);
 inline bool attn_packs_output(int nh, int nkh, int hd) { return nkh > 0 && (nh / nkh) * hd % 32 == 0 && hd % 32 == 0; }
 int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
                     const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s);
