@@ -38,7 +38,7 @@
 namespace mlq {
 
 constexpr int kTcRows = 128;      // MMA M
-constexpr int kTcThreads = 256;   // 8 warps
+constexpr int kTcThreads = 512;   // 16 warps decode; warps 0-7 also read the accumulators out
 constexpr int kTcKC = 256;        // K elements per chunk
 constexpr int kTcAtomBytes = 16384;   // one 64-wide K atom of the A tile: 128 rows x 128 B
 
@@ -111,7 +111,24 @@ template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22, 
 template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144, raw_row = chunk_bytes; };
 template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176, raw_row = chunk_bytes; };
 // a super-block and the 2 bytes before it when it starts 2 bytes past a 4-byte boundary
-template <> struct TcFmt<MLQ_Q6_K> { static constexpr int chunk_bytes = 210, raw_row = 212; };
+// (Q6_K: the 16-byte-aligned window around the super-block, at most 240 bytes)
+template <> struct TcFmt<MLQ_Q6_K> { static constexpr int chunk_bytes = 210, raw_row = 240; };
+
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// Two codes of the packed bytes q (selector 0x5140: bytes 0, 1; 0x7362: bytes 2, 3) made
+// exact fp16 integers by placing them under the exponent byte 0x64 (1024 + code), less
+// `off`, then ds * v - dm in fp32 and rounded to fp16: the same arithmetic as the scalar
+// form, at 3.5 instructions per weight instead of a byte load, shifts and a conversion each.
+__device__ __forceinline__ uint32_t codes_h2(uint32_t q, uint32_t sel, __half2 off, float ds, float dm) {
+    const float2 f = __half22float2(__hsub2(u2h2(__byte_perm(q, 0x64646464u, sel)), off));
+    return h22u(__floats2half2_rn(ds * f.x - dm, ds * f.y - dm));
+}
+__device__ __forceinline__ uint32_t codes_h2(uint32_t q, uint32_t sel, __half2 off, float ds) {
+    const float2 f = __half22float2(__hsub2(u2h2(__byte_perm(q, 0x64646464u, sel)), off));
+    return h22u(__floats2half2_rn(ds * f.x, ds * f.y));
+}
 
 // elements 8j .. 8j+7 of a 256-element row chunk (raw bytes `c`), the GGUF dequantization
 // of each format in fp32, rounded to fp16
@@ -143,18 +160,24 @@ __device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
     } else if constexpr (QT == MLQ_Q6_K) {
         // ggml's dequantize_row_q6_K: element n = 128h + 32k + l (l < 32) is
         // d * sc[8h + l/16 + 2k] * ((ql nibble | qh bits 2k..2k+1 << 4) - 32), the ql byte
-        // being ql[64h + l + 32(k & 1)] (low nibble for k < 2) and the qh byte qh[32h + l]
+        // being ql[64h + l + 32(k & 1)] (low nibble for k < 2) and the qh byte qh[32h + l];
+        // the 8 elements' codes are assembled four to a word
         const int n0 = 8 * j, h = n0 >> 7, k = (n0 >> 5) & 3, l0 = n0 & 31;
         const float ds = f16_at(c + 208) * (float)(int8_t)c[192 + 8 * h + (l0 >> 4) + 2 * k];
-        const uint8_t *ql = c + 64 * h + 32 * (k & 1), *qh = c + 128 + 32 * h;
+        uint32_t ql[2], qh[2];
+        load_words<2>(c + 64 * h + 32 * (k & 1) + l0, ql);
+        load_words<2>(c + 128 + 32 * h + l0, qh);
+        const __half2 off = u2h2(0x64206420u);   // 1056 = 1024 + 32
+        uint32_t o[4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int l = l0 + i;
-            const int lo = (k < 2) ? (ql[l] & 0xF) : (ql[l] >> 4);
-            const int q = lo | (((qh[l] >> (2 * k)) & 3) << 4);
-            v[i] = ds * (float)(q - 32);
+        for (int w = 0; w < 2; w++) {
+            const uint32_t lo = (k < 2 ? ql[w] : ql[w] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t q = lo | (((qh[w] >> (2 * k)) & 0x03030303u) << 4);
+            o[2 * w] = codes_h2(q, 0x5140u, off, ds);
+            o[2 * w + 1] = codes_h2(q, 0x7362u, off, ds);
         }
-    } else {   // Q4_K, Q5_K: one 256-element super-block per chunk
+        return make_uint4(o[0], o[1], o[2], o[3]);
+    } else {   // Q4_K, Q5_K: one 256-element super-block per chunk (16-byte aligned)
         const int sub = j >> 2, g = sub >> 1, l0 = (j & 3) * 8;
         const uint8_t *sc = c + 4;
         int s, m;
@@ -166,14 +189,19 @@ __device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
             m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
         }
         const float ds = f16_at(c) * (float)s, dm = f16_at(c + 2) * (float)m;
-        const uint8_t *qs = c + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int l = l0 + i;
-            int q = (sub & 1) ? (qs[l] >> 4) : (qs[l] & 0xF);
-            if constexpr (QT == MLQ_Q5_K) q += ((c[16 + l] >> sub) & 1) << 4;
-            v[i] = ds * (float)q - dm;
+        const uint2 qs = *reinterpret_cast<const uint2 *>(c + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g + l0);
+        uint32_t qw[2] = {qs.x, qs.y};
+        if constexpr (QT == MLQ_Q5_K) {
+            const uint2 qh = *reinterpret_cast<const uint2 *>(c + 16 + l0);
+            qw[0] = ((sub & 1 ? qw[0] >> 4 : qw[0]) & 0x0F0F0F0Fu) | (((qh.x >> sub) & 0x01010101u) << 4);
+            qw[1] = ((sub & 1 ? qw[1] >> 4 : qw[1]) & 0x0F0F0F0Fu) | (((qh.y >> sub) & 0x01010101u) << 4);
+        } else {
+            qw[0] = (sub & 1 ? qw[0] >> 4 : qw[0]) & 0x0F0F0F0Fu;
+            qw[1] = (sub & 1 ? qw[1] >> 4 : qw[1]) & 0x0F0F0F0Fu;
         }
+        const __half2 off = u2h2(0x64006400u);   // 1024
+        return make_uint4(codes_h2(qw[0], 0x5140u, off, ds, dm), codes_h2(qw[0], 0x7362u, off, ds, dm),
+                          codes_h2(qw[1], 0x5140u, off, ds, dm), codes_h2(qw[1], 0x7362u, off, ds, dm));
     }
     __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
     __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
@@ -189,8 +217,6 @@ __device__ __forceinline__ uint4 deq8(const uint8_t *c, int j) {
 // An integer code c in 0..255 becomes the fp16 value 1024 + c by placing it under the
 // exponent byte 0x64 (PRMT); subtracting 1024 + bias (HSUB2) is exact, and the one HMUL2
 // by the block scale rounds the exact product once -- the same fp16 as rounding d*q.
-__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
-__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
 __device__ __forceinline__ void bytes_to_h2(uint32_t u, __half2 bias, __half2 d, uint32_t &lo, uint32_t &hi) {
     lo = h22u(__hmul2(__hsub2(u2h2(__byte_perm(u, 0x64646464u, 0x5140)), bias), d));
@@ -323,17 +349,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         const int r0 = rt * kTcRows;
         uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
         if constexpr (QT == MLQ_Q6_K) {
-            // 4-byte pieces from the boundary at or below the super-block: 53 when it starts
-            // 2 bytes past one, else 52 pieces and its last 2 bytes (d) by a plain load, so
-            // that nothing past the super-block is read
-            for (int p = tid; p < kTcRows * 53; p += kTcThreads) {
-                const int r = p / 53, i = p - r * 53;
+            // 16-byte pieces of the aligned window around the super-block (row pitches are
+            // multiples of 16, the super-blocks only 2-byte aligned); a piece past the end of
+            // the matrix (the last row's last super-block) is copied byte by byte up to it
+            const uint8_t *w_end = a.W + (size_t)a.n_rows * a.row_bytes;
+            for (int p = tid; p < kTcRows * 15; p += kTcThreads) {
+                const int r = p / 15, i = p - r * 15;
                 if (r0 + r >= a.n_rows) continue;
                 const uint8_t *src = a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210;
-                const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 3;
-                const uint8_t *base = src - off;
-                if (i < 52 || off) cp_async4(raw + r * 212 + 4 * i, base + 4 * i);
-                else *reinterpret_cast<uint16_t *>(raw + r * 212 + 208) = *reinterpret_cast<const uint16_t *>(src + 208);
+                const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 15;
+                if (16 * i >= (int)off + 210) continue;   // the window needs ceil((off + 210) / 16) pieces
+                const uint8_t *piece = src - off + 16 * i;
+                uint8_t *dst = raw + r * 240 + 16 * i;
+                if (piece + 16 <= w_end) cp_async16(dst, piece);
+                else
+                    for (int b = 0; b < 16 && piece + b < w_end; b++) dst[b] = piece[b];
             }
         } else {
             for (int p = tid; p < kTcRows * pieces; p += kTcThreads) {
@@ -390,7 +420,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                         if constexpr (QT == MLQ_Q6_K) {
                             const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
                                                   (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
-                            h = deq8<QT>(raw + r * 212 + (src & 3), j);
+                            h = deq8<QT>(raw + r * 240 + (src & 15), j);
                         } else {
                             h = deq8<QT>(raw + r * chunk_bytes, j);
                         }
@@ -418,12 +448,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         // epilogue: accumulators -> scaled fp32 outputs
         if (!wait_mma()) break;
         tc_fence_after();
-        const int q = warp & 3, half = warp >> 2;
+        // warps 0-7: TMEM lane quarter warp % 4 (weight rows), column half warp / 4
+        const int q = warp & 3, half = (warp >> 2) & 1;
+        const bool reader = warp < 8;
         const int rl = 32 * q + (tid & 31), row = r0 + rl;
         constexpr int per = NT / 2;   // columns per warp
         if (a.n_splits == 1) {
 #pragma unroll
-            for (int c0 = 0; c0 < per; c0 += 8) {
+            for (int c0 = 0; c0 < per && reader; c0 += 8) {
                 float v[8];
                 tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
 #pragma unroll
@@ -439,7 +471,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             const size_t tile = (size_t)rt * gridDim.y + blockIdx.y;
             float *pt = a.part + (tile * a.n_splits + sp) * (size_t)(NT * kTcRows);
 #pragma unroll
-            for (int c0 = 0; c0 < per; c0 += 8) {
+            for (int c0 = 0; c0 < per && reader; c0 += 8) {
                 float v[8];
                 tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
 #pragma unroll
@@ -450,7 +482,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             __syncthreads();
             if (tid == 0) *flag_last = (atomicAdd(a.counters + tile, 1) == a.n_splits - 1) ? 1 : 0;
             __syncthreads();
-            if (*flag_last) {
+            if (*flag_last && reader) {
                 __threadfence();
                 const float *p0 = a.part + tile * a.n_splits * (size_t)(NT * kTcRows);
                 for (int c = half * per; c < half * per + per; c++) {
