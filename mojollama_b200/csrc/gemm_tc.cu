@@ -254,6 +254,75 @@ __device__ __forceinline__ void deq_block32(const uint8_t *bp, uint4 (&o)[4]) {
     }
 }
 
+// Elements 32t .. 32t+31 of a K-quant super-block (chunk bytes `c`) into four 16-byte fp16
+// chunks: the sub-block's scales are unpacked once for its 32 weights (deq8 unpacks them
+// for every 8), the codes come in as whole words.  Same arithmetic as deq8.
+//   Q4_K / Q5_K: t is the 32-element sub-block (one scale / min pair); c 16-byte aligned
+//   Q6_K: t = 4h + k, elements 128h + 32k + l (l < 32), two scales (l < 16, l >= 16);
+//         c 2-byte aligned at worst
+template <int QT>
+__device__ __forceinline__ void deq32_k(const uint8_t *c, int t, uint4 (&o)[4]) {
+    if constexpr (QT == MLQ_Q6_K) {
+        const int h = t >> 2, k = t & 3;
+        const float d = f16_at(c + 208);
+        const float ds0 = d * (float)(int8_t)c[192 + 8 * h + 2 * k];
+        const float ds1 = d * (float)(int8_t)c[192 + 8 * h + 1 + 2 * k];
+        uint32_t ql[8], qh[8];
+        load_words<8>(c + 64 * h + 32 * (k & 1), ql);
+        load_words<8>(c + 128 + 32 * h, qh);
+        const __half2 off = u2h2(0x64206420u);   // 1056 = 1024 + 32
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            const uint32_t lo = (k < 2 ? ql[w] : ql[w] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t q = lo | (((qh[w] >> (2 * k)) & 0x03030303u) << 4);
+            const float ds = w < 4 ? ds0 : ds1;
+            const uint32_t a0 = codes_h2(q, 0x5140u, off, ds), a1 = codes_h2(q, 0x7362u, off, ds);
+            if (w & 1) {
+                o[w >> 1].z = a0;
+                o[w >> 1].w = a1;
+            } else {
+                o[w >> 1].x = a0;
+                o[w >> 1].y = a1;
+            }
+        }
+    } else {   // Q4_K, Q5_K
+        const int sub = t, g = sub >> 1;
+        const uint8_t *sc = c + 4;
+        int s, m;
+        if (sub < 4) {
+            s = sc[sub] & 63;
+            m = sc[sub + 4] & 63;
+        } else {
+            s = (sc[sub + 4] & 0xF) | ((sc[sub - 4] >> 6) << 4);
+            m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
+        }
+        const float ds = f16_at(c) * (float)s, dm = f16_at(c + 2) * (float)m;
+        const uint4 *qp = reinterpret_cast<const uint4 *>(c + (QT == MLQ_Q4_K ? 16 : 48) + 32 * g);
+        const uint4 q0 = qp[0], q1 = qp[1];
+        uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t hw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if constexpr (QT == MLQ_Q5_K) {
+            const uint4 h0 = *reinterpret_cast<const uint4 *>(c + 16), h1 = *reinterpret_cast<const uint4 *>(c + 32);
+            const uint32_t hh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+            for (int w = 0; w < 8; w++) hw[w] = ((hh[w] >> sub) & 0x01010101u) << 4;
+        }
+        const __half2 off = u2h2(0x64006400u);   // 1024
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            const uint32_t q = ((sub & 1 ? qw[w] >> 4 : qw[w]) & 0x0F0F0F0Fu) | hw[w];
+            const uint32_t a0 = codes_h2(q, 0x5140u, off, ds, dm), a1 = codes_h2(q, 0x7362u, off, ds, dm);
+            if (w & 1) {
+                o[w >> 1].z = a0;
+                o[w >> 1].w = a1;
+            } else {
+                o[w >> 1].x = a0;
+                o[w >> 1].y = a1;
+            }
+        }
+    }
+}
+
 // byte offset of the 16-byte chunk (row r, K group j of 8) in a [rows][256] fp16 operand
 // stored as four 64-wide K atoms of `atom_bytes` each
 __device__ __forceinline__ uint32_t sw128_off(int r, int j, int atom_bytes) {
@@ -284,10 +353,15 @@ struct TcSmem {
     static constexpr int b_atom = NT * 128;
     static constexpr int b_bytes = 4 * b_atom;                                // NT * 512
     static constexpr int raw_bytes = kTcRows * TcFmt<QT>::raw_row;
+    // copy stages (raw weights + activation atoms): as many as fit beside the A operand, up
+    // to 4, so that the copies run up to 3 chunks ahead of the decode
+    static constexpr int stage_pair = b_bytes + raw_bytes;
+    static constexpr int n_st_fit = (227 * 1024 - a_bytes - 64 - 1024 - 16) / stage_pair;
+    static constexpr int n_st = n_st_fit > 4 ? 4 : n_st_fit;
     static constexpr int off_a = 0;
-    static constexpr int off_b = a_bytes;                                     // 2 stages
-    static constexpr int off_raw = off_b + 2 * b_bytes;                       // 2 stages
-    static constexpr int off_bar = (off_raw + 2 * raw_bytes + 15) / 16 * 16;
+    static constexpr int off_b = a_bytes;                                     // n_st stages
+    static constexpr int off_raw = off_b + n_st * b_bytes;                    // n_st stages
+    static constexpr int off_bar = (off_raw + n_st * raw_bytes + 15) / 16 * 16;
     static constexpr int total = off_bar + 64 + 1024;                         // + alignment slack
 };
 
@@ -387,14 +461,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         const int r0 = rt * kTcRows;
         const int c_begin = sp * a.chunks_per_split;
         const int c_end = min(n_chunks, c_begin + a.chunks_per_split);
-        issue_copies(rt, c_begin, 0);
-        for (int ci = c_begin; ci < c_end; ci++) {
-            const int st = (ci - c_begin) & 1;
-            // the previous chunk's MMAs read A and the other B stage: wait before reuse
-            if (!wait_mma()) break;
-            if (ci + 1 < c_end) issue_copies(rt, ci + 1, st ^ 1);
+        constexpr int NS = S::n_st;
+        static_assert(NS >= 2, "two copy stages must fit");
+        // chunks c_begin .. c_begin + NS - 2 in flight before the first decode (one commit
+        // group each, empty past the end)
+        for (int c = 0; c < NS - 1; c++) {
+            if (c_begin + c < c_end) issue_copies(rt, c_begin + c, c);
             else cp_async_commit();
-            cp_async_wait<1>();
+        }
+        for (int ci = c_begin; ci < c_end; ci++) {
+            const int st = (ci - c_begin) % NS;
+            // the previous chunk's MMAs read A and the stage refilled next: wait before reuse
+            if (!wait_mma()) break;
+            if (ci + NS - 1 < c_end) issue_copies(rt, ci + NS - 1, (ci + NS - 1 - c_begin) % NS);
+            else cp_async_commit();
+            cp_async_wait<NS - 1>();   // chunk ci's group is complete
             __syncthreads();
             // decode this chunk's raw weights into the swizzled fp16 A operand
             const uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
@@ -411,6 +492,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                     }
 #pragma unroll
                     for (int c = 0; c < 4; c++) *reinterpret_cast<uint4 *>(sa + sw128_off(r, 4 * b + c, kTcAtomBytes)) = o[c];
+                }
+            } else if constexpr (QT == MLQ_Q4_K || QT == MLQ_Q5_K || QT == MLQ_Q6_K) {
+                // thread item (row r, 32-element group t): lanes of a warp take 4 rows x 8 groups
+                for (int p = tid; p < kTcRows * 8; p += kTcThreads) {
+                    const int r = p >> 3, t = p & 7;
+                    uint4 o[4];
+                    if (r0 + r < a.n_rows) {
+                        if constexpr (QT == MLQ_Q6_K) {
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                                                  (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
+                            deq32_k<QT>(raw + r * 240 + (src & 15), t, o);
+                        } else {
+                            deq32_k<QT>(raw + r * chunk_bytes, t, o);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 4; c++) o[c] = make_uint4(0, 0, 0, 0);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; c++) *reinterpret_cast<uint4 *>(sa + sw128_off(r, 4 * t + c, kTcAtomBytes)) = o[c];
                 }
             } else {
                 for (int p = tid; p < kTcRows * 32; p += kTcThreads) {
