@@ -46,10 +46,11 @@ constexpr int kTcAtomBytes = 16384;   // one 64-wide K atom of the A tile: 128 r
 // x [M][K] fp32 -> xh [Mp][K] fp16 of x / s_t, s_t = 2^ceil(log2(max|x_t|)) (1 for a zero
 // row); rows M..Mp-1 are zero with scale 0.
 __global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh, float *__restrict__ scale, int M,
-                           int K) {
+                           int K, int Kp) {
     __shared__ float sh[32];
     const int t = blockIdx.x;
-    __half *dst = xh + (size_t)t * K;
+    __half *dst = xh + (size_t)t * Kp;
+    for (int i = K + threadIdx.x; i < Kp; i += blockDim.x) dst[i] = __float2half_rn(0.0f);   // K padding
     if (t >= M) {
         for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = __float2half_rn(0.0f);
         if (threadIdx.x == 0) scale[t] = 0.0f;
@@ -104,10 +105,15 @@ template <int QT> struct TcFmt;
 //   chunk_bytes  GGUF bytes of one row's 256-element chunk
 //   raw_row      shared-memory bytes per row of a raw stage
 template <int QT> struct TcFmt { static constexpr int chunk_bytes = 0, raw_row = 0; };
-template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34, raw_row = chunk_bytes; };
-template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18, raw_row = chunk_bytes; };
-template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20, raw_row = chunk_bytes; };
-template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22, raw_row = chunk_bytes; };
+// (32-element block formats: the 16-byte-aligned window around the chunk's blocks, whose
+// rows need not start on 16 bytes and whose last chunk may hold fewer than 8 blocks)
+template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34, raw_row = 288; };
+template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18, raw_row = 160; };
+template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20, raw_row = 176; };
+template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22, raw_row = 192; };
+template <int QT> constexpr bool tc_block32() {
+    return QT == MLQ_Q8_0 || QT == MLQ_Q4_0 || QT == MLQ_Q4_1 || QT == MLQ_Q5_0;
+}
 template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144, raw_row = chunk_bytes; };
 template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176, raw_row = chunk_bytes; };
 // a super-block and the 2 bytes before it when it starts 2 bytes past a 4-byte boundary
@@ -338,6 +344,8 @@ struct TcArgs {
     int n_rows, K, M;
     long long row_bytes;
     int n_row_tiles;
+    int Kp;                // K rounded up to whole 256-element chunks (the activation row pitch)
+    int win;               // block formats: rows not on 16 bytes or K % 256 != 0 (windowed copies)
     int *status;
     // split-K: work item w = (row tile w / n_splits, K slice w % n_splits of chunks_per_split
     // chunks); with n_splits > 1 each item leaves its partial tile in part and the last item
@@ -381,7 +389,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
     constexpr int chunk_bytes = TcFmt<QT>::chunk_bytes;
     constexpr int pieces = chunk_bytes / 16;
     const int tok0 = blockIdx.y * NT;
-    const int n_chunks = a.K / kTcKC;
+    const int n_chunks = (a.K + kTcKC - 1) / kTcKC;
     (void)n_chunks;
 
     if (warp == 0) {
@@ -439,18 +447,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                 else
                     for (int b = 0; b < 16 && piece + b < w_end; b++) dst[b] = piece[b];
             }
+        } else if (tc_block32<QT>() && a.win) {
+            // the chunk's (up to 8) blocks through 16-byte pieces of their aligned window
+            constexpr int bb = chunk_bytes / 8, np = TcFmt<QT>::raw_row / 16;
+            const int nbc = min(8, a.K / 32 - 8 * ci);
+            const uint8_t *w_end = a.W + (size_t)a.n_rows * a.row_bytes;
+            for (int p = tid; p < kTcRows * np; p += kTcThreads) {
+                const int r = p / np, i = p - r * np;
+                if (r0 + r >= a.n_rows) continue;
+                const uint8_t *src = a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes;
+                const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 15;
+                if (16 * i >= (int)off + nbc * bb) continue;
+                const uint8_t *piece = src - off + 16 * i;
+                uint8_t *dst = raw + r * TcFmt<QT>::raw_row + 16 * i;
+                if (piece + 16 <= w_end) cp_async16(dst, piece);
+                else
+                    for (int b = 0; b < 16 && piece + b < w_end; b++) dst[b] = piece[b];
+            }
         } else {
             for (int p = tid; p < kTcRows * pieces; p += kTcThreads) {
                 const int r = p / pieces, i = p - r * pieces;
                 if (r0 + r < a.n_rows)
-                    cp_async16(raw + r * chunk_bytes + 16 * i,
+                    cp_async16(raw + r * TcFmt<QT>::raw_row + 16 * i,
                                a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
             }
         }
         uint8_t *sb = smem + S::off_b + st * S::b_bytes;
         for (int p = tid; p < NT * 32; p += kTcThreads) {
             const int n = p >> 5, j = p & 31;
-            cp_async16(sb + sw128_off(n, j, S::b_atom), a.xh + (size_t)(tok0 + n) * a.K + (size_t)ci * kTcKC + 8 * j);
+            cp_async16(sb + sw128_off(n, j, S::b_atom), a.xh + (size_t)(tok0 + n) * a.Kp + (size_t)ci * kTcKC + 8 * j);
         }
         cp_async_commit();
     };
@@ -481,11 +506,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             const uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
             if constexpr (QT == MLQ_Q8_0 || QT == MLQ_Q4_0) {
                 constexpr int bb = QT == MLQ_Q8_0 ? 34 : 18;
+                const int nbc = min(8, a.K / 32 - 8 * ci);   // blocks in this chunk (the rest: zeros)
                 for (int p = tid; p < kTcRows * 8; p += kTcThreads) {
                     const int r = p >> 3, b = p & 7;
                     uint4 o[4];
-                    if (r0 + r < a.n_rows) {
-                        deq_block32<QT>(raw + r * chunk_bytes + b * bb, o);
+                    if (r0 + r < a.n_rows && b < nbc) {
+                        const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                                              (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes);
+                        deq_block32<QT>(raw + r * TcFmt<QT>::raw_row + (a.win ? (src & 15) : 0) + b * bb, o);
                     } else {
 #pragma unroll
                         for (int c = 0; c < 4; c++) o[c] = make_uint4(0, 0, 0, 0);
@@ -522,6 +550,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                             const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
                                                   (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
                             h = deq8<QT>(raw + r * 240 + (src & 15), j);
+                        } else if constexpr (tc_block32<QT>()) {   // Q4_1, Q5_0
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                                                  (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes);
+                            if ((j >> 2) < a.K / 32 - 8 * ci)
+                                h = deq8<QT>(raw + r * TcFmt<QT>::raw_row + (a.win ? (src & 15) : 0), j);
                         } else {
                             h = deq8<QT>(raw + r * chunk_bytes, j);
                         }
@@ -667,6 +700,8 @@ bool tc_supported(int qt, const uint8_t *W, int K, long long row_bytes) {
         case MLQ_Q6_K: return K % kTcKC == 0 && ((uintptr_t)W & 3) == 0;
         default: return false;
     }
+    if (qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0)   // any K % 32, 2-byte aligned
+        return K % 32 == 0 && K > 0 && ((uintptr_t)W & 1) == 0;
     return K % kTcKC == 0 && cb % 16 == 0 && row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
 }
 
@@ -707,7 +742,8 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     const LaunchEnv *env = launch_env();
     if (!env) return MLQ_ERR_NO_DEVICE;
     // split K over CTAs when the row tiles alone cannot fill the SMs
-    const int n_row_tiles = (n_rows + kTcRows - 1) / kTcRows, n_chunks = K / kTcKC;
+    const int n_row_tiles = (n_rows + kTcRows - 1) / kTcRows, n_chunks = (K + kTcKC - 1) / kTcKC;
+    const int Kp = n_chunks * kTcKC;
     int n_splits = 1;
     if (n_row_tiles * n_tok_tiles < env->num_sms) {
         n_splits = env->num_sms / (n_row_tiles * n_tok_tiles);
@@ -717,7 +753,7 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     const int cps = (n_chunks + n_splits - 1) / n_splits;
     n_splits = (n_chunks + cps - 1) / cps;
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-    const size_t xh_bytes = al((size_t)Mp * K * sizeof(__half));
+    const size_t xh_bytes = al((size_t)Mp * Kp * sizeof(__half));
     const size_t xs_bytes = al((size_t)Mp * sizeof(float));
     const size_t n_tiles = (size_t)n_row_tiles * n_tok_tiles;
     const size_t cnt_bytes = n_splits > 1 ? al(n_tiles * sizeof(int)) : 0;
@@ -729,10 +765,12 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     int *counters = n_splits > 1 ? (int *)(scr + xh_bytes + xs_bytes) : nullptr;
     float *part = n_splits > 1 ? (float *)(scr + xh_bytes + xs_bytes + cnt_bytes) : nullptr;
     if (counters && !MLQ_CUDA(cudaMemsetAsync(counters, 0, n_tiles * sizeof(int), s))) return MLQ_ERR_CUDA;
-    k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K);
+    k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K, Kp);
     count_launch();
     if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
-    TcArgs a{W, xh, xs, out, n_rows, K, M, rb, n_row_tiles, env->d_status, n_splits, cps, part, counters};
+    const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0;
+    const int win = block32 && (K % kTcKC != 0 || rb % 16 != 0 || ((uintptr_t)W & 15) != 0);
+    TcArgs a{W, xh, xs, out, n_rows, K, M, rb, n_row_tiles, Kp, win, env->d_status, n_splits, cps, part, counters};
     switch (qt) {
         case MLQ_Q8_0: return launch_tc_q<MLQ_Q8_0>(a, NT, n_tok_tiles, s);
         case MLQ_Q4_0: return launch_tc_q<MLQ_Q4_0>(a, NT, n_tok_tiles, s);
