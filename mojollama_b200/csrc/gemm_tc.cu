@@ -111,8 +111,9 @@ template <> struct TcFmt<MLQ_Q8_0> { static constexpr int chunk_bytes = 8 * 34, 
 template <> struct TcFmt<MLQ_Q4_0> { static constexpr int chunk_bytes = 8 * 18, raw_row = 160; };
 template <> struct TcFmt<MLQ_Q4_1> { static constexpr int chunk_bytes = 8 * 20, raw_row = 176; };
 template <> struct TcFmt<MLQ_Q5_0> { static constexpr int chunk_bytes = 8 * 22, raw_row = 192; };
+template <> struct TcFmt<MLQ_MXFP4> { static constexpr int chunk_bytes = 8 * 17, raw_row = 160; };
 template <int QT> constexpr bool tc_block32() {
-    return QT == MLQ_Q8_0 || QT == MLQ_Q4_0 || QT == MLQ_Q4_1 || QT == MLQ_Q5_0;
+    return QT == MLQ_Q8_0 || QT == MLQ_Q4_0 || QT == MLQ_Q4_1 || QT == MLQ_Q5_0 || QT == MLQ_MXFP4;
 }
 template <> struct TcFmt<MLQ_Q4_K> { static constexpr int chunk_bytes = 144, raw_row = chunk_bytes; };
 template <> struct TcFmt<MLQ_Q5_K> { static constexpr int chunk_bytes = 176, raw_row = chunk_bytes; };
@@ -229,8 +230,43 @@ __device__ __forceinline__ void bytes_to_h2(uint32_t u, __half2 bias, __half2 d,
     hi = h22u(__hmul2(__hsub2(u2h2(__byte_perm(u, 0x64646464u, 0x7362)), bias), d));
 }
 
+// Four E2M1 codes (one per byte, 0..15) as fp16 values of gguf's doubled table
+// {0, 1, 2, 3, 4, 6, 8, 12} with the sign bit 3: only the high byte of each fp16 value is
+// nonzero, built bytewise: magnitude m >= 2 is (1 + m % 2 / 2) * 2^(m / 2) -> exponent byte
+// 0x3C + 4 (m / 2) + 2 (m % 2); m = 1 -> 0x3C; m = 0 -> 0 (+0 for code 8 too, as the table).
+__device__ __forceinline__ void e2m1_codes_h2(uint32_t c, float scale, uint32_t &h01, uint32_t &h23) {
+    const uint32_t m = c & 0x07070707u;
+    const uint32_t e = (m >> 1) & 0x03030303u, man = m & 0x01010101u;
+    uint32_t hb = ((e << 2) | (man << 1)) + 0x3C3C3C3Cu;
+    const uint32_t small = __vcmpeq4(e, 0u), zero = __vcmpeq4(m, 0u);
+    hb = (hb & ~small) | (small & (man * 0x3Cu));
+    hb |= ((c & 0x08080808u) << 4) & ~zero;
+    const float2 f01 = __half22float2(u2h2(__byte_perm(hb, 0u, 0x1404u)));
+    const float2 f23 = __half22float2(u2h2(__byte_perm(hb, 0u, 0x3424u)));
+    h01 = h22u(__floats2half2_rn(f01.x * scale, f01.y * scale));
+    h23 = h22u(__floats2half2_rn(f23.x * scale, f23.y * scale));
+}
+
 template <int QT>
 __device__ __forceinline__ void deq_block32(const uint8_t *bp, uint4 (&o)[4]) {
+    if constexpr (QT == MLQ_MXFP4) {
+        // GGUF MXFP4 block {e, qs[16]}: element j < 16 is the low nibble of qs[j], j >= 16 the
+        // high nibble of qs[j-16]; value table[code] * 2^(e - 128) (gguf-py e8m0_to_fp32_half)
+        const float sc = e8m0_half(bp[0]);
+        uint32_t w[4];
+        load_words<4>(bp + 1, w);
+        uint32_t l[8], h[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            e2m1_codes_h2(w[i] & 0x0F0F0F0Fu, sc, l[2 * i], l[2 * i + 1]);
+            e2m1_codes_h2((w[i] >> 4) & 0x0F0F0F0Fu, sc, h[2 * i], h[2 * i + 1]);
+        }
+        o[0] = make_uint4(l[0], l[1], l[2], l[3]);
+        o[1] = make_uint4(l[4], l[5], l[6], l[7]);
+        o[2] = make_uint4(h[0], h[1], h[2], h[3]);
+        o[3] = make_uint4(h[4], h[5], h[6], h[7]);
+        return;
+    }
     const __half2 d = __half2half2(*reinterpret_cast<const __half *>(bp));   // 2-byte aligned
     if constexpr (QT == MLQ_Q8_0) {
         uint32_t w[8];
@@ -504,8 +540,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             __syncthreads();
             // decode this chunk's raw weights into the swizzled fp16 A operand
             const uint8_t *raw = smem + S::off_raw + st * S::raw_bytes;
-            if constexpr (QT == MLQ_Q8_0 || QT == MLQ_Q4_0) {
-                constexpr int bb = QT == MLQ_Q8_0 ? 34 : 18;
+            if constexpr (QT == MLQ_Q8_0 || QT == MLQ_Q4_0 || QT == MLQ_MXFP4) {
+                constexpr int bb = chunk_bytes / 8;
                 const int nbc = min(8, a.K / 32 - 8 * ci);   // blocks in this chunk (the rest: zeros)
                 for (int p = tid; p < kTcRows * 8; p += kTcThreads) {
                     const int r = p >> 3, b = p & 7;
@@ -697,11 +733,13 @@ bool tc_supported(int qt, const uint8_t *W, int K, long long row_bytes) {
         case MLQ_Q5_0: cb = TcFmt<MLQ_Q5_0>::chunk_bytes; break;
         case MLQ_Q4_K: cb = TcFmt<MLQ_Q4_K>::chunk_bytes; break;
         case MLQ_Q5_K: cb = TcFmt<MLQ_Q5_K>::chunk_bytes; break;
+        case MLQ_MXFP4: cb = TcFmt<MLQ_MXFP4>::chunk_bytes; break;
         case MLQ_Q6_K: return K % kTcKC == 0 && ((uintptr_t)W & 3) == 0;
         default: return false;
     }
     if (qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0)   // any K % 32, 2-byte aligned
         return K % 32 == 0 && K > 0 && ((uintptr_t)W & 1) == 0;
+    if (qt == MLQ_MXFP4) return K % 32 == 0 && K > 0;   // read bytewise: no alignment
     return K % kTcKC == 0 && cb % 16 == 0 && row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
 }
 
@@ -768,8 +806,9 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K, Kp);
     count_launch();
     if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
-    const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0;
-    const int win = block32 && (K % kTcKC != 0 || rb % 16 != 0 || ((uintptr_t)W & 15) != 0);
+    const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0 || qt == MLQ_MXFP4;
+    // (MXFP4 chunks are 136 bytes: never all on 16-byte boundaries)
+    const int win = block32 && (qt == MLQ_MXFP4 || K % kTcKC != 0 || rb % 16 != 0 || ((uintptr_t)W & 15) != 0);
     TcArgs a{W, xh, xs, out, n_rows, K, M, rb, n_row_tiles, Kp, win, env->d_status, n_splits, cps, part, counters};
     switch (qt) {
         case MLQ_Q8_0: return launch_tc_q<MLQ_Q8_0>(a, NT, n_tok_tiles, s);
@@ -779,6 +818,7 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
         case MLQ_Q4_K: return launch_tc_q<MLQ_Q4_K>(a, NT, n_tok_tiles, s);
         case MLQ_Q5_K: return launch_tc_q<MLQ_Q5_K>(a, NT, n_tok_tiles, s);
         case MLQ_Q6_K: return launch_tc_q<MLQ_Q6_K>(a, NT, n_tok_tiles, s);
+        case MLQ_MXFP4: return launch_tc_q<MLQ_MXFP4>(a, NT, n_tok_tiles, s);
         default: return MLQ_ERR_UNSUPPORTED;
     }
 }

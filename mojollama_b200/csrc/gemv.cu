@@ -788,25 +788,15 @@ static int tc_min_m() {
     return v;
 }
 
-static int tc_q6k_min() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("MLQ_TC_Q6K_MIN");
-        v = e ? atoi(e) : 32;
-        if (v < 1) v = 1;
-    }
-    return v;
-}
-
 template <int QT>
 static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s) {
-    // Q6_K on small matrices from tc_q6k_min() rows (MLQ_TC_Q6K_MIN, default 32): at 16 its
-    // tensor-core decode (per element, 210-byte super-blocks in 4-byte pieces) measured
-    // slower than two passes of the 8-row GEMV there; on large ones (an output head) the two
-    // passes re-stream the matrix and the GEMM wins from 16 (config-3 head at 16 tokens:
-    // step 19.5 -> 17.7 ms)
-    const int q6k_from = n_rows >= 16384 ? tc_min_m() : tc_q6k_min();
-    const int tc_from = QT == MLQ_Q6_K && tc_min_m() > 0 && tc_min_m() < q6k_from ? q6k_from : tc_min_m();
+    // every format the tensor-core GEMM takes, from tc_min_m() rows (Q6_K included since its
+    // decode packs four codes to a word: 2048 x 2048 at 16 rows 65 -> 21 us against two
+    // passes of the 8-row GEMV; config-3 step at 16 tokens 20.3 -> 16.3 ms).  MXFP4 on a
+    // large matrix keeps its block-scaled passes below 32 rows (151936 x 2048 at 16 rows:
+    // 147 us in four passes, 318 us through the fp16 decode of the GEMM)
+    int tc_from = tc_min_m();
+    if (QT == MLQ_MXFP4 && n_rows >= 16384 && tc_from > 0 && tc_from < 32) tc_from = 32;
     if (tc_from > 0 && B >= tc_from) {
         const int rc = launch_gemm_tc(W, QT, x, out, n_rows, K, B, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;

@@ -17,7 +17,7 @@ from oracle import ops as O
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
-TC_FORMATS = [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.Q4_K, F.Q5_K, F.Q6_K]
+TC_FORMATS = [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.Q4_K, F.Q5_K, F.Q6_K, F.MXFP4]
 
 
 def _mm(lib, torch, w, qt, x, n, k):
@@ -45,13 +45,13 @@ def test_tc_gemm_matches_oracle(cuda_device, qt, n, k, m):
     assert O.rel_l2(got, want) < TOL, O.rel_l2(got, want)
 
 
-@pytest.mark.parametrize("qt", [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0], ids=lambda q: F.NAMES[q])
+@pytest.mark.parametrize("qt", [F.Q8_0, F.Q4_0, F.Q4_1, F.Q5_0, F.MXFP4], ids=lambda q: F.NAMES[q])
 @pytest.mark.parametrize("n,k,m", [(2880, 2880, 16), (300, 2880, 64), (129, 96, 16), (257, 1312, 40)])
 def test_tc_gemm_block32_ragged_k(cuda_device, qt, n, k, m):
     """32-element block formats with K not a multiple of the 256-element chunk (the last
     chunk partly empty) and rows that do not start on 16 bytes (K = 2880: 3060-byte Q8_0
-    rows), down to a single partial chunk (K = 96); the last row's last piece ends at the
-    end of the weight buffer."""
+    rows; MXFP4's 17-byte blocks), down to a single partial chunk (K = 96); the last row's
+    last piece ends at the end of the weight buffer."""
     import torch
     rng = np.random.default_rng(qt * 7 + n + k)
     w = F.quantize(qt, (rng.standard_normal(n * k) * 0.02).astype(np.float32))
