@@ -157,6 +157,12 @@ static size_t moe_grouped_layout(MoeGroupedScratch *m, uint8_t *base, int gqt, i
     t.ph = take(grouped_packed_bytes(R, n_ff));
     t.g = (float *)take(sizeof(float) * (size_t)R * n_ff);
     t.u = (float *)take(sizeof(float) * (size_t)R * n_ff);
+    t.xg = (__half *)take(tc_grouped_xh_bytes(R, N));
+    t.xd = (__half *)take(tc_grouped_xh_bytes(R, n_ff));
+    t.xgl = (__half *)take(tc_grouped_xh_bytes(R, N));
+    t.xdl = (__half *)take(tc_grouped_xh_bytes(R, n_ff));
+    t.sg = (float *)take(sizeof(float) * (size_t)R);
+    t.sd = (float *)take(sizeof(float) * (size_t)R);
     if (m) *m = t;
     return o;
 }
@@ -168,6 +174,20 @@ size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_
 void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff,
                        int N) {
     moe_grouped_layout(&m, base, gqt, uqt, dqt, R, E, n_ff, N);
+}
+
+// The tensor-core path for MXFP4 experts when the rows average at least MLQ_MOE_TC_ROWS per
+// expert (default 0: off).  It is the more exact of the two (weights exact, activations as
+// fp16 part + residual) but not yet the faster: at config 4, 64 tokens (8 rows per expert)
+// its 128-row tiles ran at about the grouped GEMV's speed, 44.3 against 42.2 ms per step,
+// bound like the dense tensor-core GEMM by the per-chunk decode / MMA / barrier sequence.
+static bool moe_tc_wanted(int R, int E) {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_MOE_TC_ROWS");
+        v = e ? atoi(e) : 0;
+    }
+    return v > 0 && (long long)R >= (long long)v * E;
 }
 
 int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uint8_t *uexp, const uint8_t *dexp,
@@ -184,6 +204,31 @@ int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
     const bool pair = gqt == uqt;
     const int chunks = (R + 7) / 8 + (E < R ? E : R);
     void *items[3] = {m.items[0], m.items[1], m.items[2]};
+    // (MXFP4 experts only: their E2M1 x 2^e weights are exact in fp16 relative to each chunk's
+    // largest block, and the activations enter as an fp16 part plus its fp16 residual, so the
+    // products are as exact as fp32 sums make them; K-quant weights would be rounded to fp16)
+    if (gqt == MLQ_MXFP4 && uqt == MLQ_MXFP4 && dqt == MLQ_MXFP4 && moe_tc_wanted(R, E) &&
+        tc_grouped_supported(gqt, gexp, gstride, N) &&
+        tc_grouped_supported(uqt, uexp, ustride, N) && tc_grouped_supported(dqt, dexp, dstride, n_ff)) {
+        // many rows per expert: 128-row tiles on the tensor cores (fp16 operands, fp32 sums)
+        const int tg = (n_ff + 127) / 128, td = (N + 127) / 128;
+        int tt[3] = {pair ? 2 * tg : tg, pair ? td : tg, td};
+        int rc = launch_group_plan(eid, R, E, n_lists, items, tt, m.spos, m.srow, m.nitem, s, eid_stride);
+        if (rc == MLQ_OK) rc = launch_rows_to_f16(x, nullptr, m.srow, row_div, x_stride > 0 ? x_stride : N, 0.0f, R, N,
+                                                  m.xg, m.xgl, m.sg, s);
+        if (rc == MLQ_OK)
+            rc = launch_gemm_tc_grouped(gqt, gexp, gstride, pair ? uexp : nullptr, ustride, n_ff, N, items[0], m.nitem,
+                                        chunks * tt[0], m.xg, m.xgl, m.sg, m.g, pair ? m.u : nullptr, nullptr, s);
+        if (rc == MLQ_OK && !pair)
+            rc = launch_gemm_tc_grouped(uqt, uexp, ustride, nullptr, 0, n_ff, N, items[1], m.nitem + 1, chunks * tt[1],
+                                        m.xg, m.xgl, m.sg, m.u, nullptr, nullptr, s);
+        if (rc == MLQ_OK) rc = launch_rows_to_f16(m.g, m.u, nullptr, 1, n_ff, clamp, R, n_ff, m.xd, m.xdl, m.sd, s);
+        if (rc == MLQ_OK)
+            rc = launch_gemm_tc_grouped(dqt, dexp, dstride, nullptr, 0, N, n_ff, items[n_lists - 1],
+                                        m.nitem + n_lists - 1, chunks * tt[n_lists - 1], m.xd, m.xdl, m.sd, y, nullptr,
+                                        m.srow, s);
+        return rc;
+    }
     int rc = launch_group_plan(eid, R, E, n_lists, items, tiles, m.spos, m.srow, m.nitem, s, eid_stride);
     if (rc == MLQ_OK) rc = launch_encode_packed(x, nullptr, m.srow, R, N, m.px, s, row_div, 80.0f, x_stride);
     GroupedCall gc{};

@@ -86,6 +86,65 @@ __global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh,
     if (threadIdx.x == 0) scale[t] = s;
 }
 
+// Sorted row p of grouped experts' input as fp16 / s_p, s_p a power of two as in k_x_to_f16:
+// x[rows[p] / row_div] (row pitch x_stride; rows null: row p), or with x2 the SwiGLU of
+// sorted gate and up rows, silu(clamp(x[p], +-clamp)) * x2[p] (the grouped GEMV's GroupRows
+// arithmetic).  Columns K..Kp-1 are zero.
+__global__ void k_rows_to_f16(const float *__restrict__ x, const float *__restrict__ x2, const int *__restrict__ rows,
+                              int row_div, int x_stride, float clamp, int K, int Kp, __half *__restrict__ xh,
+                              __half *__restrict__ xl, float *__restrict__ scale) {
+    __shared__ float sh[32];
+    const int p = blockIdx.x;
+    int r = rows ? __ldg(rows + p) : p;
+    if (rows && row_div > 1) r /= row_div;
+    const float *src = x + (size_t)r * x_stride;
+    const float *src2 = x2 ? x2 + (size_t)p * x_stride : nullptr;
+    auto val = [&](int k) {
+        float v = __ldg(src + k);
+        if (src2) {
+            const float g = fminf(fmaxf(v, -clamp), clamp);
+            v = (g / (1.0f + expf(-g))) * __ldg(src2 + k);
+        }
+        return v;
+    };
+    __half *dst = xh + (size_t)p * Kp;
+    __half *dlo = xl ? xl + (size_t)p * Kp : nullptr;
+    for (int i = K + threadIdx.x; i < Kp; i += blockDim.x) {
+        dst[i] = __float2half_rn(0.0f);
+        if (dlo) dlo[i] = __float2half_rn(0.0f);
+    }
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(val(i)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) sh[0] = v;
+    }
+    __syncthreads();
+    amax = sh[0];
+    float sc;
+    if (!(amax <= 3.402823466e38f)) sc = __int_as_float(0x7fc00000);
+    else if (amax == 0.0f) sc = 1.0f;
+    else {
+        int e;
+        frexpf(amax, &e);
+        sc = ldexpf(1.0f, e);
+    }
+    const float inv = 1.0f / sc;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = val(i) * inv;
+        const __half h = __float2half_rn(v);
+        dst[i] = h;
+        if (dlo) dlo[i] = __float2half_rn(v - __half2float(h));   // the rounding residual
+    }
+    if (threadIdx.x == 0) scale[p] = sc;
+}
+
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = nt, M = 128
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int nt) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
@@ -248,11 +307,19 @@ __device__ __forceinline__ void e2m1_codes_h2(uint32_t c, float scale, uint32_t 
 }
 
 template <int QT>
-__device__ __forceinline__ void deq_block32(const uint8_t *bp, uint4 (&o)[4]) {
+__device__ __forceinline__ void deq_block32(const uint8_t *bp, uint4 (&o)[4], int emax = -1) {
     if constexpr (QT == MLQ_MXFP4) {
         // GGUF MXFP4 block {e, qs[16]}: element j < 16 is the low nibble of qs[j], j >= 16 the
-        // high nibble of qs[j-16]; value table[code] * 2^(e - 128) (gguf-py e8m0_to_fp32_half)
-        const float sc = e8m0_half(bp[0]);
+        // high nibble of qs[j-16]; value table[code] * 2^(e - 128) (gguf-py e8m0_to_fp32_half).
+        // With emax, the largest block exponent of the row within the chunk, the block is stored
+        // as table[code] * 2^(e - emax) (at most 12; fp16 holds it exactly down to 2^-24 of the
+        // chunk's largest block) and the chunk's product is scaled by 2^(emax - 128) in fp32
+        // after the MMAs, so no block scale leaves fp16's range (a block more than 2^126 below
+        // the chunk's largest is flushed to zero)
+        const int e = bp[0];
+        float sc;
+        if (emax < 0) sc = e8m0_half((uint32_t)e);
+        else sc = e - emax < -126 ? 0.0f : __uint_as_float((uint32_t)(127 + e - emax) << 23);
         uint32_t w[4];
         load_words<4>(bp + 1, w);
         uint32_t l[8], h[8];
@@ -389,6 +456,20 @@ struct TcArgs {
     int n_splits, chunks_per_split;
     float *part;
     int *counters;
+    // grouped experts (items set): work item = one 128-row tile of one expert's matrix against
+    // up to 8 of its sorted activation rows (k_group_plan's items {e, m0, mc, tile}); tiles from
+    // tiles_per_expert on are the second matrix (W2 / out2); xh / xs are indexed by sorted row,
+    // results go to row out_rows[p] (identity if null) of out; no K split
+    const int4 *items;
+    const int *n_items_dev;
+    long long estride, estride2;
+    const uint8_t *W2;
+    float *out2;
+    int tiles_per_expert;
+    const int *out_rows;
+    // grouped: the activation rows' fp16 residuals (x / s - hi); token-tile rows 0-7 take the
+    // item's rows from xh, rows 8-15 the same rows from xlo, and the two sums are added
+    const __half *xlo;
 };
 
 template <int QT, int NT>
@@ -400,13 +481,15 @@ struct TcSmem {
     // copy stages (raw weights + activation atoms): as many as fit beside the A operand, up
     // to 4, so that the copies run up to 3 chunks ahead of the decode
     static constexpr int stage_pair = b_bytes + raw_bytes;
-    static constexpr int n_st_fit = (227 * 1024 - a_bytes - 64 - 1024 - 16) / stage_pair;
+    static constexpr int n_st_fit = (227 * 1024 - a_bytes - 64 - 1024 - 4096 - 1024 - 16) / stage_pair;
     static constexpr int n_st = n_st_fit > 4 ? 4 : n_st_fit;
     static constexpr int off_a = 0;
     static constexpr int off_b = a_bytes;                                     // n_st stages
     static constexpr int off_raw = off_b + n_st * b_bytes;                    // n_st stages
     static constexpr int off_bar = (off_raw + n_st * raw_bytes + 15) / 16 * 16;
-    static constexpr int total = off_bar + 64 + 1024;                         // + alignment slack
+    static constexpr int off_cx = off_bar + 64;                               // [2][128] ints
+    static constexpr int off_lo = off_cx + 1024;                              // [128][8] floats
+    static constexpr int total = off_lo + 4096 + 1024;                        // + alignment slack
 };
 
 template <int QT, int NT>
@@ -421,10 +504,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::off_bar + 16);
     volatile int *flag_last = reinterpret_cast<volatile int *>(smem + S::off_bar + 20);
     const int tid = threadIdx.x, warp = tid >> 5;
-    constexpr int ncols = NT < 32 ? 32 : NT;
+    // MXFP4: per-chunk products (two accumulator buffers) scaled into fp32 registers
+    constexpr bool kPerChunk = QT == MLQ_MXFP4;
+    constexpr int ncols = kPerChunk ? (2 * NT < 32 ? 32 : 2 * NT) : (NT < 32 ? 32 : NT);
+    int *cx = reinterpret_cast<int *>(smem + S::off_cx);   // [2][128] chunk row exponents
+    float *lo_tile = reinterpret_cast<float *>(smem + S::off_lo);   // grouped: residual sums [128][8]
+    float accr[kPerChunk ? NT / 2 : 1];                     // warps 0-7: row rl, their NT/2 columns
     constexpr int chunk_bytes = TcFmt<QT>::chunk_bytes;
     constexpr int pieces = chunk_bytes / 16;
-    const int tok0 = blockIdx.y * NT;
+    int tok0 = blockIdx.y * NT;        // first activation row of the work item
+    int mtok = NT;                     // grouped: the item's rows (the rest of the tile: zeros)
+    const uint8_t *Wb = a.W;           // the item's weight matrix
+    float *outp = a.out;
+    const bool grouped = a.items != nullptr;
     const int n_chunks = (a.K + kTcKC - 1) / kTcKC;
     (void)n_chunks;
 
@@ -470,11 +562,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             // 16-byte pieces of the aligned window around the super-block (row pitches are
             // multiples of 16, the super-blocks only 2-byte aligned); a piece past the end of
             // the matrix (the last row's last super-block) is copied byte by byte up to it
-            const uint8_t *w_end = a.W + (size_t)a.n_rows * a.row_bytes;
+            const uint8_t *w_end = Wb + (size_t)a.n_rows * a.row_bytes;
             for (int p = tid; p < kTcRows * 15; p += kTcThreads) {
                 const int r = p / 15, i = p - r * 15;
                 if (r0 + r >= a.n_rows) continue;
-                const uint8_t *src = a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210;
+                const uint8_t *src = Wb + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210;
                 const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 15;
                 if (16 * i >= (int)off + 210) continue;   // the window needs ceil((off + 210) / 16) pieces
                 const uint8_t *piece = src - off + 16 * i;
@@ -487,11 +579,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             // the chunk's (up to 8) blocks through 16-byte pieces of their aligned window
             constexpr int bb = chunk_bytes / 8, np = TcFmt<QT>::raw_row / 16;
             const int nbc = min(8, a.K / 32 - 8 * ci);
-            const uint8_t *w_end = a.W + (size_t)a.n_rows * a.row_bytes;
+            const uint8_t *w_end = Wb + (size_t)a.n_rows * a.row_bytes;
             for (int p = tid; p < kTcRows * np; p += kTcThreads) {
                 const int r = p / np, i = p - r * np;
                 if (r0 + r >= a.n_rows) continue;
-                const uint8_t *src = a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes;
+                const uint8_t *src = Wb + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes;
                 const uintptr_t off = reinterpret_cast<uintptr_t>(src) & 15;
                 if (16 * i >= (int)off + nbc * bb) continue;
                 const uint8_t *piece = src - off + 16 * i;
@@ -505,20 +597,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                 const int r = p / pieces, i = p - r * pieces;
                 if (r0 + r < a.n_rows)
                     cp_async16(raw + r * TcFmt<QT>::raw_row + 16 * i,
-                               a.W + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
+                               Wb + (size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes + 16 * i);
             }
         }
         uint8_t *sb = smem + S::off_b + st * S::b_bytes;
         for (int p = tid; p < NT * 32; p += kTcThreads) {
             const int n = p >> 5, j = p & 31;
-            cp_async16(sb + sw128_off(n, j, S::b_atom), a.xh + (size_t)(tok0 + n) * a.Kp + (size_t)ci * kTcKC + 8 * j);
+            const bool lo = grouped && n >= 8;
+            const int nr = lo ? n - 8 : n;
+            if (nr < mtok)
+                cp_async16(sb + sw128_off(n, j, S::b_atom),
+                           (lo ? a.xlo : a.xh) + (size_t)(tok0 + nr) * a.Kp + (size_t)ci * kTcKC + 8 * j);
+            else   // grouped: rows past the item's own are zeros
+                *reinterpret_cast<uint4 *>(sb + sw128_off(n, j, S::b_atom)) = make_uint4(0, 0, 0, 0);
         }
         cp_async_commit();
     };
 
-    const int n_items = a.n_row_tiles * a.n_splits;
+    // MXFP4: add chunk c's product (its accumulator buffer, complete) times 2^(emax - 128) of
+    // each row into the registers of warps 0-7 (same lane / column split as the epilogue)
+    auto fold_chunk = [&](int c) {
+        if constexpr (kPerChunk) {
+            if (warp < 8) {
+                tc_fence_after();
+                const int q = warp & 3, half = (warp >> 2) & 1, rl = 32 * q + (tid & 31);
+                const float sc = e8m0_half((uint32_t)cx[(c & 1) * kTcRows + rl]);
+#pragma unroll
+                for (int c0 = 0; c0 < NT / 2; c0 += 8) {
+                    float v[8];
+                    tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((c & 1) * NT + half * (NT / 2) + c0), v);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) accr[c0 + i] = fmaf(v[i], sc, accr[c0 + i]);
+                }
+            }
+        }
+    };
+    const int n_items = grouped ? *a.n_items_dev : a.n_row_tiles * a.n_splits;
     for (int wi = blockIdx.x; wi < n_items && !*abort_flag; wi += gridDim.x) {
-        const int rt = wi / a.n_splits, sp = wi - rt * a.n_splits;
+        int rt = wi / a.n_splits, sp = wi - rt * a.n_splits;
+        if (grouped) {
+            const int4 it = a.items[wi];   // {expert, first sorted row, rows, tile}
+            const bool second = it.w >= a.tiles_per_expert;
+            rt = second ? it.w - a.tiles_per_expert : it.w;
+            sp = 0;
+            Wb = (second ? a.W2 : a.W) + (size_t)it.x * (size_t)(second ? a.estride2 : a.estride);
+            outp = second ? a.out2 : a.out;
+            tok0 = it.y;
+            mtok = it.z;
+        }
         const int r0 = rt * kTcRows;
         const int c_begin = sp * a.chunks_per_split;
         const int c_end = min(n_chunks, c_begin + a.chunks_per_split);
@@ -530,10 +656,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
             if (c_begin + c < c_end) issue_copies(rt, c_begin + c, c);
             else cp_async_commit();
         }
+#pragma unroll
+        for (int i = 0; i < (kPerChunk ? NT / 2 : 1); i++) accr[i] = 0.0f;
         for (int ci = c_begin; ci < c_end; ci++) {
             const int st = (ci - c_begin) % NS;
             // the previous chunk's MMAs read A and the stage refilled next: wait before reuse
             if (!wait_mma()) break;
+            if (ci > c_begin) fold_chunk(ci - 1);
             if (ci + NS - 1 < c_end) issue_copies(rt, ci + NS - 1, (ci + NS - 1 - c_begin) % NS);
             else cp_async_commit();
             cp_async_wait<NS - 1>();   // chunk ci's group is complete
@@ -546,10 +675,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                 for (int p = tid; p < kTcRows * 8; p += kTcThreads) {
                     const int r = p >> 3, b = p & 7;
                     uint4 o[4];
-                    if (r0 + r < a.n_rows && b < nbc) {
-                        const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
-                                              (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes);
-                        deq_block32<QT>(raw + r * TcFmt<QT>::raw_row + (a.win ? (src & 15) : 0) + b * bb, o);
+                    const bool valid = r0 + r < a.n_rows && b < nbc;
+                    const uintptr_t src = reinterpret_cast<uintptr_t>(Wb) +
+                                          (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes);
+                    const uint8_t *bp = raw + r * TcFmt<QT>::raw_row + (a.win ? (src & 15) : 0) + b * bb;
+                    int cmax = -1;
+                    if constexpr (QT == MLQ_MXFP4) {
+                        // the row's largest block exponent in this chunk: lanes 8j..8j+7 hold one row
+                        cmax = valid ? (int)bp[0] : 0;
+#pragma unroll
+                        for (int o2 = 1; o2 < 8; o2 <<= 1) cmax = max(cmax, __shfl_xor_sync(0xffffffffu, cmax, o2));
+                        if (b == 0) cx[(ci & 1) * kTcRows + r] = cmax;
+                    }
+                    if (valid) {
+                        deq_block32<QT>(bp, o, cmax);
                     } else {
 #pragma unroll
                         for (int c = 0; c < 4; c++) o[c] = make_uint4(0, 0, 0, 0);
@@ -564,7 +703,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                     uint4 o[4];
                     if (r0 + r < a.n_rows) {
                         if constexpr (QT == MLQ_Q6_K) {
-                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(Wb) +
                                                   (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
                             deq32_k<QT>(raw + r * 240 + (src & 15), t, o);
                         } else {
@@ -583,11 +722,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
                     uint4 h = make_uint4(0, 0, 0, 0);
                     if (r0 + r < a.n_rows) {
                         if constexpr (QT == MLQ_Q6_K) {
-                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(Wb) +
                                                   (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * 210);
                             h = deq8<QT>(raw + r * 240 + (src & 15), j);
                         } else if constexpr (tc_block32<QT>()) {   // Q4_1, Q5_0
-                            const uintptr_t src = reinterpret_cast<uintptr_t>(a.W) +
+                            const uintptr_t src = reinterpret_cast<uintptr_t>(Wb) +
                                                   (uintptr_t)((size_t)(r0 + r) * a.row_bytes + (size_t)ci * chunk_bytes);
                             if ((j >> 2) < a.K / 32 - 8 * ci)
                                 h = deq8<QT>(raw + r * TcFmt<QT>::raw_row + (a.win ? (src & 15) : 0), j);
@@ -607,9 +746,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
 #pragma unroll
                 for (int k = 0; k < kTcKC / 16; k++) {
                     const int kb = k >> 2, k16 = k & 3;
-                    umma_f16(tmem, umma_desc_sw128(a0 + kb * kTcAtomBytes + k16 * 32),
+                    // MXFP4: each chunk into its own accumulator buffer (scaled and added in fp32)
+                    umma_f16(kPerChunk ? tmem + (uint32_t)((ci & 1) * NT) : tmem,
+                             umma_desc_sw128(a0 + kb * kTcAtomBytes + k16 * 32),
                              umma_desc_sw128(b0 + kb * S::b_atom + k16 * 32), idesc,
-                             (ci > c_begin || k > 0) ? 1u : 0u);
+                             ((!kPerChunk && ci > c_begin) || k > 0) ? 1u : 0u);
                 }
                 umma_commit(mma_bar);
             }
@@ -617,20 +758,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
         }
         // epilogue: accumulators -> scaled fp32 outputs
         if (!wait_mma()) break;
+        fold_chunk(c_end - 1);
         tc_fence_after();
         // warps 0-7: TMEM lane quarter warp % 4 (weight rows), column half warp / 4
         const int q = warp & 3, half = (warp >> 2) & 1;
         const bool reader = warp < 8;
         const int rl = 32 * q + (tid & 31), row = r0 + rl;
         constexpr int per = NT / 2;   // columns per warp
-        if (a.n_splits == 1) {
+        if (grouped) {
+            // token columns 0-7 (warps 0-3) hold the rows' sums of the fp16 parts, columns 8-15
+            // (warps 4-7) those of the residuals: the latter pass through shared memory
+            float v[8];
+            if (reader) {
+                if constexpr (kPerChunk) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = accr[i];
+                } else {
+                    tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * 8), v);
+                }
+                if (half == 1) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) lo_tile[rl * 8 + i] = v[i];
+                }
+            }
+            __syncthreads();
+            if (reader && half == 0) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int t = tok0 + i;
+                    if (i < mtok && row < a.n_rows) {
+                        const int o = a.out_rows ? __ldg(a.out_rows + t) : t;
+                        outp[(size_t)o * a.n_rows + row] = (v[i] + lo_tile[rl * 8 + i]) * a.xs[t];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncthreads();
+        } else if (a.n_splits == 1) {
 #pragma unroll
             for (int c0 = 0; c0 < per && reader; c0 += 8) {
                 float v[8];
-                tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+                if constexpr (kPerChunk) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = accr[c0 + i];
+                } else {
+                    tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+                }
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const int t = tok0 + half * per + c0 + i;
+                    const int c = half * per + c0 + i, t = tok0 + c;
                     if (t < a.M && row < a.n_rows) a.out[(size_t)t * a.n_rows + row] = v[i] * a.xs[t];
                 }
             }
@@ -643,7 +819,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
 #pragma unroll
             for (int c0 = 0; c0 < per && reader; c0 += 8) {
                 float v[8];
-                tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+                if constexpr (kPerChunk) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = accr[c0 + i];
+                } else {
+                    tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * per + c0), v);
+                }
 #pragma unroll
                 for (int i = 0; i < 8; i++) pt[(size_t)(half * per + c0 + i) * kTcRows + rl] = v[i];
             }
@@ -819,6 +1000,75 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
         case MLQ_Q5_K: return launch_tc_q<MLQ_Q5_K>(a, NT, n_tok_tiles, s);
         case MLQ_Q6_K: return launch_tc_q<MLQ_Q6_K>(a, NT, n_tok_tiles, s);
         case MLQ_MXFP4: return launch_tc_q<MLQ_MXFP4>(a, NT, n_tok_tiles, s);
+        default: return MLQ_ERR_UNSUPPORTED;
+    }
+}
+
+
+static int tc_kp(int K) { return (K + kTcKC - 1) / kTcKC * kTcKC; }
+
+size_t tc_grouped_xh_bytes(int R, int K) { return (size_t)R * tc_kp(K) * sizeof(__half); }
+
+int launch_rows_to_f16(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp, int R,
+                       int K, __half *xh, __half *xl, float *xs, cudaStream_t s) {
+    if (R <= 0) return MLQ_OK;
+    k_rows_to_f16<<<R, 256, 0, s>>>(x, x2, rows, row_div, x_stride > 0 ? x_stride : K, clamp, K, tc_kp(K), xh, xl,
+                                    xs);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+bool tc_grouped_supported(int qt, const uint8_t *W, long long estride, int K) {
+    const long long rb = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    if (!tc_supported(qt, W, K, rb)) return false;
+    const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0 || qt == MLQ_MXFP4;
+    if (block32) return qt == MLQ_MXFP4 || estride % 2 == 0;
+    return qt == MLQ_Q6_K ? estride % 4 == 0 : estride % 16 == 0;
+}
+
+template <int QT>
+static int launch_tc_grouped_q(const TcArgs &a, int grid, cudaStream_t s) {
+    using S = TcSmem<QT, 16>;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_gemm_tc<QT, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::total)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    k_gemm_tc<QT, 16><<<dim3(grid, 1), kTcThreads, S::total, s>>>(a);
+    count_launch();
+    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// Grouped experts on the tensor cores: k_group_plan's items (tiles of 128 rows, chunks of up
+// to 8 sorted rows) against sorted fp16 rows xh [R][Kp] with scales xs [R]
+int launch_gemm_tc_grouped(int qt, const uint8_t *W, long long estride, const uint8_t *W2, long long estride2,
+                           int n_rows, int K, const void *items, const int *n_items_dev, int n_items_bound,
+                           const __half *xh, const __half *xl, const float *xs, float *out, float *out2,
+                           const int *out_rows, cudaStream_t s) {
+    const LaunchEnv *env = launch_env();
+    if (!xl) return MLQ_ERR_UNSUPPORTED;
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    if (!tc_grouped_supported(qt, W, estride, K) || (W2 && !tc_grouped_supported(qt, W2, estride2, K)))
+        return MLQ_ERR_UNSUPPORTED;
+    const long long rb = (long long)(K / block_elems(qt)) * block_bytes(qt);
+    const int n_row_tiles = (n_rows + kTcRows - 1) / kTcRows, n_chunks = (K + kTcKC - 1) / kTcKC;
+    const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0 || qt == MLQ_MXFP4;
+    const int win = block32 && (qt == MLQ_MXFP4 || K % kTcKC != 0 || rb % 16 != 0 || ((uintptr_t)W & 15) != 0 ||
+                                estride % 16 != 0 || (W2 && (((uintptr_t)W2 & 15) != 0 || estride2 % 16 != 0)));
+    TcArgs a{W, xh, xs, out, n_rows, K, 0, rb, n_row_tiles, tc_kp(K), win, env->d_status, 1, n_chunks, nullptr, nullptr,
+             (const int4 *)items, n_items_dev, estride, estride2, W2, out2, n_row_tiles, out_rows, xl};
+    int grid = env->num_sms < n_items_bound ? env->num_sms : n_items_bound;
+    if (grid < 1) grid = 1;
+    switch (qt) {
+        case MLQ_Q8_0: return launch_tc_grouped_q<MLQ_Q8_0>(a, grid, s);
+        case MLQ_Q4_0: return launch_tc_grouped_q<MLQ_Q4_0>(a, grid, s);
+        case MLQ_Q4_1: return launch_tc_grouped_q<MLQ_Q4_1>(a, grid, s);
+        case MLQ_Q5_0: return launch_tc_grouped_q<MLQ_Q5_0>(a, grid, s);
+        case MLQ_Q4_K: return launch_tc_grouped_q<MLQ_Q4_K>(a, grid, s);
+        case MLQ_Q5_K: return launch_tc_grouped_q<MLQ_Q5_K>(a, grid, s);
+        case MLQ_Q6_K: return launch_tc_grouped_q<MLQ_Q6_K>(a, grid, s);
+        case MLQ_MXFP4: return launch_tc_grouped_q<MLQ_MXFP4>(a, grid, s);
         default: return MLQ_ERR_UNSUPPORTED;
     }
 }

@@ -1,6 +1,7 @@
 // Internal runtime shared by the CUDA translation units of libmojollama_b200.so.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <vector>
 #include <stddef.h>
@@ -102,6 +103,17 @@ int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStrea
 int launch_gemm16(const void *W, int bf16, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s);
 // tensor-core GEMM (gemm_tc.cu); MLQ_ERR_UNSUPPORTED for formats/shapes it does not cover
 int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s);
+// grouped experts on the tensor-core GEMM (csrc/gemm_tc.cu): sorted rows converted to fp16
+// (xh [R][K rounded up to 256] halves, xs [R] power-of-two scales) by launch_rows_to_f16,
+// then one launch per matrix list over k_group_plan's items of 128-row tiles
+size_t tc_grouped_xh_bytes(int R, int K);
+int launch_rows_to_f16(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp, int R,
+                       int K, __half *xh, __half *xl, float *xs, cudaStream_t s);
+bool tc_grouped_supported(int qt, const uint8_t *W, long long estride, int K);
+int launch_gemm_tc_grouped(int qt, const uint8_t *W, long long estride, const uint8_t *W2, long long estride2,
+                           int n_rows, int K, const void *items, const int *n_items_dev, int n_items_bound,
+                           const __half *xh, const __half *xl, const float *xs, float *out, float *out2,
+                           const int *out_rows, cudaStream_t s);
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
 int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
 
@@ -221,6 +233,9 @@ struct MoeGroupedScratch {
     void *items[3];
     uint8_t *px, *ph;
     float *g, *u;
+    __half *xg, *xd;   // tensor-core path: sorted fp16 input rows of gate/up and of down,
+    __half *xgl, *xdl; // their fp16 rounding residuals
+    float *sg, *sd;    // and their power-of-two scales
 };
 size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
 void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);

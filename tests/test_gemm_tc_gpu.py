@@ -61,6 +61,21 @@ def test_tc_gemm_block32_ragged_k(cuda_device, qt, n, k, m):
     assert O.rel_l2(got, want) < TOL, O.rel_l2(got, want)
 
 
+@pytest.mark.parametrize("n,k,m", [(300, 2048, 16), (257, 2880, 64)])
+def test_tc_gemm_mxfp4_any_block_scale(cuda_device, n, k, m):
+    """MXFP4 blocks with random E8M0 scales (2^-128 .. 2^127): every chunk's product is
+    formed relative to its rows' largest block scale and scaled back in fp32, so no scale
+    leaves the fp16 operand's range"""
+    import torch
+    rng = np.random.default_rng(n + k + m)
+    w = F.random_blocks(F.MXFP4, n * k, rng)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    got = _mm(cuda_device, torch, w, F.MXFP4, x, n, k)
+    want = O.gemv(w, F.MXFP4, x, n, k)
+    assert np.isfinite(got).all()
+    assert O.rel_l2(got, want) < TOL, O.rel_l2(got, want)
+
+
 def test_tc_gemm_per_token_scale(cuda_device):
     """Tokens whose magnitudes differ by 1e8 (and a zero token) keep their own precision."""
     import torch

@@ -4,7 +4,8 @@ grouped gate/up and down GEMV) against the oracle: y[r] = down_e(silu(clamp(gate
 quant_kernels_omp.c:2157-2164 for one routed row).  Covers one-row and many-row experts
 (chunks of 8 rows and a ragged rest), unused experts, mixed gate/up types (separate
 launches), short rows (a lane group per weight row), rows whose length is not a multiple of
-128 bytes, and ids outside [0, E) (row left unwritten).  Tolerance: relative L2 <= 1e-3
+128 bytes, and ids outside [0, E) (row left unwritten).  The tensor-core grouped path (off by
+default, MLQ_MOE_TC_ROWS) is checked in a child process.  Tolerance: relative L2 <= 1e-3
 per row."""
 import ctypes
 
@@ -70,6 +71,92 @@ def _skewed(rng, E, R):
 def test_moe_rows_matches_oracle(cuda_device, qts, E, N, FF):
     rng = np.random.default_rng(E * 1000 + N)
     _run(cuda_device, qts, E, N, FF, _skewed(rng, E, 40), seed=N + FF)
+
+
+def _quantized_experts_case(E, N, FF, R, seed):
+    """MXFP4 experts quantized from N(0, 0.02) values (GPT-OSS-like block scales)"""
+    rng = np.random.default_rng(seed)
+    mats = {}
+    for name, rows, cols in (("g", FF, N), ("u", FF, N), ("d", N, FF)):
+        raw = F.quantize(F.MXFP4, (rng.standard_normal(E * rows * cols) * 0.02).astype(np.float32))
+        mats[name] = (raw, F.dequantize(F.MXFP4, raw, E * rows * cols).astype(np.float64).reshape(E, rows, cols))
+    eid = list(rng.integers(0, E, R))
+    return mats, eid
+
+
+def test_moe_rows_many_rows_per_expert(cuda_device):
+    """config-4 batch shape: 32 experts, 8 rows each on average, GPT-OSS width, MXFP4
+    quantized from N(0, 0.02) values, on the default (grouped GEMV) path"""
+    lib = cuda_device
+    E, N, FF, R = 32, 2880, 256, 256
+    mats, eid = _quantized_experts_case(E, N, FF, R, 23)
+    rng = np.random.default_rng(29)
+    x = rng.standard_normal((R, N)).astype(np.float32)
+    dev = {k: torch.from_numpy(v[0]).cuda() for k, v in mats.items()}
+    dx = torch.from_numpy(x).cuda()
+    de = torch.from_numpy(np.asarray(eid, np.int32)).cuda()
+    y = torch.full((R, N), float("nan"), device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    rb = F.row_bytes
+    rc = lib.mlq_moe_rows(F.MXFP4, F.MXFP4, F.MXFP4, vp(dev["g"]), vp(dev["u"]), vp(dev["d"]), rb(F.MXFP4, N) * FF,
+                          rb(F.MXFP4, N) * FF, rb(F.MXFP4, FF) * N, E, vp(de), R, FF, N, vp(dx), vp(y))
+    assert rc == 0, lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    G, U, D = mats["g"][1], mats["u"][1], mats["d"][1]
+    for r, e in enumerate(eid):
+        xr = x[r].astype(np.float64)
+        want = D[e] @ (O.silu_clamped(G[e] @ xr) * (U[e] @ xr))
+        assert O.rel_l2(got[r], want) < TOL, (r, e, O.rel_l2(got[r], want))
+
+
+_TC_CASE = r"""
+import ctypes, os, sys
+import numpy as np, torch
+sys.path.insert(0, os.environ["MLQ_REPO"])
+from oracle import formats as F, ops as O
+from mojollama_b200 import core
+lib = core(); assert lib.mlq_init(0) == 0
+lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+worst = 0.0
+for (E, N, FF, R, seed) in ((32, 2880, 256, 256, 23), (4, 512, 256, 40, 5), (8, 512, 512, 64, 7)):
+    rng = np.random.default_rng(seed)
+    def ex(rows, cols):
+        raw = F.random_blocks(F.MXFP4, E * rows * cols, rng)
+        return raw, F.dequantize(F.MXFP4, raw, E * rows * cols).astype(np.float64).reshape(E, rows, cols)
+    (gr, G), (ur, U), (dr, D) = ex(FF, N), ex(FF, N), ex(N, FF)
+    eid = rng.integers(0, E, R).astype(np.int32)
+    x = rng.standard_normal((R, N)).astype(np.float32)
+    d = [torch.from_numpy(v).cuda() for v in (gr, ur, dr)]
+    dx, de = torch.from_numpy(x).cuda(), torch.from_numpy(eid).cuda()
+    y = torch.full((R, N), float("nan"), device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    rb = F.row_bytes
+    assert lib.mlq_moe_rows(F.MXFP4, F.MXFP4, F.MXFP4, vp(d[0]), vp(d[1]), vp(d[2]), rb(F.MXFP4, N) * FF,
+                            rb(F.MXFP4, N) * FF, rb(F.MXFP4, FF) * N, E, vp(de), R, FF, N, vp(dx), vp(y)) == 0
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for r, e in enumerate(eid):
+        xr = x[r].astype(np.float64)
+        want = D[e] @ (O.silu_clamped(G[e] @ xr) * (U[e] @ xr))
+        worst = max(worst, O.rel_l2(got[r], want))
+print("worst", worst)
+assert worst < 1e-3, worst
+"""
+
+
+def test_moe_rows_tensor_core_path():
+    """The tensor-core grouped path (MLQ_MOE_TC_ROWS=4, read once per process: run in a child
+    process) on MXFP4 blocks with random E8M0 scales, whose products cancel heavily: 128-row
+    tiles against chunks of up to 8 sorted rows, activations as fp16 part + residual, each
+    chunk formed relative to its rows' largest block scale"""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MLQ_MOE_TC_ROWS="4", MLQ_REPO=root)
+    r = subprocess.run([sys.executable, "-c", _TC_CASE], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 def test_moe_rows_single_rows(cuda_device):
