@@ -1289,6 +1289,50 @@ def run_hybrid(torch, lib, stream, rank=0, world=1):
     return {"dec_ms": dec_ms, "pre_ms": pre_ms, "launches": launches}
 
 
+def run_hybrid_profile(args):
+    """Small case for an ncu launch list of config-5 decode steps: `--profile-steps` layers
+    ([3 SSM + 1 GQA] repeating), B = 10, 4 qwen36_batch_forward steps after 2 warm-up steps.
+    Prints the host time to issue one step and the device time of that step."""
+    import time
+
+    import torch
+    from mojollama_b200 import core
+    from mojollama_b200.kernels import load_kernels
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    stream = torch.cuda.Stream()
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    L = args.profile_steps
+    m = build_hybrid(torch, L)
+    lib.mlq_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    call = HybridCall(m, L)
+    fn = load_kernels().cengine.qwen36_batch_forward
+    B, V = Q5["B"], Q5["V"]
+    d_logits = torch.empty(B * V, device="cuda")
+    d_tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+    ws = torch.empty(12 * B * 8192 + 8, device="cuda")
+    torch.cuda.synchronize()
+    host_ms, dev_ms = [], []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for t in range(6):
+            stream.synchronize()
+            e0.record(stream)
+            t0 = time.perf_counter()
+            call(fn, d_tok.data_ptr(), B, d_logits.data_ptr(), ws.data_ptr())
+            t1 = time.perf_counter()
+            e1.record(stream)
+            call.kv_lens += 1
+            assert lib.mlq_argmax(ctypes.c_void_p(d_logits.data_ptr()), B, V, ctypes.c_void_p(d_tok.data_ptr())) == 0
+            stream.synchronize()
+            if t >= 2:
+                host_ms.append((t1 - t0) * 1e3)
+                dev_ms.append(e0.elapsed_time(e1))
+    print(json.dumps({"hybrid_profile_layers": L, "host_issue_ms": [round(x, 3) for x in host_ms],
+                      "device_ms": [round(x, 3) for x in dev_ms]}))
+    return 0
+
+
 def hybrid_line(res, world):
     c = Q5
     B, G, P = c["B"], c["gen"], c["prompt"]
@@ -1839,6 +1883,7 @@ def main():
     ap.add_argument("--no-gptoss", action="store_true", help="skip the config-4 whole-model section")
     ap.add_argument("--gptoss-profile", action="store_true", help="small config-4 case for an ncu launch list")
     ap.add_argument("--no-hybrid", action="store_true", help="skip the config-5 whole-model section")
+    ap.add_argument("--hybrid-profile", action="store_true", help="small config-5 case for an ncu launch list")
     ap.add_argument("--moe-layers", type=int, default=None)
     ap.add_argument("--moe-tokens", type=int, default=16)
     ap.add_argument("--moe-steps", type=int, default=5)
@@ -1867,6 +1912,8 @@ def main():
         return run_qwen3moe_profile(args)
     if args.hybrid_only:
         return run_hybrid_only(args, rank, world, local_rank)
+    if args.hybrid_profile:
+        return run_hybrid_profile(args)
     if args.gptoss_only:
         return run_gptoss_only(args)
     if args.gptoss_profile:

@@ -777,12 +777,15 @@ static bool fits(int M, int K) {
     return gemv_layout(M, K, 0, 0).total + 2 * (kStageTarget + 64) <= kSmemBudget;
 }
 
-// batch size from which the tensor-core GEMM takes over (MLQ_TC_MIN_M overrides; 0 = never)
+// batch size from which the tensor-core GEMM takes over (MLQ_TC_MIN_M overrides; 0 = never).
+// From 5 rows its one weight pass beats the GEMV's passes of up to 8 rows on every format
+// and shape of the sweep (2048 x 2048 Q8_0 at 10 rows: 36.3 -> 20.5 us; 151936 x 2048 Q4_K
+// at 8 rows: 306 -> 253 us); at 4 rows the packed GEMV is still ahead (15.5 against ~20 us).
 static int tc_min_m() {
     static int v = -1;
     if (v < 0) {
         const char *e = getenv("MLQ_TC_MIN_M");
-        v = e ? atoi(e) : 16;
+        v = e ? atoi(e) : 5;
         if (v < 0) v = 0;
     }
     return v;

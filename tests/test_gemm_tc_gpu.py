@@ -1,11 +1,11 @@
-"""GPU parity of the tensor-core (tcgen05) quantized GEMM that serves batches of >= 16
+"""GPU parity of the tensor-core (tcgen05) quantized GEMM that serves batches of >= 5
 tokens (the reference's *_batch_matmul math, cengine_batch_instr.c:68-534), against the
 fp64 oracle: weights dequantized exactly, x [M][K] fp32, out [M][N] fp32.
 
 Tolerance: relative L2 <= 1e-3 (the kernel rounds weights and activations once to fp16
 with a power-of-two scale per token; products and sums are fp32).  Covered: every format
 the tensor-core path takes, ragged row tiles (N not a multiple of 128), token counts that
-are not multiples of the token tile, several tiles of tokens, activations with a large
+are not multiples of the token tile (5 and 10 tokens in a 16-token tile), several tiles of tokens, activations with a large
 dynamic range, and the reference-named batch entry points."""
 import ctypes
 
@@ -34,7 +34,7 @@ def _mm(lib, torch, w, qt, x, n, k):
 
 @pytest.mark.parametrize("qt", TC_FORMATS, ids=lambda q: F.NAMES[q])
 @pytest.mark.parametrize("n,k,m", [(384, 512, 16), (200, 256, 17), (1000, 2048, 64), (130, 768, 100),
-                                   (256, 512, 256)])
+                                   (256, 512, 256), (512, 2048, 5), (300, 1024, 10)])
 def test_tc_gemm_matches_oracle(cuda_device, qt, n, k, m):
     import torch
     rng = np.random.default_rng(qt * 1000 + n + m)
