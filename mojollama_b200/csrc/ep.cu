@@ -163,6 +163,10 @@ static size_t moe_grouped_layout(MoeGroupedScratch *m, uint8_t *base, int gqt, i
     t.xdl = (__half *)take(tc_grouped_xh_bytes(R, n_ff));
     t.sg = (float *)take(sizeof(float) * (size_t)R);
     t.sd = (float *)take(sizeof(float) * (size_t)R);
+    if (gqt == MLQ_MXFP4 && uqt == MLQ_MXFP4 && dqt == MLQ_MXFP4 && N % 512 == 0 && n_ff % 512 == 0) {
+        t.bx = take(mxf4_planes_bytes(R, N));
+        t.bh = take(mxf4_planes_bytes(R, n_ff));
+    }
     if (m) *m = t;
     return o;
 }
@@ -204,6 +208,26 @@ int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
     const bool pair = gqt == uqt;
     const int chunks = (R + 7) / 8 + (E < R ? E : R);
     void *items[3] = {m.items[0], m.items[1], m.items[2]};
+    if (gqt == MLQ_MXFP4 && uqt == MLQ_MXFP4 && dqt == MLQ_MXFP4 && m.bx && m.bh) {
+        // block-scaled tensor cores: 128-row tiles of E2M1 weights against the rows' E2M1 planes
+        const int tg = (n_ff + 127) / 128, td = (N + 127) / 128;
+        if (mxf4_grouped_wanted(R, E, 2 * tg) && mxf4_grouped_supported(gexp, gstride, E, n_ff, N) &&
+            mxf4_grouped_supported(uexp, ustride, E, n_ff, N) && mxf4_grouped_supported(dexp, dstride, E, N, n_ff)) {
+            int tt[2] = {2 * tg, td};
+            int rc = launch_group_plan(eid, R, E, 2, items, tt, m.spos, m.srow, m.nitem, s, eid_stride);
+            if (rc == MLQ_OK)
+                rc = launch_mxf4_planes_rows(x, nullptr, m.srow, row_div, x_stride > 0 ? x_stride : N, 0.0f, R, N, m.bx,
+                                             s);
+            if (rc == MLQ_OK)
+                rc = launch_moe_mxf4_tc(gexp, gstride, uexp, ustride, E, n_ff, N, items[0], m.nitem, chunks * tt[0], m.bx,
+                                        R, m.g, m.u, nullptr, s);
+            if (rc == MLQ_OK) rc = launch_mxf4_planes_rows(m.g, m.u, nullptr, 1, n_ff, clamp, R, n_ff, m.bh, s);
+            if (rc == MLQ_OK)
+                rc = launch_moe_mxf4_tc(dexp, dstride, nullptr, 0, E, N, n_ff, items[1], m.nitem + 1, chunks * tt[1],
+                                        m.bh, R, y, nullptr, m.srow, s);
+            return rc;
+        }
+    }
     // (MXFP4 experts only: their E2M1 x 2^e weights are exact in fp16 relative to each chunk's
     // largest block, and the activations enter as an fp16 part plus its fp16 residual, so the
     // products are as exact as fp32 sums make them; K-quant weights would be rounded to fp16)

@@ -55,6 +55,7 @@
 #include <vector>
 
 #include "mlq_internal.h"
+#include "mxf4.cuh"
 #include "pipeline.cuh"
 #include "tcgen05.cuh"
 #include "tc_work.cuh"
@@ -69,7 +70,7 @@ constexpr int kRawRow = 272;               // bytes of one row's chunk: 16 x 17
 constexpr int kRawBytes = kRows * kRawRow; // one raw stage
 constexpr int kABytes = kRows * 256;       // packed E2M1 A chunk: two 128-byte-wide atom columns
 constexpr int kAAtom = kRows * 128;        // one atom column (16 KB)
-constexpr int kPlanes = 8;                 // E2M1 planes per activation row
+constexpr int kPlanes = kMxf4Planes;       // E2M1 planes per activation row
 constexpr int kMaxM = 8;
 constexpr int kThreads = 448;              // warps 0-7 repack, 8-11 epilogue, 12 TMA, 13 MMA
 constexpr int kWarpTma = 12, kWarpMma = 13;
@@ -104,36 +105,11 @@ constexpr int kBarRawFull = 0, kBarRawEmpty = 6, kBarAFull = 12, kBarAFree = 14,
               kBarAccEmpty = 18, kBarDrain = 20, kNumBars = 21;
 constexpr int kBarBytes = kNumBars * 8 + 32;   // + TMEM base slot + flags
 
-// kind::mxf4 block-scaled instruction descriptor: A and B E2M1, K-major, UE8M0 scales,
-// M = 128, N = n; the scale-factor byte ids of this MMA
-__device__ __forceinline__ uint32_t idesc_mxf4(int n, uint32_t sfa_id, uint32_t sfb_id) {
-    return (sfb_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) |
-           ((uint32_t)(kRows >> 4) << 24) | (sfa_id << 29);
-}
-
-__device__ __forceinline__ void umma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %6, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n}\n" ::"r"(
-            tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
-        : "memory");
-}
-
 // ---------------------------------------------------------------- activation planes
-// 2^e as a float for -127 <= e <= 127 (2^-127 is subnormal)
-__device__ __forceinline__ float pow2f(int e) {
-    return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x00400000u);
-}
-
 // Activation planes, computed by every CTA into its own shared memory (B operand image and
 // scale bytes).  One 4-lane group per (activation row m, 32-element block kb): lane j holds
 // x[4j..4j+3] and x[16+4j..16+4j+3] and writes bytes 4j..4j+3 of the block's 16 bytes (byte i
-// pairs x[i], low nibble, with x[i+16]) in each plane.  Plane 0 takes the smallest scale 2^e0
-// with amax / 2^e0 <= 6; plane p uses 2^(e0 - 2p): after plane 0 the residual is at most 2^e0
-// (half the widest E2M1 gap), after plane p >= 1 at most a quarter of plane p's scale, so no
-// plane saturates and one max-reduction per block is enough.
+// pairs x[i], low nibble, with x[i+16]) in each plane (mxf4_block_planes).
 __device__ void encode_planes(const float *__restrict__ x, int M, int K, uint8_t *sB, uint8_t *sSfb, int tid,
                               int nthreads) {
     const int nb = K / 32, n_groups = nthreads >> 2, j = tid & 3;
@@ -153,50 +129,12 @@ __device__ void encode_planes(const float *__restrict__ x, int M, int K, uint8_t
 #pragma unroll
             for (int e = 0; e < 8; e++) r[e] = 0.0f;
         }
-        float a = 0.0f;
-        bool bad = false;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            a = fmaxf(a, fabsf(r[e]));
-            bad |= !(fabsf(r[e]) <= 3.402823466e38f);
-        }
-        const bool finite = (__ballot_sync(0xffffffffu, bad) & gmask) == 0;
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2, 4));
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1, 4));
-        const uint32_t ab = __float_as_uint(a), E = ab >> 23;
-        const bool zero = ab == 0u;
-        // smallest 2^e0 with amax / 2^e0 <= 6: e0 = E - 2 when the significand is <= 1.5
-        const int e0 = E == 0u ? -127 : (int)E - 127 - ((ab & 0x7FFFFFu) <= 0x400000u ? 2 : 1);
+        uint32_t words[kPlanes], codes[kPlanes];
+        mxf4_block_planes(r, gmask, words, codes);
         if (!live) continue;
 #pragma unroll
         for (int p = 0; p < kPlanes; p++) {
-            uint32_t code = 127, word = 0;
-            if (!finite) {
-                code = 255;   // NaN scale: a non-finite activation makes every product NaN
-            } else if (!zero) {
-                const int e = max(e0 - 2 * p, -127);
-                code = (uint32_t)(e + 127);
-                const float inv = __uint_as_float((uint32_t)(127 - e) << 23), sc = pow2f(e);
-                // hardware E2M1 rounding (nearest, ties to even, saturating) of 8 elements, and
-                // the codes' values back as f16 pairs (E2M1 values are exact in f16).  Every byte
-                // goes through a 16-bit register of its own: 4-byte vector moves of 8-bit
-                // registers dropped bytes 2 and 3 in a probe of this toolchain.
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    unsigned short b;
-                    uint32_t h;
-                    asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\nmov.b16 %0, {t, t};\n}"
-                        : "=h"(b)
-                        : "f"(r[4 + q] * inv), "f"(r[q] * inv));
-                    asm("{\n.reg .b8 lo, hi;\nmov.b16 {lo, hi}, %1;\ncvt.rn.f16x2.e2m1x2 %0, lo;\n}"
-                        : "=r"(h)
-                        : "h"(b));
-                    word |= (uint32_t)(b & 0xFFu) << (8 * q);
-                    const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&h));
-                    r[q] = fmaf(-v.x, sc, r[q]);          // exact: exact product, exact difference
-                    r[4 + q] = fmaf(-v.y, sc, r[4 + q]);
-                }
-            }
+            const uint32_t word = words[p], code = codes[p];
             const int n = kPlanes * m + p;
             *reinterpret_cast<uint32_t *>(sB + bimg_off(n, 16 * kb + 4 * j, kPlanes * M)) = word;
             if (j == 0) sSfb[(size_t)n * nb + kb] = (uint8_t)code;

@@ -114,6 +114,17 @@ int launch_gemm_tc_grouped(int qt, const uint8_t *W, long long estride, const ui
                            int n_rows, int K, const void *items, const int *n_items_dev, int n_items_bound,
                            const __half *xh, const __half *xl, const float *xs, float *out, float *out2,
                            const int *out_rows, cudaStream_t s);
+// grouped MXFP4 experts on the block-scaled tensor cores (moe_mxf4_tc.cu): sorted rows encoded
+// once as E2M1 planes (launch_mxf4_planes_rows, mxf4_planes_bytes of scratch), then one launch
+// per matrix list over k_group_plan's items of 128-row tiles; K a multiple of 512
+size_t mxf4_planes_bytes(int R, int K);
+bool mxf4_grouped_supported(const uint8_t *W, long long estride, int E, int n_rows, int K);
+bool mxf4_grouped_wanted(int R, int E, int item_tiles);
+int launch_mxf4_planes_rows(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp,
+                            int R, int K, uint8_t *planes, cudaStream_t s);
+int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,
+                       int K, const void *items, const int *n_items_dev, int n_items_bound, const uint8_t *planes,
+                       int R, float *out, float *out2, const int *out_rows, cudaStream_t s);
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
 int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
 
@@ -236,6 +247,7 @@ struct MoeGroupedScratch {
     __half *xg, *xd;   // tensor-core path: sorted fp16 input rows of gate/up and of down,
     __half *xgl, *xdl; // their fp16 rounding residuals
     float *sg, *sd;    // and their power-of-two scales
+    uint8_t *bx, *bh;  // block-scaled (kind::mxf4) path: E2M1 planes of the gate/up and down inputs
 };
 size_t moe_grouped_scratch_bytes(int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);
 void moe_grouped_carve(MoeGroupedScratch &m, uint8_t *base, int gqt, int uqt, int dqt, int R, int E, int n_ff, int N);

@@ -1,0 +1,537 @@
+// Grouped MXFP4 experts on the block-scaled tensor cores (tcgen05.mma kind::mxf4): the
+// routed-expert products of a MoE layer, each active expert's weights streamed once for all of
+// its rows.
+//
+// Replaces, for GGUF MXFP4 expert tensors, the per-expert MXFP4 matmuls of the reference's
+// batched MoE layer (cengine_batch_instr.c:1113-1207, mxfp4_batch_matmul at :435-534), as
+// launch_moe_grouped's dp4a expert GEMV does, over the same plan: k_group_plan's items
+// {expert e, first sorted row m0, rows mc <= 8, 128-row tile}.
+//
+// Operands (as in gemv_mxf4_tc.cu; M = 128 weight rows, K = 64 per MMA):
+//   A  128 rows of one expert's matrix: each GGUF MXFP4 block's 16 qs bytes copied unchanged
+//      into the K-major 128-byte-swizzled operand, its E8M0 byte the A scale factor (TMEM).
+//   B  the item's mc activation rows as 8 E2M1 planes each (N = 8 mc columns, n = 8 m + p),
+//      with per-32-element E8M0 scales (TMEM).
+//   D  fp32 [128][N] in TMEM; y[m][row] = sum_p D[row][8m + p].
+// Unlike the one-matrix kernel, whose every CTA encodes the activation planes itself, the
+// rows are encoded once per layer (k_mxf4_planes_rows) into global memory, already in the B
+// operand's swizzled layout: planes [chunk][sorted row][2 atom columns x 1 KB], scale bytes
+// [chunk][sorted row][plane][16 blocks].  A work unit (item, 512-K chunk) then brings its
+// weight tile by one 2-D TMA load (no multicast) and its rows' planes and scales by two 1-D
+// bulk copies into one stage; the MMA reads B from the stage itself (8-row groups 2 KB apart).
+//
+// Warps: 0-7 repack (two groups of 4 take alternate units: thread = weight row, qs bytes into
+// the swizzled A buffer, A and B scale words into TMEM), 8-11 epilogue (TMEM -> plane sums ->
+// rows of the output), 12 TMA / bulk-copy producer, 13 MMA issuer (one thread).  CTAs take
+// items round-robin, all K chunks of an item in a row (one accumulation per item).  Every
+// mbarrier wait is bounded (2 s of %globaltimer); a wait that gives up sets the device status
+// word and the CTA drains its copies and MMAs before it frees tensor memory and exits.
+//
+// Roofline: HBM-bound.  Algorithmic bytes per launch = the active experts' matrices
+// (rows x K / 32 x 17 each) + the planes read per item.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+#include "mlq_internal.h"
+#include "mxf4.cuh"
+#include "pipeline.cuh"
+#include "tc_work.cuh"
+#include "tcgen05.cuh"
+
+namespace mlq {
+
+namespace {
+
+constexpr int kRows = 128;                       // MMA M: weight rows per tile
+constexpr int kChunkK = 512;                     // K per unit (16 MXFP4 blocks per row)
+constexpr int kRawRow = 272;                     // one row's chunk: 16 x 17 bytes
+constexpr int kRawBytes = kRows * kRawRow;       // 34816: the weight tile of a stage
+constexpr int kBRowBytes = 2048;                 // one activation row's planes per chunk (2 atom columns)
+constexpr int kMaxRows = 8;                      // activation rows per item
+constexpr int kBBytes = kMaxRows * kBRowBytes;   // 16384
+constexpr int kSfRowBytes = 128;                 // one row's scale bytes per chunk: 8 planes x 16
+constexpr int kStage = kRawBytes + kBBytes + kMaxRows * kSfRowBytes;   // 52224 = 51 KB
+constexpr int kABytes = kRows * 256;             // packed E2M1 A chunk: two 128-byte atom columns
+constexpr int kAAtom = kRows * 128;
+constexpr int kThreads = 448;
+constexpr int kWarpTma = 12, kWarpMma = 13;
+constexpr int kMaxStages = 4;
+constexpr int kAccCol = 0;                       // 2 accumulators x 64 columns
+constexpr int kSfaCol = 128;                     // 2 x 16 columns (per unit: 4 groups x 4 row quarters)
+constexpr int kSfbCol = 160;                     // 2 x 16 columns
+constexpr int kTmemCols = 256;
+constexpr int kSmemMax = 232448;
+
+constexpr int kBarRawFull = 0, kBarRawEmpty = 4, kBarAFull = 8, kBarAFree = 10, kBarAccFull = 12,
+              kBarAccEmpty = 14, kBarDrain = 16, kNumBars = 17;
+constexpr int kBarBytes = kNumBars * 8 + 32;     // + TMEM base slot + flags
+
+static_assert(kRawBytes % 1024 == 0 && kStage % 1024 == 0, "stage parts stay on 1 KB (swizzle atom) boundaries");
+
+struct GroupMxf4Args {
+    const int4 *items;        // {e, m0, mc, tile}
+    const int *n_items;       // written on the device by the planner
+    const uint8_t *planes;    // [nc][R][2048]
+    const uint8_t *scales;    // [nc][R][128]
+    float *out, *out2;        // [R][n_rows] (sorted rows); out2: tiles >= T1 (second matrix)
+    const int *out_rows;      // with it: out[out_rows[p]][n_rows] instead
+    int n_rows, nc, R, T1;
+    int erows, erows2;        // tensor-map rows between consecutive experts
+    int n_stages;
+    int off_sfx, off_bar, off_raw;
+    int *status;
+};
+
+// ---------------------------------------------------------------- activation planes
+// One 4-lane group per (sorted row p, 32-element block kb).  Row p is x[rows[p] / row_div]
+// (rows null: row p), or with x2 the SwiGLU of the sorted gate and up rows,
+// silu(clamp(x[p], +-clamp)) * x2[p] (the grouped GEMV's activation arithmetic).
+__global__ void __launch_bounds__(256) k_mxf4_planes_rows(const float *__restrict__ x, const float *__restrict__ x2,
+                                                          const int *__restrict__ rows, int row_div, int x_stride,
+                                                          float clamp, int R, int K, uint8_t *__restrict__ planes,
+                                                          uint8_t *__restrict__ scales) {
+    pdl_wait();   // the rows are an earlier kernel's output
+    pdl_trigger();
+    const int nb = K / 32, j = threadIdx.x & 3;
+    const long long gid = (long long)blockIdx.x * 64 + (threadIdx.x >> 2);
+    const bool live = gid < (long long)R * nb;
+    const int p = live ? (int)(gid / nb) : 0, kb = live ? (int)(gid - (long long)p * nb) : 0;
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) r[e] = 0.0f;
+    if (live) {
+        int src = rows ? __ldg(rows + p) : p;
+        if (rows && row_div > 1) src /= row_div;
+        const float *xr = x + (size_t)src * x_stride + 32 * kb;
+        const float *x2r = x2 ? x2 + (size_t)p * x_stride + 32 * kb : nullptr;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int k = (e < 4 ? 0 : 16) + 4 * j + (e & 3);
+            float v = __ldg(xr + k);
+            if (x2r) {
+                const float g = fminf(fmaxf(v, -clamp), clamp);
+                v = (g / (1.0f + expf(-g))) * __ldg(x2r + k);
+            }
+            r[e] = v;
+        }
+    }
+    uint32_t words[kMxf4Planes], codes[kMxf4Planes];
+    mxf4_block_planes(r, 0xFu << (threadIdx.x & 28), words, codes);
+    if (!live) return;
+    const int c = kb >> 4, b = 16 * (kb & 15) + 4 * j, ac = b >> 7, o = b & 127;
+    uint8_t *dst = planes + ((size_t)c * R + p) * kBRowBytes + ac * 1024;
+#pragma unroll
+    for (int pl = 0; pl < kMxf4Planes; pl++)
+        *reinterpret_cast<uint32_t *>(dst + pl * 128 + ((((o >> 4) ^ pl) << 4) | (o & 15))) = words[pl];
+    if (j == 0) {
+        uint8_t *sd = scales + ((size_t)c * R + p) * kSfRowBytes + (kb & 15);
+#pragma unroll
+        for (int pl = 0; pl < kMxf4Planes; pl++) sd[pl * 16] = (uint8_t)codes[pl];
+    }
+}
+
+// This CTA's units in order: local unit g -> (item index, chunk c), items b, b + G, ...
+struct ItemWalk {
+    int it, c, nc, G;
+    __device__ ItemWalk(int nc_) : it(blockIdx.x), c(0), nc(nc_), G(gridDim.x) {}
+    __device__ void next() {
+        if (++c == nc) { c = 0; it += G; }
+    }
+};
+
+// ---------------------------------------------------------------- the grouped kernel
+__global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_constant__ CUtensorMap tmap,
+                                                             const __grid_constant__ CUtensorMap tmap2,
+                                                             GroupMxf4Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = sm;                                                 // 2 x kABytes
+    uint32_t *sfx = reinterpret_cast<uint32_t *>(sm + a.off_sfx);     // [2][4][128] A scale words
+    uint8_t *sRaw = sm + a.off_raw;                                   // stages of kStage
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + a.off_bar);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + a.off_bar + kNumBars * 8);
+    volatile int *flag = reinterpret_cast<volatile int *>(sm + a.off_bar + kNumBars * 8 + 4);   // [3]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = a.n_stages, nc = a.nc;
+
+    if (warp == kWarpMma) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&bar[kBarRawFull + s], 1);
+            mbar_init(&bar[kBarRawEmpty + s], 5);   // 4 repack warps + the MMAs that read B
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&bar[kBarAFull + b], 4);
+            mbar_init(&bar[kBarAFree + b], 1);
+            mbar_init(&bar[kBarAccFull + b], 1);
+            mbar_init(&bar[kBarAccEmpty + b], 4);
+        }
+        mbar_init(&bar[kBarDrain], 1);
+        flag[0] = 0;   // repack group 0 gave up
+        flag[1] = 0;   // repack group 1 gave up
+        flag[2] = 0;   // epilogue gave up
+        fence_mbar_init();
+    }
+    if (warp == kWarpTma && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap2) : "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // items, their count and the planes come from earlier kernels
+    pdl_trigger();
+    const int n_items = __ldg(a.n_items);
+    const int G = gridDim.x;
+    const int mine = n_items > (int)blockIdx.x ? (n_items - (int)blockIdx.x + G - 1) / G : 0;
+    const int total = mine * nc;   // units of this CTA
+
+    if (warp == kWarpTma) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t once = policy_evict_first(), keep = policy_evict_last();
+            ItemWalk w(nc);
+            int g = 0;
+            for (int s = 0, ph = 0; g < total; ++g, w.next()) {
+                if (g >= S && !mbar_wait_bounded(&bar[kBarRawEmpty + s], ph ^ 1)) {
+                    set_status(a.status, DEV_ST_WAIT_EMPTY);
+                    break;
+                }
+                const int4 item = __ldg(a.items + w.it);
+                const bool second = item.w >= a.T1;
+                const int row0 = item.x * (second ? a.erows2 : a.erows) + (second ? item.w - a.T1 : item.w) * kRows;
+                const uint32_t mc = (uint32_t)item.z;
+                uint8_t *st = sRaw + (size_t)s * kStage;
+                const size_t pr = (size_t)w.c * a.R + item.y;
+                mbar_arrive_expect_tx(&bar[kBarRawFull + s], (uint32_t)kRawBytes + mc * (kBRowBytes + kSfRowBytes));
+                tma_load_2d(st, second ? &tmap2 : &tmap, w.c * (kRawRow / 2), row0, &bar[kBarRawFull + s], once);
+                bulk_g2s(st + kRawBytes, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
+                bulk_g2s(st + kRawBytes + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes,
+                         &bar[kBarRawFull + s], keep);
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+            // nothing may land in this CTA's shared memory after it exits
+            for (int h = g - S < 0 ? 0 : g - S; h < g; ++h)
+                if (!mbar_wait_bounded(&bar[kBarRawFull + h % S], (h / S) & 1)) set_status(a.status, DEV_ST_WAIT_DRAIN);
+        }
+    } else if (warp == kWarpMma) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint64_t ad0 = umma_desc_sw128(smem_u32(sA));
+            ItemWalk w(nc);
+            int sidx = -1;   // item (accumulation) index of this CTA
+            for (int g = 0; g < total; ++g, w.next()) {
+                const int ab = g & 1, s = g % S;
+                const bool seg_start = w.c == 0, seg_end = w.c == nc - 1;
+                if (seg_start) sidx++;
+                const int accb = sidx & 1;
+                if (seg_start && sidx >= 2 && !mbar_wait_bounded(&bar[kBarAccEmpty + accb], ((sidx >> 1) - 1) & 1)) {
+                    set_status(a.status, DEV_ST_WAIT_EMPTY);
+                    break;
+                }
+                // the repack of this unit is done (A, scales); its B planes have landed
+                if (!mbar_wait_bounded(&bar[kBarAFull + ab], (g >> 1) & 1) ||
+                    !mbar_wait_bounded(&bar[kBarRawFull + s], (g / S) & 1)) {
+                    set_status(a.status, DEV_ST_WAIT_FULL);
+                    break;
+                }
+                tc_fence_after();
+                const int n = kMxf4Planes * __ldg(&a.items[w.it].z);
+                const uint32_t id0 = idesc_mxf4(n, 0, 0), id2 = idesc_mxf4(n, 2, 2);
+                const uint32_t d = tmem + (uint32_t)(kAccCol + 64 * accb);
+                const uint64_t ad = ad0 + (uint64_t)(ab * (kABytes >> 4));
+                const uint64_t bd = umma_desc_sw128_sbo(smem_u32(sRaw + (size_t)s * kStage + kRawBytes), kBRowBytes);
+                const uint32_t sfa0 = tmem + (uint32_t)(kSfaCol + 16 * ab), sfb0 = tmem + (uint32_t)(kSfbCol + 16 * ab);
+                // K step j: atom column j / 4 (A: +16 KB, B: +1 KB) at +32 B per step; scale
+                // bytes 2 (j % 2) of the 128-K group j / 2 (the same byte id for A and B)
+#pragma unroll
+                for (int j = 0; j < kChunkK / 64; j++) {
+                    const uint32_t hi = (j & 1) ? 0x80000000u : 0u;
+                    umma_mxf4(d, ad + (uint64_t)((j >> 2) * (kAAtom >> 4) + (j & 3) * 2),
+                              bd + (uint64_t)((j >> 2) * (1024 >> 4) + (j & 3) * 2), (j & 1) ? id2 : id0,
+                              (sfa0 + 4 * (j >> 1)) | hi, (sfb0 + 4 * (j >> 1)) | hi, (!seg_start || j) ? 1u : 0u);
+                }
+                umma_commit(&bar[kBarAFree + ab]);
+                umma_commit(&bar[kBarRawEmpty + s]);   // the stage's B planes are read
+                if (seg_end) umma_commit(&bar[kBarAccFull + accb]);
+            }
+            // every MMA issued above has finished before tensor memory is freed
+            umma_commit(&bar[kBarDrain]);
+            if (!mbar_wait_bounded(&bar[kBarDrain], 0)) set_status(a.status, DEV_ST_WAIT_DRAIN);
+        }
+        __syncwarp();
+    } else if (warp < 8) {
+        // ---------------------------------------------------------------- repack (thread = row)
+        // group G takes units g = G mod 2 into A buffer G and scale columns G
+        const int G2 = warp >> 2, q = warp & 3;
+        const int m = threadIdx.x & 127;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+        const int m8 = m & 7;
+        const int rowoff = (m >> 3) * 1024 + m8 * 128;
+        ItemWalk w(nc);
+        if (G2) w.next();
+        for (int g = G2; g < total; g += 2, w.next(), w.next()) {
+            const int s = g % S, ab = G2;
+            bool ok = !flag[G2];
+            if (ok && !warp_wait(&bar[kBarRawFull + s], (g / S) & 1, lane)) ok = false;
+            uint32_t R[68];
+            const uint8_t *st = sRaw + (size_t)s * kStage;
+            if (ok) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
+#pragma unroll
+                for (int i = 0; i < 17; i++) {
+                    const uint4 v = src[i];
+                    R[4 * i] = v.x; R[4 * i + 1] = v.y; R[4 * i + 2] = v.z; R[4 * i + 3] = v.w;
+                }
+            }
+            if (ok && g >= 2 && !warp_wait(&bar[kBarAFree + ab], ((g >> 1) - 1) & 1, lane)) ok = false;
+            if (ok) {
+                uint8_t *dstA = sA + ab * kABytes + rowoff;
+#pragma unroll
+                for (int b = 0; b < 16; b++) {
+                    const int o = 17 * b + 1, wd = o >> 2, sh = (o & 3) * 8;
+                    uint4 v;
+                    if (sh == 0) {
+                        v = make_uint4(R[wd], R[wd + 1], R[wd + 2], R[wd + 3]);
+                    } else {
+                        v.x = __funnelshift_r(R[wd], R[wd + 1], sh);
+                        v.y = __funnelshift_r(R[wd + 1], R[wd + 2], sh);
+                        v.z = __funnelshift_r(R[wd + 2], R[wd + 3], sh);
+                        v.w = __funnelshift_r(R[wd + 3], R[wd + 4], sh);
+                    }
+                    *reinterpret_cast<uint4 *>(dstA + (b >> 3) * kAAtom + (((b & 7) ^ m8) << 4)) = v;
+                }
+                // A scale bytes e(b) at byte 17 b of the row chunk, four per word (one 128-K group)
+#pragma unroll
+                for (int gi = 0; gi < 4; gi++) {
+                    const int o0 = 17 * (4 * gi), o1 = o0 + 17, o2 = o0 + 34, o3 = o0 + 51;
+                    const uint32_t t01 = __byte_perm(R[o0 >> 2], R[o1 >> 2], (uint32_t)((o0 & 3) | ((4 + (o1 & 3)) << 4)));
+                    const uint32_t t23 = __byte_perm(R[o2 >> 2], R[o3 >> 2], (uint32_t)((o2 & 3) | ((4 + (o3 & 3)) << 4)));
+                    sfx[(ab * 4 + gi) * kRows + m] = __byte_perm(t01, t23, 0x5410);
+                }
+            } else {
+                flag[G2] = 1;
+            }
+            named_bar_sync(1 + G2, 128);
+            if (flag[G2]) break;   // set before the barrier by a warp of this group: uniform
+            // A scale layout read by the MMA: lane r of every lane quarter, column 4 gi + j holds
+            // the 4 scale bytes of weight row r + 32 j
+            uint32_t v[16];
+#pragma unroll
+            for (int gi = 0; gi < 4; gi++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) v[4 * gi + j] = sfx[(ab * 4 + gi) * kRows + lane + 32 * j];
+            tmem_st16(tq + (uint32_t)(kSfaCol + 16 * ab), v);
+            // B scale words, in the same layout: column 4 gi + j of lane r = the 4 scale bytes
+            // of 128-K group gi of B column n = r + 32 j; columns past N carry scale 1 (their B
+            // rows are never read).  The stage is released here: its B planes stay until the
+            // MMAs that read them commit (the fifth arrival)
+            const int n_cols = kMxf4Planes * __ldg(&a.items[w.it].z);
+            const uint8_t *sf = st + kRawBytes + kBBytes;
+            uint32_t vb[16];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int n = lane + 32 * j;
+#pragma unroll
+                for (int gi = 0; gi < 4; gi++)
+                    vb[4 * gi + j] = n < n_cols ? *reinterpret_cast<const uint32_t *>(sf + n * 16 + 4 * gi) : 0x7F7F7F7Fu;
+            }
+            tmem_st16(tq + (uint32_t)(kSfbCol + 16 * ab), vb);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar[kBarRawEmpty + s]);
+            tmem_st_wait();
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar[kBarAFull + ab]);
+        }
+        if (flag[G2]) set_status(a.status, DEV_ST_WAIT_FULL);
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3, rl = 32 * q + lane;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+        ItemWalk w(nc);
+        int sidx = -1;
+        for (int g = 0; g < total; ++g, w.next()) {
+            if (w.c == 0) sidx++;
+            if (w.c != nc - 1) continue;
+            const int accb = sidx & 1;
+            const int4 item = __ldg(a.items + w.it);
+            const bool ok = warp_wait(&bar[kBarAccFull + accb], (sidx >> 1) & 1, lane);
+            float y[kMaxRows];
+#pragma unroll
+            for (int t = 0; t < kMaxRows; t++) y[t] = 0.0f;
+            if (ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int t = 0; t < kMaxRows; t++) {
+                    if (t < item.z) {
+                        float v[8];
+                        tmem_ld8(tq + (uint32_t)(kAccCol + 64 * accb + 8 * t), v);
+#pragma unroll
+                        for (int p = kMxf4Planes - 1; p >= 0; p--) y[t] += v[p];
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar[kBarAccEmpty + accb]);
+            } else if (lane == 0) {
+                flag[2] = 1;
+                set_status(a.status, DEV_ST_WAIT_FULL);
+            }
+            named_bar_sync(3, 128);
+            if (flag[2]) break;   // set before the barrier by an epilogue warp: uniform
+            const bool second = item.w >= a.T1;
+            const int row = (second ? item.w - a.T1 : item.w) * kRows + rl;
+            if (row < a.n_rows) {
+                float *dst = second ? a.out2 : a.out;
+#pragma unroll
+                for (int t = 0; t < kMaxRows; t++) {
+                    if (t < item.z) {
+                        const int p = item.y + t;
+                        const int orow = a.out_rows ? __ldg(a.out_rows + p) : p;
+                        dst[(size_t)orow * a.n_rows + row] = y[t];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// MLQ_MOE_MXF4_TC: 0 off, 1 (default) when the items fill the GPU at least once, 2 always
+int mxf4_group_mode() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MLQ_MOE_MXF4_TC");
+        v = e ? atoi(e) : 1;
+        if (v < 0) v = 0;
+    }
+    return v;
+}
+
+}  // namespace
+
+// at least one item per SM: min(R, E) active (expert, 8-row chunk) pairs x tiles per chunk
+bool mxf4_grouped_wanted(int R, int E, int item_tiles) {
+    const int mode = mxf4_group_mode();
+    if (mode == 0) return false;
+    if (mode >= 2) return true;
+    const LaunchEnv *env = launch_env();
+    return env && (long long)(R < E ? R : E) * item_tiles >= env->num_sms;
+}
+
+size_t mxf4_planes_bytes(int R, int K) {
+    const size_t nc = (size_t)(K + kChunkK - 1) / kChunkK;
+    return nc * (size_t)R * (kBRowBytes + kSfRowBytes);
+}
+
+// The expert matrices as TMA tiles: K a multiple of 512 (rows of whole 272-byte chunks, a row
+// pitch that is a multiple of 16 bytes), a 16-byte-aligned base, experts a whole number of
+// rows apart, and every row index inside int range.
+bool mxf4_grouped_supported(const uint8_t *W, long long estride, int E, int n_rows, int K) {
+    if (!mxf4_group_mode() || !W || K <= 0 || K % kChunkK || n_rows <= 0 || E <= 0 || ((uintptr_t)W & 15))
+        return false;
+    const long long row_bytes = (long long)(K / 32) * 17;
+    if (estride < row_bytes * n_rows || estride % row_bytes) return false;
+    return (long long)(E - 1) * (estride / row_bytes) + n_rows < (1ll << 31);
+}
+
+int launch_mxf4_planes_rows(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp,
+                            int R, int K, uint8_t *planes, cudaStream_t s) {
+    if (R <= 0) return MLQ_OK;
+    if (K % kChunkK) return MLQ_ERR_UNSUPPORTED;
+    const long long groups = (long long)R * (K / 32);
+    uint8_t *scales = planes + (size_t)(K / kChunkK) * R * kBRowBytes;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = getenv("MLQ_NO_PDL") ? 0 : 1;
+    cfg.stream = s;
+    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3((unsigned)((groups + 63) / 64));
+    count_launch();
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_mxf4_planes_rows, x, x2, rows, row_div, x_stride, clamp, R, K, planes,
+                                       scales))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
+}
+
+int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,
+                       int K, const void *items, const int *n_items_dev, int n_items_bound, const uint8_t *planes,
+                       int R, float *out, float *out2, const int *out_rows, cudaStream_t s) {
+    if (n_items_bound <= 0 || R <= 0) return MLQ_OK;
+    if (!mxf4_grouped_supported(W, estride, E, n_rows, K) || (W2 && !mxf4_grouped_supported(W2, estride2, E, n_rows, K)))
+        return MLQ_ERR_UNSUPPORTED;
+    const LaunchEnv *env = launch_env();
+    if (!env) return MLQ_ERR_NO_DEVICE;
+    const long long row_bytes = (long long)(K / 32) * 17;
+    const long long erows = estride / row_bytes, erows2 = W2 ? estride2 / row_bytes : 0;
+    CUtensorMap tmap, tmap2;
+    if (!tc_tensor_map_rows(&tmap, W, (E - 1) * erows + n_rows, row_bytes, kRawRow, kRows)) return MLQ_ERR_UNSUPPORTED;
+    if (!tc_tensor_map_rows(&tmap2, W2 ? W2 : W, W2 ? (E - 1) * erows2 + n_rows : (E - 1) * erows + n_rows, row_bytes,
+                            kRawRow, kRows))
+        return MLQ_ERR_UNSUPPORTED;
+    const int off_sfx = 2 * kABytes;
+    const int off_bar = off_sfx + 2 * 4 * kRows * 4;
+    const int off_raw = (off_bar + kBarBytes + 1023) / 1024 * 1024;
+    int n_stages = (kSmemMax - 1024 - off_raw) / kStage;
+    if (n_stages > kMaxStages) n_stages = kMaxStages;
+    if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
+    const int smem = 1024 + off_raw + n_stages * kStage;
+    static bool attr = false;
+    if (!attr) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(k_moe_mxf4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax)))
+            return MLQ_ERR_CUDA;
+        attr = true;
+    }
+    GroupMxf4Args a{};
+    a.items = reinterpret_cast<const int4 *>(items);
+    a.n_items = n_items_dev;
+    a.planes = planes;
+    a.scales = planes + (size_t)(K / kChunkK) * R * kBRowBytes;
+    a.out = out;
+    a.out2 = out2;
+    a.out_rows = out_rows;
+    a.n_rows = n_rows;
+    a.nc = K / kChunkK;
+    a.R = R;
+    a.T1 = (n_rows + kRows - 1) / kRows;
+    a.erows = (int)erows;
+    a.erows2 = (int)erows2;
+    a.n_stages = n_stages;
+    a.off_sfx = off_sfx;
+    a.off_bar = off_bar;
+    a.off_raw = off_raw;
+    a.status = env->d_status;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = getenv("MLQ_NO_PDL") ? 0 : 1;
+    cfg.stream = s;
+    cfg.blockDim = dim3(kThreads);
+    cfg.gridDim = dim3((unsigned)(n_items_bound < env->num_sms ? n_items_bound : env->num_sms));
+    cfg.dynamicSmemBytes = (size_t)smem;
+    count_launch();
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_moe_mxf4_tc, tmap, tmap2, a)) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+}  // namespace mlq

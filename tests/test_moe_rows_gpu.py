@@ -4,9 +4,10 @@ grouped gate/up and down GEMV) against the oracle: y[r] = down_e(silu(clamp(gate
 quant_kernels_omp.c:2157-2164 for one routed row).  Covers one-row and many-row experts
 (chunks of 8 rows and a ragged rest), unused experts, mixed gate/up types (separate
 launches), short rows (a lane group per weight row), rows whose length is not a multiple of
-128 bytes, and ids outside [0, E) (row left unwritten).  The tensor-core grouped path (off by
-default, MLQ_MOE_TC_ROWS) is checked in a child process.  Tolerance: relative L2 <= 1e-3
-per row."""
+128 bytes, and ids outside [0, E) (row left unwritten).  The fp16 tensor-core grouped path (off by
+default, MLQ_MOE_TC_ROWS) and the block-scaled (kind::mxf4) one for MXFP4 experts
+(MLQ_MOE_MXF4_TC: forced on, and against the GEMV path) are checked in child processes.
+Tolerance: relative L2 <= 1e-3 per row."""
 import ctypes
 
 import numpy as np
@@ -156,6 +157,81 @@ def test_moe_rows_tensor_core_path():
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     env = dict(os.environ, MLQ_MOE_TC_ROWS="4", MLQ_REPO=root)
     r = subprocess.run([sys.executable, "-c", _TC_CASE], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+_MXF4_CASE = r"""
+import ctypes, os, sys
+import numpy as np, torch
+sys.path.insert(0, os.environ["MLQ_REPO"])
+from oracle import formats as F, ops as O
+from mojollama_b200 import core
+lib = core(); assert lib.mlq_init(0) == 0
+lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+# (E, N, FF, R, seed, weights, packed rows): K of one and of four 512-wide chunks, experts with
+# 1 to 20+ rows (chunks of 8 and a ragged rest), unused experts, ids outside [0, E).
+# Bars: 1e-3 for weights quantized from N(0, 0.02) values (measured: block-scaled 1.2e-5,
+# GEMV 5e-5); 1e-2 for random blocks, whose E8M0 scales span 2^-27..2^13 within a row so that
+# the fp32 sums cancel heavily (measured: block-scaled 1.6e-3, GEMV 7.6e-3)
+for (E, N, FF, R, seed, kind, packed) in ((8, 512, 512, 64, 7, "random", False), (12, 2048, 512, 40, 9, "quant", False),
+                                          (32, 1024, 1024, 80, 11, "quant", True), (4, 512, 1024, 37, 13, "random", True)):
+    rng = np.random.default_rng(seed)
+    def ex(rows, cols):
+        if kind == "random":
+            raw = F.random_blocks(F.MXFP4, E * rows * cols, rng)
+        else:
+            raw = F.quantize(F.MXFP4, (rng.standard_normal(E * rows * cols) * 0.02).astype(np.float32))
+        return raw, F.dequantize(F.MXFP4, raw, E * rows * cols).astype(np.float64).reshape(E, rows, cols)
+    (gr, G), (ur, U), (dr, D) = ex(FF, N), ex(FF, N), ex(N, FF)
+    eid = rng.integers(0, E, R).astype(np.int32)
+    eid[:12] = 1                      # one expert with 12+ rows
+    eid[R - 1] = -1                   # left unwritten
+    x = rng.standard_normal((R, N)).astype(np.float32)
+    d = [torch.from_numpy(v).cuda() for v in (gr, ur, dr)]
+    y = torch.full((R, N), float("nan"), device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    rb = F.row_bytes
+    strides = (rb(F.MXFP4, N) * FF, rb(F.MXFP4, N) * FF, rb(F.MXFP4, FF) * N)
+    if packed:
+        rows = np.zeros((R, N + 4), np.float32)
+        rows[:, :N] = x
+        rows[:, N] = eid.view(np.float32)
+        drows = torch.from_numpy(rows).cuda()
+        rc = lib.mlq_moe_rows_packed(F.MXFP4, F.MXFP4, F.MXFP4, vp(d[0]), vp(d[1]), vp(d[2]), *strides, E, vp(drows),
+                                     R, FF, N, vp(y))
+    else:
+        dx, de = torch.from_numpy(x).cuda(), torch.from_numpy(eid).cuda()
+        rc = lib.mlq_moe_rows(F.MXFP4, F.MXFP4, F.MXFP4, vp(d[0]), vp(d[1]), vp(d[2]), *strides, E, vp(de), R, FF, N,
+                              vp(dx), vp(y))
+    assert rc == 0, lib.mlq_last_error_message()
+    torch.cuda.synchronize()
+    assert lib.mlq_device_status() == 0
+    got = y.cpu().numpy()
+    case = 0.0
+    for r, e in enumerate(eid):
+        if e < 0:
+            assert np.isnan(got[r]).all()
+            continue
+        xr = x[r].astype(np.float64)
+        want = D[e] @ (O.silu_clamped(G[e] @ xr) * (U[e] @ xr))
+        case = max(case, O.rel_l2(got[r], want))
+    print("case", E, N, FF, R, kind, packed, "worst", case)
+    assert case < (1e-3 if kind == "quant" else 1e-2), case
+"""
+
+
+@pytest.mark.parametrize("mode", ["2", "0"])
+def test_moe_rows_block_scaled_path(mode):
+    """MXFP4 experts with K a multiple of 512 on the block-scaled tensor cores (MLQ_MOE_MXF4_TC=2:
+    taken at every size; read once per process, so a child process) and, with 0, the same cases
+    on the grouped GEMV: the sorted rows encoded once as 8 E2M1 planes each, 128-row tiles of
+    one expert against its chunk of up to 8 rows, dense and packed (in-band id) input rows"""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MLQ_MOE_MXF4_TC=mode, MLQ_REPO=root)
+    r = subprocess.run([sys.executable, "-c", _MXF4_CASE], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
