@@ -125,6 +125,11 @@ int launch_mxf4_planes_rows(const float *x, const float *x2, const int *rows, in
 int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,
                        int K, const void *items, const int *n_items_dev, int n_items_bound, const uint8_t *planes,
                        int R, float *out, float *out2, const int *out_rows, cudaStream_t s);
+// one MXFP4 matrix (or a pair with the same shape: out2 = W2 x) times all R encoded rows, on the
+// same kernel: out [R][n_rows]
+bool mxf4_dense_supported(const uint8_t *W, int n_rows, int K);
+int launch_mxf4_dense_tc(const uint8_t *W, const uint8_t *W2, int n_rows, int K, const uint8_t *planes, int R,
+                         float *out, float *out2, cudaStream_t s);
 int launch_quantize_q8_0(const float *x, uint8_t *q8, int64_t n, cudaStream_t s);
 int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s);
 

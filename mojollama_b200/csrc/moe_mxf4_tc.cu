@@ -82,8 +82,18 @@ struct GroupMxf4Args {
     int erows, erows2;        // tensor-map rows between consecutive experts
     int n_stages;
     int off_sfx, off_bar, off_raw;
+    int dense_T;              // > 0: no item list; item i = tile i % dense_T of rows 8 (i / dense_T)..
     int *status;
 };
+
+// work item it: from the planner's list, or in dense mode (one matrix pair, every row) computed
+__device__ __forceinline__ int4 item_at(const GroupMxf4Args &a, int it) {
+    if (a.dense_T) {
+        const int ch = it / a.dense_T, m0 = 8 * ch;
+        return make_int4(0, m0, min(8, a.R - m0), it - ch * a.dense_T);
+    }
+    return __ldg(a.items + it);
+}
 
 // ---------------------------------------------------------------- activation planes
 // One 4-lane group per (sorted row p, 32-element block kb).  Row p is x[rows[p] / row_div]
@@ -190,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     const uint32_t tmem = *tmem_slot;
     pdl_wait();   // items, their count and the planes come from earlier kernels
     pdl_trigger();
-    const int n_items = __ldg(a.n_items);
+    const int n_items = a.dense_T ? (a.R + 7) / 8 * a.dense_T : __ldg(a.n_items);
     const int G = gridDim.x;
     const int mine = n_items > (int)blockIdx.x ? (n_items - (int)blockIdx.x + G - 1) / G : 0;
     const int total = mine * nc;   // units of this CTA
@@ -206,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     set_status(a.status, DEV_ST_WAIT_EMPTY);
                     break;
                 }
-                const int4 item = __ldg(a.items + w.it);
+                const int4 item = item_at(a, w.it);
                 const bool second = item.w >= a.T1;
                 const int row0 = item.x * (second ? a.erows2 : a.erows) + (second ? item.w - a.T1 : item.w) * kRows;
                 const uint32_t mc = (uint32_t)item.z;
@@ -245,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     break;
                 }
                 tc_fence_after();
-                const int n = kMxf4Planes * __ldg(&a.items[w.it].z);
+                const int n = kMxf4Planes * item_at(a, w.it).z;
                 const uint32_t id0 = idesc_mxf4(n, 0, 0), id2 = idesc_mxf4(n, 2, 2);
                 const uint32_t d = tmem + (uint32_t)(kAccCol + 64 * accb);
                 const uint64_t ad = ad0 + (uint64_t)(ab * (kABytes >> 4));
@@ -335,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             // of 128-K group gi of B column n = r + 32 j; columns past N carry scale 1 (their B
             // rows are never read).  The stage is released here: its B planes stay until the
             // MMAs that read them commit (the fifth arrival)
-            const int n_cols = kMxf4Planes * __ldg(&a.items[w.it].z);
+            const int n_cols = kMxf4Planes * item_at(a, w.it).z;
             const uint8_t *sf = st + kRawBytes + kBBytes;
             uint32_t vb[16];
 #pragma unroll
@@ -365,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             if (w.c == 0) sidx++;
             if (w.c != nc - 1) continue;
             const int accb = sidx & 1;
-            const int4 item = __ldg(a.items + w.it);
+            const int4 item = item_at(a, w.it);
             const bool ok = warp_wait(&bar[kBarAccFull + accb], (sidx >> 1) & 1, lane);
             float y[kMaxRows];
 #pragma unroll
@@ -473,9 +483,9 @@ int launch_mxf4_planes_rows(const float *x, const float *x2, const int *rows, in
                : MLQ_ERR_CUDA;
 }
 
-int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,
-                       int K, const void *items, const int *n_items_dev, int n_items_bound, const uint8_t *planes,
-                       int R, float *out, float *out2, const int *out_rows, cudaStream_t s) {
+static int launch_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E,
+                          int n_rows, int K, const void *items, const int *n_items_dev, int n_items_bound, int dense_T,
+                          const uint8_t *planes, int R, float *out, float *out2, const int *out_rows, cudaStream_t s) {
     if (n_items_bound <= 0 || R <= 0) return MLQ_OK;
     if (!mxf4_grouped_supported(W, estride, E, n_rows, K) || (W2 && !mxf4_grouped_supported(W2, estride2, E, n_rows, K)))
         return MLQ_ERR_UNSUPPORTED;
@@ -519,6 +529,7 @@ int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, l
     a.off_sfx = off_sfx;
     a.off_bar = off_bar;
     a.off_raw = off_raw;
+    a.dense_T = dense_T;
     a.status = env->d_status;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
@@ -532,6 +543,25 @@ int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, l
     cfg.dynamicSmemBytes = (size_t)smem;
     count_launch();
     return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_moe_mxf4_tc, tmap, tmap2, a)) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,
+                       int K, const void *items, const int *n_items_dev, int n_items_bound, const uint8_t *planes,
+                       int R, float *out, float *out2, const int *out_rows, cudaStream_t s) {
+    return launch_mxf4_tc(W, estride, W2, estride2, E, n_rows, K, items, n_items_dev, n_items_bound, 0, planes, R, out,
+                          out2, out_rows, s);
+}
+
+bool mxf4_dense_supported(const uint8_t *W, int n_rows, int K) {
+    return mxf4_grouped_supported(W, (long long)(K / 32) * 17 * n_rows, 1, n_rows, K);
+}
+
+int launch_mxf4_dense_tc(const uint8_t *W, const uint8_t *W2, int n_rows, int K, const uint8_t *planes, int R,
+                         float *out, float *out2, cudaStream_t s) {
+    const long long st = (long long)(K / 32) * 17 * n_rows;
+    const int T = (W2 ? 2 : 1) * ((n_rows + kRows - 1) / kRows);
+    return launch_mxf4_tc(W, st, W2, st, 1, n_rows, K, nullptr, nullptr, (R + 7) / 8 * T, T, planes, R, out, out2,
+                          nullptr, s);
 }
 
 }  // namespace mlq

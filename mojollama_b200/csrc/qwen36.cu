@@ -343,6 +343,12 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
     float *score = (float *)cs.scratch(sizeof(float) * B);
     const size_t attn_sb = attn_scratch_bytes(B, NH, HD);
     float *attn_scr = (float *)cs.scratch(attn_sb);
+    // shared experts on the block-scaled tensor cores: the rows' E2M1 planes (input, SwiGLU)
+    uint8_t *shp_x = nullptr, *shp_h = nullptr;
+    if (max_si > 0 && B >= 2 && N % 512 == 0) {
+        shp_x = (uint8_t *)cs.scratch(mxf4_planes_bytes(B, N));
+        shp_h = (uint8_t *)cs.scratch(mxf4_planes_bytes(B, (max_si + 511) / 512 * 512));
+    }
     // reference-compatibility V columns beyond the projection come from ws's qkv slice
     const float *v_ext = nullptr;
     if (compat && any_attn && a->ws) {
@@ -531,10 +537,20 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
             k_shexp_score<<<B, 256, 0, s>>>(xn, sr, score, N);
             count_launch();
-            MLQ_TRY(launch_matmul(sg, sgq, xn, g, si, N, B, 0, s));
-            MLQ_TRY(launch_matmul(su, suq, xn, u, si, N, B, 0, s));
-            MLQ_TRY(launch_swiglu(g, g, u, (long long)B * si, s));
-            MLQ_TRY(launch_matmul(sd, sdq, g, tmp, N, si, B, 0, s));
+            if (shp_x && sgq == MLQ_MXFP4 && suq == MLQ_MXFP4 && sdq == MLQ_MXFP4 && si % 512 == 0 &&
+                mxf4_dense_supported(sg, si, N) && mxf4_dense_supported(su, si, N) && mxf4_dense_supported(sd, N, si)) {
+                // MXFP4 (the GGUF shared-expert type): gate and up in one launch of the grouped
+                // block-scaled kernel over all B rows, silu(clamp(g, +-80)) * u encoded, then down
+                MLQ_TRY(launch_mxf4_planes_rows(xn, nullptr, nullptr, 1, N, 0.0f, B, N, shp_x, s));
+                MLQ_TRY(launch_mxf4_dense_tc(sg, su, si, N, shp_x, B, g, u, s));
+                MLQ_TRY(launch_mxf4_planes_rows(g, u, nullptr, 1, si, 80.0f, B, si, shp_h, s));
+                MLQ_TRY(launch_mxf4_dense_tc(sd, nullptr, N, si, shp_h, B, tmp, nullptr, s));
+            } else {
+                MLQ_TRY(launch_matmul(sg, sgq, xn, g, si, N, B, 0, s));
+                MLQ_TRY(launch_matmul(su, suq, xn, u, si, N, B, 0, s));
+                MLQ_TRY(launch_swiglu(g, g, u, (long long)B * si, s));
+                MLQ_TRY(launch_matmul(sd, sdq, g, tmp, N, si, B, 0, s));
+            }
             if (rc == MLQ_OK) {
                 k_add_scaled_if_pos<<<dim3(grid_cols(N), B), 256, 0, s>>>(x, tmp, score, N);
                 count_launch();

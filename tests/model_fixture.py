@@ -173,21 +173,23 @@ def ws_stride(m, B):
 
 
 # ------------------------------------------------------------------ qwen36_batch_forward
-def make_qwen36_model(seed=0, qkv_layout="std", L=4, layer_pattern=(1, 1, 1, 0)):
+def make_qwen36_model(seed=0, qkv_layout="std", L=4, layer_pattern=(1, 1, 1, 0), N=256, experts=(8, 2, 256),
+                      expert_fmt=F.Q4_0, shexp_fmt=F.Q8_0):
     """Hybrid model in qwen36_batch_forward's layout: SSM layers (layer_types 1) and
-    attention layers with a fused QKV projection; MoE (Q4_0 experts, F32 router) with a
-    Q8_0 shared expert.  qkv_layout 'std': rows NH*HD + 2*n_kv (Q|K|V); 'ref': NH*HD + 2N
-    (Q|K|V with N-wide K and V sections, the layout the reference's split assumes)."""
+    attention layers with a fused QKV projection; MoE (experts = (E, top-k, n_ff) of
+    expert_fmt, F32 router) with a 512-wide shared expert of shexp_fmt.  qkv_layout 'std': rows
+    NH*HD + 2*n_kv (Q|K|V); 'ref': NH*HD + 2N (Q|K|V with N-wide K and V sections, the layout
+    the reference's split assumes)."""
     rng = np.random.default_rng(seed)
-    m = dict(L=L, N=256, NH=4, NKH=2, HD=64, FF=512, V=320, eps=1e-6, rope_dim=32, max_ctx=64,
+    m = dict(L=L, N=N, NH=4, NKH=2, HD=64, FF=512, V=320, eps=1e-6, rope_dim=32, max_ctx=64,
              ssm_inner=256, ssm_groups=32, ssm_state=128, ssm_dt_rank=32)
     N, inner, n_kv = m["N"], m["NH"] * m["HD"], m["NKH"] * m["HD"]
     m["emb"] = (rng.standard_normal((m["V"], N)) * 0.5).astype(np.float32)
     m["onw"] = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
     m["wout"] = _w(rng, F.Q8_0, m["V"], N)
     m["cos"], m["sin"] = O.rope_tables(m["max_ctx"], m["HD"], m["rope_dim"])
-    E, k, M = 8, 2, 256
-    m["moe"] = dict(E=E, k=k, M=M, gq=F.Q4_0, uq=F.Q4_0, dq=F.Q4_0)
+    E, k, M = experts
+    m["moe"] = dict(E=E, k=k, M=M, gq=expert_fmt, uq=expert_fmt, dq=expert_fmt)
     layers = []
     for l in range(L):
         ly = {"an": (1 + 0.1 * rng.standard_normal(N)).astype(np.float32),
@@ -210,9 +212,9 @@ def make_qwen36_model(seed=0, qkv_layout="std", L=4, layer_pattern=(1, 1, 1, 0))
             ly["o"] = _w(rng, F.Q4_0, N, inner)
         ly["router"] = (rng.standard_normal((E, N)) * 0.2).astype(np.float32)
         for name, rows, cols in (("gate_exps", M, N), ("up_exps", M, N), ("down_exps", N, M)):
-            ly[name] = {e: _w(rng, F.Q4_0, rows, cols)[0] for e in range(E)}
-        ly["shexp"] = {"si": 512, "g": _w(rng, F.Q8_0, 512, N), "u": _w(rng, F.Q8_0, 512, N),
-                       "d": _w(rng, F.Q8_0, N, 512), "router": (rng.standard_normal(N) * 0.1).astype(np.float32)}
+            ly[name] = {e: _w(rng, expert_fmt, rows, cols)[0] for e in range(E)}
+        ly["shexp"] = {"si": 512, "g": _w(rng, shexp_fmt, 512, N), "u": _w(rng, shexp_fmt, 512, N),
+                       "d": _w(rng, shexp_fmt, N, 512), "router": (rng.standard_normal(N) * 0.1).astype(np.float32)}
         layers.append(ly)
     m["layers"] = layers
     return m

@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 
 from mojollama_b200.kernels import load_kernels
+from oracle import formats as F
 from oracle import model as OM
 from oracle import ops as O
 from oracle import ref as R
@@ -82,6 +83,34 @@ def test_qwen36_host_kv_external_rows_and_rewind(cuda_device):
             assert O.rel_l2(got, want) < TOL, (conv, step)
             kv_lens += 1
             st["kv_lens"] += 1
+
+
+def test_qwen36_mxfp4_experts_block_scaled(cuda_device):
+    """MXFP4 routed experts (32, top-8, at 6 tokens: 48 rows, where the grouped kind::mxf4
+    kernel is taken by default) and an MXFP4 shared expert (all 6 rows through the same kernel
+    in dense mode: gate and up in one launch), N = 512, host KV, against the oracle.  The first
+    step is held to TOL; later steps carry the first's rounding through the SSM state and the
+    KV rows, and are held to 3e-3 and to the greedy rule (same argmax wherever the oracle's top-2
+    margin exceeds 1e-2).  Measured: 6e-4 then 1.6-1.8e-3, the same as on the grouped GEMV
+    path (MLQ_MOE_MXF4_TC=0: 7.9e-4, 1.7-1.9e-3)"""
+    k = load_kernels()
+    m = make_qwen36_model(seed=51, N=512, experts=(32, 8, 512), expert_fmt=F.MXFP4, shexp_fmt=F.MXFP4)
+    kv_k, kv_v, kv_lens, ssm = _state(m)
+    call = Qwen36Call(m, kv_k, kv_v, kv_lens, ssm)
+    st = OM.qwen36_new_state(m)
+    rng = np.random.default_rng(52)
+    for step in range(3):
+        toks = rng.integers(0, m["V"], 6).astype(np.int32)
+        got, x, _ = _step(call, k.cengine.qwen36_batch_forward, m, 6, toks)
+        want, xw = OM.qwen36_step(m, st, toks)
+        bar = TOL if step == 0 else 3e-3
+        assert O.rel_l2(got, want) < bar, (step, O.rel_l2(got, want))
+        assert O.rel_l2(x, xw) < bar, (step, O.rel_l2(x, xw))
+        top2 = np.sort(want, axis=1)[:, -2:]
+        sure = top2[:, 1] - top2[:, 0] > 1e-2
+        assert (got.argmax(1) == want.argmax(1))[sure].all(), step
+        kv_lens += 1
+        st["kv_lens"] += 1
 
 
 def test_qwen36_device_kv_matches_oracle(cuda_device):
