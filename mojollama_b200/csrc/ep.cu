@@ -163,7 +163,7 @@ static size_t moe_grouped_layout(MoeGroupedScratch *m, uint8_t *base, int gqt, i
     t.xdl = (__half *)take(tc_grouped_xh_bytes(R, n_ff));
     t.sg = (float *)take(sizeof(float) * (size_t)R);
     t.sd = (float *)take(sizeof(float) * (size_t)R);
-    if (gqt == MLQ_MXFP4 && uqt == MLQ_MXFP4 && dqt == MLQ_MXFP4 && N % 512 == 0 && n_ff % 512 == 0) {
+    if (gqt == MLQ_MXFP4 && uqt == MLQ_MXFP4 && dqt == MLQ_MXFP4) {
         t.bx = take(mxf4_planes_bytes(R, N));
         t.bh = take(mxf4_planes_bytes(R, n_ff));
     }

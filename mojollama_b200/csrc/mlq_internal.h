@@ -116,7 +116,7 @@ int launch_gemm_tc_grouped(int qt, const uint8_t *W, long long estride, const ui
                            const int *out_rows, cudaStream_t s);
 // grouped MXFP4 experts on the block-scaled tensor cores (moe_mxf4_tc.cu): sorted rows encoded
 // once as E2M1 planes (launch_mxf4_planes_rows, mxf4_planes_bytes of scratch), then one launch
-// per matrix list over k_group_plan's items of 128-row tiles; K a multiple of 512
+// per matrix list over k_group_plan's items of 128-row tiles; K % 32 == 0 (TMA tiles when K % 512 == 0 and the rows are 16-byte aligned, else 16-byte windows)
 size_t mxf4_planes_bytes(int R, int K);
 bool mxf4_grouped_supported(const uint8_t *W, long long estride, int E, int n_rows, int K);
 bool mxf4_grouped_wanted(int R, int E, int item_tiles);

@@ -13,6 +13,11 @@
 //   B  the item's mc activation rows as 8 E2M1 planes each (N = 8 mc columns, n = 8 m + p),
 //      with per-32-element E8M0 scales (TMEM).
 //   D  fp32 [128][N] in TMEM; y[m][row] = sum_p D[row][8m + p].
+// Weight tiles: one 2-D TMA box when K is a multiple of 512 and the rows are 16-byte aligned;
+// otherwise (GPT-OSS: K = 2880, 1530-byte rows) the producer warp copies each row's chunk as
+// the 16-byte-aligned windows that cover it (cp.async, completion on the stage's mbarrier), the
+// repack thread shifts its row out of its window slot, and a last partial chunk's missing
+// blocks enter as zero codes with scale 1 (the planes past K are zero too).
 // Unlike the one-matrix kernel, whose every CTA encodes the activation planes itself, the
 // rows are encoded once per layer (k_mxf4_planes_rows) into global memory, already in the B
 // operand's swizzled layout: planes [chunk][sorted row][2 atom columns x 1 KB], scale bytes
@@ -69,7 +74,17 @@ constexpr int kBarRawFull = 0, kBarRawEmpty = 4, kBarAFull = 8, kBarAFree = 10, 
               kBarAccEmpty = 14, kBarDrain = 16, kNumBars = 17;
 constexpr int kBarBytes = kNumBars * 8 + 32;     // + TMEM base slot + flags
 
-static_assert(kRawBytes % 1024 == 0 && kStage % 1024 == 0, "stage parts stay on 1 KB (swizzle atom) boundaries");
+// Rows that cannot be TMA tiles (a row pitch that is not a multiple of 16 bytes, K not a
+// multiple of 512): each row's chunk arrives as the 16-byte-aligned windows that cover it
+// (at most 18), one 288-byte slot per row
+constexpr int kWinRow = 288;
+template <bool kWin> struct StageLayout {
+    static constexpr int raw = kRows * (kWin ? kWinRow : kRawRow);        // weight part
+    static constexpr int bytes = raw + kBBytes + kMaxRows * kSfRowBytes;   // 51 / 53 KB
+};
+static_assert(kRawBytes % 1024 == 0 && kStage % 1024 == 0 && StageLayout<true>::bytes % 1024 == 0 &&
+                  StageLayout<true>::raw % 1024 == 0,
+              "stage parts stay on 1 KB (swizzle atom) boundaries");
 
 struct GroupMxf4Args {
     const int4 *items;        // {e, m0, mc, tile}
@@ -83,6 +98,10 @@ struct GroupMxf4Args {
     int n_stages;
     int off_sfx, off_bar, off_raw;
     int dense_T;              // > 0: no item list; item i = tile i % dense_T of rows 8 (i / dense_T)..
+    // windowed copies: the matrices' base addresses, expert strides, row pitch and K
+    const uint8_t *W, *W2;
+    long long estride, estride2;
+    int row_bytes, K;
     int *status;
 };
 
@@ -99,20 +118,21 @@ __device__ __forceinline__ int4 item_at(const GroupMxf4Args &a, int it) {
 // One 4-lane group per (sorted row p, 32-element block kb).  Row p is x[rows[p] / row_div]
 // (rows null: row p), or with x2 the SwiGLU of the sorted gate and up rows,
 // silu(clamp(x[p], +-clamp)) * x2[p] (the grouped GEMV's activation arithmetic).
+// Blocks from K / 32 up to the last 512-K chunk's end are encoded as zeros (codes 0, scale 1).
 __global__ void __launch_bounds__(256) k_mxf4_planes_rows(const float *__restrict__ x, const float *__restrict__ x2,
                                                           const int *__restrict__ rows, int row_div, int x_stride,
                                                           float clamp, int R, int K, uint8_t *__restrict__ planes,
                                                           uint8_t *__restrict__ scales) {
     pdl_wait();   // the rows are an earlier kernel's output
     pdl_trigger();
-    const int nb = K / 32, j = threadIdx.x & 3;
+    const int nb = K / 32, nbp = (K + kChunkK - 1) / kChunkK * (kChunkK / 32), j = threadIdx.x & 3;
     const long long gid = (long long)blockIdx.x * 64 + (threadIdx.x >> 2);
-    const bool live = gid < (long long)R * nb;
-    const int p = live ? (int)(gid / nb) : 0, kb = live ? (int)(gid - (long long)p * nb) : 0;
+    const bool live = gid < (long long)R * nbp;
+    const int p = live ? (int)(gid / nbp) : 0, kb = live ? (int)(gid - (long long)p * nbp) : 0;
     float r[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) r[e] = 0.0f;
-    if (live) {
+    if (live && kb < nb) {
         int src = rows ? __ldg(rows + p) : p;
         if (rows && row_div > 1) src /= row_div;
         const float *xr = x + (size_t)src * x_stride + 32 * kb;
@@ -153,14 +173,18 @@ struct ItemWalk {
 };
 
 // ---------------------------------------------------------------- the grouped kernel
+template <bool kWin>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_constant__ CUtensorMap tmap,
                                                              const __grid_constant__ CUtensorMap tmap2,
                                                              GroupMxf4Args a) {
+    constexpr int RB = StageLayout<kWin>::raw, ST = StageLayout<kWin>::bytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = sm;                                                 // 2 x kABytes
-    uint32_t *sfx = reinterpret_cast<uint32_t *>(sm + a.off_sfx);     // [2][4][128] A scale words
-    uint8_t *sRaw = sm + a.off_raw;                                   // stages of kStage
+    // A scale words [2][4][128] (windowed: [4][128] at the start of the unit's own stage, over
+    // weight windows already read into registers)
+    uint32_t *sfx = kWin ? nullptr : reinterpret_cast<uint32_t *>(sm + a.off_sfx);
+    uint8_t *sRaw = sm + a.off_raw;                                   // stages of ST bytes
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm + a.off_bar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + a.off_bar + kNumBars * 8);
     volatile int *flag = reinterpret_cast<volatile int *>(sm + a.off_bar + kNumBars * 8 + 4);   // [3]
@@ -175,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&bar[kBarRawFull + s], 1);
+            mbar_init(&bar[kBarRawFull + s], kWin ? 33 : 1);   // windowed: every producer lane's copies + lane 0
             mbar_init(&bar[kBarRawEmpty + s], 5);   // 4 repack warps + the MMAs that read B
         }
         for (int b = 0; b < 2; b++) {
@@ -190,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         flag[2] = 0;   // epilogue gave up
         fence_mbar_init();
     }
-    if (warp == kWarpTma && lane == 0) {
+    if (!kWin && warp == kWarpTma && lane == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap2) : "memory");
     }
@@ -205,8 +229,54 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     const int mine = n_items > (int)blockIdx.x ? (n_items - (int)blockIdx.x + G - 1) / G : 0;
     const int total = mine * nc;   // units of this CTA
 
-    if (warp == kWarpTma) {
-        // ---------------------------------------------------------------- producer
+    if (kWin && warp == kWarpTma) {
+        // ---------------------------------------------------------------- producer (windows)
+        // lane l copies rows l, l + 32, l + 64, l + 96 of the tile as the 16-byte windows that
+        // cover their chunk (the last window holds at least one byte of the row, so it stays
+        // inside the row's allocation); lane 0 adds the planes' bulk copies
+        const uint64_t keep = policy_evict_last();
+        ItemWalk w(nc);
+        int g = 0;
+        for (int s = 0, ph = 0; g < total; ++g, w.next()) {
+            if (g >= S && !warp_wait(&bar[kBarRawEmpty + s], ph ^ 1, lane)) {
+                if (lane == 0) set_status(a.status, DEV_ST_WAIT_EMPTY);
+                break;
+            }
+            const int4 item = item_at(a, w.it);
+            const bool second = item.w >= a.T1;
+            const int tile = second ? item.w - a.T1 : item.w;
+            const uint8_t *base = (second ? a.W2 : a.W) + (size_t)item.x * (size_t)(second ? a.estride2 : a.estride) +
+                                  (size_t)w.c * kRawRow;
+            const int len = min(kRawRow, a.row_bytes - w.c * kRawRow);
+            const uint32_t mc = (uint32_t)item.z;
+            uint8_t *st = sRaw + (size_t)s * ST;
+            if (lane == 0) {
+                const size_t pr = (size_t)w.c * a.R + item.y;
+                mbar_arrive_expect_tx(&bar[kBarRawFull + s], mc * (kBRowBytes + kSfRowBytes));
+                bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
+                bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int rr = lane + 32 * i, row = tile * kRows + rr;
+                if (row >= a.n_rows) continue;
+                const uintptr_t start = reinterpret_cast<uintptr_t>(base) + (uintptr_t)row * (uintptr_t)a.row_bytes;
+                const uintptr_t end = start + (uintptr_t)len;
+                uint8_t *dst = st + rr * kWinRow;
+                for (uintptr_t p = start & ~(uintptr_t)15; p < end; p += 16, dst += 16)
+                    cp_async16(dst, reinterpret_cast<const void *>(p));
+            }
+            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bar[kBarRawFull + s]))
+                         : "memory");
+            if (++s == S) { s = 0; ph ^= 1; }
+        }
+        // nothing may land in this CTA's shared memory after it exits
+        if (lane == 0)
+            for (int h = g - S < 0 ? 0 : g - S; h < g; ++h)
+                if (!mbar_wait_bounded(&bar[kBarRawFull + h % S], (h / S) & 1)) set_status(a.status, DEV_ST_WAIT_DRAIN);
+        __syncwarp();
+    } else if (warp == kWarpTma) {
+        // ---------------------------------------------------------------- producer (TMA)
         if (lane == 0) {
             const uint64_t once = policy_evict_first(), keep = policy_evict_last();
             ItemWalk w(nc);
@@ -220,13 +290,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                 const bool second = item.w >= a.T1;
                 const int row0 = item.x * (second ? a.erows2 : a.erows) + (second ? item.w - a.T1 : item.w) * kRows;
                 const uint32_t mc = (uint32_t)item.z;
-                uint8_t *st = sRaw + (size_t)s * kStage;
+                uint8_t *st = sRaw + (size_t)s * ST;
                 const size_t pr = (size_t)w.c * a.R + item.y;
-                mbar_arrive_expect_tx(&bar[kBarRawFull + s], (uint32_t)kRawBytes + mc * (kBRowBytes + kSfRowBytes));
+                mbar_arrive_expect_tx(&bar[kBarRawFull + s], (uint32_t)RB + mc * (kBRowBytes + kSfRowBytes));
                 tma_load_2d(st, second ? &tmap2 : &tmap, w.c * (kRawRow / 2), row0, &bar[kBarRawFull + s], once);
-                bulk_g2s(st + kRawBytes, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
-                bulk_g2s(st + kRawBytes + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes,
-                         &bar[kBarRawFull + s], keep);
+                bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
+                bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
                 if (++s == S) { s = 0; ph ^= 1; }
             }
             // nothing may land in this CTA's shared memory after it exits
@@ -259,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                 const uint32_t id0 = idesc_mxf4(n, 0, 0), id2 = idesc_mxf4(n, 2, 2);
                 const uint32_t d = tmem + (uint32_t)(kAccCol + 64 * accb);
                 const uint64_t ad = ad0 + (uint64_t)(ab * (kABytes >> 4));
-                const uint64_t bd = umma_desc_sw128_sbo(smem_u32(sRaw + (size_t)s * kStage + kRawBytes), kBRowBytes);
+                const uint64_t bd = umma_desc_sw128_sbo(smem_u32(sRaw + (size_t)s * ST + RB), kBRowBytes);
                 const uint32_t sfa0 = tmem + (uint32_t)(kSfaCol + 16 * ab), sfb0 = tmem + (uint32_t)(kSfbCol + 16 * ab);
                 // K step j: atom column j / 4 (A: +16 KB, B: +1 KB) at +32 B per step; scale
                 // bytes 2 (j % 2) of the 128-K group j / 2 (the same byte id for A and B)
@@ -294,15 +363,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             bool ok = !flag[G2];
             if (ok && !warp_wait(&bar[kBarRawFull + s], (g / S) & 1, lane)) ok = false;
             uint32_t R[68];
-            const uint8_t *st = sRaw + (size_t)s * kStage;
+            const uint8_t *st = sRaw + (size_t)s * ST;
+            // valid 32-element blocks of this chunk: the last chunk of a K that is not a multiple
+            // of 512 has fewer, and its other blocks enter as zero codes with scale 1
+            const int nvalid = min(16, a.K / 32 - 16 * w.c);
             if (ok) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
+                if constexpr (kWin) {
+                    // this row's chunk starts (start mod 16) bytes into its window slot
+                    const int4 item = item_at(a, w.it);
+                    const bool second = item.w >= a.T1;
+                    const int row = (second ? item.w - a.T1 : item.w) * kRows + m;
+                    const uintptr_t start = reinterpret_cast<uintptr_t>(second ? a.W2 : a.W) +
+                                            (uintptr_t)item.x * (uintptr_t)(second ? a.estride2 : a.estride) +
+                                            (uintptr_t)w.c * kRawRow + (uintptr_t)row * (uintptr_t)a.row_bytes;
+                    const int off = (int)(start & 15), sh = (off & 3) * 8;
+                    const uint32_t *wp = reinterpret_cast<const uint32_t *>(st + m * kWinRow + (off & ~3));
+                    uint32_t prev = wp[0];
 #pragma unroll
-                for (int i = 0; i < 17; i++) {
-                    const uint4 v = src[i];
-                    R[4 * i] = v.x; R[4 * i + 1] = v.y; R[4 * i + 2] = v.z; R[4 * i + 3] = v.w;
+                    for (int i = 0; i < 68; i++) {
+                        const uint32_t nxt = wp[i + 1];
+                        R[i] = __funnelshift_r(prev, nxt, sh);
+                        prev = nxt;
+                    }
+                } else {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
+#pragma unroll
+                    for (int i = 0; i < 17; i++) {
+                        const uint4 v = src[i];
+                        R[4 * i] = v.x; R[4 * i + 1] = v.y; R[4 * i + 2] = v.z; R[4 * i + 3] = v.w;
+                    }
                 }
             }
+            // windowed: every row of the group is in registers before the scale words below
+            // overwrite the start of the stage
+            if (kWin) named_bar_sync(1 + G2, 128);
+            uint32_t *sx = kWin ? reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(st)) : sfx + ab * 4 * kRows;
             if (ok && g >= 2 && !warp_wait(&bar[kBarAFree + ab], ((g >> 1) - 1) & 1, lane)) ok = false;
             if (ok) {
                 uint8_t *dstA = sA + ab * kABytes + rowoff;
@@ -318,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                         v.z = __funnelshift_r(R[wd + 2], R[wd + 3], sh);
                         v.w = __funnelshift_r(R[wd + 3], R[wd + 4], sh);
                     }
+                    if (b >= nvalid) v = make_uint4(0u, 0u, 0u, 0u);
                     *reinterpret_cast<uint4 *>(dstA + (b >> 3) * kAAtom + (((b & 7) ^ m8) << 4)) = v;
                 }
                 // A scale bytes e(b) at byte 17 b of the row chunk, four per word (one 128-K group)
@@ -326,7 +422,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     const int o0 = 17 * (4 * gi), o1 = o0 + 17, o2 = o0 + 34, o3 = o0 + 51;
                     const uint32_t t01 = __byte_perm(R[o0 >> 2], R[o1 >> 2], (uint32_t)((o0 & 3) | ((4 + (o1 & 3)) << 4)));
                     const uint32_t t23 = __byte_perm(R[o2 >> 2], R[o3 >> 2], (uint32_t)((o2 & 3) | ((4 + (o3 & 3)) << 4)));
-                    sfx[(ab * 4 + gi) * kRows + m] = __byte_perm(t01, t23, 0x5410);
+                    uint32_t wd = __byte_perm(t01, t23, 0x5410);
+                    if (4 * gi + 4 > nvalid) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            if (4 * gi + j >= nvalid) wd = (wd & ~(0xFFu << (8 * j))) | (0x7Fu << (8 * j));
+                    }
+                    sx[gi * kRows + m] = wd;
                 }
             } else {
                 flag[G2] = 1;
@@ -339,14 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
 #pragma unroll
             for (int gi = 0; gi < 4; gi++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) v[4 * gi + j] = sfx[(ab * 4 + gi) * kRows + lane + 32 * j];
+                for (int j = 0; j < 4; j++) v[4 * gi + j] = sx[gi * kRows + lane + 32 * j];
             tmem_st16(tq + (uint32_t)(kSfaCol + 16 * ab), v);
             // B scale words, in the same layout: column 4 gi + j of lane r = the 4 scale bytes
             // of 128-K group gi of B column n = r + 32 j; columns past N carry scale 1 (their B
-            // rows are never read).  The stage is released here: its B planes stay until the
-            // MMAs that read them commit (the fifth arrival)
+            // rows are never read)
             const int n_cols = kMxf4Planes * item_at(a, w.it).z;
-            const uint8_t *sf = st + kRawBytes + kBBytes;
+            const uint8_t *sf = st + RB + kBBytes;
             uint32_t vb[16];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -356,13 +457,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     vb[4 * gi + j] = n < n_cols ? *reinterpret_cast<const uint32_t *>(sf + n * 16 + 4 * gi) : 0x7F7F7F7Fu;
             }
             tmem_st16(tq + (uint32_t)(kSfbCol + 16 * ab), vb);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar[kBarRawEmpty + s]);
             tmem_st_wait();
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bar[kBarAFull + ab]);
+            // the stage is released (its B planes stay until the MMAs that read them commit: the
+            // fifth arrival) and the A buffer handed to the MMA
+            if (lane == 0) {
+                mbar_arrive(&bar[kBarRawEmpty + s]);
+                mbar_arrive(&bar[kBarAFull + ab]);
+            }
         }
         if (flag[G2]) set_status(a.status, DEV_ST_WAIT_FULL);
     } else {
@@ -423,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     }
 }
 
-// MLQ_MOE_MXF4_TC: 0 off, 1 (default) when the items fill the GPU at least once, 2 always
+// MLQ_MOE_MXF4_TC: 0 off, 1 (default) when the items fill the GPU at least twice, 2 always
 int mxf4_group_mode() {
     static int v = -1;
     if (v < 0) {
@@ -436,13 +540,15 @@ int mxf4_group_mode() {
 
 }  // namespace
 
-// at least one item per SM: min(R, E) active (expert, 8-row chunk) pairs x tiles per chunk
+// at least two items per SM, estimated as min(R, E) active (expert, 8-row chunk) pairs x tiles
+// per chunk: with fewer, the SMs that get a second item set the time (config 4 at one token,
+// 4 experts x 46 tiles = 184 items: 4.69 ms per step against 4.15 on the grouped GEMV)
 bool mxf4_grouped_wanted(int R, int E, int item_tiles) {
     const int mode = mxf4_group_mode();
     if (mode == 0) return false;
     if (mode >= 2) return true;
     const LaunchEnv *env = launch_env();
-    return env && (long long)(R < E ? R : E) * item_tiles >= env->num_sms;
+    return env && (long long)(R < E ? R : E) * item_tiles >= 2ll * env->num_sms;
 }
 
 size_t mxf4_planes_bytes(int R, int K) {
@@ -450,23 +556,29 @@ size_t mxf4_planes_bytes(int R, int K) {
     return nc * (size_t)R * (kBRowBytes + kSfRowBytes);
 }
 
-// The expert matrices as TMA tiles: K a multiple of 512 (rows of whole 272-byte chunks, a row
-// pitch that is a multiple of 16 bytes), a 16-byte-aligned base, experts a whole number of
-// rows apart, and every row index inside int range.
-bool mxf4_grouped_supported(const uint8_t *W, long long estride, int E, int n_rows, int K) {
-    if (!mxf4_group_mode() || !W || K <= 0 || K % kChunkK || n_rows <= 0 || E <= 0 || ((uintptr_t)W & 15))
-        return false;
+// Whether the expert matrices can be TMA tiles: K a multiple of 512 (rows of whole 272-byte
+// chunks, a row pitch that is a multiple of 16 bytes), a 16-byte-aligned base, experts a whole
+// number of rows apart, and every row index inside int range.  Otherwise the kernel copies each
+// row's chunks as 16-byte windows (any K % 32 == 0, any alignment).
+static bool mxf4_tma_ok(const uint8_t *W, long long estride, int E, int n_rows, int K) {
+    if (K % kChunkK || ((uintptr_t)W & 15)) return false;
     const long long row_bytes = (long long)(K / 32) * 17;
-    if (estride < row_bytes * n_rows || estride % row_bytes) return false;
+    if (estride % row_bytes) return false;
     return (long long)(E - 1) * (estride / row_bytes) + n_rows < (1ll << 31);
+}
+
+bool mxf4_grouped_supported(const uint8_t *W, long long estride, int E, int n_rows, int K) {
+    if (!mxf4_group_mode() || !W || K <= 0 || K % 32 || n_rows <= 0 || E <= 0) return false;
+    return estride >= (long long)(K / 32) * 17 * n_rows;
 }
 
 int launch_mxf4_planes_rows(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp,
                             int R, int K, uint8_t *planes, cudaStream_t s) {
     if (R <= 0) return MLQ_OK;
-    if (K % kChunkK) return MLQ_ERR_UNSUPPORTED;
-    const long long groups = (long long)R * (K / 32);
-    uint8_t *scales = planes + (size_t)(K / kChunkK) * R * kBRowBytes;
+    if (K <= 0 || K % 32) return MLQ_ERR_UNSUPPORTED;
+    const int nc = (K + kChunkK - 1) / kChunkK;
+    const long long groups = (long long)R * nc * (kChunkK / 32);
+    uint8_t *scales = planes + (size_t)nc * R * kBRowBytes;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -491,36 +603,49 @@ static int launch_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2
         return MLQ_ERR_UNSUPPORTED;
     const LaunchEnv *env = launch_env();
     if (!env) return MLQ_ERR_NO_DEVICE;
+    const int nc = (K + kChunkK - 1) / kChunkK;
     const long long row_bytes = (long long)(K / 32) * 17;
-    const long long erows = estride / row_bytes, erows2 = W2 ? estride2 / row_bytes : 0;
-    CUtensorMap tmap, tmap2;
-    if (!tc_tensor_map_rows(&tmap, W, (E - 1) * erows + n_rows, row_bytes, kRawRow, kRows)) return MLQ_ERR_UNSUPPORTED;
-    if (!tc_tensor_map_rows(&tmap2, W2 ? W2 : W, W2 ? (E - 1) * erows2 + n_rows : (E - 1) * erows + n_rows, row_bytes,
-                            kRawRow, kRows))
-        return MLQ_ERR_UNSUPPORTED;
+    const bool tma = mxf4_tma_ok(W, estride, E, n_rows, K) && (!W2 || mxf4_tma_ok(W2, estride2, E, n_rows, K));
+    const long long erows = tma ? estride / row_bytes : 0, erows2 = tma && W2 ? estride2 / row_bytes : 0;
+    CUtensorMap tmap{}, tmap2{};
+    if (tma) {
+        if (!tc_tensor_map_rows(&tmap, W, (E - 1) * erows + n_rows, row_bytes, kRawRow, kRows) ||
+            !tc_tensor_map_rows(&tmap2, W2 ? W2 : W, W2 ? (E - 1) * erows2 + n_rows : (E - 1) * erows + n_rows,
+                                row_bytes, kRawRow, kRows))
+            return MLQ_ERR_UNSUPPORTED;
+    }
+    // shared memory: 2 A buffers, (TMA) the A scale words, barriers, then the stages
+    const int stage = tma ? StageLayout<false>::bytes : StageLayout<true>::bytes;
     const int off_sfx = 2 * kABytes;
-    const int off_bar = off_sfx + 2 * 4 * kRows * 4;
+    const int off_bar = off_sfx + (tma ? 2 * 4 * kRows * 4 : 0);
     const int off_raw = (off_bar + kBarBytes + 1023) / 1024 * 1024;
-    int n_stages = (kSmemMax - 1024 - off_raw) / kStage;
+    int n_stages = (kSmemMax - 1024 - off_raw) / stage;
     if (n_stages > kMaxStages) n_stages = kMaxStages;
     if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
-    const int smem = 1024 + off_raw + n_stages * kStage;
-    static bool attr = false;
-    if (!attr) {
-        if (!MLQ_CUDA(cudaFuncSetAttribute(k_moe_mxf4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax)))
+    const int smem = 1024 + off_raw + n_stages * stage;
+    static bool attr[2] = {false, false};
+    if (!attr[tma]) {
+        if (!MLQ_CUDA(cudaFuncSetAttribute(tma ? k_moe_mxf4_tc<false> : k_moe_mxf4_tc<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax)))
             return MLQ_ERR_CUDA;
-        attr = true;
+        attr[tma] = true;
     }
     GroupMxf4Args a{};
+    a.W = W;
+    a.W2 = W2 ? W2 : W;
+    a.estride = estride;
+    a.estride2 = W2 ? estride2 : estride;
+    a.row_bytes = (int)row_bytes;
+    a.K = K;
     a.items = reinterpret_cast<const int4 *>(items);
     a.n_items = n_items_dev;
     a.planes = planes;
-    a.scales = planes + (size_t)(K / kChunkK) * R * kBRowBytes;
+    a.scales = planes + (size_t)nc * R * kBRowBytes;
     a.out = out;
     a.out2 = out2;
     a.out_rows = out_rows;
     a.n_rows = n_rows;
-    a.nc = K / kChunkK;
+    a.nc = nc;
     a.R = R;
     a.T1 = (n_rows + kRows - 1) / kRows;
     a.erows = (int)erows;
@@ -542,7 +667,9 @@ static int launch_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2
     cfg.gridDim = dim3((unsigned)(n_items_bound < env->num_sms ? n_items_bound : env->num_sms));
     cfg.dynamicSmemBytes = (size_t)smem;
     count_launch();
-    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_moe_mxf4_tc, tmap, tmap2, a)) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, tma ? k_moe_mxf4_tc<false> : k_moe_mxf4_tc<true>, tmap, tmap2, a))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 int launch_moe_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2, long long estride2, int E, int n_rows,

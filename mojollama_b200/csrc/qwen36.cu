@@ -345,9 +345,9 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
     float *attn_scr = (float *)cs.scratch(attn_sb);
     // shared experts on the block-scaled tensor cores: the rows' E2M1 planes (input, SwiGLU)
     uint8_t *shp_x = nullptr, *shp_h = nullptr;
-    if (max_si > 0 && B >= 2 && N % 512 == 0) {
+    if (max_si > 0 && B >= 2) {
         shp_x = (uint8_t *)cs.scratch(mxf4_planes_bytes(B, N));
-        shp_h = (uint8_t *)cs.scratch(mxf4_planes_bytes(B, (max_si + 511) / 512 * 512));
+        shp_h = (uint8_t *)cs.scratch(mxf4_planes_bytes(B, max_si));
     }
     // reference-compatibility V columns beyond the projection come from ws's qkv slice
     const float *v_ext = nullptr;
@@ -537,7 +537,7 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
             k_shexp_score<<<B, 256, 0, s>>>(xn, sr, score, N);
             count_launch();
-            if (shp_x && sgq == MLQ_MXFP4 && suq == MLQ_MXFP4 && sdq == MLQ_MXFP4 && si % 512 == 0 &&
+            if (shp_x && sgq == MLQ_MXFP4 && suq == MLQ_MXFP4 && sdq == MLQ_MXFP4 && si % 32 == 0 &&
                 mxf4_dense_supported(sg, si, N) && mxf4_dense_supported(su, si, N) && mxf4_dense_supported(sd, N, si)) {
                 // MXFP4 (the GGUF shared-expert type): gate and up in one launch of the grouped
                 // block-scaled kernel over all B rows, silu(clamp(g, +-80)) * u encoded, then down

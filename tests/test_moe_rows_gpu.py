@@ -173,8 +173,12 @@ lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 # Bars: 1e-3 for weights quantized from N(0, 0.02) values (measured: block-scaled 1.2e-5,
 # GEMV 5e-5); 1e-2 for random blocks, whose E8M0 scales span 2^-27..2^13 within a row so that
 # the fp32 sums cancel heavily (measured: block-scaled 1.6e-3, GEMV 7.6e-3)
+# GPT-OSS width (K = 2880: 1530-byte rows, 16-byte windows, a last chunk of 10 blocks; down
+# K = 320: one partial chunk, 23 row tiles the last half full) and 51- / 85-byte rows (odd row
+# addresses)
 for (E, N, FF, R, seed, kind, packed) in ((8, 512, 512, 64, 7, "random", False), (12, 2048, 512, 40, 9, "quant", False),
-                                          (32, 1024, 1024, 80, 11, "quant", True), (4, 512, 1024, 37, 13, "random", True)):
+                                          (32, 1024, 1024, 80, 11, "quant", True), (4, 512, 1024, 37, 13, "random", True),
+                                          (4, 2880, 320, 24, 17, "quant", False), (3, 96, 160, 30, 19, "random", True)):
     rng = np.random.default_rng(seed)
     def ex(rows, cols):
         if kind == "random":
@@ -222,7 +226,7 @@ for (E, N, FF, R, seed, kind, packed) in ((8, 512, 512, 64, 7, "random", False),
 
 @pytest.mark.parametrize("mode", ["2", "0"])
 def test_moe_rows_block_scaled_path(mode):
-    """MXFP4 experts with K a multiple of 512 on the block-scaled tensor cores (MLQ_MOE_MXF4_TC=2:
+    """MXFP4 experts on the block-scaled tensor cores (MLQ_MOE_MXF4_TC=2:
     taken at every size; read once per process, so a child process) and, with 0, the same cases
     on the grouped GEMV: the sorted rows encoded once as 8 E2M1 planes each, 128-row tiles of
     one expert against its chunk of up to 8 rows, dense and packed (in-band id) input rows"""
