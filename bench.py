@@ -1857,10 +1857,47 @@ def run_profile_case(fmt: str, rows: int, launches: int = 3) -> int:
     return 0
 
 
+def run_moe_profile(shape: str, launches: int = 3) -> int:
+    """Small case for ncu of the grouped MXFP4 expert kernels: `shape` = E,N,FF,R (experts,
+    model width, expert width, routed rows), random MXFP4 experts with small scales, rows
+    spread uniformly over the experts; mlq_moe_rows two warm-up calls then `launches` more.
+    Prints each call's device time and the expert bytes it streams."""
+    import torch
+    from mojollama_b200 import core
+    E, N, FF, R = (int(v) for v in shape.split(","))
+    lib = core()
+    assert lib.mlq_init(0) == 0
+    lib.mlq_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rb_n, rb_f = N // 32 * 17, FF // 32 * 17
+    mats = [_random_blocks(torch, 39, E * FF * N // 32, g), _random_blocks(torch, 39, E * FF * N // 32, g),
+            _random_blocks(torch, 39, E * N * FF // 32, g)]
+    eid = torch.from_numpy(np.random.default_rng(5).integers(0, E, R).astype(np.int32)).cuda()
+    x = torch.randn(R, N, device="cuda") * 0.5
+    y = torch.empty(R, N, device="cuda")
+    active = int(torch.unique(eid).numel())
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    times = []
+    for i in range(2 + launches):
+        evs[0].record()
+        rc = lib.mlq_moe_rows(39, 39, 39, vp(mats[0]), vp(mats[1]), vp(mats[2]), rb_n * FF, rb_n * FF, rb_f * N, E,
+                              vp(eid), R, FF, N, vp(x), vp(y))
+        evs[1].record()
+        assert rc == 0, lib.mlq_last_error_message()
+        torch.cuda.synchronize()
+        if i >= 2:
+            times.append(round(evs[0].elapsed_time(evs[1]) * 1e3, 1))
+    print(json.dumps({"moe_profile": [E, N, FF, R], "active_experts": active, "us_per_call": times,
+                      "expert_bytes": active * (2 * FF * rb_n + N * rb_f)}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile", default=None, help="run the small single-kernel ncu case for FORMAT")
     ap.add_argument("--profile-rows", type=int, default=65536)
+    ap.add_argument("--moe-profile", default=None, help="grouped MXFP4 expert case for ncu: E,N,FF,R")
     ap.add_argument("--profile-tc", default=None, help="small tensor-core GEMM case for ncu: FORMAT")
     ap.add_argument("--profile-m", type=int, default=64)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1900,6 +1937,8 @@ def main():
         return run_profile_case(args.profile, args.profile_rows)
     if args.profile_tc:
         return run_profile_tc(args.profile_tc, args.profile_rows, args.profile_m)
+    if args.moe_profile:
+        return run_moe_profile(args.moe_profile)
     if args.decode_only:
         return run_decode_only(args)
     if args.decode_profile:
