@@ -72,7 +72,12 @@ constexpr int kSmemMax = 232448;
 
 constexpr int kBarRawFull = 0, kBarRawEmpty = 4, kBarAFull = 8, kBarAFree = 10, kBarAccFull = 12,
               kBarAccEmpty = 14, kBarDrain = 16, kNumBars = 17;
-constexpr int kBarBytes = kNumBars * 8 + 32;     // + TMEM base slot + flags
+// after the barriers: TMEM base slot + flags, then each stage's work item, written by the producer
+// before the stage's copies are armed (the MMA thread and the repack warps read it from here
+// after the stage's full-barrier wait, instead of loading it from global memory per unit)
+constexpr int kItemOff = 192;
+constexpr int kBarBytes = kItemOff + 16 * kMaxStages;
+static_assert(kNumBars * 8 + 16 <= kItemOff, "item records follow the barriers and flags");
 
 // Rows that cannot be TMA tiles (a row pitch that is not a multiple of 16 bytes, K not a
 // multiple of 512): each row's chunk arrives as the 16-byte-aligned windows that cover it
@@ -188,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm + a.off_bar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + a.off_bar + kNumBars * 8);
     volatile int *flag = reinterpret_cast<volatile int *>(sm + a.off_bar + kNumBars * 8 + 4);   // [3]
+    int4 *s_item = reinterpret_cast<int4 *>(sm + a.off_bar + kItemOff);                       // [kMaxStages]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.n_stages, nc = a.nc;
 
@@ -236,13 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         // inside the row's allocation); lane 0 adds the planes' bulk copies
         const uint64_t keep = policy_evict_last();
         ItemWalk w(nc);
+        // the current item and the next one, loaded an item ahead
+        int4 item = total ? item_at(a, w.it) : make_int4(0, 0, 0, 0);
+        int4 nxt = w.it + G < n_items ? item_at(a, w.it + G) : item;
         int g = 0;
         for (int s = 0, ph = 0; g < total; ++g, w.next()) {
             if (g >= S && !warp_wait(&bar[kBarRawEmpty + s], ph ^ 1, lane)) {
                 if (lane == 0) set_status(a.status, DEV_ST_WAIT_EMPTY);
                 break;
             }
-            const int4 item = item_at(a, w.it);
             const bool second = item.w >= a.T1;
             const int tile = second ? item.w - a.T1 : item.w;
             const uint8_t *base = (second ? a.W2 : a.W) + (size_t)item.x * (size_t)(second ? a.estride2 : a.estride) +
@@ -252,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             uint8_t *st = sRaw + (size_t)s * ST;
             if (lane == 0) {
                 const size_t pr = (size_t)w.c * a.R + item.y;
+                s_item[s] = item;
                 mbar_arrive_expect_tx(&bar[kBarRawFull + s], mc * (kBRowBytes + kSfRowBytes));
                 bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
                 bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
@@ -268,6 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             }
             asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bar[kBarRawFull + s]))
                          : "memory");
+            if (w.c == nc - 1) {
+                item = nxt;
+                if (w.it + 2 * G < n_items) nxt = item_at(a, w.it + 2 * G);
+            }
             if (++s == S) { s = 0; ph ^= 1; }
         }
         // nothing may land in this CTA's shared memory after it exits
@@ -280,22 +293,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         if (lane == 0) {
             const uint64_t once = policy_evict_first(), keep = policy_evict_last();
             ItemWalk w(nc);
+            int4 item = total ? item_at(a, w.it) : make_int4(0, 0, 0, 0);
+            int4 nxt = w.it + G < n_items ? item_at(a, w.it + G) : item;
             int g = 0;
             for (int s = 0, ph = 0; g < total; ++g, w.next()) {
                 if (g >= S && !mbar_wait_bounded(&bar[kBarRawEmpty + s], ph ^ 1)) {
                     set_status(a.status, DEV_ST_WAIT_EMPTY);
                     break;
                 }
-                const int4 item = item_at(a, w.it);
                 const bool second = item.w >= a.T1;
                 const int row0 = item.x * (second ? a.erows2 : a.erows) + (second ? item.w - a.T1 : item.w) * kRows;
                 const uint32_t mc = (uint32_t)item.z;
                 uint8_t *st = sRaw + (size_t)s * ST;
                 const size_t pr = (size_t)w.c * a.R + item.y;
+                s_item[s] = item;
                 mbar_arrive_expect_tx(&bar[kBarRawFull + s], (uint32_t)RB + mc * (kBRowBytes + kSfRowBytes));
                 tma_load_2d(st, second ? &tmap2 : &tmap, w.c * (kRawRow / 2), row0, &bar[kBarRawFull + s], once);
                 bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
                 bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
+                if (w.c == nc - 1) {
+                    item = nxt;
+                    if (w.it + 2 * G < n_items) nxt = item_at(a, w.it + 2 * G);
+                }
                 if (++s == S) { s = 0; ph ^= 1; }
             }
             // nothing may land in this CTA's shared memory after it exits
@@ -324,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     break;
                 }
                 tc_fence_after();
-                const int n = kMxf4Planes * item_at(a, w.it).z;
+                const int n = kMxf4Planes * s_item[s].z;
                 const uint32_t id0 = idesc_mxf4(n, 0, 0), id2 = idesc_mxf4(n, 2, 2);
                 const uint32_t d = tmem + (uint32_t)(kAccCol + 64 * accb);
                 const uint64_t ad = ad0 + (uint64_t)(ab * (kABytes >> 4));
@@ -370,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             if (ok) {
                 if constexpr (kWin) {
                     // this row's chunk starts (start mod 16) bytes into its window slot
-                    const int4 item = item_at(a, w.it);
+                    const int4 item = s_item[s];
                     const bool second = item.w >= a.T1;
                     const int row = (second ? item.w - a.T1 : item.w) * kRows + m;
                     const uintptr_t start = reinterpret_cast<uintptr_t>(second ? a.W2 : a.W) +
@@ -446,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
             // B scale words, in the same layout: column 4 gi + j of lane r = the 4 scale bytes
             // of 128-K group gi of B column n = r + 32 j; columns past N carry scale 1 (their B
             // rows are never read)
-            const int n_cols = kMxf4Planes * item_at(a, w.it).z;
+            const int n_cols = kMxf4Planes * s_item[s].z;
             const uint8_t *sf = st + RB + kBBytes;
             uint32_t vb[16];
 #pragma unroll
