@@ -283,6 +283,8 @@ __global__ void k_attn_merge(const float *__restrict__ part_ml, const float *__r
 // KV append: row (b, pos_b) of K and V gets k_new/v_new [B][NKH*HD]
 __global__ void k_kv_write(KVView kv, float *k_base, float *v_base, const float *__restrict__ k_new,
                            const float *__restrict__ v_new, const int *__restrict__ pos, int pos_scalar, int row) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int b = blockIdx.y;
     const int t = pos ? pos[b] : pos_scalar;
     const long long off = kv_offset(kv, b, t);
@@ -454,9 +456,7 @@ int launch_rope_kv(float *q, float *k, const float *v, int B, int nh, int nkh, i
 int launch_kv_write(const KVView &kv, float *k_base, float *v_base, const float *k_new, const float *v_new,
                     const int *pos_dev, int pos_scalar, int B, int row, cudaStream_t s) {
     dim3 grid((row + 255) / 256, B);
-    k_kv_write<<<grid, 256, 0, s>>>(kv, k_base, v_base, k_new, v_new, pos_dev, pos_scalar, row);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_kv_write, dim3(grid), dim3(256), 0, s, kv, k_base, v_base, k_new, v_new, pos_dev, pos_scalar, row)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 size_t attn_scratch_bytes(int B, int nh, int hd) { return (size_t)B * nh * 64 * (hd + 2) * sizeof(float); }

@@ -47,6 +47,8 @@ constexpr int kTcAtomBytes = 16384;   // one 64-wide K atom of the A tile: 128 r
 // row); rows M..Mp-1 are zero with scale 0.
 __global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh, float *__restrict__ scale, int M,
                            int K, int Kp) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     __shared__ float sh[32];
     const int t = blockIdx.x;
     __half *dst = xh + (size_t)t * Kp;
@@ -93,6 +95,8 @@ __global__ void k_x_to_f16(const float *__restrict__ x, __half *__restrict__ xh,
 __global__ void k_rows_to_f16(const float *__restrict__ x, const float *__restrict__ x2, const int *__restrict__ rows,
                               int row_div, int x_stride, float clamp, int K, int Kp, __half *__restrict__ xh,
                               __half *__restrict__ xl, float *__restrict__ scale) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     __shared__ float sh[32];
     const int p = blockIdx.x;
     int r = rows ? __ldg(rows + p) : p;
@@ -494,6 +498,8 @@ struct TcSmem {
 
 template <int QT, int NT>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(TcArgs a) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     using S = TcSmem<QT, NT>;
     extern __shared__ uint8_t smem_raw[];
     // operand atoms must start on 1024-byte boundaries
@@ -938,9 +944,8 @@ static int launch_tc_t(const TcArgs &a, int n_tok_tiles, cudaStream_t s) {
     int gx = env->num_sms / n_tok_tiles;
     if (gx < 1) gx = 1;
     if (gx > a.n_row_tiles * a.n_splits) gx = a.n_row_tiles * a.n_splits;
-    k_gemm_tc<QT, NT><<<dim3(gx, n_tok_tiles), kTcThreads, S::total, s>>>(a);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_gemm_tc<QT, NT>, dim3(gx, n_tok_tiles), dim3(kTcThreads), S::total, s, a)) ? MLQ_OK
+                                                                                                             : MLQ_ERR_CUDA;
 }
 
 template <int QT>
@@ -984,9 +989,7 @@ int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_r
     int *counters = n_splits > 1 ? (int *)(scr + xh_bytes + xs_bytes) : nullptr;
     float *part = n_splits > 1 ? (float *)(scr + xh_bytes + xs_bytes + cnt_bytes) : nullptr;
     if (counters && !MLQ_CUDA(cudaMemsetAsync(counters, 0, n_tiles * sizeof(int), s))) return MLQ_ERR_CUDA;
-    k_x_to_f16<<<Mp, 256, 0, s>>>(x, xh, xs, M, K, Kp);
-    count_launch();
-    if (!MLQ_CUDA(cudaGetLastError())) return MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(launch_pdl_k(k_x_to_f16, dim3(Mp), dim3(256), 0, s, x, xh, xs, M, K, Kp))) return MLQ_ERR_CUDA;
     const bool block32 = qt == MLQ_Q8_0 || qt == MLQ_Q4_0 || qt == MLQ_Q4_1 || qt == MLQ_Q5_0 || qt == MLQ_MXFP4;
     // (MXFP4 chunks are 136 bytes: never all on 16-byte boundaries)
     const int win = block32 && (qt == MLQ_MXFP4 || K % kTcKC != 0 || rb % 16 != 0 || ((uintptr_t)W & 15) != 0);
@@ -1012,10 +1015,8 @@ size_t tc_grouped_xh_bytes(int R, int K) { return (size_t)R * tc_kp(K) * sizeof(
 int launch_rows_to_f16(const float *x, const float *x2, const int *rows, int row_div, int x_stride, float clamp, int R,
                        int K, __half *xh, __half *xl, float *xs, cudaStream_t s) {
     if (R <= 0) return MLQ_OK;
-    k_rows_to_f16<<<R, 256, 0, s>>>(x, x2, rows, row_div, x_stride > 0 ? x_stride : K, clamp, K, tc_kp(K), xh, xl,
-                                    xs);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_rows_to_f16, dim3(R), dim3(256), 0, s, x, x2, rows, row_div, x_stride > 0 ? x_stride : K, clamp, K, tc_kp(K), xh, xl,
+                                    xs)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 bool tc_grouped_supported(int qt, const uint8_t *W, long long estride, int K) {
@@ -1035,9 +1036,8 @@ static int launch_tc_grouped_q(const TcArgs &a, int grid, cudaStream_t s) {
             return MLQ_ERR_CUDA;
         attr = true;
     }
-    k_gemm_tc<QT, 16><<<dim3(grid, 1), kTcThreads, S::total, s>>>(a);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_gemm_tc<QT, 16>, dim3(grid, 1), dim3(kTcThreads), S::total, s, a)) ? MLQ_OK
+                                                                                                       : MLQ_ERR_CUDA;
 }
 
 // Grouped experts on the tensor cores: k_group_plan's items (tiles of 128 rows, chunks of up

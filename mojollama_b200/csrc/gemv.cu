@@ -511,6 +511,8 @@ template <typename WT>
 __global__ void __launch_bounds__(256) k_gemv_float_rows(const WT *__restrict__ W, const float *__restrict__ x,
                                                          float *__restrict__ out, int n_rows, int K, int nb_x,
                                                          int vec_ok) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     constexpr int V = 16 / sizeof(WT);
     __shared__ float part[8][kFewRowsMaxB];
     const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -572,7 +574,7 @@ __global__ void __launch_bounds__(256) k_gemv_float_rows(const WT *__restrict__ 
 // Launch with programmatic stream serialization: the kernel may start while the previous
 // kernel on the stream finishes; it calls pdl_wait() before touching anything that kernel
 // writes.  MLQ_NO_PDL=1 launches normally.
-static bool pdl_enabled() {
+bool pdl_enabled() {
     static int v = -1;
     if (v < 0) {
         const char *e = getenv("MLQ_NO_PDL");
@@ -800,6 +802,10 @@ static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, in
     // 147 us in four passes, 318 us through the fp16 decode of the GEMM)
     int tc_from = tc_min_m();
     if (QT == MLQ_MXFP4 && n_rows >= 16384 && tc_from > 0 && tc_from < 32) tc_from = 32;
+    // MXFP4 rows that fit one pass of the block-scaled GEMV (up to 8 at K <= 1024) stay there:
+    // one launch, against the GEMM's activation conversion plus its own launch
+    const int mx_pass = K <= 1024 ? 8 : K <= 2048 ? 4 : K <= 4096 ? 2 : 1;
+    if (QT == MLQ_MXFP4 && B <= mx_pass) tc_from = 0;
     if (tc_from > 0 && B >= tc_from) {
         const int rc = launch_gemm_tc(W, QT, x, out, n_rows, K, B, s);
         if (rc != MLQ_ERR_UNSUPPORTED) return rc;
@@ -807,7 +813,7 @@ static int launch_q(const uint8_t *W, const float *x, float *out, int n_rows, in
     if constexpr (QT == MLQ_MXFP4) {
         // block-scaled tensor cores: groups of up to 8 activation rows per weight pass
         int b = 0, rc = MLQ_OK;
-        const int g = K <= 1024 ? 8 : K <= 2048 ? 4 : K <= 4096 ? 2 : 1;
+        const int g = mx_pass;
         for (; b < B && rc == MLQ_OK; b += g) {
             const int take = B - b < g ? B - b : g;
             rc = launch_gemv_mxf4_tc(W, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K, take, s);
@@ -868,11 +874,11 @@ static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows
         // too few rows for a warp each to fill the GPU: a CTA per row
         for (int b = 0; b < B; b += kFewRowsMaxB) {
             const int take = (B - b) < kFewRowsMaxB ? (B - b) : kFewRowsMaxB;
-            k_gemv_float_rows<WT><<<n_rows, 256, 0, s>>>(w, x + (size_t)b * K, out + (size_t)b * n_rows, n_rows, K,
-                                                         take, vec_ok);
-            count_launch();
+            if (!MLQ_CUDA(launch_pdl_k(k_gemv_float_rows<WT>, dim3(n_rows), dim3(256), 0, s, w, x + (size_t)b * K,
+                                       out + (size_t)b * n_rows, n_rows, K, take, vec_ok)))
+                return MLQ_ERR_CUDA;
         }
-        return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+        return MLQ_OK;
     }
     const int warps = n_rows;
     int grid = (warps * 32 + 255) / 256;
@@ -1256,6 +1262,8 @@ struct PlanLists {
 __global__ void __launch_bounds__(kPlanThreads) k_group_plan(const int *__restrict__ eid, int eid_stride, int R, int E,
                                                              PlanLists pl, int *__restrict__ sorted_pos,
                                                              int *__restrict__ src_row, int *__restrict__ n_items) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     extern __shared__ int sm_plan[];
     int *run = sm_plan;          // [E] counts, then running positions
     int *so = run + E;           // [E + 1] first sorted position of each expert
@@ -1511,9 +1519,10 @@ int launch_group_plan(const int *eid, int R, int E, int n_lists, void *const *it
         pl.tiles[l] = tiles[l];
     }
     const size_t sm = sizeof(int) * (3 * (size_t)E + 2 + (size_t)kPlanWarps * E);
-    k_group_plan<<<1, kPlanThreads, sm, s>>>(eid, eid_stride, R, E, pl, sorted_pos, src_row, n_items);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_group_plan, dim3(1), dim3(kPlanThreads), sm, s, eid, eid_stride, R, E, pl,
+                                 sorted_pos, src_row, n_items))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------------------ decode GEMV

@@ -53,6 +53,26 @@ struct LaunchEnvScope {
 cudaStream_t stream();
 int *dev_status();
 void count_launch(int n = 1);
+// Programmatic dependent launch (MLQ_NO_PDL=1 turns it off): the kernel may be scheduled while
+// the previous kernel on the stream drains; it must execute griddepcontrol.wait (pdl_wait())
+// before it reads or writes any memory that kernel touches.  Counts the launch.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 bool ref_compat();
 
 // ---- pointer handling ------------------------------------------------------------------

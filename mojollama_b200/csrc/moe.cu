@@ -417,6 +417,8 @@ int launch_moe_experts(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
 // renormalisation of the k weights (1/(sum + 1e-10)).
 __global__ void k_router_topk(const float *__restrict__ logits, int B, int E, int k, int renorm,
                               int *__restrict__ idx, float *__restrict__ w) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (b >= B) return;
@@ -480,9 +482,7 @@ int launch_router_topk(const float *logits, int B, int E, int k, int renorm, int
         set_error(MLQ_ERR_CAPACITY, "router: %d experts, top-%d (at most 256 experts)", E, k);
         return MLQ_ERR_CAPACITY;
     }
-    k_router_topk<<<(B * 32 + 127) / 128, 128, 0, s>>>(logits, B, E, k, renorm, idx, w);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_router_topk, dim3((B * 32 + 127) / 128), dim3(128), 0, s, logits, B, E, k, renorm, idx, w)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 }  // namespace mlq

@@ -58,6 +58,8 @@ __device__ __forceinline__ float block_max(float v, float *sh) {
 // input to `res` (the reference's residual copy); bit1: in-place allowed (always true)
 __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
                            float *__restrict__ res, int n, float eps, int flags) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     __shared__ float sh[32];
     const float *xr = x + (size_t)blockIdx.x * n;
     float *orow = out + (size_t)blockIdx.x * n;
@@ -129,6 +131,8 @@ __global__ void __launch_bounds__(256) k_rms_norm_encode(float *__restrict__ out
 
 // mode 0: exact x/(1+exp(-x)); mode 1: simd_ops.c's Pade tanh body + exact tail
 __global__ void k_silu(float *__restrict__ out, const float *__restrict__ x, long long n, int mode) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const long long body = (mode == 1) ? (n - n % 8) : 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float v = x[i];
@@ -151,6 +155,8 @@ __global__ void k_silu(float *__restrict__ out, const float *__restrict__ x, lon
 
 // h = silu(clamp(g, -80, 80)) * u   (quant_kernels_omp.c:2157-2164)
 __global__ void k_swiglu(float *__restrict__ h, const float *__restrict__ g, const float *__restrict__ u, long long n) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         float gv = fminf(fmaxf(g[i], -80.0f), 80.0f);
         h[i] = (gv / (1.0f + expf(-gv))) * u[i];
@@ -158,6 +164,8 @@ __global__ void k_swiglu(float *__restrict__ h, const float *__restrict__ g, con
 }
 
 __global__ void k_add(float *__restrict__ out, const float *__restrict__ a, const float *__restrict__ b, long long n) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = a[i] + b[i];
 }
@@ -213,6 +221,8 @@ __global__ void k_rope_init(float *cos_t, float *sin_t, int max_ctx, int hd, int
 __global__ void k_rope_neox(float *__restrict__ buf, int nh, int hd, const int *__restrict__ pos_dev, int pos_host,
                             const float *__restrict__ cos_t, const float *__restrict__ sin_t, int rope_dim,
                             int rows_stride) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int hd2 = rope_dim / 2;
     const int row = blockIdx.y;
     const int pos = pos_dev ? pos_dev[row] : pos_host;
@@ -237,9 +247,7 @@ static int grid_for(long long n, int threads = 256) {
 
 int launch_rms_norm(float *out, const float *x, const float *w, float *res, int rows, int n, float eps, int flags,
                     cudaStream_t s) {
-    k_rms_norm<<<rows, 256, 0, s>>>(out, x, w, res, n, eps, flags);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_rms_norm, dim3(rows), dim3(256), 0, s, out, x, w, res, n, eps, flags)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 int launch_rms_norm_encode(float *out, const float *x, const float *w, float *res, int rows, int n, float eps,
@@ -263,21 +271,15 @@ int launch_rms_norm_encode(float *out, const float *x, const float *w, float *re
 }
 
 int launch_silu(float *out, const float *x, long long n, int mode, cudaStream_t s) {
-    k_silu<<<grid_for(n), 256, 0, s>>>(out, x, n, mode);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_silu, dim3(grid_for(n)), dim3(256), 0, s, out, x, n, mode)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 int launch_swiglu(float *h, const float *g, const float *u, long long n, cudaStream_t s) {
-    k_swiglu<<<grid_for(n), 256, 0, s>>>(h, g, u, n);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_swiglu, dim3(grid_for(n)), dim3(256), 0, s, h, g, u, n)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 int launch_add(float *out, const float *a, const float *b, long long n, cudaStream_t s) {
-    k_add<<<grid_for(n), 256, 0, s>>>(out, a, b, n);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_add, dim3(grid_for(n)), dim3(256), 0, s, out, a, b, n)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 int launch_softmax(float *x, int rows, int n, cudaStream_t s) {
@@ -301,9 +303,7 @@ int launch_rope_init(float *cos_t, float *sin_t, int max_ctx, int hd, int rope_d
 int launch_rope_neox(float *buf, int rows, int rows_stride, int nh, int hd, const int *pos_dev, int pos_host,
                      const float *cos_t, const float *sin_t, int rope_dim, cudaStream_t s) {
     dim3 grid(grid_for((long long)nh * (rope_dim / 2)) > 64 ? 64 : grid_for((long long)nh * (rope_dim / 2)), rows);
-    k_rope_neox<<<grid, 256, 0, s>>>(buf, nh, hd, pos_dev, pos_host, cos_t, sin_t, rope_dim, rows_stride);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_rope_neox, dim3(grid), dim3(256), 0, s, buf, nh, hd, pos_dev, pos_host, cos_t, sin_t, rope_dim, rows_stride)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 }  // namespace mlq

@@ -40,12 +40,15 @@
 
 #include "../../include/mojollama_b200.h"
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
 // V slice with an optional fallback source for columns past the projection
 __global__ void k_copy_cols_ext(float *__restrict__ dst, const float *__restrict__ src, int n, int src_stride,
                                 int off, int src_width, const float *__restrict__ ext) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int b = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int c = off + i;
@@ -85,6 +88,8 @@ __global__ void k_emb_q4k_ref(const uint8_t *__restrict__ emb, const int *__rest
 
 __global__ void k_embed_rows(const float *__restrict__ emb, const int *__restrict__ tokens, float *__restrict__ x,
                              int N, int V) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int b = blockIdx.y;
     int t = tokens[b];
     if (t < 0 || t >= V) t = 0;
@@ -94,6 +99,8 @@ __global__ void k_embed_rows(const float *__restrict__ emb, const int *__restric
 
 __global__ void k_shexp_score(const float *__restrict__ xn, const float *__restrict__ r, float *__restrict__ score,
                               int N) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     __shared__ float sh[32];
     const int b = blockIdx.x;
     float s = 0.0f;
@@ -112,6 +119,8 @@ __global__ void k_shexp_score(const float *__restrict__ xn, const float *__restr
 
 __global__ void k_add_scaled_if_pos(float *__restrict__ x, const float *__restrict__ y, const float *__restrict__ score,
                                     int N) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const int b = blockIdx.y;
     const float sc = score[b];
     if (!(sc > 0.0f)) return;
@@ -148,9 +157,7 @@ int launch_embed(const void *emb, int emb_quant, const int *d_tok, const int *h_
         }
         return MLQ_OK;
     }
-    k_embed_rows<<<dim3(grid_cols(N), B), 256, 0, s>>>((const float *)emb, d_tok, x, N, V);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_embed_rows, dim3(dim3(grid_cols(N), B)), dim3(256), 0, s, (const float *)emb, d_tok, x, N, V)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 size_t embed_bytes(int emb_quant, int N, int V) {
@@ -451,11 +458,13 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             MLQ_TRY(launch_matmul(wqkv, a->qkv_qt[l], xn, qkv, nq, N, B, 0, s));
             const int voff = compat ? inner + N : inner + (nq - inner) / 2;
             if (rc == MLQ_OK) {
-                k_copy_cols_ext<<<dim3(grid_cols(inner), B), 256, 0, s>>>(q, qkv, inner, nq, 0, nq, nullptr);
-                k_copy_cols_ext<<<dim3(grid_cols(n_kv), B), 256, 0, s>>>(k, qkv, n_kv, nq, inner, nq, nullptr);
-                k_copy_cols_ext<<<dim3(grid_cols(n_kv), B), 256, 0, s>>>(v, qkv, n_kv, nq, voff, nq,
-                                                                         v_ext ? v_ext + nq : nullptr);
-                count_launch(3);
+                const float *none = nullptr, *vx = v_ext ? v_ext + nq : nullptr;
+                MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_copy_cols_ext, dim3(grid_cols(inner), B), dim3(256), 0, s, q, qkv, inner,
+                                              nq, 0, nq, none)) ? MLQ_OK : MLQ_ERR_CUDA);
+                MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_copy_cols_ext, dim3(grid_cols(n_kv), B), dim3(256), 0, s, k, qkv, n_kv,
+                                              nq, inner, nq, none)) ? MLQ_OK : MLQ_ERR_CUDA);
+                MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_copy_cols_ext, dim3(grid_cols(n_kv), B), dim3(256), 0, s, v, qkv, n_kv,
+                                              nq, voff, nq, vx)) ? MLQ_OK : MLQ_ERR_CUDA);
             }
             MLQ_TRY(launch_rope_neox(q, B, inner, NH, HD, nullptr, pos, cos_t, sin_t, rope_dim, s));
             MLQ_TRY(launch_rope_neox(k, B, n_kv, nkh, HD, nullptr, pos, cos_t, sin_t, rope_dim, s));
@@ -535,8 +544,8 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             const uint8_t *su = (const uint8_t *)cs.weights(a->shexp_up_raw[l], mlq_row_bytes(suq, N) * (size_t)si);
             const uint8_t *sd = (const uint8_t *)cs.weights(a->shexp_down_raw[l], mlq_row_bytes(sdq, si) * (size_t)N);
             if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
-            k_shexp_score<<<B, 256, 0, s>>>(xn, sr, score, N);
-            count_launch();
+            MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_shexp_score, dim3(B), dim3(256), 0, s, xn, sr, score, N)) ? MLQ_OK
+                                                                                                        : MLQ_ERR_CUDA);
             if (shp_x && sgq == MLQ_MXFP4 && suq == MLQ_MXFP4 && sdq == MLQ_MXFP4 && si % 32 == 0 &&
                 mxf4_dense_supported(sg, si, N) && mxf4_dense_supported(su, si, N) && mxf4_dense_supported(sd, N, si)) {
                 // MXFP4 (the GGUF shared-expert type): gate and up in one launch of the grouped
@@ -552,8 +561,8 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
                 MLQ_TRY(launch_matmul(sd, sdq, g, tmp, N, si, B, 0, s));
             }
             if (rc == MLQ_OK) {
-                k_add_scaled_if_pos<<<dim3(grid_cols(N), B), 256, 0, s>>>(x, tmp, score, N);
-                count_launch();
+                MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_add_scaled_if_pos, dim3(grid_cols(N), B), dim3(256), 0, s, x, tmp,
+                                              score, N)) ? MLQ_OK : MLQ_ERR_CUDA);
             }
         }
     }

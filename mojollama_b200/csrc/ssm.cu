@@ -17,11 +17,14 @@
 #include <math.h>
 
 #include "mlq_internal.h"
+#include "pipeline.cuh"
 
 namespace mlq {
 
 __global__ void k_ssm_interm(const float *__restrict__ x, const float *__restrict__ conv_w, float *__restrict__ interm,
                              int B, int N, int inner) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     const long long total = (long long)B * inner;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total; t += (long long)gridDim.x * blockDim.x) {
         const int b = (int)(t / inner), i = (int)(t - (long long)b * inner);
@@ -37,6 +40,8 @@ __global__ void k_ssm_state(const float *__restrict__ x, const float *__restrict
                             const float *__restrict__ dt_bias, const float *__restrict__ alpha,
                             const float *__restrict__ beta, float *__restrict__ state, int B, int N, int state_size,
                             int dt_rank) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     extern __shared__ float sh[];   // [B] a_disc, [B] bx
     const int g = blockIdx.x;
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
@@ -61,6 +66,8 @@ __global__ void k_ssm_state(const float *__restrict__ x, const float *__restrict
 }
 
 __global__ void k_mul(float *__restrict__ a, const float *__restrict__ b, long long n) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         a[i] *= b[i];
 }
@@ -71,19 +78,18 @@ int launch_ssm_decode_step(const float *x, float *interm, const float *conv_w, c
     const long long total = (long long)B * inner;
     int grid = (int)((total + 255) / 256);
     if (grid > 4096) grid = 4096;
-    k_ssm_interm<<<grid, 256, 0, s>>>(x, conv_w, interm, B, N, inner);
-    k_ssm_state<<<groups, 128, sizeof(float) * 2 * B, s>>>(x, a_param, dt_bias, alpha, beta, state, B, N, state_size,
-                                                            dt_rank);
-    count_launch(2);
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    if (!MLQ_CUDA(launch_pdl_k(k_ssm_interm, dim3(grid), dim3(256), 0, s, x, conv_w, interm, B, N, inner)))
+        return MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_ssm_state, dim3(groups), dim3(128), sizeof(float) * 2 * B, s, x, a_param, dt_bias,
+                                 alpha, beta, state, B, N, state_size, dt_rank))
+               ? MLQ_OK
+               : MLQ_ERR_CUDA;
 }
 
 int launch_mul(float *a, const float *b, long long n, cudaStream_t s) {
     int grid = (int)((n + 255) / 256);
     if (grid > 4096) grid = 4096;
-    k_mul<<<grid, 256, 0, s>>>(a, b, n);
-    count_launch();
-    return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(launch_pdl_k(k_mul, dim3(grid), dim3(256), 0, s, a, b, n)) ? MLQ_OK : MLQ_ERR_CUDA;
 }
 
 }  // namespace mlq

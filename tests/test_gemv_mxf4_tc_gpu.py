@@ -55,9 +55,10 @@ def test_mxf4_tc_matches_oracle(cuda_device, n, k, m):
 
 
 def test_mxf4_tc_batch_in_passes(cuda_device):
-    """B = 11 at K = 2048 runs as passes of 4 activation rows over the same weights."""
+    """B = 4 at K = 4096 runs as two passes of 2 activation rows over the same weights (from 5
+    rows a batch that needs more than one pass goes to the tensor-core GEMM)."""
     import torch
-    n, k, m = 777, 2048, 11
+    n, k, m = 777, 4096, 4
     rng = np.random.default_rng(3)
     w = _weights(rng, n, k)
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -65,7 +66,7 @@ def test_mxf4_tc_batch_in_passes(cuda_device):
     want = O.gemv(w, F.MXFP4, x, n, k)
     for t in range(m):
         assert O.rel_l2(got[t], want[t]) < TOL, t
-    assert launches == 3, launches
+    assert launches == 2, launches
 
 
 def test_mxf4_tc_dynamic_range(cuda_device):
