@@ -14,10 +14,11 @@
 //      with per-32-element E8M0 scales (TMEM).
 //   D  fp32 [128][N] in TMEM; y[m][row] = sum_p D[row][8m + p].
 // Weight tiles: one 2-D TMA box when K is a multiple of 512 and the rows are 16-byte aligned;
-// otherwise (GPT-OSS: K = 2880, 1530-byte rows) the producer warp copies each row's chunk as
-// the 16-byte-aligned windows that cover it (cp.async, completion on the stage's mbarrier), the
-// repack thread shifts its row out of its window slot, and a last partial chunk's missing
-// blocks enter as zero codes with scale 1 (the planes past K are zero too).
+// otherwise (GPT-OSS: K = 2880, 1530-byte rows) each repack thread copies its own row's chunk
+// as the 16-byte-aligned windows that cover it (cp.async, completion on the stage's mbarrier)
+// one unit ahead -- two stages, one per repack group -- and shifts its row out of its window
+// slot; a last partial chunk's missing blocks enter as zero codes with scale 1 (the planes past
+// K are zero too).
 // Unlike the one-matrix kernel, whose every CTA encodes the activation planes itself, the
 // rows are encoded once per layer (k_mxf4_planes_rows) into global memory, already in the B
 // operand's swizzled layout: planes [chunk][sorted row][2 atom columns x 1 KB], scale bytes
@@ -81,7 +82,8 @@ static_assert(kNumBars * 8 + 16 <= kItemOff, "item records follow the barriers a
 
 // Rows that cannot be TMA tiles (a row pitch that is not a multiple of 16 bytes, K not a
 // multiple of 512): each row's chunk arrives as the 16-byte-aligned windows that cover it
-// (at most 18), one 288-byte slot per row
+// (at most 18), one 288-byte slot per row (a 304-byte pitch with 16-byte reads, free of bank
+// conflicts, measured the same)
 constexpr int kWinRow = 288;
 template <bool kWin> struct StageLayout {
     static constexpr int raw = kRows * (kWin ? kWinRow : kRawRow);        // weight part
@@ -177,6 +179,25 @@ struct ItemWalk {
     }
 };
 
+// Windowed mode: this thread's weight row of unit (item, chunk c) as the 16-byte-aligned windows
+// that cover it, into its 288-byte slot of the stage (the last window holds at least one byte of
+// the row, so it stays inside the row's allocation)
+__device__ __forceinline__ void copy_row_windows(const GroupMxf4Args &a, int4 item, int c, int m, uint8_t *st) {
+    const bool second = item.w >= a.T1;
+    const int row = (second ? item.w - a.T1 : item.w) * kRows + m;
+    if (row >= a.n_rows) return;
+    const uintptr_t start = reinterpret_cast<uintptr_t>(second ? a.W2 : a.W) +
+                            (uintptr_t)item.x * (uintptr_t)(second ? a.estride2 : a.estride) + (uintptr_t)c * kRawRow +
+                            (uintptr_t)row * (uintptr_t)a.row_bytes;
+    const uintptr_t end = start + (uintptr_t)min(kRawRow, a.row_bytes - c * kRawRow);
+    uint8_t *dst = st + m * kWinRow;
+    for (uintptr_t p = start & ~(uintptr_t)15; p < end; p += 16, dst += 16) cp_async16(dst, reinterpret_cast<const void *>(p));
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // ---------------------------------------------------------------- the grouped kernel
 template <bool kWin>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_constant__ CUtensorMap tmap,
@@ -186,9 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = sm;                                                 // 2 x kABytes
-    // A scale words [2][4][128] (windowed: [4][128] at the start of the unit's own stage, over
-    // weight windows already read into registers)
-    uint32_t *sfx = kWin ? nullptr : reinterpret_cast<uint32_t *>(sm + a.off_sfx);
+    uint32_t *sfx = reinterpret_cast<uint32_t *>(sm + a.off_sfx);    // [2][4][128] A scale words
     uint8_t *sRaw = sm + a.off_raw;                                   // stages of ST bytes
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm + a.off_bar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + a.off_bar + kNumBars * 8);
@@ -205,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&bar[kBarRawFull + s], kWin ? 33 : 1);   // windowed: every producer lane's copies + lane 0
+            mbar_init(&bar[kBarRawFull + s], kWin ? 129 : 1);   // windowed: the repack group's 128 rows + the producer
             mbar_init(&bar[kBarRawEmpty + s], 5);   // 4 repack warps + the MMAs that read B
         }
         for (int b = 0; b < 2; b++) {
@@ -235,61 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     const int mine = n_items > (int)blockIdx.x ? (n_items - (int)blockIdx.x + G - 1) / G : 0;
     const int total = mine * nc;   // units of this CTA
 
-    if (kWin && warp == kWarpTma) {
-        // ---------------------------------------------------------------- producer (windows)
-        // lane l copies rows l, l + 32, l + 64, l + 96 of the tile as the 16-byte windows that
-        // cover their chunk (the last window holds at least one byte of the row, so it stays
-        // inside the row's allocation); lane 0 adds the planes' bulk copies
-        const uint64_t keep = policy_evict_last();
-        ItemWalk w(nc);
-        // the current item and the next one, loaded an item ahead
-        int4 item = total ? item_at(a, w.it) : make_int4(0, 0, 0, 0);
-        int4 nxt = w.it + G < n_items ? item_at(a, w.it + G) : item;
-        int g = 0;
-        for (int s = 0, ph = 0; g < total; ++g, w.next()) {
-            if (g >= S && !warp_wait(&bar[kBarRawEmpty + s], ph ^ 1, lane)) {
-                if (lane == 0) set_status(a.status, DEV_ST_WAIT_EMPTY);
-                break;
-            }
-            const bool second = item.w >= a.T1;
-            const int tile = second ? item.w - a.T1 : item.w;
-            const uint8_t *base = (second ? a.W2 : a.W) + (size_t)item.x * (size_t)(second ? a.estride2 : a.estride) +
-                                  (size_t)w.c * kRawRow;
-            const int len = min(kRawRow, a.row_bytes - w.c * kRawRow);
-            const uint32_t mc = (uint32_t)item.z;
-            uint8_t *st = sRaw + (size_t)s * ST;
-            if (lane == 0) {
-                const size_t pr = (size_t)w.c * a.R + item.y;
-                s_item[s] = item;
-                mbar_arrive_expect_tx(&bar[kBarRawFull + s], mc * (kBRowBytes + kSfRowBytes));
-                bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
-                bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int rr = lane + 32 * i, row = tile * kRows + rr;
-                if (row >= a.n_rows) continue;
-                const uintptr_t start = reinterpret_cast<uintptr_t>(base) + (uintptr_t)row * (uintptr_t)a.row_bytes;
-                const uintptr_t end = start + (uintptr_t)len;
-                uint8_t *dst = st + rr * kWinRow;
-                for (uintptr_t p = start & ~(uintptr_t)15; p < end; p += 16, dst += 16)
-                    cp_async16(dst, reinterpret_cast<const void *>(p));
-            }
-            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bar[kBarRawFull + s]))
-                         : "memory");
-            if (w.c == nc - 1) {
-                item = nxt;
-                if (w.it + 2 * G < n_items) nxt = item_at(a, w.it + 2 * G);
-            }
-            if (++s == S) { s = 0; ph ^= 1; }
-        }
-        // nothing may land in this CTA's shared memory after it exits
-        if (lane == 0)
-            for (int h = g - S < 0 ? 0 : g - S; h < g; ++h)
-                if (!mbar_wait_bounded(&bar[kBarRawFull + h % S], (h / S) & 1)) set_status(a.status, DEV_ST_WAIT_DRAIN);
-        __syncwarp();
-    } else if (warp == kWarpTma) {
-        // ---------------------------------------------------------------- producer (TMA)
+    if (warp == kWarpTma) {
+        // ---------------------------------------------------------------- producer
+        // TMA mode: the weight tile (2-D TMA box) and the rows' planes and scales (1-D bulk
+        // copies).  Windowed mode: the planes and scales only; the repack threads copy their
+        // own rows' windows (copy_row_windows)
         if (lane == 0) {
             const uint64_t once = policy_evict_first(), keep = policy_evict_last();
             ItemWalk w(nc);
@@ -307,8 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                 uint8_t *st = sRaw + (size_t)s * ST;
                 const size_t pr = (size_t)w.c * a.R + item.y;
                 s_item[s] = item;
-                mbar_arrive_expect_tx(&bar[kBarRawFull + s], (uint32_t)RB + mc * (kBRowBytes + kSfRowBytes));
-                tma_load_2d(st, second ? &tmap2 : &tmap, w.c * (kRawRow / 2), row0, &bar[kBarRawFull + s], once);
+                mbar_arrive_expect_tx(&bar[kBarRawFull + s], (kWin ? 0u : (uint32_t)RB) + mc * (kBRowBytes + kSfRowBytes));
+                if (!kWin) tma_load_2d(st, second ? &tmap2 : &tmap, w.c * (kRawRow / 2), row0, &bar[kBarRawFull + s], once);
                 bulk_g2s(st + RB, a.planes + pr * kBRowBytes, mc * kBRowBytes, &bar[kBarRawFull + s], keep);
                 bulk_g2s(st + RB + kBBytes, a.scales + pr * kSfRowBytes, mc * kSfRowBytes, &bar[kBarRawFull + s], keep);
                 if (w.c == nc - 1) {
@@ -377,8 +346,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         const int rowoff = (m >> 3) * 1024 + m8 * 128;
         ItemWalk w(nc);
         if (G2) w.next();
+        // windowed mode (two stages, stage G2 always this group's): the group copies its own rows,
+        // one unit ahead -- the first unit here, each next one as soon as the current unit's rows
+        // are in registers
+        if (kWin && G2 < total) {
+            copy_row_windows(a, item_at(a, w.it), w.c, m, sRaw + (size_t)G2 * ST);
+            cp_async_arrive_noinc(&bar[kBarRawFull + G2]);
+        }
         for (int g = G2; g < total; g += 2, w.next(), w.next()) {
             const int s = g % S, ab = G2;
+            ItemWalk wn = w;   // this group's next unit, g + 2
+            wn.next();
+            wn.next();
+            const int4 nitem = kWin && g + 2 < total ? item_at(a, wn.it) : make_int4(0, 0, 0, 0);
             bool ok = !flag[G2];
             if (ok && !warp_wait(&bar[kBarRawFull + s], (g / S) & 1, lane)) ok = false;
             uint32_t R[68];
@@ -404,6 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                         R[i] = __funnelshift_r(prev, nxt, sh);
                         prev = nxt;
                     }
+                    if (g + 2 < total) {
+                        copy_row_windows(a, nitem, wn.c, m, const_cast<uint8_t *>(st));
+                        cp_async_arrive_noinc(&bar[kBarRawFull + s]);
+                    }
                 } else {
                     const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
 #pragma unroll
@@ -413,10 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                     }
                 }
             }
-            // windowed: every row of the group is in registers before the scale words below
-            // overwrite the start of the stage
-            if (kWin) named_bar_sync(1 + G2, 128);
-            uint32_t *sx = kWin ? reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(st)) : sfx + ab * 4 * kRows;
+            uint32_t *sx = sfx + ab * 4 * kRows;
             if (ok && g >= 2 && !warp_wait(&bar[kBarAFree + ab], ((g >> 1) - 1) & 1, lane)) ok = false;
             if (ok) {
                 uint8_t *dstA = sA + ab * kABytes + rowoff;
@@ -633,13 +614,14 @@ static int launch_mxf4_tc(const uint8_t *W, long long estride, const uint8_t *W2
                                 row_bytes, kRawRow, kRows))
             return MLQ_ERR_UNSUPPORTED;
     }
-    // shared memory: 2 A buffers, (TMA) the A scale words, barriers, then the stages
+    // shared memory: 2 A buffers, the A scale words, barriers, then the stages
     const int stage = tma ? StageLayout<false>::bytes : StageLayout<true>::bytes;
     const int off_sfx = 2 * kABytes;
-    const int off_bar = off_sfx + (tma ? 2 * 4 * kRows * 4 : 0);
+    const int off_bar = off_sfx + 2 * 4 * kRows * 4;
     const int off_raw = (off_bar + kBarBytes + 1023) / 1024 * 1024;
     int n_stages = (kSmemMax - 1024 - off_raw) / stage;
     if (n_stages > kMaxStages) n_stages = kMaxStages;
+    if (!tma) n_stages = 2;   // windowed: one stage per repack group (each group refills its own)
     if (n_stages < 2) return MLQ_ERR_UNSUPPORTED;
     const int smem = 1024 + off_raw + n_stages * stage;
     static bool attr[2] = {false, false};
