@@ -104,7 +104,7 @@ struct GroupMxf4Args {
     int erows, erows2;        // tensor-map rows between consecutive experts
     int n_stages;
     int off_sfx, off_bar, off_raw;
-    int dense_T;              // > 0: no item list; item i = tile i % dense_T of rows 8 (i / dense_T)..
+    int dense_T;              // > 0: no item list; dense_T tiles x ceil(R / 8) row chunks (item_at)
     // windowed copies: the matrices' base addresses, expert strides, row pitch and K
     const uint8_t *W, *W2;
     long long estride, estride2;
@@ -112,11 +112,13 @@ struct GroupMxf4Args {
     int *status;
 };
 
-// work item it: from the planner's list, or in dense mode (one matrix pair, every row) computed
+// work item it: from the planner's list, or in dense mode (one matrix pair, every row) computed,
+// tile-major: the 8-row chunks of one tile are consecutive items, taken by neighbouring CTAs at
+// about the same time, so the tile comes from DRAM once and from L2 for the other chunks
 __device__ __forceinline__ int4 item_at(const GroupMxf4Args &a, int it) {
     if (a.dense_T) {
-        const int ch = it / a.dense_T, m0 = 8 * ch;
-        return make_int4(0, m0, min(8, a.R - m0), it - ch * a.dense_T);
+        const int nch = (a.R + 7) / 8, tile = it / nch, m0 = 8 * (it - tile * nch);
+        return make_int4(0, m0, min(8, a.R - m0), tile);
     }
     return __ldg(a.items + it);
 }
