@@ -510,13 +510,16 @@ constexpr int kFewRowsMaxB = 16;
 template <typename WT>
 __global__ void __launch_bounds__(256) k_gemv_float_rows(const WT *__restrict__ W, const float *__restrict__ x,
                                                          float *__restrict__ out, int n_rows, int K, int nb_x,
-                                                         int vec_ok) {
+                                                         int vec_ok, const WT *__restrict__ w_extra,
+                                                         float *__restrict__ out_extra) {
     pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
     pdl_trigger();
     constexpr int V = 16 / sizeof(WT);
     __shared__ float part[8][kFewRowsMaxB];
     const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const WT *wr = W + (size_t)row * K;
+    // CTA n_rows (when w_extra is given): one more row from its own pointer, out_extra[m]
+    const bool extra = row == n_rows;
+    const WT *wr = extra ? w_extra : W + (size_t)row * K;
     float acc[kFewRowsMaxB];
 #pragma unroll
     for (int m = 0; m < kFewRowsMaxB; m++) acc[m] = 0.0f;
@@ -566,7 +569,8 @@ __global__ void __launch_bounds__(256) k_gemv_float_rows(const WT *__restrict__ 
         float sum = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; w++) sum += part[w][threadIdx.x];
-        out[(size_t)threadIdx.x * n_rows + row] = sum;
+        if (extra) out_extra[threadIdx.x] = sum;
+        else out[(size_t)threadIdx.x * n_rows + row] = sum;
     }
 }
 
@@ -892,8 +896,10 @@ static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows
         // too few rows for a warp each to fill the GPU: a CTA per row
         for (int b = 0; b < B; b += kFewRowsMaxB) {
             const int take = (B - b) < kFewRowsMaxB ? (B - b) : kFewRowsMaxB;
+            const WT *none = nullptr;
+            float *none_out = nullptr;
             if (!MLQ_CUDA(launch_pdl_k(k_gemv_float_rows<WT>, dim3(n_rows), dim3(256), 0, s, w, x + (size_t)b * K,
-                                       out + (size_t)b * n_rows, n_rows, K, take, vec_ok)))
+                                       out + (size_t)b * n_rows, n_rows, K, take, vec_ok, none, none_out)))
                 return MLQ_ERR_CUDA;
         }
         return MLQ_OK;
@@ -912,6 +918,22 @@ static int launch_float(const uint8_t *W, const float *x, float *out, int n_rows
         count_launch();
     }
     return MLQ_CUDA(cudaGetLastError()) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+// fp32 router rows plus one more fp32 row from its own pointer in the same launch (a MoE
+// layer's router and its shared expert's gate score): out [B][n_rows], out_extra [B]
+int launch_router_rows_f32(const float *W, const float *w_extra, const float *x, float *out, float *out_extra,
+                           int n_rows, int K, int B, cudaStream_t s) {
+    const int vec_ok = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(w_extra) & 15) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    for (int b = 0; b < B; b += kFewRowsMaxB) {
+        const int take = (B - b) < kFewRowsMaxB ? (B - b) : kFewRowsMaxB;
+        if (!MLQ_CUDA(launch_pdl_k(k_gemv_float_rows<float>, dim3(n_rows + 1), dim3(256), 0, s, W, x + (size_t)b * K,
+                                   out + (size_t)b * n_rows, n_rows, K, take, vec_ok, w_extra, out_extra + b)))
+            return MLQ_ERR_CUDA;
+    }
+    return MLQ_OK;
 }
 
 int launch_matmul(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int B,

@@ -310,8 +310,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mxf4_tc(const __grid_const
                     const uint4 v = src[i];
                     R[4 * i] = v.x; R[4 * i + 1] = v.y; R[4 * i + 2] = v.z; R[4 * i + 3] = v.w;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar[kBarRawEmpty + s]);
             }
             if (ok && g >= 2 && !warp_wait(&bar[kBarAFree + ab], ((g >> 1) - 1) & 1, lane)) ok = false;
             if (ok) {
@@ -338,6 +336,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mxf4_tc(const __grid_const
                     const uint32_t t23 = __byte_perm(R[o2 >> 2], R[o3 >> 2], (uint32_t)((o2 & 3) | ((4 + (o3 & 3)) << 4)));
                     sfx[(ab * 4 + gi) * kRows + m] = __byte_perm(t01, t23, 0x5410);
                 }
+                // the raw stage is released only now, after its rows were used above.  Released
+                // right after the loads were issued, the stage's next TMA box (which fills rows 0,
+                // 1, ... first) overwrote rows 0-15 before some of those loads had read them: about
+                // one call in 30 had 1-3 wrong rows among a tile's first 16
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar[kBarRawEmpty + s]);
             } else {
                 rp_abort[G] = 1;
             }

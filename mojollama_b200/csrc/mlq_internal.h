@@ -121,6 +121,10 @@ int launch_dequantize(const uint8_t *W, int qt, float *out, int64_t n, cudaStrea
 // 16-bit float weights (bf16 = 1 / f16 = 0) times B fp32 activation rows through cuBLAS
 // (blas.cu); MLQ_ERR_UNSUPPORTED when unavailable
 int launch_gemm16(const void *W, int bf16, const float *x, float *out, int n_rows, int K, int B, cudaStream_t s);
+// fp32 router rows and one extra fp32 row (a shared expert's gate score) in one launch (gemv.cu):
+// out [B][n_rows], out_extra [B]
+int launch_router_rows_f32(const float *W, const float *w_extra, const float *x, float *out, float *out_extra,
+                           int n_rows, int K, int B, cudaStream_t s);
 // tensor-core GEMM (gemm_tc.cu); MLQ_ERR_UNSUPPORTED for formats/shapes it does not cover
 int launch_gemm_tc(const uint8_t *W, int qt, const float *x, float *out, int n_rows, int K, int M, cudaStream_t s);
 // grouped experts on the tensor-core GEMM (csrc/gemm_tc.cu): sorted rows converted to fp16

@@ -349,8 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         ItemWalk w(nc);
         if (G2) w.next();
         // windowed mode (two stages, stage G2 always this group's): the group copies its own rows,
-        // one unit ahead -- the first unit here, each next one as soon as the current unit's rows
-        // are in registers
+        // one unit ahead -- the first unit here, each next one once the current unit's rows have
+        // been repacked
         if (kWin && G2 < total) {
             copy_row_windows(a, item_at(a, w.it), w.c, m, sRaw + (size_t)G2 * ST);
             cp_async_arrive_noinc(&bar[kBarRawFull + G2]);
@@ -385,10 +385,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                         const uint32_t nxt = wp[i + 1];
                         R[i] = __funnelshift_r(prev, nxt, sh);
                         prev = nxt;
-                    }
-                    if (g + 2 < total) {
-                        copy_row_windows(a, nitem, wn.c, m, const_cast<uint8_t *>(st));
-                        cp_async_arrive_noinc(&bar[kBarRawFull + s]);
                     }
                 } else {
                     const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
@@ -431,6 +427,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                             if (4 * gi + j >= nvalid) wd = (wd & ~(0xFFu << (8 * j))) | (0x7Fu << (8 * j));
                     }
                     sx[gi * kRows + m] = wd;
+                }
+                // windowed: this thread's row of the group's next unit, into the slot just read --
+                // only now, after the row's words were used above, so that no copy can land before
+                // the loads of the current row have read it (a release right after the loads let
+                // the one-matrix GEMV's next TMA box overwrite rows before they were read)
+                if (kWin && g + 2 < total) {
+                    copy_row_windows(a, nitem, wn.c, m, const_cast<uint8_t *>(st));
+                    cp_async_arrive_noinc(&bar[kBarRawFull + s]);
                 }
             } else {
                 flag[G2] = 1;

@@ -513,7 +513,17 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
         const uint8_t *ue = (const uint8_t *)cs.weights(a->up_exp_raw[l], extent(us, um));
         const uint8_t *de = (const uint8_t *)cs.weights(a->down_exp_raw[l], extent(ds, dm));
         if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
-        MLQ_TRY(launch_matmul(wr, rqt, xn, lg, E, N, B, 0, s));
+        // an fp32 router and a shared expert: its gate score rides in the router's launch as
+        // one more row (the score is used after the routed experts; xn is unchanged until then)
+        bool score_done = false;
+        if (rqt == MLQ_F32 && a->shexp_router && a->shexp_router[l]) {
+            const float *sr = (const float *)cs.weights(a->shexp_router[l], sizeof(float) * N);
+            if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
+            MLQ_TRY(launch_router_rows_f32((const float *)wr, sr, xn, lg, score, E, N, B, s));
+            score_done = true;
+        } else {
+            MLQ_TRY(launch_matmul(wr, rqt, xn, lg, E, N, B, 0, s));
+        }
         MLQ_TRY(launch_router_topk(lg, B, E, topk, 1, e_idx, e_w, s));
         const bool grouped = N % 32 == 0 && M % 32 == 0 && E <= 1024 && grouped_tiles_per_expert(gqt, M, N) &&
                              grouped_tiles_per_expert(uqt, M, N) && grouped_tiles_per_expert(dqt, N, M) &&
@@ -544,8 +554,9 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             const uint8_t *su = (const uint8_t *)cs.weights(a->shexp_up_raw[l], mlq_row_bytes(suq, N) * (size_t)si);
             const uint8_t *sd = (const uint8_t *)cs.weights(a->shexp_down_raw[l], mlq_row_bytes(sdq, si) * (size_t)N);
             if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_ARG; break; }
-            MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_shexp_score, dim3(B), dim3(256), 0, s, xn, sr, score, N)) ? MLQ_OK
-                                                                                                        : MLQ_ERR_CUDA);
+            if (!score_done)
+                MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_shexp_score, dim3(B), dim3(256), 0, s, xn, sr, score, N)) ? MLQ_OK
+                                                                                                            : MLQ_ERR_CUDA);
             if (shp_x && sgq == MLQ_MXFP4 && suq == MLQ_MXFP4 && sdq == MLQ_MXFP4 && si % 32 == 0 &&
                 mxf4_dense_supported(sg, si, N) && mxf4_dense_supported(su, si, N) && mxf4_dense_supported(sd, N, si)) {
                 // MXFP4 (the GGUF shared-expert type): gate and up in one launch of the grouped
