@@ -77,7 +77,8 @@ constexpr int kBarRawFull = 0, kBarRawEmpty = 4, kBarAFull = 8, kBarAFree = 10, 
 // before the stage's copies are armed (the MMA thread and the repack warps read it from here
 // after the stage's full-barrier wait, instead of loading it from global memory per unit)
 constexpr int kItemOff = 192;
-constexpr int kBarBytes = kItemOff + 16 * kMaxStages;
+constexpr int kDepOff = kItemOff + 16 * kMaxStages;   // windowed: one word per repack thread
+constexpr int kBarBytes = kDepOff + 4 * 256;
 static_assert(kNumBars * 8 + 16 <= kItemOff, "item records follow the barriers and flags");
 
 // Rows that cannot be TMA tiles (a row pitch that is not a multiple of 16 bytes, K not a
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + a.off_bar + kNumBars * 8);
     volatile int *flag = reinterpret_cast<volatile int *>(sm + a.off_bar + kNumBars * 8 + 4);   // [3]
     int4 *s_item = reinterpret_cast<int4 *>(sm + a.off_bar + kItemOff);                       // [kMaxStages]
+    uint32_t *s_dep = reinterpret_cast<uint32_t *>(sm + a.off_bar + kDepOff);                 // [256]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.n_stages, nc = a.nc;
 
@@ -350,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
         if (G2) w.next();
         // windowed mode (two stages, stage G2 always this group's): the group copies its own rows,
         // one unit ahead -- the first unit here, each next one once the current unit's rows have
-        // been repacked
+        // been read
         if (kWin && G2 < total) {
             copy_row_windows(a, item_at(a, w.it), w.c, m, sRaw + (size_t)G2 * ST);
             cp_async_arrive_noinc(&bar[kBarRawFull + G2]);
@@ -385,6 +387,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                         const uint32_t nxt = wp[i + 1];
                         R[i] = __funnelshift_r(prev, nxt, sh);
                         prev = nxt;
+                    }
+                    if (g + 2 < total) {
+                        // this thread's row of the group's next unit, into the slot just read.  The
+                        // copies must not land before this row's loads have read the slot: the XOR
+                        // of the row's words (it needs every load's data) is stored first and the
+                        // warp synchronises, so the copies issue only after all the loads returned
+                        uint32_t dep = 0;
+#pragma unroll
+                        for (int i = 0; i < 68; i++) dep ^= R[i];
+                        s_dep[threadIdx.x] = dep;
+                        __syncwarp();
+                        copy_row_windows(a, nitem, wn.c, m, const_cast<uint8_t *>(st));
+                        cp_async_arrive_noinc(&bar[kBarRawFull + s]);
                     }
                 } else {
                     const uint4 *src = reinterpret_cast<const uint4 *>(st + m * kRawRow);
@@ -427,14 +442,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_mxf4_tc(const __grid_consta
                             if (4 * gi + j >= nvalid) wd = (wd & ~(0xFFu << (8 * j))) | (0x7Fu << (8 * j));
                     }
                     sx[gi * kRows + m] = wd;
-                }
-                // windowed: this thread's row of the group's next unit, into the slot just read --
-                // only now, after the row's words were used above, so that no copy can land before
-                // the loads of the current row have read it (a release right after the loads let
-                // the one-matrix GEMV's next TMA box overwrite rows before they were read)
-                if (kWin && g + 2 < total) {
-                    copy_row_windows(a, nitem, wn.c, m, const_cast<uint8_t *>(st));
-                    cp_async_arrive_noinc(&bar[kBarRawFull + s]);
                 }
             } else {
                 flag[G2] = 1;
