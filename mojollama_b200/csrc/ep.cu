@@ -96,23 +96,29 @@ __global__ void k_ep_gather(const float *__restrict__ x, const int *__restrict__
 }
 
 // out[t] = residual[t] + sum_i w[t][i] * y[pos[t*k + i]]   (i in order)
+// out[t] = residual[t] + sum_i w[t k + i] y[pos[t k + i]]; with ys, then out[t] += score[t] ys[t]
+// where score[t] > 0 (a shared expert's output, added after the routed ones as a separate step
+// would add it)
 __global__ void k_ep_combine(const float *__restrict__ y, const int *__restrict__ pos, const float *__restrict__ w,
-                             int k, int N, const float *__restrict__ residual, float *__restrict__ out) {
+                             int k, int N, const float *__restrict__ residual, float *__restrict__ out,
+                             const float *__restrict__ ys, const float *__restrict__ score) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x;
+    const float sc = ys ? score[t] : 0.0f;
     for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < N; c += gridDim.y * blockDim.x) {
         float acc = residual ? residual[(size_t)t * N + c] : 0.0f;
         for (int i = 0; i < k; i++) {
             const int r = pos ? pos[t * k + i] : t * k + i;
             acc = fmaf(w[t * k + i], y[(size_t)r * N + c], acc);
         }
+        if (ys && sc > 0.0f) acc = fmaf(sc, ys[(size_t)t * N + c], acc);
         out[(size_t)t * N + c] = acc;
     }
 }
 
 int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
-                      float *out, cudaStream_t s) {
+                      float *out, cudaStream_t s, const float *ys, const float *score) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(T, (N + 255) / 256);   // columns spread over CTAs: one token is 8 CTAs at N = 2048
     cfg.blockDim = dim3(256);
@@ -123,7 +129,8 @@ int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int
     cfg.attrs = at;
     cfg.numAttrs = 1;
     count_launch();
-    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_ep_combine, y, pos, w, k, N, residual, out)) ? MLQ_OK : MLQ_ERR_CUDA;
+    return MLQ_CUDA(cudaLaunchKernelEx(&cfg, k_ep_combine, y, pos, w, k, N, residual, out, ys, score)) ? MLQ_OK
+                                                                                                      : MLQ_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------ grouped routed experts

@@ -160,6 +160,9 @@ int launch_q8act_to_f32(const uint8_t *x_q8, float *x, int64_t n, cudaStream_t s
 // ops.cu
 int launch_rms_norm(float *out, const float *x, const float *w, float *res, int rows, int n, float eps, int flags,
                     cudaStream_t s);
+// x += y, then out = RMSNorm(x) (as launch_rms_norm with res null) in one launch
+int launch_add_rms_norm(float *x, const float *y, const float *w, float *out, int rows, int n, float eps, int flags,
+                        cudaStream_t s);
 int launch_silu(float *out, const float *x, long long n, int mode, cudaStream_t s);
 int launch_swiglu(float *h, const float *g, const float *u, long long n, cudaStream_t s);
 int launch_add(float *out, const float *a, const float *b, long long n, cudaStream_t s);
@@ -288,7 +291,7 @@ int launch_moe_grouped(int gqt, int uqt, int dqt, const uint8_t *gexp, const uin
                        cudaStream_t s, int eid_stride = 1, int x_stride = 0);
 // out[t] = residual[t] (if set) + sum_i w[t * k + i] * y[pos[t * k + i]] (pos null: identity)
 int launch_ep_combine(const float *y, const int *pos, const float *w, int T, int k, int N, const float *residual,
-                      float *out, cudaStream_t s);
+                      float *out, cudaStream_t s, const float *ys = nullptr, const float *score = nullptr);
 // decode GEMV over up to 4 same-type matrices sharing packed activation rows [B <= 8]:
 // out_i = (res_i +) W_i x, or with pair (2 matrices, same rows) out_0 = silu(W_0 x) * (W_1 x);
 // MLQ_ERR_UNSUPPORTED when the shape or type does not suit it

@@ -87,6 +87,40 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
     }
 }
 
+// x += y on the row, then k_rms_norm of the new row (res null): one launch for the residual add
+// of a block's output and the next block's norm.  Each thread re-reads only what it wrote.
+__global__ void k_add_rms_norm(float *__restrict__ x, const float *__restrict__ y, const float *__restrict__ w,
+                               float *__restrict__ out, int n, float eps, int flags) {
+    pdl_wait();   // programmatic dependent launch: nothing is touched before the previous kernel ends
+    pdl_trigger();
+    __shared__ float sh[32];
+    float *xr = x + (size_t)blockIdx.x * n;
+    const float *yr = y + (size_t)blockIdx.x * n;
+    float *orow = out + (size_t)blockIdx.x * n;
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = xr[i] + yr[i];
+        xr[i] = v;
+        if (flags & 1) {
+            if (v != v) v = 0.0f;
+            v = fminf(fmaxf(v, -1000.0f), 1000.0f);
+        }
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, sh);
+    const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = xr[i];
+        if (flags & 1) {
+            if (v != v) v = 0.0f;
+            v = fminf(fmaxf(v, -1000.0f), 1000.0f);
+        }
+        orow[i] = (v * inv) * (w ? w[i] : 1.0f);
+    }
+}
+
 // k_rms_norm with the normalised row also written as a packed activation row (the
 // input encoding of the GEMVs that read it).  CTA (slice, row): every CTA of a row sums the
 // squares of the whole row (one pass over n floats), then normalises and encodes only its
@@ -248,6 +282,12 @@ static int grid_for(long long n, int threads = 256) {
 int launch_rms_norm(float *out, const float *x, const float *w, float *res, int rows, int n, float eps, int flags,
                     cudaStream_t s) {
     return MLQ_CUDA(launch_pdl_k(k_rms_norm, dim3(rows), dim3(256), 0, s, out, x, w, res, n, eps, flags)) ? MLQ_OK : MLQ_ERR_CUDA;
+}
+
+int launch_add_rms_norm(float *x, const float *y, const float *w, float *out, int rows, int n, float eps, int flags,
+                        cudaStream_t s) {
+    return MLQ_CUDA(launch_pdl_k(k_add_rms_norm, dim3(rows), dim3(256), 0, s, x, y, w, out, n, eps, flags)) ? MLQ_OK
+                                                                                                           : MLQ_ERR_CUDA;
 }
 
 int launch_rms_norm_encode(float *out, const float *x, const float *w, float *res, int rows, int n, float eps,

@@ -446,7 +446,6 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
             }
             MLQ_TRY(launch_mul(att, g, (long long)B * IN, s));
             MLQ_TRY(launch_matmul(wo, a->ssm_out_qt[l], att, tmp, N, IN, B, 0, s));
-            MLQ_TRY(launch_add(x, x, tmp, (long long)B * N, s));
         } else {
             const int nq = a->qkv_nr[l];
             const uint8_t *wqkv = (const uint8_t *)cs.weights(a->attn_qkv_raw[l],
@@ -484,11 +483,11 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
                     rc = MLQ_ERR_CUDA;
             }
             MLQ_TRY(launch_matmul(wo, a->out_qt[l], att, tmp, N, inner, B, 0, s));
-            MLQ_TRY(launch_add(x, x, tmp, (long long)B * N, s));
         }
         // FFN
         const float *fnw = (const float *)cs.weights(a->ffn_norm_w[l], sizeof(float) * N);
-        MLQ_TRY(launch_rms_norm(xn, x, fnw, nullptr, B, N, a->eps, 1, s));
+        // x += the block's output (tmp), then the FFN norm, in one launch
+        MLQ_TRY(launch_add_rms_norm(x, tmp, fnw, xn, B, N, a->eps, 1, s));
         const bool has_moe = E > 0 && topk > 0 && a->gate_exp_raw && a->gate_exp_raw[l] && a->moe_router_raw &&
                              a->moe_router_raw[l];
         if (!has_moe || rc != MLQ_OK) continue;
@@ -528,23 +527,26 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
         const bool grouped = N % 32 == 0 && M % 32 == 0 && E <= 1024 && grouped_tiles_per_expert(gqt, M, N) &&
                              grouped_tiles_per_expert(uqt, M, N) && grouped_tiles_per_expert(dqt, N, M) &&
                              !getenv("MLQ_NO_GROUPED_MOE");
+        const bool shexp = a->shexp_router && a->shexp_router[l];
+        float *ym = nullptr;   // grouped: the routed rows, combined after the shared expert
         if (grouped && rc == MLQ_OK) {
             // every active expert streamed once for all of its (token, slot) rows, then
             // x += sum_i w_i y_i in slot order (moe_forward_omp's +-80 SiLU clamp)
             const int R = B * topk;
             uint8_t *mscr = (uint8_t *)cs.scratch(moe_grouped_scratch_bytes(gqt, uqt, dqt, R, E, M, N));
-            float *ym = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
+            ym = (float *)cs.scratch(sizeof(float) * (size_t)R * N);
             if (cs.failed) { rc = mlq_last_error() ? mlq_last_error() : MLQ_ERR_CUDA; break; }
             MoeGroupedScratch ms;
             moe_grouped_carve(ms, mscr, gqt, uqt, dqt, R, E, M, N);
             MLQ_TRY(launch_moe_grouped(gqt, uqt, dqt, ge, ue, de, gs, us, ds, E, e_idx, R, topk, M, N, xn, ym, 80.0f,
                                        ms, s));
-            MLQ_TRY(launch_ep_combine(ym, nullptr, e_w, B, topk, N, x, x, s));
+            // with a shared expert the combine also adds its scaled output (below): one launch
+            if (!shexp) MLQ_TRY(launch_ep_combine(ym, nullptr, e_w, B, topk, N, x, x, s));
         } else {
             MLQ_TRY(launch_moe_experts(gqt, uqt, dqt, ge, ue, de, gs, us, ds, e_idx, e_w, topk, B, M, N, xn, hm, hm2, x,
                                        x, 80.0f, s));
         }
-        if (a->shexp_router && a->shexp_router[l]) {
+        if (shexp) {
             const int si = a->shexp_int ? a->shexp_int[l] : 512;
             const int sgq = a->shexp_gate_qt ? a->shexp_gate_qt[l] : MLQ_MXFP4;
             const int suq = a->shexp_up_qt ? a->shexp_up_qt[l] : MLQ_MXFP4;
@@ -571,7 +573,10 @@ int mlq_qwen36_batch_forward(const MlqQwen36Args *a) {
                 MLQ_TRY(launch_swiglu(g, g, u, (long long)B * si, s));
                 MLQ_TRY(launch_matmul(sd, sdq, g, tmp, N, si, B, 0, s));
             }
-            if (rc == MLQ_OK) {
+            if (ym) {
+                // x += sum_i w_i y_i, then x += score * shared where score > 0, in one launch
+                MLQ_TRY(launch_ep_combine(ym, nullptr, e_w, B, topk, N, x, x, s, tmp, score));
+            } else if (rc == MLQ_OK) {
                 MLQ_TRY(MLQ_CUDA(launch_pdl_k(k_add_scaled_if_pos, dim3(grid_cols(N), B), dim3(256), 0, s, x, tmp,
                                               score, N)) ? MLQ_OK : MLQ_ERR_CUDA);
             }
