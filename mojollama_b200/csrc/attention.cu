@@ -342,10 +342,12 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
     }
     int span = max_seq_len;
     if (window > 0 && span > window) span = window;
-    // enough CTAs to cover the SMs; >= 64 positions per split
+    // enough CTAs to cover the SMs; >= 32 positions (one tile) per split.  (At >= 64, config 5's
+    // 10 sequences x 2 KV heads ran as 20-40 CTAs of 8 query heads each: +120-150 us per
+    // attention layer at positions 64-160)
     const int ctas = B * nkh;
     int n_splits = 1;
-    while (n_splits < 64 && ctas * n_splits < 2 * env->num_sms && span / (n_splits * 2) >= 64) n_splits *= 2;
+    while (n_splits < 64 && ctas * n_splits < 2 * env->num_sms && span / (n_splits * 2) >= 32) n_splits *= 2;
     const int chunk = (span + n_splits - 1) / n_splits;
     const size_t need = (size_t)B * nh * n_splits * (hd + 2) * sizeof(float);
     if (n_splits > 1 && (!scratch || scratch_bytes < need)) n_splits = 1;
