@@ -59,8 +59,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
     extern __shared__ float sm[];
     pdl_wait();   // q, the KV rows and the split scratch follow earlier kernels
     pdl_trigger();
-    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int rep = nh / nkh;
+    // blockIdx.y = KV head g x query-head part hp: this CTA takes rep of the KV head's nh / nkh
+    // query heads, from query head h0
+    const int hsplit = gridDim.y / nkh;
+    const int split = blockIdx.x, g = blockIdx.y / hsplit, hp = blockIdx.y - g * hsplit, b = blockIdx.z;
+    const int rep = nh / nkh / hsplit;
+    const int h0 = g * (nh / nkh) + hp * rep;
     const int n_splits = gridDim.x;
     const int sl = seq_lens ? seq_lens[b] : seq_len_scalar;
     const int lo_all = (window > 0 && sl > window) ? sl - window : 0;
@@ -80,7 +84,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
     if (rp.pos) {
         // q heads g*rep.. and the new k row of head g, rotated as k_rope_kv does, then q scaled
         const int hd2 = rp.rope_dim / 2, row = nkh * HD;
-        for (int i = tid; i < rep * HD; i += blockDim.x) qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i];
+        for (int i = tid; i < rep * HD; i += blockDim.x) qs[i] = q[((size_t)b * nh + (size_t)h0) * HD + i];
         for (int d = tid; d < HD; d += blockDim.x) {
             nk[d] = rp.k_new[(size_t)b * row + (size_t)g * HD + d];
             nv[d] = rp.v_new[(size_t)b * row + (size_t)g * HD + d];
@@ -99,7 +103,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
         for (int i = tid; i < rep * HD; i += blockDim.x) qs[i] *= scale;
     } else {
         for (int i = tid; i < rep * HD; i += blockDim.x)
-            qs[i] = q[((size_t)b * nh + (size_t)g * rep) * HD + i] * scale;
+            qs[i] = q[((size_t)b * nh + (size_t)h0) * HD + i] * scale;
     }
     for (int h = tid; h < rep; h += blockDim.x) {
         ms[h] = -INFINITY;
@@ -114,8 +118,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
 
     const float *kb = kv_kbase(kv, b);
     const float *vb = kv_vbase(kv, b);
-    if (rp.pos && p_new >= t0 && p_new < t1) {
-        // this CTA's positions include the new one: store its k / v rows of head g
+    if (rp.pos && hp == 0 && p_new >= t0 && p_new < t1) {
+        // this CTA's positions include the new one (and it is head g's first part): store the
+        // k / v rows of head g
         const long long off = kv_offset(kv, b, p_new);
         if (off >= 0) {
             const int row = nkh * HD;
@@ -221,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
         const int i = tid + j * kAttnThreads;
         if (i < rep * HD) {
             const int h = i / HD, d = i - h * HD;
-            const int head = g * rep + h;
+            const int head = h0 + h;
             if (n_splits == 1) {
                 const float l = ls[h];
                 out[((size_t)b * nh + head) * HD + d] = (l > 0.0f) ? acc[j] / l : 0.0f;
@@ -232,7 +237,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
     }
     if (n_splits > 1) {
         for (int h = tid; h < rep; h += blockDim.x) {
-            const size_t o = (((size_t)b * nh + g * rep + h) * n_splits + split) * 2;
+            const size_t o = (((size_t)b * nh + h0 + h) * n_splits + split) * 2;
             part_ml[o] = ms[h];
             part_ml[o + 1] = ls[h];
         }
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const float *__res
         // this CTA's rep heads are rep * HD / 32 whole 32-element blocks of row b
         __syncthreads();
         const int warp = tid >> 5, lane = tid & 31, K = nh * HD;
-        const int kb0 = g * rep * HD / 32;
+        const int kb0 = h0 * HD / 32;
         for (int j = warp; j < rep * HD / 32; j += kAttnThreads / 32) {
             const int kb = kb0 + j;
             encode_block_packed(out[(size_t)b * K + 32 * kb + lane], b, kb, K, planes, lane);
@@ -342,20 +347,26 @@ int launch_attn_decode(const float *q, const KVView &kv, const int *seq_lens_dev
     }
     int span = max_seq_len;
     if (window > 0 && span > window) span = window;
-    // enough CTAs to cover the SMs; >= 32 positions (one tile) per split.  (At >= 64, config 5's
-    // 10 sequences x 2 KV heads ran as 20-40 CTAs of 8 query heads each: +120-150 us per
-    // attention layer at positions 64-160)
+    // enough CTAs to cover the SMs: first the positions split, >= 32 (one tile) per split; then,
+    // while the CTAs still do not cover the SMs, the query heads of a KV head split over CTAs (each
+    // part re-reads the KV tiles, from L2).  Positions first: a tile's fixed cost (its load and
+    // three block barriers) is shared by all of a CTA's heads -- heads first made config 3 at
+    // 16 sequences 17.5 -> 20.1 ms.  (Config 5's 10 sequences x 2 KV heads had run as 20-40
+    // CTAs of 8 query heads each: +120-150 us per attention layer at positions 64-160; config 3
+    // at one sequence as 4-8 CTAs.)
     const int ctas = B * nkh;
     int n_splits = 1;
     while (n_splits < 64 && ctas * n_splits < 2 * env->num_sms && span / (n_splits * 2) >= 32) n_splits *= 2;
+    int hsplit = 1;
+    while (rep % (2 * hsplit) == 0 && ctas * n_splits * hsplit < env->num_sms) hsplit *= 2;
     const int chunk = (span + n_splits - 1) / n_splits;
     const size_t need = (size_t)B * nh * n_splits * (hd + 2) * sizeof(float);
     if (n_splits > 1 && (!scratch || scratch_bytes < need)) n_splits = 1;
     const int chunk1 = n_splits == 1 ? (span > 0 ? span : 1) : chunk;
     float *part_ml = scratch;
     float *part_acc = scratch ? scratch + (size_t)B * nh * n_splits * 2 : nullptr;
-    dim3 grid(n_splits, nkh, B);
-    const size_t smem = attn_smem(rep, hd);
+    dim3 grid(n_splits, nkh * hsplit, B);
+    const size_t smem = attn_smem(rep / hsplit, hd);
 #define MLQ_ATTN_CASE(HD_)                                                                                    \
     case HD_: {                                                                                               \
         static bool attr = false;                                                                             \
