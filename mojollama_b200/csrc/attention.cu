@@ -11,11 +11,11 @@
 //   paged pool  [page][page_size][NKH*HD] per layer  (PageTable, cengine_batch_instr.c:160-214)
 // The kernel reads pages in place through the table -- no gather copy.
 //
-// Split-K flash decode: CTA (split, kv head g, sequence b) streams a contiguous chunk
-// of positions in 32-position tiles through shared memory, computes the scores of all
-// NH/NKH query heads that share g, keeps an online softmax (running max / sum) per
-// head and accumulates P.V in registers; it writes (max, sum, acc[HD]) per head and
-// split.  k_attn_merge combines the splits with their log-sum-exp weights.  With one
+// Split-K flash decode: CTA (split, kv head g x query-head part, sequence b) streams a
+// contiguous chunk of positions in 32-position tiles through shared memory, computes the
+// scores of its query heads (all NH/NKH that share g, or a part of them when the launcher
+// splits them over CTAs), keeps an online softmax (running max / sum) per head and
+// accumulates P.V in registers; it writes (max, sum, acc[HD]) per head and split.  k_attn_merge combines the splits with their log-sum-exp weights.  With one
 // split the first kernel writes the output directly.  Optional sliding window: only
 // the last `window` positions are attended (GPT-OSS alternate layers).
 // Roofline: HBM-bound on the K and V rows read (2 * seq * NKH * HD * 4 bytes per
